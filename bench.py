@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""Benchmark: the OLMoE-1B-7B-shaped MoE hot path on B200.
+
+One step = one pass of T tokens through the 16 MoE blocks of an OLMoE-1B-7B-
+shaped model (hidden 2048, 64 experts, top-8, SwiGLU intermediate 1024, bf16
+weights ~N(0, 0.02), seeded; inputs ~N(0, 1)).  Each block is the engine's MoE
+block, x += MoE(rmsnorm(x)) (rabbit2.c:512-542).  The default T = 1 is batch-1
+decode; --tokens 4096 is the prefill-sized layer call.
+
+  value  tokens/s over the whole job, device-timed with CUDA events, inputs and
+         weights resident in HBM (16 layers x 805 MB of weights per step, so the
+         working set is ~100x the 126 MB L2: no flush needed);
+  e2e    the same metric through the engine-facing C call with host buffers
+         (rbt_moe_block: pinned host x in, x and routing out, per layer);
+  roofline of the dominant kernel, from per-stage CUDA-event timing in a
+         separate profiled pass, against MEASURED_PEAKS.json;
+  cpu_baseline the reference's own CPU MoE layer (rabbit2.c compiled, through
+         oracle/_ref) on the host cores, on a bounded sample.
+
+--impl reference times only that CPU path (rank 0) and prints its line.
+Multi-GPU (torchrun): every rank runs an independent replica on its own tokens
+(no collective on the data path), value = all tokens / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+D, H, E, K, LAYERS = 2048, 1024, 64, 8, 16
+METRIC = "olmoe_moe_stack_tok_per_s"
+UNIT = "tok/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="rabbit2_b200", choices=["rabbit2_b200", "reference"])
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--routing", default="natural", choices=["natural", "zipf"])
+    ap.add_argument("--path", type=int, default=0, help="0 auto, 1 GEMV, 2 tcgen05 GEMM")
+    ap.add_argument("--profile-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def workload_desc(args):
+    return {"workload": f"olmoe1b7b_moe_stack_{args.layers}L_T{args.tokens}_{args.routing}",
+            "tokens_per_step_per_gpu": args.tokens, "layers": args.layers, "dim": D, "expert_hidden": H,
+            "n_experts": E, "top_k": K, "weights": "bf16 ~N(0,0.02) seeded, .rbt2 expert blobs",
+            "inputs": "f32 ~N(0,1) seeded", "routing": args.routing,
+            "l2": "working set 16 x 805 MB weights per step >> 126 MB L2 (no flush needed)",
+            "parallelism": f"replicas{args.gpus}"}
+
+
+# ----------------------------------------------------------------------------- CPU reference
+
+def host_layers(n, seed0, device):
+    """Host copies (router bf16 bits, expert blobs) of n seeded OLMoE layers."""
+    from rabbit2_b200 import workload
+    out = []
+    for l in range(n):
+        router, experts, stride = workload.device_layer(D, H, E, seed=seed0 + l, device=device)
+        out.append(workload.host_copy(router, experts) + (stride,))
+        del router, experts
+    return out
+
+
+def cpu_reference_run(args, seconds=None, steps=None, warmup=0, device="cuda"):
+    """Time the reference CPU MoE block (oracle/_ref, else the C restatement).
+
+    A step is the bench step's work on a bounded sample of its tokens: one layer
+    call per layer over `sample` tokens (weights of 2 distinct layers, cycled:
+    each is 805 MB, far beyond any CPU cache).  Returns (tok/s, info)."""
+    from oracle.oracle import MoeLayerHost, Oracle, Reference, available_reference
+    from rabbit2_b200 import workload
+    if available_reference():
+        lib, kind = Reference(), "reference"
+        kernel = "avx2" if lib.set_kernel(True) else "scalar"
+    else:
+        lib, kind, kernel = Oracle(), "port", "scalar"
+    ncores = len(os.sched_getaffinity(0))
+    sample = min(args.tokens, ncores)
+    threads = max(1, min(sample, ncores))
+    layers = host_layers(2, seed0=1, device=device)
+    bias = workload.zipf_bias(E, 1.2, seed=0) if args.routing == "zipf" else None
+    hosts = [MoeLayerHost(D, H, E, K, 1, 0, r, e, s, ffn_norm=np.ones(D, np.float32), router_bias=bias)
+             for (r, e, s) in layers]
+    x = np.random.default_rng(1000).standard_normal((sample, D)).astype(np.float32)
+
+    def one_step():
+        y = x
+        for l in range(args.layers):
+            y, _ = lib.moe_block(hosts[l % 2], y, nthreads=threads)
+        return y
+
+    for _ in range(warmup):
+        one_step()
+    t0, n = time.perf_counter(), 0
+    while True:
+        one_step()
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (seconds is not None and el >= seconds):
+            break
+    value = sample * n / el
+    info = {"kind": kind, "cores": threads,
+            "sample": f"{n} steps x {args.layers} MoE blocks x {sample} token(s), rabbit2.c --kernel {kernel}, "
+                      f"{threads} thread(s) of {ncores} host cores; {el:.1f} s",
+            "host_cpu": cpu_model()}
+    return value, info, el / n * 1e3
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    try:
+        import torch
+        device = "cuda" if torch.cuda.is_available() else "cpu"
+    except ImportError:
+        device = "cpu"
+    value, info, ms = cpu_reference_run(args, steps=args.steps, warmup=args.warmup, device=device)
+    cfg = workload_desc(args)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": dict(info, value=value, unit=UNIT),
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index):
+        self.index, self.proc = index, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.samples = []
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 8:
+                self.samples.append(parts)
+
+    def summary(self):
+        if not getattr(self, "samples", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            for n, v in zip(names, s[4:]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.samples[0][1]) if self.samples[0][1].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+def stage_bytes(T, U, S):
+    """Algorithmic HBM bytes per launch of each stage (bf16 weights, f32 activations)."""
+    w = 2
+    return {"rmsnorm": T * D * 4 * 2 + D * 4,
+            "router": E * D * w + T * D * 4 + T * K * 8,
+            "gate_up": U * 2 * H * D * w + T * D * 4 + S * H * 4,
+            "down": U * H * D * w + S * H * 4 + S * D * 4,
+            "combine": S * D * 4 + T * D * 4 * 2 + S * 8}
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from rabbit2_b200 import moe, workload
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    T, L = args.tokens, args.layers
+    stride = workload.layer_stride(D, H)
+    ctx = moe.MoeContext(D, E, K, H, L, moe.DT_BF16, 0, stride, device=local_rank)
+    ctx.set_path(args.path)
+    ones = torch.ones(D, device=dev)
+    keep = []
+    bias = workload.zipf_bias(E, 1.2, seed=0) if args.routing == "zipf" else None
+    for l in range(L):
+        router, experts, _ = workload.device_layer(D, H, E, seed=1 + l, device=dev)
+        ctx.bind_layer(l, router, experts, ones)
+        keep.append((router, experts))
+        if bias is not None:
+            ctx.set_router_bias(l, bias)
+    ctx.reserve(T)
+    x0 = workload.inputs(T, D, seed=1000 + rank, device=dev)
+    x = torch.empty_like(x0)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        x.copy_(x0)
+        for l in range(L):
+            ctx.block_device(l, x, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ctx.profile(timing=0, reset=True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.profile(reset=True)["launches"]
+    ms = ev0.elapsed_time(ev1) / args.steps
+    barrier()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T / (ms / 1e3)
+
+    # e2e through the engine-facing host call: pinned x in, x + routing out, per layer
+    xh = torch.empty((T, D), dtype=torch.float32, pin_memory=True)
+    rh = torch.empty((T, K), dtype=torch.int32, pin_memory=True)
+    x0h = x0.cpu()
+    lib, handle = ctx.lib, ctx.handle
+
+    def host_step():
+        xh.copy_(x0h)
+        for l in range(L):
+            if not lib.rbt_moe_block(handle, l, xh.data_ptr(), T, rh.data_ptr(), K):
+                raise moe.RbtMoeError(lib.rbt_moe_last_error().decode())
+
+    for _ in range(max(args.warmup, 3)):
+        host_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_step()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": L * T * D * 4,
+           "d2h_bytes_per_step": L * (T * D * 4 + T * K * 4),
+           "how": "rbt_moe_block per layer on pinned host memory; wall clock of synchronous calls"}
+
+    # profiled pass: per-stage device time (events between the kernels of each call)
+    ctx.profile(timing=1, reset=True)
+    hist = np.zeros(E, np.int64)
+    U_sum = 0
+    for _ in range(args.profile_steps):
+        x.copy_(x0)
+        for l in range(L):
+            ctx.block_device(l, x, stream=stream)
+            h = ctx.expert_histogram()
+            hist += h
+            U_sum += int((h > 0).sum())
+    prof = ctx.profile(timing=0, reset=True)
+    calls = args.profile_steps * L
+    U = U_sum / calls
+    S = T * K
+    bytes_per = stage_bytes(T, U, S)
+    per_launch_ms = {n: prof["stage_ms"][n] / max(prof["stage_launches"][n], 1) for n in bytes_per}
+    dom = max(per_launch_ms, key=lambda n: prof["stage_ms"][n])
+    hbm, bf16, src = peaks()
+    achieved = bytes_per[dom] / (per_launch_ms[dom] / 1e3) / 1e9
+    layer_bytes = E * D * 2 + U * 3 * H * D * 2 + T * D * 4 * 2 + T * K * 8
+    layer_ms = ms / L
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": src, "traffic": None,
+                "algorithmic_bytes_per_launch": bytes_per[dom], "avg_launch_ms": per_launch_ms[dom],
+                "stage_ms_per_launch": per_launch_ms,
+                "layer": {"us_per_layer": layer_ms * 1e3, "algorithmic_bytes": layer_bytes,
+                          "achieved_gbs": layer_bytes / (layer_ms / 1e3) / 1e9,
+                          "frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm,
+                          "distinct_experts_per_layer": U}}
+    out = None
+    if rank == 0:
+        out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_desc(args),
+               "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
+               "expert_histogram": hist.tolist()}
+    ctx.close()
+    return out
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    args.gpus = world
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            v, info, _ = cpu_reference_run(args, seconds=args.cpu_seconds, device="cuda")
+            line["cpu_baseline"] = dict(info, value=v, unit=UNIT)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,129 @@
+/*
+ * rbt_moe.h -- C ABI of librbt_moe.so, the sm_100a (B200) implementation of the
+ * RABBIT2 engine's MoE feed-forward.
+ *
+ * The reference engine (rabbit2/src/rabbit2.c) has no library boundary: the MoE
+ * block is inline code in forward() (rabbit2.c:511-542) on top of the static
+ * matvec() (:357-390) and get_expert() (:261-300).  These entry points are the
+ * calls a maintainer puts in place of that block; INTEGRATION.md shows the
+ * patch.  All pointers are plain C pointers; no CUDA or torch types appear.
+ *
+ * Conventions, mirroring the reference's own functions:
+ *   - every int-returning call returns 1 on success and 0 on error, like
+ *     forward()/load_model() (rabbit2.c:199,455); the message goes to stderr
+ *     and to rbt_moe_last_error();
+ *   - one host thread drives a context (the reference is single-threaded);
+ *   - matrices are row-major [out, in] in the model dtype (0 = f32, 1 = bf16),
+ *     vectors are f32, and an expert is the .rbt2 blob w1[H,D] | w3[H,D] |
+ *     w2[D,H], expert_stride bytes apart (rabbit2.c:166-193).
+ */
+#ifndef RBT_MOE_H
+#define RBT_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RBT_MOE_DT_F32 0
+#define RBT_MOE_DT_BF16 1
+#define RBT_MOE_MAX_TOPK 64     /* MAX_TOPK, rabbit2.c:59 */
+#define RBT_MOE_MAX_EXPERTS 256
+
+/* The MoE part of the model config (Config, rabbit2.c:63-68) plus the expert
+ * stride the loader computes (Model.expert_stride, rabbit2.c:173). */
+typedef struct RbtMoeConfig {
+    int32_t dim;            /* D */
+    int32_t n_experts;      /* E */
+    int32_t top_k;          /* K */
+    int32_t expert_hidden;  /* H */
+    int32_t n_layers;
+    int32_t dtype;          /* RBT_MOE_DT_F32 or RBT_MOE_DT_BF16 */
+    int32_t norm_topk;      /* 1: renormalise the chosen weights to sum to 1 */
+    float rms_eps;
+    uint64_t expert_stride; /* bytes between expert blobs */
+} RbtMoeConfig;
+
+typedef struct RbtMoe RbtMoe; /* opaque context: one per (model, GPU) */
+
+/* Create a context on CUDA device `device`.  Replaces the expert cache set-up
+ * (expert_cache_init, rabbit2.c:236-253): experts live in HBM instead. */
+int rbt_moe_create(RbtMoe **out, const RbtMoeConfig *cfg, int device);
+void rbt_moe_destroy(RbtMoe *m);
+
+/* Upload one layer's MoE weights from host memory (e.g. the mmap'd .rbt2):
+ * ffn_norm [D] f32 (may be NULL if only rbt_moe_ffn is used), router [E,D],
+ * experts = the layer's first expert blob (E blobs, expert_stride apart).
+ * Replaces get_expert() (rabbit2.c:261-300): one copy, then resident in HBM. */
+int rbt_moe_load_layer(RbtMoe *m, int layer, const float *ffn_norm, const void *router, const void *experts);
+
+/* Same as rbt_moe_load_layer, but binds DEVICE pointers the caller owns and
+ * keeps alive (no copy). */
+int rbt_moe_bind_layer(RbtMoe *m, int layer, const float *d_ffn_norm, const void *d_router, const void *d_experts);
+
+/* Optional additive router-logit bias [E] f32 (host pointer), applied before the
+ * softmax; NULL removes it.  Not in the reference (its router has no bias): it
+ * only builds skewed-routing workloads.  Without it results equal the reference. */
+int rbt_moe_set_router_bias(RbtMoe *m, int layer, const float *bias);
+
+/* The MoE block of forward(), rabbit2.c:512-542, for n_tokens rows at once:
+ *   x[t] += MoE(rmsnorm(x[t], ffn_norm))        x: [n_tokens, D] f32, in place
+ * routing_out (may be NULL) receives the chosen experts in selection order,
+ * row t at routing_out + t*routing_stride (the engine passes
+ * routing + layer*top_k with stride n_layers*top_k).  Host pointers; returns
+ * after the results are in host memory. */
+int rbt_moe_block(RbtMoe *m, int layer, float *x, int n_tokens, int32_t *routing_out, int routing_stride);
+
+/* The MoE feed-forward without the norm and residual, rabbit2.c:513-541:
+ *   moe_out[t] = sum_k w_k * W2_k (silu(W1_k xb[t]) * (W3_k xb[t]))
+ * xb, moe_out: [n_tokens, D] f32 host pointers. */
+int rbt_moe_ffn(RbtMoe *m, int layer, const float *xb, int n_tokens, float *moe_out, int32_t *routing_out,
+                int routing_stride);
+
+/* Device-pointer forms of the two calls above, enqueued on `stream` (a
+ * cudaStream_t; NULL = the context's own stream) without synchronising.
+ * x/xb/out/routing_out must be device pointers; xb may equal moe_out. */
+int rbt_moe_block_device(RbtMoe *m, int layer, float *d_x, int n_tokens, int32_t *d_routing_out,
+                         int routing_stride, void *stream);
+int rbt_moe_ffn_device(RbtMoe *m, int layer, const float *d_xb, int n_tokens, float *d_moe_out,
+                       int32_t *d_routing_out, int routing_stride, void *stream);
+
+/* Reserve the context's device workspace for up to n_tokens rows per call, so
+ * that later calls of that size allocate nothing (e.g. before stream capture). */
+int rbt_moe_reserve(RbtMoe *m, int n_tokens);
+
+/* Per-expert routed-token counts of the most recent call, [n_experts] int32
+ * (host pointer), in the key=value spirit of the engine's cache counters. */
+int rbt_moe_expert_histogram(RbtMoe *m, int32_t *counts_out);
+
+/* Force the path for later calls: 0 automatic (default), 1 the CUDA-core GEMV
+ * path, 2 the tcgen05 grouped-GEMM path (needs D, H multiples of 64, bf16). */
+int rbt_moe_set_path(RbtMoe *m, int path);
+
+/* Launch accounting and per-stage device timing.  Stages: 0 rmsnorm, 1 router +
+ * top-k + permute, 2 gate/up + SwiGLU, 3 down, 4 combine, 5 operand gather
+ * (GEMM path).  With timing enabled every call records CUDA events between its
+ * kernels and waits for them, so time a run with timing off and profile
+ * separately.  The reference's only timing is wall clock on stderr
+ * (rabbit2.c:742-744). */
+#define RBT_MOE_STAGES 8
+typedef struct RbtMoeProfile {
+    int64_t calls;                           /* MoE calls since the last reset */
+    int64_t launches;                        /* kernels this context launched since the reset */
+    double stage_ms[RBT_MOE_STAGES];         /* summed device time per stage (timing on) */
+    int64_t stage_launches[RBT_MOE_STAGES];  /* kernels per stage */
+} RbtMoeProfile;
+
+/* timing: 1 on, 0 off, -1 unchanged; reset: zero the counters after reading;
+ * out may be NULL. */
+int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
+
+/* Last error message of the calling thread ("" if none). */
+const char *rbt_moe_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RBT_MOE_H */

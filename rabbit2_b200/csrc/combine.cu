@@ -1,0 +1,97 @@
+// combine.cu -- K5: weighted combine of the k expert outputs of each token, plus
+// the residual add of the block form (rabbit2.c:530-542), and the ffn RMSNorm
+// that feeds the block form (rabbit2.c:512, rmsnorm at :392-397).
+//
+// Combine order follows the reference: moe = 0; moe += w_k * y_k for k in
+// selection order (product rounded, then added); x += moe.  Each output element
+// gathers its k inputs by slot position, so the result is deterministic (no
+// floating-point atomics).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rbt {
+namespace {
+
+constexpr int kThreads = 256;
+
+__global__ void __launch_bounds__(kThreads) combine_vec4_kernel(CombineArgs a) {
+    const int D4 = a.D / 4;
+    const long total = (long)a.T * D4;
+    for (long i = (long)blockIdx.x * kThreads + threadIdx.x; i < total; i += (long)gridDim.x * kThreads) {
+        const int t = (int)(i / D4), d = (int)(i - (long)t * D4) * 4;
+        float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < a.K; k++) {
+            const int s = t * a.K + k;
+            const float w = a.wt[s];
+            const float4 y = *reinterpret_cast<const float4*>(a.y + (size_t)a.slot_pos[s] * a.D + d);
+            m.x = __fadd_rn(m.x, __fmul_rn(w, y.x));
+            m.y = __fadd_rn(m.y, __fmul_rn(w, y.y));
+            m.z = __fadd_rn(m.z, __fmul_rn(w, y.z));
+            m.w = __fadd_rn(m.w, __fmul_rn(w, y.w));
+        }
+        if (a.resid) {
+            const float4 x = *reinterpret_cast<const float4*>(a.resid + (size_t)t * a.D + d);
+            m = make_float4(__fadd_rn(x.x, m.x), __fadd_rn(x.y, m.y), __fadd_rn(x.z, m.z), __fadd_rn(x.w, m.w));
+        }
+        *reinterpret_cast<float4*>(a.out + (size_t)t * a.D + d) = m;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) combine_scalar_kernel(CombineArgs a) {
+    const long total = (long)a.T * a.D;
+    for (long i = (long)blockIdx.x * kThreads + threadIdx.x; i < total; i += (long)gridDim.x * kThreads) {
+        const int t = (int)(i / a.D), d = (int)(i - (long)t * a.D);
+        float m = 0.0f;
+        for (int k = 0; k < a.K; k++) {
+            const int s = t * a.K + k;
+            m = __fadd_rn(m, __fmul_rn(a.wt[s], a.y[(size_t)a.slot_pos[s] * a.D + d]));
+        }
+        if (a.resid) m = __fadd_rn(a.resid[(size_t)t * a.D + d], m);
+        a.out[(size_t)t * a.D + d] = m;
+    }
+}
+
+// out[t] = (x[t] * inv) * w, inv = 1 / sqrtf(mean(x^2) + eps); one CTA per token.
+// The sum of squares is a parallel fp32 reduction (the reference's is sequential,
+// so xb may differ from it in the last bit).
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* x, const float* w, float* out, int D,
+                                                           float eps) {
+    __shared__ float s_part[kThreads / 32];
+    const float* xr = x + (size_t)blockIdx.x * D;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < D; i += kThreads) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < kThreads / 32 ? s_part[threadIdx.x] : 0.0f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) s_part[0] = v;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s_part[0], (float)D), eps));
+    float* o = out + (size_t)blockIdx.x * D;
+    for (int i = threadIdx.x; i < D; i += kThreads) o[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+}  // namespace
+
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s) {
+    if (a.T <= 0) return cudaSuccess;
+    const bool vec = (a.D % 4 == 0) && (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) &&
+                     (!a.resid || reinterpret_cast<uintptr_t>(a.resid) % 16 == 0);
+    const long work = vec ? (long)a.T * (a.D / 4) : (long)a.T * a.D;
+    const long blocks = (work + kThreads - 1) / kThreads;
+    const int grid = (int)(blocks < 148L * 16 ? blocks : 148L * 16);
+    if (vec) combine_vec4_kernel<<<grid, kThreads, 0, s>>>(a);
+    else combine_scalar_kernel<<<grid, kThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, int D, float eps, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    rmsnorm_kernel<<<T, kThreads, 0, s>>>(x, w, out, D, eps);
+    return cudaGetLastError();
+}
+
+}  // namespace rbt

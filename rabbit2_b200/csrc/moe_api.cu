@@ -1,0 +1,409 @@
+// moe_api.cu -- the C ABI of librbt_moe.so (include/rbt_moe.h): context,
+// HBM-resident expert weights, workspace, and the per-call launch sequence
+//
+//   [rmsnorm] -> router/top-k/permute (K1) -> gate-up (K3|K4) -> down (K3|K4)
+//   -> combine + residual (K5)
+//
+// Replaces, in the reference engine, the MoE block of forward()
+// (rabbit2.c:511-542), the CPU matvec kernels it calls (:323-390) and the
+// expert fetch seam get_expert()/ExpertCache (:83-94, :236-300).
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <new>
+#include <vector>
+
+#include "../../include/rbt_moe.h"
+#include "kernels.h"
+
+namespace rbt {
+int router_token_tiles(int T);
+}
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "rbt_moe: %s\n", g_err);
+    return 0;
+}
+
+#define CU(call)                                                                                  \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess) return fail("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                                   \
+    } while (0)
+
+struct Layer {
+    const float* ffn_norm = nullptr;
+    const void* router = nullptr;
+    const uint8_t* experts = nullptr;
+    float* bias = nullptr;        // device [E] or null
+    void* owned = nullptr;        // allocation made by rbt_moe_load_layer
+};
+
+struct Workspace {
+    int cap = 0;                  // tokens per call the buffers hold
+    void* block = nullptr;
+    float *xb, *logits, *wt, *h, *y, *hx, *hout;
+    int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active, *hrouting;
+    unsigned *tile_counter, *done_counter;
+};
+
+}  // namespace
+
+struct RbtMoe {
+    RbtMoeConfig cfg;
+    bool timing = false;
+    RbtMoeProfile prof{};
+    cudaEvent_t ev[RBT_MOE_STAGES + 1] = {};
+    int device = 0;
+    int sm_count = 0;
+    int path = 0;
+    size_t esz = 2;
+    cudaStream_t stream = nullptr;
+    std::vector<Layer> layers;
+    Workspace ws;
+};
+
+namespace {
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int set_device(RbtMoe* m) {
+    CU(cudaSetDevice(m->device));
+    return 1;
+}
+
+// Grow the workspace to hold `T` tokens (allocates; not legal during capture).
+int reserve(RbtMoe* m, int T) {
+    if (T <= m->ws.cap) return 1;
+    const RbtMoeConfig& c = m->cfg;
+    const size_t D = c.dim, E = c.n_experts, K = c.top_k, H = c.expert_hidden, S = (size_t)T * K;
+    const size_t tiles = (size_t)rbt::router_token_tiles(T) + 1;
+    struct Part { void** p; size_t bytes; };
+    Workspace w;
+    w.cap = T;
+    std::vector<Part> parts = {
+        {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
+        {(void**)&w.wt, S * 4},                  {(void**)&w.h, S * H * 4},
+        {(void**)&w.y, S * D * 4},               {(void**)&w.hx, (size_t)T * D * 4},
+        {(void**)&w.hout, (size_t)T * D * 4},    {(void**)&w.idx, S * 4},
+        {(void**)&w.counts, E * 4},              {(void**)&w.offsets, (E + 1) * 4},
+        {(void**)&w.perm, S * 4},                {(void**)&w.slot_pos, S * 4},
+        {(void**)&w.active, E * 4},              {(void**)&w.n_active, 4},
+        {(void**)&w.hrouting, S * 4},            {(void**)&w.tile_counter, tiles * 4},
+        {(void**)&w.done_counter, 4},
+    };
+    size_t total = 0;
+    for (auto& p : parts) total = align_up(total, 256) + p.bytes;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    CU(cudaStreamIsCapturing(m->stream, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+        return fail("workspace for %d tokens must be reserved before stream capture (rbt_moe_reserve)", T);
+    void* block = nullptr;
+    CU(cudaMalloc(&block, total));
+    size_t off = 0;
+    for (auto& p : parts) {
+        off = align_up(off, 256);
+        *p.p = (char*)block + off;
+        off += p.bytes;
+    }
+    // counters must start at zero; the kernels return them to zero after use
+    CU(cudaMemsetAsync(w.tile_counter, 0, tiles * 4, m->stream));
+    CU(cudaMemsetAsync(w.done_counter, 0, 4, m->stream));
+    CU(cudaMemsetAsync(w.counts, 0, E * 4, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    if (m->ws.block) CU(cudaFree(m->ws.block));
+    w.block = block;
+    m->ws = w;
+    return 1;
+}
+
+int check_layer(RbtMoe* m, int layer, bool need_norm) {
+    if (!m) return fail("null context");
+    if (layer < 0 || layer >= m->cfg.n_layers) return fail("layer %d out of range [0, %d)", layer, m->cfg.n_layers);
+    const Layer& L = m->layers[layer];
+    if (!L.router || !L.experts) return fail("layer %d has no weights (rbt_moe_load_layer / rbt_moe_bind_layer)", layer);
+    if (need_norm && !L.ffn_norm) return fail("layer %d has no ffn_norm (needed by the block form)", layer);
+    return 1;
+}
+
+// Stage bookkeeping: count every launch; with timing on, bracket stages with
+// events on the launching stream.
+struct StageClock {
+    RbtMoe* m;
+    cudaStream_t s;
+    int last = -1;
+    int open_stage = -1;
+    int begin(int stage) {
+        m->prof.launches++;
+        m->prof.stage_launches[stage]++;
+        if (!m->timing) return 1;
+        if (open_stage >= 0 && !end()) return 0;
+        CU(cudaEventRecord(m->ev[0], s));
+        open_stage = stage;
+        return 1;
+    }
+    int end() {
+        if (!m->timing || open_stage < 0) return 1;
+        CU(cudaEventRecord(m->ev[1], s));
+        CU(cudaEventSynchronize(m->ev[1]));
+        float ms = 0.f;
+        CU(cudaEventElapsedTime(&ms, m->ev[0], m->ev[1]));
+        m->prof.stage_ms[open_stage] += ms;
+        open_stage = -1;
+        return 1;
+    }
+};
+
+// The whole MoE call on device pointers.  block: x is the residual stream,
+// updated in place; otherwise out = moe(xb).
+int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* routing, int routing_stride,
+            cudaStream_t s, bool block) {
+    if (!check_layer(m, layer, block)) return 0;
+    if (T < 0) return fail("n_tokens must be >= 0 (got %d)", T);
+    if (T == 0) return 1;
+    if (routing && routing_stride < m->cfg.top_k)
+        return fail("routing_stride %d < top_k %d", routing_stride, m->cfg.top_k);
+    if (!set_device(m) || !reserve(m, T)) return 0;
+    const RbtMoeConfig& c = m->cfg;
+    const Layer& L = m->layers[layer];
+    Workspace& w = m->ws;
+    StageClock clk{m, s};
+    m->prof.calls++;
+    const float* xb = x;
+    if (block) {
+        if (!clk.begin(0)) return 0;
+        CU(rbt::launch_rmsnorm(x, L.ffn_norm, w.xb, T, c.dim, c.rms_eps, s));
+        xb = w.xb;
+    }
+    rbt::RouterArgs ra{};
+    ra.xb = xb;
+    ra.T = T; ra.D = c.dim; ra.E = c.n_experts; ra.K = c.top_k;
+    ra.router = L.router; ra.dtype = c.dtype; ra.bias = L.bias; ra.norm_topk = c.norm_topk;
+    ra.logits = w.logits; ra.idx = w.idx; ra.wt = w.wt;
+    ra.routing_out = routing; ra.routing_stride = routing_stride;
+    ra.tile_counter = w.tile_counter; ra.done_counter = w.done_counter;
+    ra.counts = w.counts; ra.offsets = w.offsets; ra.perm = w.perm; ra.slot_pos = w.slot_pos;
+    ra.active = w.active; ra.n_active = w.n_active;
+    if (!clk.begin(1)) return 0;
+    CU(rbt::launch_router(ra, s));
+
+    rbt::GemvArgs ga{};
+    ga.xb = xb; ga.experts = L.experts; ga.stride = c.expert_stride;
+    ga.T = T; ga.D = c.dim; ga.H = c.expert_hidden; ga.E = c.n_experts; ga.K = c.top_k; ga.dtype = c.dtype;
+    ga.perm = w.perm; ga.offsets = w.offsets; ga.active = w.active; ga.n_active = w.n_active;
+    ga.h = w.h; ga.y = w.y; ga.grid = m->sm_count;
+    if (!clk.begin(2)) return 0;
+    CU(rbt::launch_gateup_gemv(ga, s));
+    if (!clk.begin(3)) return 0;
+    CU(rbt::launch_down_gemv(ga, s));
+
+    rbt::CombineArgs ca{};
+    ca.resid = block ? x : nullptr;
+    ca.y = w.y; ca.wt = w.wt; ca.slot_pos = w.slot_pos;
+    ca.out = block ? const_cast<float*>(x) : out;
+    ca.T = T; ca.D = c.dim; ca.K = c.top_k;
+    if (!clk.begin(4)) return 0;
+    CU(rbt::launch_combine(ca, s));
+    return clk.end();
+}
+
+// Host-pointer wrapper: stage through the workspace's device buffers.
+int forward_host(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* routing, int routing_stride,
+                 bool block) {
+    if (!m) return fail("null context");
+    if (T < 0) return fail("n_tokens must be >= 0 (got %d)", T);
+    if (T == 0) return 1;
+    if (!x || !out) return fail("null input/output pointer");
+    if (!set_device(m) || !reserve(m, T)) return 0;
+    const RbtMoeConfig& c = m->cfg;
+    Workspace& w = m->ws;
+    const size_t bytes = (size_t)T * c.dim * sizeof(float);
+    CU(cudaMemcpyAsync(w.hx, x, bytes, cudaMemcpyHostToDevice, m->stream));
+    float* dout = block ? w.hx : w.hout;
+    if (!forward(m, layer, w.hx, dout, T, routing ? w.hrouting : nullptr, c.top_k, m->stream, block)) return 0;
+    CU(cudaMemcpyAsync(out, dout, bytes, cudaMemcpyDeviceToHost, m->stream));
+    if (routing)
+        CU(cudaMemcpy2DAsync(routing, (size_t)routing_stride * 4, w.hrouting, (size_t)c.top_k * 4,
+                             (size_t)c.top_k * 4, T, cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* rbt_moe_last_error(void) { return g_err; }
+
+int rbt_moe_create(RbtMoe** out, const RbtMoeConfig* cfg, int device) {
+    if (!out || !cfg) return fail("null argument");
+    *out = nullptr;
+    const RbtMoeConfig& c = *cfg;
+    if (c.dim <= 0 || c.expert_hidden <= 0 || c.n_layers <= 0 || c.n_experts <= 0 || c.top_k <= 0)
+        return fail("invalid config: dims must be positive");
+    if (c.top_k > c.n_experts || c.top_k > rbt::kMaxTopK)
+        return fail("invalid config: top_k %d (n_experts %d, max %d)", c.top_k, c.n_experts, rbt::kMaxTopK);
+    if (c.n_experts > rbt::kMaxExperts) return fail("n_experts %d above the supported %d", c.n_experts, rbt::kMaxExperts);
+    if (c.dtype != RBT_MOE_DT_F32 && c.dtype != RBT_MOE_DT_BF16) return fail("dtype must be 0 (f32) or 1 (bf16)");
+    const size_t esz = c.dtype == RBT_MOE_DT_BF16 ? 2 : 4;
+    if (c.expert_stride < 3ull * c.expert_hidden * c.dim * esz) return fail("expert_stride smaller than one expert");
+    int ndev = 0;
+    CU(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail("device %d out of range (%d visible)", device, ndev);
+    CU(cudaSetDevice(device));
+    RbtMoe* m = new (std::nothrow) RbtMoe();
+    if (!m) return fail("out of host memory");
+    m->cfg = c;
+    m->device = device;
+    m->esz = esz;
+    m->layers.resize(c.n_layers);
+    bool ok = cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
+    for (int i = 0; ok && i < 2; i++) ok = cudaEventCreate(&m->ev[i]) == cudaSuccess;
+    if (!ok) {
+        delete m;
+        return fail("cannot initialise CUDA device %d", device);
+    }
+    *out = m;
+    return 1;
+}
+
+void rbt_moe_destroy(RbtMoe* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    for (Layer& L : m->layers) {
+        cudaFree(L.owned);
+        cudaFree(L.bias);
+    }
+    cudaFree(m->ws.block);
+    for (int i = 0; i < 2; i++)
+        if (m->ev[i]) cudaEventDestroy(m->ev[i]);
+    cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int rbt_moe_load_layer(RbtMoe* m, int layer, const float* ffn_norm, const void* router, const void* experts) {
+    if (!m) return fail("null context");
+    if (layer < 0 || layer >= m->cfg.n_layers) return fail("layer %d out of range", layer);
+    if (!router || !experts) return fail("null router/experts pointer");
+    if (!set_device(m)) return 0;
+    const RbtMoeConfig& c = m->cfg;
+    const size_t b_exp = (size_t)c.n_experts * c.expert_stride;
+    const size_t b_router = (size_t)c.n_experts * c.dim * m->esz;
+    const size_t b_norm = (size_t)c.dim * 4;
+    const size_t o_router = align_up(b_exp, 256), o_norm = align_up(o_router + b_router, 256);
+    Layer& L = m->layers[layer];
+    if (L.owned) CU(cudaFree(L.owned));
+    L.owned = nullptr;
+    void* p = nullptr;
+    CU(cudaMalloc(&p, o_norm + b_norm));
+    L.owned = p;
+    CU(cudaMemcpy(p, experts, b_exp, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy((char*)p + o_router, router, b_router, cudaMemcpyHostToDevice));
+    if (ffn_norm) CU(cudaMemcpy((char*)p + o_norm, ffn_norm, b_norm, cudaMemcpyHostToDevice));
+    L.experts = (const uint8_t*)p;
+    L.router = (char*)p + o_router;
+    L.ffn_norm = ffn_norm ? (const float*)((char*)p + o_norm) : nullptr;
+    return 1;
+}
+
+int rbt_moe_bind_layer(RbtMoe* m, int layer, const float* d_ffn_norm, const void* d_router, const void* d_experts) {
+    if (!m) return fail("null context");
+    if (layer < 0 || layer >= m->cfg.n_layers) return fail("layer %d out of range", layer);
+    if (!d_router || !d_experts) return fail("null router/experts pointer");
+    if (!set_device(m)) return 0;
+    Layer& L = m->layers[layer];
+    if (L.owned) CU(cudaFree(L.owned));
+    L.owned = nullptr;
+    L.ffn_norm = d_ffn_norm;
+    L.router = d_router;
+    L.experts = (const uint8_t*)d_experts;
+    return 1;
+}
+
+int rbt_moe_set_router_bias(RbtMoe* m, int layer, const float* bias) {
+    if (!m) return fail("null context");
+    if (layer < 0 || layer >= m->cfg.n_layers) return fail("layer %d out of range", layer);
+    if (!set_device(m)) return 0;
+    Layer& L = m->layers[layer];
+    if (!bias) {
+        if (L.bias) CU(cudaFree(L.bias));
+        L.bias = nullptr;
+        return 1;
+    }
+    if (!L.bias) CU(cudaMalloc(&L.bias, (size_t)m->cfg.n_experts * 4));
+    CU(cudaMemcpy(L.bias, bias, (size_t)m->cfg.n_experts * 4, cudaMemcpyHostToDevice));
+    return 1;
+}
+
+int rbt_moe_reserve(RbtMoe* m, int n_tokens) {
+    if (!m) return fail("null context");
+    if (n_tokens < 0) return fail("n_tokens must be >= 0");
+    return set_device(m) && reserve(m, n_tokens);
+}
+
+int rbt_moe_block(RbtMoe* m, int layer, float* x, int n_tokens, int32_t* routing_out, int routing_stride) {
+    return forward_host(m, layer, x, x, n_tokens, routing_out, routing_stride, true);
+}
+
+int rbt_moe_ffn(RbtMoe* m, int layer, const float* xb, int n_tokens, float* moe_out, int32_t* routing_out,
+                int routing_stride) {
+    return forward_host(m, layer, xb, moe_out, n_tokens, routing_out, routing_stride, false);
+}
+
+int rbt_moe_block_device(RbtMoe* m, int layer, float* d_x, int n_tokens, int32_t* d_routing_out, int routing_stride,
+                         void* stream) {
+    if (!m) return fail("null context");
+    if (!d_x && n_tokens > 0) return fail("null x");
+    return forward(m, layer, d_x, d_x, n_tokens, d_routing_out, routing_stride,
+                   stream ? (cudaStream_t)stream : m->stream, true);
+}
+
+int rbt_moe_ffn_device(RbtMoe* m, int layer, const float* d_xb, int n_tokens, float* d_moe_out,
+                       int32_t* d_routing_out, int routing_stride, void* stream) {
+    if (!m) return fail("null context");
+    if ((!d_xb || !d_moe_out) && n_tokens > 0) return fail("null xb/moe_out");
+    return forward(m, layer, d_xb, d_moe_out, n_tokens, d_routing_out, routing_stride,
+                   stream ? (cudaStream_t)stream : m->stream, false);
+}
+
+int rbt_moe_expert_histogram(RbtMoe* m, int32_t* counts_out) {
+    if (!m || !counts_out) return fail("null argument");
+    if (!set_device(m)) return 0;
+    if (!m->ws.block) {
+        memset(counts_out, 0, sizeof(int32_t) * (size_t)m->cfg.n_experts);
+        return 1;
+    }
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(counts_out, m->ws.counts, sizeof(int32_t) * (size_t)m->cfg.n_experts, cudaMemcpyDeviceToHost));
+    return 1;
+}
+
+int rbt_moe_profile(RbtMoe* m, int timing, int reset, RbtMoeProfile* out) {
+    if (!m) return fail("null context");
+    if (out) *out = m->prof;
+    if (reset) m->prof = RbtMoeProfile{};
+    if (timing >= 0) m->timing = timing != 0;
+    return 1;
+}
+
+int rbt_moe_set_path(RbtMoe* m, int path) {
+    if (!m) return fail("null context");
+    if (path < 0 || path > 2) return fail("path must be 0, 1 or 2");
+    m->path = path;
+    return 1;
+}
+
+}  // extern "C"

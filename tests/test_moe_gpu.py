@@ -1,0 +1,178 @@
+"""GPU parity: librbt_moe.so through its C ABI against the CPU oracle.
+
+Bars: routing indices bit-exact; MoE outputs within a
+max relative error of 1e-3, measured here as max|got - want| / max|want| with
+fp32 accumulation on both sides -- the tests use tighter bounds where the
+arithmetic allows them (MOE_RTOL) and keep 1e-3 as the hard ceiling.
+
+A routing difference is tolerated only where the oracle's own probabilities
+of the two swapped experts are within one ulp (glibc's expf differs from a
+correctly rounded exp on ~8e-5 of inputs, by one ulp).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle.oracle import MoeLayerHost, Oracle  # noqa: E402
+from rabbit2_b200 import moe, workload  # noqa: E402
+from tests.golden.cases import case_keys, load_case, pack_layer  # noqa: E402
+
+MOE_RTOL = 2e-5      # what fp32 accumulation in a different order reaches at these sizes
+NORTH_STAR = 1e-3
+
+
+def rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def orc():
+    return Oracle()
+
+
+def assert_routing(got, want, probs=None):
+    if np.array_equal(got, want):
+        return
+    assert probs is not None, "routing differs"
+    bad = np.argwhere(got != want)
+    for t, k in bad:
+        pa, pb = probs[t, got[t, k]], probs[t, want[t, k]]
+        assert abs(np.float32(pa) - np.float32(pb)) <= np.spacing(np.float32(max(pa, pb))), (t, k, pa, pb)
+
+
+@pytest.mark.parametrize("key", case_keys())
+def test_golden_cases(orc, key):
+    case = load_case(key)
+    cfg = case["cfg"]
+    from rabbit2_b200.rbt2fmt import expert_stride
+    ctx = moe.MoeContext(cfg.dim, cfg.n_experts, cfg.top_k, cfg.expert_hidden, cfg.n_layers, cfg.dtype,
+                         cfg.norm_topk, expert_stride(cfg), rms_eps=cfg.rms_eps)
+    try:
+        for li in range(cfg.n_layers):
+            router, experts, ffn_norm = pack_layer(cfg, case["weights"]["layers"][li])
+            ctx.load_layer(li, router, experts, ffn_norm)
+            host = MoeLayerHost(cfg.dim, cfg.expert_hidden, cfg.n_experts, cfg.top_k, cfg.dtype, cfg.norm_topk,
+                                router, experts, experts.shape[1], ffn_norm=ffn_norm, rms_eps=cfg.rms_eps)
+            # ffn form vs the reference's NumPy golden and the oracle
+            out, routing = ctx.ffn(li, case["xb"][li])
+            np.testing.assert_array_equal(routing, case["routing"][:, li, :])
+            assert rel_err(out, case["moe"][li]) < 1e-4
+            want, want_r, _ = orc.moe_ffn(host, case["xb"][li])
+            np.testing.assert_array_equal(routing, want_r)
+            assert rel_err(out, want) < MOE_RTOL
+            # block form (in place on the residual stream), routing strided like the engine's [T, L, K]
+            xo, routing_b = ctx.block(li, case["x"][li], routing_stride=cfg.n_layers * cfg.top_k)
+            np.testing.assert_array_equal(routing_b, case["routing"][:, li, :])
+            assert rel_err(xo - case["x"][li], case["moe"][li]) < 1e-4
+    finally:
+        ctx.close()
+
+
+def olmoe_ctx(n_layers=1, seed=11, bias=None):
+    s = workload.OLMOE
+    router, experts, stride = workload.device_layer(s["dim"], s["expert_hidden"], s["n_experts"], seed)
+    ctx = moe.MoeContext(s["dim"], s["n_experts"], s["top_k"], s["expert_hidden"], n_layers, moe.DT_BF16, 0,
+                         stride)
+    ctx.bind_layer(0, router, experts)
+    if bias is not None:
+        ctx.set_router_bias(0, bias)
+    r_h, e_h = workload.host_copy(router, experts)
+    host = MoeLayerHost(s["dim"], s["expert_hidden"], s["n_experts"], s["top_k"], moe.DT_BF16, 0, r_h, e_h, stride,
+                        router_bias=bias)
+    return ctx, host
+
+
+@pytest.fixture(scope="module")
+def olmoe():
+    ctx, host = olmoe_ctx()
+    yield ctx, host
+    ctx.close()
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 16, 64, 256])
+def test_olmoe_layer_vs_oracle(orc, olmoe, T):
+    ctx, host = olmoe
+    x = workload.inputs(T, 2048, seed=100 + T)
+    out = torch.empty_like(x)
+    routing = torch.empty(T, 8, dtype=torch.int32, device="cuda")
+    ctx.ffn_device(0, x, out, routing)
+    torch.cuda.synchronize()
+    xh = x.cpu().numpy()
+    want, want_r, _ = orc.moe_ffn(host, xh, nthreads=8)
+    _, _, probs = orc.router_topk(host, xh)
+    assert_routing(routing.cpu().numpy(), want_r, probs)
+    err = rel_err(out.cpu().numpy(), want)
+    assert err < MOE_RTOL, err
+    counts = ctx.expert_histogram()
+    np.testing.assert_array_equal(counts, np.bincount(want_r.ravel(), minlength=64))
+
+
+@pytest.mark.parametrize("T", [1, 16, 256])
+def test_olmoe_zipf_routing(orc, T):
+    bias = workload.zipf_bias(64, 1.2, seed=5)
+    ctx, host = olmoe_ctx(seed=12, bias=bias)
+    try:
+        x = workload.inputs(T, 2048, seed=200 + T)
+        out = torch.empty_like(x)
+        routing = torch.empty(T, 8, dtype=torch.int32, device="cuda")
+        ctx.ffn_device(0, x, out, routing)
+        torch.cuda.synchronize()
+        xh = x.cpu().numpy()
+        want, want_r, _ = orc.moe_ffn(host, xh, nthreads=8)
+        _, _, probs = orc.router_topk(host, xh)
+        assert_routing(routing.cpu().numpy(), want_r, probs)
+        assert rel_err(out.cpu().numpy(), want) < MOE_RTOL
+    finally:
+        ctx.close()
+
+
+def test_olmoe_large_batch_routing_and_sampled_outputs(orc, olmoe):
+    """T = 4096 (the prefill microbench size): routing of every token against the
+    oracle's router, outputs of 48 sampled tokens against the full oracle."""
+    ctx, host = olmoe
+    T = 4096
+    x = workload.inputs(T, 2048, seed=4096)
+    out = torch.empty_like(x)
+    routing = torch.empty(T, 8, dtype=torch.int32, device="cuda")
+    ctx.ffn_device(0, x, out, routing)
+    torch.cuda.synchronize()
+    xh = x.cpu().numpy()
+    want_r, _, probs = orc.router_topk(host, xh)
+    assert_routing(routing.cpu().numpy(), want_r, probs)
+    sample = np.random.default_rng(0).choice(T, 48, replace=False)
+    want, _, _ = orc.moe_ffn(host, xh[sample], nthreads=8)
+    assert rel_err(out.cpu().numpy()[sample], want) < MOE_RTOL
+    # a size-independent property: the histogram sums to T*K
+    assert ctx.expert_histogram().sum() == T * 8
+
+
+def test_deterministic_and_host_api_matches_device_api(olmoe):
+    ctx, _ = olmoe
+    T = 16
+    x = workload.inputs(T, 2048, seed=7)
+    out1, out2 = torch.empty_like(x), torch.empty_like(x)
+    ctx.ffn_device(0, x, out1)
+    ctx.ffn_device(0, x, out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out1.view(torch.int32), out2.view(torch.int32))
+    host_out, _ = ctx.ffn(0, x.cpu().numpy())
+    np.testing.assert_array_equal(host_out.view(np.uint32), out1.cpu().numpy().view(np.uint32))
+
+
+def test_zero_tokens_and_bad_arguments(olmoe):
+    ctx, _ = olmoe
+    x = torch.empty(0, 2048, device="cuda")
+    ctx.ffn_device(0, x, x, T=0)
+    with pytest.raises(moe.RbtMoeError, match="layer"):
+        ctx.ffn(3, np.zeros((1, 2048), np.float32))
+    with pytest.raises(moe.RbtMoeError, match="n_tokens"):
+        ctx.ffn_device(0, workload.inputs(1, 2048, 0), torch.empty(1, 2048, device="cuda"), T=-1)
+    with pytest.raises(moe.RbtMoeError, match="routing_stride"):
+        ctx.ffn_device(0, workload.inputs(1, 2048, 0), torch.empty(1, 2048, device="cuda"),
+                       torch.empty(1, 8, dtype=torch.int32, device="cuda"), routing_stride=4)
+    with pytest.raises(moe.RbtMoeError, match="ffn_norm"):
+        ctx.block(0, np.zeros((1, 2048), np.float32))
