@@ -212,14 +212,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
-def stage_bytes(T, U, S):
-    """Algorithmic HBM bytes per launch of each stage (bf16 weights, f32 activations)."""
+def stage_cost(T, U, S):
+    """Algorithmic HBM bytes and FLOPs per launch of each stage (bf16 weights, f32 activations)."""
     w = 2
-    return {"rmsnorm": T * D * 4 * 2 + D * 4,
-            "router": E * D * w + T * D * 4 + T * K * 8,
-            "gate_up": U * 2 * H * D * w + T * D * 4 + S * H * 4,
-            "down": U * H * D * w + S * H * 4 + S * D * 4,
-            "combine": S * D * 4 + T * D * 4 * 2 + S * 8}
+    bytes_ = {"rmsnorm": T * D * 4 * 2 + D * 4,
+              "router": E * D * w + T * D * 4 + T * K * 8,
+              "gate_up": U * 2 * H * D * w + T * D * 4 + S * H * 4,
+              "down": U * H * D * w + S * H * 4 + S * D * 4,
+              "combine": S * D * 4 + T * D * 4 * 2 + S * 8,
+              "gather": T * D * 4 + S * D * 4}
+    flops = {"router": 2 * T * E * D, "gate_up": 4 * S * H * D, "down": 2 * S * H * D}
+    return bytes_, flops
 
 
 def run_ours(args, rank, world, local_rank):
@@ -245,31 +248,52 @@ def run_ours(args, rank, world, local_rank):
     ctx.reserve(T)
     x0 = workload.inputs(T, D, seed=1000 + rank, device=dev)
     x = torch.empty_like(x0)
-    stream = torch.cuda.current_stream()
 
     def step():
+        st = torch.cuda.current_stream()
         x.copy_(x0)
         for l in range(L):
-            ctx.block_device(l, x, stream=stream)
+            ctx.block_device(l, x, stream=st)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ctx.profile(timing=0, reset=True)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
+    # eager warm-up, and the routed-expert statistics of every layer
+    s = torch.cuda.Stream(device=dev)
+    hist = np.zeros(E, np.int64)
+    U_sum = 0
+    with torch.cuda.stream(s):
+        for _ in range(max(args.warmup, 3)):
             step()
-        ev1.record(stream)
+        x.copy_(x0)
+        for l in range(L):
+            ctx.block_device(l, x, stream=s)
+            h = ctx.expert_histogram()
+            hist += h
+            U_sum += int((h > 0).sum())
+    torch.cuda.synchronize()
+    U = U_sum / L
+
+    # the timed step is a CUDA graph of the 16 layer calls (5 kernels each)
+    ctx.profile(timing=0, reset=True)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    launches_per_step = ctx.profile(reset=True)["launches"]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            g.replay()
         torch.cuda.synchronize()
-    launches = ctx.profile(reset=True)["launches"]
+        barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local_rank) as clocks:
+            ev0.record(s)
+            for _ in range(args.steps):
+                g.replay()
+            ev1.record(s)
+            torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / args.steps
     barrier()
     if world > 1:
@@ -303,45 +327,61 @@ def run_ours(args, rank, world, local_rank):
         e2e_ms = float(t.item())
     e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": L * T * D * 4,
            "d2h_bytes_per_step": L * (T * D * 4 + T * K * 4),
-           "how": "rbt_moe_block per layer on pinned host memory; wall clock of synchronous calls"}
+           "how": "rbt_moe_block per layer (host x in, x and routing out, synchronous), pinned host memory, "
+                  "wall clock"}
 
-    # profiled pass: per-stage device time (events between the kernels of each call)
+    # profiled replays: a second graph with event-record nodes at every stage boundary
     ctx.profile(timing=1, reset=True)
-    hist = np.zeros(E, np.int64)
-    U_sum = 0
-    for _ in range(args.profile_steps):
-        x.copy_(x0)
-        for l in range(L):
-            ctx.block_device(l, x, stream=stream)
-            h = ctx.expert_histogram()
-            hist += h
-            U_sum += int((h > 0).sum())
-    prof = ctx.profile(timing=0, reset=True)
-    calls = args.profile_steps * L
-    U = U_sum / calls
+    gp = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gp):
+        step()
+    prof_launch = ctx.profile(timing=-1)["stage_launches"]
+    stage_ms = {}
+    with torch.cuda.stream(s):
+        for _ in range(args.profile_steps):
+            gp.replay()
+            torch.cuda.synchronize()
+            for n, v in ctx.profile()["stage_ms"].items():
+                stage_ms[n] = stage_ms.get(n, 0.0) + v
+    ctx.profile(timing=0, reset=True)
+    del gp
     S = T * K
-    bytes_per = stage_bytes(T, U, S)
-    per_launch_ms = {n: prof["stage_ms"][n] / max(prof["stage_launches"][n], 1) for n in bytes_per}
-    dom = max(per_launch_ms, key=lambda n: prof["stage_ms"][n])
+    bytes_per, flops_per = stage_cost(T, U, S)
+    per_launch_ms = {n: stage_ms[n] / (prof_launch[n] * args.profile_steps)
+                     for n in bytes_per if prof_launch.get(n)}
+    dom = max(per_launch_ms, key=lambda n: per_launch_ms[n] * prof_launch[n])
     hbm, bf16, src = peaks()
-    achieved = bytes_per[dom] / (per_launch_ms[dom] / 1e3) / 1e9
     layer_bytes = E * D * 2 + U * 3 * H * D * 2 + T * D * 4 * 2 + T * K * 8
+    layer_flops = T * (2 * E * D + 6 * K * H * D)
     layer_ms = ms / L
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "peak_source": src, "traffic": None,
-                "algorithmic_bytes_per_launch": bytes_per[dom], "avg_launch_ms": per_launch_ms[dom],
+    t_dom = per_launch_ms[dom] / 1e3
+    gbs = bytes_per[dom] / t_dom / 1e9
+    tfs = flops_per.get(dom, 0) / t_dom / 1e12
+    tensor_bound = tfs / bf16 > gbs / hbm
+    roofline = {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom,
+                "achieved": tfs if tensor_bound else gbs, "peak": bf16 if tensor_bound else hbm,
+                "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                "frac": (tfs / bf16) if tensor_bound else (gbs / hbm), "peak_source": src, "traffic": None,
+                "algorithmic_bytes_per_launch": bytes_per[dom], "algorithmic_flops_per_launch": flops_per.get(dom, 0),
+                "avg_launch_ms": per_launch_ms[dom],
                 "stage_ms_per_launch": per_launch_ms,
+                "stage_share": {n: per_launch_ms[n] * prof_launch[n] / sum(per_launch_ms[k] * prof_launch[k]
+                                                                            for k in per_launch_ms)
+                                for n in per_launch_ms},
+                "timing": "CUDA events recorded as nodes of a captured graph of the step",
                 "layer": {"us_per_layer": layer_ms * 1e3, "algorithmic_bytes": layer_bytes,
-                          "achieved_gbs": layer_bytes / (layer_ms / 1e3) / 1e9,
-                          "frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm,
+                          "algorithmic_flops": layer_flops,
+                          "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm,
+                          "tensor_frac": layer_flops / (layer_ms / 1e3) / 1e12 / bf16,
                           "distinct_experts_per_layer": U}}
     out = None
     if rank == 0:
         out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_desc(args),
-               "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
-               "expert_histogram": hist.tolist()}
+               "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+               "roofline": roofline, "expert_histogram": hist.tolist()}
+    del g
     ctx.close()
     return out
 

@@ -83,8 +83,10 @@ int rbt_moe_ffn(RbtMoe *m, int layer, const float *xb, int n_tokens, float *moe_
                 int routing_stride);
 
 /* Device-pointer forms of the two calls above, enqueued on `stream` (a
- * cudaStream_t; NULL = the context's own stream) without synchronising.
- * x/xb/out/routing_out must be device pointers; xb may equal moe_out. */
+ * cudaStream_t, passed through as is: NULL is the CUDA default stream) without
+ * synchronising; they allocate nothing once rbt_moe_reserve covered n_tokens,
+ * so they can be captured into a CUDA graph.  x/xb/out/routing_out must be
+ * device pointers; xb may equal moe_out. */
 int rbt_moe_block_device(RbtMoe *m, int layer, float *d_x, int n_tokens, int32_t *d_routing_out,
                          int routing_stride, void *stream);
 int rbt_moe_ffn_device(RbtMoe *m, int layer, const float *d_xb, int n_tokens, float *d_moe_out,
@@ -104,10 +106,13 @@ int rbt_moe_set_path(RbtMoe *m, int path);
 
 /* Launch accounting and per-stage device timing.  Stages: 0 rmsnorm, 1 router +
  * top-k + permute, 2 gate/up + SwiGLU, 3 down, 4 combine, 5 operand gather
- * (GEMM path).  With timing enabled every call records CUDA events between its
- * kernels and waits for them, so time a run with timing off and profile
- * separately.  The reference's only timing is wall clock on stderr
- * (rabbit2.c:742-744). */
+ * (GEMM path).  With timing on, every call records a CUDA event at each stage
+ * boundary on its stream (as graph nodes when the stream is being captured)
+ * and nothing waits; stage_ms sums the intervals recorded since the last reset,
+ * read from the events' latest timestamps (so after a graph replay it holds
+ * that replay's times).  Event gaps include host launch latency unless the
+ * calls run from a CUDA graph.  The reference's only timing is wall clock on
+ * stderr (rabbit2.c:742-744). */
 #define RBT_MOE_STAGES 8
 typedef struct RbtMoeProfile {
     int64_t calls;                           /* MoE calls since the last reset */

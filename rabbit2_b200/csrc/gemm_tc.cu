@@ -1,0 +1,391 @@
+// gemm_tc.cu -- K4: grouped expert GEMM on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA) for prefill-sized batches.  Replaces the per-token
+// matvecs of rabbit2.c:534-538 when many tokens share an expert.
+//
+// Formulation ("swap AB"): the weight rows are the MMA's M = 128 side and the
+// routed tokens of one expert are its N side, so an expert with few tokens
+// wastes little work:
+//   gate/up:  [W1; W3] rows (128 of H each)  x  X_e^T   -> two 128 x BN accumulators,
+//             epilogue h = silu(g) * u, stored as bf16 hi + lo
+//   down:     W2 rows (128 of D)             x  H_e^T   -> one 128 x BN accumulator,
+//             epilogue y (f32)
+// Precision: weights are bf16 as stored in the model file.  Activations are f32
+// and are split into bf16 hi = rn(x) and lo = rn(x - hi) (16 significant bits);
+// each K step issues two MMAs (hi and lo) into the same f32 accumulator.  One
+// bf16 operand alone gives ~3e-3 relative error on this layer, over the 1e-3 bar.
+//
+// Pipeline per CTA (persistent, one CTA per SM, 192 threads):
+//   warp 0  TMA producer: weight tile via a 3-D map over the expert blobs
+//           (x = K, y = row, z = expert; no multicast), token tiles via 2-D maps
+//   warp 1  TMEM owner and MMA issuer (one thread), tcgen05.commit to mbarriers
+//   warps 2-5  epilogue: tcgen05.ld 32x32b, SwiGLU / split / store
+// Two TMEM accumulator buffers let the epilogue of tile i overlap the MMAs of
+// tile i+1.  Every mbarrier wait is bounded by %globaltimer; on timeout the
+// kernel records an error code in `status`, drains its in-flight copies and
+// MMAs (again bounded), frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_ptx.cuh"
+
+namespace rbt {
+namespace {
+
+using namespace tc;
+
+constexpr int kBM = 128;   // weight rows per tile (MMA M)
+constexpr int kBN = 128;   // routed tokens per tile (MMA N)
+constexpr int kBK = 64;    // K elements per stage = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB, also kBN * kBK * 2
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
+
+template <bool kGateUp>
+struct Cfg {
+    static constexpr int NA = kGateUp ? 2 : 1;                 // weight tiles per stage
+    static constexpr int kStageBytes = (NA + 2) * kTileBytes;  // + token hi + token lo
+    static constexpr int kStages = kGateUp ? 3 : 4;
+    static constexpr int kAccCols = NA * kBN;                  // TMEM columns per accumulator buffer
+    static constexpr int kTmemCols = 2 * kAccCols;             // double buffered (512 or 256)
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void record_error(unsigned* status, unsigned code) {
+    atomicCAS(status, 0u, code);
+}
+
+template <bool kGateUp>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_bhi,
+                       const __grid_constant__ CUtensorMap tm_blo, TcGemmArgs a) {
+    using C = Cfg<kGateUp>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* full = bars;                       // [kStages] TMA landed
+    uint64_t* empty = bars + C::kStages;         // [kStages] MMAs done reading
+    uint64_t* tfull = bars + 2 * C::kStages;     // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;                // [2] accumulator drained
+    uint64_t* done = tempty + 2;                 // [1] drain barrier for the MMA issuer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4 * 32);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tm_w);
+        prefetch_tmap(&tm_bhi);
+        prefetch_tmap(&tm_blo);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int n_tiles = *a.n_tb * a.MB;
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_parity[C::kStages];
+        bool used[C::kStages];
+        for (int s = 0; s < C::kStages; s++) used[s] = false;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+            const int tbi = tile / a.MB, mb = tile - tbi * a.MB;
+            const int e = a.tb_e[tbi], p0 = a.tb_p0[tbi];
+            for (int kb = 0; kb < a.KB; kb++) {
+                if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kWaitNs)) {
+                    record_error(a.status, 0x101);
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + stage * C::kStageBytes;
+                mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+                tma_load_3d(st, &tm_w, &full[stage], kb * kBK, mb * kBM, e);
+                if (kGateUp) tma_load_3d(st + kTileBytes, &tm_w, &full[stage], kb * kBK, a.H + mb * kBM, e);
+                tma_load_2d(st + C::NA * kTileBytes, &tm_bhi, &full[stage], kb * kBK, p0);
+                tma_load_2d(st + (C::NA + 1) * kTileBytes, &tm_blo, &full[stage], kb * kBK, p0);
+                used[stage] = true;
+                last_parity[stage] = phase;
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        // every copy this thread issued has landed before the CTA may exit
+        for (int s = 0; s < C::kStages; s++)
+            if (used[s] && !mbar_wait_bounded(&full[s], last_parity[s], kWaitNs)) record_error(a.status, 0x102);
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int buf = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+            if (!mbar_wait_bounded(&tempty[buf], acc_phase ^ 1u, kWaitNs)) {
+                record_error(a.status, 0x201);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d1 = tmem_base + buf * C::kAccCols;
+            for (int kb = 0; kb < a.KB; kb++) {
+                if (!mbar_wait_bounded(&full[stage], phase, kWaitNs)) {
+                    record_error(a.status, 0x202);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+                const uint32_t sbh = sa + C::NA * kTileBytes, sbl = sbh + kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; kk++) {
+                    const uint32_t koff = kk * 32;  // 16 bf16 = 32 bytes along K
+                    const uint64_t bh = sw128_kmajor_desc(sbh + koff), bl = sw128_kmajor_desc(sbl + koff);
+                    const uint64_t a1 = sw128_kmajor_desc(sa + koff);
+                    mma_bf16(d1, a1, bh, idesc, (kb | kk) != 0);
+                    mma_bf16(d1, a1, bl, idesc, 1u);
+                    if (kGateUp) {
+                        const uint64_t a3 = sw128_kmajor_desc(sa + kTileBytes + koff);
+                        mma_bf16(d1 + kBN, a3, bh, idesc, (kb | kk) != 0);
+                        mma_bf16(d1 + kBN, a3, bl, idesc, 1u);
+                    }
+                }
+                mma_commit(&empty[stage]);
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            mma_commit(&tfull[buf]);
+            if (++buf == 2) {
+                buf = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        // all MMAs issued by this thread have completed before TMEM is freed
+        mma_commit(done);
+        if (!mbar_wait_bounded(done, 0, kWaitNs)) record_error(a.status, 0x203);
+    } else if (warp >= 2) {
+        // ------------------------------------------------ epilogue (4 warps = 128 TMEM lanes)
+        const int q = warp & 3;          // TMEM lane quadrant this warp may access
+        const int row = q * 32 + lane;   // weight row within the tile
+        int buf = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int tbi = tile / a.MB, mb = tile - tbi * a.MB;
+            const int p0 = a.tb_p0[tbi], p1 = a.tb_p1[tbi];
+            const int ntok = min(kBN, p1 - p0);
+            bool ok = mbar_wait_bounded(&tfull[buf], acc_phase, kWaitNs);
+            ok = __all_sync(FULL_MASK, ok);
+            if (!ok) {
+                record_error(a.status, 0x301);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::kAccCols;
+            for (int j0 = 0; j0 < ntok; j0 += 32) {
+                uint32_t g[32];
+                tmem_ld_32x32b_x32(tbase + j0, g);
+                if (kGateUp) {
+                    uint32_t u[32];
+                    tmem_ld_32x32b_x32(tbase + kBN + j0, u);
+                    tmem_ld_wait();
+                    const int col = mb * kBM + row;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        const int p = p0 + j0 + jj;
+                        if (j0 + jj < ntok) {
+                            const float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
+                            const float hv = gv / (1.0f + expf(-gv)) * uv;
+                            const __nv_bfloat16 hi = __float2bfloat16_rn(hv);
+                            const __nv_bfloat16 lo = __float2bfloat16_rn(hv - __bfloat162float(hi));
+                            static_cast<__nv_bfloat16*>(a.h_hi)[(size_t)p * a.H + col] = hi;
+                            static_cast<__nv_bfloat16*>(a.h_lo)[(size_t)p * a.H + col] = lo;
+                        }
+                    }
+                } else {
+                    tmem_ld_wait();
+                    const int col = mb * kBM + row;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        const int p = p0 + j0 + jj;
+                        if (j0 + jj < ntok) a.y[(size_t)p * a.D + col] = __uint_as_float(g[jj]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[buf]);
+            if (++buf == 2) {
+                buf = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// f32 rows of x, gathered into expert order, split into bf16 hi + lo.
+__global__ void __launch_bounds__(256) gather_split_kernel(const float* __restrict__ xb, const int32_t* perm, int S,
+                                                           int D, int K, __nv_bfloat16* xhi, __nv_bfloat16* xlo) {
+    const int vpr = D / 8;
+    const long total = (long)S * vpr;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int p = (int)(i / vpr), v = (int)(i - (long)p * vpr);
+        const int t = perm[p] / K;
+        const float4* src = reinterpret_cast<const float4*>(xb + (size_t)t * D + v * 8);
+        const float4 f0 = __ldg(src), f1 = __ldg(src + 1);
+        const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+        __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            hi[q] = __float2bfloat16_rn(f[q]);
+            lo[q] = __float2bfloat16_rn(f[q] - __bfloat162float(hi[q]));
+        }
+        *reinterpret_cast<uint4*>(xhi + (size_t)p * D + v * 8) = *reinterpret_cast<const uint4*>(hi);
+        *reinterpret_cast<uint4*>(xlo + (size_t)p * D + v * 8) = *reinterpret_cast<const uint4*>(lo);
+    }
+}
+
+// Token blocks of kBN routed slots per active expert (one CTA, E <= 256).
+__global__ void __launch_bounds__(256) tc_schedule_kernel(const int32_t* counts, const int32_t* offsets, int E,
+                                                          int32_t* tb_e, int32_t* tb_p0, int32_t* tb_p1,
+                                                          int32_t* n_tb) {
+    __shared__ int32_t s_nt[kMaxExperts + 1];
+    const int e = threadIdx.x;
+    const int nt = (e < E) ? (counts[e] + kBN - 1) / kBN : 0;
+    s_nt[e] = nt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int i = 0; i < E; i++) {
+            const int c = s_nt[i];
+            s_nt[i] = run;
+            run += c;
+        }
+        s_nt[kMaxExperts] = run;
+        *n_tb = run;
+    }
+    __syncthreads();
+    if (e < E) {
+        const int base = s_nt[e], p_end = offsets[e + 1];
+        for (int j = 0; j < nt; j++) {
+            tb_e[base + j] = e;
+            tb_p0[base + j] = offsets[e] + j * kBN;
+            tb_p1[base + j] = p_end;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+template <bool kGateUp>
+cudaError_t launch_gemm(const CUtensorMap& w, const CUtensorMap& bhi, const CUtensorMap& blo, const TcGemmArgs& a,
+                        int grid, cudaStream_t s) {
+    using C = Cfg<kGateUp>;
+    cudaError_t err = cudaFuncSetAttribute(moe_tc_gemm_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    moe_tc_gemm_kernel<kGateUp><<<grid, kThreads, C::kSmemBytes, s>>>(w, bhi, blo, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int tc_block_n() { return kBN; }
+
+bool tc_supported(int D, int H, int dtype) {
+    return dtype == 1 && D % kBM == 0 && H % kBM == 0 && D % kBK == 0 && H % kBK == 0 && encode_fn() != nullptr;
+}
+
+// Row-major bf16 matrix [rows, cols] as a 2-D TMA map with a kBK x box_rows box.
+bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Per-expert row-major bf16 matrices [rows, cols] `stride` bytes apart as a 3-D
+// map (x = column, y = row, z = expert) with a kBK x kBM x 1 box.
+bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)E};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)stride};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)kBM, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
+                                cudaStream_t s) {
+    if (S <= 0) return cudaSuccess;
+    const long total = (long)S * (D / 8);
+    const long blocks = (total + 255) / 256;
+    gather_split_kernel<<<(int)(blocks < 148L * 8 ? blocks : 148L * 8), 256, 0, s>>>(
+        xb, perm, S, D, K, static_cast<__nv_bfloat16*>(xhi), static_cast<__nv_bfloat16*>(xlo));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int32_t* tb_e, int32_t* tb_p0,
+                               int32_t* tb_p1, int32_t* n_tb, cudaStream_t s) {
+    tc_schedule_kernel<<<1, 256, 0, s>>>(counts, offsets, E, tb_e, tb_p0, tb_p1, n_tb);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tc_gateup(const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
+                             const TcGemmArgs& a, int grid, cudaStream_t s) {
+    return launch_gemm<true>(w, xhi, xlo, a, grid, s);
+}
+
+cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const CUtensorMap& hlo, const TcGemmArgs& a,
+                           int grid, cudaStream_t s) {
+    return launch_gemm<false>(w, hhi, hlo, a, grid, s);
+}
+
+}  // namespace rbt

@@ -1,6 +1,7 @@
 // kernels.h -- internal launch interface of the MoE kernels (not part of the C ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -63,5 +64,32 @@ struct CombineArgs {
 };
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s);
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, int D, float eps, cudaStream_t s);
+
+// K4: tcgen05 grouped GEMM (gemm_tc.cu).
+struct TcGemmArgs {
+    const int32_t* tb_e;      // [n_tb] expert of each token block
+    const int32_t* tb_p0;     // [n_tb] first slot position of the block
+    const int32_t* tb_p1;     // [n_tb] end of the expert's slot range
+    const int32_t* n_tb;      // [1]
+    int MB;                   // 128-row weight blocks per token block (H/128 gate/up, D/128 down)
+    int KB;                   // 64-element K blocks (D/64 gate/up, H/64 down)
+    int H, D;
+    void* h_hi;               // [S_cap, H] bf16 (gate/up output)
+    void* h_lo;
+    float* y;                 // [S_cap, D] f32 (down output)
+    unsigned* status;         // 0, or the code of a timed-out pipeline wait
+};
+int tc_block_n();
+bool tc_supported(int D, int H, int dtype);
+bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int box_rows);
+bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride);
+cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
+                                cudaStream_t s);
+cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int32_t* tb_e, int32_t* tb_p0,
+                               int32_t* tb_p1, int32_t* n_tb, cudaStream_t s);
+cudaError_t launch_tc_gateup(const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
+                             const TcGemmArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const CUtensorMap& hlo, const TcGemmArgs& a,
+                           int grid, cudaStream_t s);
 
 }  // namespace rbt

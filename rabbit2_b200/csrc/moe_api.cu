@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <new>
@@ -48,6 +49,9 @@ struct Layer {
     const uint8_t* experts = nullptr;
     float* bias = nullptr;        // device [E] or null
     void* owned = nullptr;        // allocation made by rbt_moe_load_layer
+    bool tc = false;              // tensor maps below are valid
+    CUtensorMap w_gateup;         // [E][2H][D] bf16 rows (w1 then w3), 3-D
+    CUtensorMap w_down;           // [E][D][H] bf16 rows (w2), 3-D
 };
 
 struct Workspace {
@@ -55,19 +59,31 @@ struct Workspace {
     void* block = nullptr;
     float *xb, *logits, *wt, *h, *y, *hx, *hout;
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active, *hrouting;
-    unsigned *tile_counter, *done_counter;
+    unsigned *tile_counter, *done_counter, *status;
+    // tcgen05 path: split-bf16 operands in expert order and the token-block list
+    void *xhi, *xlo, *hhi, *hlo;
+    int32_t *tb_e, *tb_p0, *tb_p1, *n_tb;
+    bool tc_maps = false;
+    CUtensorMap m_xhi, m_xlo, m_hhi, m_hlo;
 };
 
 }  // namespace
+
+struct StageMark {
+    int stage, ev_begin, ev_end;  // indices into the event pool
+};
 
 struct RbtMoe {
     RbtMoeConfig cfg;
     bool timing = false;
     RbtMoeProfile prof{};
-    cudaEvent_t ev[RBT_MOE_STAGES + 1] = {};
+    std::vector<cudaEvent_t> ev_pool;  // timing events, created when timing is switched on
+    int ev_used = 0;
+    std::vector<StageMark> marks;      // stage intervals recorded since the last reset
     int device = 0;
     int sm_count = 0;
     int path = 0;
+    int gemm_min_tokens = 64;  // automatic path: tensor-core GEMM from this many tokens
     size_t esz = 2;
     cudaStream_t stream = nullptr;
     std::vector<Layer> layers;
@@ -89,10 +105,19 @@ int reserve(RbtMoe* m, int T) {
     const RbtMoeConfig& c = m->cfg;
     const size_t D = c.dim, E = c.n_experts, K = c.top_k, H = c.expert_hidden, S = (size_t)T * K;
     const size_t tiles = (size_t)rbt::router_token_tiles(T) + 1;
+    const size_t ntb = S / rbt::tc_block_n() + E + 1;
+    const bool tc = rbt::tc_supported(c.dim, c.expert_hidden, c.dtype);
+    // split-bf16 operand rows: at least one full 128-row TMA box, whole boxes
+    const size_t SB = tc ? ((S > 128 ? S : 128) + 127) / 128 * 128 : 0;
     struct Part { void** p; size_t bytes; };
     Workspace w;
     w.cap = T;
     std::vector<Part> parts = {
+        {(void**)&w.xhi, SB * D * 2},            {(void**)&w.xlo, SB * D * 2},
+        {(void**)&w.hhi, SB * H * 2},            {(void**)&w.hlo, SB * H * 2},
+        {(void**)&w.tb_e, ntb * 4},              {(void**)&w.tb_p0, ntb * 4},
+        {(void**)&w.tb_p1, ntb * 4},             {(void**)&w.n_tb, 4},
+        {(void**)&w.status, 4},
         {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
         {(void**)&w.wt, S * 4},                  {(void**)&w.h, S * H * 4},
         {(void**)&w.y, S * D * 4},               {(void**)&w.hx, (size_t)T * D * 4},
@@ -121,11 +146,31 @@ int reserve(RbtMoe* m, int T) {
     CU(cudaMemsetAsync(w.tile_counter, 0, tiles * 4, m->stream));
     CU(cudaMemsetAsync(w.done_counter, 0, 4, m->stream));
     CU(cudaMemsetAsync(w.counts, 0, E * 4, m->stream));
+    CU(cudaMemsetAsync(w.status, 0, 4, m->stream));
     CU(cudaStreamSynchronize(m->stream));
+    if (tc) {
+        w.tc_maps = rbt::make_map_2d(&w.m_xhi, w.xhi, c.dim, (long)SB, rbt::tc_block_n()) &&
+                    rbt::make_map_2d(&w.m_xlo, w.xlo, c.dim, (long)SB, rbt::tc_block_n()) &&
+                    rbt::make_map_2d(&w.m_hhi, w.hhi, c.expert_hidden, (long)SB, rbt::tc_block_n()) &&
+                    rbt::make_map_2d(&w.m_hlo, w.hlo, c.expert_hidden, (long)SB, rbt::tc_block_n());
+    }
     if (m->ws.block) CU(cudaFree(m->ws.block));
     w.block = block;
     m->ws = w;
     return 1;
+}
+
+// Tensor maps of the layer's expert blobs for the tcgen05 path (bf16 only).
+void layer_maps(RbtMoe* m, Layer& L) {
+    const RbtMoeConfig& c = m->cfg;
+    L.tc = false;
+    if (!rbt::tc_supported(c.dim, c.expert_hidden, c.dtype) || (c.expert_stride % 16) != 0 ||
+        (reinterpret_cast<uintptr_t>(L.experts) % 16) != 0)
+        return;
+    L.tc = rbt::make_map_experts(&L.w_gateup, L.experts, c.dim, 2 * c.expert_hidden, c.n_experts,
+                                 c.expert_stride) &&
+           rbt::make_map_experts(&L.w_down, L.experts + (size_t)2 * c.expert_hidden * c.dim * 2, c.expert_hidden,
+                                 c.dim, c.n_experts, c.expert_stride);
 }
 
 int check_layer(RbtMoe* m, int layer, bool need_norm) {
@@ -137,29 +182,35 @@ int check_layer(RbtMoe* m, int layer, bool need_norm) {
     return 1;
 }
 
-// Stage bookkeeping: count every launch; with timing on, bracket stages with
-// events on the launching stream.
+// Stage bookkeeping: count every launch; with timing on, record an event at
+// every stage boundary on the launching stream (cudaEventRecordExternal, so the
+// records become graph nodes under stream capture).  Nothing waits here; the
+// intervals are read by rbt_moe_profile.
 struct StageClock {
     RbtMoe* m;
     cudaStream_t s;
-    int last = -1;
     int open_stage = -1;
+    int open_ev = -1;
+    int mark() {
+        if (m->ev_used >= (int)m->ev_pool.size()) return -1;  // pool exhausted: stop recording
+        const int i = m->ev_used++;
+        if (cudaEventRecordWithFlags(m->ev_pool[i], s, cudaEventRecordExternal) != cudaSuccess) return -1;
+        return i;
+    }
     int begin(int stage) {
         m->prof.launches++;
         m->prof.stage_launches[stage]++;
         if (!m->timing) return 1;
-        if (open_stage >= 0 && !end()) return 0;
-        CU(cudaEventRecord(m->ev[0], s));
+        const int e = mark();
+        if (open_stage >= 0 && open_ev >= 0 && e >= 0) m->marks.push_back({open_stage, open_ev, e});
         open_stage = stage;
+        open_ev = e;
         return 1;
     }
     int end() {
         if (!m->timing || open_stage < 0) return 1;
-        CU(cudaEventRecord(m->ev[1], s));
-        CU(cudaEventSynchronize(m->ev[1]));
-        float ms = 0.f;
-        CU(cudaEventElapsedTime(&ms, m->ev[0], m->ev[1]));
-        m->prof.stage_ms[open_stage] += ms;
+        const int e = mark();
+        if (open_ev >= 0 && e >= 0) m->marks.push_back({open_stage, open_ev, e});
         open_stage = -1;
         return 1;
     }
@@ -198,15 +249,38 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     if (!clk.begin(1)) return 0;
     CU(rbt::launch_router(ra, s));
 
-    rbt::GemvArgs ga{};
-    ga.xb = xb; ga.experts = L.experts; ga.stride = c.expert_stride;
-    ga.T = T; ga.D = c.dim; ga.H = c.expert_hidden; ga.E = c.n_experts; ga.K = c.top_k; ga.dtype = c.dtype;
-    ga.perm = w.perm; ga.offsets = w.offsets; ga.active = w.active; ga.n_active = w.n_active;
-    ga.h = w.h; ga.y = w.y; ga.grid = m->sm_count;
-    if (!clk.begin(2)) return 0;
-    CU(rbt::launch_gateup_gemv(ga, s));
-    if (!clk.begin(3)) return 0;
-    CU(rbt::launch_down_gemv(ga, s));
+    // the split kernel reads xb with 16-byte vectors
+    const bool tc_ready = L.tc && w.tc_maps && (reinterpret_cast<uintptr_t>(xb) % 16 == 0);
+    if (m->path == 2 && !tc_ready)
+        return fail("tensor-core path requested but unavailable (needs bf16 weights, D and H multiples of 128, "
+                    "16-byte aligned input)");
+    const bool use_tc = tc_ready && (m->path == 2 || (m->path == 0 && T >= m->gemm_min_tokens));
+    if (use_tc) {
+        const int S = T * c.top_k;
+        if (!clk.begin(5)) return 0;
+        CU(rbt::launch_gather_split(xb, w.perm, S, c.dim, c.top_k, w.xhi, w.xlo, s));
+        CU(rbt::launch_tc_schedule(w.counts, w.offsets, c.n_experts, w.tb_e, w.tb_p0, w.tb_p1, w.n_tb, s));
+        m->prof.launches++;
+        rbt::TcGemmArgs ta{};
+        ta.tb_e = w.tb_e; ta.tb_p0 = w.tb_p0; ta.tb_p1 = w.tb_p1; ta.n_tb = w.n_tb;
+        ta.H = c.expert_hidden; ta.D = c.dim; ta.h_hi = w.hhi; ta.h_lo = w.hlo; ta.y = w.y; ta.status = w.status;
+        ta.MB = c.expert_hidden / 128; ta.KB = c.dim / 64;
+        if (!clk.begin(2)) return 0;
+        CU(rbt::launch_tc_gateup(L.w_gateup, w.m_xhi, w.m_xlo, ta, m->sm_count, s));
+        ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
+        if (!clk.begin(3)) return 0;
+        CU(rbt::launch_tc_down(L.w_down, w.m_hhi, w.m_hlo, ta, m->sm_count, s));
+    } else {
+        rbt::GemvArgs ga{};
+        ga.xb = xb; ga.experts = L.experts; ga.stride = c.expert_stride;
+        ga.T = T; ga.D = c.dim; ga.H = c.expert_hidden; ga.E = c.n_experts; ga.K = c.top_k; ga.dtype = c.dtype;
+        ga.perm = w.perm; ga.offsets = w.offsets; ga.active = w.active; ga.n_active = w.n_active;
+        ga.h = w.h; ga.y = w.y; ga.grid = m->sm_count;
+        if (!clk.begin(2)) return 0;
+        CU(rbt::launch_gateup_gemv(ga, s));
+        if (!clk.begin(3)) return 0;
+        CU(rbt::launch_down_gemv(ga, s));
+    }
 
     rbt::CombineArgs ca{};
     ca.resid = block ? x : nullptr;
@@ -216,6 +290,18 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     if (!clk.begin(4)) return 0;
     CU(rbt::launch_combine(ca, s));
     return clk.end();
+}
+
+// A tensor-core pipeline wait that timed out leaves a code in the status word.
+int check_status(RbtMoe* m) {
+    if (!m->ws.block) return 1;
+    unsigned st = 0;
+    CU(cudaMemcpy(&st, m->ws.status, 4, cudaMemcpyDeviceToHost));
+    if (st) {
+        CU(cudaMemset(m->ws.status, 0, 4));
+        return fail("tensor-core GEMM pipeline wait timed out (code 0x%x)", st);
+    }
+    return 1;
 }
 
 // Host-pointer wrapper: stage through the workspace's device buffers.
@@ -237,7 +323,7 @@ int forward_host(RbtMoe* m, int layer, const float* x, float* out, int T, int32_
         CU(cudaMemcpy2DAsync(routing, (size_t)routing_stride * 4, w.hrouting, (size_t)c.top_k * 4,
                              (size_t)c.top_k * 4, T, cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
-    return 1;
+    return check_status(m);
 }
 
 }  // namespace
@@ -267,10 +353,10 @@ int rbt_moe_create(RbtMoe** out, const RbtMoeConfig* cfg, int device) {
     m->cfg = c;
     m->device = device;
     m->esz = esz;
+    if (const char* v = getenv("RBT_MOE_GEMM_MIN_TOKENS")) m->gemm_min_tokens = atoi(v);
     m->layers.resize(c.n_layers);
     bool ok = cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device) == cudaSuccess &&
               cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
-    for (int i = 0; ok && i < 2; i++) ok = cudaEventCreate(&m->ev[i]) == cudaSuccess;
     if (!ok) {
         delete m;
         return fail("cannot initialise CUDA device %d", device);
@@ -288,8 +374,7 @@ void rbt_moe_destroy(RbtMoe* m) {
         cudaFree(L.bias);
     }
     cudaFree(m->ws.block);
-    for (int i = 0; i < 2; i++)
-        if (m->ev[i]) cudaEventDestroy(m->ev[i]);
+    for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
     cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -316,6 +401,7 @@ int rbt_moe_load_layer(RbtMoe* m, int layer, const float* ffn_norm, const void* 
     L.experts = (const uint8_t*)p;
     L.router = (char*)p + o_router;
     L.ffn_norm = ffn_norm ? (const float*)((char*)p + o_norm) : nullptr;
+    layer_maps(m, L);
     return 1;
 }
 
@@ -330,6 +416,7 @@ int rbt_moe_bind_layer(RbtMoe* m, int layer, const float* d_ffn_norm, const void
     L.ffn_norm = d_ffn_norm;
     L.router = d_router;
     L.experts = (const uint8_t*)d_experts;
+    layer_maps(m, L);
     return 1;
 }
 
@@ -367,16 +454,14 @@ int rbt_moe_block_device(RbtMoe* m, int layer, float* d_x, int n_tokens, int32_t
                          void* stream) {
     if (!m) return fail("null context");
     if (!d_x && n_tokens > 0) return fail("null x");
-    return forward(m, layer, d_x, d_x, n_tokens, d_routing_out, routing_stride,
-                   stream ? (cudaStream_t)stream : m->stream, true);
+    return forward(m, layer, d_x, d_x, n_tokens, d_routing_out, routing_stride, (cudaStream_t)stream, true);
 }
 
 int rbt_moe_ffn_device(RbtMoe* m, int layer, const float* d_xb, int n_tokens, float* d_moe_out,
                        int32_t* d_routing_out, int routing_stride, void* stream) {
     if (!m) return fail("null context");
     if ((!d_xb || !d_moe_out) && n_tokens > 0) return fail("null xb/moe_out");
-    return forward(m, layer, d_xb, d_moe_out, n_tokens, d_routing_out, routing_stride,
-                   stream ? (cudaStream_t)stream : m->stream, false);
+    return forward(m, layer, d_xb, d_moe_out, n_tokens, d_routing_out, routing_stride, (cudaStream_t)stream, false);
 }
 
 int rbt_moe_expert_histogram(RbtMoe* m, int32_t* counts_out) {
@@ -393,9 +478,27 @@ int rbt_moe_expert_histogram(RbtMoe* m, int32_t* counts_out) {
 
 int rbt_moe_profile(RbtMoe* m, int timing, int reset, RbtMoeProfile* out) {
     if (!m) return fail("null context");
-    if (out) *out = m->prof;
-    if (reset) m->prof = RbtMoeProfile{};
+    if (!set_device(m)) return 0;
+    if (out) {
+        *out = m->prof;
+        for (int i = 0; i < RBT_MOE_STAGES; i++) out->stage_ms[i] = 0.0;
+        for (const StageMark& k : m->marks) {
+            float ms = 0.f;
+            CU(cudaEventSynchronize(m->ev_pool[k.ev_end]));
+            CU(cudaEventElapsedTime(&ms, m->ev_pool[k.ev_begin], m->ev_pool[k.ev_end]));
+            out->stage_ms[k.stage] += ms;
+        }
+    }
+    if (reset) {
+        m->prof = RbtMoeProfile{};
+        m->marks.clear();
+        m->ev_used = 0;
+    }
     if (timing >= 0) m->timing = timing != 0;
+    if (m->timing && m->ev_pool.empty()) {
+        m->ev_pool.resize(4096);
+        for (cudaEvent_t& e : m->ev_pool) CU(cudaEventCreate(&e));
+    }
     return 1;
 }
 

@@ -241,7 +241,19 @@ __global__ void __launch_bounds__(kThreads) router_small_kernel(RouterArgs a) {
         const float* wr = ws + el * kSmallStride;
         const float* xr = xs + tl * kSmallStride;
         const int main_end = min(cols, D4 - c0);  // columns of this chunk in the 4-chain part
-        for (int i = c; i < main_end; i += 4) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
+        // eight chain steps per pass: the loads run ahead, the adds keep their order
+        int i = c;
+        for (; i + 28 < main_end; i += 32) {
+            float w[8], x[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                w[u] = wr[i + 4 * u];
+                x[u] = xr[i + 4 * u];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) s = __fadd_rn(s, __fmul_rn(w[u], x[u]));
+        }
+        for (; i < main_end; i += 4) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
         if (c == 0)
             for (int i = max(main_end, 0); i < cols; i++) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
     }

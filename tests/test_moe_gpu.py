@@ -19,8 +19,10 @@ from oracle.oracle import MoeLayerHost, Oracle  # noqa: E402
 from rabbit2_b200 import moe, workload  # noqa: E402
 from tests.golden.cases import case_keys, load_case, pack_layer  # noqa: E402
 
-MOE_RTOL = 2e-5      # what fp32 accumulation in a different order reaches at these sizes
+MOE_RTOL = 2e-5      # CUDA-core path: fp32 accumulation in a different order
+MOE_RTOL_TC = 1e-4   # tensor-core path: bf16 hi+lo split activations (16 significant bits)
 NORTH_STAR = 1e-3
+GEMM_MIN_TOKENS = 64  # automatic path switch of librbt_moe (RBT_MOE_GEMM_MIN_TOKENS)
 
 
 def rel_err(got, want):
@@ -106,7 +108,7 @@ def test_olmoe_layer_vs_oracle(orc, olmoe, T):
     _, _, probs = orc.router_topk(host, xh)
     assert_routing(routing.cpu().numpy(), want_r, probs)
     err = rel_err(out.cpu().numpy(), want)
-    assert err < MOE_RTOL, err
+    assert err < (MOE_RTOL_TC if T >= GEMM_MIN_TOKENS else MOE_RTOL), err
     counts = ctx.expert_histogram()
     np.testing.assert_array_equal(counts, np.bincount(want_r.ravel(), minlength=64))
 
@@ -125,7 +127,7 @@ def test_olmoe_zipf_routing(orc, T):
         want, want_r, _ = orc.moe_ffn(host, xh, nthreads=8)
         _, _, probs = orc.router_topk(host, xh)
         assert_routing(routing.cpu().numpy(), want_r, probs)
-        assert rel_err(out.cpu().numpy(), want) < MOE_RTOL
+        assert rel_err(out.cpu().numpy(), want) < (MOE_RTOL_TC if T >= GEMM_MIN_TOKENS else MOE_RTOL)
     finally:
         ctx.close()
 
@@ -145,7 +147,7 @@ def test_olmoe_large_batch_routing_and_sampled_outputs(orc, olmoe):
     assert_routing(routing.cpu().numpy(), want_r, probs)
     sample = np.random.default_rng(0).choice(T, 48, replace=False)
     want, _, _ = orc.moe_ffn(host, xh[sample], nthreads=8)
-    assert rel_err(out.cpu().numpy()[sample], want) < MOE_RTOL
+    assert rel_err(out.cpu().numpy()[sample], want) < MOE_RTOL_TC
     # a size-independent property: the histogram sums to T*K
     assert ctx.expert_histogram().sum() == T * 8
 
@@ -176,3 +178,80 @@ def test_zero_tokens_and_bad_arguments(olmoe):
                        torch.empty(1, 8, dtype=torch.int32, device="cuda"), routing_stride=4)
     with pytest.raises(moe.RbtMoeError, match="ffn_norm"):
         ctx.block(0, np.zeros((1, 2048), np.float32))
+
+
+@pytest.mark.parametrize("T", [1, 5, 16, 64, 130, 256])
+def test_tensor_core_path_vs_oracle(orc, olmoe, T):
+    """The tcgen05 grouped GEMM forced on at every size, including single-token experts
+    and token blocks that end mid-tile."""
+    ctx, host = olmoe
+    ctx.set_path(moe.PATH_GEMM)
+    try:
+        x = workload.inputs(T, 2048, seed=300 + T)
+        out = torch.empty_like(x)
+        routing = torch.empty(T, 8, dtype=torch.int32, device="cuda")
+        ctx.ffn_device(0, x, out, routing)
+        torch.cuda.synchronize()
+        xh = x.cpu().numpy()
+        want, want_r, _ = orc.moe_ffn(host, xh, nthreads=8)
+        _, _, probs = orc.router_topk(host, xh)
+        assert_routing(routing.cpu().numpy(), want_r, probs)
+        err = rel_err(out.cpu().numpy(), want)
+        assert err < MOE_RTOL_TC, err
+        # the host call reports a timed-out pipeline wait as an error; none here
+        ctx.ffn(0, xh[:1])
+    finally:
+        ctx.set_path(moe.PATH_AUTO)
+
+
+def test_tensor_core_and_gemv_paths_agree(olmoe):
+    """Both paths on the same 512 tokens (Zipf-skewed experts get several token blocks)."""
+    ctx, _ = olmoe
+    T = 512
+    x = workload.inputs(T, 2048, seed=77)
+    outs = []
+    for path in (moe.PATH_GEMV, moe.PATH_GEMM):
+        ctx.set_path(path)
+        o = torch.empty_like(x)
+        ctx.ffn_device(0, x, o)
+        outs.append(o)
+    ctx.set_path(moe.PATH_AUTO)
+    torch.cuda.synchronize()
+    assert rel_err(outs[1].cpu().numpy(), outs[0].cpu().numpy().astype(np.float64)) < MOE_RTOL_TC
+
+
+def test_tensor_core_path_small_shape_zipf(orc):
+    """A second bf16 shape (D 256, H 512, 8 experts, top-2) with a skewed router."""
+    D, H, E, K = 256, 512, 8, 2
+    router, experts, stride = workload.device_layer(D, H, E, seed=21)
+    bias = workload.zipf_bias(E, 1.2, seed=2)
+    ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_BF16, 1, stride)
+    try:
+        ctx.bind_layer(0, router, experts)
+        ctx.set_router_bias(0, bias)
+        ctx.set_path(moe.PATH_GEMM)
+        r_h, e_h = workload.host_copy(router, experts)
+        host = MoeLayerHost(D, H, E, K, moe.DT_BF16, 1, r_h, e_h, stride, router_bias=bias)
+        for T in (3, 200, 700):
+            x = workload.inputs(T, D, seed=T)
+            got, got_r = ctx.ffn(0, x.cpu().numpy())
+            want, want_r, _ = orc.moe_ffn(host, x.cpu().numpy(), nthreads=8)
+            _, _, probs = orc.router_topk(host, x.cpu().numpy())
+            assert_routing(got_r, want_r, probs)
+            assert rel_err(got, want) < MOE_RTOL_TC
+    finally:
+        ctx.close()
+
+
+def test_tensor_core_path_rejects_f32_weights():
+    D, H, E, K = 256, 512, 8, 2
+    from rabbit2_b200.rbt2fmt import ModelConfig, expert_stride
+    stride = expert_stride(ModelConfig(dim=D, expert_hidden=H, dtype=moe.DT_F32))
+    ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_F32, 0, stride)
+    try:
+        ctx.load_layer(0, np.zeros((E, D), np.float32), np.zeros((E, stride), np.uint8))
+        ctx.set_path(moe.PATH_GEMM)
+        with pytest.raises(moe.RbtMoeError, match="tensor-core path"):
+            ctx.ffn(0, np.ones((4, D), np.float32))
+    finally:
+        ctx.close()
