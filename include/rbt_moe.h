@@ -100,8 +100,10 @@ int rbt_moe_reserve(RbtMoe *m, int n_tokens);
  * (host pointer), in the key=value spirit of the engine's cache counters. */
 int rbt_moe_expert_histogram(RbtMoe *m, int32_t *counts_out);
 
-/* Force the path for later calls: 0 automatic (default), 1 the CUDA-core GEMV
- * path, 2 the tcgen05 grouped-GEMM path (needs D, H multiples of 64, bf16). */
+/* Force the path for later calls: 0 automatic (default), 1 CUDA-core GEMV
+ * (weight streaming through shared memory when the shapes allow it), 2 the
+ * tcgen05 grouped GEMM (bf16, D and H multiples of 128), 3 the plain CUDA-core
+ * GEMV with a separate combine (any dtype and shape). */
 int rbt_moe_set_path(RbtMoe *m, int path);
 
 /* Launch accounting and per-stage device timing.  Stages: 0 rmsnorm, 1 router +

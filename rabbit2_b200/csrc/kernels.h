@@ -65,6 +65,27 @@ struct CombineArgs {
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s);
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, int D, float eps, cudaStream_t s);
 
+// K3 (decode, bf16): bulk-copy weight streaming (gemv_stream.cu).
+struct StreamArgs {
+    const float* xb;          // [T, D] normalised input
+    const float* resid;       // [T, D] residual (block form) or nullptr
+    float* out;               // [T, D] output (may alias resid)
+    const uint8_t* experts;
+    size_t stride;
+    int T, D, H, K;
+    const int32_t* perm;
+    const int32_t* offsets;
+    const int32_t* active;
+    const int32_t* n_active;
+    const int32_t* slot_pos;
+    const float* wt;
+    float* h;                 // [T*K, H]
+    unsigned* status;
+};
+bool stream_supported(const StreamArgs& a, int dtype);
+cudaError_t launch_gateup_stream(const StreamArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_down_combine_stream(const StreamArgs& a, int grid, cudaStream_t s);
+
 // K4: tcgen05 grouped GEMM (gemm_tc.cu).
 struct TcGemmArgs {
     const int32_t* tb_e;      // [n_tb] expert of each token block

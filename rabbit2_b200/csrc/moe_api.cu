@@ -216,6 +216,18 @@ struct StageClock {
     }
 };
 
+rbt::StreamArgs sa_of(RbtMoe* m, const Layer& L, const float* xb, const float* x, float* out, int T, bool block) {
+    const RbtMoeConfig& c = m->cfg;
+    const Workspace& w = m->ws;
+    rbt::StreamArgs a{};
+    a.xb = xb; a.resid = block ? x : nullptr; a.out = block ? const_cast<float*>(x) : out;
+    a.experts = L.experts; a.stride = c.expert_stride;
+    a.T = T; a.D = c.dim; a.H = c.expert_hidden; a.K = c.top_k;
+    a.perm = w.perm; a.offsets = w.offsets; a.active = w.active; a.n_active = w.n_active;
+    a.slot_pos = w.slot_pos; a.wt = w.wt; a.h = w.h; a.status = w.status;
+    return a;
+}
+
 // The whole MoE call on device pointers.  block: x is the residual stream,
 // updated in place; otherwise out = moe(xb).
 int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* routing, int routing_stride,
@@ -270,6 +282,13 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
         if (!clk.begin(3)) return 0;
         CU(rbt::launch_tc_down(L.w_down, w.m_hhi, w.m_hlo, ta, m->sm_count, s));
+    } else if (m->path != 3 && rbt::stream_supported(sa_of(m, L, xb, x, out, T, block), c.dtype)) {
+        const rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, block);
+        if (!clk.begin(2)) return 0;
+        CU(rbt::launch_gateup_stream(sa, m->sm_count, s));
+        if (!clk.begin(3)) return 0;
+        CU(rbt::launch_down_combine_stream(sa, m->sm_count, s));
+        return clk.end();
     } else {
         rbt::GemvArgs ga{};
         ga.xb = xb; ga.experts = L.experts; ga.stride = c.expert_stride;
@@ -483,9 +502,14 @@ int rbt_moe_profile(RbtMoe* m, int timing, int reset, RbtMoeProfile* out) {
         *out = m->prof;
         for (int i = 0; i < RBT_MOE_STAGES; i++) out->stage_ms[i] = 0.0;
         for (const StageMark& k : m->marks) {
+            // intervals whose events carry no timestamp yet (a captured graph not
+            // replayed so far) contribute nothing
             float ms = 0.f;
-            CU(cudaEventSynchronize(m->ev_pool[k.ev_end]));
-            CU(cudaEventElapsedTime(&ms, m->ev_pool[k.ev_begin], m->ev_pool[k.ev_end]));
+            if (cudaEventSynchronize(m->ev_pool[k.ev_end]) != cudaSuccess ||
+                cudaEventElapsedTime(&ms, m->ev_pool[k.ev_begin], m->ev_pool[k.ev_end]) != cudaSuccess) {
+                (void)cudaGetLastError();
+                continue;
+            }
             out->stage_ms[k.stage] += ms;
         }
     }
@@ -504,7 +528,7 @@ int rbt_moe_profile(RbtMoe* m, int timing, int reset, RbtMoeProfile* out) {
 
 int rbt_moe_set_path(RbtMoe* m, int path) {
     if (!m) return fail("null context");
-    if (path < 0 || path > 2) return fail("path must be 0, 1 or 2");
+    if (path < 0 || path > 3) return fail("path must be 0, 1, 2 or 3");
     m->path = path;
     return 1;
 }

@@ -150,3 +150,28 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 
 }  // namespace tc
 }  // namespace rbt
+
+namespace rbt {
+namespace tc {
+
+// 1-D bulk copy global -> shared (the non-tensor TMA form), completion counted
+// in bytes on `bar`.  dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Named barrier over `count` threads (a subset of the CTA).
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Programmatic dependent launch: wait for the preceding kernel's results /
+// let the next kernel in the stream begin its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+}  // namespace tc
+}  // namespace rbt

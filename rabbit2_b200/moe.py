@@ -19,7 +19,7 @@ LIB_PATH = os.path.join(HERE, "librbt_moe.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "rbt_moe.h")
 
 DT_F32, DT_BF16 = 0, 1
-PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
+PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_GEMV_PLAIN = 0, 1, 2, 3
 
 
 class RbtMoeError(RuntimeError):

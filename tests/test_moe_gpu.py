@@ -95,20 +95,28 @@ def olmoe():
     ctx.close()
 
 
+@pytest.mark.parametrize("path", [moe.PATH_AUTO, moe.PATH_GEMV_PLAIN])
 @pytest.mark.parametrize("T", [1, 2, 3, 16, 64, 256])
-def test_olmoe_layer_vs_oracle(orc, olmoe, T):
+def test_olmoe_layer_vs_oracle(orc, olmoe, T, path):
+    """Automatic path (bf16 weight streaming below 64 tokens, tensor cores above) and
+    the plain CUDA-core GEMV with its separate combine."""
     ctx, host = olmoe
     x = workload.inputs(T, 2048, seed=100 + T)
     out = torch.empty_like(x)
     routing = torch.empty(T, 8, dtype=torch.int32, device="cuda")
-    ctx.ffn_device(0, x, out, routing)
-    torch.cuda.synchronize()
+    ctx.set_path(path)
+    try:
+        ctx.ffn_device(0, x, out, routing)
+        torch.cuda.synchronize()
+    finally:
+        ctx.set_path(moe.PATH_AUTO)
+    tensor_cores = path == moe.PATH_AUTO and T >= GEMM_MIN_TOKENS
     xh = x.cpu().numpy()
     want, want_r, _ = orc.moe_ffn(host, xh, nthreads=8)
     _, _, probs = orc.router_topk(host, xh)
     assert_routing(routing.cpu().numpy(), want_r, probs)
     err = rel_err(out.cpu().numpy(), want)
-    assert err < (MOE_RTOL_TC if T >= GEMM_MIN_TOKENS else MOE_RTOL), err
+    assert err < (MOE_RTOL_TC if tensor_cores else MOE_RTOL), err
     counts = ctx.expert_histogram()
     np.testing.assert_array_equal(counts, np.bincount(want_r.ravel(), minlength=64))
 
@@ -150,6 +158,27 @@ def test_olmoe_large_batch_routing_and_sampled_outputs(orc, olmoe):
     assert rel_err(out.cpu().numpy()[sample], want) < MOE_RTOL_TC
     # a size-independent property: the histogram sums to T*K
     assert ctx.expert_histogram().sum() == T * 8
+
+
+@pytest.mark.parametrize("T", [1, 7, 40])
+def test_weight_streaming_path_block_form(orc, olmoe, T):
+    """The block form (x += MoE(rmsnorm(x))) on the streaming decode kernels, with the
+    combine and residual fused into the down projection; in place on device memory."""
+    ctx, host = olmoe
+    ones = torch.ones(2048, device="cuda")
+    ctx.bind_layer(0, ctx._keep[0][0], ctx._keep[0][1], ones)
+    x = workload.inputs(T, 2048, seed=500 + T) * 3.0
+    x_in = x.clone()
+    ctx.set_path(moe.PATH_GEMV)
+    try:
+        ctx.block_device(0, x)
+        torch.cuda.synchronize()
+    finally:
+        ctx.set_path(moe.PATH_AUTO)
+    host.ffn_norm = np.ones(2048, np.float32)
+    want, want_r = orc.moe_block(host, x_in.cpu().numpy(), nthreads=8)
+    got = x.cpu().numpy()
+    assert rel_err(got - x_in.cpu().numpy(), want - x_in.cpu().numpy()) < MOE_RTOL
 
 
 def test_deterministic_and_host_api_matches_device_api(olmoe):
