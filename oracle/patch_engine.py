@@ -1,0 +1,46 @@
+"""Build recipe: the reference engine with its MoE block on the GPU.
+
+    python oracle/patch_engine.py <rabbit2.c> <out.c>
+
+Writes a copy of the reference engine source (rabbit2/src/rabbit2.c) into
+oracle/_ref/ with the four insertions INTEGRATION.md documents -- the include of
+rabbit2_b200/engine/rbt_engine_hook.h and its three call sites -- and nothing
+else changed.  oracle/Makefile compiles it against librbt_moe.so into
+oracle/_ref/rabbit2_cuda.  Each insertion is anchored on one reference line and
+fails loudly if that line is missing or not unique.
+"""
+import sys
+
+INSERTIONS = [
+    # (anchor line, where, text)
+    ("static int forward(Model *m, State *s, int token, int pos, int32_t *routing_out) {", "before",
+     '#include "rbt_engine_hook.h"\n\n'),
+    ("        /* ---- MoE feed-forward ---- */", "after",
+     "        {\n"
+     "            int g_ = rbt_engine_moe(m, l, s->x, routing_out + (size_t)l * c->top_k);\n"
+     "            if (g_ < 0) return 0;\n"
+     "            if (g_) continue;\n"
+     "        }\n"),
+    ('        else if (!strcmp(argv[i], "--kernel") && i + 1 < argc) kernel = argv[++i];', "before",
+     '        else if (!strcmp(argv[i], "--device") && i + 1 < argc) rbt_engine_device = argv[++i];\n'),
+    ("    if (!load_model(&m, argv[1])) return 1;", "after",
+     "    if (!rbt_engine_init(&m)) return 1;\n"),
+]
+
+
+def patch(src: str) -> str:
+    lines = src.splitlines(keepends=True)
+    for anchor, where, text in INSERTIONS:
+        hits = [i for i, ln in enumerate(lines) if ln.rstrip("\n") == anchor]
+        if len(hits) != 1:
+            raise SystemExit(f"anchor found {len(hits)} times: {anchor!r}")
+        i = hits[0]
+        lines.insert(i if where == "before" else i + 1, text)
+    return "".join(lines)
+
+
+if __name__ == "__main__":
+    with open(sys.argv[1]) as f:
+        out = patch(f.read())
+    with open(sys.argv[2], "w") as f:
+        f.write(out)

@@ -33,8 +33,12 @@ struct RouterArgs {
     int32_t* slot_pos;        // [T*K] inverse of perm
     int32_t* active;          // [E] experts with counts > 0, ascending
     int32_t* n_active;        // [1]
+    int32_t* tile_cnt;        // [n_tiles, E] routed slots per (token tile, expert)
+    int32_t* tile_base;       // [n_tiles, E] first position of the tile's slots of each expert
+    int32_t* slot_rank;       // [T*K] rank of a slot among its tile's slots of the same expert
 };
-cudaError_t launch_router(const RouterArgs& a, cudaStream_t s);
+// Kernels launched are reported in *launches (1 or 2).
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches);
 
 // K3: grouped GEMV over the active experts (CUDA cores, fp32 accumulation).
 struct GemvArgs {

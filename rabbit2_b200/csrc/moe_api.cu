@@ -59,6 +59,7 @@ struct Workspace {
     void* block = nullptr;
     float *xb, *logits, *wt, *h, *y, *hx, *hout;
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active, *hrouting;
+    int32_t *tile_cnt, *tile_base, *slot_rank;
     unsigned *tile_counter, *done_counter, *status;
     // tcgen05 path: split-bf16 operands in expert order and the token-block list
     void *xhi, *xlo, *hhi, *hlo;
@@ -118,6 +119,8 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.tb_e, ntb * 4},              {(void**)&w.tb_p0, ntb * 4},
         {(void**)&w.tb_p1, ntb * 4},             {(void**)&w.n_tb, 4},
         {(void**)&w.status, 4},
+        {(void**)&w.tile_cnt, tiles * E * 4},    {(void**)&w.tile_base, tiles * E * 4},
+        {(void**)&w.slot_rank, S * 4},
         {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
         {(void**)&w.wt, S * 4},                  {(void**)&w.h, S * H * 4},
         {(void**)&w.y, S * D * 4},               {(void**)&w.hx, (size_t)T * D * 4},
@@ -258,8 +261,11 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     ra.tile_counter = w.tile_counter; ra.done_counter = w.done_counter;
     ra.counts = w.counts; ra.offsets = w.offsets; ra.perm = w.perm; ra.slot_pos = w.slot_pos;
     ra.active = w.active; ra.n_active = w.n_active;
+    ra.tile_cnt = w.tile_cnt; ra.tile_base = w.tile_base; ra.slot_rank = w.slot_rank;
     if (!clk.begin(1)) return 0;
-    CU(rbt::launch_router(ra, s));
+    int router_launches = 0;
+    CU(rbt::launch_router(ra, s, &router_launches));
+    m->prof.launches += router_launches - 1;
 
     // the split kernel reads xb with 16-byte vectors
     const bool tc_ready = L.tc && w.tc_maps && (reinterpret_cast<uintptr_t>(xb) % 16 == 0);

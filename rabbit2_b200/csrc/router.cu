@@ -41,24 +41,41 @@ __device__ __forceinline__ float load_w<float>(const float* p) { return *p; }
 // Stage rows [r0, r0+rows) x columns [c0, c0+cols) of a row-major [*, D] matrix
 // into shared memory as f32 (row stride `ss` floats, a multiple of 4).  Rows at
 // or past `nrows` are left unwritten: the results that would read them are
-// never stored.  16-byte vector loads when the rows allow them.
+// never stored.  Each thread issues up to 8 independent 16-byte loads before
+// converting and storing, so a chunk costs one memory latency, not eight.
 template <typename T>
 __device__ __forceinline__ void stage_rows(float* dst, int ss, const T* src, int D, int r0, int rows, int nrows,
                                            int c0, int cols) {
     constexpr int V = 16 / sizeof(T);
+    constexpr int B = 8;
     const int valid = max(0, min(rows, nrows - r0));
     const bool vec = (D % V == 0) && (c0 % V == 0) && (cols % V == 0) &&
                      ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
     if (vec) {
-        const int vpr = cols / V;
-        for (int i = threadIdx.x; i < valid * vpr; i += blockDim.x) {
-            const int r = i / vpr, cv = i - r * vpr;
-            const uint4 v = *reinterpret_cast<const uint4*>(src + (size_t)(r0 + r) * D + c0 + cv * V);
-            float f[V];
-            WeightTraits<T>::unpack(v, f);
-            float* d = dst + r * ss + cv * V;
+        const int vpr = cols / V, n = valid * vpr;
+        for (int base = threadIdx.x; base < n; base += blockDim.x * B) {
+            uint4 v[B];
 #pragma unroll
-            for (int q = 0; q < V; q += 4) *reinterpret_cast<float4*>(d + q) = make_float4(f[q], f[q + 1], f[q + 2], f[q + 3]);
+            for (int b = 0; b < B; b++) {
+                const int i = base + b * blockDim.x;
+                if (i < n) {
+                    const int r = i / vpr, cv = i - r * vpr;
+                    v[b] = *reinterpret_cast<const uint4*>(src + (size_t)(r0 + r) * D + c0 + cv * V);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int i = base + b * blockDim.x;
+                if (i < n) {
+                    const int r = i / vpr, cv = i - r * vpr;
+                    float f[V];
+                    WeightTraits<T>::unpack(v[b], f);
+                    float* d = dst + r * ss + cv * V;
+#pragma unroll
+                    for (int q = 0; q < V; q += 4)
+                        *reinterpret_cast<float4*>(d + q) = make_float4(f[q], f[q + 1], f[q + 2], f[q + 3]);
+                }
+            }
         }
     } else {
         for (int i = threadIdx.x; i < valid * cols; i += blockDim.x) {
@@ -68,77 +85,128 @@ __device__ __forceinline__ void stage_rows(float* dst, int ss, const T* src, int
     }
 }
 
-// Softmax + top-k of one token tile, one warp per token (rabbit2.c:514-528).
+// Exclusive prefix sum over the 256 threads of a CTA (all threads call it).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* total) {
+    __shared__ int s_warp[kThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(FULL_MASK, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    int base = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; w++) {
+        base += (w < warp) ? s_warp[w] : 0;
+        all += s_warp[w];
+    }
+    __syncthreads();
+    if (total) *total = all;
+    return base + incl - v;
+}
+
+// Softmax + top-k of one token, by one warp (rabbit2.c:514-528).  `lrow` holds
+// the E logits (shared or global memory; kGlobal reads bypass L1 because other
+// CTAs wrote them).  Writes idx/wt/routing_out of token t and leaves the chosen
+// experts in s_idx[0..K).
+template <int NJ, bool kGlobal>
+__device__ void topk_token(const RouterArgs& a, const float* lrow, int t, float* s_ex, int32_t* s_idx, float* s_w) {
+    const int lane = threadIdx.x & 31;
+    const int E = a.E, K = a.K;
+    float l[NJ];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NJ; j++) {
+        const int e = lane + 32 * j;
+        l[j] = (e < E) ? (kGlobal ? __ldcg(lrow + e) : lrow[e]) : -INFINITY;
+        mx = fmaxf(mx, l[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
+    float p[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; j++) {
+        const int e = lane + 32 * j;
+        p[j] = (e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
+        if (e < E) s_ex[e] = p[j];
+    }
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0)
+        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, s_ex[e]);
+    sum = __shfl_sync(FULL_MASK, sum, 0);
+#pragma unroll
+    for (int j = 0; j < NJ; j++) p[j] = __fdiv_rn(p[j], sum);
+    unsigned used = 0;
+    for (int k = 0; k < K; k++) {
+        float bp = -INFINITY;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            if (e < E && !((used >> j) & 1u) && (p[j] > bp || be == 0x7fffffff)) {
+                bp = p[j];
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float op = __shfl_xor_sync(FULL_MASK, bp, o);
+            const int oe = __shfl_xor_sync(FULL_MASK, be, o);
+            if (oe != 0x7fffffff && (be == 0x7fffffff || op > bp || (op == bp && oe < be))) {
+                bp = op;
+                be = oe;
+            }
+        }
+        if ((be & 31) == lane) used |= 1u << (be >> 5);
+        if (lane == 0) {
+            s_idx[k] = be;
+            s_w[k] = bp;
+        }
+    }
+    __syncwarp();
+    float wsum = 0.0f;
+    for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_w[k]);  // every lane, same order
+    for (int k = lane; k < K; k += 32) {
+        const float w = a.norm_topk ? __fdiv_rn(s_w[k], wsum) : s_w[k];
+        a.idx[(size_t)t * K + k] = s_idx[k];
+        a.wt[(size_t)t * K + k] = w;
+        if (a.routing_out) a.routing_out[(size_t)t * a.routing_stride + k] = s_idx[k];
+    }
+    __syncwarp();
+}
+
+// Softmax + top-k of a token tile whose logits other CTAs wrote, one warp per token.
 __device__ void finish_tokens(const RouterArgs& a, int t0, int tcount) {
     __shared__ float s_ex[kThreads / 32][kMaxExperts];
     __shared__ int32_t s_idx[kThreads / 32][kMaxTopK];
     __shared__ float s_w[kThreads / 32][kMaxTopK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int E = a.E, K = a.K;
-    constexpr int NJ = kMaxExperts / 32;
-    for (int tl = warp; tl < tcount; tl += kThreads / 32) {
-        const int t = t0 + tl;
-        float l[NJ];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            l[j] = (e < E) ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
-            mx = fmaxf(mx, l[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
-        float p[NJ];
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            p[j] = (float)exp((double)__fsub_rn(l[j], mx));
-            if (e < E) s_ex[warp][e] = p[j];
-        }
-        __syncwarp();
-        float sum = 0.0f;
-        if (lane == 0)
-            for (int e = 0; e < E; e++) sum = __fadd_rn(sum, s_ex[warp][e]);
-        sum = __shfl_sync(FULL_MASK, sum, 0);
-#pragma unroll
-        for (int j = 0; j < NJ; j++) p[j] = __fdiv_rn(p[j], sum);
-        unsigned used = 0;
-        for (int k = 0; k < K; k++) {
-            float bp = -INFINITY;
-            int be = 0x7fffffff;
-#pragma unroll
-            for (int j = 0; j < NJ; j++) {
-                const int e = lane + 32 * j;
-                if (e < E && !((used >> j) & 1u) && (p[j] > bp || be == 0x7fffffff)) {
-                    bp = p[j];
-                    be = e;
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float op = __shfl_xor_sync(FULL_MASK, bp, o);
-                const int oe = __shfl_xor_sync(FULL_MASK, be, o);
-                if (oe != 0x7fffffff && (be == 0x7fffffff || op > bp || (op == bp && oe < be))) {
-                    bp = op;
-                    be = oe;
-                }
-            }
-            if ((be & 31) == lane) used |= 1u << (be >> 5);
-            if (lane == 0) {
-                s_idx[warp][k] = be;
-                s_w[warp][k] = bp;
-            }
-        }
-        __syncwarp();
-        float wsum = 0.0f;
-        for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_w[warp][k]);  // every lane, same order
-        for (int k = lane; k < K; k += 32) {
-            const float w = a.norm_topk ? __fdiv_rn(s_w[warp][k], wsum) : s_w[warp][k];
-            a.idx[(size_t)t * K + k] = s_idx[warp][k];
-            a.wt[(size_t)t * K + k] = w;
-            if (a.routing_out) a.routing_out[(size_t)t * a.routing_stride + k] = s_idx[warp][k];
-        }
-        __syncwarp();
+    const int warp = threadIdx.x >> 5;
+    for (int tl = warp; tl < tcount; tl += kThreads / 32)
+        topk_token<kMaxExperts / 32, true>(a, a.logits + (size_t)(t0 + tl) * a.E, t0 + tl, s_ex[warp], s_idx[warp],
+                                           s_w[warp]);
+}
+
+// Given this thread's expert count (thread e, e < E), write counts, offsets,
+// the active-expert list and n_active; optionally keep the offsets in s_off.
+__device__ void publish_offsets(const RouterArgs& a, int cnt, int* s_off) {
+    const int e = threadIdx.x;
+    int total = 0;
+    const int off = block_exclusive_scan(cnt, &total);
+    int n_act = 0;
+    const int apos = block_exclusive_scan(cnt > 0 ? 1 : 0, &n_act);
+    if (e < a.E) {
+        a.offsets[e] = off;
+        a.counts[e] = cnt;
+        if (cnt > 0) a.active[apos] = e;
+        if (s_off) s_off[e] = off;
+    }
+    if (e == 0) {
+        a.offsets[a.E] = total;
+        *a.n_active = n_act;
     }
 }
 
@@ -154,18 +222,7 @@ __device__ void build_permutation(const RouterArgs& a) {
     __syncthreads();
     for (int s = tid; s < S; s += kThreads) atomicAdd(&s_cnt[__ldcg(a.idx + s)], 1);
     __syncthreads();
-    if (tid == 0) {
-        int run = 0, na = 0;
-        for (int e = 0; e < E; e++) {
-            a.offsets[e] = run;
-            s_base[e] = run;
-            a.counts[e] = s_cnt[e];
-            if (s_cnt[e] > 0) a.active[na++] = e;
-            run += s_cnt[e];
-        }
-        a.offsets[E] = run;
-        *a.n_active = na;
-    }
+    publish_offsets(a, tid < E ? s_cnt[tid] : 0, s_base);
     __syncthreads();
     for (int c0 = 0; c0 < S; c0 += kThreads) {
         const int s = c0 + tid;
@@ -325,6 +382,239 @@ __global__ void __launch_bounds__(kThreads) router_large_kernel(RouterArgs a) {
     tile_epilogue(a, t0, tcount);
 }
 
+// ---------------------------------------------------------------------------
+// Wide router (E <= 64, D % 4 == 0, T > 8): one CTA holds every expert for a
+// tile of 16 tokens, so softmax/top-k need no other CTA.  Thread (e, g) keeps
+// the four chains of expert e for tokens g, g+4, g+8, g+12 as packed f32 pairs
+// (mul.rn.f32x2 / add.rn.f32x2: each half is one IEEE-rounded f32 operation,
+// the same arithmetic as the scalar chains).  Router-weight and activation
+// chunks of 128 columns are double-buffered in shared memory with cp.async.
+// Each tile then ranks its routed slots per expert (stable) and publishes its
+// per-expert counts; the last tile turns the counts into expert offsets and
+// per-tile bases, and scatter_kernel places every slot.
+constexpr int kWideTokens = 16;
+constexpr int kWideChunk = 128;
+constexpr int kWideExperts = 64;
+constexpr int kWideXStride = kWideChunk + 4;  // floats: 528-byte rows (16-byte aligned)
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <typename WT>
+struct WideCfg {
+    // router rows in shared memory: 128 elements + a skew that staggers rows by
+    // two banks (bf16) / four banks (f32) so a warp's 32 experts read conflict-free
+    static constexpr int kWStride = kWideChunk + (sizeof(WT) == 2 ? 4 : 4);
+    static constexpr int kWBytes = kWideExperts * kWStride * (int)sizeof(WT);
+    static constexpr int kXBytes = kWideTokens * kWideXStride * 4;
+    static constexpr int kStageBytes = kWBytes + kXBytes;
+    static constexpr int kSmem = 2 * kStageBytes;
+};
+
+// Stable per-tile ranking of routed slots by expert; writes slot_rank[] and the
+// tile's per-expert counts.  s_eidx: the tile's chosen experts, slot order.
+__device__ void rank_tile_slots(const RouterArgs& a, const int32_t* s_eidx, int nslots, int slot0, int tile) {
+    __shared__ int32_t s_cnt[kMaxExperts];
+    __shared__ int32_t s_wcnt[kThreads / 32][kMaxExperts];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    for (int e = tid; e < a.E; e += kThreads) s_cnt[e] = 0;
+    for (int i = tid; i < (kThreads / 32) * kMaxExperts; i += kThreads) (&s_wcnt[0][0])[i] = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < nslots; c0 += kThreads) {
+        const int sl = c0 + tid;
+        const int e = (sl < nslots) ? s_eidx[sl] : -1;
+        const unsigned peers = __match_any_sync(FULL_MASK, e);
+        const int rank = __popc(peers & lanemask_lt());
+        if (e >= 0 && rank == 0) s_wcnt[warp][e] = __popc(peers);
+        __syncthreads();
+        if (e >= 0) {
+            int pre = s_cnt[e];
+            for (int w = 0; w < warp; w++) pre += s_wcnt[w][e];
+            a.slot_rank[slot0 + sl] = pre + rank;
+        }
+        __syncthreads();
+        for (int ee = tid; ee < a.E; ee += kThreads) {
+            int tot = 0;
+            for (int w = 0; w < kThreads / 32; w++) {
+                tot += s_wcnt[w][ee];
+                s_wcnt[w][ee] = 0;
+            }
+            s_cnt[ee] += tot;
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < a.E; e += kThreads) a.tile_cnt[(size_t)tile * a.E + e] = s_cnt[e];
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
+    using C = WideCfg<WT>;
+    extern __shared__ __align__(16) uint8_t wsmem[];
+    __shared__ float s_logit[kWideTokens][kWideExperts];
+    __shared__ float s_ex[kThreads / 32][kWideExperts];
+    __shared__ float s_w[kThreads / 32][kMaxTopK];
+    __shared__ int32_t s_eidx[kWideTokens * kMaxTopK];
+    const int tid = threadIdx.x;
+    const int e = tid & 63, g = tid >> 6;
+    const int t0 = blockIdx.x * kWideTokens;
+    const int tcount = min(kWideTokens, a.T - t0);
+    const int D = a.D, E = a.E;
+    const WT* W = static_cast<const WT*>(a.router);
+    const int nch = (D + kWideChunk - 1) / kWideChunk;
+
+    auto issue = [&](int ch, int buf) {
+        uint8_t* st = wsmem + buf * C::kStageBytes;
+        WT* ws = reinterpret_cast<WT*>(st);
+        float* xs = reinterpret_cast<float*>(st + C::kWBytes);
+        const int c0 = ch * kWideChunk, cols = min(kWideChunk, D - c0);
+        if (sizeof(WT) == 2) {  // 4 bf16 = 8 bytes per copy
+            const int per_row = cols / 4;
+            for (int i = tid; i < E * per_row; i += kThreads) {
+                const int r = i / per_row, q = i - r * per_row;
+                cp_async8(ws + r * C::kWStride + q * 4, W + (size_t)r * D + c0 + q * 4);
+            }
+        } else {  // 4 f32 = 16 bytes per copy
+            const int per_row = cols / 4;
+            for (int i = tid; i < E * per_row; i += kThreads) {
+                const int r = i / per_row, q = i - r * per_row;
+                cp_async16(ws + r * C::kWStride + q * 4, W + (size_t)r * D + c0 + q * 4);
+            }
+        }
+        const int per_row = cols / 4;
+        for (int i = tid; i < tcount * per_row; i += kThreads) {
+            const int r = i / per_row, q = i - r * per_row;
+            cp_async16(xs + r * kWideXStride + q * 4, a.xb + (size_t)(t0 + r) * D + c0 + q * 4);
+        }
+        cp_async_commit();
+    };
+
+    uint64_t acc01[4], acc23[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc01[j] = acc23[j] = 0ull;  // +0.0f pairs
+    issue(0, 0);
+    for (int ch = 0; ch < nch; ch++) {
+        if (ch + 1 < nch) {
+            issue(ch + 1, (ch + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint8_t* st = wsmem + (ch & 1) * C::kStageBytes;
+        const WT* wr = reinterpret_cast<const WT*>(st) + e * C::kWStride;
+        const float* xs = reinterpret_cast<const float*>(st + C::kWBytes);
+        const int cols = min(kWideChunk, D - ch * kWideChunk);
+        if (e < E) {
+#pragma unroll 4
+            for (int i = 0; i < cols; i += 4) {
+                float w0, w1, w2, w3;
+                if (sizeof(WT) == 2) {
+                    const uint2 q = *reinterpret_cast<const uint2*>(wr + i);
+                    w0 = __uint_as_float(q.x << 16);
+                    w1 = __uint_as_float(q.x & 0xffff0000u);
+                    w2 = __uint_as_float(q.y << 16);
+                    w3 = __uint_as_float(q.y & 0xffff0000u);
+                } else {
+                    const float4 q = *reinterpret_cast<const float4*>(wr + i);
+                    w0 = q.x; w1 = q.y; w2 = q.z; w3 = q.w;
+                }
+                const uint64_t w01 = f2_pack(w0, w1), w23 = f2_pack(w2, w3);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float4 x = *reinterpret_cast<const float4*>(xs + (g + 4 * j) * kWideXStride + i);
+                    acc01[j] = f2_add(acc01[j], f2_mul(w01, f2_pack(x.x, x.y)));
+                    acc23[j] = f2_add(acc23[j], f2_mul(w23, f2_pack(x.z, x.w)));
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (e < E) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int tl = g + 4 * j;
+            float logit = __fadd_rn(__fadd_rn(f2_lo(acc01[j]), f2_hi(acc01[j])),
+                                    __fadd_rn(f2_lo(acc23[j]), f2_hi(acc23[j])));
+            if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
+            s_logit[tl][e] = logit;
+        }
+    }
+    __syncthreads();
+    const int warp = tid >> 5;
+    for (int tl = warp; tl < tcount; tl += kThreads / 32)
+        topk_token<2, false>(a, s_logit[tl], t0 + tl, s_ex[warp], s_eidx + tl * a.K, s_w[warp]);
+    __syncthreads();
+    rank_tile_slots(a, s_eidx, tcount * a.K, t0 * a.K, blockIdx.x);
+
+    // the last tile to finish turns per-tile counts into offsets and tile bases
+    __shared__ unsigned s_ticket;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_ticket = atomicAdd(a.done_counter, 1u);
+    __syncthreads();
+    if (s_ticket != gridDim.x - 1) return;
+    __threadfence();
+    const int ntiles = gridDim.x;
+    int tot = 0;
+    if (tid < E)
+        for (int t = 0; t < ntiles; t++) tot += __ldcg(a.tile_cnt + (size_t)t * E + tid);
+    __shared__ int s_off[kMaxExperts];
+    publish_offsets(a, tot, s_off);
+    __syncthreads();
+    if (tid < E) {
+        int run = s_off[tid];
+        for (int t = 0; t < ntiles; t++) {
+            a.tile_base[(size_t)t * E + tid] = run;
+            run += __ldcg(a.tile_cnt + (size_t)t * E + tid);
+        }
+    }
+    if (tid == 0) *a.done_counter = 0;
+}
+
+// Places every routed slot of a tile: position = tile base of its expert + its
+// stable rank within the tile.
+__global__ void __launch_bounds__(kThreads) scatter_kernel(RouterArgs a) {
+    const int t0 = blockIdx.x * kWideTokens;
+    const int nslots = min(kWideTokens, a.T - t0) * a.K;
+    for (int sl = threadIdx.x; sl < nslots; sl += kThreads) {
+        const int s = t0 * a.K + sl;
+        const int pos = a.tile_base[(size_t)blockIdx.x * a.E + a.idx[s]] + a.slot_rank[s];
+        a.perm[pos] = s;
+        a.slot_pos[s] = pos;
+    }
+}
+
+bool wide_ok(const RouterArgs& a) {
+    const size_t esz = a.dtype == 1 ? 2 : 4;
+    return a.E <= kWideExperts && a.D % 4 == 0 && a.K * kWideTokens <= kWideTokens * kMaxTopK &&
+           (reinterpret_cast<uintptr_t>(a.router) % (esz * 4)) == 0 && (reinterpret_cast<uintptr_t>(a.xb) % 16) == 0;
+}
+
 template <typename KernelT>
 cudaError_t launch_with_smem(KernelT kernel, dim3 grid, size_t smem, const RouterArgs& a, cudaStream_t s) {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -334,11 +624,20 @@ cudaError_t launch_with_smem(KernelT kernel, dim3 grid, size_t smem, const Route
 }
 
 template <typename WT>
-cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s) {
+cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s, int* launches) {
     const int egroups = (a.E + kExpertsPerCta - 1) / kExpertsPerCta;
+    *launches = 1;
     if (a.T <= kSmallTokens) {
         const size_t smem = 2ull * kExpertsPerCta * kSmallStride * sizeof(float);
         return launch_with_smem(router_small_kernel<WT>, dim3(1, egroups), smem, a, s);
+    }
+    if (wide_ok(a)) {
+        const int tiles = (a.T + kWideTokens - 1) / kWideTokens;
+        cudaError_t err = launch_with_smem(router_wide_kernel<WT>, dim3(tiles), WideCfg<WT>::kSmem, a, s);
+        if (err != cudaSuccess) return err;
+        *launches = 2;
+        scatter_kernel<<<tiles, kThreads, 0, s>>>(a);
+        return cudaGetLastError();
     }
     auto grid_for = [&](int tt) { return dim3((a.T + tt - 1) / tt, egroups); };
     if (a.T >= 2048) {
@@ -355,16 +654,13 @@ cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s) {
 
 }  // namespace
 
-// Token tiles the router grid uses for T tokens (sizes the tile counters).
-int router_token_tiles(int T) {
-    if (T <= kSmallTokens) return 1;
-    const int tt = T >= 2048 ? 128 : (T >= 512 ? 64 : 32);
-    return (T + tt - 1) / tt;
-}
+// Token tiles any router variant uses for T tokens (sizes the per-tile arrays).
+int router_token_tiles(int T) { return T <= kSmallTokens ? 1 : (T + kWideTokens - 1) / kWideTokens; }
 
-cudaError_t launch_router(const RouterArgs& a, cudaStream_t s) {
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches) {
+    *launches = 0;
     if (a.T <= 0) return cudaSuccess;
-    return a.dtype == 1 ? launch_typed<uint16_t>(a, s) : launch_typed<float>(a, s);
+    return a.dtype == 1 ? launch_typed<uint16_t>(a, s, launches) : launch_typed<float>(a, s, launches);
 }
 
 }  // namespace rbt

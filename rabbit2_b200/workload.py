@@ -49,3 +49,46 @@ def zipf_bias(E: int, s: float = 1.2, seed: int = 0) -> np.ndarray:
     ranks = np.random.default_rng(seed).permutation(E).astype(np.float64) + 1.0
     p = ranks ** -s
     return np.log(p / p.sum()).astype(np.float32)
+
+
+def tiny_olmoe_config():
+    """The CPU-runnable config: dim 256, 4 layers, 4 heads x 64, QK-norm, RoPE 10000,
+    8 experts top-2, expert hidden 512, vocab 4096, f32 weights."""
+    from rabbit2_b200.rbt2fmt import DT_F32
+    return ModelConfig(vocab=4096, dim=256, n_layers=4, n_heads=4, n_kv_heads=4, head_dim=64, n_experts=8,
+                       top_k=2, expert_hidden=512, max_seq=512, dtype=DT_F32, qk_norm=1, norm_topk=0,
+                       rope_theta=10000.0, rms_eps=1e-5)
+
+
+def write_model(path, cfg, seed=0, std=0.02):
+    """A random-init model file: matrices ~N(0, std) (rounded to the file dtype), norms 1.
+
+    Draw order, from one numpy default_rng(seed): tok_emb; per layer wq, wk, wv, wo,
+    router, then each expert's w1, w3, w2; lm_head."""
+    from rabbit2_b200.rbt2fmt import ModelWriter, round_to_dtype
+    rng = np.random.default_rng(seed)
+    q_dim, kv_dim = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+
+    def mat(r, c):
+        return round_to_dtype(std * rng.standard_normal((r, c), dtype=np.float32), cfg.dtype)
+
+    ones = lambda n: np.ones(n, np.float32)  # noqa: E731
+    with ModelWriter(path, cfg) as w:
+        L = w.offsets
+        w.matrix(L["tok_emb"], mat(cfg.vocab, cfg.dim))
+        for li, lo in enumerate(L["layers"]):
+            w.vector(lo["attn_norm"], ones(cfg.dim))
+            w.matrix(lo["wq"], mat(q_dim, cfg.dim))
+            w.matrix(lo["wk"], mat(kv_dim, cfg.dim))
+            w.matrix(lo["wv"], mat(kv_dim, cfg.dim))
+            w.matrix(lo["wo"], mat(cfg.dim, q_dim))
+            if cfg.qk_norm:
+                w.vector(lo["q_norm"], ones(q_dim))
+                w.vector(lo["k_norm"], ones(kv_dim))
+            w.vector(lo["ffn_norm"], ones(cfg.dim))
+            w.matrix(lo["router"], mat(cfg.n_experts, cfg.dim))
+            for e in range(cfg.n_experts):
+                w.expert(li, e, mat(cfg.expert_hidden, cfg.dim), mat(cfg.expert_hidden, cfg.dim),
+                         mat(cfg.dim, cfg.expert_hidden))
+        w.vector(L["final_norm"], ones(cfg.dim))
+        w.matrix(L["lm_head"], mat(cfg.vocab, cfg.dim))

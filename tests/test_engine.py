@@ -1,0 +1,87 @@
+"""The drop-in, end to end: the reference engine built with rbt_engine_hook.h
+(oracle/_ref/rabbit2_cuda, made by oracle/Makefile from oracle/patch_engine.py)
+against the unmodified reference engine (oracle/_ref/rabbit2) on the same
+model file, through the engine's own CLI -- the interface the Python tools use
+(tools/run.py, serve.py: subprocess calls of `rabbit2 --gen` / `--dump`).
+
+Bars: greedy ids identical over 64 steps, routing identical, logits within a
+max relative error of 1e-3 (max|d| / max|ref|).
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from rabbit2_b200 import workload
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "oracle", "_ref", "rabbit2")
+CUDA = os.path.join(ROOT, "oracle", "_ref", "rabbit2_cuda")
+needs_bins = pytest.mark.skipif(not (os.path.exists(REF) and os.path.exists(CUDA)),
+                                reason="oracle/_ref engines not built (reference source absent when building)")
+
+
+@pytest.fixture(scope="module")
+def tiny_model(tmp_path_factory):
+    cfg = workload.tiny_olmoe_config()
+    path = str(tmp_path_factory.mktemp("model") / "tiny_olmoe.rbt2")
+    workload.write_model(path, cfg, seed=0)
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(0, cfg.vocab, size=128).tolist()
+    return path, cfg, prompt
+
+
+def dump(binary, model, tokens, tmp, extra=()):
+    lg, rt = os.path.join(tmp, "l.bin"), os.path.join(tmp, "r.bin")
+    p = subprocess.run([binary, model, "--dump", lg, rt, "--ctx", "256", *extra, *map(str, tokens)],
+                       capture_output=True, text=True)
+    assert p.returncode == 0, p.stderr
+    return np.fromfile(lg, "<f4"), np.fromfile(rt, "<i4"), p.stderr
+
+
+def gen(binary, model, tokens, n, extra=()):
+    p = subprocess.run([binary, model, "--gen", str(n), "--ctx", "256", *extra, *map(str, tokens)],
+                       capture_output=True, text=True)
+    assert p.returncode == 0, p.stderr
+    return [int(t) for t in p.stdout.split()], p.stderr
+
+
+@needs_bins
+def test_cpu_device_is_the_unmodified_engine(tiny_model, tmp_path):
+    """--device cpu (the default) leaves the reference path byte-identical."""
+    model, _, prompt = tiny_model
+    a = dump(REF, model, prompt[:16], str(tmp_path))
+    b = dump(CUDA, model, prompt[:16], str(tmp_path), ["--device", "cpu"])
+    assert a[0].tobytes() == b[0].tobytes() and a[1].tobytes() == b[1].tobytes()
+
+
+@needs_bins
+def test_bad_device_is_rejected(tiny_model):
+    model, _, prompt = tiny_model
+    p = subprocess.run([CUDA, model, "--gen", "1", "--device", "tpu", "1"], capture_output=True, text=True)
+    assert p.returncode == 1 and "--device" in p.stderr
+
+
+@needs_bins
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="checks the no-GPU failure")
+def test_cuda_device_without_gpu_fails_loudly(tiny_model):
+    model, _, prompt = tiny_model
+    p = subprocess.run([CUDA, model, "--gen", "1", "--device", "cuda", "1"], capture_output=True, text=True)
+    assert p.returncode == 1 and "rbt_moe" in p.stderr
+
+
+@needs_bins
+@pytest.mark.gpu
+def test_gpu_moe_engine_matches_reference(tiny_model, tmp_path):
+    """Config 1 (tiny OLMoE, f32): 128-token prompt, then 64 greedy tokens."""
+    model, cfg, prompt = tiny_model
+    want_ids, _ = gen(REF, model, prompt, 64)
+    got_ids, log = gen(CUDA, model, prompt, 64, ["--device", "cuda"])
+    assert "moe device: cuda" in log
+    assert got_ids == want_ids
+    wl, wr, _ = dump(REF, model, prompt, str(tmp_path))
+    gl, gr, _ = dump(CUDA, model, prompt, str(tmp_path), ["--device", "cuda"])
+    np.testing.assert_array_equal(gr, wr)
+    err = np.abs(gl.astype(np.float64) - wl).max() / np.abs(wl).max()
+    assert err < 1e-3, err

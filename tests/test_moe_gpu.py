@@ -175,7 +175,9 @@ def test_weight_streaming_path_block_form(orc, olmoe, T):
         torch.cuda.synchronize()
     finally:
         ctx.set_path(moe.PATH_AUTO)
-    host.ffn_norm = np.ones(2048, np.float32)
+        ctx.bind_layer(0, ctx._keep[0][0], ctx._keep[0][1])  # the shared layer has no ffn_norm
+    host = MoeLayerHost(host.D, host.H, host.E, host.K, host.dtype, host.norm_topk, host.router, host.experts,
+                        host.expert_stride, ffn_norm=np.ones(2048, np.float32))
     want, want_r = orc.moe_block(host, x_in.cpu().numpy(), nthreads=8)
     got = x.cpu().numpy()
     assert rel_err(got - x_in.cpu().numpy(), want - x_in.cpu().numpy()) < MOE_RTOL
