@@ -103,12 +103,13 @@ int rbt_moe_expert_histogram(RbtMoe *m, int32_t *counts_out);
 /* Force the path for later calls: 0 automatic (default), 1 CUDA-core GEMV
  * (weight streaming through shared memory when the shapes allow it), 2 the
  * tcgen05 grouped GEMM (bf16, D and H multiples of 128), 3 the plain CUDA-core
- * GEMV with a separate combine (any dtype and shape). */
+ * GEMV with a separate combine (any dtype and shape), 4 the single-kernel
+ * batch-1 decode (bf16, one token, D <= 2048; automatic for one token). */
 int rbt_moe_set_path(RbtMoe *m, int path);
 
 /* Launch accounting and per-stage device timing.  Stages: 0 rmsnorm, 1 router +
  * top-k + permute, 2 gate/up + SwiGLU, 3 down, 4 combine, 5 operand gather
- * (GEMM path).  With timing on, every call records a CUDA event at each stage
+ * (GEMM path), 6 the fused one-token decode kernel.  With timing on, every call records a CUDA event at each stage
  * boundary on its stream (as graph nodes when the stream is being captured)
  * and nothing waits; stage_ms sums the intervals recorded since the last reset,
  * read from the events' latest timestamps (so after a graph replay it holds

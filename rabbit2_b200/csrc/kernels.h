@@ -90,6 +90,29 @@ bool stream_supported(const StreamArgs& a, int dtype);
 cudaError_t launch_gateup_stream(const StreamArgs& a, int grid, cudaStream_t s);
 cudaError_t launch_down_combine_stream(const StreamArgs& a, int grid, cudaStream_t s);
 
+// Batch-1 decode: the whole MoE block in one cooperative kernel (decode_fused.cu).
+struct DecodeArgs {
+    const float* x;           // [D] residual stream (block form) or normalised input (ffn form)
+    float* out;               // [D] output; equals x in the block form
+    const float* ffn_norm;    // [D] for the block form, nullptr for the ffn form
+    float eps;
+    const uint16_t* router;   // [E, D] bf16
+    const float* bias;        // [E] or nullptr
+    const uint8_t* experts;
+    size_t stride;
+    int D, H, E, K, norm_topk;
+    float* logits;            // [E] scratch
+    float* h;                 // [K, H] scratch
+    int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active;
+    float* wt;
+    int32_t* routing_out;     // [K] or nullptr
+    unsigned* bar;            // [2] grid-barrier counters, zero between calls
+    unsigned* status;
+};
+bool decode_fused_supported(int T, int D, int H, int E, int K, int dtype, const void* experts, size_t stride,
+                            const void* x, const void* router);
+cudaError_t launch_decode_fused(const DecodeArgs& a, int grid, cudaStream_t s);
+
 // K4: tcgen05 grouped GEMM (gemm_tc.cu).
 struct TcGemmArgs {
     const int32_t* tb_e;      // [n_tb] expert of each token block

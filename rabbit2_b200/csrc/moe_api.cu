@@ -60,7 +60,7 @@ struct Workspace {
     float *xb, *logits, *wt, *h, *y, *hx, *hout;
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active, *hrouting;
     int32_t *tile_cnt, *tile_base, *slot_rank;
-    unsigned *tile_counter, *done_counter, *status;
+    unsigned *tile_counter, *done_counter, *status, *gbar;
     // tcgen05 path: split-bf16 operands in expert order and the token-block list
     void *xhi, *xlo, *hhi, *hlo;
     int32_t *tb_e, *tb_p0, *tb_p1, *n_tb;
@@ -118,7 +118,7 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.hhi, SB * H * 2},            {(void**)&w.hlo, SB * H * 2},
         {(void**)&w.tb_e, ntb * 4},              {(void**)&w.tb_p0, ntb * 4},
         {(void**)&w.tb_p1, ntb * 4},             {(void**)&w.n_tb, 4},
-        {(void**)&w.status, 4},
+        {(void**)&w.status, 4},                  {(void**)&w.gbar, 8},
         {(void**)&w.tile_cnt, tiles * E * 4},    {(void**)&w.tile_base, tiles * E * 4},
         {(void**)&w.slot_rank, S * 4},
         {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
@@ -150,6 +150,7 @@ int reserve(RbtMoe* m, int T) {
     CU(cudaMemsetAsync(w.done_counter, 0, 4, m->stream));
     CU(cudaMemsetAsync(w.counts, 0, E * 4, m->stream));
     CU(cudaMemsetAsync(w.status, 0, 4, m->stream));
+    CU(cudaMemsetAsync(w.gbar, 0, 8, m->stream));
     CU(cudaStreamSynchronize(m->stream));
     if (tc) {
         w.tc_maps = rbt::make_map_2d(&w.m_xhi, w.xhi, c.dim, (long)SB, rbt::tc_block_n()) &&
@@ -246,6 +247,22 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     Workspace& w = m->ws;
     StageClock clk{m, s};
     m->prof.calls++;
+    if ((m->path == 0 || m->path == 4) &&
+        rbt::decode_fused_supported(T, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, L.experts,
+                                    c.expert_stride, x, L.router)) {
+        rbt::DecodeArgs da{};
+        da.x = x; da.out = block ? const_cast<float*>(x) : out; da.ffn_norm = block ? L.ffn_norm : nullptr;
+        da.eps = c.rms_eps; da.router = static_cast<const uint16_t*>(L.router); da.bias = L.bias;
+        da.experts = L.experts; da.stride = c.expert_stride;
+        da.D = c.dim; da.H = c.expert_hidden; da.E = c.n_experts; da.K = c.top_k; da.norm_topk = c.norm_topk;
+        da.logits = w.logits; da.h = w.h; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
+        da.perm = w.perm; da.slot_pos = w.slot_pos; da.active = w.active; da.n_active = w.n_active; da.wt = w.wt;
+        da.routing_out = routing; da.bar = w.gbar; da.status = w.status;
+        if (!clk.begin(6)) return 0;
+        CU(rbt::launch_decode_fused(da, m->sm_count, s));
+        return clk.end();
+    }
+    if (m->path == 4) return fail("fused decode path requested but unavailable (needs T == 1, bf16, D <= 2048)");
     const float* xb = x;
     if (block) {
         if (!clk.begin(0)) return 0;
@@ -324,6 +341,7 @@ int check_status(RbtMoe* m) {
     CU(cudaMemcpy(&st, m->ws.status, 4, cudaMemcpyDeviceToHost));
     if (st) {
         CU(cudaMemset(m->ws.status, 0, 4));
+        CU(cudaMemset(m->ws.gbar, 0, 8));
         return fail("tensor-core GEMM pipeline wait timed out (code 0x%x)", st);
     }
     return 1;
@@ -534,7 +552,7 @@ int rbt_moe_profile(RbtMoe* m, int timing, int reset, RbtMoeProfile* out) {
 
 int rbt_moe_set_path(RbtMoe* m, int path) {
     if (!m) return fail("null context");
-    if (path < 0 || path > 3) return fail("path must be 0, 1, 2 or 3");
+    if (path < 0 || path > 4) return fail("path must be 0..4");
     m->path = path;
     return 1;
 }

@@ -19,7 +19,7 @@ LIB_PATH = os.path.join(HERE, "librbt_moe.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "rbt_moe.h")
 
 DT_F32, DT_BF16 = 0, 1
-PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_GEMV_PLAIN = 0, 1, 2, 3
+PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_GEMV_PLAIN, PATH_DECODE_FUSED = 0, 1, 2, 3, 4
 
 
 class RbtMoeError(RuntimeError):
@@ -37,7 +37,7 @@ class RbtMoeProfile(C.Structure):
                 ("stage_launches", C.c_int64 * 8)]
 
 
-STAGES = ("rmsnorm", "router", "gate_up", "down", "combine", "gather", "", "")
+STAGES = ("rmsnorm", "router", "gate_up", "down", "combine", "gather", "decode_fused", "")
 
 _lib = None
 

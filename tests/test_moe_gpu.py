@@ -286,3 +286,89 @@ def test_tensor_core_path_rejects_f32_weights():
             ctx.ffn(0, np.ones((4, D), np.float32))
     finally:
         ctx.close()
+
+
+@pytest.mark.parametrize("zipf", [False, True])
+def test_fused_decode_kernel_block_and_ffn(orc, zipf):
+    """Batch-1 decode as one cooperative kernel (router, top-k, experts, combine,
+    residual), both forms, against the oracle; 20 calls in a row must agree bit for
+    bit (the grid-barrier counters return to zero after every call)."""
+    bias = workload.zipf_bias(64, 1.2, seed=9) if zipf else None
+    ctx, host = olmoe_ctx(seed=31, bias=bias)
+    try:
+        ones = torch.ones(2048, device="cuda")
+        ctx.bind_layer(0, ctx._keep[0][0], ctx._keep[0][1], ones)
+        ctx.set_path(moe.PATH_DECODE_FUSED)
+        hb = MoeLayerHost(host.D, host.H, host.E, host.K, host.dtype, 0, host.router, host.experts,
+                          host.expert_stride, ffn_norm=np.ones(2048, np.float32), router_bias=bias)
+        for seed in range(4):
+            x = workload.inputs(1, 2048, seed=700 + seed) * 2.0
+            # ffn form
+            out = torch.empty_like(x)
+            routing = torch.empty(1, 8, dtype=torch.int32, device="cuda")
+            ctx.ffn_device(0, x, out, routing)
+            want, want_r, _ = orc.moe_ffn(hb, x.cpu().numpy())
+            _, _, probs = orc.router_topk(hb, x.cpu().numpy())
+            assert_routing(routing.cpu().numpy(), want_r, probs)
+            assert rel_err(out.cpu().numpy(), want) < MOE_RTOL
+            np.testing.assert_array_equal(ctx.expert_histogram(), np.bincount(want_r.ravel(), minlength=64))
+            # block form, in place
+            xb = x.clone()
+            ctx.block_device(0, xb, routing)
+            wantb, want_rb = orc.moe_block(hb, x.cpu().numpy())
+            assert_routing(routing.cpu().numpy(), want_rb, None if np.array_equal(routing.cpu().numpy(), want_rb)
+                           else orc.router_topk(hb, x.cpu().numpy())[2])
+            assert rel_err(xb.cpu().numpy() - x.cpu().numpy(), wantb - x.cpu().numpy()) < MOE_RTOL
+        x = workload.inputs(1, 2048, seed=800)
+        outs = []
+        for _ in range(20):
+            o = torch.empty_like(x)
+            ctx.ffn_device(0, x, o)
+            outs.append(o)
+        torch.cuda.synchronize()
+        for o in outs[1:]:
+            assert torch.equal(o.view(torch.int32), outs[0].view(torch.int32))
+        ctx.ffn(0, x.cpu().numpy())  # the host call checks the kernel's status word
+    finally:
+        ctx.close()
+
+
+def test_decode_layers_in_a_cuda_graph(orc):
+    """Three layers of the block form captured in one CUDA graph and replayed."""
+    L = 3
+    s = workload.OLMOE
+    ctx = moe.MoeContext(s["dim"], 64, 8, s["expert_hidden"], L, moe.DT_BF16, 0,
+                         workload.layer_stride(2048, 1024))
+    try:
+        ones = torch.ones(2048, device="cuda")
+        hosts = []
+        for l in range(L):
+            r, e, stride = workload.device_layer(2048, 1024, 64, seed=40 + l)
+            ctx.bind_layer(l, r, e, ones)
+            rh, eh = workload.host_copy(r, e)
+            hosts.append(MoeLayerHost(2048, 1024, 64, 8, moe.DT_BF16, 0, rh, eh, stride,
+                                      ffn_norm=np.ones(2048, np.float32)))
+        ctx.reserve(1)
+        x0 = workload.inputs(1, 2048, seed=41)
+        x = x0.clone()
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            for l in range(L):  # warm
+                ctx.block_device(l, x, stream=st)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            cs = torch.cuda.current_stream()
+            x.copy_(x0)
+            for l in range(L):
+                ctx.block_device(l, x, stream=cs)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        want = x0.cpu().numpy()
+        for l in range(L):
+            want, _ = orc.moe_block(hosts[l], want)
+        assert rel_err(x.cpu().numpy() - x0.cpu().numpy(), want - x0.cpu().numpy()) < 1e-4
+        del g
+    finally:
+        ctx.close()
