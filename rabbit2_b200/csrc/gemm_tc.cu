@@ -36,31 +36,34 @@ namespace {
 using namespace tc;
 
 constexpr int kBM = 128;   // weight rows per tile (MMA M)
-constexpr int kBN = 128;   // routed tokens per tile (MMA N)
 constexpr int kBK = 64;    // K elements per stage = one 128-byte swizzle row
 constexpr int kThreads = 192;
-constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB, also kBN * kBK * 2
+constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB weight tile
+constexpr int kStageBudget = 200 * 1024;   // shared memory for the operand ring
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 
-template <bool kGateUp>
+// BN: routed tokens per tile (the MMA's N), 32, 64 or 128.
+template <bool kGateUp, int BN>
 struct Cfg {
     static constexpr int NA = kGateUp ? 2 : 1;                 // weight tiles per stage
-    static constexpr int kStageBytes = (NA + 2) * kTileBytes;  // + token hi + token lo
-    static constexpr int kStages = kGateUp ? 3 : 4;
-    static constexpr int kAccCols = NA * kBN;                  // TMEM columns per accumulator buffer
-    static constexpr int kTmemCols = 2 * kAccCols;             // double buffered (512 or 256)
+    static constexpr int kBTileBytes = BN * kBK * 2;           // one token tile (hi or lo)
+    static constexpr int kStageBytes = NA * kTileBytes + 2 * kBTileBytes;
+    static constexpr int kStages = kStageBudget / kStageBytes > 6 ? 6 : kStageBudget / kStageBytes;
+    static constexpr int kAccCols = NA * BN;                   // TMEM columns per accumulator buffer
+    static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;  // double buffered
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(kTmemCols <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation");
 };
 
 __device__ __forceinline__ void record_error(unsigned* status, unsigned code) {
     atomicCAS(status, 0u, code);
 }
 
-template <bool kGateUp>
+template <bool kGateUp, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_bhi,
                        const __grid_constant__ CUtensorMap tm_blo, TcGemmArgs a) {
-    using C = Cfg<kGateUp>;
+    using C = Cfg<kGateUp, BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(st, &tm_w, &full[stage], kb * kBK, mb * kBM, e);
                 if (kGateUp) tma_load_3d(st + kTileBytes, &tm_w, &full[stage], kb * kBK, a.H + mb * kBM, e);
                 tma_load_2d(st + C::NA * kTileBytes, &tm_bhi, &full[stage], kb * kBK, p0);
-                tma_load_2d(st + (C::NA + 1) * kTileBytes, &tm_blo, &full[stage], kb * kBK, p0);
+                tma_load_2d(st + C::NA * kTileBytes + C::kBTileBytes, &tm_blo, &full[stage], kb * kBK, p0);
                 used[stage] = true;
                 last_parity[stage] = phase;
                 if (++stage == C::kStages) {
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (used[s] && !mbar_wait_bounded(&full[s], last_parity[s], kWaitNs)) record_error(a.status, 0x102);
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN);
+        constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
         int stage = 0;
         uint32_t phase = 0;
         int buf = 0;
@@ -154,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
-                const uint32_t sbh = sa + C::NA * kTileBytes, sbl = sbh + kTileBytes;
+                const uint32_t sbh = sa + C::NA * kTileBytes, sbl = sbh + C::kBTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; kk++) {
                     const uint32_t koff = kk * 32;  // 16 bf16 = 32 bytes along K
@@ -164,8 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_bf16(d1, a1, bl, idesc, 1u);
                     if (kGateUp) {
                         const uint64_t a3 = sw128_kmajor_desc(sa + kTileBytes + koff);
-                        mma_bf16(d1 + kBN, a3, bh, idesc, (kb | kk) != 0);
-                        mma_bf16(d1 + kBN, a3, bl, idesc, 1u);
+                        mma_bf16(d1 + BN, a3, bh, idesc, (kb | kk) != 0);
+                        mma_bf16(d1 + BN, a3, bl, idesc, 1u);
                     }
                 }
                 mma_commit(&empty[stage]);
@@ -193,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int tbi = tile / a.MB, mb = tile - tbi * a.MB;
             const int p0 = a.tb_p0[tbi], p1 = a.tb_p1[tbi];
-            const int ntok = min(kBN, p1 - p0);
+            const int ntok = min(BN, p1 - p0);
             bool ok = mbar_wait_bounded(&tfull[buf], acc_phase, kWaitNs);
             ok = __all_sync(FULL_MASK, ok);
             if (!ok) {
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_32x32b_x32(tbase + j0, g);
                 if (kGateUp) {
                     uint32_t u[32];
-                    tmem_ld_32x32b_x32(tbase + kBN + j0, u);
+                    tmem_ld_32x32b_x32(tbase + BN + j0, u);
                     tmem_ld_wait();
                     const int col = mb * kBM + row;
 #pragma unroll
@@ -269,13 +272,13 @@ __global__ void __launch_bounds__(256) gather_split_kernel(const float* __restri
     }
 }
 
-// Token blocks of kBN routed slots per active expert (one CTA, E <= 256).
+// Token blocks of bn routed slots per active expert (one CTA, E <= 256).
 __global__ void __launch_bounds__(256) tc_schedule_kernel(const int32_t* counts, const int32_t* offsets, int E,
-                                                          int32_t* tb_e, int32_t* tb_p0, int32_t* tb_p1,
+                                                          int bn, int32_t* tb_e, int32_t* tb_p0, int32_t* tb_p1,
                                                           int32_t* n_tb) {
     __shared__ int32_t s_nt[kMaxExperts + 1];
     const int e = threadIdx.x;
-    const int nt = (e < E) ? (counts[e] + kBN - 1) / kBN : 0;
+    const int nt = (e < E) ? (counts[e] + bn - 1) / bn : 0;
     s_nt[e] = nt;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -293,7 +296,7 @@ __global__ void __launch_bounds__(256) tc_schedule_kernel(const int32_t* counts,
         const int base = s_nt[e], p_end = offsets[e + 1];
         for (int j = 0; j < nt; j++) {
             tb_e[base + j] = e;
-            tb_p0[base + j] = offsets[e] + j * kBN;
+            tb_p0[base + j] = offsets[e] + j * bn;
             tb_p1[base + j] = p_end;
         }
     }
@@ -316,20 +319,41 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+template <bool kGateUp, int BN>
+cudaError_t launch_gemm_bn(const CUtensorMap& w, const CUtensorMap& bhi, const CUtensorMap& blo,
+                           const TcGemmArgs& a, int grid, cudaStream_t s) {
+    using C = Cfg<kGateUp, BN>;
+    cudaError_t err = cudaFuncSetAttribute(moe_tc_gemm_kernel<kGateUp, BN>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    moe_tc_gemm_kernel<kGateUp, BN><<<grid, kThreads, C::kSmemBytes, s>>>(w, bhi, blo, a);
+    return cudaGetLastError();
+}
+
 template <bool kGateUp>
 cudaError_t launch_gemm(const CUtensorMap& w, const CUtensorMap& bhi, const CUtensorMap& blo, const TcGemmArgs& a,
                         int grid, cudaStream_t s) {
-    using C = Cfg<kGateUp>;
-    cudaError_t err = cudaFuncSetAttribute(moe_tc_gemm_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           C::kSmemBytes);
-    if (err != cudaSuccess) return err;
-    moe_tc_gemm_kernel<kGateUp><<<grid, kThreads, C::kSmemBytes, s>>>(w, bhi, blo, a);
-    return cudaGetLastError();
+    switch (a.BN) {
+        case 32: return launch_gemm_bn<kGateUp, 32>(w, bhi, blo, a, grid, s);
+        case 64: return launch_gemm_bn<kGateUp, 64>(w, bhi, blo, a, grid, s);
+        case 128: return launch_gemm_bn<kGateUp, 128>(w, bhi, blo, a, grid, s);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace
 
-int tc_block_n() { return kBN; }
+int tc_block_n() { return 128; }
+
+// Token-tile width for a call of T tokens: the MMA's N is wasted on empty
+// columns when an expert sees fewer tokens than N (uniform routing gives
+// T*K/E tokens per expert).
+int tc_pick_bn(int T, int K, int E) {
+    const long per_expert = ((long)T * K + E - 1) / E;
+    if (per_expert <= 32) return 32;
+    if (per_expert <= 96) return 64;
+    return 128;
+}
 
 bool tc_supported(int D, int H, int dtype) {
     return dtype == 1 && D % kBM == 0 && H % kBM == 0 && D % kBK == 0 && H % kBK == 0 && encode_fn() != nullptr;
@@ -372,9 +396,9 @@ cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int
     return cudaGetLastError();
 }
 
-cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int32_t* tb_e, int32_t* tb_p0,
-                               int32_t* tb_p1, int32_t* n_tb, cudaStream_t s) {
-    tc_schedule_kernel<<<1, 256, 0, s>>>(counts, offsets, E, tb_e, tb_p0, tb_p1, n_tb);
+cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int bn, int32_t* tb_e,
+                               int32_t* tb_p0, int32_t* tb_p1, int32_t* n_tb, cudaStream_t s) {
+    tc_schedule_kernel<<<1, 256, 0, s>>>(counts, offsets, E, bn, tb_e, tb_p0, tb_p1, n_tb);
     return cudaGetLastError();
 }
 

@@ -119,6 +119,7 @@ struct TcGemmArgs {
     const int32_t* tb_p0;     // [n_tb] first slot position of the block
     const int32_t* tb_p1;     // [n_tb] end of the expert's slot range
     const int32_t* n_tb;      // [1]
+    int BN;                   // routed tokens per tile: 32, 64 or 128
     int MB;                   // 128-row weight blocks per token block (H/128 gate/up, D/128 down)
     int KB;                   // 64-element K blocks (D/64 gate/up, H/64 down)
     int H, D;
@@ -128,13 +129,14 @@ struct TcGemmArgs {
     unsigned* status;         // 0, or the code of a timed-out pipeline wait
 };
 int tc_block_n();
+int tc_pick_bn(int T, int K, int E);
 bool tc_supported(int D, int H, int dtype);
 bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int box_rows);
 bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride);
 cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
                                 cudaStream_t s);
-cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int32_t* tb_e, int32_t* tb_p0,
-                               int32_t* tb_p1, int32_t* n_tb, cudaStream_t s);
+cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int bn, int32_t* tb_e,
+                               int32_t* tb_p0, int32_t* tb_p1, int32_t* n_tb, cudaStream_t s);
 cudaError_t launch_tc_gateup(const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
                              const TcGemmArgs& a, int grid, cudaStream_t s);
 cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const CUtensorMap& hlo, const TcGemmArgs& a,

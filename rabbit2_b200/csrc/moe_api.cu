@@ -65,7 +65,7 @@ struct Workspace {
     void *xhi, *xlo, *hhi, *hlo;
     int32_t *tb_e, *tb_p0, *tb_p1, *n_tb;
     bool tc_maps = false;
-    CUtensorMap m_xhi, m_xlo, m_hhi, m_hlo;
+    CUtensorMap m_xhi[3], m_xlo[3], m_hhi[3], m_hlo[3];  // token-tile widths 32, 64, 128
 };
 
 }  // namespace
@@ -106,7 +106,7 @@ int reserve(RbtMoe* m, int T) {
     const RbtMoeConfig& c = m->cfg;
     const size_t D = c.dim, E = c.n_experts, K = c.top_k, H = c.expert_hidden, S = (size_t)T * K;
     const size_t tiles = (size_t)rbt::router_token_tiles(T) + 1;
-    const size_t ntb = S / rbt::tc_block_n() + E + 1;
+    const size_t ntb = S / 32 + E + 1;  // token blocks at the narrowest tile width
     const bool tc = rbt::tc_supported(c.dim, c.expert_hidden, c.dtype);
     // split-bf16 operand rows: at least one full 128-row TMA box, whole boxes
     const size_t SB = tc ? ((S > 128 ? S : 128) + 127) / 128 * 128 : 0;
@@ -153,10 +153,14 @@ int reserve(RbtMoe* m, int T) {
     CU(cudaMemsetAsync(w.gbar, 0, 8, m->stream));
     CU(cudaStreamSynchronize(m->stream));
     if (tc) {
-        w.tc_maps = rbt::make_map_2d(&w.m_xhi, w.xhi, c.dim, (long)SB, rbt::tc_block_n()) &&
-                    rbt::make_map_2d(&w.m_xlo, w.xlo, c.dim, (long)SB, rbt::tc_block_n()) &&
-                    rbt::make_map_2d(&w.m_hhi, w.hhi, c.expert_hidden, (long)SB, rbt::tc_block_n()) &&
-                    rbt::make_map_2d(&w.m_hlo, w.hlo, c.expert_hidden, (long)SB, rbt::tc_block_n());
+        w.tc_maps = true;
+        for (int i = 0; i < 3; i++) {
+            const int bn = 32 << i;
+            w.tc_maps = w.tc_maps && rbt::make_map_2d(&w.m_xhi[i], w.xhi, c.dim, (long)SB, bn) &&
+                        rbt::make_map_2d(&w.m_xlo[i], w.xlo, c.dim, (long)SB, bn) &&
+                        rbt::make_map_2d(&w.m_hhi[i], w.hhi, c.expert_hidden, (long)SB, bn) &&
+                        rbt::make_map_2d(&w.m_hlo[i], w.hlo, c.expert_hidden, (long)SB, bn);
+        }
     }
     if (m->ws.block) CU(cudaFree(m->ws.block));
     w.block = block;
@@ -294,17 +298,20 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         const int S = T * c.top_k;
         if (!clk.begin(5)) return 0;
         CU(rbt::launch_gather_split(xb, w.perm, S, c.dim, c.top_k, w.xhi, w.xlo, s));
-        CU(rbt::launch_tc_schedule(w.counts, w.offsets, c.n_experts, w.tb_e, w.tb_p0, w.tb_p1, w.n_tb, s));
+        const int bn = rbt::tc_pick_bn(T, c.top_k, c.n_experts);
+        const int bi = bn == 32 ? 0 : (bn == 64 ? 1 : 2);
+        CU(rbt::launch_tc_schedule(w.counts, w.offsets, c.n_experts, bn, w.tb_e, w.tb_p0, w.tb_p1, w.n_tb, s));
         m->prof.launches++;
         rbt::TcGemmArgs ta{};
+        ta.BN = bn;
         ta.tb_e = w.tb_e; ta.tb_p0 = w.tb_p0; ta.tb_p1 = w.tb_p1; ta.n_tb = w.n_tb;
         ta.H = c.expert_hidden; ta.D = c.dim; ta.h_hi = w.hhi; ta.h_lo = w.hlo; ta.y = w.y; ta.status = w.status;
         ta.MB = c.expert_hidden / 128; ta.KB = c.dim / 64;
         if (!clk.begin(2)) return 0;
-        CU(rbt::launch_tc_gateup(L.w_gateup, w.m_xhi, w.m_xlo, ta, m->sm_count, s));
+        CU(rbt::launch_tc_gateup(L.w_gateup, w.m_xhi[bi], w.m_xlo[bi], ta, m->sm_count, s));
         ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
         if (!clk.begin(3)) return 0;
-        CU(rbt::launch_tc_down(L.w_down, w.m_hhi, w.m_hlo, ta, m->sm_count, s));
+        CU(rbt::launch_tc_down(L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
     } else if (m->path != 3 && rbt::stream_supported(sa_of(m, L, xb, x, out, T, block), c.dtype)) {
         const rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, block);
         if (!clk.begin(2)) return 0;
