@@ -220,8 +220,11 @@ def stage_cost(T, U, S):
               "gate_up": U * 2 * H * D * w + T * D * 4 + S * H * 4,
               "down": U * H * D * w + S * H * 4 + S * D * 4,
               "combine": S * D * 4 + T * D * 4 * 2 + S * 8,
-              "gather": T * D * 4 + S * D * 4}
-    flops = {"router": 2 * T * E * D, "gate_up": 4 * S * H * D, "down": 2 * S * H * D}
+              "gather": T * D * 4 + S * D * 4,
+              # the one-token kernel: router + the U experts' three matrices + x in/out + h through L2
+              "decode_fused": E * D * w + U * 3 * H * D * w + T * D * 4 * 2 + 2 * S * H * 4}
+    flops = {"router": 2 * T * E * D, "gate_up": 4 * S * H * D, "down": 2 * S * H * D,
+             "decode_fused": T * (2 * E * D + 6 * K * H * D)}
     return bytes_, flops
 
 

@@ -84,7 +84,7 @@ struct RbtMoe {
     int device = 0;
     int sm_count = 0;
     int path = 0;
-    int gemm_min_tokens = 64;  // automatic path: tensor-core GEMM from this many tokens
+    int gemm_min_tokens = 2;   // automatic path: tensor-core GEMM from this many tokens (one token: fused decode)
     size_t esz = 2;
     cudaStream_t stream = nullptr;
     std::vector<Layer> layers;

@@ -22,7 +22,7 @@ from tests.golden.cases import case_keys, load_case, pack_layer  # noqa: E402
 MOE_RTOL = 2e-5      # CUDA-core path: fp32 accumulation in a different order
 MOE_RTOL_TC = 1e-4   # tensor-core path: bf16 hi+lo split activations (16 significant bits)
 NORTH_STAR = 1e-3
-GEMM_MIN_TOKENS = 64  # automatic path switch of librbt_moe (RBT_MOE_GEMM_MIN_TOKENS)
+GEMM_MIN_TOKENS = 2   # automatic path switch of librbt_moe (RBT_MOE_GEMM_MIN_TOKENS)
 
 
 def rel_err(got, want):
