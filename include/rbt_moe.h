@@ -128,6 +128,34 @@ typedef struct RbtMoeProfile {
  * out may be NULL. */
 int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
 
+/* The one-token MoE block for callers that cannot allocate GPU memory.  No
+ * counterpart in the reference (its engine has no GPU and no allocator
+ * constraints); it exists for code that runs inside a framework which already
+ * owns the device memory (a caching allocator, or a server that reserves most
+ * of HBM up front), and for latency-critical decode loops that cannot take
+ * cudaMalloc's implicit synchronisation.  It needs no context and calls no
+ * cudaMalloc, cudaFree or allocating library routine: its scratch is a fixed
+ * RBT_MOE_NOALLOC_SCRATCH_BYTES array in the library's own device memory,
+ * present on every GPU that loads the library until the process exits.
+ *
+ * Runs on the calling thread's current CUDA device, enqueued on `stream`
+ * (NULL = default stream), without synchronising.  All pointers are device
+ * pointers: the layer's weights exactly as for rbt_moe_bind_layer,
+ * d_router_bias may be NULL, and d_routing_out ([top_k] int32) may be NULL.
+ * d_ffn_norm != NULL gives the block form, d_out = d_x + MoE(rmsnorm(d_x))
+ * (d_out may equal d_x); d_ffn_norm == NULL gives d_out = MoE(d_x).
+ * Limits: bf16 weights, dim <= 2048 and a multiple of 8, 16-byte aligned
+ * d_x/d_router/d_experts, and scratch of n_experts and top_k * expert_hidden
+ * floats within RBT_MOE_NOALLOC_SCRATCH_BYTES (top_k * expert_hidden <= 8192);
+ * other models are rejected with an error.  The first call on a device looks
+ * up the array's device address; make that first call before any stream
+ * capture.  Calls share the array: two calls whose kernels overlap on the GPU
+ * (unordered streams) race. */
+#define RBT_MOE_NOALLOC_SCRATCH_BYTES 49152
+int rbt_moe_decode_noalloc(const RbtMoeConfig *cfg, const float *d_ffn_norm, const void *d_router,
+                           const float *d_router_bias, const void *d_experts, const float *d_x, float *d_out,
+                           int32_t *d_routing_out, void *stream);
+
 /* Last error message of the calling thread ("" if none). */
 const char *rbt_moe_last_error(void);
 

@@ -36,6 +36,16 @@ int fail(const char* fmt, ...) {
     return 0;
 }
 
+}  // namespace
+
+namespace rbt {
+// Sets the calling thread's rbt_moe_last_error() text (used by the entry points
+// defined in other files of the library).
+void set_last_error(const char* msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
+}  // namespace rbt
+
+namespace {
+
 #define CU(call)                                                                                  \
     do {                                                                                          \
         cudaError_t e_ = (call);                                                                  \
