@@ -144,9 +144,9 @@ int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
  * d_router_bias may be NULL, and d_routing_out ([top_k] int32) may be NULL.
  * d_ffn_norm != NULL gives the block form, d_out = d_x + MoE(rmsnorm(d_x))
  * (d_out may equal d_x); d_ffn_norm == NULL gives d_out = MoE(d_x).
- * Limits: bf16 weights, dim <= 2048 and a multiple of 8, 16-byte aligned
- * d_x/d_router/d_experts, and scratch of n_experts and top_k * expert_hidden
- * floats within RBT_MOE_NOALLOC_SCRATCH_BYTES (top_k * expert_hidden <= 8192);
+ * Limits: bf16 weights, dim <= 2048 and a multiple of 8, expert_hidden <=
+ * 1024, top_k <= 16, 16-byte aligned d_x/d_router/d_experts, and scratch of
+ * n_experts + top_k * expert_hidden floats within RBT_MOE_NOALLOC_SCRATCH_BYTES;
  * other models are rejected with an error.  The first call on a device looks
  * up the array's device address; make that first call before any stream
  * capture.  Calls share the array: two calls whose kernels overlap on the GPU

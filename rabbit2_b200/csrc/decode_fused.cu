@@ -3,28 +3,33 @@
 // experts' SwiGLU FFNs, the weighted combine and the residual -- as a single
 // cooperative launch of one CTA per SM.  Batch-1 decode is memory-bound on the
 // K experts' weights (8 x 12 MB at OLMoE-1B-7B), so the kernel exists to keep
-// HBM streaming and to avoid launch gaps and cross-kernel drains.
+// HBM streaming: no launch gaps and no kernel-boundary drains.  Cross-CTA
+// ordering is by counters in global memory (release by __threadfence +
+// atomic, acquire by ld.acquire), each wait bounded by %globaltimer; the launch
+// is cooperative, so every CTA is resident and every wait ends.
 //
-// Phases (grid barriers are bounded spins on a global counter; the launch is
-// cooperative, so every CTA is resident):
-//   0  every CTA: x (and rmsnorm(x) for the block form) into shared memory --
-//      the same deterministic reduction everywhere, so every CTA holds the same xb
-//   1  CTA b computes router logits e = b, b+G, ...: the four sequential chains
-//      of the reference's scalar matvec (rabbit2.c:378-387), separately rounded
-//      products and sums, combined (s0+s1)+(s2+s3); logits to global
-//   -- grid barrier 1
-//   2  every CTA: softmax and top-k from the E logits (one warp, exactly as the
-//      router kernel), the K slots sorted by expert; CTA 0 publishes routing
-//   3  gate/up: the producer thread streams 8 rows of w1 and of w3 per unit with
-//      cp.async.bulk into a 3 x 64 KB ring; 8 consumer warps form
-//      h = silu(w1 . x) * (w3 . x) with packed fma.rn.f32x2 (x in registers)
-//   -- grid barrier 2 (consumer warps only: the producer is already streaming
-//      w2 rows into the ring, which do not depend on h)
-//   4  down + combine + residual: h of the K slots in shared memory; units of
-//      2 output rows x K experts; out[d] = x[d] + sum_k w_k y_k[d], k in
-//      selection order (rabbit2.c:539-542)
-// Every wait (mbarrier or grid barrier) is bounded by %globaltimer; a timeout
-// records a code in `status` and the kernel unwinds.
+//   0  every CTA: bulk-copies x (and, if it computes one, its router row) into
+//      shared memory; rmsnorm(x) for the block form, the same fixed-order
+//      reduction in every CTA so all hold the same xb
+//   1  CTAs compute router logits -- the four sequential chains of the
+//      reference's scalar matvec (rabbit2.c:378-387), separately rounded
+//      products and sums, (s0+s1)+(s2+s3) -- each expert by two CTAs when the
+//      grid has room; the first copy to finish publishes it (both are equal)
+//   2  every CTA, as soon as all E logits are published: softmax and top-k
+//      (selection order = rank: higher probability, or equal and lower index),
+//      the K slots sorted by expert; CTA 0 publishes the routing outputs
+//   3  gate/up: each CTA takes a contiguous range of units (8 rows of w1 and
+//      the same 8 rows of w3); as soon as routing is known its producer thread
+//      issues L2 prefetches for every weight byte the CTA will need (gate/up
+//      units and its w2 rows), so HBM streams continuously while the
+//      units pass through a 3 x 64 KB shared-memory ring (cp.async.bulk, now L2
+//      hits); 8 consumer warps form h = silu(w1 . x) * (w3 . x) (packed
+//      fma.rn.f32x2, x in registers)
+//   -- grid barrier (consumer warps only; the producer keeps loading w2 rows)
+//   4  down + combine: units of 2 output rows x the K experts; consumer warp w
+//      keeps the h rows of chosen experts w and w+8 in registers; then
+//      out[d] = x[d] + sum_k w_k y_k[d] in selection order (rabbit2.c:539-542)
+// The last CTA to leave returns every counter to zero.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -41,9 +46,13 @@ constexpr int kThreads = (kWarps + 1) * 32;
 constexpr int kSlot = 65536;       // ring slot bytes
 constexpr int kSlots = 3;
 constexpr int kGURows = 8;         // w1/w3 rows per gate-up unit
+constexpr int kMaxH = 1024;        // a lane's slice of one h row stays in registers (H / 256 vectors)
 constexpr int kDR = 2;             // w2 rows per down unit
-constexpr int kHBuf = 32768;       // h of the K slots, bytes
 constexpr uint64_t kWaitNs = 2000000000ull;
+
+// sync words (a.sync): [0] CTAs done, [1] grid-barrier arrivals, [2..3] unused,
+// [4, 4+E) logit published, [4+E, 4+E+K) unused
+constexpr int kSyncHead = 4;
 
 __device__ __forceinline__ void record_error(unsigned* status, unsigned code) { atomicCAS(status, 0u, code); }
 
@@ -68,15 +77,13 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     return v;
 }
 
-// One thread: publish this CTA's writes, arrive, and wait until `target` CTAs
-// have arrived.  Returns false on timeout.
-__device__ bool grid_arrive_wait(unsigned* counter, unsigned target) {
-    __threadfence();
-    atomicAdd(counter, 1u);
+// Spin (bounded) until *p >= target.
+__device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
+    if (ld_acquire(p) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire(counter) < target) {
+    while (ld_acquire(p) < target) {
         if (globaltimer_ns() - t0 > kWaitNs) return false;
-        __nanosleep(64);
+        __nanosleep(32);
     }
     return true;
 }
@@ -84,21 +91,29 @@ __device__ bool grid_arrive_wait(unsigned* counter, unsigned target) {
 __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem;
-    float* hbuf = reinterpret_cast<float*>(smem + kSlots * kSlot);        // [K][H]
-    float* ybuf = hbuf + kHBuf / 4;                                       // [2 units][K][kDR]
-    static_assert(kSlot >= kMaxExperts * 4, "softmax scratch lives in ring slot 2");
-    __shared__ uint64_t full[kSlots], empty[kSlots], hbar;
+    float* ybuf = reinterpret_cast<float*>(smem + kSlots * kSlot);  // [band rows][K]
+    __shared__ uint64_t full[kSlots], empty[kSlots], xbar, rbar;
     __shared__ int32_t s_idx[kMaxTopK], s_pos[kMaxTopK], s_act[kMaxTopK];
-    __shared__ float s_p[kMaxTopK], s_w[kMaxTopK];
+    __shared__ float s_p[kMaxTopK], s_w[kMaxTopK], s_prob[kMaxExperts];
     __shared__ float s_red[kThreads / 32];
     __shared__ int s_fail;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = a.D, H = a.H, E = a.E, K = a.K;
-    const int G = gridDim.x;
-    float* xs = reinterpret_cast<float*>(ring);             // phase 0-2: xb [D]
-    float* wrow = reinterpret_cast<float*>(ring + kSlot);   // phase 1: one router row as f32 [D]
-    float* s_ex = reinterpret_cast<float*>(ring + 2 * kSlot);  // phase 2: exp(l - max) [E]
+    const int G = gridDim.x, b = blockIdx.x;
+    unsigned* done_cnt = a.sync;
+    unsigned* bar_cnt = a.sync + 1;
+    unsigned* lflag = a.sync + kSyncHead;
+    float* xs = reinterpret_cast<float*>(ring);                   // phases 0-2: xb [D]
+    uint16_t* wrow = reinterpret_cast<uint16_t*>(ring + kSlot);   // phase 1: this CTA's router rows
+
+    // router rows this CTA computes: two copies of every expert when the grid has room
+    const bool dup = G >= 2 * E;
+    const int e_first = dup ? (b < 2 * E ? b % E : E) : b;
+    const int e_step = dup ? E : G;
+    int n_rows = 0;
+    for (int e = e_first; e < E; e += e_step) n_rows++;
+    if (dup && n_rows > 1) n_rows = 1;
 
     if (tid == 0) {
         s_fail = 0;
@@ -106,11 +121,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarps);
         }
-        mbar_init(&hbar, 1);
+        mbar_init(&xbar, 1);
+        mbar_init(&rbar, 1);
         fence_mbar_init();
+        mbar_arrive_expect_tx(&xbar, (uint32_t)D * 4);
+        bulk_load(xs, a.x, (uint32_t)D * 4, &xbar);
+        if (n_rows > 0) {
+            mbar_arrive_expect_tx(&rbar, (uint32_t)n_rows * D * 2);
+            for (int j = 0; j < n_rows; j++)
+                bulk_load(wrow + (size_t)j * D, a.router + (size_t)(e_first + j * e_step) * D, (uint32_t)D * 2, &rbar);
+        }
     }
     // ---------------------------------------------------------------- phase 0
-    for (int i = tid * 4; i < D; i += kThreads * 4) *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.x + i);
+    __syncthreads();
+    if (!mbar_wait_bounded(&xbar, 0, kWaitNs)) {
+        record_error(a.status, 0x604);
+        s_fail = 1;
+    }
     __syncthreads();
     if (a.ffn_norm) {  // rmsnorm, the same fixed-order reduction in every CTA
         float ss = 0.0f;
@@ -126,30 +153,40 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
         __syncthreads();
     }
     // ---------------------------------------------------------------- phase 1: exact router logits
-    for (int e = blockIdx.x; e < E; e += G) {
-        for (int i = tid * 8; i < D; i += kThreads * 8) {
-            const uint4 v = *reinterpret_cast<const uint4*>(a.router + (size_t)e * D + i);
-            float f[8];
-            WeightTraits<uint16_t>::unpack(v, f);
-            *reinterpret_cast<float4*>(wrow + i) = make_float4(f[0], f[1], f[2], f[3]);
-            *reinterpret_cast<float4*>(wrow + i + 4) = make_float4(f[4], f[5], f[6], f[7]);
+    // The products w[i]*x[i] are independent: every thread rounds its share of
+    // them into `prods`, laid out chain-major (chain c = i mod 4 holds its D/4
+    // products contiguously).  Lane c of warp 0 then runs chain c's D/4
+    // dependent adds in order, reading 4 products per 16-byte load.
+    float* prods = reinterpret_cast<float*>(ring + 2 * kSlot);  // [4][D/4]
+    for (int j = 0; j < n_rows; j++) {
+        const int e = e_first + j * e_step;
+        if (j == 0) {
+            const bool got = mbar_wait_bounded(&rbar, 0, kWaitNs);
+            if (!got) {
+                record_error(a.status, 0x600);
+                s_fail = 1;
+            }
         }
+        __syncthreads();
+        if (s_fail) break;
+        const uint16_t* wr = wrow + (size_t)j * D;
+        const int q = D / 4;
+        for (int i = tid; i < 4 * q; i += kThreads)
+            prods[(i & 3) * q + (i >> 2)] = __fmul_rn(bf16_bits_to_f32(wr[i]), xs[i]);
         __syncthreads();
         if (warp == 0) {
             float s = 0.0f;
             if (lane < 4) {
-                int i = lane;
-                for (; i + 28 < D; i += 32) {
-                    float w[8], x[8];
-#pragma unroll
-                    for (int u = 0; u < 8; u++) {
-                        w[u] = wrow[i + 4 * u];
-                        x[u] = xs[i + 4 * u];
-                    }
-#pragma unroll
-                    for (int u = 0; u < 8; u++) s = __fadd_rn(s, __fmul_rn(w[u], x[u]));
+                const float* pc = prods + lane * q;
+                int i = 0;
+                for (; i + 4 <= q; i += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(pc + i);
+                    s = __fadd_rn(s, v.x);
+                    s = __fadd_rn(s, v.y);
+                    s = __fadd_rn(s, v.z);
+                    s = __fadd_rn(s, v.w);
                 }
-                for (; i < D; i += 4) s = __fadd_rn(s, __fmul_rn(wrow[i], xs[i]));
+                for (; i < q; i++) s = __fadd_rn(s, pc[i]);
             }
             const float s1 = __shfl_down_sync(FULL_MASK, s, 1);
             const float a01 = __fadd_rn(s, s1);
@@ -157,26 +194,34 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
             if (lane == 0) {
                 float logit = __fadd_rn(a01, a23);
                 if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
-                a.logits[e] = logit;
+                a.logits[e] = logit;  // both copies write the same bits
+                __threadfence();
+                atomicExch(lflag + e, 1u);
             }
         }
         __syncthreads();
     }
-    __syncthreads();
-    if (tid == 0 && !grid_arrive_wait(a.bar, (unsigned)G)) {
-        record_error(a.status, 0x601);
-        s_fail = 1;
+    // ---------------------------------------------------------------- phase 2: softmax, top-k, slot order
+    if (warp == 0) {
+        bool ok = true;
+        for (int e = lane; e < E; e += 32) ok = ok && wait_count(lflag + e, 1u);
+        if (!__all_sync(FULL_MASK, ok)) {
+            if (lane == 0) {
+                record_error(a.status, 0x601);
+                s_fail = 1;
+            }
+        }
     }
     __syncthreads();
-    // ---------------------------------------------------------------- phase 2: softmax, top-k, slot order
     if (warp == 0 && !s_fail) {
         constexpr int NJ = kMaxExperts / 32;
+        const int nj = (E + 31) / 32;
         float l[NJ], p[NJ];
         float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int e = lane + 32 * j;
-            l[j] = (e < E) ? __ldcg(a.logits + e) : -INFINITY;
+            l[j] = (j < nj && e < E) ? __ldcg(a.logits + e) : -INFINITY;
             mx = fmaxf(mx, l[j]);
         }
 #pragma unroll
@@ -184,44 +229,44 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int e = lane + 32 * j;
-            p[j] = (e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
-            if (e < E) s_ex[e] = p[j];
+            p[j] = (j < nj && e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
         }
-        __syncwarp();
+        // the sequential sum in expert order (rabbit2.c:403), values passed by shuffles
         float sum = 0.0f;
-        if (lane == 0)
-            for (int e = 0; e < E; e++) sum = __fadd_rn(sum, s_ex[e]);
-        sum = __shfl_sync(FULL_MASK, sum, 0);
 #pragma unroll
-        for (int j = 0; j < NJ; j++) p[j] = __fdiv_rn(p[j], sum);
-        unsigned used = 0;
-        for (int k = 0; k < K; k++) {
-            float bp = -INFINITY;
-            int be = 0x7fffffff;
+        for (int j = 0; j < NJ; j++) {
+            if (j < nj) {
 #pragma unroll
-            for (int j = 0; j < NJ; j++) {
-                const int e = lane + 32 * j;
-                if (e < E && !((used >> j) & 1u) && (p[j] > bp || be == 0x7fffffff)) {
-                    bp = p[j];
-                    be = e;
+                for (int src = 0; src < 32; src++) {
+                    const float v = __shfl_sync(FULL_MASK, p[j], src);
+                    if (32 * j + src < E) sum = __fadd_rn(sum, v);
                 }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float op = __shfl_xor_sync(FULL_MASK, bp, o);
-                const int oe = __shfl_xor_sync(FULL_MASK, be, o);
-                if (oe != 0x7fffffff && (be == 0x7fffffff || op > bp || (op == bp && oe < be))) {
-                    bp = op;
-                    be = oe;
-                }
-            }
-            if ((be & 31) == lane) used |= 1u << (be >> 5);
-            if (lane == 0) {
-                s_idx[k] = be;
-                s_p[k] = bp;
             }
         }
-        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            if (j < nj && e < E) s_prob[e] = __fdiv_rn(p[j], sum);
+        }
+    }
+    __syncthreads();
+    // top-k by rank: expert e is chosen in round r when exactly r experts beat it
+    // (higher probability, or equal probability and lower index) -- the order of
+    // the reference's K rounds of strict-'>' scans (rabbit2.c:519-528)
+    if (!s_fail && tid < E) {
+        const float pe = s_prob[tid];
+        int r = 0;
+        for (int f = 0; f < E; f++) {
+            const float pf = s_prob[f];
+            r += (pf > pe) || (pf == pe && f < tid);
+        }
+        if (r < K) {
+            s_idx[r] = tid;
+            s_p[r] = pe;
+        }
+    }
+    __syncthreads();
+    if (warp == 0 && !s_fail) {
         float wsum = 0.0f;
         for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
         for (int k = lane; k < K; k += 32) {
@@ -232,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
             s_act[pos] = s_idx[k];
         }
         __syncwarp();
-        if (blockIdx.x == 0) {  // the routing outputs of the call
+        if (b == 0) {  // the routing outputs of the call
             for (int k = lane; k < K; k += 32) {
                 a.idx[k] = s_idx[k];
                 a.wt[k] = s_w[k];
@@ -261,13 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
 
     const int nvx = D / 8;   // 16-byte vectors per w1/w3 row
     const int nvh = H / 8;   // per w2 row
-    const uint32_t gu_half = (uint32_t)kGURows * D * 2;         // 8 rows of w1 (or w3)
-    const uint32_t dn_rows = (uint32_t)kDR * H * 2;             // 2 rows of w2 of one expert
+    const uint32_t gu_half = (uint32_t)kGURows * D * 2;  // 8 rows of w1 (or w3)
+    const uint32_t dn_rows = (uint32_t)kDR * H * 2;      // 2 rows of w2 of one expert
     const int units_per_e = H / kGURows;
     const int n_gu = fail0 ? 0 : K * units_per_e;
-    const int g0 = (int)((long)n_gu * blockIdx.x / G), g1 = (int)((long)n_gu * (blockIdx.x + 1) / G);
+    const int g0 = (int)((long)n_gu * b / G), g1 = (int)((long)n_gu * (b + 1) / G);
     const int n_dn = fail0 ? 0 : D / kDR;
-    const int d0 = (int)((long)n_dn * blockIdx.x / G), d1 = (int)((long)n_dn * (blockIdx.x + 1) / G);
+    const int d0 = (int)((long)n_dn * b / G), d1 = (int)((long)n_dn * (b + 1) / G);
+    const int ups = (int)(kSlot / ((uint32_t)K * dn_rows)) >= 2 ? 2 : 1;  // down units per ring slot
 
     // consumer lanes keep their slice of xb in registers before the ring is reused
     float xr[64];
@@ -300,14 +346,29 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
                 bulk_load(st + gu_half, w1 + (size_t)H * D * 2, gu_half, &full[slot]);
                 issued++;
                 if (++slot == kSlots) { slot = 0; ph ^= 1u; }
+                if (issued == kSlots || u + 1 == g1) {
+                    // the ring is full: ask L2 for everything else this CTA will read,
+                    // so HBM keeps streaming however long the ring takes to drain
+                    for (int v = u + 1; v < g1; v++) {
+                        const uint8_t* p1 = a.experts + (size_t)s_act[v / units_per_e] * a.stride +
+                                            (size_t)(v % units_per_e) * gu_half;
+                        prefetch_l2(p1, gu_half);
+                        prefetch_l2(p1 + (size_t)H * D * 2, gu_half);
+                    }
+                    if (d1 > d0)
+                        for (int pa = 0; pa < K; pa++)
+                            prefetch_l2(a.experts + (size_t)s_act[pa] * a.stride + (size_t)2 * H * D * 2 +
+                                            (size_t)d0 * dn_rows,
+                                        (uint32_t)(d1 - d0) * dn_rows);
+                }
             }
-            for (int u = d0; ok && u < d1; u += 2) {  // two down units per slot
+            for (int u = d0; ok && u < d1; u += ups) {  // down units, `ups` per slot
                 if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, kWaitNs)) {
                     record_error(a.status, 0x612);
                     ok = false;
                     break;
                 }
-                const int nu = min(2, d1 - u);
+                const int nu = min(ups, d1 - u);
                 uint8_t* st = ring + slot * kSlot;
                 mbar_arrive_expect_tx(&full[slot], nu * K * dn_rows);
                 for (int j = 0; j < nu; j++)
@@ -364,97 +425,115 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
             if (lane == 0) a.h[(size_t)pa * H + r] = gs / (1.0f + expf(-gs)) * us;
             if (++slot == kSlots) { slot = 0; ph ^= 1u; }
         }
-        // every CTA's h rows are written before any CTA reads h
-        named_sync(1, kWarps * 32);
-        if (tid == 0) {
-            if (!ok || s_fail || !grid_arrive_wait(a.bar, (unsigned)(2 * G))) {
-                if (ok && !s_fail) record_error(a.status, 0x602);
-                s_fail = 1;
-            } else {
-                mbar_arrive_expect_tx(&hbar, (uint32_t)K * H * 4);
-                bulk_load(hbuf, a.h, (uint32_t)K * H * 4, &hbar);
-            }
-        }
-        named_sync(1, kWarps * 32);
-        ok = ok && !s_fail;
-        if (ok) {
-            const bool got = mbar_wait_bounded(&hbar, 0, kWaitNs);
-            if (!__all_sync(FULL_MASK, got)) {
-                record_error(a.status, 0x622);
-                ok = false;
-            }
-        }
+        // every CTA's h rows are written (and every CTA has read x) before any
+        // CTA reads h or writes out
         if (!ok && lane == 0) s_fail = 1;
         named_sync(1, kWarps * 32);
-        // from here `ok` only changes through s_fail after a named barrier, so all
-        // consumer warps take the same number of barriers
-        for (int u = d0; !s_fail && u < d1; u += 2) {
+        if (tid == 0 && !s_fail) {
+            __threadfence();
+            atomicAdd(bar_cnt, 1u);
+            if (!wait_count(bar_cnt, (unsigned)G)) {
+                record_error(a.status, 0x602);
+                s_fail = 1;
+            }
+        }
+        named_sync(1, kWarps * 32);
+        // warp w owns the chosen experts w and w + 8: their h rows stay in registers
+        // for the whole phase, so shared memory only streams weights
+        float hr[2][32];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const int pa = warp + kWarps * q;
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                const int v = lane + 32 * m;
+                float4 h0 = make_float4(0.f, 0.f, 0.f, 0.f), h1 = h0;
+                if (!s_fail && pa < K && v < nvh) {
+                    h0 = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)pa * H + v * 8));
+                    h1 = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)pa * H + v * 8 + 4));
+                }
+                hr[q][8 * m] = h0.x; hr[q][8 * m + 1] = h0.y; hr[q][8 * m + 2] = h0.z; hr[q][8 * m + 3] = h0.w;
+                hr[q][8 * m + 4] = h1.x; hr[q][8 * m + 5] = h1.y; hr[q][8 * m + 6] = h1.z; hr[q][8 * m + 7] = h1.w;
+            }
+        }
+        // the per-expert results of the CTA's whole output band collect in ybuf
+        // ([row][slot position]); one barrier, then one combine
+        for (int u = d0; ok && !s_fail && u < d1; u += ups) {
             const bool got = mbar_wait_bounded(&full[slot], ph, kWaitNs);
             if (!__all_sync(FULL_MASK, got)) {
                 record_error(a.status, 0x623);
                 ok = false;
-                if (lane == 0) s_fail = 1;
+                break;
             }
-            const int nu = min(2, d1 - u);
+            const int nu = min(ups, d1 - u);
             const uint8_t* st = ring + slot * kSlot;
-            if (ok) {
-                for (int task = warp; task < nu * K * kDR; task += kWarps) {
-                    const int jr = task / kDR, rr = task - jr * kDR;    // jr = j*K + pa
-                    const int pa = jr % K;
-                    const uint4* w = reinterpret_cast<const uint4*>(st + jr * dn_rows + rr * H * 2);
-                    const float* hv = hbuf + (size_t)pa * H;
-                    uint64_t acc[4] = {0, 0, 0, 0};
-                    for (int v = lane; v < nvh; v += 32) {
-                        const uint4 q = w[v];
-                        const float4 h0 = *reinterpret_cast<const float4*>(hv + v * 8);
-                        const float4 h1 = *reinterpret_cast<const float4*>(hv + v * 8 + 4);
-                        acc[0] = ffma2(bf2(q.x), f2(h0.x, h0.y), acc[0]);
-                        acc[1] = ffma2(bf2(q.y), f2(h0.z, h0.w), acc[1]);
-                        acc[2] = ffma2(bf2(q.z), f2(h1.x, h1.y), acc[2]);
-                        acc[3] = ffma2(bf2(q.w), f2(h1.z, h1.w), acc[3]);
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const int pa = warp + kWarps * q;
+                if (pa >= K) continue;
+                for (int j = 0; j < nu; j++) {
+#pragma unroll
+                    for (int rr = 0; rr < kDR; rr++) {
+                        const uint4* w = reinterpret_cast<const uint4*>(st + (j * K + pa) * dn_rows + rr * H * 2);
+                        uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+                        for (int m = 0; m < 4; m++) {
+                            const int v = lane + 32 * m;
+                            if (v < nvh) {
+                                const uint4 qv = w[v];
+                                acc[0] = ffma2(bf2(qv.x), f2(hr[q][8 * m], hr[q][8 * m + 1]), acc[0]);
+                                acc[1] = ffma2(bf2(qv.y), f2(hr[q][8 * m + 2], hr[q][8 * m + 3]), acc[1]);
+                                acc[2] = ffma2(bf2(qv.z), f2(hr[q][8 * m + 4], hr[q][8 * m + 5]), acc[2]);
+                                acc[3] = ffma2(bf2(qv.w), f2(hr[q][8 * m + 6], hr[q][8 * m + 7]), acc[3]);
+                            }
+                        }
+                        const float sd = warp_sum((f2sum(acc[0]) + f2sum(acc[1])) + (f2sum(acc[2]) + f2sum(acc[3])));
+                        if (lane == 0) ybuf[((u - d0 + j) * kDR + rr) * K + pa] = sd;
                     }
-                    const float s = warp_sum((f2sum(acc[0]) + f2sum(acc[1])) + (f2sum(acc[2]) + f2sum(acc[3])));
-                    if (lane == 0) ybuf[jr * kDR + rr] = s;
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (++slot == kSlots) { slot = 0; ph ^= 1u; }
-            named_sync(1, kWarps * 32);
-            ok = !s_fail;
-            if (ok && tid < nu * kDR) {  // combine in selection order, then the residual
-                const int j = tid / kDR, rr = tid - j * kDR;
-                const int d = (u + j) * kDR + rr;
-                float mo = 0.0f;
-                for (int k = 0; k < K; k++) mo = __fadd_rn(mo, __fmul_rn(s_w[k], ybuf[(j * K + s_pos[k]) * kDR + rr]));
-                a.out[d] = a.ffn_norm ? __fadd_rn(a.x[d], mo) : mo;
-            }
-            named_sync(1, kWarps * 32);
+        }
+        if (!ok && lane == 0) s_fail = 1;
+        named_sync(1, kWarps * 32);
+        const int nrows = (d1 - d0) * kDR;
+        if (!s_fail && tid < nrows) {  // combine in selection order, then the residual
+            const int d = d0 * kDR + tid;
+            float mo = 0.0f;
+            for (int k = 0; k < K; k++) mo = __fadd_rn(mo, __fmul_rn(s_w[k], ybuf[tid * K + s_pos[k]]));
+            a.out[d] = a.ffn_norm ? __fadd_rn(a.x[d], mo) : mo;
         }
     }
     __syncthreads();
-    if (tid == 0) {  // the last CTA out returns the barrier counters to zero
+    if (tid == 0) {  // the last CTA out returns every counter to zero
         __threadfence();
-        if (atomicAdd(a.bar + 1, 1u) == (unsigned)G - 1) {
-            atomicExch(a.bar, 0u);
-            atomicExch(a.bar + 1, 0u);
+        if (atomicAdd(done_cnt, 1u) == (unsigned)G - 1) {
+            for (int i = 1; i < kSyncHead + E + K; i++) atomicExch(a.sync + i, 0u);
+            __threadfence();
+            atomicExch(done_cnt, 0u);
         }
     }
 }
 
 }  // namespace
 
+int decode_sync_words(int E, int K) { return kSyncHead + E + K; }
+
 bool decode_fused_supported(int T, int D, int H, int E, int K, int dtype, const void* experts, size_t stride,
                             const void* x, const void* router) {
-    return T == 1 && dtype == 1 && D % 8 == 0 && D <= 2048 && H % kGURows == 0 && H % 8 == 0 && D % kDR == 0 &&
-           E <= kMaxExperts && K <= kMaxTopK && (size_t)K * H * 4 <= (size_t)kHBuf &&
-           2 * kGURows * D * 2 <= kSlot && 2 * K * kDR * H * 2 <= kSlot && stride % 16 == 0 &&
+    return T == 1 && dtype == 1 && D % 16 == 0 && D <= 2048 && H % kGURows == 0 && H % 8 == 0 && H <= kMaxH &&
+           D % kDR == 0 && E <= kMaxExperts && K <= 2 * kWarps && 2 * kGURows * D * 2 <= kSlot &&
+           K * kDR * H * 2 <= kSlot && stride % 16 == 0 &&
            (reinterpret_cast<uintptr_t>(experts) % 16) == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
            (reinterpret_cast<uintptr_t>(router) % 16) == 0;
 }
 
 cudaError_t launch_decode_fused(const DecodeArgs& a, int grid, cudaStream_t s) {
-    const size_t smem = (size_t)kSlots * kSlot + kHBuf + 2 * (size_t)a.K * kDR * 4;
+    // the output band of a CTA (ceil((D/2)/grid) units of 2 rows) times K results
+    const size_t band_rows = (size_t)kDR * ((a.D / kDR + grid - 1) / grid);
+    const size_t smem = (size_t)kSlots * kSlot + band_rows * a.K * 4;
     cudaError_t err = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess) return err;

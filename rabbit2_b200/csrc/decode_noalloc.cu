@@ -61,12 +61,12 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 // Byte offsets of the scratch parts for one configuration; returns the total.
 struct Layout {
-    size_t logits, h, idx, wt, counts, offsets, perm, slot_pos, active, n_active, bar, status, total;
+    size_t logits, h, idx, wt, counts, offsets, perm, slot_pos, active, n_active, sync, status, total;
 };
 Layout layout_for(int E, int K, int H) {
     Layout l{};
     size_t o = 0;
-    l.bar = o;        o = align256(o + 2 * sizeof(unsigned));
+    l.sync = o;       o = align256(o + (size_t)rbt::decode_sync_words(E, K) * sizeof(unsigned));
     l.status = o;     o = align256(o + sizeof(unsigned));
     l.n_active = o;   o = align256(o + sizeof(int32_t));
     l.logits = o;     o = align256(o + (size_t)E * sizeof(float));
@@ -99,7 +99,8 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     if (!rbt::decode_fused_supported(1, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, d_experts,
                                      c.expert_stride, d_x, d_router))
         return fail("rbt_moe_decode_noalloc: unsupported model for the one-token kernel (needs bf16 weights, "
-                    "dim <= 2048 and a multiple of 8, top_k * expert_hidden <= 8192, 16-byte aligned pointers)");
+                    "dim <= 2048 and a multiple of 8, expert_hidden <= 1024, top_k <= 16, 16-byte aligned "
+                    "pointers)");
     if (d_out != d_x && (reinterpret_cast<uintptr_t>(d_out) % 4) != 0)
         return fail("rbt_moe_decode_noalloc: misaligned output");
 
@@ -128,7 +129,7 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     }
     uint8_t* base = static_cast<uint8_t*>(setup.scratch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // the grid-barrier counters and the status word must start at zero
+    // the cross-CTA counters and the status word must start at zero
     err = cudaMemsetAsync(base, 0, l.logits, s);
     if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: cudaMemsetAsync failed: %s", cudaGetErrorString(err));
 
@@ -157,7 +158,7 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     a.n_active = reinterpret_cast<int32_t*>(base + l.n_active);
     a.wt = reinterpret_cast<float*>(base + l.wt);
     a.routing_out = d_routing_out;
-    a.bar = reinterpret_cast<unsigned*>(base + l.bar);
+    a.sync = reinterpret_cast<unsigned*>(base + l.sync);
     a.status = reinterpret_cast<unsigned*>(base + l.status);
     err = rbt::launch_decode_fused(a, setup.sm_count, s);
     if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: launch failed: %s", cudaGetErrorString(err));

@@ -106,9 +106,10 @@ struct DecodeArgs {
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active;
     float* wt;
     int32_t* routing_out;     // [K] or nullptr
-    unsigned* bar;            // [2] grid-barrier counters, zero between calls
+    unsigned* sync;           // [decode_sync_words(E, K)] cross-CTA counters, zero between calls
     unsigned* status;
 };
+int decode_sync_words(int E, int K);
 bool decode_fused_supported(int T, int D, int H, int E, int K, int dtype, const void* experts, size_t stride,
                             const void* x, const void* router);
 cudaError_t launch_decode_fused(const DecodeArgs& a, int grid, cudaStream_t s);

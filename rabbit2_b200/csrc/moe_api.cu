@@ -128,7 +128,8 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.hhi, SB * H * 2},            {(void**)&w.hlo, SB * H * 2},
         {(void**)&w.tb_e, ntb * 4},              {(void**)&w.tb_p0, ntb * 4},
         {(void**)&w.tb_p1, ntb * 4},             {(void**)&w.n_tb, 4},
-        {(void**)&w.status, 4},                  {(void**)&w.gbar, 8},
+        {(void**)&w.status, 4},
+        {(void**)&w.gbar, (size_t)rbt::decode_sync_words((int)E, (int)K) * 4},
         {(void**)&w.tile_cnt, tiles * E * 4},    {(void**)&w.tile_base, tiles * E * 4},
         {(void**)&w.slot_rank, S * 4},
         {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
@@ -160,7 +161,7 @@ int reserve(RbtMoe* m, int T) {
     CU(cudaMemsetAsync(w.done_counter, 0, 4, m->stream));
     CU(cudaMemsetAsync(w.counts, 0, E * 4, m->stream));
     CU(cudaMemsetAsync(w.status, 0, 4, m->stream));
-    CU(cudaMemsetAsync(w.gbar, 0, 8, m->stream));
+    CU(cudaMemsetAsync(w.gbar, 0, (size_t)rbt::decode_sync_words((int)E, (int)K) * 4, m->stream));
     CU(cudaStreamSynchronize(m->stream));
     if (tc) {
         w.tc_maps = true;
@@ -271,7 +272,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         da.D = c.dim; da.H = c.expert_hidden; da.E = c.n_experts; da.K = c.top_k; da.norm_topk = c.norm_topk;
         da.logits = w.logits; da.h = w.h; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
         da.perm = w.perm; da.slot_pos = w.slot_pos; da.active = w.active; da.n_active = w.n_active; da.wt = w.wt;
-        da.routing_out = routing; da.bar = w.gbar; da.status = w.status;
+        da.routing_out = routing; da.sync = w.gbar; da.status = w.status;
         if (!clk.begin(6)) return 0;
         CU(rbt::launch_decode_fused(da, m->sm_count, s));
         return clk.end();
@@ -358,7 +359,7 @@ int check_status(RbtMoe* m) {
     CU(cudaMemcpy(&st, m->ws.status, 4, cudaMemcpyDeviceToHost));
     if (st) {
         CU(cudaMemset(m->ws.status, 0, 4));
-        CU(cudaMemset(m->ws.gbar, 0, 8));
+        CU(cudaMemset(m->ws.gbar, 0, (size_t)rbt::decode_sync_words(m->cfg.n_experts, m->cfg.top_k) * 4));
         return fail("tensor-core GEMM pipeline wait timed out (code 0x%x)", st);
     }
     return 1;

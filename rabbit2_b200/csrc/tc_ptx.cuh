@@ -175,3 +175,15 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 
 }  // namespace tc
 }  // namespace rbt
+
+namespace rbt {
+namespace tc {
+
+// Bulk prefetch of global memory into L2 (no shared memory, no completion).
+// addr and bytes must be multiples of 16.
+__device__ __forceinline__ void prefetch_l2(const void* addr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(addr), "r"(bytes) : "memory");
+}
+
+}  // namespace tc
+}  // namespace rbt
