@@ -44,7 +44,7 @@ UNIT = "tok/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="rabbit2_b200", choices=["rabbit2_b200", "reference"])
     ap.add_argument("--tokens", type=int, default=1)
@@ -165,51 +165,95 @@ def run_reference(args, rank):
 # ----------------------------------------------------------------------------- GPU
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
-    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
-             "clocks_event_reasons.sw_power_cap"
+    """SM clock and throttle-reason samples taken while the timed region runs.
 
-    def __init__(self, index):
-        self.index, self.proc = index, None
+    A host thread polls NVML every ~2 ms from just before the first timed launch until the
+    closing synchronize, so even a timed region of a few milliseconds is sampled under load.
+    The GPU is found by its PCI bus id, so the index order of NVML and CUDA does not matter.
+    Falls back to `nvidia-smi -lms 200` where NVML is not importable.
+    """
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
+
+    def __init__(self, device_index, period_s=0.002):
+        self.device_index, self.period = device_index, period_s
+        self.samples, self.max_mhz, self.error = [], None, None
+
+    def _handle(self, nvml):
+        import torch
+        p = torch.cuda.get_device_properties(self.device_index)
+        bus = getattr(p, "pci_bus_id", None)
+        if bus is not None:
+            busid = "%08X:%02X:%02X.0" % (getattr(p, "pci_domain_id", 0), bus, getattr(p, "pci_device_id", 0))
+            try:
+                return nvml.nvmlDeviceGetHandleByPciBusId_v2(busid)
+            except Exception:
+                pass
+        return nvml.nvmlDeviceGetHandleByIndex(self.device_index)
+
+    def _poll(self, nvml, h):
+        while not self._stop.is_set():
+            try:
+                mhz = nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM)
+                mask = nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(mhz), int(mask)))
+            except Exception as exc:  # keep the bench going; report why there are no samples
+                self.error = repr(exc)
+                return
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
+        self._thread = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml as nvml
+            nvml.nvmlInit()
+            h = self._handle(nvml)
+            self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._poll, args=(nvml, h), daemon=True)
+            self._thread.start()
+        except Exception as exc:
+            self.error = repr(exc)
+            self._smi = None
+            try:
+                self._smi = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.device_index), "--query-gpu=clocks.sm,clocks.max.sm,"
+                     "clocks_event_reasons.active", "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                pass
         return self
 
     def __exit__(self, *exc):
-        self.samples = []
-        if self.proc is None:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
             return
-        self.proc.terminate()
+        smi = getattr(self, "_smi", None)
+        if smi is None:
+            return
+        smi.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            out, _ = smi.communicate(timeout=5)
         except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
+            smi.kill()
+            out, _ = smi.communicate()
         for line in out.splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) == 8:
-                self.samples.append(parts)
+            try:
+                self.samples.append((float(parts[0]), int(parts[2], 16)))
+                self.max_mhz = float(parts[1])
+            except (ValueError, IndexError):
+                pass
 
     def summary(self):
-        if not getattr(self, "samples", None):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for s in self.samples:
-            for n, v in zip(names, s[4:]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(self.samples[0][1]) if self.samples[0][1].replace(".", "").isdigit() else None,
-                "reasons": sorted(reasons), "samples": len(self.samples)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no clock samples: %s" % self.error]}
+        reasons = sorted({n for _, m in self.samples for n, bit in self.REASONS if m & bit})
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples),
+                "sm_mhz_min": min(s for s, _ in self.samples), "source": "nvml" if self._thread else "nvidia-smi"}
 
 
 def stage_cost(T, U, S):

@@ -144,14 +144,15 @@ int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
  * d_router_bias may be NULL, and d_routing_out ([top_k] int32) may be NULL.
  * d_ffn_norm != NULL gives the block form, d_out = d_x + MoE(rmsnorm(d_x))
  * (d_out may equal d_x); d_ffn_norm == NULL gives d_out = MoE(d_x).
- * Limits: bf16 weights, dim <= 2048 and a multiple of 8, expert_hidden <=
- * 1024, top_k <= 16, 16-byte aligned d_x/d_router/d_experts, and scratch of
- * n_experts + top_k * expert_hidden floats within RBT_MOE_NOALLOC_SCRATCH_BYTES;
- * other models are rejected with an error.  The first call on a device looks
+ * Limits: bf16 weights, dim <= 2048 and a multiple of 16, expert_hidden a
+ * multiple of 8, n_experts <= 256, top_k <= 64, 16-byte aligned
+ * d_x/d_router/d_experts, and scratch of (SM count x dim) floats plus the
+ * routing buffers within RBT_MOE_NOALLOC_SCRATCH_BYTES (1.5 MiB: a 148-SM
+ * B200 at dim 2048 needs 1.16 MiB); other models are rejected with an error.  The first call on a device looks
  * up the array's device address; make that first call before any stream
  * capture.  Calls share the array: two calls whose kernels overlap on the GPU
  * (unordered streams) race. */
-#define RBT_MOE_NOALLOC_SCRATCH_BYTES 49152
+#define RBT_MOE_NOALLOC_SCRATCH_BYTES 1572864
 int rbt_moe_decode_noalloc(const RbtMoeConfig *cfg, const float *d_ffn_norm, const void *d_router,
                            const float *d_router_bias, const void *d_experts, const float *d_x, float *d_out,
                            int32_t *d_routing_out, void *stream);

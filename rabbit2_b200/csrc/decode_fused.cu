@@ -3,34 +3,39 @@
 // experts' SwiGLU FFNs, the weighted combine and the residual -- as a single
 // cooperative launch of one CTA per SM.  Batch-1 decode is memory-bound on the
 // K experts' weights (8 x 12 MB at OLMoE-1B-7B), so the kernel exists to keep
-// HBM streaming: no launch gaps and no kernel-boundary drains.  Cross-CTA
-// ordering is by counters in global memory (release by __threadfence +
-// atomic, acquire by ld.acquire), each wait bounded by %globaltimer; the launch
-// is cooperative, so every CTA is resident and every wait ends.
+// HBM streaming: no launch gaps, no kernel-boundary drains, and every weight
+// byte read exactly once in a single streaming phase.  Cross-CTA ordering is by
+// words in global memory (release by atomics / __threadfence, acquire by
+// ld.acquire), each wait bounded by %globaltimer; the launch is cooperative, so
+// every CTA is resident and every wait ends.
 //
-//   0  every CTA: bulk-copies x (and, if it computes one, its router row) into
-//      shared memory; rmsnorm(x) for the block form, the same fixed-order
-//      reduction in every CTA so all hold the same xb
+//   0  every CTA: bulk-copies its router row(s) into shared memory (static
+//      weights, so before griddepcontrol.wait: this overlaps the previous
+//      kernel's tail), then x; rmsnorm(x) for the block form, the same
+//      fixed-order reduction in every CTA so all hold the same xb
 //   1  CTAs compute router logits -- the four sequential chains of the
 //      reference's scalar matvec (rabbit2.c:378-387), separately rounded
 //      products and sums, (s0+s1)+(s2+s3) -- each expert by two CTAs when the
-//      grid has room; the first copy to finish publishes it (both are equal)
-//   2  every CTA, as soon as all E logits are published: softmax and top-k
-//      (selection order = rank: higher probability, or equal and lower index),
-//      the K slots sorted by expert; CTA 0 publishes the routing outputs
-//   3  gate/up: each CTA takes a contiguous range of units (8 rows of w1 and
-//      the same 8 rows of w3); as soon as routing is known its producer thread
-//      issues L2 prefetches for every weight byte the CTA will need (gate/up
-//      units and its w2 rows), so HBM streams continuously while the
-//      units pass through a 3 x 64 KB shared-memory ring (cp.async.bulk, now L2
-//      hits); 8 consumer warps form h = silu(w1 . x) * (w3 . x) (packed
-//      fma.rn.f32x2, x in registers)
-//   -- grid barrier (consumer warps only; the producer keeps loading w2 rows)
-//   4  down + combine: units of 2 output rows x the K experts; consumer warp w
-//      keeps the h rows of chosen experts w and w+8 in registers; then
-//      out[d] = x[d] + sum_k w_k y_k[d] in selection order (rabbit2.c:539-542)
+//      grid has room; a logit is published with its ready bit in one 64-bit word
+//   2  every CTA, as soon as all E logits are published: softmax (exp, then the
+//      sequential sum in expert order, rabbit2.c:399-405) and top-k (selection
+//      order = rank: higher probability, or equal and lower index); CTA 0
+//      publishes the routing outputs
+//   3  units of 8 hidden rows of one chosen expert, a contiguous range per CTA.
+//      A unit is w1 and w3 rows [r, r+8) (two bulk copies) and the w2 columns
+//      [r, r+8) of all D rows (a 3-D TMA tile); as soon as routing is known the
+//      producer thread asks L2 for every byte of the CTA's later units, so HBM
+//      streams the whole 3 x K x H x D x 2 bytes in one pass while the units
+//      move through a 2 x 96 KB shared-memory ring.  Warp w forms
+//      h_w = silu(w1_w . xb) * (w3_w . xb) scaled by the expert's combine
+//      weight; then each thread adds w2[d, r..r+8) . h to its 8 output rows.
+//      The CTA's partial MoE output over all D rows stays in registers.
+//   4  every CTA writes its partial [D]; one grid barrier; CTA b sums its band
+//      of rows over all CTAs in a fixed order and writes out = x + moe
+//      (rabbit2.c:539-542)
 // The last CTA to leave returns every counter to zero.
 #include <cuda_bf16.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,18 +46,42 @@ namespace {
 
 using namespace tc;
 
-constexpr int kWarps = 8;
-constexpr int kThreads = (kWarps + 1) * 32;
-constexpr int kSlot = 65536;       // ring slot bytes
-constexpr int kSlots = 3;
-constexpr int kGURows = 8;         // w1/w3 rows per gate-up unit
-constexpr int kMaxH = 1024;        // a lane's slice of one h row stays in registers (H / 256 vectors)
-constexpr int kDR = 2;             // w2 rows per down unit
+constexpr int kWarps = 8;                  // consumer warps
+constexpr int kConsumers = kWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + the producer warp
+constexpr int kSlot = 96 * 1024;           // ring slot: w1 rows | w3 rows | w2 column tile
+constexpr int kSlots = 2;
+constexpr int kGURows = 8;                 // hidden rows per unit (one per consumer warp)
+constexpr int kMaxD = 2048;                // xb slices and output rows held in registers
+constexpr int kRowsPerThread = kMaxD / kConsumers;
+constexpr int kBoxRows = 256;              // rows of one w2 TMA box (the TMA limit)
 constexpr uint64_t kWaitNs = 2000000000ull;
+// phases 0-2 keep their staging in ring slot 0
+constexpr int kXsOff = 0;                  // xb [D] f32
+constexpr int kProdOff = 8 * 1024;         // router products, chain-major [4][D/4] f32
+constexpr int kWrowOff = 16 * 1024;        // this CTA's router rows, bf16
+constexpr int kWrowBytes = 64 * 1024;
 
-// sync words (a.sync): [0] CTAs done, [1] grid-barrier arrivals, [2..3] unused,
-// [4, 4+E) logit published, [4+E, 4+E+K) unused
+// sync words (a.sync, 32-bit): [0] CTAs done, [1] grid-barrier arrivals,
+// [2..3] unused, [4, 4+2E) one 64-bit word per expert: bit 32 = published,
+// low 32 bits = the logit
 constexpr int kSyncHead = 4;
+
+#ifdef RBT_DECODE_TIMELINE
+// Optional phase timestamps (%globaltimer) of every CTA, read back with
+// rbt_decode_timeline_read(); built only with -DRBT_DECODE_TIMELINE.
+// Two buffers, alternating by launch, so consecutive launches can be compared.
+__device__ unsigned long long g_timeline[2 * 256 * 16];
+__device__ unsigned g_timeline_seq;
+#define TIMELINE(i)                                                                                   \
+    do {                                                                                              \
+        if (blockIdx.x < 256) g_timeline[(tl_par * 256 + blockIdx.x) * 16 + (i)] = globaltimer_ns(); \
+    } while (0)
+#else
+#define TIMELINE(i) \
+    do {            \
+    } while (0)
+#endif
 
 __device__ __forceinline__ void record_error(unsigned* status, unsigned code) { atomicCAS(status, 0u, code); }
 
@@ -76,6 +105,11 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // Spin (bounded) until *p >= target.
 __device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
@@ -88,24 +122,73 @@ __device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
     return true;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* ring = smem;
-    float* ybuf = reinterpret_cast<float*>(smem + kSlots * kSlot);  // [band rows][K]
+// Spin (bounded) until the logit word is published; returns the logit in *v.
+__device__ __forceinline__ bool wait_logit(const unsigned long long* p, float* v) {
+    unsigned long long w = ld_acquire64(p);
+    if (!(w >> 32)) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!((w = ld_acquire64(p)) >> 32)) {
+            if (globaltimer_ns() - t0 > kWaitNs) return false;
+            __nanosleep(20);
+        }
+    }
+    *v = __uint_as_float((uint32_t)w);
+    return true;
+}
+
+// Named barrier over n threads that also returns the OR of `pred` over them.
+__device__ __forceinline__ bool named_sync_or(int id, int n, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+
+// L2 prefetch of one TMA box (no shared memory, no completion)
+__device__ __forceinline__ void prefetch_tile_3d(const CUtensorMap* map, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(x), "r"(y),
+                 "r"(z)
+                 : "memory");
+}
+
+__host__ __device__ constexpr int w2_box_rows(int D) { return D < kBoxRows ? D : kBoxRows; }
+__host__ __device__ constexpr int w2_boxes(int D) { return (D + w2_box_rows(D) - 1) / w2_box_rows(D); }
+__host__ __device__ constexpr int w2_offset(int D) { return (2 * kGURows * D * 2 + 1023) / 1024 * 1024; }
+
+// kW2T: the w2 part of a unit comes from the transposed copy a.w2t ([E][H][D],
+// rows r..r+8 are one contiguous 8*D*2-byte run); otherwise from w2 itself as a
+// [D x 8] column tile through w2map.  Shared memory then holds [8][D] or [D][8].
+template <bool kW2T>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_decode_fused_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap w2map) {
+    extern __shared__ __align__(1024) uint8_t ring[];
     __shared__ uint64_t full[kSlots], empty[kSlots], xbar, rbar;
-    __shared__ int32_t s_idx[kMaxTopK], s_pos[kMaxTopK], s_act[kMaxTopK];
-    __shared__ float s_p[kMaxTopK], s_w[kMaxTopK], s_prob[kMaxExperts];
+    __shared__ int32_t s_idx[kMaxTopK], s_act[kMaxTopK];
+    __shared__ float s_p[kMaxTopK], s_wpos[kMaxTopK];
+    __shared__ __align__(16) float s_prob[kMaxExperts];
+    __shared__ __align__(16) float s_h[kSlots][kGURows];
     __shared__ float s_red[kThreads / 32];
     __shared__ int s_fail;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = a.D, H = a.H, E = a.E, K = a.K;
     const int G = gridDim.x, b = blockIdx.x;
+#ifdef RBT_DECODE_TIMELINE
+    const unsigned tl_par = *(volatile unsigned*)&g_timeline_seq & 1u;
+#endif
     unsigned* done_cnt = a.sync;
     unsigned* bar_cnt = a.sync + 1;
-    unsigned* lflag = a.sync + kSyncHead;
-    float* xs = reinterpret_cast<float*>(ring);                   // phases 0-2: xb [D]
-    uint16_t* wrow = reinterpret_cast<uint16_t*>(ring + kSlot);   // phase 1: this CTA's router rows
+    unsigned long long* lword = reinterpret_cast<unsigned long long*>(a.sync + kSyncHead);
+    float* xs = reinterpret_cast<float*>(ring + kXsOff);
+    float* prods = reinterpret_cast<float*>(ring + kProdOff);
+    uint16_t* wrow = reinterpret_cast<uint16_t*>(ring + kWrowOff);
+    TIMELINE(0);
 
     // router rows this CTA computes: two copies of every expert when the grid has room
     const bool dup = G >= 2 * E;
@@ -124,14 +207,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
         mbar_init(&xbar, 1);
         mbar_init(&rbar, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(&xbar, (uint32_t)D * 4);
-        bulk_load(xs, a.x, (uint32_t)D * 4, &xbar);
-        if (n_rows > 0) {
+        prefetch_tmap(&w2map);
+        if (n_rows > 0) {  // static weights: no need to wait for the previous kernel
             mbar_arrive_expect_tx(&rbar, (uint32_t)n_rows * D * 2);
             for (int j = 0; j < n_rows; j++)
                 bulk_load(wrow + (size_t)j * D, a.router + (size_t)(e_first + j * e_step) * D, (uint32_t)D * 2, &rbar);
         }
     }
+    // x, the sync words and every output may belong to the previous kernel in
+    // the stream until this returns (programmatic dependent launch)
+    pdl_wait();
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&xbar, (uint32_t)D * 4);
+        bulk_load(xs, a.x, (uint32_t)D * 4, &xbar);
+    }
+    pdl_launch_dependents();
     // ---------------------------------------------------------------- phase 0
     __syncthreads();
     if (!mbar_wait_bounded(&xbar, 0, kWaitNs)) {
@@ -148,16 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
         float tot = 0.0f;
         for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
         const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), a.eps));
-        __syncthreads();
         for (int i = tid; i < D; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), a.ffn_norm[i]);
         __syncthreads();
     }
+    TIMELINE(1);
     // ---------------------------------------------------------------- phase 1: exact router logits
     // The products w[i]*x[i] are independent: every thread rounds its share of
     // them into `prods`, laid out chain-major (chain c = i mod 4 holds its D/4
     // products contiguously).  Lane c of warp 0 then runs chain c's D/4
     // dependent adds in order, reading 4 products per 16-byte load.
-    float* prods = reinterpret_cast<float*>(ring + 2 * kSlot);  // [4][D/4]
     for (int j = 0; j < n_rows; j++) {
         const int e = e_first + j * e_step;
         if (j == 0) {
@@ -166,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
                 record_error(a.status, 0x600);
                 s_fail = 1;
             }
+            if (tid == 0) TIMELINE(2);
         }
         __syncthreads();
         if (s_fail) break;
@@ -194,59 +284,66 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
             if (lane == 0) {
                 float logit = __fadd_rn(a01, a23);
                 if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
-                a.logits[e] = logit;  // both copies write the same bits
-                __threadfence();
-                atomicExch(lflag + e, 1u);
+                // both copies publish the same bits
+                atomicExch(lword + e, (1ull << 32) | (unsigned long long)__float_as_uint(logit));
             }
         }
         __syncthreads();
     }
+    if (tid == 0) TIMELINE(3);
     // ---------------------------------------------------------------- phase 2: softmax, top-k, slot order
     if (warp == 0) {
-        bool ok = true;
-        for (int e = lane; e < E; e += 32) ok = ok && wait_count(lflag + e, 1u);
+        constexpr int NJ = kMaxExperts / 32;
+        const int nj = (E + 31) / 32;
+        float l[NJ], p[NJ];
+        bool ok = !s_fail;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            l[j] = -INFINITY;
+            if (ok && j < nj && e < E) ok = wait_logit(lword + e, &l[j]);
+        }
         if (!__all_sync(FULL_MASK, ok)) {
             if (lane == 0) {
                 record_error(a.status, 0x601);
                 s_fail = 1;
             }
-        }
-    }
-    __syncthreads();
-    if (warp == 0 && !s_fail) {
-        constexpr int NJ = kMaxExperts / 32;
-        const int nj = (E + 31) / 32;
-        float l[NJ], p[NJ];
-        float mx = -INFINITY;
+        } else {
+            float mx = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            l[j] = (j < nj && e < E) ? __ldcg(a.logits + e) : -INFINITY;
-            mx = fmaxf(mx, l[j]);
-        }
+            for (int j = 0; j < NJ; j++) mx = fmaxf(mx, l[j]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
 #pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            p[j] = (j < nj && e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
-        }
-        // the sequential sum in expert order (rabbit2.c:403), values passed by shuffles
-        float sum = 0.0f;
+            for (int j = 0; j < NJ; j++) {
+                const int e = lane + 32 * j;
+                p[j] = (j < nj && e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
+                if (j < nj && e < E) s_prob[e] = p[j];
+            }
+            __syncwarp();
+            // the sequential sum in expert order (rabbit2.c:403)
+            float sum = 0.0f;
+            if (lane == 0) {
+                int e = 0;
+                for (; e + 4 <= E; e += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(s_prob + e);
+                    sum = __fadd_rn(sum, v.x);
+                    sum = __fadd_rn(sum, v.y);
+                    sum = __fadd_rn(sum, v.z);
+                    sum = __fadd_rn(sum, v.w);
+                }
+                for (; e < E; e++) sum = __fadd_rn(sum, s_prob[e]);
+            }
+            sum = __shfl_sync(FULL_MASK, sum, 0);
+            __syncwarp();
 #pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            if (j < nj) {
-#pragma unroll
-                for (int src = 0; src < 32; src++) {
-                    const float v = __shfl_sync(FULL_MASK, p[j], src);
-                    if (32 * j + src < E) sum = __fadd_rn(sum, v);
+            for (int j = 0; j < NJ; j++) {
+                const int e = lane + 32 * j;
+                if (j < nj && e < E) {
+                    s_prob[e] = __fdiv_rn(p[j], sum);
+                    if (b == 0) a.logits[e] = l[j];
                 }
             }
-        }
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            if (j < nj && e < E) s_prob[e] = __fdiv_rn(p[j], sum);
         }
     }
     __syncthreads();
@@ -270,22 +367,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
         float wsum = 0.0f;
         for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
         for (int k = lane; k < K; k += 32) {
-            s_w[k] = a.norm_topk ? __fdiv_rn(s_p[k], wsum) : s_p[k];
+            const float w = a.norm_topk ? __fdiv_rn(s_p[k], wsum) : s_p[k];
             int pos = 0;  // rank of this slot's expert among the chosen ones
             for (int j = 0; j < K; j++) pos += s_idx[j] < s_idx[k];
-            s_pos[k] = pos;
             s_act[pos] = s_idx[k];
-        }
-        __syncwarp();
-        if (b == 0) {  // the routing outputs of the call
-            for (int k = lane; k < K; k += 32) {
+            s_wpos[pos] = w;
+            if (b == 0) {  // the routing outputs of the call
                 a.idx[k] = s_idx[k];
-                a.wt[k] = s_w[k];
-                a.slot_pos[k] = s_pos[k];
-                a.perm[s_pos[k]] = k;
-                a.active[s_pos[k]] = s_idx[k];
+                a.wt[k] = w;
+                a.slot_pos[k] = pos;
+                a.perm[pos] = k;
+                a.active[pos] = s_idx[k];
                 if (a.routing_out) a.routing_out[k] = s_idx[k];
             }
+        }
+        if (b == 0) {
             for (int e = lane; e < E; e += 32) {
                 int c = 0, below = 0;
                 for (int k = 0; k < K; k++) {
@@ -302,18 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
         }
     }
     __syncthreads();
+    if (tid == 0) TIMELINE(4);
     const bool fail0 = s_fail != 0;
 
-    const int nvx = D / 8;   // 16-byte vectors per w1/w3 row
-    const int nvh = H / 8;   // per w2 row
-    const uint32_t gu_half = (uint32_t)kGURows * D * 2;  // 8 rows of w1 (or w3)
-    const uint32_t dn_rows = (uint32_t)kDR * H * 2;      // 2 rows of w2 of one expert
+    const int nvx = D / 8;                                 // 16-byte vectors per w1/w3 row
+    const uint32_t gu_half = (uint32_t)kGURows * D * 2;    // 8 rows of w1 (or w3)
+    const int boxr = w2_box_rows(D), nbox = w2_boxes(D);
+    const uint32_t w2_bytes = (uint32_t)nbox * boxr * kGURows * 2;  // whole boxes, zero-filled past D
+    const int w2_off = w2_offset(D);
     const int units_per_e = H / kGURows;
-    const int n_gu = fail0 ? 0 : K * units_per_e;
-    const int g0 = (int)((long)n_gu * b / G), g1 = (int)((long)n_gu * (b + 1) / G);
-    const int n_dn = fail0 ? 0 : D / kDR;
-    const int d0 = (int)((long)n_dn * b / G), d1 = (int)((long)n_dn * (b + 1) / G);
-    const int ups = (int)(kSlot / ((uint32_t)K * dn_rows)) >= 2 ? 2 : 1;  // down units per ring slot
+    const int n_units = fail0 ? 0 : K * units_per_e;
+    const int g0 = (int)((long)n_units * b / G), g1 = (int)((long)n_units * (b + 1) / G);
 
     // consumer lanes keep their slice of xb in registers before the ring is reused
     float xr[64];
@@ -338,48 +433,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
                     ok = false;
                     break;
                 }
-                const int e = s_act[u / units_per_e], rg = u % units_per_e;
-                const uint8_t* w1 = a.experts + (size_t)e * a.stride + (size_t)rg * gu_half;
+                const int e = s_act[u / units_per_e], r0 = (u % units_per_e) * kGURows;
+                const uint8_t* w1 = a.experts + (size_t)e * a.stride + (size_t)r0 * D * 2;
                 uint8_t* st = ring + slot * kSlot;
-                mbar_arrive_expect_tx(&full[slot], 2 * gu_half);
+                mbar_arrive_expect_tx(&full[slot], 2 * gu_half + (kW2T ? gu_half : w2_bytes));
                 bulk_load(st, w1, gu_half, &full[slot]);
                 bulk_load(st + gu_half, w1 + (size_t)H * D * 2, gu_half, &full[slot]);
+                if (kW2T)
+                    bulk_load(st + w2_off, a.w2t + (size_t)e * a.w2t_stride + (size_t)r0 * D * 2, gu_half,
+                              &full[slot]);
+                else
+                    for (int i = 0; i < nbox; i++)
+                        tma_load_3d(st + w2_off + i * boxr * kGURows * 2, &w2map, &full[slot], r0, i * boxr, e);
                 issued++;
                 if (++slot == kSlots) { slot = 0; ph ^= 1u; }
-                if (issued == kSlots || u + 1 == g1) {
+                if (issued == kSlots) {
                     // the ring is full: ask L2 for everything else this CTA will read,
                     // so HBM keeps streaming however long the ring takes to drain
                     for (int v = u + 1; v < g1; v++) {
-                        const uint8_t* p1 = a.experts + (size_t)s_act[v / units_per_e] * a.stride +
-                                            (size_t)(v % units_per_e) * gu_half;
+                        const int ev = s_act[v / units_per_e], rv = (v % units_per_e) * kGURows;
+                        const uint8_t* p1 = a.experts + (size_t)ev * a.stride + (size_t)rv * D * 2;
                         prefetch_l2(p1, gu_half);
                         prefetch_l2(p1 + (size_t)H * D * 2, gu_half);
+                        if (kW2T)
+                            prefetch_l2(a.w2t + (size_t)ev * a.w2t_stride + (size_t)rv * D * 2, gu_half);
+                        else
+                            for (int i = 0; i < nbox; i++) prefetch_tile_3d(&w2map, rv, i * boxr, ev);
                     }
-                    if (d1 > d0)
-                        for (int pa = 0; pa < K; pa++)
-                            prefetch_l2(a.experts + (size_t)s_act[pa] * a.stride + (size_t)2 * H * D * 2 +
-                                            (size_t)d0 * dn_rows,
-                                        (uint32_t)(d1 - d0) * dn_rows);
                 }
             }
-            for (int u = d0; ok && u < d1; u += ups) {  // down units, `ups` per slot
-                if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, kWaitNs)) {
-                    record_error(a.status, 0x612);
-                    ok = false;
-                    break;
-                }
-                const int nu = min(ups, d1 - u);
-                uint8_t* st = ring + slot * kSlot;
-                mbar_arrive_expect_tx(&full[slot], nu * K * dn_rows);
-                for (int j = 0; j < nu; j++)
-                    for (int pa = 0; pa < K; pa++) {
-                        const uint8_t* src = a.experts + (size_t)s_act[pa] * a.stride + (size_t)2 * H * D * 2 +
-                                             (size_t)(u + j) * dn_rows;
-                        bulk_load(st + (j * K + pa) * dn_rows, src, dn_rows, &full[slot]);
-                    }
-                issued++;
-                if (++slot == kSlots) { slot = 0; ph ^= 1u; }
-            }
+            TIMELINE(8);
             for (int i = 0; i < kSlots && i < issued; i++) {  // drain
                 if (--slot < 0) { slot = kSlots - 1; ph ^= 1u; }
                 if (!mbar_wait_bounded(&full[slot], ph, kWaitNs)) record_error(a.status, 0x613);
@@ -387,24 +470,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
         }
     } else {
         // ------------------------------------------------------------ consumers
+        uint64_t acc[kRowsPerThread];
+#pragma unroll
+        for (int j = 0; j < kRowsPerThread; j++) acc[j] = 0;
         int slot = 0;
         uint32_t ph = 0;
         bool ok = true;
-        for (int u = g0; ok && u < g1; u++) {
-            const bool got = mbar_wait_bounded(&full[slot], ph, kWaitNs);
-            if (!__all_sync(FULL_MASK, got)) {
-                record_error(a.status, 0x621);
-                ok = false;
-                break;
-            }
-            const int pa = u / units_per_e, r = (u % units_per_e) * kGURows + warp;
-            const uint4* w1 = reinterpret_cast<const uint4*>(ring + slot * kSlot + warp * D * 2);
-            const uint4* w3 = reinterpret_cast<const uint4*>(ring + slot * kSlot + gu_half + warp * D * 2);
+        for (int u = g0; u < g1; u++) {
+            const bool got = __all_sync(FULL_MASK, mbar_wait_bounded(&full[slot], ph, kWaitNs));
+            if (tid == 0 && u == g0) TIMELINE(9);
+            if (!got && lane == 0) record_error(a.status, 0x621);
+            const int pa = u / units_per_e;
+            const uint8_t* st = ring + slot * kSlot;
+            // gate/up: warp w forms hidden row r0 + w
+            const uint4* w1 = reinterpret_cast<const uint4*>(st + warp * D * 2);
+            const uint4* w3 = reinterpret_cast<const uint4*>(st + gu_half + warp * D * 2);
             uint64_t g[4] = {0, 0, 0, 0}, up[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int v = lane + 32 * j;
-                if (v < nvx) {
+                if (got && v < nvx) {
                     const uint4 q1 = w1[v], q3 = w3[v];
                     const uint64_t x01 = f2(xr[8 * j], xr[8 * j + 1]), x23 = f2(xr[8 * j + 2], xr[8 * j + 3]);
                     const uint64_t x45 = f2(xr[8 * j + 4], xr[8 * j + 5]), x67 = f2(xr[8 * j + 6], xr[8 * j + 7]);
@@ -418,17 +503,77 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
                     up[3] = ffma2(bf2(q3.w), x67, up[3]);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
             const float gs = warp_sum((f2sum(g[0]) + f2sum(g[1])) + (f2sum(g[2]) + f2sum(g[3])));
             const float us = warp_sum((f2sum(up[0]) + f2sum(up[1])) + (f2sum(up[2]) + f2sum(up[3])));
-            if (lane == 0) a.h[(size_t)pa * H + r] = gs / (1.0f + expf(-gs)) * us;
+            // silu(h1) * h3 (rabbit2.c:407, :536), times the expert's combine weight
+            if (lane == 0) s_h[slot][warp] = gs / (1.0f + expf(-gs)) * us * s_wpos[pa];
+            // every consumer warp reaches this barrier once per unit, and the
+            // barrier's OR of the timeouts ends the loop in all of them together
+            if (named_sync_or(1, kConsumers, !got)) {
+                s_fail = 1;
+                ok = false;
+                break;
+            }
+            const float4 ha = *reinterpret_cast<const float4*>(&s_h[slot][0]);
+            const float4 hb = *reinterpret_cast<const float4*>(&s_h[slot][4]);
+            if (kW2T) {
+                // down: this thread's output rows d = 8 tid .. 8 tid + 7, from the 8
+                // transposed rows r0..r0+8 ([8][D] in shared memory)
+                if (8 * tid < D) {
+                    const float hv[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+                    const uint4* w2r = reinterpret_cast<const uint4*>(st + w2_off) + tid;
+#pragma unroll
+                    for (int r = 0; r < kGURows; r++) {
+                        const uint4 q = w2r[r * (D / 8)];
+                        const uint64_t hh = f2(hv[r], hv[r]);
+                        acc[0] = ffma2(bf2(q.x), hh, acc[0]);
+                        acc[1] = ffma2(bf2(q.y), hh, acc[1]);
+                        acc[2] = ffma2(bf2(q.z), hh, acc[2]);
+                        acc[3] = ffma2(bf2(q.w), hh, acc[3]);
+                    }
+                }
+            } else {
+                // down: this thread's output rows d = tid + 256 j, columns r0..r0+8 of w2
+                const uint64_t h01 = f2(ha.x, ha.y), h23 = f2(ha.z, ha.w), h45 = f2(hb.x, hb.y),
+                               h67 = f2(hb.z, hb.w);
+                const uint4* w2c = reinterpret_cast<const uint4*>(st + w2_off);
+#pragma unroll
+                for (int j = 0; j < kRowsPerThread; j++) {
+                    const int d = tid + kConsumers * j;
+                    if (d < D) {
+                        const uint4 q = w2c[d];
+                        acc[j] = ffma2(bf2(q.x), h01, acc[j]);
+                        acc[j] = ffma2(bf2(q.y), h23, acc[j]);
+                        acc[j] = ffma2(bf2(q.z), h45, acc[j]);
+                        acc[j] = ffma2(bf2(q.w), h67, acc[j]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
             if (++slot == kSlots) { slot = 0; ph ^= 1u; }
         }
-        // every CTA's h rows are written (and every CTA has read x) before any
-        // CTA reads h or writes out
+        if (tid == 0) TIMELINE(5);
+        // this CTA's partial of the MoE output, every row (zeros if it had no units)
+        float* part = a.partials + (size_t)b * D;
+        if (kW2T) {
+            // acc[i] holds rows (8 tid + 2i, 8 tid + 2i + 1)
+            if (8 * tid < D) {
+                float4* p4 = reinterpret_cast<float4*>(part + 8 * tid);
+                p4[0] = make_float4(__uint_as_float((uint32_t)acc[0]), __uint_as_float((uint32_t)(acc[0] >> 32)),
+                                    __uint_as_float((uint32_t)acc[1]), __uint_as_float((uint32_t)(acc[1] >> 32)));
+                p4[1] = make_float4(__uint_as_float((uint32_t)acc[2]), __uint_as_float((uint32_t)(acc[2] >> 32)),
+                                    __uint_as_float((uint32_t)acc[3]), __uint_as_float((uint32_t)(acc[3] >> 32)));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kRowsPerThread; j++) {
+                const int d = tid + kConsumers * j;
+                if (d < D) part[d] = f2sum(acc[j]);
+            }
+        }
         if (!ok && lane == 0) s_fail = 1;
-        named_sync(1, kWarps * 32);
+        named_sync(1, kConsumers);
         if (tid == 0 && !s_fail) {
             __threadfence();
             atomicAdd(bar_cnt, 1u);
@@ -437,117 +582,164 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(DecodeArg
                 s_fail = 1;
             }
         }
-        named_sync(1, kWarps * 32);
-        // warp w owns the chosen experts w and w + 8: their h rows stay in registers
-        // for the whole phase, so shared memory only streams weights
-        float hr[2][32];
-#pragma unroll
-        for (int q = 0; q < 2; q++) {
-            const int pa = warp + kWarps * q;
-#pragma unroll
-            for (int m = 0; m < 4; m++) {
-                const int v = lane + 32 * m;
-                float4 h0 = make_float4(0.f, 0.f, 0.f, 0.f), h1 = h0;
-                if (!s_fail && pa < K && v < nvh) {
-                    h0 = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)pa * H + v * 8));
-                    h1 = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)pa * H + v * 8 + 4));
-                }
-                hr[q][8 * m] = h0.x; hr[q][8 * m + 1] = h0.y; hr[q][8 * m + 2] = h0.z; hr[q][8 * m + 3] = h0.w;
-                hr[q][8 * m + 4] = h1.x; hr[q][8 * m + 5] = h1.y; hr[q][8 * m + 6] = h1.z; hr[q][8 * m + 7] = h1.w;
+        named_sync(1, kConsumers);
+        if (tid == 0) TIMELINE(6);
+        // band reduction: rows [4 c0, 4 c1) summed over every CTA's partial in a
+        // fixed order (8 interleaved chains per row, then a fixed pairwise tree)
+        const int n4 = D / 4;
+        const int c0 = (int)((long)n4 * b / G), c1 = (int)((long)n4 * (b + 1) / G);
+        const int nc = c1 - c0, nrow = 4 * nc;
+        float4* red = reinterpret_cast<float4*>(ring);  // [G][nc]; every ring copy has landed
+        if (!s_fail)
+            for (int i = tid; i < G * nc; i += kConsumers) {
+                const int gg = i / nc, c = i - gg * nc;
+                red[i] = __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t)gg * D) + c0 + c);
             }
-        }
-        // the per-expert results of the CTA's whole output band collect in ybuf
-        // ([row][slot position]); one barrier, then one combine
-        for (int u = d0; ok && !s_fail && u < d1; u += ups) {
-            const bool got = mbar_wait_bounded(&full[slot], ph, kWaitNs);
-            if (!__all_sync(FULL_MASK, got)) {
-                record_error(a.status, 0x623);
-                ok = false;
-                break;
-            }
-            const int nu = min(ups, d1 - u);
-            const uint8_t* st = ring + slot * kSlot;
-#pragma unroll
-            for (int q = 0; q < 2; q++) {
-                const int pa = warp + kWarps * q;
-                if (pa >= K) continue;
-                for (int j = 0; j < nu; j++) {
-#pragma unroll
-                    for (int rr = 0; rr < kDR; rr++) {
-                        const uint4* w = reinterpret_cast<const uint4*>(st + (j * K + pa) * dn_rows + rr * H * 2);
-                        uint64_t acc[4] = {0, 0, 0, 0};
-#pragma unroll
-                        for (int m = 0; m < 4; m++) {
-                            const int v = lane + 32 * m;
-                            if (v < nvh) {
-                                const uint4 qv = w[v];
-                                acc[0] = ffma2(bf2(qv.x), f2(hr[q][8 * m], hr[q][8 * m + 1]), acc[0]);
-                                acc[1] = ffma2(bf2(qv.y), f2(hr[q][8 * m + 2], hr[q][8 * m + 3]), acc[1]);
-                                acc[2] = ffma2(bf2(qv.z), f2(hr[q][8 * m + 4], hr[q][8 * m + 5]), acc[2]);
-                                acc[3] = ffma2(bf2(qv.w), f2(hr[q][8 * m + 6], hr[q][8 * m + 7]), acc[3]);
-                            }
-                        }
-                        const float sd = warp_sum((f2sum(acc[0]) + f2sum(acc[1])) + (f2sum(acc[2]) + f2sum(acc[3])));
-                        if (lane == 0) ybuf[((u - d0 + j) * kDR + rr) * K + pa] = sd;
-                    }
+        named_sync(1, kConsumers);
+        if (!s_fail) {
+            const float* redf = reinterpret_cast<const float*>(red);
+            for (int rb = 0; rb < nrow; rb += kConsumers / 8) {
+                const int row = rb + tid / 8, part8 = tid % 8;
+                float s = 0.0f;
+                if (row < nrow)
+                    for (int gg = part8; gg < G; gg += 8) s += redf[gg * nrow + row];
+                s += __shfl_xor_sync(FULL_MASK, s, 1);
+                s += __shfl_xor_sync(FULL_MASK, s, 2);
+                s += __shfl_xor_sync(FULL_MASK, s, 4);
+                if (part8 == 0 && row < nrow) {
+                    const int d = 4 * c0 + row;
+                    a.out[d] = a.ffn_norm ? __fadd_rn(a.x[d], s) : s;
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            if (++slot == kSlots) { slot = 0; ph ^= 1u; }
-        }
-        if (!ok && lane == 0) s_fail = 1;
-        named_sync(1, kWarps * 32);
-        const int nrows = (d1 - d0) * kDR;
-        if (!s_fail && tid < nrows) {  // combine in selection order, then the residual
-            const int d = d0 * kDR + tid;
-            float mo = 0.0f;
-            for (int k = 0; k < K; k++) mo = __fadd_rn(mo, __fmul_rn(s_w[k], ybuf[tid * K + s_pos[k]]));
-            a.out[d] = a.ffn_norm ? __fadd_rn(a.x[d], mo) : mo;
         }
     }
     __syncthreads();
-    if (tid == 0) {  // the last CTA out returns every counter to zero
+    if (tid == 0) TIMELINE(7);
+    // the last CTA out returns every counter to zero (its threads in parallel)
+    __shared__ int s_last;
+    if (tid == 0) {
         __threadfence();
-        if (atomicAdd(done_cnt, 1u) == (unsigned)G - 1) {
-            for (int i = 1; i < kSyncHead + E + K; i++) atomicExch(a.sync + i, 0u);
+        s_last = atomicAdd(done_cnt, 1u) == (unsigned)G - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        for (int i = 1 + tid; i < kSyncHead + 2 * E; i += kThreads) a.sync[i] = 0u;
+        __syncthreads();
+        if (tid == 0) {
             __threadfence();
             atomicExch(done_cnt, 0u);
+#ifdef RBT_DECODE_TIMELINE
+            g_timeline[(tl_par * 256 + 255) * 16 + 15] = globaltimer_ns();
+            atomicAdd(&g_timeline_seq, 1u);
+#endif
         }
     }
+}
+
+// w2t[e][r][d] = w2[e][d][r]: one expert per blockIdx.z, 32 x 32 tiles through shared memory
+__global__ void transpose_w2_kernel(const uint8_t* experts, size_t stride, int D, int H, uint16_t* w2t) {
+    __shared__ uint16_t tile[32][33];
+    const int e = blockIdx.z;
+    const uint16_t* w2 = reinterpret_cast<const uint16_t*>(experts + (size_t)e * stride + (size_t)2 * H * D * 2);
+    uint16_t* out = w2t + (size_t)e * H * D;
+    const int r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int d = d0 + j, r = r0 + threadIdx.x;
+        if (d < D && r < H) tile[j][threadIdx.x] = w2[(size_t)d * H + r];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = r0 + j, d = d0 + threadIdx.x;
+        if (d < D && r < H) out[(size_t)r * D + d] = tile[threadIdx.x][j];
+    }
+}
+
+bool g_pdl_refused = false;
+
+// RBT_MOE_DECODE_PDL=0 launches without programmatic dependent launch
+bool decode_pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("RBT_MOE_DECODE_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 }  // namespace
 
-int decode_sync_words(int E, int K) { return kSyncHead + E + K; }
+int decode_sync_words(int E, int K) { return kSyncHead + 2 * E + K; }
+
+size_t decode_partials_bytes(int grid, int D) { return (size_t)grid * D * sizeof(float); }
+
+cudaError_t transpose_w2(const void* experts, size_t stride, int D, int H, int E, void* w2t, cudaStream_t s) {
+    if (E <= 0) return cudaSuccess;
+    transpose_w2_kernel<<<dim3((H + 31) / 32, (D + 31) / 32, E), dim3(32, 8), 0, s>>>(
+        static_cast<const uint8_t*>(experts), stride, D, H, static_cast<uint16_t*>(w2t));
+    return cudaGetLastError();
+}
 
 bool decode_fused_supported(int T, int D, int H, int E, int K, int dtype, const void* experts, size_t stride,
                             const void* x, const void* router) {
-    return T == 1 && dtype == 1 && D % 16 == 0 && D <= 2048 && H % kGURows == 0 && H % 8 == 0 && H <= kMaxH &&
-           D % kDR == 0 && E <= kMaxExperts && K <= 2 * kWarps && 2 * kGURows * D * 2 <= kSlot &&
-           K * kDR * H * 2 <= kSlot && stride % 16 == 0 &&
-           (reinterpret_cast<uintptr_t>(experts) % 16) == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
-           (reinterpret_cast<uintptr_t>(router) % 16) == 0;
+    return T == 1 && dtype == 1 && D % 16 == 0 && D <= kMaxD && H % kGURows == 0 && E <= kMaxExperts &&
+           K <= kMaxTopK && K <= E && w2_offset(D) + w2_boxes(D) * w2_box_rows(D) * kGURows * 2 <= kSlot &&
+           stride % 16 == 0 && (reinterpret_cast<uintptr_t>(experts) % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(x) % 16) == 0 && (reinterpret_cast<uintptr_t>(router) % 16) == 0;
 }
 
-cudaError_t launch_decode_fused(const DecodeArgs& a, int grid, cudaStream_t s) {
-    // the output band of a CTA (ceil((D/2)/grid) units of 2 rows) times K results
-    const size_t band_rows = (size_t)kDR * ((a.D / kDR + grid - 1) / grid);
-    const size_t smem = (size_t)kSlots * kSlot + band_rows * a.K * 4;
-    cudaError_t err = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)smem);
+bool make_decode_w2_map(CUtensorMap* map, const void* experts, int D, int H, int E, size_t stride) {
+    // w2 of expert e is the row-major [D, H] matrix at experts + e*stride + 2*H*D*2;
+    // a box is 8 columns (one unit's hidden rows) by up to 256 output rows
+    const uint8_t* w2 = static_cast<const uint8_t*>(experts) + (size_t)2 * H * D * 2;
+    return make_map_3d_plain(map, w2, H, D, E, stride, kGURows, w2_box_rows(D));
+}
+
+cudaError_t launch_decode_fused(const DecodeArgs& a, const CUtensorMap& w2map, int grid, cudaStream_t s) {
+    const int rows_per_cta = (a.E + grid - 1) / grid;
+    if ((size_t)rows_per_cta * a.D * 2 > (size_t)kWrowBytes || a.D * 4 > kProdOff - kXsOff ||
+        (size_t)grid * ((a.D / 4 + grid - 1) / grid) * 16 > (size_t)kSlots * kSlot)
+        return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kSlots * kSlot;
+    if (a.w2t && (a.w2t_stride % 16 != 0 || reinterpret_cast<uintptr_t>(a.w2t) % 16 != 0))
+        return cudaErrorInvalidValue;
+    cudaError_t err = cudaFuncSetAttribute(moe_decode_fused_kernel<true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err == cudaSuccess)
+        err = cudaFuncSetAttribute(moe_decode_fused_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, a);
+    cfg.numAttrs = (g_pdl_refused || !decode_pdl_enabled()) ? 1 : 2;
+    auto kernel = a.w2t ? moe_decode_fused_kernel<true> : moe_decode_fused_kernel<false>;
+    err = cudaLaunchKernelEx(&cfg, kernel, a, w2map);
+    if (err != cudaSuccess && cfg.numAttrs == 2) {
+        // a driver that refuses the pair launches without the overlap
+        (void)cudaGetLastError();
+        g_pdl_refused = true;
+        cfg.numAttrs = 1;
+        err = cudaLaunchKernelEx(&cfg, kernel, a, w2map);
+    }
+    return err;
 }
 
 }  // namespace rbt
+
+#ifdef RBT_DECODE_TIMELINE
+extern "C" int rbt_decode_timeline_read(void* host) {
+    return cudaMemcpyFromSymbol(host, rbt::g_timeline, sizeof(rbt::g_timeline)) == cudaSuccess;
+}
+extern "C" int rbt_decode_timeline_seq(void) {
+    unsigned v = 0;
+    cudaMemcpyFromSymbol(&v, rbt::g_timeline_seq, sizeof v);
+    return (int)v;
+}
+#endif

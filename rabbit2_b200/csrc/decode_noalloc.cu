@@ -33,7 +33,7 @@ void set_last_error(const char* msg);
 
 namespace {
 
-constexpr size_t kScratchBytes = 48 * 1024;  // RBT_MOE_NOALLOC_SCRATCH_BYTES
+constexpr size_t kScratchBytes = RBT_MOE_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
@@ -61,9 +61,9 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 // Byte offsets of the scratch parts for one configuration; returns the total.
 struct Layout {
-    size_t logits, h, idx, wt, counts, offsets, perm, slot_pos, active, n_active, sync, status, total;
+    size_t logits, partials, idx, wt, counts, offsets, perm, slot_pos, active, n_active, sync, status, total;
 };
-Layout layout_for(int E, int K, int H) {
+Layout layout_for(int E, int K, int D, int grid) {
     Layout l{};
     size_t o = 0;
     l.sync = o;       o = align256(o + (size_t)rbt::decode_sync_words(E, K) * sizeof(unsigned));
@@ -77,7 +77,7 @@ Layout layout_for(int E, int K, int H) {
     l.perm = o;       o = align256(o + (size_t)K * sizeof(int32_t));
     l.slot_pos = o;   o = align256(o + (size_t)K * sizeof(int32_t));
     l.active = o;     o = align256(o + (size_t)K * sizeof(int32_t));
-    l.h = o;          o = align256(o + (size_t)K * H * sizeof(float));
+    l.partials = o;   o = align256(o + rbt::decode_partials_bytes(grid, D));
     l.total = o;
     return l;
 }
@@ -91,16 +91,11 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     const RbtMoeConfig& c = *cfg;
     if (c.dim <= 0 || c.expert_hidden <= 0 || c.n_experts <= 0 || c.top_k <= 0 || c.top_k > c.n_experts)
         return fail("rbt_moe_decode_noalloc: invalid config");
-    const Layout l = layout_for(c.n_experts, c.top_k, c.expert_hidden);
-    if (l.total > kScratchBytes)
-        return fail("rbt_moe_decode_noalloc: this model needs %zu bytes of scratch, above the fixed %zu-byte "
-                    "buffer (n_experts + top_k * expert_hidden too large)",
-                    l.total, kScratchBytes);
     if (!rbt::decode_fused_supported(1, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, d_experts,
                                      c.expert_stride, d_x, d_router))
         return fail("rbt_moe_decode_noalloc: unsupported model for the one-token kernel (needs bf16 weights, "
-                    "dim <= 2048 and a multiple of 8, expert_hidden <= 1024, top_k <= 16, 16-byte aligned "
-                    "pointers)");
+                    "dim <= 2048 and a multiple of 16, expert_hidden a multiple of 8, n_experts <= 256, "
+                    "top_k <= 64, 16-byte aligned pointers)");
     if (d_out != d_x && (reinterpret_cast<uintptr_t>(d_out) % 4) != 0)
         return fail("rbt_moe_decode_noalloc: misaligned output");
 
@@ -127,6 +122,14 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
         }
         setup = g_setup[dev];
     }
+    const Layout l = layout_for(c.n_experts, c.top_k, c.dim, setup.sm_count);
+    if (l.total > kScratchBytes)
+        return fail("rbt_moe_decode_noalloc: this model needs %zu bytes of scratch on this GPU (%d SMs x dim "
+                    "%d partial sums), above the fixed %zu-byte buffer",
+                    l.total, setup.sm_count, c.dim, kScratchBytes);
+    CUtensorMap w2map;
+    if (!rbt::make_decode_w2_map(&w2map, d_experts, c.dim, c.expert_hidden, c.n_experts, c.expert_stride))
+        return fail("rbt_moe_decode_noalloc: cannot describe the w2 columns as a TMA tensor map");
     uint8_t* base = static_cast<uint8_t*>(setup.scratch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // the cross-CTA counters and the status word must start at zero
@@ -148,7 +151,7 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     a.K = c.top_k;
     a.norm_topk = c.norm_topk;
     a.logits = reinterpret_cast<float*>(base + l.logits);
-    a.h = reinterpret_cast<float*>(base + l.h);
+    a.partials = reinterpret_cast<float*>(base + l.partials);
     a.idx = reinterpret_cast<int32_t*>(base + l.idx);
     a.counts = reinterpret_cast<int32_t*>(base + l.counts);
     a.offsets = reinterpret_cast<int32_t*>(base + l.offsets);
@@ -160,7 +163,7 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     a.routing_out = d_routing_out;
     a.sync = reinterpret_cast<unsigned*>(base + l.sync);
     a.status = reinterpret_cast<unsigned*>(base + l.status);
-    err = rbt::launch_decode_fused(a, setup.sm_count, s);
+    err = rbt::launch_decode_fused(a, w2map, setup.sm_count, s);
     if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: launch failed: %s", cudaGetErrorString(err));
     return 1;
 }

@@ -386,6 +386,19 @@ bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, in
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_3d_plain(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride, int box_cols,
+                       int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)E};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)stride};
+    cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
                                 cudaStream_t s) {
     if (S <= 0) return cudaSuccess;

@@ -101,8 +101,10 @@ struct DecodeArgs {
     const uint8_t* experts;
     size_t stride;
     int D, H, E, K, norm_topk;
-    float* logits;            // [E] scratch
-    float* h;                 // [K, H] scratch
+    float* logits;            // [E] the router logits (written by CTA 0)
+    float* partials;          // [grid, D] scratch: each CTA's partial MoE output
+    const uint8_t* w2t;       // [E][H][D] bf16 transposed w2 (rows of a unit contiguous), or nullptr
+    size_t w2t_stride;        // bytes per expert in w2t (H * D * 2)
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active;
     float* wt;
     int32_t* routing_out;     // [K] or nullptr
@@ -110,9 +112,14 @@ struct DecodeArgs {
     unsigned* status;
 };
 int decode_sync_words(int E, int K);
+size_t decode_partials_bytes(int grid, int D);
 bool decode_fused_supported(int T, int D, int H, int E, int K, int dtype, const void* experts, size_t stride,
                             const void* x, const void* router);
-cudaError_t launch_decode_fused(const DecodeArgs& a, int grid, cudaStream_t s);
+// the 3-D TMA map of every expert's w2 columns the kernel reads (8 columns x 256 rows per box)
+bool make_decode_w2_map(CUtensorMap* map, const void* experts, int D, int H, int E, size_t stride);
+cudaError_t launch_decode_fused(const DecodeArgs& a, const CUtensorMap& w2map, int grid, cudaStream_t s);
+// w2t[e] = w2[e]^T for the E experts of a layer (bf16 [H, D] each)
+cudaError_t transpose_w2(const void* experts, size_t stride, int D, int H, int E, void* w2t, cudaStream_t s);
 
 // K4: tcgen05 grouped GEMM (gemm_tc.cu).
 struct TcGemmArgs {
@@ -134,6 +141,9 @@ int tc_pick_bn(int T, int K, int E);
 bool tc_supported(int D, int H, int dtype);
 bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int box_rows);
 bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride);
+// bf16 [E][rows][cols] with row pitch cols*2 and matrix pitch `stride`, unswizzled boxes
+bool make_map_3d_plain(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride, int box_cols,
+                       int box_rows);
 cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
                                 cudaStream_t s);
 cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int bn, int32_t* tb_e,

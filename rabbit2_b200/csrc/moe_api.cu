@@ -62,12 +62,15 @@ struct Layer {
     bool tc = false;              // tensor maps below are valid
     CUtensorMap w_gateup;         // [E][2H][D] bf16 rows (w1 then w3), 3-D
     CUtensorMap w_down;           // [E][D][H] bf16 rows (w2), 3-D
+    bool dec = false;             // w2_cols is valid
+    CUtensorMap w2_cols;          // w2 column tiles of the one-token kernel
+    void* w2t = nullptr;          // [E][H][D] transposed w2 for the one-token kernel, owned (or null)
 };
 
 struct Workspace {
     int cap = 0;                  // tokens per call the buffers hold
     void* block = nullptr;
-    float *xb, *logits, *wt, *h, *y, *hx, *hout;
+    float *xb, *logits, *wt, *h, *y, *hx, *hout, *partials;
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active, *hrouting;
     int32_t *tile_cnt, *tile_base, *slot_rank;
     unsigned *tile_counter, *done_counter, *status, *gbar;
@@ -141,6 +144,7 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.active, E * 4},              {(void**)&w.n_active, 4},
         {(void**)&w.hrouting, S * 4},            {(void**)&w.tile_counter, tiles * 4},
         {(void**)&w.done_counter, 4},
+        {(void**)&w.partials, rbt::decode_partials_bytes(m->sm_count, (int)D)},
     };
     size_t total = 0;
     for (auto& p : parts) total = align_up(total, 256) + p.bytes;
@@ -179,10 +183,40 @@ int reserve(RbtMoe* m, int T) {
     return 1;
 }
 
-// Tensor maps of the layer's expert blobs for the tcgen05 path (bf16 only).
+// RBT_MOE_DECODE_W2T=0: no transposed w2 copy (the one-token kernel then reads w2 as column tiles)
+bool decode_w2t_enabled() {
+    const char* v = getenv("RBT_MOE_DECODE_W2T");
+    return !(v && v[0] == '0');
+}
+
+// Tensor maps of the layer's expert blobs for the tcgen05 path (bf16 only), and
+// the one-token kernel's w2 map and transposed w2.
 void layer_maps(RbtMoe* m, Layer& L) {
     const RbtMoeConfig& c = m->cfg;
     L.tc = false;
+    L.dec = c.dtype == 1 && (c.expert_stride % 16) == 0 && (reinterpret_cast<uintptr_t>(L.experts) % 16) == 0 &&
+            (c.expert_hidden % 8) == 0 && c.dim <= 2048 &&
+            rbt::make_decode_w2_map(&L.w2_cols, L.experts, c.dim, c.expert_hidden, c.n_experts, c.expert_stride);
+    // the one-token kernel streams w2 fastest as rows of its transpose: one
+    // contiguous run per unit instead of a tile of 16-byte pieces
+    if (L.w2t) cudaFree(L.w2t);
+    L.w2t = nullptr;
+    if (L.dec && decode_w2t_enabled()) {
+        const size_t bytes = (size_t)c.n_experts * c.expert_hidden * c.dim * 2;
+        void* p = nullptr;
+        bool ok = cudaMalloc(&p, bytes) == cudaSuccess;
+        // the weights may still be in flight on another stream of the caller
+        ok = ok && cudaDeviceSynchronize() == cudaSuccess &&
+             rbt::transpose_w2(L.experts, c.expert_stride, c.dim, c.expert_hidden, c.n_experts, p, m->stream) ==
+                 cudaSuccess &&
+             cudaStreamSynchronize(m->stream) == cudaSuccess;
+        if (ok) {
+            L.w2t = p;
+        } else {  // without the copy the kernel reads w2 as column tiles
+            (void)cudaGetLastError();
+            if (p) cudaFree(p);
+        }
+    }
     if (!rbt::tc_supported(c.dim, c.expert_hidden, c.dtype) || (c.expert_stride % 16) != 0 ||
         (reinterpret_cast<uintptr_t>(L.experts) % 16) != 0)
         return;
@@ -262,7 +296,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     Workspace& w = m->ws;
     StageClock clk{m, s};
     m->prof.calls++;
-    if ((m->path == 0 || m->path == 4) &&
+    if ((m->path == 0 || m->path == 4) && L.dec &&
         rbt::decode_fused_supported(T, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, L.experts,
                                     c.expert_stride, x, L.router)) {
         rbt::DecodeArgs da{};
@@ -270,11 +304,12 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         da.eps = c.rms_eps; da.router = static_cast<const uint16_t*>(L.router); da.bias = L.bias;
         da.experts = L.experts; da.stride = c.expert_stride;
         da.D = c.dim; da.H = c.expert_hidden; da.E = c.n_experts; da.K = c.top_k; da.norm_topk = c.norm_topk;
-        da.logits = w.logits; da.h = w.h; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
+        da.logits = w.logits; da.partials = w.partials;
+        da.w2t = static_cast<const uint8_t*>(L.w2t); da.w2t_stride = (size_t)c.expert_hidden * c.dim * 2; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
         da.perm = w.perm; da.slot_pos = w.slot_pos; da.active = w.active; da.n_active = w.n_active; da.wt = w.wt;
         da.routing_out = routing; da.sync = w.gbar; da.status = w.status;
         if (!clk.begin(6)) return 0;
-        CU(rbt::launch_decode_fused(da, m->sm_count, s));
+        CU(rbt::launch_decode_fused(da, L.w2_cols, m->sm_count, s));
         return clk.end();
     }
     if (m->path == 4) return fail("fused decode path requested but unavailable (needs T == 1, bf16, D <= 2048)");
@@ -433,6 +468,7 @@ void rbt_moe_destroy(RbtMoe* m) {
     for (Layer& L : m->layers) {
         cudaFree(L.owned);
         cudaFree(L.bias);
+        cudaFree(L.w2t);
     }
     cudaFree(m->ws.block);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);

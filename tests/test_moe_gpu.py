@@ -333,6 +333,55 @@ def test_fused_decode_kernel_block_and_ffn(orc, zipf):
         ctx.close()
 
 
+@pytest.mark.parametrize("D,H,E,K,norm", [(512, 2048, 32, 4, 0), (512, 2048, 32, 4, 1), (272, 40, 8, 2, 0),
+                                            (2048, 1024, 256, 16, 0), (256, 64, 64, 64, 1), (16, 8, 2, 1, 0)])
+def test_fused_decode_shapes(orc, D, H, E, K, norm):
+    """The one-token kernel away from the OLMoE shape: expert_hidden above 1024,
+    dims that are not a multiple of the 256-row w2 box (zero-filled tail), two
+    router rows per CTA (E = 256), top_k = E, norm_topk, and the smallest shape."""
+    router, experts, stride = workload.device_layer(D, H, E, seed=D + H + E + K)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ffn_norm = 1.0 + 0.1 * torch.randn(D, generator=g, device="cuda")
+    ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_BF16, norm, stride)
+    try:
+        ctx.bind_layer(0, router, experts, ffn_norm)
+        ctx.set_path(moe.PATH_DECODE_FUSED)
+        r_h, e_h = workload.host_copy(router, experts)
+        host = MoeLayerHost(D, H, E, K, moe.DT_BF16, norm, r_h, e_h, stride, ffn_norm=ffn_norm.cpu().numpy())
+        for seed in range(3):
+            x = workload.inputs(1, D, seed=900 + seed) * 2.0
+            xh = x.cpu().numpy()
+            out = torch.empty_like(x)
+            routing = torch.empty(1, K, dtype=torch.int32, device="cuda")
+            ctx.ffn_device(0, x, out, routing)
+            want, want_r, _ = orc.moe_ffn(host, xh)
+            _, _, probs = orc.router_topk(host, xh)
+            assert_routing(routing.cpu().numpy(), want_r, probs)
+            assert rel_err(out.cpu().numpy(), want) < MOE_RTOL
+            xb = x.clone()
+            ctx.block_device(0, xb, routing)
+            wantb, want_rb = orc.moe_block(host, xh)
+            assert_routing(routing.cpu().numpy(), want_rb, None if np.array_equal(routing.cpu().numpy(), want_rb)
+                           else orc.router_topk(host, xh)[2])
+            # the residual add rounds to the ulp of x, which can dwarf a small MoE output
+            got_b = xb.cpu().numpy().astype(np.float64)
+            bound = MOE_RTOL * np.abs(wantb - xh).max() + np.spacing(np.abs(xh).astype(np.float32)).max()
+            assert np.abs(got_b - wantb).max() <= bound
+        ctx.ffn(0, xh)  # the host call checks the kernel's status word
+        # the entry point without a context reads w2 as column tiles instead of its transpose
+        import ctypes as C
+        fn = ctx.lib.rbt_moe_decode_noalloc
+        fn.argtypes = [C.POINTER(moe.RbtMoeConfig)] + [C.c_void_p] * 8
+        fn.restype = C.c_int
+        out_n = torch.full_like(x, float("nan"))
+        assert fn(C.byref(ctx.cfg), None, router.data_ptr(), None, experts.data_ptr(), x.data_ptr(),
+                  out_n.data_ptr(), None, None) == 1, ctx.lib.rbt_moe_last_error()
+        torch.cuda.synchronize()
+        assert rel_err(out_n.cpu().numpy(), want) < MOE_RTOL
+    finally:
+        ctx.close()
+
+
 def test_decode_layers_in_a_cuda_graph(orc):
     """Three layers of the block form captured in one CUDA graph and replayed."""
     L = 3

@@ -73,14 +73,19 @@ def test_noalloc_decode_matches_context_path():
         ctx.close()
 
 
-def test_noalloc_decode_rejects_models_beyond_its_scratch():
+def test_noalloc_decode_rejects_models_beyond_its_limits():
+    """Shapes the one-token kernel does not take are refused on the host, before
+    anything is launched (the pointers here are dummies and are never read)."""
     lib = moe.load_library()
     noalloc = _bind(lib)
-    D, H, E, K = 2048, 4096, 64, 8  # top_k * expert_hidden * 4 bytes = 128 KiB > the fixed buffer
-    cfg = moe.RbtMoeConfig(D, E, K, H, 1, moe.DT_BF16, 0, 1e-5, 3 * H * D * 2)
-    x = torch.zeros(1, D, device="cuda")
+    x = torch.zeros(1, 4096, device="cuda")
     dummy = torch.zeros(16, dtype=torch.uint8, device="cuda")
-    ok = noalloc(C.byref(cfg), None, dummy.data_ptr(), None, dummy.data_ptr(), x.data_ptr(), x.data_ptr(), None,
-                 None)
-    assert ok == 0
-    assert b"scratch" in lib.rbt_moe_last_error()
+    for D, H, E, K in [(4096, 1024, 64, 8),   # dim above 2048
+                       (2040, 1024, 64, 8),   # dim not a multiple of 16
+                       (2048, 1020, 64, 8),   # expert_hidden not a multiple of 8
+                       (2048, 1024, 512, 8)]:  # more experts than the kernel's 256
+        cfg = moe.RbtMoeConfig(D, E, K, H, 1, moe.DT_BF16, 0, 1e-5, 3 * H * D * 2 + 4096)
+        ok = noalloc(C.byref(cfg), None, dummy.data_ptr(), None, dummy.data_ptr(), x.data_ptr(), x.data_ptr(),
+                     None, None)
+        assert ok == 0, (D, H, E, K)
+        assert b"unsupported model" in lib.rbt_moe_last_error()
