@@ -146,7 +146,7 @@ int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
  * (d_out may equal d_x); d_ffn_norm == NULL gives d_out = MoE(d_x).
  * Limits: bf16 weights, dim <= 2048 and a multiple of 16, expert_hidden a
  * multiple of 8, n_experts <= 256, top_k <= 64, 16-byte aligned
- * d_x/d_router/d_experts, and scratch of (SM count x dim) floats plus the
+ * d_x/d_router/d_experts/d_ffn_norm, and scratch of (SM count x dim) floats plus the
  * routing buffers within RBT_MOE_NOALLOC_SCRATCH_BYTES (1.5 MiB: a 148-SM
  * B200 at dim 2048 needs 1.16 MiB); other models are rejected with an error.  The first call on a device looks
  * up the array's device address; make that first call before any stream

@@ -9,9 +9,9 @@
 // ld.acquire), each wait bounded by %globaltimer; the launch is cooperative, so
 // every CTA is resident and every wait ends.
 //
-//   0  every CTA: bulk-copies its router row(s) into shared memory (static
-//      weights, so before griddepcontrol.wait: this overlaps the previous
-//      kernel's tail), then x; rmsnorm(x) for the block form, the same
+//   0  every CTA: bulk-copies its router row(s) and ffn_norm into shared memory
+//      (static weights, so before griddepcontrol.wait: this overlaps the
+//      previous kernel's tail), then x; rmsnorm(x) for the block form, the same
 //      fixed-order reduction in every CTA so all hold the same xb
 //   1  CTAs compute router logits -- the four sequential chains of the
 //      reference's scalar matvec (rabbit2.c:378-387), separately rounded
@@ -22,18 +22,18 @@
 //      order = rank: higher probability, or equal and lower index); CTA 0
 //      publishes the routing outputs
 //   3  units of 8 hidden rows of one chosen expert, a contiguous range per CTA.
-//      A unit is w1 and w3 rows [r, r+8) (two bulk copies) and the w2 columns
-//      [r, r+8) of all D rows (a 3-D TMA tile); as soon as routing is known the
-//      producer thread asks L2 for every byte of the CTA's later units, so HBM
-//      streams the whole 3 x K x H x D x 2 bytes in one pass while the units
-//      move through a 2 x 96 KB shared-memory ring.  Warp w forms
+//      A unit is w1 and w3 rows [r, r+8) (two bulk copies) and the w2 part for
+//      hidden rows [r, r+8): rows of the transposed copy (one bulk copy) or a
+//      [D x 8] column tile of w2 itself (3-D TMA).  The units stream through a
+//      2 x 96 KB shared-memory ring.  Warp w forms
 //      h_w = silu(w1_w . xb) * (w3_w . xb) scaled by the expert's combine
-//      weight; then each thread adds w2[d, r..r+8) . h to its 8 output rows.
+//      weight; then each thread adds the w2 . h products to its 8 output rows.
 //      The CTA's partial MoE output over all D rows stays in registers.
 //   4  every CTA writes its partial [D]; one grid barrier; CTA b sums its band
 //      of rows over all CTAs in a fixed order and writes out = x + moe
-//      (rabbit2.c:539-542)
-// The last CTA to leave returns every counter to zero.
+//      (rabbit2.c:539-542).  After the barrier CTA 0 clears the logit words and
+//      the last CTA past it clears the barrier counters, and the next layer's
+//      router row and ffn_norm are prefetched into L2.
 #include <cuda_bf16.h>
 #include <stdlib.h>
 
@@ -49,7 +49,7 @@ using namespace tc;
 constexpr int kWarps = 8;                  // consumer warps
 constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + the producer warp
-constexpr int kSlot = 96 * 1024;           // ring slot: w1 rows | w3 rows | w2 column tile
+constexpr int kSlot = 96 * 1024;           // ring slot: w1 rows | w3 rows | w2 part
 constexpr int kSlots = 2;
 constexpr int kGURows = 8;                 // hidden rows per unit (one per consumer warp)
 constexpr int kMaxD = 2048;                // xb slices and output rows held in registers
@@ -61,21 +61,26 @@ constexpr int kXsOff = 0;                  // xb [D] f32
 constexpr int kProdOff = 8 * 1024;         // router products, chain-major [4][D/4] f32
 constexpr int kWrowOff = 16 * 1024;        // this CTA's router rows, bf16
 constexpr int kWrowBytes = 64 * 1024;
+constexpr int kNormOff = 80 * 1024;        // ffn_norm [D] f32
 
-// sync words (a.sync, 32-bit): [0] CTAs done, [1] grid-barrier arrivals,
-// [2..3] unused, [4, 4+2E) one 64-bit word per expert: bit 32 = published,
-// low 32 bits = the logit
-constexpr int kSyncHead = 4;
+// sync words (a.sync, 32-bit): [0] CTAs past the grid barrier, [1] grid-barrier
+// arrivals, [2..31] unused, then one 64-bit word per expert at the start of its own
+// 128-byte line (every CTA polls every word: separate lines spread the polls over
+// the L2 slices): bit 32 = published, low 32 bits = the logit.  All are zero
+// between launches: the last CTA past the barrier clears [0] and [1], CTA 0 clears
+// the logit words.
+constexpr int kSyncHead = 32;
+constexpr int kLogitStride = 16;  // 64-bit words between two experts' logit words
 
 #ifdef RBT_DECODE_TIMELINE
 // Optional phase timestamps (%globaltimer) of every CTA, read back with
 // rbt_decode_timeline_read(); built only with -DRBT_DECODE_TIMELINE.
 // Two buffers, alternating by launch, so consecutive launches can be compared.
-__device__ unsigned long long g_timeline[2 * 256 * 16];
+__device__ unsigned long long g_timeline[2 * 256 * 32];
 __device__ unsigned g_timeline_seq;
 #define TIMELINE(i)                                                                                   \
     do {                                                                                              \
-        if (blockIdx.x < 256) g_timeline[(tl_par * 256 + blockIdx.x) * 16 + (i)] = globaltimer_ns(); \
+        if (blockIdx.x < 256) g_timeline[(tl_par * 256 + blockIdx.x) * 32 + (i)] = globaltimer_ns(); \
     } while (0)
 #else
 #define TIMELINE(i) \
@@ -127,10 +132,8 @@ __device__ __forceinline__ bool wait_logit(const unsigned long long* p, float* v
     unsigned long long w = ld_acquire64(p);
     if (!(w >> 32)) {
         const uint64_t t0 = globaltimer_ns();
-        while (!((w = ld_acquire64(p)) >> 32)) {
+        while (!((w = ld_acquire64(p)) >> 32))
             if (globaltimer_ns() - t0 > kWaitNs) return false;
-            __nanosleep(20);
-        }
     }
     *v = __uint_as_float((uint32_t)w);
     return true;
@@ -150,13 +153,6 @@ __device__ __forceinline__ bool named_sync_or(int id, int n, bool pred) {
     return r != 0;
 }
 
-// L2 prefetch of one TMA box (no shared memory, no completion)
-__device__ __forceinline__ void prefetch_tile_3d(const CUtensorMap* map, int x, int y, int z) {
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(x), "r"(y),
-                 "r"(z)
-                 : "memory");
-}
-
 __host__ __device__ constexpr int w2_box_rows(int D) { return D < kBoxRows ? D : kBoxRows; }
 __host__ __device__ constexpr int w2_boxes(int D) { return (D + w2_box_rows(D) - 1) / w2_box_rows(D); }
 __host__ __device__ constexpr int w2_offset(int D) { return (2 * kGURows * D * 2 + 1023) / 1024 * 1024; }
@@ -168,7 +164,7 @@ template <bool kW2T>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_decode_fused_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap w2map) {
     extern __shared__ __align__(1024) uint8_t ring[];
-    __shared__ uint64_t full[kSlots], empty[kSlots], xbar, rbar;
+    __shared__ uint64_t full[kSlots], empty[kSlots], xbar, rbar, nbar;
     __shared__ int32_t s_idx[kMaxTopK], s_act[kMaxTopK];
     __shared__ float s_p[kMaxTopK], s_wpos[kMaxTopK];
     __shared__ __align__(16) float s_prob[kMaxExperts];
@@ -182,12 +178,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef RBT_DECODE_TIMELINE
     const unsigned tl_par = *(volatile unsigned*)&g_timeline_seq & 1u;
 #endif
-    unsigned* done_cnt = a.sync;
+    unsigned* past_cnt = a.sync;
     unsigned* bar_cnt = a.sync + 1;
     unsigned long long* lword = reinterpret_cast<unsigned long long*>(a.sync + kSyncHead);
     float* xs = reinterpret_cast<float*>(ring + kXsOff);
     float* prods = reinterpret_cast<float*>(ring + kProdOff);
     uint16_t* wrow = reinterpret_cast<uint16_t*>(ring + kWrowOff);
+    float* norm_s = reinterpret_cast<float*>(ring + kNormOff);
     TIMELINE(0);
 
     // router rows this CTA computes: two copies of every expert when the grid has room
@@ -206,12 +203,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(&xbar, 1);
         mbar_init(&rbar, 1);
+        mbar_init(&nbar, 1);
         fence_mbar_init();
         prefetch_tmap(&w2map);
-        if (n_rows > 0) {  // static weights: no need to wait for the previous kernel
+        // static weights: no need to wait for the previous kernel
+        if (n_rows > 0) {
             mbar_arrive_expect_tx(&rbar, (uint32_t)n_rows * D * 2);
             for (int j = 0; j < n_rows; j++)
                 bulk_load(wrow + (size_t)j * D, a.router + (size_t)(e_first + j * e_step) * D, (uint32_t)D * 2, &rbar);
+        }
+        if (a.ffn_norm) {
+            mbar_arrive_expect_tx(&nbar, (uint32_t)D * 4);
+            bulk_load(norm_s, a.ffn_norm, (uint32_t)D * 4, &nbar);
         }
     }
     // x, the sync words and every output may belong to the previous kernel in
@@ -229,16 +232,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         s_fail = 1;
     }
     __syncthreads();
+    if (tid == 0) TIMELINE(13);
     if (a.ffn_norm) {  // rmsnorm, the same fixed-order reduction in every CTA
         float ss = 0.0f;
         for (int i = tid; i < D; i += kThreads) ss = fmaf(xs[i], xs[i], ss);
         ss = warp_sum(ss);
         if (lane == 0) s_red[warp] = ss;
+        if (!mbar_wait_bounded(&nbar, 0, kWaitNs)) {
+            record_error(a.status, 0x605);
+            s_fail = 1;
+        }
         __syncthreads();
         float tot = 0.0f;
         for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
         const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), a.eps));
-        for (int i = tid; i < D; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), a.ffn_norm[i]);
+        for (int i = tid; i < D; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), norm_s[i]);
         __syncthreads();
     }
     TIMELINE(1);
@@ -264,9 +272,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = tid; i < 4 * q; i += kThreads)
             prods[(i & 3) * q + (i >> 2)] = __fmul_rn(bf16_bits_to_f32(wr[i]), xs[i]);
         __syncthreads();
+        if (tid == 0 && j == 0) TIMELINE(14);
         if (warp == 0) {
             float s = 0.0f;
             if (lane < 4) {
+                // the dependent adds are the critical path (about 4.6 cycles per product)
                 const float* pc = prods + lane * q;
                 int i = 0;
                 for (; i + 4 <= q; i += 4) {
@@ -282,87 +292,106 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float a01 = __fadd_rn(s, s1);
             const float a23 = __shfl_down_sync(FULL_MASK, a01, 2);
             if (lane == 0) {
+                if (j == 0) TIMELINE(15);
                 float logit = __fadd_rn(a01, a23);
                 if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
                 // both copies publish the same bits
-                atomicExch(lword + e, (1ull << 32) | (unsigned long long)__float_as_uint(logit));
+                atomicExch(lword + (size_t)e * kLogitStride, (1ull << 32) | (unsigned long long)__float_as_uint(logit));
             }
         }
         __syncthreads();
     }
+    // consumer lanes keep their slices of xb (elements 8v..8v+8, v = lane + 32 j) in
+    // registers from here on (loaded while the logits propagate); the ring region
+    // holding xs is reused after routing
+    const int nvx = D / 8;  // 16-byte bf16 vectors per w1/w3 row
+    float xr[64];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int v = lane + 32 * j;
+        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        if (warp < kWarps && v < nvx) {
+            lo = reinterpret_cast<const float4*>(xs)[2 * v];
+            hi = reinterpret_cast<const float4*>(xs)[2 * v + 1];
+        }
+        xr[8 * j] = lo.x; xr[8 * j + 1] = lo.y; xr[8 * j + 2] = lo.z; xr[8 * j + 3] = lo.w;
+        xr[8 * j + 4] = hi.x; xr[8 * j + 5] = hi.y; xr[8 * j + 6] = hi.z; xr[8 * j + 7] = hi.w;
+    }
     if (tid == 0) TIMELINE(3);
     // ---------------------------------------------------------------- phase 2: softmax, top-k, slot order
-    if (warp == 0) {
-        constexpr int NJ = kMaxExperts / 32;
-        const int nj = (E + 31) / 32;
-        float l[NJ], p[NJ];
-        bool ok = !s_fail;
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            l[j] = -INFINITY;
-            if (ok && j < nj && e < E) ok = wait_logit(lword + e, &l[j]);
+    // thread e < E owns expert e
+    float lg = -INFINITY;
+    bool ok2 = !s_fail;
+    if (ok2 && tid < E) ok2 = wait_logit(lword + (size_t)tid * kLogitStride, &lg);
+    if (!__syncthreads_and(ok2)) {
+        if (tid == 0) {
+            record_error(a.status, 0x601);
+            s_fail = 1;
         }
-        if (!__all_sync(FULL_MASK, ok)) {
-            if (lane == 0) {
-                record_error(a.status, 0x601);
-                s_fail = 1;
-            }
-        } else {
-            float mx = -INFINITY;
+    } else {
+        if (tid == 0) TIMELINE(10);
+        float mx = lg;
 #pragma unroll
-            for (int j = 0; j < NJ; j++) mx = fmaxf(mx, l[j]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
-#pragma unroll
-            for (int j = 0; j < NJ; j++) {
-                const int e = lane + 32 * j;
-                p[j] = (j < nj && e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
-                if (j < nj && e < E) s_prob[e] = p[j];
-            }
-            __syncwarp();
-            // the sequential sum in expert order (rabbit2.c:403)
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
+        if (lane == 0) s_red[warp] = mx;
+        __syncthreads();
+        if (tid == 0) TIMELINE(16);
+        mx = s_red[0];
+        for (int w = 1; w < (E + 31) / 32; w++) mx = fmaxf(mx, s_red[w]);
+        // exp in double, rounded once (correctly rounded expf)
+        const float pe = tid < E ? (float)exp((double)__fsub_rn(lg, mx)) : 0.0f;
+        if (tid < E) s_prob[tid] = pe;
+        __syncthreads();
+        if (tid == 0) TIMELINE(17);
+        if (tid == 0) {  // the sequential sum in expert order (rabbit2.c:403)
             float sum = 0.0f;
-            if (lane == 0) {
-                int e = 0;
-                for (; e + 4 <= E; e += 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(s_prob + e);
-                    sum = __fadd_rn(sum, v.x);
-                    sum = __fadd_rn(sum, v.y);
-                    sum = __fadd_rn(sum, v.z);
-                    sum = __fadd_rn(sum, v.w);
-                }
-                for (; e < E; e++) sum = __fadd_rn(sum, s_prob[e]);
+            int e = 0;
+            for (; e + 4 <= E; e += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(s_prob + e);
+                sum = __fadd_rn(sum, v.x);
+                sum = __fadd_rn(sum, v.y);
+                sum = __fadd_rn(sum, v.z);
+                sum = __fadd_rn(sum, v.w);
             }
-            sum = __shfl_sync(FULL_MASK, sum, 0);
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < NJ; j++) {
-                const int e = lane + 32 * j;
-                if (j < nj && e < E) {
-                    s_prob[e] = __fdiv_rn(p[j], sum);
-                    if (b == 0) a.logits[e] = l[j];
-                }
-            }
+            for (; e < E; e++) sum = __fadd_rn(sum, s_prob[e]);
+            s_red[0] = sum;
         }
+        __syncthreads();
+        if (tid == 0) TIMELINE(18);
+        if (tid < E) {
+            s_prob[tid] = __fdiv_rn(pe, s_red[0]);
+            if (b == 0) a.logits[tid] = lg;
+        }
+        if (tid == 0) TIMELINE(11);
     }
     __syncthreads();
     // top-k by rank: expert e is chosen in round r when exactly r experts beat it
     // (higher probability, or equal probability and lower index) -- the order of
-    // the reference's K rounds of strict-'>' scans (rabbit2.c:519-528)
-    if (!s_fail && tid < E) {
-        const float pe = s_prob[tid];
+    // the reference's K rounds of strict-'>' scans (rabbit2.c:519-528).
+    // 4 threads per expert (E <= 72; one per expert otherwise), each counting a quarter of the rivals
+    {
+        const int split = E <= kThreads / 4 ? 4 : 1;
+        const int e = tid / split, part = tid % split;
         int r = 0;
-        for (int f = 0; f < E; f++) {
-            const float pf = s_prob[f];
-            r += (pf > pe) || (pf == pe && f < tid);
+        float pe = 0.0f;
+        if (!s_fail && e < E) {
+            pe = s_prob[e];
+            for (int f = part; f < E; f += split) {
+                const float pf = s_prob[f];
+                r += (pf > pe) || (pf == pe && f < e);
+            }
         }
-        if (r < K) {
-            s_idx[r] = tid;
+        if (split == 4) {  // the 4 threads of an expert are adjacent lanes of one warp
+            r += __shfl_xor_sync(FULL_MASK, r, 1);
+            r += __shfl_xor_sync(FULL_MASK, r, 2);
+        }
+        if (!s_fail && e < E && part == 0 && r < K) {
+            s_idx[r] = e;
             s_p[r] = pe;
         }
     }
     __syncthreads();
+    if (tid == 0) TIMELINE(12);
     if (warp == 0 && !s_fail) {
         float wsum = 0.0f;
         for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
@@ -401,8 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) TIMELINE(4);
     const bool fail0 = s_fail != 0;
 
-    const int nvx = D / 8;                                 // 16-byte vectors per w1/w3 row
-    const uint32_t gu_half = (uint32_t)kGURows * D * 2;    // 8 rows of w1 (or w3)
+    const uint32_t gu_half = (uint32_t)kGURows * D * 2;  // 8 rows of w1 (or w3)
     const int boxr = w2_box_rows(D), nbox = w2_boxes(D);
     const uint32_t w2_bytes = (uint32_t)nbox * boxr * kGURows * 2;  // whole boxes, zero-filled past D
     const int w2_off = w2_offset(D);
@@ -410,18 +438,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_units = fail0 ? 0 : K * units_per_e;
     const int g0 = (int)((long)n_units * b / G), g1 = (int)((long)n_units * (b + 1) / G);
 
-    // consumer lanes keep their slice of xb in registers before the ring is reused
-    float xr[64];
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int v = lane + 32 * j;
-#pragma unroll
-        for (int q = 0; q < 8; q++) xr[8 * j + q] = (v < nvx) ? xs[v * 8 + q] : 0.0f;
-    }
-    __syncthreads();
-
     if (warp == kWarps) {
         // ------------------------------------------------------------ producer
+        // (an L2 prefetch of the CTA's later units measured slower: the ring alone
+        // keeps enough bytes in flight)
         if (lane == 0) {
             int slot = 0;
             uint32_t ph = 0;
@@ -447,20 +467,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_3d(st + w2_off + i * boxr * kGURows * 2, &w2map, &full[slot], r0, i * boxr, e);
                 issued++;
                 if (++slot == kSlots) { slot = 0; ph ^= 1u; }
-                if (issued == kSlots) {
-                    // the ring is full: ask L2 for everything else this CTA will read,
-                    // so HBM keeps streaming however long the ring takes to drain
-                    for (int v = u + 1; v < g1; v++) {
-                        const int ev = s_act[v / units_per_e], rv = (v % units_per_e) * kGURows;
-                        const uint8_t* p1 = a.experts + (size_t)ev * a.stride + (size_t)rv * D * 2;
-                        prefetch_l2(p1, gu_half);
-                        prefetch_l2(p1 + (size_t)H * D * 2, gu_half);
-                        if (kW2T)
-                            prefetch_l2(a.w2t + (size_t)ev * a.w2t_stride + (size_t)rv * D * 2, gu_half);
-                        else
-                            for (int i = 0; i < nbox; i++) prefetch_tile_3d(&w2map, rv, i * boxr, ev);
-                    }
-                }
             }
             TIMELINE(8);
             for (int i = 0; i < kSlots && i < issued; i++) {  // drain
@@ -573,6 +579,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (!ok && lane == 0) s_fail = 1;
+        // this CTA's band of output rows; the residual x of the band is read now, off
+        // the critical path (only this CTA writes these rows, after the barrier)
+        const int n4 = D / 4;
+        const int c0 = (int)((long)n4 * b / G), c1 = (int)((long)n4 * (b + 1) / G);
+        const int nc = c1 - c0, nrow = 4 * nc;
+        const int my_row = tid / 8, part8 = tid % 8;
+        float xres = 0.0f;
+        if (a.ffn_norm && part8 == 0 && my_row < nrow) xres = a.x[4 * c0 + my_row];
         named_sync(1, kConsumers);
         if (tid == 0 && !s_fail) {
             __threadfence();
@@ -586,20 +600,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tid == 0) TIMELINE(6);
         // band reduction: rows [4 c0, 4 c1) summed over every CTA's partial in a
         // fixed order (8 interleaved chains per row, then a fixed pairwise tree)
-        const int n4 = D / 4;
-        const int c0 = (int)((long)n4 * b / G), c1 = (int)((long)n4 * (b + 1) / G);
-        const int nc = c1 - c0, nrow = 4 * nc;
         float4* red = reinterpret_cast<float4*>(ring);  // [G][nc]; every ring copy has landed
-        if (!s_fail)
-            for (int i = tid; i < G * nc; i += kConsumers) {
-                const int gg = i / nc, c = i - gg * nc;
-                red[i] = __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t)gg * D) + c0 + c);
+        constexpr int kLd = 4;  // partial vectors per thread in flight at once
+        for (int i0 = 0; !s_fail && i0 < G * nc; i0 += kLd * kConsumers) {
+            float4 v[kLd];
+#pragma unroll
+            for (int k = 0; k < kLd; k++) {
+                const int i = i0 + k * kConsumers + tid;
+                if (i < G * nc) {
+                    const int gg = i / nc, c = i - gg * nc;
+                    v[k] = __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t)gg * D) + c0 + c);
+                }
             }
+#pragma unroll
+            for (int k = 0; k < kLd; k++) {
+                const int i = i0 + k * kConsumers + tid;
+                if (i < G * nc) red[i] = v[k];
+            }
+        }
+        if (!s_fail) {
+            // every CTA has read the logits (before it arrived): clear them for the next launch
+            if (b == 0)
+                for (int e = tid; e < E; e += kConsumers) lword[(size_t)e * kLogitStride] = 0ull;
+            // the last CTA past the barrier clears the barrier (nobody is waiting on it any more)
+            if (tid == 0 && atomicAdd(past_cnt, 1u) == (unsigned)G - 1) {
+                *bar_cnt = 0u;
+                *past_cnt = 0u;
+#ifdef RBT_DECODE_TIMELINE
+                atomicAdd(&g_timeline_seq, 1u);
+#endif
+            }
+            // the next layer's router row and ffn_norm into L2 for its first phase
+            if (tid == 32 && a.next_router && b < E)
+                prefetch_l2(a.next_router + (size_t)b * D * 2, (uint32_t)D * 2);
+            if (tid == 64 && a.next_norm && b == G - 1) prefetch_l2(a.next_norm, (uint32_t)D * 4);
+        }
         named_sync(1, kConsumers);
         if (!s_fail) {
             const float* redf = reinterpret_cast<const float*>(red);
             for (int rb = 0; rb < nrow; rb += kConsumers / 8) {
-                const int row = rb + tid / 8, part8 = tid % 8;
+                const int row = rb + my_row;
                 float s = 0.0f;
                 if (row < nrow)
                     for (int gg = part8; gg < G; gg += 8) s += redf[gg * nrow + row];
@@ -608,32 +648,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 s += __shfl_xor_sync(FULL_MASK, s, 4);
                 if (part8 == 0 && row < nrow) {
                     const int d = 4 * c0 + row;
-                    a.out[d] = a.ffn_norm ? __fadd_rn(a.x[d], s) : s;
+                    const float xr0 = rb == 0 ? xres : (a.ffn_norm ? a.x[d] : 0.0f);
+                    a.out[d] = a.ffn_norm ? __fadd_rn(xr0, s) : s;
                 }
             }
         }
     }
-    __syncthreads();
     if (tid == 0) TIMELINE(7);
-    // the last CTA out returns every counter to zero (its threads in parallel)
-    __shared__ int s_last;
-    if (tid == 0) {
-        __threadfence();
-        s_last = atomicAdd(done_cnt, 1u) == (unsigned)G - 1;
-    }
-    __syncthreads();
-    if (s_last) {
-        for (int i = 1 + tid; i < kSyncHead + 2 * E; i += kThreads) a.sync[i] = 0u;
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            atomicExch(done_cnt, 0u);
-#ifdef RBT_DECODE_TIMELINE
-            g_timeline[(tl_par * 256 + 255) * 16 + 15] = globaltimer_ns();
-            atomicAdd(&g_timeline_seq, 1u);
-#endif
-        }
-    }
 }
 
 // w2t[e][r][d] = w2[e][d][r]: one expert per blockIdx.z, 32 x 32 tiles through shared memory
@@ -667,7 +688,7 @@ bool decode_pdl_enabled() {
 
 }  // namespace
 
-int decode_sync_words(int E, int K) { return kSyncHead + 2 * E + K; }
+int decode_sync_words(int E, int K) { return kSyncHead + 2 * kLogitStride * E + K; }
 
 size_t decode_partials_bytes(int grid, int D) { return (size_t)grid * D * sizeof(float); }
 
@@ -698,9 +719,13 @@ cudaError_t launch_decode_fused(const DecodeArgs& a, const CUtensorMap& w2map, i
     if ((size_t)rows_per_cta * a.D * 2 > (size_t)kWrowBytes || a.D * 4 > kProdOff - kXsOff ||
         (size_t)grid * ((a.D / 4 + grid - 1) / grid) * 16 > (size_t)kSlots * kSlot)
         return cudaErrorInvalidValue;
+    auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) != 0; };
+    // every pointer the kernel bulk-copies or prefetches from must be 16-byte aligned
+    if ((a.w2t && (a.w2t_stride % 16 != 0 || misaligned(a.w2t))) || misaligned(a.ffn_norm) ||
+        misaligned(a.next_router) || misaligned(a.next_norm) || misaligned(a.x) || misaligned(a.router) ||
+        misaligned(a.experts))
+        return cudaErrorMisalignedAddress;
     const size_t smem = (size_t)kSlots * kSlot;
-    if (a.w2t && (a.w2t_stride % 16 != 0 || reinterpret_cast<uintptr_t>(a.w2t) % 16 != 0))
-        return cudaErrorInvalidValue;
     cudaError_t err = cudaFuncSetAttribute(moe_decode_fused_kernel<true>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err == cudaSuccess)

@@ -98,6 +98,8 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
                     "top_k <= 64, 16-byte aligned pointers)");
     if (d_out != d_x && (reinterpret_cast<uintptr_t>(d_out) % 4) != 0)
         return fail("rbt_moe_decode_noalloc: misaligned output");
+    if ((reinterpret_cast<uintptr_t>(d_ffn_norm) % 16) != 0)
+        return fail("rbt_moe_decode_noalloc: d_ffn_norm must be 16-byte aligned");
 
     // once per device, with that device current: the device address of the array
     int dev = 0;

@@ -105,6 +105,8 @@ struct DecodeArgs {
     float* partials;          // [grid, D] scratch: each CTA's partial MoE output
     const uint8_t* w2t;       // [E][H][D] bf16 transposed w2 (rows of a unit contiguous), or nullptr
     size_t w2t_stride;        // bytes per expert in w2t (H * D * 2)
+    const uint8_t* next_router;  // [E, D] bf16 router of the layer that runs next (L2 prefetch), or nullptr
+    const float* next_norm;      // [D] ffn_norm of the layer that runs next (L2 prefetch), or nullptr
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active;
     float* wt;
     int32_t* routing_out;     // [K] or nullptr

@@ -297,6 +297,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     StageClock clk{m, s};
     m->prof.calls++;
     if ((m->path == 0 || m->path == 4) && L.dec &&
+        (!block || (reinterpret_cast<uintptr_t>(L.ffn_norm) % 16) == 0) &&
         rbt::decode_fused_supported(T, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, L.experts,
                                     c.expert_stride, x, L.router)) {
         rbt::DecodeArgs da{};
@@ -305,7 +306,12 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         da.experts = L.experts; da.stride = c.expert_stride;
         da.D = c.dim; da.H = c.expert_hidden; da.E = c.n_experts; da.K = c.top_k; da.norm_topk = c.norm_topk;
         da.logits = w.logits; da.partials = w.partials;
-        da.w2t = static_cast<const uint8_t*>(L.w2t); da.w2t_stride = (size_t)c.expert_hidden * c.dim * 2; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
+        da.w2t = static_cast<const uint8_t*>(L.w2t); da.w2t_stride = (size_t)c.expert_hidden * c.dim * 2;
+        // decode runs the layers in order, and after the last comes the first of the next token
+        const Layer& N = m->layers[(layer + 1) % c.n_layers];
+        auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
+        da.next_router = aligned(N.router) ? static_cast<const uint8_t*>(N.router) : nullptr;
+        da.next_norm = aligned(N.ffn_norm) ? N.ffn_norm : nullptr; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
         da.perm = w.perm; da.slot_pos = w.slot_pos; da.active = w.active; da.n_active = w.n_active; da.wt = w.wt;
         da.routing_out = routing; da.sync = w.gbar; da.status = w.status;
         if (!clk.begin(6)) return 0;
