@@ -58,10 +58,11 @@ constexpr int kBoxRows = 256;              // rows of one w2 TMA box (the TMA li
 constexpr uint64_t kWaitNs = 2000000000ull;
 // phases 0-2 keep their staging in ring slot 0
 constexpr int kXsOff = 0;                  // xb [D] f32
-constexpr int kProdOff = 8 * 1024;         // router products, chain-major [4][D/4] f32
-constexpr int kWrowOff = 16 * 1024;        // this CTA's router rows, bf16
+constexpr int kProdOff = 8 * 1024;         // router products, chain-major [4][D/4 + kProdPad] f32
+constexpr int kProdPad = 4;                // floats between chains: the 4 chain lanes hit different banks
+constexpr int kWrowOff = 24 * 1024;        // this CTA's router rows, bf16
 constexpr int kWrowBytes = 64 * 1024;
-constexpr int kNormOff = 80 * 1024;        // ffn_norm [D] f32
+constexpr int kNormOff = 88 * 1024;        // ffn_norm [D] f32
 
 // sync words (a.sync, 32-bit): [0] CTAs past the grid barrier, [1] grid-barrier
 // arrivals, [2..31] unused, then one 64-bit word per expert at the start of its own
@@ -120,10 +121,8 @@ __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long l
 __device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
     if (ld_acquire(p) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire(p) < target) {
+    while (ld_acquire(p) < target)
         if (globaltimer_ns() - t0 > kWaitNs) return false;
-        __nanosleep(32);
-    }
     return true;
 }
 
@@ -164,8 +163,9 @@ template <bool kW2T>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_decode_fused_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap w2map) {
     extern __shared__ __align__(1024) uint8_t ring[];
-    __shared__ uint64_t full[kSlots], empty[kSlots], xbar, rbar, nbar;
-    __shared__ int32_t s_idx[kMaxTopK], s_act[kMaxTopK];
+    __shared__ uint64_t full[kSlots], empty[kSlots], rbar, nbar;
+    __shared__ int s_cnt[kThreads / 32];
+    __shared__ int32_t s_idx[kMaxTopK], s_act[kMaxTopK], s_kpos[kMaxTopK];
     __shared__ float s_p[kMaxTopK], s_wpos[kMaxTopK];
     __shared__ __align__(16) float s_prob[kMaxExperts];
     __shared__ __align__(16) float s_h[kSlots][kGURows];
@@ -201,7 +201,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarps);
         }
-        mbar_init(&xbar, 1);
         mbar_init(&rbar, 1);
         mbar_init(&nbar, 1);
         fence_mbar_init();
@@ -220,22 +219,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // x, the sync words and every output may belong to the previous kernel in
     // the stream until this returns (programmatic dependent launch)
     pdl_wait();
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&xbar, (uint32_t)D * 4);
-        bulk_load(xs, a.x, (uint32_t)D * 4, &xbar);
-    }
     pdl_launch_dependents();
     // ---------------------------------------------------------------- phase 0
-    __syncthreads();
-    if (!mbar_wait_bounded(&xbar, 0, kWaitNs)) {
-        record_error(a.status, 0x604);
-        s_fail = 1;
+    // x straight from L2 (the previous kernel wrote it) into shared memory, squares on the way
+    float ss = 0.0f;
+    for (int i4 = tid; i4 < D / 4; i4 += kThreads) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.x) + i4);
+        reinterpret_cast<float4*>(xs)[i4] = v;
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
     }
     __syncthreads();
     if (tid == 0) TIMELINE(13);
     if (a.ffn_norm) {  // rmsnorm, the same fixed-order reduction in every CTA
-        float ss = 0.0f;
-        for (int i = tid; i < D; i += kThreads) ss = fmaf(xs[i], xs[i], ss);
         ss = warp_sum(ss);
         if (lane == 0) s_red[warp] = ss;
         if (!mbar_wait_bounded(&nbar, 0, kWaitNs)) {
@@ -268,16 +266,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
         if (s_fail) break;
         const uint16_t* wr = wrow + (size_t)j * D;
-        const int q = D / 4;
+        const int q = D / 4, qp = q + kProdPad;
         for (int i = tid; i < 4 * q; i += kThreads)
-            prods[(i & 3) * q + (i >> 2)] = __fmul_rn(bf16_bits_to_f32(wr[i]), xs[i]);
+            prods[(i & 3) * qp + (i >> 2)] = __fmul_rn(bf16_bits_to_f32(wr[i]), xs[i]);
         __syncthreads();
         if (tid == 0 && j == 0) TIMELINE(14);
         if (warp == 0) {
             float s = 0.0f;
             if (lane < 4) {
                 // the dependent adds are the critical path (about 4.6 cycles per product)
-                const float* pc = prods + lane * q;
+                const float* pc = prods + lane * qp;
                 int i = 0;
                 for (; i + 4 <= q; i += 4) {
                     const float4 v = *reinterpret_cast<const float4*>(pc + i);
@@ -368,7 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // top-k by rank: expert e is chosen in round r when exactly r experts beat it
     // (higher probability, or equal probability and lower index) -- the order of
     // the reference's K rounds of strict-'>' scans (rabbit2.c:519-528).
-    // 4 threads per expert (E <= 72; one per expert otherwise), each counting a quarter of the rivals
+    // 4 threads per expert (E <= 72; one per expert otherwise), each counting a
+    // contiguous quarter of the rivals.  The chosen experts' position in expert
+    // order (the unit order) comes from a ballot over the experts' first threads.
     {
         const int split = E <= kThreads / 4 ? 4 : 1;
         const int e = tid / split, part = tid % split;
@@ -376,7 +376,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         float pe = 0.0f;
         if (!s_fail && e < E) {
             pe = s_prob[e];
-            for (int f = part; f < E; f += split) {
+            const int f0 = part * E / split, f1 = (part + 1) * E / split;
+            int f = f0;
+            if ((f0 & 3) == 0)
+                for (; f + 4 <= f1; f += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(s_prob + f);
+                    r += (v.x > pe) || (v.x == pe && f < e);
+                    r += (v.y > pe) || (v.y == pe && f + 1 < e);
+                    r += (v.z > pe) || (v.z == pe && f + 2 < e);
+                    r += (v.w > pe) || (v.w == pe && f + 3 < e);
+                }
+            for (; f < f1; f++) {
                 const float pf = s_prob[f];
                 r += (pf > pe) || (pf == pe && f < e);
             }
@@ -385,40 +395,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             r += __shfl_xor_sync(FULL_MASK, r, 1);
             r += __shfl_xor_sync(FULL_MASK, r, 2);
         }
-        if (!s_fail && e < E && part == 0 && r < K) {
-            s_idx[r] = e;
-            s_p[r] = pe;
+        const bool first = !s_fail && e < E && part == 0;
+        const bool chosen = first && r < K;
+        const unsigned m = __ballot_sync(FULL_MASK, chosen);
+        if (lane == 0) s_cnt[warp] = __popc(m);
+        __syncthreads();
+        if (tid == 0) TIMELINE(12);
+        if (first) {
+            int below = __popc(m & lanemask_lt());  // chosen experts with a lower index
+            for (int w = 0; w < warp; w++) below += s_cnt[w];
+            if (chosen) {
+                s_idx[r] = e;
+                s_p[r] = pe;
+                s_act[below] = e;
+                s_kpos[r] = below;
+                s_wpos[below] = pe;
+            }
+            if (b == 0) {
+                a.counts[e] = chosen ? 1 : 0;
+                a.offsets[e] = below;
+            }
         }
     }
     __syncthreads();
-    if (tid == 0) TIMELINE(12);
     if (warp == 0 && !s_fail) {
-        float wsum = 0.0f;
-        for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
-        for (int k = lane; k < K; k += 32) {
-            const float w = a.norm_topk ? __fdiv_rn(s_p[k], wsum) : s_p[k];
-            int pos = 0;  // rank of this slot's expert among the chosen ones
-            for (int j = 0; j < K; j++) pos += s_idx[j] < s_idx[k];
-            s_act[pos] = s_idx[k];
-            s_wpos[pos] = w;
-            if (b == 0) {  // the routing outputs of the call
+        if (a.norm_topk) {  // the sequential sum in selection order (rabbit2.c:529-531)
+            float wsum = 0.0f;
+            for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
+            for (int k = lane; k < K; k += 32) s_wpos[s_kpos[k]] = __fdiv_rn(s_p[k], wsum);
+            __syncwarp();
+        }
+        if (b == 0) {  // the routing outputs of the call
+            for (int k = lane; k < K; k += 32) {
+                const int pos = s_kpos[k];
                 a.idx[k] = s_idx[k];
-                a.wt[k] = w;
+                a.wt[k] = s_wpos[pos];
                 a.slot_pos[k] = pos;
                 a.perm[pos] = k;
                 a.active[pos] = s_idx[k];
                 if (a.routing_out) a.routing_out[k] = s_idx[k];
-            }
-        }
-        if (b == 0) {
-            for (int e = lane; e < E; e += 32) {
-                int c = 0, below = 0;
-                for (int k = 0; k < K; k++) {
-                    c += s_idx[k] == e;
-                    below += s_idx[k] < e;
-                }
-                a.counts[e] = c;
-                a.offsets[e] = below;
             }
             if (lane == 0) {
                 a.offsets[E] = K;
@@ -583,14 +598,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the critical path (only this CTA writes these rows, after the barrier)
         const int n4 = D / 4;
         const int c0 = (int)((long)n4 * b / G), c1 = (int)((long)n4 * (b + 1) / G);
-        const int nc = c1 - c0, nrow = 4 * nc;
-        const int my_row = tid / 8, part8 = tid % 8;
-        float xres = 0.0f;
-        if (a.ffn_norm && part8 == 0 && my_row < nrow) xres = a.x[4 * c0 + my_row];
+        const int nc = c1 - c0;
+        const int col = tid >> 3, grp = tid & 7;  // 32 float4 columns x 8 groups of CTAs per pass
+        float4 xres = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.ffn_norm && grp == 0 && col < nc) xres = __ldcg(reinterpret_cast<const float4*>(a.x) + c0 + col);
         named_sync(1, kConsumers);
         if (tid == 0 && !s_fail) {
-            __threadfence();
-            atomicAdd(bar_cnt, 1u);
+            // release: this CTA's partial (ordered before by the named barrier) is
+            // visible at gpu scope before the arrival is
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar_cnt) : "memory");
             if (!wait_count(bar_cnt, (unsigned)G)) {
                 record_error(a.status, 0x602);
                 s_fail = 1;
@@ -598,26 +614,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_sync(1, kConsumers);
         if (tid == 0) TIMELINE(6);
-        // band reduction: rows [4 c0, 4 c1) summed over every CTA's partial in a
-        // fixed order (8 interleaved chains per row, then a fixed pairwise tree)
-        float4* red = reinterpret_cast<float4*>(ring);  // [G][nc]; every ring copy has landed
-        constexpr int kLd = 4;  // partial vectors per thread in flight at once
-        for (int i0 = 0; !s_fail && i0 < G * nc; i0 += kLd * kConsumers) {
-            float4 v[kLd];
-#pragma unroll
-            for (int k = 0; k < kLd; k++) {
-                const int i = i0 + k * kConsumers + tid;
-                if (i < G * nc) {
-                    const int gg = i / nc, c = i - gg * nc;
-                    v[k] = __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t)gg * D) + c0 + c);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < kLd; k++) {
-                const int i = i0 + k * kConsumers + tid;
-                if (i < G * nc) red[i] = v[k];
-            }
-        }
         if (!s_fail) {
             // every CTA has read the logits (before it arrived): clear them for the next launch
             if (b == 0)
@@ -635,21 +631,52 @@ __global__ void __launch_bounds__(kThreads, 1)
                 prefetch_l2(a.next_router + (size_t)b * D * 2, (uint32_t)D * 2);
             if (tid == 64 && a.next_norm && b == G - 1) prefetch_l2(a.next_norm, (uint32_t)D * 4);
         }
-        named_sync(1, kConsumers);
-        if (!s_fail) {
-            const float* redf = reinterpret_cast<const float*>(red);
-            for (int rb = 0; rb < nrow; rb += kConsumers / 8) {
-                const int row = rb + my_row;
-                float s = 0.0f;
-                if (row < nrow)
-                    for (int gg = part8; gg < G; gg += 8) s += redf[gg * nrow + row];
-                s += __shfl_xor_sync(FULL_MASK, s, 1);
-                s += __shfl_xor_sync(FULL_MASK, s, 2);
-                s += __shfl_xor_sync(FULL_MASK, s, 4);
-                if (part8 == 0 && row < nrow) {
-                    const int d = 4 * c0 + row;
-                    const float xr0 = rb == 0 ? xres : (a.ffn_norm ? a.x[d] : 0.0f);
-                    a.out[d] = a.ffn_norm ? __fadd_rn(xr0, s) : s;
+        // band reduction: float4 column c0 + col (4 rows) summed over the CTAs
+        // g = grp, grp + 8, ... in order, then a fixed pairwise tree over the 8
+        // groups; the loads of a pass are all in flight together
+        constexpr int kLdR = 20;
+        for (int cb = 0; !s_fail && cb < nc; cb += kConsumers / 8) {
+            const int cc = cb + col;
+            float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (cc < nc) {
+                const float4* src = reinterpret_cast<const float4*>(a.partials) + c0 + cc;
+                for (int gb = grp; gb < G; gb += 8 * kLdR) {
+                    float4 v[kLdR];
+#pragma unroll
+                    for (int k = 0; k < kLdR; k++) {
+                        const int g = gb + 8 * k;
+                        v[k] = g < G ? __ldcg(src + (size_t)g * n4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int k = 0; k < kLdR; k++) {
+                        s4.x += v[k].x;
+                        s4.y += v[k].y;
+                        s4.z += v[k].z;
+                        s4.w += v[k].w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                s4.x += __shfl_xor_sync(FULL_MASK, s4.x, o);
+                s4.y += __shfl_xor_sync(FULL_MASK, s4.y, o);
+                s4.z += __shfl_xor_sync(FULL_MASK, s4.z, o);
+                s4.w += __shfl_xor_sync(FULL_MASK, s4.w, o);
+            }
+            if (grp == 0 && cc < nc) {
+                float4 xv = xres;
+                if (cb > 0 && a.ffn_norm) xv = __ldcg(reinterpret_cast<const float4*>(a.x) + c0 + cc);
+                float* o = a.out + 4 * (size_t)(c0 + cc);
+                if (a.ffn_norm) {
+                    o[0] = __fadd_rn(xv.x, s4.x);
+                    o[1] = __fadd_rn(xv.y, s4.y);
+                    o[2] = __fadd_rn(xv.z, s4.z);
+                    o[3] = __fadd_rn(xv.w, s4.w);
+                } else {
+                    o[0] = s4.x;
+                    o[1] = s4.y;
+                    o[2] = s4.z;
+                    o[3] = s4.w;
                 }
             }
         }
