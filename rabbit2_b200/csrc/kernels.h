@@ -36,6 +36,7 @@ struct RouterArgs {
     int32_t* tile_cnt;        // [n_tiles, E] routed slots per (token tile, expert)
     int32_t* tile_base;       // [n_tiles, E] first position of the tile's slots of each expert
     int32_t* slot_rank;       // [T*K] rank of a slot among its tile's slots of the same expert
+    int tile_tokens;          // set by launch_router: tokens per tile of the per-tile permutation (0: one tile)
 };
 // Kernels launched are reported in *launches (1 or 2).
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches);

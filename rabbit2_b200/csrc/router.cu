@@ -17,6 +17,8 @@
 // CTA to finish a token tile (atomic counter) runs softmax/top-k for its tokens;
 // the last token tile to finish builds the expert permutation.  Counters are
 // returned to zero by the CTA that consumed them, so no memset between calls.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -26,7 +28,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kExpertsPerCta = 8;
 constexpr int kSmallTokens = 8;          // token tile of the thread-per-chain kernel
-constexpr int kSmallChunk = 2048;        // columns staged per pass (small kernel)
+constexpr int kMidTokens = 256;          // the thread-per-chain kernel up to this many tokens
+constexpr int kSmallChunk = 1024;        // columns staged per pass (small kernel): 66 KB, 3 CTAs per SM
 constexpr int kSmallStride = kSmallChunk + 4;  // == 4 (mod 32): conflict-free chain reads
 constexpr int kLargeChunk = 128;
 constexpr int kLargeStride = kLargeChunk + 4;
@@ -251,8 +254,14 @@ __device__ void build_permutation(const RouterArgs& a) {
     }
 }
 
+__device__ void rank_tile_slots(const RouterArgs& a, const int32_t* s_eidx, int nslots, int slot0, int tile);
+__device__ void finish_tiles(const RouterArgs& a, int ntiles);
+
 // After this CTA's logits are written: the last CTA of the token tile runs
-// softmax/top-k; the last finished tile builds the permutation.
+// softmax/top-k for its tokens.  With one token tile the same CTA then builds
+// the permutation; with several (a.tile_tokens set), each tile ranks its slots
+// per expert, the last tile turns the tile counts into offsets and tile bases,
+// and scatter_kernel places the slots.
 __device__ void tile_epilogue(const RouterArgs& a, int t0, int tcount) {
     __shared__ unsigned s_ticket;
     __threadfence();
@@ -262,6 +271,24 @@ __device__ void tile_epilogue(const RouterArgs& a, int t0, int tcount) {
     if (s_ticket != gridDim.y - 1) return;
     __threadfence();
     finish_tokens(a, t0, tcount);
+    if (a.tile_tokens > 0 && gridDim.x > 1) {
+        __shared__ int32_t s_eidx[kSmallTokens * kMaxTopK];
+        __syncthreads();
+        for (int i = threadIdx.x; i < tcount * a.K; i += kThreads) s_eidx[i] = a.idx[(size_t)t0 * a.K + i];
+        __syncthreads();
+        rank_tile_slots(a, s_eidx, tcount * a.K, t0 * a.K, blockIdx.x);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            a.tile_counter[blockIdx.x] = 0;
+            s_ticket = atomicAdd(a.done_counter, 1u);
+        }
+        __syncthreads();
+        if (s_ticket != gridDim.x - 1) return;
+        __threadfence();
+        finish_tiles(a, gridDim.x);
+        return;
+    }
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -471,6 +498,54 @@ __device__ void rank_tile_slots(const RouterArgs& a, const int32_t* s_eidx, int 
     for (int e = tid; e < a.E; e += kThreads) a.tile_cnt[(size_t)tile * a.E + e] = s_cnt[e];
 }
 
+// Run by the last token tile: per-expert totals (counts, offsets, active list)
+// and every tile's first position per expert.
+__device__ void finish_tiles(const RouterArgs& a, int ntiles) {
+    const int tid = threadIdx.x, E = a.E;
+    // thread (pe, part) owns the contiguous tile range [part*n/P, (part+1)*n/P) of
+    // expert pe (P = 256 / E parts, 1 to 4); the per-tile counts are read 16 loads
+    // at a time, since L2 latency (not bandwidth) is the cost of this single-CTA step
+    constexpr int kMaxParts = 4;
+    __shared__ int s_part[kMaxParts][kMaxExperts];
+    __shared__ int s_off[kMaxExperts];
+    const int P = max(1, min(kMaxParts, kThreads / E));
+    const int pe = tid % E, part = tid / E;
+    const bool mine = part < P;
+    const int tb0 = (int)((long)part * ntiles / P), tb1 = (int)((long)(part + 1) * ntiles / P);
+    int psum = 0;
+    if (mine)
+        for (int t = tb0; t < tb1; t += 16) {
+            int c[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) c[k] = t + k < tb1 ? __ldcg(a.tile_cnt + (size_t)(t + k) * E + pe) : 0;
+#pragma unroll
+            for (int k = 0; k < 16; k++) psum += c[k];
+        }
+    if (mine) s_part[part][pe] = psum;
+    __syncthreads();
+    int tot = 0;
+    if (tid < E)
+        for (int p = 0; p < P; p++) tot += s_part[p][tid];
+    publish_offsets(a, tot, s_off);
+    __syncthreads();
+    if (mine) {
+        int run = s_off[pe];
+        for (int p = 0; p < part; p++) run += s_part[p][pe];
+        for (int t = tb0; t < tb1; t += 16) {
+            int c[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) c[k] = t + k < tb1 ? __ldcg(a.tile_cnt + (size_t)(t + k) * E + pe) : 0;
+#pragma unroll
+            for (int k = 0; k < 16; k++)
+                if (t + k < tb1) {
+                    a.tile_base[(size_t)(t + k) * E + pe] = run;
+                    run += c[k];
+                }
+        }
+    }
+    if (tid == 0) *a.done_counter = 0;
+}
+
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
     using C = WideCfg<WT>;
@@ -579,28 +654,14 @@ __global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
     __syncthreads();
     if (s_ticket != gridDim.x - 1) return;
     __threadfence();
-    const int ntiles = gridDim.x;
-    int tot = 0;
-    if (tid < E)
-        for (int t = 0; t < ntiles; t++) tot += __ldcg(a.tile_cnt + (size_t)t * E + tid);
-    __shared__ int s_off[kMaxExperts];
-    publish_offsets(a, tot, s_off);
-    __syncthreads();
-    if (tid < E) {
-        int run = s_off[tid];
-        for (int t = 0; t < ntiles; t++) {
-            a.tile_base[(size_t)t * E + tid] = run;
-            run += __ldcg(a.tile_cnt + (size_t)t * E + tid);
-        }
-    }
-    if (tid == 0) *a.done_counter = 0;
+    finish_tiles(a, gridDim.x);
 }
 
 // Places every routed slot of a tile: position = tile base of its expert + its
 // stable rank within the tile.
 __global__ void __launch_bounds__(kThreads) scatter_kernel(RouterArgs a) {
-    const int t0 = blockIdx.x * kWideTokens;
-    const int nslots = min(kWideTokens, a.T - t0) * a.K;
+    const int t0 = blockIdx.x * a.tile_tokens;
+    const int nslots = min(a.tile_tokens, a.T - t0) * a.K;
     for (int sl = threadIdx.x; sl < nslots; sl += kThreads) {
         const int s = t0 * a.K + sl;
         const int pos = a.tile_base[(size_t)blockIdx.x * a.E + a.idx[s]] + a.slot_rank[s];
@@ -627,16 +688,31 @@ template <typename WT>
 cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s, int* launches) {
     const int egroups = (a.E + kExpertsPerCta - 1) / kExpertsPerCta;
     *launches = 1;
-    if (a.T <= kSmallTokens) {
+    static const int mid_tokens = [] {
+        const char* v = getenv("RBT_ROUTER_MID_TOKENS");  // tuning: the thread-per-chain kernel up to this T
+        return v ? atoi(v) : kMidTokens;
+    }();
+    if (a.T <= kSmallTokens || a.T <= mid_tokens) {
+        // thread per chain: token tiles of 8 x expert groups of 8 (latency, not
+        // issue rate, bounds a few hundred tokens)
         const size_t smem = 2ull * kExpertsPerCta * kSmallStride * sizeof(float);
-        return launch_with_smem(router_small_kernel<WT>, dim3(1, egroups), smem, a, s);
+        const int tiles = (a.T + kSmallTokens - 1) / kSmallTokens;
+        RouterArgs b = a;
+        b.tile_tokens = tiles > 1 ? kSmallTokens : 0;
+        cudaError_t err = launch_with_smem(router_small_kernel<WT>, dim3(tiles, egroups), smem, b, s);
+        if (err != cudaSuccess || tiles == 1) return err;
+        *launches = 2;
+        scatter_kernel<<<tiles, kThreads, 0, s>>>(b);
+        return cudaGetLastError();
     }
     if (wide_ok(a)) {
         const int tiles = (a.T + kWideTokens - 1) / kWideTokens;
-        cudaError_t err = launch_with_smem(router_wide_kernel<WT>, dim3(tiles), WideCfg<WT>::kSmem, a, s);
+        RouterArgs b = a;
+        b.tile_tokens = kWideTokens;
+        cudaError_t err = launch_with_smem(router_wide_kernel<WT>, dim3(tiles), WideCfg<WT>::kSmem, b, s);
         if (err != cudaSuccess) return err;
         *launches = 2;
-        scatter_kernel<<<tiles, kThreads, 0, s>>>(a);
+        scatter_kernel<<<tiles, kThreads, 0, s>>>(b);
         return cudaGetLastError();
     }
     auto grid_for = [&](int tt) { return dim3((a.T + tt - 1) / tt, egroups); };
@@ -655,7 +731,8 @@ cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s, int* launches) {
 }  // namespace
 
 // Token tiles any router variant uses for T tokens (sizes the per-tile arrays).
-int router_token_tiles(int T) { return T <= kSmallTokens ? 1 : (T + kWideTokens - 1) / kWideTokens; }
+// (tiles of 8 tokens: at least as many as any variant uses, for every T' <= T)
+int router_token_tiles(int T) { return T <= kSmallTokens ? 1 : (T + kSmallTokens - 1) / kSmallTokens; }
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches) {
     *launches = 0;
