@@ -18,8 +18,12 @@ decode; --tokens 4096 is the prefill-sized layer call.
          oracle/_ref) on the host cores, on a bounded sample.
 
 --impl reference times only that CPU path (rank 0) and prints its line.
-Multi-GPU (torchrun): every rank runs an independent replica on its own tokens
-(no collective on the data path), value = all tokens / max-over-ranks time.
+Multi-GPU (torchrun, N ranks): expert parallelism.  Rank g holds experts
+[g*64/N, (g+1)*64/N) of every layer and its own T tokens; each layer routes
+locally, sends every token once to each GPU that owns one of its experts (NCCL
+all-to-all), runs its experts, and adds the returned partial rows in rank order
+(rabbit2_b200/ep.py).  value = N*T tokens / max-over-ranks step time (weak
+scaling: T tokens per GPU).
 """
 from __future__ import annotations
 
@@ -72,7 +76,7 @@ def workload_desc(args):
             "n_experts": E, "top_k": K, "weights": "bf16 ~N(0,0.02) seeded, .rbt2 expert blobs",
             "inputs": "f32 ~N(0,1) seeded", "routing": args.routing,
             "l2": "working set 16 x 805 MB weights per step >> 126 MB L2 (no flush needed)",
-            "parallelism": f"replicas{args.gpus}"}
+            "parallelism": f"ep{args.gpus}" if args.gpus > 1 else "single"}
 
 
 # ----------------------------------------------------------------------------- CPU reference
@@ -280,7 +284,159 @@ def stage_cost(T, U, S):
     return bytes_, flops
 
 
+def run_ep(args, rank, world, local_rank):
+    """Expert-parallel step over `world` GPUs (one process each)."""
+    import torch
+    import torch.distributed as dist
+    from rabbit2_b200 import ep, moe, workload
+
+    dev = torch.device("cuda", local_rank)
+    T, L = args.tokens, args.layers
+    epr = E // world
+    e0 = rank * epr
+    stride = workload.layer_stride(D, H)
+    ctx = moe.MoeContext(D, E, K, H, L, moe.DT_BF16, 0, stride, device=local_rank)
+    ctx.set_path(args.path)
+    ctx.set_expert_range(e0, epr)
+    ones = torch.ones(D, device=dev)
+    keep = []
+    bias = workload.zipf_bias(E, 1.2, seed=0) if args.routing == "zipf" else None
+    for l in range(L):
+        router, experts, _ = workload.device_layer(D, H, E, seed=1 + l, device=dev)
+        local = experts[e0:e0 + epr].clone()
+        del experts
+        ctx.bind_layer(l, router, local, ones)
+        keep.append((router, local))
+        if bias is not None:
+            ctx.set_router_bias(l, bias)
+    ctx.reserve(max(T * world, 1))  # a GPU receives at most every token of every rank
+    # decode-sized calls: fixed dispatch segments (no host read of the counts), so the
+    # whole step is captured in one CUDA graph, NCCL all-to-alls included
+    small = T <= 256
+    m = ep.ExpertParallelMoe(ep.GpuOps(ctx, world), capacity=T if small else None)
+    x0 = workload.inputs(T, D, seed=1000 + rank, device=dev)
+    x = torch.empty_like(x0)
+
+    def step():
+        x.copy_(x0)
+        for l in range(L):
+            m.block(l, x)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    # routed-expert statistics of one step: every rank's local counts, gathered
+    hist = torch.zeros(E, dtype=torch.int64, device=dev)
+    U_sum = 0
+    x.copy_(x0)
+    for l in range(L):
+        m.block(l, x)
+        loc = torch.zeros(E, dtype=torch.int64, device=dev)
+        loc[e0:e0 + epr] = torch.from_numpy(ctx.expert_histogram()[:epr].astype(np.int64)).to(dev)
+        dist.all_reduce(loc)
+        hist += loc
+        U_sum += int((loc > 0).sum())
+    U = U_sum / L
+    ctx.profile(timing=0, reset=True)
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = ctx.profile(reset=True)["launches"] + 3 * L  # + plan, pack, combine per layer
+    g = None
+    if small:
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        torch.cuda.synchronize()
+        for _ in range(3):
+            g.replay()
+    run_step = g.replay if g is not None else step
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        ev0.record()
+        for _ in range(args.steps):
+            run_step()
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    dist.barrier()
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = world * T / (ms / 1e3)
+
+    # e2e: this rank's tokens from pinned host memory in, the block output back, every step
+    xh = x0.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+
+    def host_step():
+        xg = xh.to(dev, non_blocking=True)
+        for l in range(L):
+            m.block(l, xg)
+        oh.copy_(xg, non_blocking=True)
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        host_step()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_step()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    t = torch.tensor([e2e_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
+           "d2h_bytes_per_step": T * D * 4,
+           "how": "ExpertParallelMoe.block per layer on this rank's tokens copied in from pinned host memory, "
+                  "output copied back, wall clock, max over ranks (per-rank bytes)"}
+
+    hbm, bf16, src = peaks()
+    layer_ms = ms / L
+    # whole-job algorithmic bytes and flops of one layer, then per GPU
+    layer_bytes = world * E * D * 2 + U * 3 * H * D * 2 + world * T * D * 4 * 2 + world * T * K * 8
+    layer_flops = world * T * (2 * E * D + 6 * K * H * D)
+    gbs = layer_bytes / world / (layer_ms / 1e3) / 1e9
+    tfs = layer_flops / world / (layer_ms / 1e3) / 1e12
+    tensor_bound = tfs / bf16 > gbs / hbm
+    roofline = {"bound": "tensor" if tensor_bound else "hbm", "kernel": "ep_layer",
+                "achieved": tfs if tensor_bound else gbs, "peak": bf16 if tensor_bound else hbm,
+                "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                "frac": (tfs / bf16) if tensor_bound else (gbs / hbm), "peak_source": src, "traffic": None,
+                "timing": ("CUDA events around the timed steps (route, plan, pack, NCCL all-to-all, experts, "
+                           "NCCL all-to-all, combine per layer" + ("; the step replayed as one CUDA graph"
+                                                                   if g is not None else "") +
+                           "), max over ranks; per GPU: the job's algorithmic bytes or flops of a layer / N / "
+                           "layer time"),
+                "layer": {"us_per_layer": layer_ms * 1e3, "algorithmic_bytes_job": layer_bytes,
+                          "algorithmic_flops_job": layer_flops, "distinct_experts_per_layer": U,
+                          "experts_per_gpu": epr}}
+    out = None
+    if rank == 0:
+        out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_desc(args),
+               "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+               "roofline": roofline, "expert_histogram": hist.cpu().tolist(),
+               "dispatch_rows_last_layer": {"sent": m.last_counts[0], "received": m.last_counts[1]}}
+    if g is not None:
+        del g  # a graph holding NCCL calls goes before the process group
+    torch.cuda.synchronize()
+    ctx.close()
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
+    if world > 1:
+        return run_ep(args, rank, world, local_rank)
     import torch
     import torch.distributed as dist
     from rabbit2_b200 import moe, workload

@@ -92,6 +92,57 @@ int rbt_moe_block_device(RbtMoe *m, int layer, float *d_x, int n_tokens, int32_t
 int rbt_moe_ffn_device(RbtMoe *m, int layer, const float *d_xb, int n_tokens, float *d_moe_out,
                        int32_t *d_routing_out, int routing_stride, void *stream);
 
+/* ---- Expert parallelism across the GPUs of one node (no counterpart in the
+ * reference, which runs one process on CPU; the per-GPU arithmetic is that of
+ * rabbit2.c:512-542).  GPU g owns experts [g*E/N, (g+1)*E/N); each GPU routes its
+ * own tokens with the whole router, sends every token once to each GPU that owns
+ * one of its top-k experts, and adds the partial outputs that come back in
+ * ascending GPU order.  The exchanges are NCCL all-to-alls issued by the caller
+ * (rabbit2_b200/ep.py); these calls prepare and consume their buffers. */
+
+/* Narrow the context to experts [first_expert, first_expert + n_experts_local):
+ * rbt_moe_load_layer / bind_layer then take those n_experts_local blobs, and the
+ * block/ffn calls are replaced by rbt_moe_route_device + rbt_moe_experts_device.
+ * Call before any layer is loaded or bound. */
+int rbt_moe_set_expert_range(RbtMoe *m, int first_expert, int n_experts_local);
+
+/* Router of the layer for n_tokens rows: block != 0 gives d_xb = rmsnorm(d_x)
+ * (rabbit2.c:512), block == 0 copies d_x into d_xb; then d_idx [n_tokens,
+ * top_k] receives the global expert ids in selection order and d_wt the combine
+ * weights (rabbit2.c:513-531), bit-exact as in rbt_moe_block. */
+int rbt_moe_route_device(RbtMoe *m, int layer, const float *d_x, int n_tokens, int block, float *d_xb,
+                         int32_t *d_idx, float *d_wt, void *stream);
+
+/* The experts of this context on routing computed elsewhere: d_idx [n_rows,
+ * top_k] holds expert ids local to the range (0 .. n_experts_local-1) or -1 for
+ * slots another GPU computes; d_out[r] = sum over the local slots, in k order,
+ * of d_wt[r,k] * FFN_k(d_xb[r]) (rabbit2.c:532-541). */
+int rbt_moe_experts_device(RbtMoe *m, int layer, const float *d_xb, int n_rows, const int32_t *d_idx,
+                           const float *d_wt, float *d_out, void *stream);
+
+/* Dispatch plan: d_pos [n_tokens, n_ranks] = position of token t among the
+ * tokens sent to GPU g (ascending t) or -1; d_counts [n_ranks] = tokens sent to
+ * each GPU.  GPU g owns experts [g*experts_per_rank, (g+1)*experts_per_rank).
+ * capacity > 0 (>= n_tokens): fixed segments instead, position t in a segment of
+ * `capacity` rows per GPU, so the exchange sizes are known without reading
+ * d_counts on the host (slots of rows not routed there must be -1 in the send
+ * idx buffer: fill it with -1 before rbt_ep_pack). */
+int rbt_ep_plan(const int32_t *d_idx, int n_tokens, int top_k, int n_ranks, int experts_per_rank, int capacity,
+                int32_t *d_pos, int32_t *d_counts, void *stream);
+
+/* Send buffers in GPU order (segment g starts at counts[0] + ... + counts[g-1]):
+ * rows [., dim] = d_xb[t], idx [., top_k] = expert ids local to GPU g or -1,
+ * wt [., top_k] = the token's combine weights. */
+int rbt_ep_pack(const float *d_xb, const int32_t *d_idx, const float *d_wt, int n_tokens, int dim, int top_k,
+                int n_ranks, int experts_per_rank, const int32_t *d_pos, const int32_t *d_counts, float *d_send_rows,
+                int32_t *d_send_idx, float *d_send_wt, void *stream);
+
+/* d_out[t] = d_x[t] (if not NULL) + the returned partial rows of token t added
+ * in ascending GPU order; d_back_rows is laid out like the send rows.  d_out
+ * may equal d_x. */
+int rbt_ep_combine(const float *d_x, int n_tokens, int dim, int n_ranks, const int32_t *d_pos,
+                   const int32_t *d_counts, const float *d_back_rows, float *d_out, void *stream);
+
 /* Reserve the context's device workspace for up to n_tokens rows per call, so
  * that later calls of that size allocate nothing (e.g. before stream capture). */
 int rbt_moe_reserve(RbtMoe *m, int n_tokens);

@@ -21,9 +21,10 @@ __global__ void __launch_bounds__(kThreads) combine_vec4_kernel(CombineArgs a) {
         const int t = (int)(i / D4), d = (int)(i - (long)t * D4) * 4;
         float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int k = 0; k < a.K; k++) {
-            const int s = t * a.K + k;
+            const int s = t * a.K + k, sp = a.slot_pos[s];
+            if (sp < 0) continue;  // a slot another GPU computes (expert parallelism)
             const float w = a.wt[s];
-            const float4 y = *reinterpret_cast<const float4*>(a.y + (size_t)a.slot_pos[s] * a.D + d);
+            const float4 y = *reinterpret_cast<const float4*>(a.y + (size_t)sp * a.D + d);
             m.x = __fadd_rn(m.x, __fmul_rn(w, y.x));
             m.y = __fadd_rn(m.y, __fmul_rn(w, y.y));
             m.z = __fadd_rn(m.z, __fmul_rn(w, y.z));
@@ -43,8 +44,8 @@ __global__ void __launch_bounds__(kThreads) combine_scalar_kernel(CombineArgs a)
         const int t = (int)(i / a.D), d = (int)(i - (long)t * a.D);
         float m = 0.0f;
         for (int k = 0; k < a.K; k++) {
-            const int s = t * a.K + k;
-            m = __fadd_rn(m, __fmul_rn(a.wt[s], a.y[(size_t)a.slot_pos[s] * a.D + d]));
+            const int s = t * a.K + k, sp = a.slot_pos[s];
+            if (sp >= 0) m = __fadd_rn(m, __fmul_rn(a.wt[s], a.y[(size_t)sp * a.D + d]));
         }
         if (a.resid) m = __fadd_rn(a.resid[(size_t)t * a.D + d], m);
         a.out[(size_t)t * a.D + d] = m;

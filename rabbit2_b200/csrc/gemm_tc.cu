@@ -251,9 +251,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // f32 rows of x, gathered into expert order, split into bf16 hi + lo.
+// n_slots (device, or null for S): the routed slots to gather; fewer than S when
+// some slots belong to experts on other GPUs.
 __global__ void __launch_bounds__(256) gather_split_kernel(const float* __restrict__ xb, const int32_t* perm, int S,
-                                                           int D, int K, __nv_bfloat16* xhi, __nv_bfloat16* xlo) {
+                                                           const int32_t* n_slots, int D, int K,
+                                                           __nv_bfloat16* xhi, __nv_bfloat16* xlo) {
     const int vpr = D / 8;
+    if (n_slots) S = min(S, *n_slots);
     const long total = (long)S * vpr;
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int p = (int)(i / vpr), v = (int)(i - (long)p * vpr);
@@ -399,13 +403,13 @@ bool make_map_3d_plain(CUtensorMap* map, const void* base, int cols, int rows, i
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
-                                cudaStream_t s) {
+cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, const int32_t* n_slots, int D, int K,
+                                void* xhi, void* xlo, cudaStream_t s) {
     if (S <= 0) return cudaSuccess;
     const long total = (long)S * (D / 8);
     const long blocks = (total + 255) / 256;
     gather_split_kernel<<<(int)(blocks < 148L * 8 ? blocks : 148L * 8), 256, 0, s>>>(
-        xb, perm, S, D, K, static_cast<__nv_bfloat16*>(xhi), static_cast<__nv_bfloat16*>(xlo));
+        xb, perm, S, n_slots, D, K, static_cast<__nv_bfloat16*>(xhi), static_cast<__nv_bfloat16*>(xlo));
     return cudaGetLastError();
 }
 

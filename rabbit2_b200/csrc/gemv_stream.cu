@@ -323,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1) down_combine_stream_kernel(Stream
                     const int t = i / kDR, dr = i - t * kDR;
                     float mo = 0.0f;
                     for (int k = 0; k < K; k++) {
-                        const int s = t * K + k;
-                        mo = __fadd_rn(mo, __fmul_rn(a.wt[s], ybuf[a.slot_pos[s] * kDR + dr]));
+                        const int s = t * K + k, sp = a.slot_pos[s];
+                        if (sp >= 0) mo = __fadd_rn(mo, __fmul_rn(a.wt[s], ybuf[sp * kDR + dr]));
                     }
                     const size_t o = (size_t)t * D + d0 + dr;
                     a.out[o] = a.resid ? __fadd_rn(a.resid[o], mo) : mo;

@@ -40,6 +40,9 @@ struct RouterArgs {
 };
 // Kernels launched are reported in *launches (1 or 2).
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches);
+// The permutation of given routing (a.idx in [0, a.E) or -1): counts, offsets,
+// active list, perm and slot_pos (-1 for slots outside this GPU's experts).
+cudaError_t launch_route_given(const RouterArgs& a, cudaStream_t s, int* launches);
 
 // K3: grouped GEMV over the active experts (CUDA cores, fp32 accumulation).
 struct GemvArgs {
@@ -147,7 +150,8 @@ bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, in
 // bf16 [E][rows][cols] with row pitch cols*2 and matrix pitch `stride`, unswizzled boxes
 bool make_map_3d_plain(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride, int box_cols,
                        int box_rows);
-cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, int D, int K, void* xhi, void* xlo,
+cudaError_t launch_gather_split(const float* xb, const int32_t* perm, int S, const int32_t* n_slots, int D, int K,
+                                void* xhi, void* xlo,
                                 cudaStream_t s);
 cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, int E, int bn, int32_t* tb_e,
                                int32_t* tb_p0, int32_t* tb_p1, int32_t* n_tb, cudaStream_t s);

@@ -99,6 +99,8 @@ struct RbtMoe {
     int path = 0;
     int gemm_min_tokens = 2;   // automatic path: tensor-core GEMM from this many tokens (one token: fused decode)
     size_t esz = 2;
+    int e0 = 0;                // expert parallelism: this context holds experts [e0, e0 + n_local)
+    int n_local = 0;           // == cfg.n_experts unless rbt_moe_set_expert_range narrowed it
     cudaStream_t stream = nullptr;
     std::vector<Layer> layers;
     Workspace ws;
@@ -194,7 +196,8 @@ bool decode_w2t_enabled() {
 void layer_maps(RbtMoe* m, Layer& L) {
     const RbtMoeConfig& c = m->cfg;
     L.tc = false;
-    L.dec = c.dtype == 1 && (c.expert_stride % 16) == 0 && (reinterpret_cast<uintptr_t>(L.experts) % 16) == 0 &&
+    L.dec = m->n_local == c.n_experts && c.dtype == 1 && (c.expert_stride % 16) == 0 &&
+            (reinterpret_cast<uintptr_t>(L.experts) % 16) == 0 &&
             (c.expert_hidden % 8) == 0 && c.dim <= 2048 &&
             rbt::make_decode_w2_map(&L.w2_cols, L.experts, c.dim, c.expert_hidden, c.n_experts, c.expert_stride);
     // the one-token kernel streams w2 fastest as rows of its transpose: one
@@ -220,10 +223,10 @@ void layer_maps(RbtMoe* m, Layer& L) {
     if (!rbt::tc_supported(c.dim, c.expert_hidden, c.dtype) || (c.expert_stride % 16) != 0 ||
         (reinterpret_cast<uintptr_t>(L.experts) % 16) != 0)
         return;
-    L.tc = rbt::make_map_experts(&L.w_gateup, L.experts, c.dim, 2 * c.expert_hidden, c.n_experts,
+    L.tc = rbt::make_map_experts(&L.w_gateup, L.experts, c.dim, 2 * c.expert_hidden, m->n_local,
                                  c.expert_stride) &&
            rbt::make_map_experts(&L.w_down, L.experts + (size_t)2 * c.expert_hidden * c.dim * 2, c.expert_hidden,
-                                 c.dim, c.n_experts, c.expert_stride);
+                                 c.dim, m->n_local, c.expert_stride);
 }
 
 int check_layer(RbtMoe* m, int layer, bool need_norm) {
@@ -283,9 +286,18 @@ rbt::StreamArgs sa_of(RbtMoe* m, const Layer& L, const float* xb, const float* x
 
 // The whole MoE call on device pointers.  block: x is the residual stream,
 // updated in place; otherwise out = moe(xb).
+// given_idx / given_wt (expert parallelism): the routing comes from outside, with
+// expert ids local to this context's range and -1 for slots computed elsewhere;
+// x is then the router input itself (no norm, no router) and out = the weighted
+// sum over the local slots.
 int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* routing, int routing_stride,
-            cudaStream_t s, bool block) {
+            cudaStream_t s, bool block, const int32_t* given_idx = nullptr, const float* given_wt = nullptr) {
     if (!check_layer(m, layer, block)) return 0;
+    const bool given = given_idx != nullptr;
+    if (!given && m->n_local != m->cfg.n_experts)
+        return fail("this context holds experts [%d, %d) only (expert parallelism): use rbt_moe_route_device and "
+                    "rbt_moe_experts_device", m->e0, m->e0 + m->n_local);
+    const int E_run = given ? m->n_local : m->cfg.n_experts;
     if (T < 0) return fail("n_tokens must be >= 0 (got %d)", T);
     if (T == 0) return 1;
     if (routing && routing_stride < m->cfg.top_k)
@@ -296,7 +308,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     Workspace& w = m->ws;
     StageClock clk{m, s};
     m->prof.calls++;
-    if ((m->path == 0 || m->path == 4) && L.dec &&
+    if (!given && (m->path == 0 || m->path == 4) && L.dec &&
         (!block || (reinterpret_cast<uintptr_t>(L.ffn_norm) % 16) == 0) &&
         rbt::decode_fused_supported(T, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, L.experts,
                                     c.expert_stride, x, L.router)) {
@@ -318,9 +330,10 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         CU(rbt::launch_decode_fused(da, L.w2_cols, m->sm_count, s));
         return clk.end();
     }
-    if (m->path == 4) return fail("fused decode path requested but unavailable (needs T == 1, bf16, D <= 2048)");
+    if (m->path == 4 && !given)
+        return fail("fused decode path requested but unavailable (needs T == 1, bf16, D <= 2048)");
     const float* xb = x;
-    if (block) {
+    if (block && !given) {
         if (!clk.begin(0)) return 0;
         CU(rbt::launch_rmsnorm(x, L.ffn_norm, w.xb, T, c.dim, c.rms_eps, s));
         xb = w.xb;
@@ -337,8 +350,17 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     ra.tile_cnt = w.tile_cnt; ra.tile_base = w.tile_base; ra.slot_rank = w.slot_rank;
     if (!clk.begin(1)) return 0;
     int router_launches = 0;
-    CU(rbt::launch_router(ra, s, &router_launches));
+    if (given) {  // the permutation of the given slots over the local experts
+        ra.E = E_run;
+        ra.idx = const_cast<int32_t*>(given_idx);
+        ra.wt = const_cast<float*>(given_wt);
+        ra.routing_out = nullptr;
+        CU(rbt::launch_route_given(ra, s, &router_launches));
+    } else {
+        CU(rbt::launch_router(ra, s, &router_launches));
+    }
     m->prof.launches += router_launches - 1;
+    const float* wt = given ? given_wt : w.wt;
 
     // the split kernel reads xb with 16-byte vectors
     const bool tc_ready = L.tc && w.tc_maps && (reinterpret_cast<uintptr_t>(xb) % 16 == 0);
@@ -349,10 +371,11 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     if (use_tc) {
         const int S = T * c.top_k;
         if (!clk.begin(5)) return 0;
-        CU(rbt::launch_gather_split(xb, w.perm, S, c.dim, c.top_k, w.xhi, w.xlo, s));
-        const int bn = rbt::tc_pick_bn(T, c.top_k, c.n_experts);
+        CU(rbt::launch_gather_split(xb, w.perm, S, given ? w.offsets + E_run : nullptr, c.dim, c.top_k, w.xhi,
+                                    w.xlo, s));
+        const int bn = rbt::tc_pick_bn(T, c.top_k, E_run);
         const int bi = bn == 32 ? 0 : (bn == 64 ? 1 : 2);
-        CU(rbt::launch_tc_schedule(w.counts, w.offsets, c.n_experts, bn, w.tb_e, w.tb_p0, w.tb_p1, w.n_tb, s));
+        CU(rbt::launch_tc_schedule(w.counts, w.offsets, E_run, bn, w.tb_e, w.tb_p0, w.tb_p1, w.n_tb, s));
         m->prof.launches++;
         rbt::TcGemmArgs ta{};
         ta.BN = bn;
@@ -364,8 +387,9 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
         if (!clk.begin(3)) return 0;
         CU(rbt::launch_tc_down(L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
-    } else if (m->path != 3 && rbt::stream_supported(sa_of(m, L, xb, x, out, T, block), c.dtype)) {
-        const rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, block);
+    } else if (m->path != 3 && rbt::stream_supported(sa_of(m, L, xb, x, out, T, block && !given), c.dtype)) {
+        rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, block && !given);
+        sa.wt = wt;
         if (!clk.begin(2)) return 0;
         CU(rbt::launch_gateup_stream(sa, m->sm_count, s));
         if (!clk.begin(3)) return 0;
@@ -374,7 +398,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     } else {
         rbt::GemvArgs ga{};
         ga.xb = xb; ga.experts = L.experts; ga.stride = c.expert_stride;
-        ga.T = T; ga.D = c.dim; ga.H = c.expert_hidden; ga.E = c.n_experts; ga.K = c.top_k; ga.dtype = c.dtype;
+        ga.T = T; ga.D = c.dim; ga.H = c.expert_hidden; ga.E = E_run; ga.K = c.top_k; ga.dtype = c.dtype;
         ga.perm = w.perm; ga.offsets = w.offsets; ga.active = w.active; ga.n_active = w.n_active;
         ga.h = w.h; ga.y = w.y; ga.grid = m->sm_count;
         if (!clk.begin(2)) return 0;
@@ -384,9 +408,9 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     }
 
     rbt::CombineArgs ca{};
-    ca.resid = block ? x : nullptr;
-    ca.y = w.y; ca.wt = w.wt; ca.slot_pos = w.slot_pos;
-    ca.out = block ? const_cast<float*>(x) : out;
+    ca.resid = block && !given ? x : nullptr;
+    ca.y = w.y; ca.wt = wt; ca.slot_pos = w.slot_pos;
+    ca.out = block && !given ? const_cast<float*>(x) : out;
     ca.T = T; ca.D = c.dim; ca.K = c.top_k;
     if (!clk.begin(4)) return 0;
     CU(rbt::launch_combine(ca, s));
@@ -453,6 +477,7 @@ int rbt_moe_create(RbtMoe** out, const RbtMoeConfig* cfg, int device) {
     RbtMoe* m = new (std::nothrow) RbtMoe();
     if (!m) return fail("out of host memory");
     m->cfg = c;
+    m->n_local = c.n_experts;
     m->device = device;
     m->esz = esz;
     if (const char* v = getenv("RBT_MOE_GEMM_MIN_TOKENS")) m->gemm_min_tokens = atoi(v);
@@ -488,7 +513,7 @@ int rbt_moe_load_layer(RbtMoe* m, int layer, const float* ffn_norm, const void* 
     if (!router || !experts) return fail("null router/experts pointer");
     if (!set_device(m)) return 0;
     const RbtMoeConfig& c = m->cfg;
-    const size_t b_exp = (size_t)c.n_experts * c.expert_stride;
+    const size_t b_exp = (size_t)m->n_local * c.expert_stride;
     const size_t b_router = (size_t)c.n_experts * c.dim * m->esz;
     const size_t b_norm = (size_t)c.dim * 4;
     const size_t o_router = align_up(b_exp, 256), o_norm = align_up(o_router + b_router, 256);
@@ -565,6 +590,60 @@ int rbt_moe_ffn_device(RbtMoe* m, int layer, const float* d_xb, int n_tokens, fl
     if (!m) return fail("null context");
     if ((!d_xb || !d_moe_out) && n_tokens > 0) return fail("null xb/moe_out");
     return forward(m, layer, d_xb, d_moe_out, n_tokens, d_routing_out, routing_stride, (cudaStream_t)stream, false);
+}
+
+int rbt_moe_set_expert_range(RbtMoe* m, int first_expert, int n_experts_local) {
+    if (!m) return fail("null context");
+    const int E = m->cfg.n_experts;
+    if (first_expert < 0 || n_experts_local <= 0 || first_expert + n_experts_local > E)
+        return fail("expert range [%d, %d) outside [0, %d)", first_expert, first_expert + n_experts_local, E);
+    for (const Layer& L : m->layers)
+        if (L.experts) return fail("set the expert range before loading or binding any layer");
+    m->e0 = first_expert;
+    m->n_local = n_experts_local;
+    return 1;
+}
+
+int rbt_moe_route_device(RbtMoe* m, int layer, const float* d_x, int n_tokens, int block, float* d_xb,
+                         int32_t* d_idx, float* d_wt, void* stream) {
+    if (!m) return fail("null context");
+    if (n_tokens < 0) return fail("n_tokens must be >= 0 (got %d)", n_tokens);
+    if (n_tokens == 0) return 1;
+    if (!d_x || !d_xb || !d_idx || !d_wt) return fail("null argument");
+    if (!check_layer(m, layer, block != 0) || !set_device(m) || !reserve(m, n_tokens)) return 0;
+    const RbtMoeConfig& c = m->cfg;
+    const Layer& L = m->layers[layer];
+    Workspace& w = m->ws;
+    cudaStream_t s = (cudaStream_t)stream;
+    StageClock clk{m, s};
+    m->prof.calls++;
+    if (block) {
+        if (!clk.begin(0)) return 0;
+        CU(rbt::launch_rmsnorm(d_x, L.ffn_norm, d_xb, n_tokens, c.dim, c.rms_eps, s));
+    } else if (d_xb != d_x) {
+        CU(cudaMemcpyAsync(d_xb, d_x, (size_t)n_tokens * c.dim * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    }
+    rbt::RouterArgs ra{};
+    ra.xb = d_xb;
+    ra.T = n_tokens; ra.D = c.dim; ra.E = c.n_experts; ra.K = c.top_k;
+    ra.router = L.router; ra.dtype = c.dtype; ra.bias = L.bias; ra.norm_topk = c.norm_topk;
+    ra.logits = w.logits; ra.idx = d_idx; ra.wt = d_wt;
+    ra.tile_counter = w.tile_counter; ra.done_counter = w.done_counter;
+    ra.counts = w.counts; ra.offsets = w.offsets; ra.perm = w.perm; ra.slot_pos = w.slot_pos;
+    ra.active = w.active; ra.n_active = w.n_active;
+    ra.tile_cnt = w.tile_cnt; ra.tile_base = w.tile_base; ra.slot_rank = w.slot_rank;
+    if (!clk.begin(1)) return 0;
+    int launches = 0;
+    CU(rbt::launch_router(ra, s, &launches));
+    m->prof.launches += launches - 1;
+    return clk.end();
+}
+
+int rbt_moe_experts_device(RbtMoe* m, int layer, const float* d_xb, int n_rows, const int32_t* d_idx,
+                           const float* d_wt, float* d_out, void* stream) {
+    if (!m) return fail("null context");
+    if (n_rows > 0 && (!d_xb || !d_idx || !d_wt || !d_out)) return fail("null argument");
+    return forward(m, layer, d_xb, d_out, n_rows, nullptr, m->cfg.top_k, (cudaStream_t)stream, false, d_idx, d_wt);
 }
 
 int rbt_moe_expert_histogram(RbtMoe* m, int32_t* counts_out) {

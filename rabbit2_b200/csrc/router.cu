@@ -664,10 +664,39 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(RouterArgs a) {
     const int nslots = min(a.tile_tokens, a.T - t0) * a.K;
     for (int sl = threadIdx.x; sl < nslots; sl += kThreads) {
         const int s = t0 * a.K + sl;
-        const int pos = a.tile_base[(size_t)blockIdx.x * a.E + a.idx[s]] + a.slot_rank[s];
+        const int e = a.idx[s];
+        if (e < 0 || e >= a.E) {  // a slot computed on another GPU (expert parallelism)
+            a.slot_pos[s] = -1;
+            continue;
+        }
+        const int pos = a.tile_base[(size_t)blockIdx.x * a.E + e] + a.slot_rank[s];
         a.perm[pos] = s;
         a.slot_pos[s] = pos;
     }
+}
+
+// The permutation of routing that comes from outside (expert parallelism): a.idx
+// holds expert ids of this GPU's range, or -1 for slots other GPUs compute.  Tiles
+// of 16 tokens rank their slots per expert; the last tile computes offsets and
+// tile bases; scatter_kernel places the slots (and marks the others -1).
+__global__ void __launch_bounds__(kThreads) route_given_kernel(RouterArgs a) {
+    __shared__ int32_t s_eidx[kWideTokens * kMaxTopK];
+    const int t0 = blockIdx.x * kWideTokens;
+    const int nslots = min(kWideTokens, a.T - t0) * a.K;
+    for (int i = threadIdx.x; i < nslots; i += kThreads) {
+        const int e = a.idx[(size_t)t0 * a.K + i];
+        s_eidx[i] = (e >= 0 && e < a.E) ? e : -1;
+    }
+    __syncthreads();
+    rank_tile_slots(a, s_eidx, nslots, t0 * a.K, blockIdx.x);
+    __shared__ unsigned s_ticket;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_ticket = atomicAdd(a.done_counter, 1u);
+    __syncthreads();
+    if (s_ticket != gridDim.x - 1) return;
+    __threadfence();
+    finish_tiles(a, gridDim.x);
 }
 
 bool wide_ok(const RouterArgs& a) {
@@ -733,6 +762,21 @@ cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s, int* launches) {
 // Token tiles any router variant uses for T tokens (sizes the per-tile arrays).
 // (tiles of 8 tokens: at least as many as any variant uses, for every T' <= T)
 int router_token_tiles(int T) { return T <= kSmallTokens ? 1 : (T + kSmallTokens - 1) / kSmallTokens; }
+
+cudaError_t launch_route_given(const RouterArgs& a, cudaStream_t s, int* launches) {
+    *launches = 0;
+    if (a.T <= 0) return cudaSuccess;
+    if (a.K > kMaxTopK || a.E > kMaxExperts) return cudaErrorInvalidValue;
+    const int tiles = (a.T + kWideTokens - 1) / kWideTokens;
+    RouterArgs b = a;
+    b.tile_tokens = kWideTokens;
+    route_given_kernel<<<tiles, kThreads, 0, s>>>(b);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    scatter_kernel<<<tiles, kThreads, 0, s>>>(b);
+    *launches = 2;
+    return cudaGetLastError();
+}
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches) {
     *launches = 0;

@@ -64,6 +64,12 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_moe_expert_histogram": [vp, vp],
         "rbt_moe_set_path": [vp, i32],
         "rbt_moe_profile": [vp, i32, i32, C.POINTER(RbtMoeProfile)],
+        "rbt_moe_set_expert_range": [vp, i32, i32],
+        "rbt_moe_route_device": [vp, i32, vp, i32, i32, vp, vp, vp, vp],
+        "rbt_moe_experts_device": [vp, i32, vp, i32, vp, vp, vp, vp],
+        "rbt_ep_plan": [vp, i32, i32, i32, i32, i32, vp, vp, vp],
+        "rbt_ep_pack": [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp],
+        "rbt_ep_combine": [vp, i32, i32, i32, vp, vp, vp, vp, vp],
     }
     for name, argtypes in sig.items():
         fn = getattr(lib, name)
@@ -169,6 +175,24 @@ class MoeContext:
         self._call(self.lib.rbt_moe_block_device, self.handle, layer, _ptr(x), T, _ptr(routing),
                    routing_stride or self.K, _ptr(stream) if stream is not None else None)
 
+    # expert parallelism
+    def set_expert_range(self, first_expert, n_local):
+        """Hold only experts [first_expert, first_expert + n_local) (before any layer is bound)."""
+        self._call(self.lib.rbt_moe_set_expert_range, self.handle, first_expert, n_local)
+        self.e0, self.n_local = first_expert, n_local
+
+    def route_device(self, layer, x, xb, idx, wt, block=True, T=None, stream=None):
+        """Router only: xb = rmsnorm(x) (block) or x; idx/wt [T, K] global ids and weights."""
+        T = x.shape[0] if T is None else T
+        self._call(self.lib.rbt_moe_route_device, self.handle, layer, _ptr(x), T, int(block), _ptr(xb), _ptr(idx),
+                   _ptr(wt), _ptr(stream) if stream is not None else None)
+
+    def experts_device(self, layer, xb, idx, wt, out, n=None, stream=None):
+        """out[r] = sum over local slots (idx >= 0, ids local to the range) of wt * FFN(xb[r])."""
+        n = xb.shape[0] if n is None else n
+        self._call(self.lib.rbt_moe_experts_device, self.handle, layer, _ptr(xb), n, _ptr(idx), _ptr(wt),
+                   _ptr(out), _ptr(stream) if stream is not None else None)
+
     def profile(self, timing=-1, reset=False):
         """Launch counts and per-stage device ms since the last reset (dict)."""
         p = RbtMoeProfile()
@@ -188,4 +212,4 @@ def declared_symbols(header: str = HEADER):
     import re
     with open(header) as f:
         text = f.read()
-    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(rbt_moe_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(rbt_(?:moe|ep)_\w+)\s*\(", text, flags=re.M)))
