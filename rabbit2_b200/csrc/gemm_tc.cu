@@ -13,6 +13,10 @@
 // and are split into bf16 hi = rn(x) and lo = rn(x - hi) (16 significant bits);
 // each K step issues two MMAs (hi and lo) into the same f32 accumulator.  One
 // bf16 operand alone gives ~3e-3 relative error on this layer, over the 1e-3 bar.
+// The gate/up GEMM can instead run one fp16 MMA per K step (kF16): an fp16 copy
+// of w1/w3 (bf16 values convert exactly unless they are fp16-subnormal), and the
+// activation row scaled by a power of two so its largest element is below 2^14,
+// rounded once to fp16 (11 significant bits); the epilogue undoes the scale.
 //
 // Pipeline per CTA (persistent, one CTA per SM, 192 threads):
 //   warp 0  TMA producer: weight tile via a 3-D map over the expert blobs
@@ -25,6 +29,7 @@
 // MMAs (again bounded), frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -43,11 +48,12 @@ constexpr int kStageBudget = 200 * 1024;   // shared memory for the operand ring
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 
 // BN: routed tokens per tile (the MMA's N), 32, 64 or 128.
-template <bool kGateUp, int BN>
+template <bool kGateUp, int BN, bool kF16 = false>
 struct Cfg {
     static constexpr int NA = kGateUp ? 2 : 1;                 // weight tiles per stage
-    static constexpr int kBTileBytes = BN * kBK * 2;           // one token tile (hi or lo)
-    static constexpr int kStageBytes = NA * kTileBytes + 2 * kBTileBytes;
+    static constexpr int NB = kF16 ? 1 : 2;                    // token tiles per stage (hi, lo | fp16)
+    static constexpr int kBTileBytes = BN * kBK * 2;           // one token tile
+    static constexpr int kStageBytes = NA * kTileBytes + NB * kBTileBytes;
     static constexpr int kStages = kStageBudget / kStageBytes > 6 ? 6 : kStageBudget / kStageBytes;
     static constexpr int kAccCols = NA * BN;                   // TMEM columns per accumulator buffer
     static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;  // double buffered
@@ -59,11 +65,12 @@ __device__ __forceinline__ void record_error(unsigned* status, unsigned code) {
     atomicCAS(status, 0u, code);
 }
 
-template <bool kGateUp, int BN>
+template <bool kGateUp, int BN, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_bhi,
                        const __grid_constant__ CUtensorMap tm_blo, TcGemmArgs a) {
-    using C = Cfg<kGateUp, BN>;
+    using C = Cfg<kGateUp, BN, kF16>;
+    static_assert(kGateUp || !kF16, "the fp16 form is the gate/up GEMM's");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
@@ -122,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(st, &tm_w, &full[stage], kb * kBK, mb * kBM, e);
                 if (kGateUp) tma_load_3d(st + kTileBytes, &tm_w, &full[stage], kb * kBK, a.H + mb * kBM, e);
                 tma_load_2d(st + C::NA * kTileBytes, &tm_bhi, &full[stage], kb * kBK, p0);
-                tma_load_2d(st + C::NA * kTileBytes + C::kBTileBytes, &tm_blo, &full[stage], kb * kBK, p0);
+                if (!kF16) tma_load_2d(st + C::NA * kTileBytes + C::kBTileBytes, &tm_blo, &full[stage], kb * kBK, p0);
                 used[stage] = true;
                 last_parity[stage] = phase;
                 if (++stage == C::kStages) {
@@ -136,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (used[s] && !mbar_wait_bounded(&full[s], last_parity[s], kWaitNs)) record_error(a.status, 0x102);
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+        constexpr uint32_t idesc = kF16 ? idesc_f16_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
         int stage = 0;
         uint32_t phase = 0;
         int buf = 0;
@@ -164,11 +171,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t bh = sw128_kmajor_desc(sbh + koff), bl = sw128_kmajor_desc(sbl + koff);
                     const uint64_t a1 = sw128_kmajor_desc(sa + koff);
                     mma_bf16(d1, a1, bh, idesc, (kb | kk) != 0);
-                    mma_bf16(d1, a1, bl, idesc, 1u);
+                    if (!kF16) mma_bf16(d1, a1, bl, idesc, 1u);
                     if (kGateUp) {
                         const uint64_t a3 = sw128_kmajor_desc(sa + kTileBytes + koff);
                         mma_bf16(d1 + BN, a3, bh, idesc, (kb | kk) != 0);
-                        mma_bf16(d1 + BN, a3, bl, idesc, 1u);
+                        if (!kF16) mma_bf16(d1 + BN, a3, bl, idesc, 1u);
                     }
                 }
                 mma_commit(&empty[stage]);
@@ -217,7 +224,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int jj = 0; jj < 32; jj++) {
                         const int p = p0 + j0 + jj;
                         if (j0 + jj < ntok) {
-                            const float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
+                            float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
+                            if (kF16) {  // undo the activation row's power-of-two scale (exact)
+                                const float sc = a.bscale[p];
+                                gv *= sc;
+                                uv *= sc;
+                            }
                             const float hv = gv / (1.0f + expf(-gv)) * uv;
                             const __nv_bfloat16 hi = __float2bfloat16_rn(hv);
                             const __nv_bfloat16 lo = __float2bfloat16_rn(hv - __bfloat162float(hi));
@@ -323,25 +335,78 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <bool kGateUp, int BN>
+template <bool kGateUp, int BN, bool kF16>
 cudaError_t launch_gemm_bn(const CUtensorMap& w, const CUtensorMap& bhi, const CUtensorMap& blo,
                            const TcGemmArgs& a, int grid, cudaStream_t s) {
-    using C = Cfg<kGateUp, BN>;
-    cudaError_t err = cudaFuncSetAttribute(moe_tc_gemm_kernel<kGateUp, BN>,
+    using C = Cfg<kGateUp, BN, kF16>;
+    cudaError_t err = cudaFuncSetAttribute(moe_tc_gemm_kernel<kGateUp, BN, kF16>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (err != cudaSuccess) return err;
-    moe_tc_gemm_kernel<kGateUp, BN><<<grid, kThreads, C::kSmemBytes, s>>>(w, bhi, blo, a);
+    moe_tc_gemm_kernel<kGateUp, BN, kF16><<<grid, kThreads, C::kSmemBytes, s>>>(w, bhi, blo, a);
     return cudaGetLastError();
 }
 
-template <bool kGateUp>
+template <bool kGateUp, bool kF16 = false>
 cudaError_t launch_gemm(const CUtensorMap& w, const CUtensorMap& bhi, const CUtensorMap& blo, const TcGemmArgs& a,
                         int grid, cudaStream_t s) {
     switch (a.BN) {
-        case 32: return launch_gemm_bn<kGateUp, 32>(w, bhi, blo, a, grid, s);
-        case 64: return launch_gemm_bn<kGateUp, 64>(w, bhi, blo, a, grid, s);
-        case 128: return launch_gemm_bn<kGateUp, 128>(w, bhi, blo, a, grid, s);
+        case 32: return launch_gemm_bn<kGateUp, 32, kF16>(w, bhi, blo, a, grid, s);
+        case 64: return launch_gemm_bn<kGateUp, 64, kF16>(w, bhi, blo, a, grid, s);
+        case 128: return launch_gemm_bn<kGateUp, 128, kF16>(w, bhi, blo, a, grid, s);
         default: return cudaErrorInvalidValue;
+    }
+}
+
+// fp16 rows for the gate/up GEMM: one warp per routed slot; the row is scaled by
+// 2^-s (s from its largest magnitude, so that every element is below 2^14) and
+// rounded once to fp16; scale[p] = 2^s.
+__global__ void __launch_bounds__(256) gather_f16_kernel(const float* __restrict__ xb, const int32_t* perm, int S,
+                                                         const int32_t* n_slots, int D, int K, __half* xh,
+                                                         float* scale) {
+    if (n_slots) S = min(S, *n_slots);
+    const int lane = threadIdx.x & 31;
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < S; p += nw) {
+        const float4* src = reinterpret_cast<const float4*>(xb + (size_t)(perm[p] / K) * D);
+        float mx = 0.0f;
+        for (int v = lane; v < D / 4; v += 32) {
+            const float4 f = __ldg(src + v);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // mx < 2^e for its binary exponent e (mx = m * 2^e, 0.5 <= m < 1): the
+        // scaled row stays below 2^14
+        int sexp = 0;
+        if (mx > 0.0f) {
+            int e;
+            frexpf(mx, &e);
+            sexp = e - 14;
+        }
+        if (lane == 0) scale[p] = ldexpf(1.0f, sexp);
+        for (int v = lane; v < D / 4; v += 32) {
+            const float4 f = __ldg(src + v);
+            const __half2 h01 = __floats2half2_rn(ldexpf(f.x, -sexp), ldexpf(f.y, -sexp));
+            const __half2 h23 = __floats2half2_rn(ldexpf(f.z, -sexp), ldexpf(f.w, -sexp));
+            __half2* d = reinterpret_cast<__half2*>(xh + (size_t)p * D + v * 4);
+            d[0] = h01;
+            d[1] = h23;
+        }
+    }
+}
+
+// w1|w3 of every expert as one fp16 matrix [2H, D] per expert (rows w1 then w3),
+// contiguous; *overflow is set if a value does not fit fp16.
+__global__ void convert_gateup_f16_kernel(const uint8_t* experts, size_t stride, int D, int H, int E, __half* out,
+                                          unsigned* overflow) {
+    const size_t per = (size_t)2 * H * D;
+    const size_t total = per * E;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t e = i / per, j = i - e * per;
+        const uint16_t b = reinterpret_cast<const uint16_t*>(experts + e * stride)[j];
+        const float f = __uint_as_float((uint32_t)b << 16);
+        if (fabsf(f) > 65504.0f) atomicExch(overflow, 1u);
+        out[i] = __float2half_rn(f);
     }
 }
 
@@ -422,6 +487,27 @@ cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, in
 cudaError_t launch_tc_gateup(const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
                              const TcGemmArgs& a, int grid, cudaStream_t s) {
     return launch_gemm<true>(w, xhi, xlo, a, grid, s);
+}
+
+cudaError_t launch_tc_gateup_f16(const CUtensorMap& w16, const CUtensorMap& xh, const TcGemmArgs& a, int grid,
+                                 cudaStream_t s) {
+    if (!a.bscale) return cudaErrorInvalidValue;
+    return launch_gemm<true, true>(w16, xh, xh, a, grid, s);
+}
+
+cudaError_t launch_gather_f16(const float* xb, const int32_t* perm, int S, const int32_t* n_slots, int D, int K,
+                              void* xh, float* scale, cudaStream_t s) {
+    if (S <= 0) return cudaSuccess;
+    const int blocks = (S + 7) / 8 < 148 * 16 ? (S + 7) / 8 : 148 * 16;
+    gather_f16_kernel<<<blocks, 256, 0, s>>>(xb, perm, S, n_slots, D, K, static_cast<__half*>(xh), scale);
+    return cudaGetLastError();
+}
+
+cudaError_t convert_gateup_f16(const void* experts, size_t stride, int D, int H, int E, void* out, unsigned* overflow,
+                               cudaStream_t s) {
+    convert_gateup_f16_kernel<<<148 * 8, 256, 0, s>>>(static_cast<const uint8_t*>(experts), stride, D, H, E,
+                                                       static_cast<__half*>(out), overflow);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const CUtensorMap& hlo, const TcGemmArgs& a,

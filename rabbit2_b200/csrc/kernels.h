@@ -141,6 +141,7 @@ struct TcGemmArgs {
     void* h_lo;
     float* y;                 // [S_cap, D] f32 (down output)
     unsigned* status;         // 0, or the code of a timed-out pipeline wait
+    const float* bscale;      // [S_cap] power-of-two scale of each fp16 activation row (fp16 gate/up only)
 };
 int tc_block_n();
 int tc_pick_bn(int T, int K, int E);
@@ -157,6 +158,14 @@ cudaError_t launch_tc_schedule(const int32_t* counts, const int32_t* offsets, in
                                int32_t* tb_p0, int32_t* tb_p1, int32_t* n_tb, cudaStream_t s);
 cudaError_t launch_tc_gateup(const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
                              const TcGemmArgs& a, int grid, cudaStream_t s);
+// The gate/up GEMM with one fp16 MMA per K step: w16 maps the fp16 copy of w1|w3
+// (convert_gateup_f16), xh the fp16 activation rows (launch_gather_f16).
+cudaError_t launch_tc_gateup_f16(const CUtensorMap& w16, const CUtensorMap& xh, const TcGemmArgs& a, int grid,
+                                 cudaStream_t s);
+cudaError_t launch_gather_f16(const float* xb, const int32_t* perm, int S, const int32_t* n_slots, int D, int K,
+                              void* xh, float* scale, cudaStream_t s);
+cudaError_t convert_gateup_f16(const void* experts, size_t stride, int D, int H, int E, void* out, unsigned* overflow,
+                               cudaStream_t s);
 cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const CUtensorMap& hlo, const TcGemmArgs& a,
                            int grid, cudaStream_t s);
 

@@ -65,12 +65,14 @@ struct Layer {
     bool dec = false;             // w2_cols is valid
     CUtensorMap w2_cols;          // w2 column tiles of the one-token kernel
     void* w2t = nullptr;          // [E][H][D] transposed w2 for the one-token kernel, owned (or null)
+    void* w16 = nullptr;          // [E][2H][D] fp16 copy of w1|w3 for the fp16 gate/up GEMM, owned (or null)
+    CUtensorMap w_gateup16;       // its 3-D map (valid when w16 is set)
 };
 
 struct Workspace {
     int cap = 0;                  // tokens per call the buffers hold
     void* block = nullptr;
-    float *xb, *logits, *wt, *h, *y, *hx, *hout, *partials;
+    float *xb, *logits, *wt, *h, *y, *hx, *hout, *partials, *bscale;
     int32_t *idx, *counts, *offsets, *perm, *slot_pos, *active, *n_active, *hrouting;
     int32_t *tile_cnt, *tile_base, *slot_rank;
     unsigned *tile_counter, *done_counter, *status, *gbar;
@@ -147,6 +149,7 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.hrouting, S * 4},            {(void**)&w.tile_counter, tiles * 4},
         {(void**)&w.done_counter, 4},
         {(void**)&w.partials, rbt::decode_partials_bytes(m->sm_count, (int)D)},
+        {(void**)&w.bscale, (SB > 0 ? SB : 1) * 4},
     };
     size_t total = 0;
     for (auto& p : parts) total = align_up(total, 256) + p.bytes;
@@ -185,6 +188,15 @@ int reserve(RbtMoe* m, int T) {
     return 1;
 }
 
+// RBT_MOE_TC_F16=1 (read when a layer is bound or loaded): the gate/up GEMM runs
+// one fp16 MMA per K step on an fp16 copy of w1|w3 (+2*H*D*2 bytes per expert)
+// with fp16 activations, ~3e-4 relative error on the OLMoE layer, 10-20% faster;
+// by default it keeps the split-bf16 activations (two MMAs per K step, ~1e-5).
+bool tc_f16_enabled() {
+    const char* v = getenv("RBT_MOE_TC_F16");
+    return v && v[0] == '1';
+}
+
 // RBT_MOE_DECODE_W2T=0: no transposed w2 copy (the one-token kernel then reads w2 as column tiles)
 bool decode_w2t_enabled() {
     const char* v = getenv("RBT_MOE_DECODE_W2T");
@@ -196,6 +208,8 @@ bool decode_w2t_enabled() {
 void layer_maps(RbtMoe* m, Layer& L) {
     const RbtMoeConfig& c = m->cfg;
     L.tc = false;
+    if (L.w16) cudaFree(L.w16);
+    L.w16 = nullptr;
     L.dec = m->n_local == c.n_experts && c.dtype == 1 && (c.expert_stride % 16) == 0 &&
             (reinterpret_cast<uintptr_t>(L.experts) % 16) == 0 &&
             (c.expert_hidden % 8) == 0 && c.dim <= 2048 &&
@@ -227,6 +241,27 @@ void layer_maps(RbtMoe* m, Layer& L) {
                                  c.expert_stride) &&
            rbt::make_map_experts(&L.w_down, L.experts + (size_t)2 * c.expert_hidden * c.dim * 2, c.expert_hidden,
                                  c.dim, m->n_local, c.expert_stride);
+    if (L.tc && tc_f16_enabled()) {
+        // fp16 copy of w1|w3; kept only if every value fits fp16
+        const size_t per = (size_t)2 * c.expert_hidden * c.dim * 2;
+        void* p = nullptr;
+        unsigned* flag = nullptr;
+        unsigned over = 1;
+        bool ok = cudaMalloc(&p, per * m->n_local) == cudaSuccess && cudaMalloc(&flag, 4) == cudaSuccess &&
+                  cudaMemset(flag, 0, 4) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+                  rbt::convert_gateup_f16(L.experts, c.expert_stride, c.dim, c.expert_hidden, m->n_local, p, flag,
+                                          m->stream) == cudaSuccess &&
+                  cudaMemcpyAsync(&over, flag, 4, cudaMemcpyDeviceToHost, m->stream) == cudaSuccess &&
+                  cudaStreamSynchronize(m->stream) == cudaSuccess && over == 0 &&
+                  rbt::make_map_experts(&L.w_gateup16, p, c.dim, 2 * c.expert_hidden, m->n_local, per);
+        if (flag) cudaFree(flag);
+        if (ok) {
+            L.w16 = p;
+        } else {  // without it the gate/up GEMM uses the split-bf16 activations
+            (void)cudaGetLastError();
+            if (p) cudaFree(p);
+        }
+    }
 }
 
 int check_layer(RbtMoe* m, int layer, bool need_norm) {
@@ -370,9 +405,14 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     const bool use_tc = tc_ready && (m->path == 2 || (m->path == 0 && T >= m->gemm_min_tokens));
     if (use_tc) {
         const int S = T * c.top_k;
+        const bool f16 = L.w16 != nullptr;
         if (!clk.begin(5)) return 0;
-        CU(rbt::launch_gather_split(xb, w.perm, S, given ? w.offsets + E_run : nullptr, c.dim, c.top_k, w.xhi,
-                                    w.xlo, s));
+        if (f16)  // fp16 rows (in the hi buffer) and their scales
+            CU(rbt::launch_gather_f16(xb, w.perm, S, given ? w.offsets + E_run : nullptr, c.dim, c.top_k, w.xhi,
+                                      w.bscale, s));
+        else
+            CU(rbt::launch_gather_split(xb, w.perm, S, given ? w.offsets + E_run : nullptr, c.dim, c.top_k, w.xhi,
+                                        w.xlo, s));
         const int bn = rbt::tc_pick_bn(T, c.top_k, E_run);
         const int bi = bn == 32 ? 0 : (bn == 64 ? 1 : 2);
         CU(rbt::launch_tc_schedule(w.counts, w.offsets, E_run, bn, w.tb_e, w.tb_p0, w.tb_p1, w.n_tb, s));
@@ -382,8 +422,12 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         ta.tb_e = w.tb_e; ta.tb_p0 = w.tb_p0; ta.tb_p1 = w.tb_p1; ta.n_tb = w.n_tb;
         ta.H = c.expert_hidden; ta.D = c.dim; ta.h_hi = w.hhi; ta.h_lo = w.hlo; ta.y = w.y; ta.status = w.status;
         ta.MB = c.expert_hidden / 128; ta.KB = c.dim / 64;
+        ta.bscale = w.bscale;
         if (!clk.begin(2)) return 0;
-        CU(rbt::launch_tc_gateup(L.w_gateup, w.m_xhi[bi], w.m_xlo[bi], ta, m->sm_count, s));
+        if (f16)
+            CU(rbt::launch_tc_gateup_f16(L.w_gateup16, w.m_xhi[bi], ta, m->sm_count, s));
+        else
+            CU(rbt::launch_tc_gateup(L.w_gateup, w.m_xhi[bi], w.m_xlo[bi], ta, m->sm_count, s));
         ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
         if (!clk.begin(3)) return 0;
         CU(rbt::launch_tc_down(L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
@@ -500,6 +544,7 @@ void rbt_moe_destroy(RbtMoe* m) {
         cudaFree(L.owned);
         cudaFree(L.bias);
         cudaFree(L.w2t);
+        cudaFree(L.w16);
     }
     cudaFree(m->ws.block);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
