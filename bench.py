@@ -263,8 +263,8 @@ class ClockSampler:
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the same
 # workload (natural routing); the profile summary named beside each figure holds the capture.
 MEASURED_TRAFFIC = {
-    ("decode_fused", 1): (102.230784e6 + 5.230080e6, "profiles/decode_fused_olmoe_T1.md"),
-    ("gate_up", 4096): (818.029056e6 + 121.075200e6, "profiles/prefill_tc_olmoe_T4096.md"),
+    ("decode_fused", 1): (101.294080e6 + 3.348480e6, "profiles/decode_fused_olmoe_T1.md"),
+    ("gate_up", 4096): (870.818304e6 + 121.764352e6, "profiles/prefill_tc_olmoe_T4096.md"),
 }
 
 
