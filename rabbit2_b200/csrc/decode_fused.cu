@@ -64,12 +64,14 @@ constexpr int kWrowOff = 24 * 1024;        // this CTA's router rows, bf16
 constexpr int kWrowBytes = 64 * 1024;
 constexpr int kNormOff = 88 * 1024;        // ffn_norm [D] f32
 
-// sync words (a.sync, 32-bit): [0] CTAs past the grid barrier, [1] grid-barrier
-// arrivals, [2..31] unused, then one 64-bit word per expert at the start of its own
-// 128-byte line (every CTA polls every word: separate lines spread the polls over
-// the L2 slices): bit 32 = published, low 32 bits = the logit.  All are zero
-// between launches: the last CTA past the barrier clears [0] and [1], CTA 0 clears
-// the logit words.
+// sync words (a.sync, 32-bit): [0..1] unused, [2..3] the grid barrier's arrival
+// count (64-bit), [4..31] unused, then one 64-bit word per expert at the start of
+// its own 128-byte line (every CTA polls every word: separate lines spread the
+// polls over the L2 slices): bit 32 = published, low 32 bits = the logit.
+// The arrival count only grows: the n-th launch since the words were zeroed waits
+// for n x G arrivals, which each CTA learns from the count its own arrival returns,
+// so nothing has to reset it.  The logit words are zero between launches: CTA 0
+// clears them after the barrier.
 constexpr int kSyncHead = 32;
 constexpr int kLogitStride = 16;  // 64-bit words between two experts' logit words
 
@@ -106,11 +108,6 @@ __device__ __forceinline__ float f2sum(uint64_t v) {
 // bf16 pair (one 32-bit word) -> packed f32 pair
 __device__ __forceinline__ uint64_t bf2(uint32_t w) { return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)); }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -118,10 +115,10 @@ __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long l
 }
 
 // Spin (bounded) until *p >= target.
-__device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
-    if (ld_acquire(p) >= target) return true;
+__device__ __forceinline__ bool wait_count(const unsigned long long* p, unsigned long long target) {
+    if (ld_acquire64(p) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire(p) < target)
+    while (ld_acquire64(p) < target)
         if (globaltimer_ns() - t0 > kWaitNs) return false;
     return true;
 }
@@ -165,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t ring[];
     __shared__ uint64_t full[kSlots], empty[kSlots], rbar, nbar;
     __shared__ int s_cnt[kThreads / 32];
+    __shared__ unsigned long long s_seen;  // ranks given to chosen experts, one bit each
     __shared__ int32_t s_idx[kMaxTopK], s_act[kMaxTopK], s_kpos[kMaxTopK];
     __shared__ float s_p[kMaxTopK], s_wpos[kMaxTopK];
     __shared__ __align__(16) float s_prob[kMaxExperts];
@@ -178,8 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef RBT_DECODE_TIMELINE
     const unsigned tl_par = *(volatile unsigned*)&g_timeline_seq & 1u;
 #endif
-    unsigned* past_cnt = a.sync;
-    unsigned* bar_cnt = a.sync + 1;
+    unsigned long long* bar_cnt = reinterpret_cast<unsigned long long*>(a.sync + 2);
     unsigned long long* lword = reinterpret_cast<unsigned long long*>(a.sync + kSyncHead);
     float* xs = reinterpret_cast<float*>(ring + kXsOff);
     float* prods = reinterpret_cast<float*>(ring + kProdOff);
@@ -197,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (tid == 0) {
         s_fail = 0;
+        s_seen = 0ull;
         for (int s = 0; s < kSlots; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarps);
@@ -221,37 +219,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
     // ---------------------------------------------------------------- phase 0
-    // x straight from L2 (the previous kernel wrote it) into shared memory, squares on the way
+    // x straight from L2 (the previous kernel wrote it) into registers, squares on the
+    // way: thread t holds the float4s t and t + kThreads (D <= 2048 = 2 x 4 x 288 - 256)
+    const int n4 = D / 4;
+    float4 xv[2];
     float ss = 0.0f;
-    for (int i4 = tid; i4 < D / 4; i4 += kThreads) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.x) + i4);
-        reinterpret_cast<float4*>(xs)[i4] = v;
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int i4 = tid + k * kThreads;
+        xv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i4 < n4) {
+            xv[k] = __ldcg(reinterpret_cast<const float4*>(a.x) + i4);
+            ss = fmaf(xv[k].x, xv[k].x, ss);
+            ss = fmaf(xv[k].y, xv[k].y, ss);
+            ss = fmaf(xv[k].z, xv[k].z, ss);
+            ss = fmaf(xv[k].w, xv[k].w, ss);
+        }
     }
-    __syncthreads();
     if (tid == 0) TIMELINE(13);
+    ss = warp_sum(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();  // the warp sums, and the mbarrier initialisation
     if (a.ffn_norm) {  // rmsnorm, the same fixed-order reduction in every CTA
-        ss = warp_sum(ss);
-        if (lane == 0) s_red[warp] = ss;
         if (!mbar_wait_bounded(&nbar, 0, kWaitNs)) {
             record_error(a.status, 0x605);
             s_fail = 1;
         }
-        __syncthreads();
         float tot = 0.0f;
         for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
         const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), a.eps));
-        for (int i = tid; i < D; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), norm_s[i]);
-        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int i4 = tid + k * kThreads;
+            if (i4 < n4) {
+                const float4 nw = reinterpret_cast<const float4*>(norm_s)[i4];
+                xv[k].x = __fmul_rn(__fmul_rn(xv[k].x, inv), nw.x);
+                xv[k].y = __fmul_rn(__fmul_rn(xv[k].y, inv), nw.y);
+                xv[k].z = __fmul_rn(__fmul_rn(xv[k].z, inv), nw.z);
+                xv[k].w = __fmul_rn(__fmul_rn(xv[k].w, inv), nw.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int i4 = tid + k * kThreads;
+        if (i4 < n4) reinterpret_cast<float4*>(xs)[i4] = xv[k];
     }
     TIMELINE(1);
     // ---------------------------------------------------------------- phase 1: exact router logits
-    // The products w[i]*x[i] are independent: every thread rounds its share of
-    // them into `prods`, laid out chain-major (chain c = i mod 4 holds its D/4
-    // products contiguously).  Lane c of warp 0 then runs chain c's D/4
+    // The products w[i]*x[i] are independent: every thread rounds those of its own
+    // float4s of xb into `prods`, laid out chain-major (chain c = i mod 4 holds its
+    // D/4 products contiguously).  Lane c of warp 0 then runs chain c's D/4
     // dependent adds in order, reading 4 products per 16-byte load.
     for (int j = 0; j < n_rows; j++) {
         const int e = e_first + j * e_step;
@@ -263,28 +281,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (tid == 0) TIMELINE(2);
         }
-        __syncthreads();
-        if (s_fail) break;
         const uint16_t* wr = wrow + (size_t)j * D;
         const int q = D / 4, qp = q + kProdPad;
-        for (int i = tid; i < 4 * q; i += kThreads)
-            prods[(i & 3) * qp + (i >> 2)] = __fmul_rn(bf16_bits_to_f32(wr[i]), xs[i]);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int i4 = tid + k * kThreads;
+            if (i4 < n4) {
+                const uint2 w4 = *reinterpret_cast<const uint2*>(wr + 4 * i4);
+                prods[i4] = __fmul_rn(__uint_as_float(w4.x << 16), xv[k].x);
+                prods[qp + i4] = __fmul_rn(__uint_as_float(w4.x & 0xffff0000u), xv[k].y);
+                prods[2 * qp + i4] = __fmul_rn(__uint_as_float(w4.y << 16), xv[k].z);
+                prods[3 * qp + i4] = __fmul_rn(__uint_as_float(w4.y & 0xffff0000u), xv[k].w);
+            }
+        }
         __syncthreads();
+        if (s_fail) break;
         if (tid == 0 && j == 0) TIMELINE(14);
         if (warp == 0) {
             float s = 0.0f;
             if (lane < 4) {
                 // the dependent adds are the critical path (about 4.6 cycles per product)
+                // (unrolled so that the 16-byte loads run well ahead of the adds)
                 const float* pc = prods + lane * qp;
-                int i = 0;
-                for (; i + 4 <= q; i += 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(pc + i);
+                const float4* pc4 = reinterpret_cast<const float4*>(pc);
+                const int q4 = q >> 2;
+#pragma unroll 8
+                for (int i4 = 0; i4 < q4; i4++) {
+                    const float4 v = pc4[i4];
                     s = __fadd_rn(s, v.x);
                     s = __fadd_rn(s, v.y);
                     s = __fadd_rn(s, v.z);
                     s = __fadd_rn(s, v.w);
                 }
-                for (; i < q; i++) s = __fadd_rn(s, pc[i]);
+                for (int i = 4 * q4; i < q; i++) s = __fadd_rn(s, pc[i]);
             }
             const float s1 = __shfl_down_sync(FULL_MASK, s, 1);
             const float a01 = __fadd_rn(s, s1);
@@ -293,12 +322,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j == 0) TIMELINE(15);
                 float logit = __fadd_rn(a01, a23);
                 if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
-                // both copies publish the same bits
+                // both copies publish the same bits (an exchange at L2 measured faster to
+                // reach the pollers than a plain 64-bit store)
                 atomicExch(lword + (size_t)e * kLogitStride, (1ull << 32) | (unsigned long long)__float_as_uint(logit));
             }
         }
         __syncthreads();
     }
+    if (n_rows == 0) __syncthreads();  // xs complete
     // consumer lanes keep their slices of xb (elements 8v..8v+8, v = lane + 32 j) in
     // registers from here on (loaded while the logits propagate); the ring region
     // holding xs is reused after routing
@@ -369,6 +400,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 4 threads per expert (E <= 72; one per expert otherwise), each counting a
     // contiguous quarter of the rivals.  The chosen experts' position in expert
     // order (the unit order) comes from a ballot over the experts' first threads.
+    // A consistent ranking gives ranks 0..K-1 to exactly K experts; a NaN
+    // probability breaks the order (every comparison with it is false), and the
+    // call then fails instead of indexing with an incomplete routing.
     {
         const int split = E <= kThreads / 4 ? 4 : 1;
         const int e = tid / split, part = tid % split;
@@ -397,13 +431,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const bool first = !s_fail && e < E && part == 0;
         const bool chosen = first && r < K;
+        if (chosen) atomicOr(&s_seen, 1ull << r);
         const unsigned m = __ballot_sync(FULL_MASK, chosen);
         if (lane == 0) s_cnt[warp] = __popc(m);
         __syncthreads();
         if (tid == 0) TIMELINE(12);
-        if (first) {
-            int below = __popc(m & lanemask_lt());  // chosen experts with a lower index
-            for (int w = 0; w < warp; w++) below += s_cnt[w];
+        // chosen experts in the warps before this one, and in all warps: a scan of
+        // the per-warp counts across lanes (lane w holds warp w's count)
+        const int cw = lane < kThreads / 32 ? s_cnt[lane] : 0;
+        int incl = cw;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(FULL_MASK, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const int n_chosen = __shfl_sync(FULL_MASK, incl, 31);
+        const int warp_base = __shfl_sync(FULL_MASK, incl - cw, warp);
+        const bool valid = !s_fail && n_chosen == K && s_seen == (K == 64 ? ~0ull : (1ull << K) - 1);
+        if (valid && first) {
+            const int below = warp_base + __popc(m & lanemask_lt());  // chosen experts with a lower index
             if (chosen) {
                 s_idx[r] = e;
                 s_p[r] = pe;
@@ -416,16 +462,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 a.offsets[e] = below;
             }
         }
+        // (a thread that reads the flag set here computes valid = false as well)
+        if (!valid && tid == 0 && !s_fail) {
+            record_error(a.status, 0x603);
+            s_fail = 1;
+        }
     }
     __syncthreads();
-    if (warp == 0 && !s_fail) {
-        if (a.norm_topk) {  // the sequential sum in selection order (rabbit2.c:529-531)
+    if (a.norm_topk) {  // the sequential sum in selection order (rabbit2.c:529-531)
+        if (warp == 0 && !s_fail) {
             float wsum = 0.0f;
             for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
             for (int k = lane; k < K; k += 32) s_wpos[s_kpos[k]] = __fdiv_rn(s_p[k], wsum);
-            __syncwarp();
         }
-        if (b == 0) {  // the routing outputs of the call
+        __syncthreads();
+    }
+    const bool fail0 = s_fail != 0;
+    if (warp == 0 && !fail0) {
+        if (b == 0) {  // the routing outputs of the call (global memory only: no barrier after)
             for (int k = lane; k < K; k += 32) {
                 const int pos = s_kpos[k];
                 a.idx[k] = s_idx[k];
@@ -441,9 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-    __syncthreads();
     if (tid == 0) TIMELINE(4);
-    const bool fail0 = s_fail != 0;
 
     const uint32_t gu_half = (uint32_t)kGURows * D * 2;  // 8 rows of w1 (or w3)
     const int boxr = w2_box_rows(D), nbox = w2_boxes(D);
@@ -606,8 +658,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tid == 0 && !s_fail) {
             // release: this CTA's partial (ordered before by the named barrier) is
             // visible at gpu scope before the arrival is
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar_cnt) : "memory");
-            if (!wait_count(bar_cnt, (unsigned)G)) {
+            // The count before this arrival is n G + m (m arrivals of this launch came
+            // first), so the barrier completes at (n + 1) G; the last arrival needs no poll.
+            unsigned long long before;
+            asm volatile("atom.release.gpu.global.add.u64 %0, [%1], 1;" : "=l"(before) : "l"(bar_cnt) : "memory");
+            const unsigned long long target = (before / (unsigned)G + 1) * (unsigned)G;
+            if (before + 1 < target && !wait_count(bar_cnt, target)) {
                 record_error(a.status, 0x602);
                 s_fail = 1;
             }
@@ -618,14 +674,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // every CTA has read the logits (before it arrived): clear them for the next launch
             if (b == 0)
                 for (int e = tid; e < E; e += kConsumers) lword[(size_t)e * kLogitStride] = 0ull;
-            // the last CTA past the barrier clears the barrier (nobody is waiting on it any more)
-            if (tid == 0 && atomicAdd(past_cnt, 1u) == (unsigned)G - 1) {
-                *bar_cnt = 0u;
-                *past_cnt = 0u;
 #ifdef RBT_DECODE_TIMELINE
-                atomicAdd(&g_timeline_seq, 1u);
+            if (b == 0 && tid == 0) atomicAdd(&g_timeline_seq, 1u);
 #endif
-            }
             // the next layer's router row and ffn_norm into L2 for its first phase
             if (tid == 32 && a.next_router && b < E)
                 prefetch_l2(a.next_router + (size_t)b * D * 2, (uint32_t)D * 2);

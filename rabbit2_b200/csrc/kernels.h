@@ -37,7 +37,13 @@ struct RouterArgs {
     int32_t* tile_base;       // [n_tiles, E] first position of the tile's slots of each expert
     int32_t* slot_rank;       // [T*K] rank of a slot among its tile's slots of the same expert
     int tile_tokens;          // set by launch_router: tokens per tile of the per-tile permutation (0: one tile)
+    const uint16_t* router_cm;  // the router in chain-major order (router_to_chain_major), or nullptr
+    unsigned* status;         // error word (a bounded wait that ran out), or nullptr
 };
+// The token router's copy of a bf16 router [E, D]: chain-major, 16-byte groups
+// (E <= 64, D % 256 == 0; E * D * 2 bytes at `out`).
+bool router_chain_major_supported(int E, int D, int dtype);
+cudaError_t router_to_chain_major(const void* router, int E, int D, void* out, cudaStream_t s);
 // Kernels launched are reported in *launches (1 or 2).
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches);
 // The permutation of given routing (a.idx in [0, a.E) or -1): counts, offsets,

@@ -13,6 +13,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <new>
 #include <vector>
 
@@ -66,6 +67,7 @@ struct Layer {
     CUtensorMap w2_cols;          // w2 column tiles of the one-token kernel
     void* w2t = nullptr;          // [E][H][D] transposed w2 for the one-token kernel, owned (or null)
     void* w16 = nullptr;          // [E][2H][D] fp16 copy of w1|w3 for the fp16 gate/up GEMM, owned (or null)
+    void* router_cm = nullptr;    // [E*D] bf16 chain-major copy of the router for the token router, owned (or null)
     CUtensorMap w_gateup16;       // its 3-D map (valid when w16 is set)
 };
 
@@ -137,7 +139,8 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.tb_p1, ntb * 4},             {(void**)&w.n_tb, 4},
         {(void**)&w.status, 4},
         {(void**)&w.gbar, (size_t)rbt::decode_sync_words((int)E, (int)K) * 4},
-        {(void**)&w.tile_cnt, tiles * E * 4},    {(void**)&w.tile_base, tiles * E * 4},
+        // (the token router keeps one 64-bit expert mask per token in tile_cnt)
+        {(void**)&w.tile_cnt, std::max(tiles * E * 4, (size_t)T * 8)}, {(void**)&w.tile_base, tiles * E * 4},
         {(void**)&w.slot_rank, S * 4},
         {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
         {(void**)&w.wt, S * 4},                  {(void**)&w.h, S * H * 4},
@@ -210,6 +213,24 @@ void layer_maps(RbtMoe* m, Layer& L) {
     L.tc = false;
     if (L.w16) cudaFree(L.w16);
     L.w16 = nullptr;
+    // the token router (2..256 tokens) reads the router in chain-major order: a
+    // copy of E*D*2 bytes (256 KB at OLMoE), made once per binding
+    if (L.router_cm) cudaFree(L.router_cm);
+    L.router_cm = nullptr;
+    if (L.router && rbt::router_chain_major_supported(c.n_experts, c.dim, c.dtype)) {
+        void* p = nullptr;
+        bool ok = cudaMalloc(&p, (size_t)c.n_experts * c.dim * 2) == cudaSuccess;
+        // the router may still be in flight on another stream of the caller
+        ok = ok && cudaDeviceSynchronize() == cudaSuccess &&
+             rbt::router_to_chain_major(L.router, c.n_experts, c.dim, p, m->stream) == cudaSuccess &&
+             cudaStreamSynchronize(m->stream) == cudaSuccess;
+        if (ok) {
+            L.router_cm = p;
+        } else {  // without the copy the other router kernels run
+            (void)cudaGetLastError();
+            if (p) cudaFree(p);
+        }
+    }
     L.dec = m->n_local == c.n_experts && c.dtype == 1 && (c.expert_stride % 16) == 0 &&
             (reinterpret_cast<uintptr_t>(L.experts) % 16) == 0 &&
             (c.expert_hidden % 8) == 0 && c.dim <= 2048 &&
@@ -383,6 +404,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     ra.counts = w.counts; ra.offsets = w.offsets; ra.perm = w.perm; ra.slot_pos = w.slot_pos;
     ra.active = w.active; ra.n_active = w.n_active;
     ra.tile_cnt = w.tile_cnt; ra.tile_base = w.tile_base; ra.slot_rank = w.slot_rank;
+    ra.router_cm = static_cast<const uint16_t*>(L.router_cm); ra.status = w.status;
     if (!clk.begin(1)) return 0;
     int router_launches = 0;
     if (given) {  // the permutation of the given slots over the local experts
@@ -545,6 +567,7 @@ void rbt_moe_destroy(RbtMoe* m) {
         cudaFree(L.bias);
         cudaFree(L.w2t);
         cudaFree(L.w16);
+        cudaFree(L.router_cm);
     }
     cudaFree(m->ws.block);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
@@ -677,6 +700,7 @@ int rbt_moe_route_device(RbtMoe* m, int layer, const float* d_x, int n_tokens, i
     ra.counts = w.counts; ra.offsets = w.offsets; ra.perm = w.perm; ra.slot_pos = w.slot_pos;
     ra.active = w.active; ra.n_active = w.n_active;
     ra.tile_cnt = w.tile_cnt; ra.tile_base = w.tile_base; ra.slot_rank = w.slot_rank;
+    ra.router_cm = static_cast<const uint16_t*>(L.router_cm); ra.status = w.status;
     if (!clk.begin(1)) return 0;
     int launches = 0;
     CU(rbt::launch_router(ra, s, &launches));

@@ -21,9 +21,31 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 namespace rbt {
 namespace {
+
+using namespace tc;
+
+#ifdef RBT_ROUTER_TIMELINE
+// Optional phase timestamps (%globaltimer) of every CTA of the last launch, read
+// back with rbt_router_timeline_read(); built only with -DRBT_ROUTER_TIMELINE.
+__device__ unsigned long long g_rtl[4096][16];
+#define RTL(i)                                                                                \
+    do {                                                                                      \
+        if (threadIdx.x == 0) {                                                               \
+            const unsigned cta_ = blockIdx.y * gridDim.x + blockIdx.x;                        \
+            unsigned long long t_;                                                            \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                            \
+            if (cta_ < 4096) g_rtl[cta_][i] = t_;                                             \
+        }                                                                                     \
+    } while (0)
+#else
+#define RTL(i) \
+    do {       \
+    } while (0)
+#endif
 
 constexpr int kThreads = 256;
 constexpr int kExpertsPerCta = 8;
@@ -268,15 +290,18 @@ __device__ void tile_epilogue(const RouterArgs& a, int t0, int tcount) {
     __syncthreads();
     if (threadIdx.x == 0) s_ticket = atomicAdd(a.tile_counter + blockIdx.x, 1u);
     __syncthreads();
+    RTL(3);
     if (s_ticket != gridDim.y - 1) return;
     __threadfence();
     finish_tokens(a, t0, tcount);
+    RTL(4);
     if (a.tile_tokens > 0 && gridDim.x > 1) {
         __shared__ int32_t s_eidx[kSmallTokens * kMaxTopK];
         __syncthreads();
         for (int i = threadIdx.x; i < tcount * a.K; i += kThreads) s_eidx[i] = a.idx[(size_t)t0 * a.K + i];
         __syncthreads();
         rank_tile_slots(a, s_eidx, tcount * a.K, t0 * a.K, blockIdx.x);
+        RTL(5);
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -284,9 +309,11 @@ __device__ void tile_epilogue(const RouterArgs& a, int t0, int tcount) {
             s_ticket = atomicAdd(a.done_counter, 1u);
         }
         __syncthreads();
+        RTL(6);
         if (s_ticket != gridDim.x - 1) return;
         __threadfence();
         finish_tiles(a, gridDim.x);
+        RTL(7);
         return;
     }
     __threadfence();
@@ -316,12 +343,14 @@ __global__ void __launch_bounds__(kThreads) router_small_kernel(RouterArgs a) {
     const int D = a.D, D4 = D & ~3;
     const WT* W = static_cast<const WT*>(a.router);
     float s = 0.0f;
+    RTL(0);
     for (int c0 = 0; c0 < D; c0 += kSmallChunk) {
         const int cols = min(kSmallChunk, D - c0);
         __syncthreads();
         stage_rows<WT>(ws, kSmallStride, W, D, e0, kExpertsPerCta, a.E, c0, cols);
         stage_rows<float>(xs, kSmallStride, a.xb, D, t0, kSmallTokens, a.T, c0, cols);
         __syncthreads();
+        if (c0 == 0) RTL(1);
         const float* wr = ws + el * kSmallStride;
         const float* xr = xs + tl * kSmallStride;
         const int main_end = min(cols, D4 - c0);  // columns of this chunk in the 4-chain part
@@ -341,6 +370,7 @@ __global__ void __launch_bounds__(kThreads) router_small_kernel(RouterArgs a) {
         if (c == 0)
             for (int i = max(main_end, 0); i < cols; i++) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
     }
+    RTL(2);
     // (s0 + s1) + (s2 + s3) across the four chain lanes
     const float s1 = __shfl_down_sync(FULL_MASK, s, 1);
     const float a01 = __fadd_rn(s, s1);  // lanes c=0: s0+s1, c=2: s2+s3
@@ -660,6 +690,7 @@ __global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
 // Places every routed slot of a tile: position = tile base of its expert + its
 // stable rank within the tile.
 __global__ void __launch_bounds__(kThreads) scatter_kernel(RouterArgs a) {
+    RTL(14);
     const int t0 = blockIdx.x * a.tile_tokens;
     const int nslots = min(a.tile_tokens, a.T - t0) * a.K;
     for (int sl = threadIdx.x; sl < nslots; sl += kThreads) {
@@ -673,6 +704,7 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(RouterArgs a) {
         a.perm[pos] = s;
         a.slot_pos[s] = pos;
     }
+    RTL(15);
 }
 
 // The permutation of routing that comes from outside (expert parallelism): a.idx
@@ -699,6 +731,288 @@ __global__ void __launch_bounds__(kThreads) route_given_kernel(RouterArgs a) {
     finish_tiles(a, gridDim.x);
 }
 
+// ---------------------------------------------------------------------------
+// Token router (bf16, E <= 64, D % 256 == 0, 2 <= T <= 256): one
+// CTA per token holds all E x 4 chains, so softmax and top-k need no other CTA,
+// and the last CTA builds the whole permutation.  Thread 4e + c runs chain c of
+// expert e.  The router is read from a chain-major copy made when the layer is
+// bound (router_to_chain_major): group g of 8 consecutive chain elements of
+// every (e, c) is one 16-byte piece, and all 4E pieces of a group are adjacent,
+//   cm[((g * E + e) * 4 + c) * 8 + u] = W[e][c + 4 (8 g + u)],
+// so a warp reads 512 contiguous bytes per group and a chunk of kTokGroups
+// groups is one contiguous bulk copy.  Chunks stream through a 3-slot ring.
+constexpr int kTokMaxE = 64;
+constexpr int kTokGroups = 8;           // 16-byte groups per chunk: 64 chain elements
+constexpr int kTokBufs = 3;
+constexpr int kTokMaxTokens = 256;
+constexpr uint64_t kTokWaitNs = 2000000000ull;
+
+__host__ __device__ inline size_t tok_chunk_bytes(int E) { return (size_t)kTokGroups * E * 4 * 16; }
+__host__ __device__ inline size_t tok_smem_bytes(int D, int E) {
+    const size_t x = (size_t)4 * (D / 4 + 4) * sizeof(float);
+    const size_t ring = kTokBufs * tok_chunk_bytes(E);
+    // the last CTA's permutation tables: masks, slot k per (token, expert), part counts, offsets
+    const size_t stage = (size_t)kTokMaxTokens * sizeof(uint64_t) + (size_t)kTokMaxTokens * kTokMaxE +
+                         (size_t)(kThreads + kTokMaxE) * sizeof(int);
+    return (ring > stage ? ring : stage) + x;
+}
+
+__global__ void router_cm_kernel(const uint16_t* w, int E, int D, uint16_t* cm) {
+    const size_t n = (size_t)E * D;
+    for (size_t o = (size_t)blockIdx.x * blockDim.x + threadIdx.x; o < n; o += (size_t)gridDim.x * blockDim.x) {
+        const int u = (int)(o & 7), c = (int)((o >> 3) & 3);
+        const size_t ge = o >> 5;  // g * E + e
+        const int e = (int)(ge % E), g = (int)(ge / E);
+        cm[o] = w[(size_t)e * D + c + 4 * (8 * g + u)];
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) router_tok_kernel(RouterArgs a) {
+    extern __shared__ __align__(128) uint8_t tsm[];
+    __shared__ uint64_t full[kTokBufs];
+    __shared__ float s_logit[kTokMaxE];
+    __shared__ __align__(16) float s_prob[kTokMaxE];
+    __shared__ float s_red[kThreads / 32];
+    __shared__ int s_cnt[kThreads / 32];
+    __shared__ int32_t s_idx[kMaxTopK];
+    __shared__ float s_p[kMaxTopK];
+    __shared__ unsigned long long s_seen;
+    __shared__ unsigned s_ticket;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t = blockIdx.x, D = a.D, E = a.E, K = a.K, T = a.T;
+    const int q4 = D / 4, nq = D / (32 * kTokGroups), xs = q4 + 4;
+    const size_t cbytes = tok_chunk_bytes(E), celems = cbytes / 2;
+    uint16_t* ring = reinterpret_cast<uint16_t*>(tsm);
+    float* xcm = reinterpret_cast<float*>(tsm + (tok_smem_bytes(D, E) - (size_t)4 * xs * sizeof(float)));
+    const uint16_t* cm = a.router_cm;
+    int n_issued = 0;  // copies issued (thread 0)
+    RTL(0);
+    if (tid == 0) {
+        s_seen = 0ull;
+        for (int b = 0; b < kTokBufs; b++) mbar_init(&full[b], 1);
+        fence_mbar_init();
+        for (int q = 0; q < nq && q < kTokBufs; q++) {
+            mbar_arrive_expect_tx(&full[q], (uint32_t)cbytes);
+            bulk_load(ring + (size_t)q * celems, cm + (size_t)q * celems, (uint32_t)cbytes, &full[q]);
+            n_issued++;
+        }
+    }
+    // this token's xb, chain-major: xcm[c][j] = xb[t][c + 4 j] (rows 4 banks apart)
+    for (int i4 = tid; i4 < q4; i4 += kThreads) {
+        const float4 v = reinterpret_cast<const float4*>(a.xb + (size_t)t * D)[i4];
+        xcm[i4] = v.x;
+        xcm[xs + i4] = v.y;
+        xcm[2 * xs + i4] = v.z;
+        xcm[3 * xs + i4] = v.w;
+    }
+    for (int k = tid; k < K; k += kThreads) a.slot_pos[(size_t)t * K + k] = -1;  // until placed
+    __syncthreads();  // x staged, barriers initialised
+    RTL(1);
+    const int e = tid >> 2, c = tid & 3;
+    const bool chain = e < E;
+    float s = 0.0f;
+    bool ok = true;
+    for (int q = 0; q < nq; q++) {
+        const int b = q % kTokBufs;
+        ok = ok && mbar_wait_bounded(&full[b], (uint32_t)(q / kTokBufs) & 1u, kTokWaitNs);
+        if (ok && chain) {
+            const uint4* wq = reinterpret_cast<const uint4*>(ring + (size_t)b * celems) + tid;
+            const float* xq = xcm + c * xs + q * (8 * kTokGroups);
+#pragma unroll
+            for (int g = 0; g < kTokGroups; g++) {
+                const uint4 w = wq[g * 4 * E];
+                const float4 x0 = *reinterpret_cast<const float4*>(xq + 8 * g);
+                const float4 x1 = *reinterpret_cast<const float4*>(xq + 8 * g + 4);
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.x << 16), x0.x));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.x & 0xffff0000u), x0.y));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.y << 16), x0.z));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.y & 0xffff0000u), x0.w));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.z << 16), x1.x));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.z & 0xffff0000u), x1.y));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.w << 16), x1.z));
+                s = __fadd_rn(s, __fmul_rn(__uint_as_float(w.w & 0xffff0000u), x1.w));
+            }
+        }
+        __syncthreads();  // slot b is free again
+        if (tid == 0 && ok && q + kTokBufs < nq) {
+            mbar_arrive_expect_tx(&full[b], (uint32_t)cbytes);
+            bulk_load(ring + (size_t)b * celems, cm + (size_t)(q + kTokBufs) * celems, (uint32_t)cbytes, &full[b]);
+            n_issued++;
+        }
+    }
+    if (tid == 0 && !ok) {
+        // a wait ran out: wait (bounded) for the copies still in flight (the latest
+        // phase of each slot) before this CTA's shared memory can be given up
+        for (int q = n_issued - kTokBufs < 0 ? 0 : n_issued - kTokBufs; q < n_issued; q++)
+            (void)mbar_wait_bounded(&full[q % kTokBufs], (uint32_t)(q / kTokBufs) & 1u, kTokWaitNs);
+    }
+    RTL(2);
+    // (s0 + s1) + (s2 + s3) across the four chain lanes of an expert
+    const float s1 = __shfl_down_sync(FULL_MASK, s, 1);
+    const float a01 = __fadd_rn(s, s1);
+    const float a23 = __shfl_down_sync(FULL_MASK, a01, 2);
+    if (chain && c == 0) {
+        float logit = __fadd_rn(a01, a23);
+        if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
+        s_logit[e] = logit;
+    }
+    if (!ok && tid == 0 && a.status) atomicCAS(a.status, 0u, 0x640u);
+    __syncthreads();
+    // softmax (rabbit2.c:399-405): thread e < E owns expert e
+    const float lg = tid < E ? s_logit[tid] : -INFINITY;
+    float mx = lg;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = s_red[0];
+    for (int w = 1; w < (E + 31) / 32; w++) mx = fmaxf(mx, s_red[w]);
+    // exp in double, rounded once (correctly rounded expf)
+    const float pe = tid < E ? (float)exp((double)__fsub_rn(lg, mx)) : 0.0f;
+    if (tid < E) s_prob[tid] = pe;
+    __syncthreads();
+    if (tid == 0) {  // the sequential sum in expert order (rabbit2.c:403)
+        float sum = 0.0f;
+        int f = 0;
+        for (; f + 4 <= E; f += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(s_prob + f);
+            sum = __fadd_rn(sum, v.x);
+            sum = __fadd_rn(sum, v.y);
+            sum = __fadd_rn(sum, v.z);
+            sum = __fadd_rn(sum, v.w);
+        }
+        for (; f < E; f++) sum = __fadd_rn(sum, s_prob[f]);
+        s_red[0] = sum;
+    }
+    __syncthreads();
+    if (tid < E) {
+        s_prob[tid] = __fdiv_rn(pe, s_red[0]);
+        a.logits[(size_t)t * E + tid] = lg;
+    }
+    __syncthreads();
+    RTL(3);
+    // top-k by rank (rabbit2.c:519-528): expert e is chosen in round r when exactly r
+    // experts beat it (higher probability, or equal and lower index); 4 threads per
+    // expert, each counting a quarter of the rivals
+    {
+        const int re = tid >> 2, part = tid & 3;
+        int r = 0;
+        float pr = 0.0f;
+        if (re < E) {
+            pr = s_prob[re];
+            const int f0 = part * E / 4, f1 = (part + 1) * E / 4;
+            for (int f = f0; f < f1; f++) {
+                const float pf = s_prob[f];
+                r += (pf > pr) || (pf == pr && f < re);
+            }
+        }
+        r += __shfl_xor_sync(FULL_MASK, r, 1);
+        r += __shfl_xor_sync(FULL_MASK, r, 2);
+        const bool chosen = re < E && part == 0 && r < K;
+        if (chosen) atomicOr(&s_seen, 1ull << r);
+        const unsigned m = __ballot_sync(FULL_MASK, chosen);
+        if (lane == 0) s_cnt[warp] = __popc(m);
+        __syncthreads();
+        int n_chosen = 0;
+        for (int w = 0; w < kThreads / 32; w++) n_chosen += s_cnt[w];
+        // A consistent ranking gives ranks 0..K-1 to exactly K experts.  A NaN
+        // probability breaks the order (every comparison with it is false); the token
+        // then takes experts 0..K-1 (its output is NaN, as the reference's would be).
+        const bool valid = n_chosen == K && s_seen == (K == 64 ? ~0ull : (1ull << K) - 1);
+        if (valid && chosen) {
+            s_idx[r] = re;
+            s_p[r] = pr;
+        }
+        if (!valid)
+            for (int k = tid; k < K; k += kThreads) {
+                s_idx[k] = k;
+                s_p[k] = s_prob[k];
+            }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float wsum = 0.0f;
+        if (a.norm_topk)  // the sequential sum in selection order (rabbit2.c:529-531)
+            for (int k = 0; k < K; k++) wsum = __fadd_rn(wsum, s_p[k]);
+        unsigned long long mask = 0ull;
+        for (int k = lane; k < K; k += 32) {
+            const int ek = s_idx[k];
+            a.idx[(size_t)t * K + k] = ek;
+            a.wt[(size_t)t * K + k] = a.norm_topk ? __fdiv_rn(s_p[k], wsum) : s_p[k];
+            if (a.routing_out) a.routing_out[(size_t)t * a.routing_stride + k] = ek;
+            mask |= 1ull << ek;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mask |= __shfl_xor_sync(FULL_MASK, mask, o);
+        if (lane == 0) reinterpret_cast<unsigned long long*>(a.tile_cnt)[t] = mask;
+    }
+    // the last CTA to finish builds the permutation of all T*K slots
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_ticket = atomicAdd(a.done_counter, 1u);
+    __syncthreads();
+    RTL(4);
+    if (s_ticket != (unsigned)T - 1) return;
+    __threadfence();
+    // (the ring is free now) every token's mask and each (token, expert)'s slot k
+    unsigned long long* smask = reinterpret_cast<unsigned long long*>(tsm);               // [T]
+    uint8_t* kpos = tsm + (size_t)kTokMaxTokens * sizeof(unsigned long long);             // [T][E]
+    int* s_part = reinterpret_cast<int*>(kpos + (size_t)kTokMaxTokens * kTokMaxE);        // [P][E]
+    int* s_off = s_part + kThreads;                                                       // [E]
+    for (int i = tid; i < T; i += kThreads) smask[i] = __ldcg(reinterpret_cast<const unsigned long long*>(a.tile_cnt) + i);
+    for (int sl = tid; sl < T * K; sl += kThreads) {
+        const int ek = __ldcg(a.idx + sl);
+        if (ek >= 0 && ek < E) kpos[(sl / K) * E + ek] = (uint8_t)(sl % K);
+    }
+    __syncthreads();
+    // thread (xe, part): the tokens of its contiguous part routed to expert xe
+    const int P = kThreads / E, xe = tid % E, part = tid / E;
+    const bool mine = part < P;
+    const int u0 = (int)((long)T * part / P), u1 = (int)((long)T * (part + 1) / P);
+    int pc = 0;
+    if (mine)
+        for (int i = u0; i < u1; i++) pc += (int)((smask[i] >> xe) & 1ull);
+    if (mine) s_part[part * E + xe] = pc;
+    __syncthreads();
+    int cnt = 0;
+    if (tid < E)
+        for (int p = 0; p < P; p++) cnt += s_part[p * E + tid];
+    int total = 0;
+    const int off = block_exclusive_scan(cnt, &total);
+    int n_act = 0;
+    const int apos = block_exclusive_scan(cnt > 0 ? 1 : 0, &n_act);
+    if (tid < E) {
+        a.counts[tid] = cnt;
+        a.offsets[tid] = off;
+        if (cnt > 0) a.active[apos] = tid;
+        s_off[tid] = off;
+    }
+    if (tid == 0) {
+        a.offsets[E] = total;
+        *a.n_active = n_act;
+        *a.done_counter = 0;
+    }
+    __syncthreads();
+    // the expert's slots in token order (stable, as the reference's per-token loop)
+    if (mine) {
+        int pos = s_off[xe];
+        for (int p = 0; p < part; p++) pos += s_part[p * E + xe];
+        for (int i = u0; i < u1; i++)
+            if ((smask[i] >> xe) & 1ull) {
+                const int sl = i * K + kpos[i * E + xe];
+                a.perm[pos] = sl;
+                a.slot_pos[sl] = pos;
+                pos++;
+            }
+    }
+    RTL(5);
+}
+
+bool tok_ok(const RouterArgs& a) {
+    return a.router_cm && a.dtype == 1 && a.E <= kTokMaxE && a.D % 256 == 0 && a.T >= 2 && a.T <= kTokMaxTokens &&
+           a.K <= kMaxTopK && a.tile_cnt && a.done_counter;
+}
+
 bool wide_ok(const RouterArgs& a) {
     const size_t esz = a.dtype == 1 ? 2 : 4;
     return a.E <= kWideExperts && a.D % 4 == 0 && a.K * kWideTokens <= kWideTokens * kMaxTopK &&
@@ -721,6 +1035,14 @@ cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s, int* launches) {
         const char* v = getenv("RBT_ROUTER_MID_TOKENS");  // tuning: the thread-per-chain kernel up to this T
         return v ? atoi(v) : kMidTokens;
     }();
+    static const bool tok_on = [] {
+        const char* v = getenv("RBT_ROUTER_TOK");  // RBT_ROUTER_TOK=0: without the token router
+        return !(v && v[0] == '0');
+    }();
+    if (tok_on && tok_ok(a) && a.T <= mid_tokens) {
+        // one CTA per token; softmax, top-k and the permutation in the same launch
+        return launch_with_smem(router_tok_kernel, dim3(a.T), tok_smem_bytes(a.D, a.E), a, s);
+    }
     if (a.T <= kSmallTokens || a.T <= mid_tokens) {
         // thread per chain: token tiles of 8 x expert groups of 8 (latency, not
         // issue rate, bounds a few hundred tokens)
@@ -784,4 +1106,26 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches) {
     return a.dtype == 1 ? launch_typed<uint16_t>(a, s, launches) : launch_typed<float>(a, s, launches);
 }
 
+bool router_chain_major_supported(int E, int D, int dtype) {
+    return dtype == 1 && E > 0 && E <= kTokMaxE && D > 0 && D % 256 == 0;
+}
+
+cudaError_t router_to_chain_major(const void* router, int E, int D, void* out, cudaStream_t s) {
+    if (!router_chain_major_supported(E, D, 1)) return cudaErrorInvalidValue;
+    const size_t n = (size_t)E * D;
+    const int grid = (int)((n + 255) / 256 < 2048 ? (n + 255) / 256 : 2048);
+    router_cm_kernel<<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(router), E, D, static_cast<uint16_t*>(out));
+    return cudaGetLastError();
+}
+
 }  // namespace rbt
+
+#ifdef RBT_ROUTER_TIMELINE
+extern "C" int rbt_router_timeline_read(void* host) {
+    return cudaMemcpyFromSymbol(host, rbt::g_rtl, sizeof(rbt::g_rtl)) == cudaSuccess;
+}
+extern "C" int rbt_router_timeline_clear(void) {
+    static unsigned long long zeros[4096 * 16];
+    return cudaMemcpyToSymbol(rbt::g_rtl, zeros, sizeof(zeros)) == cudaSuccess;
+}
+#endif
