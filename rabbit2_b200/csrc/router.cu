@@ -533,9 +533,10 @@ __device__ void rank_tile_slots(const RouterArgs& a, const int32_t* s_eidx, int 
 __device__ void finish_tiles(const RouterArgs& a, int ntiles) {
     const int tid = threadIdx.x, E = a.E;
     // thread (pe, part) owns the contiguous tile range [part*n/P, (part+1)*n/P) of
-    // expert pe (P = 256 / E parts, 1 to 4); the per-tile counts are read 16 loads
+    // expert pe (P = 256 / E parts, 1 to 4); the per-tile counts are read 32 loads
     // at a time, since L2 latency (not bandwidth) is the cost of this single-CTA step
     constexpr int kMaxParts = 4;
+    constexpr int kFinLd = 32;
     __shared__ int s_part[kMaxParts][kMaxExperts];
     __shared__ int s_off[kMaxExperts];
     const int P = max(1, min(kMaxParts, kThreads / E));
@@ -544,12 +545,12 @@ __device__ void finish_tiles(const RouterArgs& a, int ntiles) {
     const int tb0 = (int)((long)part * ntiles / P), tb1 = (int)((long)(part + 1) * ntiles / P);
     int psum = 0;
     if (mine)
-        for (int t = tb0; t < tb1; t += 16) {
-            int c[16];
+        for (int t = tb0; t < tb1; t += kFinLd) {
+            int c[kFinLd];
 #pragma unroll
-            for (int k = 0; k < 16; k++) c[k] = t + k < tb1 ? __ldcg(a.tile_cnt + (size_t)(t + k) * E + pe) : 0;
+            for (int k = 0; k < kFinLd; k++) c[k] = t + k < tb1 ? __ldcg(a.tile_cnt + (size_t)(t + k) * E + pe) : 0;
 #pragma unroll
-            for (int k = 0; k < 16; k++) psum += c[k];
+            for (int k = 0; k < kFinLd; k++) psum += c[k];
         }
     if (mine) s_part[part][pe] = psum;
     __syncthreads();
@@ -561,12 +562,12 @@ __device__ void finish_tiles(const RouterArgs& a, int ntiles) {
     if (mine) {
         int run = s_off[pe];
         for (int p = 0; p < part; p++) run += s_part[p][pe];
-        for (int t = tb0; t < tb1; t += 16) {
-            int c[16];
+        for (int t = tb0; t < tb1; t += kFinLd) {
+            int c[kFinLd];
 #pragma unroll
-            for (int k = 0; k < 16; k++) c[k] = t + k < tb1 ? __ldcg(a.tile_cnt + (size_t)(t + k) * E + pe) : 0;
+            for (int k = 0; k < kFinLd; k++) c[k] = t + k < tb1 ? __ldcg(a.tile_cnt + (size_t)(t + k) * E + pe) : 0;
 #pragma unroll
-            for (int k = 0; k < 16; k++)
+            for (int k = 0; k < kFinLd; k++)
                 if (t + k < tb1) {
                     a.tile_base[(size_t)(t + k) * E + pe] = run;
                     run += c[k];
@@ -960,9 +961,19 @@ __global__ void __launch_bounds__(kThreads) router_tok_kernel(RouterArgs a) {
     int* s_part = reinterpret_cast<int*>(kpos + (size_t)kTokMaxTokens * kTokMaxE);        // [P][E]
     int* s_off = s_part + kThreads;                                                       // [E]
     for (int i = tid; i < T; i += kThreads) smask[i] = __ldcg(reinterpret_cast<const unsigned long long*>(a.tile_cnt) + i);
-    for (int sl = tid; sl < T * K; sl += kThreads) {
-        const int ek = __ldcg(a.idx + sl);
-        if (ek >= 0 && ek < E) kpos[(sl / K) * E + ek] = (uint8_t)(sl % K);
+    // (loads of 8 slots in flight at a time: one L2 round trip per 8, not per slot)
+    for (int sl0 = 0; sl0 < T * K; sl0 += 8 * kThreads) {
+        int ek[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int sl = sl0 + u * kThreads + tid;
+            ek[u] = sl < T * K ? __ldcg(a.idx + sl) : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int sl = sl0 + u * kThreads + tid;
+            if (ek[u] >= 0 && ek[u] < E) kpos[(sl / K) * E + ek[u]] = (uint8_t)(sl % K);
+        }
     }
     __syncthreads();
     // thread (xe, part): the tokens of its contiguous part routed to expert xe
