@@ -299,6 +299,32 @@ def test_tensor_core_path_small_shape_zipf(orc):
         ctx.close()
 
 
+@pytest.mark.parametrize("T", [2, 37, 129, 256])
+def test_token_router_second_shape(orc, T):
+    """The token router (bf16, E <= 64, D % 256 == 0, 2..256 tokens: one CTA per token,
+    permutation by the last CTA) away from the OLMoE shape: 48 experts (not a multiple of
+    32), top-6, a skewed router; routing bit-exact, the permutation consistent with it
+    (per-expert counts), outputs at the tensor-core bar."""
+    D, H, E, K = 512, 256, 48, 6
+    router, experts, stride = workload.device_layer(D, H, E, seed=31)
+    bias = workload.zipf_bias(E, 1.2, seed=3)
+    ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_BF16, 0, stride)
+    try:
+        ctx.bind_layer(0, router, experts)
+        ctx.set_router_bias(0, bias)
+        r_h, e_h = workload.host_copy(router, experts)
+        host = MoeLayerHost(D, H, E, K, moe.DT_BF16, 0, r_h, e_h, stride, router_bias=bias)
+        x = workload.inputs(T, D, seed=300 + T)
+        got, got_r = ctx.ffn(0, x.cpu().numpy())
+        want, want_r, _ = orc.moe_ffn(host, x.cpu().numpy(), nthreads=8)
+        _, _, probs = orc.router_topk(host, x.cpu().numpy())
+        assert_routing(got_r, want_r, probs)
+        np.testing.assert_array_equal(ctx.expert_histogram(), np.bincount(got_r.ravel(), minlength=E))
+        assert rel_err(got, want) < MOE_RTOL_TC
+    finally:
+        ctx.close()
+
+
 def test_tensor_core_path_rejects_f32_weights():
     D, H, E, K = 256, 512, 8, 2
     from rabbit2_b200.rbt2fmt import ModelConfig, expert_stride
