@@ -433,6 +433,41 @@ def test_fused_decode_shapes(orc, D, H, E, K, norm):
         ctx.close()
 
 
+def test_fused_decode_logit_order_differs_from_probability_order(orc):
+    """The one-token kernel ranks the rounded probabilities, as the reference does
+    (rabbit2.c:516-528), not the logits.  Here the two orders differ: experts 3 and
+    4 have logits 1.0 and the next float above it, which round to the same
+    logit - max (-4.0) and so to the same probability; the probabilities choose
+    expert 3 (lower index on a tie), the logits would choose expert 4.  The
+    kernel's routing and output equal the oracle's."""
+    D, H, E, K = 256, 64, 16, 4
+    _, experts, stride = workload.device_layer(D, H, E, seed=77)
+    router = torch.zeros(E, D, dtype=torch.bfloat16, device="cuda")  # logits = bias exactly
+    bias = np.full(E, -5.0, np.float32)
+    bias[:3] = 5.0
+    bias[3] = 1.0
+    bias[4] = np.nextafter(np.float32(1.0), np.float32(2.0))
+    ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_BF16, 0, stride)
+    try:
+        ctx.bind_layer(0, router, experts)
+        ctx.set_router_bias(0, bias)
+        r_h, e_h = workload.host_copy(router, experts)
+        host = MoeLayerHost(D, H, E, K, moe.DT_BF16, 0, r_h, e_h, stride, router_bias=bias)
+        x = workload.inputs(1, D, seed=3)
+        out = torch.empty_like(x)
+        routing = torch.empty(1, K, dtype=torch.int32, device="cuda")
+        ctx.set_path(moe.PATH_DECODE_FUSED)
+        ctx.ffn_device(0, x, out, routing)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(routing.cpu().numpy(), [[0, 1, 2, 3]])
+        want, want_r, _ = orc.moe_ffn(host, x.cpu().numpy())
+        np.testing.assert_array_equal(want_r, [[0, 1, 2, 3]])
+        assert rel_err(out.cpu().numpy(), want) < MOE_RTOL
+        ctx.ffn(0, x.cpu().numpy())  # the host call checks the kernel's status word
+    finally:
+        ctx.close()
+
+
 def test_decode_layers_in_a_cuda_graph(orc):
     """Three layers of the block form captured in one CUDA graph and replayed."""
     L = 3
