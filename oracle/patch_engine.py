@@ -3,16 +3,17 @@
     python oracle/patch_engine.py <rabbit2.c> <out.c>
 
 Writes a copy of the reference engine source (rabbit2/src/rabbit2.c) into
-oracle/_ref/ with the four insertions INTEGRATION.md documents -- the include of
-rabbit2_b200/engine/rbt_engine_hook.h and its three call sites -- and nothing
-else changed.  oracle/Makefile compiles it against librbt_moe.so into
-oracle/_ref/rabbit2_cuda.  Each insertion is anchored on one reference line and
+oracle/_ref/ with the edits INTEGRATION.md documents -- the include of
+rabbit2_b200/engine/rbt_engine_hook.h, its two CLI flags, its init call, the
+MoE-block call and the batched prompt before the prompt loop -- and nothing else
+changed.  oracle/Makefile compiles it against librbt_moe.so into
+oracle/_ref/rabbit2_cuda.  Each edit is anchored on one reference line and
 fails loudly if that line is missing or not unique.
 """
 import sys
 
 INSERTIONS = [
-    # (anchor line, where, text)
+    # (anchor line, where: before / after / replace, text)
     ("static int forward(Model *m, State *s, int token, int pos, int32_t *routing_out) {", "before",
      '#include "rbt_engine_hook.h"\n\n'),
     ("        /* ---- MoE feed-forward ---- */", "after",
@@ -22,9 +23,18 @@ INSERTIONS = [
      "            if (g_) continue;\n"
      "        }\n"),
     ('        else if (!strcmp(argv[i], "--kernel") && i + 1 < argc) kernel = argv[++i];', "before",
-     '        else if (!strcmp(argv[i], "--device") && i + 1 < argc) rbt_engine_device = argv[++i];\n'),
+     '        else if (!strcmp(argv[i], "--device") && i + 1 < argc) rbt_engine_device = argv[++i];\n'
+     '        else if (!strcmp(argv[i], "--prefill") && i + 1 < argc) rbt_engine_prefill_mode = argv[++i];\n'),
     ("    if (!load_model(&m, argv[1])) return 1;", "after",
      "    if (!rbt_engine_init(&m)) return 1;\n"),
+    ("    double t0 = now_sec();", "after",
+     "    const int rbt_pre_ = rbt_engine_prefill(&m, &s, tokens, nt, routing, fl, fr);\n"
+     "    if (rbt_pre_ < 0) {\n"
+     "        if (fl) { fclose(fl); fclose(fr); }\n"
+     "        return 1;\n"
+     "    }\n"),
+    ("    for (int i = 0; i < nt; i++) {", "replace",
+     "    for (int i = rbt_pre_ ? nt : 0; i < nt; i++) {\n"),
 ]
 
 
@@ -35,7 +45,10 @@ def patch(src: str) -> str:
         if len(hits) != 1:
             raise SystemExit(f"anchor found {len(hits)} times: {anchor!r}")
         i = hits[0]
-        lines.insert(i if where == "before" else i + 1, text)
+        if where == "replace":
+            lines[i] = text
+        else:
+            lines.insert(i if where == "before" else i + 1, text)
     return "".join(lines)
 
 

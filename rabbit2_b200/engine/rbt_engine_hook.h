@@ -3,12 +3,18 @@
  * blocks on the GPU through librbt_moe.so (include/rbt_moe.h).
  *
  * Included by rabbit2.c right before forward() (it uses the engine's Model,
- * LayerOff, VEC and MAT from rabbit2.c:63-103,230-231).  Three call sites:
+ * State, LayerOff, VEC, MAT and its rmsnorm / matvec / rope / softmax, all
+ * defined above forward()).  Call sites:
  *   main(), argument loop:  --device cpu|cuda   sets rbt_engine_device
+ *                           --prefill batch|token   sets rbt_engine_prefill_mode
  *   main(), after load_model():  rbt_engine_init(&m)
  *   forward(), first line of the MoE block (rabbit2.c:511):
  *       { int g = rbt_engine_moe(m, l, s->x, routing_out + (size_t)l * c->top_k);
  *         if (g < 0) return 0; if (g) continue; }
+ *   main(), before the prompt loop (rabbit2.c:703-704):
+ *       const int pre = rbt_engine_prefill(&m, &s, tokens, nt, routing, fl, fr);
+ *       (on -1: close the dump files, return 1), and the loop starts at
+ *       i = pre ? nt : 0.
  * With --device cpu (the default) nothing changes: the engine's own CPU block runs.
  * With --device cuda every layer's router and expert blobs are copied once from
  * the mapped file into HBM, and each MoE block is one rbt_moe_block() call that
@@ -20,9 +26,15 @@
 #include "rbt_moe.h"
 
 static const char *rbt_engine_device = NULL;
+static const char *rbt_engine_prefill_mode = NULL;  /* --prefill batch|token */
 static RbtMoe *rbt_engine_ctx = NULL;
 
 static int rbt_engine_init(Model *m) {
+    if (rbt_engine_prefill_mode && strcmp(rbt_engine_prefill_mode, "batch") != 0 &&
+        strcmp(rbt_engine_prefill_mode, "token") != 0) {
+        fprintf(stderr, "--prefill must be batch or token\n");
+        return 0;
+    }
     if (!rbt_engine_device || !strcmp(rbt_engine_device, "cpu")) return 1;
     if (strcmp(rbt_engine_device, "cuda") != 0) {
         fprintf(stderr, "--device must be cpu or cuda\n");
@@ -54,6 +66,110 @@ static int rbt_engine_init(Model *m) {
 static int rbt_engine_moe(Model *m, int layer, float *x, int32_t *routing_row) {
     if (!rbt_engine_ctx) return 0;
     return rbt_moe_block(rbt_engine_ctx, layer, x, 1, routing_row, m->c.top_k) ? 1 : -1;
+}
+
+/* ---- the prompt as one batch per layer ----
+ * The engine's prompt loop runs forward() token by token, so each MoE block sees
+ * one token.  With --device cuda the prompt instead runs layer by layer: every
+ * prompt token's attention half of layer l (on the CPU, as the engine computes it),
+ * then ONE rbt_moe_block call for all of them, which the library runs on the
+ * tensor cores.  Attention of token t at layer l reads the KV cache of positions
+ * <= t of layer l only, which tokens 0..t have written by then, so the order
+ * changes no value.  --prefill token keeps the engine's per-token loop. */
+
+/* Layer l's attention half for the token at position pos; x [dim] is updated in
+ * place.  These are the engine's own calls on the same values in the same order
+ * as forward() makes them for one token (rabbit2.c:472-509), so the results are
+ * the same bits. */
+static void rbt_engine_attention(Model *m, State *s, int l, float *x, int pos) {
+    const Config *c = &m->c;
+    const LayerOff *ly = &m->layers[l];
+    const int D = c->dim, hd = c->head_dim;
+    const int nq = c->n_heads * hd, nkv = c->n_kv_heads * hd, heads_per_kv = c->n_heads / c->n_kv_heads;
+    rmsnorm(s->xb, x, VEC(m, ly->attn_norm), D, c->rms_eps);
+    matvec(s->q, MAT(m, ly->wq), c->dtype, s->xb, nq, D);
+    matvec(s->k, MAT(m, ly->wk), c->dtype, s->xb, nkv, D);
+    matvec(s->v, MAT(m, ly->wv), c->dtype, s->xb, nkv, D);
+    if (c->qk_norm) {
+        rmsnorm(s->q, s->q, VEC(m, ly->q_norm), nq, c->rms_eps);
+        rmsnorm(s->k, s->k, VEC(m, ly->k_norm), nkv, c->rms_eps);
+    }
+    rope(s->q, c->n_heads, hd, pos, c->rope_theta);
+    rope(s->k, c->n_kv_heads, hd, pos, c->rope_theta);
+    float *keys = s->kcache + (size_t)l * s->ctx * nkv, *vals = s->vcache + (size_t)l * s->ctx * nkv;
+    memcpy(keys + (size_t)pos * nkv, s->k, (size_t)nkv * sizeof(float));
+    memcpy(vals + (size_t)pos * nkv, s->v, (size_t)nkv * sizeof(float));
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int h = 0; h < c->n_heads; h++) {
+        const float *q = s->q + (size_t)h * hd;
+        const size_t kv_col = (size_t)(h / heads_per_kv) * hd;
+        for (int t = 0; t <= pos; t++) {
+            const float *kt = keys + (size_t)t * nkv + kv_col;
+            float d = 0.0f;
+            for (int i = 0; i < hd; i++) d += q[i] * kt[i];
+            s->att[t] = d * scale;
+        }
+        softmax(s->att, pos + 1);
+        float *o = s->attn_out + (size_t)h * hd;
+        for (int i = 0; i < hd; i++) o[i] = 0.0f;
+        for (int t = 0; t <= pos; t++) {
+            const float *vt = vals + (size_t)t * nkv + kv_col;
+            const float w = s->att[t];
+            for (int i = 0; i < hd; i++) o[i] += w * vt[i];
+        }
+    }
+    matvec(s->xb, MAT(m, ly->wo), c->dtype, s->attn_out, D, nq);
+    for (int i = 0; i < D; i++) x[i] += s->xb[i];
+}
+
+/* The prompt tokens[0..nt) at positions 0..nt: 1 when it ran here (the last
+ * token's logits in s->logits and its routing rows in `routing`, as the engine's
+ * loop leaves them; with --dump every token's logits and routing rows written to
+ * fl / fr in the engine's format), 0 when not enabled (the engine's loop runs),
+ * -1 on an error (message on stderr). */
+static int rbt_engine_prefill(Model *m, State *s, const int *tokens, int nt, int32_t *routing, FILE *fl,
+                              FILE *fr) {
+    if (!rbt_engine_ctx || nt < 2 || (rbt_engine_prefill_mode && !strcmp(rbt_engine_prefill_mode, "token")))
+        return 0;
+    const Config *c = &m->c;
+    const int D = c->dim;
+    const size_t row = (size_t)c->n_layers * c->top_k;  /* routing ints per token */
+    float *X = (float *)malloc((size_t)nt * D * sizeof(float));
+    int32_t *R = (int32_t *)malloc((size_t)nt * row * sizeof(int32_t));
+    if (!X || !R) {
+        free(X);
+        free(R);
+        fprintf(stderr, "out of memory for the batched prompt (try --prefill token)\n");
+        return -1;
+    }
+    for (int t = 0; t < nt; t++) {  /* embedding rows, converted as forward() does */
+        float *x = X + (size_t)t * D;
+        if (c->dtype == DT_F32) {
+            memcpy(x, (const float *)MAT(m, m->tok_emb) + (size_t)tokens[t] * D, (size_t)D * sizeof(float));
+        } else {
+            const uint16_t *e = (const uint16_t *)MAT(m, m->tok_emb) + (size_t)tokens[t] * D;
+            for (int i = 0; i < D; i++) x[i] = bf16f(e[i]);
+        }
+    }
+    int ok = 1;
+    for (int l = 0; ok && l < c->n_layers; l++) {
+        for (int t = 0; t < nt; t++) rbt_engine_attention(m, s, l, X + (size_t)t * D, t);
+        ok = rbt_moe_block(rbt_engine_ctx, l, X, nt, R + (size_t)l * c->top_k, (int)row);
+    }
+    /* final norm and lm_head: every token for --dump, else the last one only */
+    for (int t = fl ? 0 : nt - 1; ok && t < nt; t++) {
+        rmsnorm(s->xb, X + (size_t)t * D, VEC(m, m->final_norm), D, c->rms_eps);
+        matvec(s->logits, MAT(m, m->lm_head), c->dtype, s->xb, c->vocab, D);
+        if (fl && (fwrite(s->logits, sizeof(float), (size_t)c->vocab, fl) != (size_t)c->vocab ||
+                   fwrite(R + (size_t)t * row, sizeof(int32_t), row, fr) != row)) {
+            fprintf(stderr, "cannot write the dump files\n");
+            ok = 0;
+        }
+    }
+    if (ok) memcpy(routing, R + (size_t)(nt - 1) * row, row * sizeof(int32_t));
+    free(X);
+    free(R);
+    return ok ? 1 : -1;
 }
 
 #endif /* RBT_ENGINE_HOOK_H */
