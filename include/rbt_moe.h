@@ -208,6 +208,49 @@ int rbt_moe_decode_noalloc(const RbtMoeConfig *cfg, const float *d_ffn_norm, con
                            const float *d_router_bias, const void *d_experts, const float *d_x, float *d_out,
                            int32_t *d_routing_out, void *stream);
 
+/* ---- The whole forward() on the GPU (rabbit2.c:455-550) ----
+ * The engine's forward(Model*, State*, token, pos, routing_out) computes one
+ * token: embedding row, then per layer RMSNorm, Q/K/V projections, whole-
+ * projection QK-norm, RoPE, causal attention over the KV cache, the output
+ * projection and residual, then the MoE block; then the final norm and lm_head.
+ * An RbtModel holds every weight and the KV cache in HBM and runs that token as
+ * one CUDA graph; the MoE blocks are rbt_moe_block's kernels. */
+
+/* The engine's Config (rabbit2.c:63-68, the on-disk header fields in order) plus
+ * Model.expert_stride (rabbit2.c:173). */
+typedef struct RbtModelConfig {
+    int32_t vocab, dim, n_layers, n_heads, n_kv_heads, head_dim;
+    int32_t n_experts, top_k, expert_hidden, max_seq;
+    int32_t dtype, qk_norm, norm_topk;
+    float rope_theta, rms_eps;
+    uint64_t expert_stride;
+} RbtModelConfig;
+
+typedef struct RbtModel RbtModel; /* opaque: weights, KV cache and graphs on one GPU */
+
+/* Create a model on CUDA device `device` with a KV cache of `ctx` positions
+ * (1..max_seq); the State of rabbit2.c:101-106 lives on the GPU. */
+int rbt_model_create(RbtModel **out, const RbtModelConfig *cfg, int ctx, int device);
+void rbt_model_destroy(RbtModel *m);
+
+/* Upload weights from host memory (the mmap'd .rbt2; Model/LayerOff offsets of
+ * rabbit2.c:70-100): tok_emb [vocab,dim], final_norm [dim] f32, lm_head
+ * [vocab,dim]; per layer attn_norm [dim], wq [n_heads*head_dim, dim], wk and wv
+ * [n_kv_heads*head_dim, dim], wo [dim, n_heads*head_dim], q_norm/k_norm (f32,
+ * NULL when qk_norm is 0), ffn_norm [dim], router [n_experts, dim] and the
+ * layer's first expert blob.  Every layer and the globals must be loaded before
+ * rbt_model_forward. */
+int rbt_model_load_globals(RbtModel *m, const void *tok_emb, const float *final_norm, const void *lm_head);
+int rbt_model_load_layer(RbtModel *m, int layer, const float *attn_norm, const void *wq, const void *wk,
+                         const void *wv, const void *wo, const float *q_norm, const float *k_norm,
+                         const float *ffn_norm, const void *router, const void *experts);
+
+/* forward(): the token at position pos (0 <= pos < ctx; positions are filled in
+ * order, as the engine does).  logits [vocab] (host, or NULL to skip lm_head)
+ * and routing_out [n_layers*top_k] (host, or NULL) receive the engine's
+ * s->logits and routing rows. */
+int rbt_model_forward(RbtModel *m, int token, int pos, float *logits, int32_t *routing_out);
+
 /* Last error message of the calling thread ("" if none). */
 const char *rbt_moe_last_error(void);
 

@@ -1,0 +1,630 @@
+// model.cu -- the rest of the engine's forward() on the GPU (rabbit2.c:455-550):
+// embedding, attention half of every layer, final norm and lm_head.  The MoE
+// blocks are rbt_moe_block_device (moe_api.cu) on the same stream.
+//
+// One token (decode, batch 1) per call, as forward() does.  Everything the engine
+// keeps in State (rabbit2.c:101-106) lives in HBM: the residual x, q|k|v, the KV
+// cache [n_layers][ctx][kv_dim] (f32, as the engine keeps it), the logits.  The
+// token and position are read from device memory, so the whole token -- 2 + 4 L
+// kernels -- is one CUDA graph, replayed per token:
+//
+//   embed                       x = tok_emb[token]                       (:461-467)
+//   per layer l:
+//     norm_gemv                 q|k|v = [wq;wk;wv] . rmsnorm(x)          (:473-476)
+//     attn_decode (heads x splits)
+//                               whole-projection QK-norm, RoPE at pos,    (:477-483)
+//                               k, v into the cache, scores, softmax, the (:485-506)
+//                               weighted V sum of one split of positions;
+//                               the last split of a head to finish merges
+//                               the splits (max / sum rescaling)
+//     out_proj                  x += wo . attn_out                       (:507-508)
+//     rbt_moe_block_device      x += MoE(rmsnorm(x))                     (:511-542)
+//   norm_gemv                   logits = lm_head . rmsnorm(x)            (:545-546)
+//
+// The GEMVs stream each weight row once with 16-byte loads (HBM-bound: at the
+// OLMoE shape 24 MB q|k|v + 8 MB wo per layer and 206 MB of lm_head per token).
+// Arithmetic is fp32; sums are in a fixed order, so results are deterministic,
+// and differ from the engine's sequential sums by reassociation only.  RoPE
+// uses a table of the engine's own angles (fp64 pow/cos/sin, rounded to f32,
+// computed on the host by the same formula as rope(), rabbit2.c:410-421).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <new>
+#include <vector>
+
+#include "../../include/rbt_moe.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_ptx.cuh"
+
+namespace rbt {
+void set_last_error(const char* msg);
+int moe_status_ok(RbtMoe* m);
+}  // namespace rbt
+
+namespace {
+
+using namespace rbt;
+using namespace rbt::tc;
+
+int fail(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "rbt_model: %s\n", buf);
+    set_last_error(buf);
+    return 0;
+}
+
+#define CU(call)                                                                                  \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess) return fail("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                                   \
+    } while (0)
+
+constexpr int kGemvThreads = 512;
+constexpr int kGemvUnroll = 8;   // 16-byte weight loads in flight per lane
+constexpr int kAttnThreads = 128;
+constexpr int kSplit = 64;       // positions per attention split
+constexpr int kMaxHeadDim = 256;
+
+struct Step {
+    int token, pos;
+};
+
+// ---------------------------------------------------------------- embedding
+template <typename WT>
+__global__ void embed_kernel(const WT* emb, int D, const Step* step, float* x) {
+    pdl_wait();
+    const size_t row = (size_t)step->token * D;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x)
+        x[i] = WeightTraits<WT>::load1(emb + row + i);
+}
+
+// ---------------------------------------------------------------- GEMV rows
+// out row r = W[r, :] . xs (xs: `cols` floats in shared memory); warp-per-row,
+// rows r = global warp, + total warps, ...; epi(r, dot) stores the row.
+template <typename WT, typename Epi>
+__device__ __forceinline__ void gemv_rows(const float* xs, int cols, const WT* W, int rows, Epi epi) {
+    constexpr int kV = WeightTraits<WT>::kVec;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int nvec = cols / kV;
+    for (int r = blockIdx.x * nwarps + warp; r < rows; r += gridDim.x * nwarps) {
+        const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)r * cols);
+        float acc = 0.0f;
+        for (int v0 = 0; v0 < nvec; v0 += 32 * kGemvUnroll) {
+            uint4 q[kGemvUnroll];
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; u++) {
+                const int v = v0 + lane + 32 * u;
+                q[u] = v < nvec ? ld_stream16(wr + v) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; u++) {
+                const int v = v0 + lane + 32 * u;
+                if (v < nvec) {
+                    float f[kV];
+                    WeightTraits<WT>::unpack(q[u], f);
+                    const float* xv = xs + (size_t)v * kV;
+#pragma unroll
+                    for (int e = 0; e < kV; e++) acc = fmaf(f[e], xv[e], acc);
+                }
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) epi(r, acc);
+    }
+}
+
+// out[r] = W[r, :] . rmsnorm(x, nw) for r < rows.  Every CTA normalises x itself
+// with the same fixed-order sum, so all hold the same bits (rmsnorm, rabbit2.c:392-397).
+template <typename WT>
+__global__ void __launch_bounds__(kGemvThreads) norm_gemv_kernel(const float* x, const float* nw, float eps,
+                                                                 int D, const WT* W, int rows, float* out) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float red[kGemvThreads / 32];
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        const float v = x[i];
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += red[w];
+    const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), eps));
+    for (int i = threadIdx.x; i < D; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
+    __syncthreads();
+    gemv_rows<WT>(xs, D, W, rows, [&](int r, float v) { out[r] = v; });
+}
+
+// x[r] += wo[r, :] . attn_out  (rabbit2.c:507-508)
+template <typename WT>
+__global__ void __launch_bounds__(kGemvThreads) out_proj_kernel(const float* ao, int nq, const WT* wo, int D,
+                                                                float* x) {
+    extern __shared__ __align__(16) float xs[];
+    pdl_wait();
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) xs[i] = __ldcg(ao + i);
+    __syncthreads();
+    gemv_rows<WT>(xs, nq, wo, D, [&](int r, float v) { x[r] = __fadd_rn(x[r], v); });
+}
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+    const float* qkv;       // [nq + 2 nkv]: q | k | v of this token
+    const float* q_norm;    // [nq] or nullptr (no QK-norm)
+    const float* k_norm;    // [nkv]
+    float eps, scale;
+    const float* rope_cos;  // [ctx][head_dim / 2]
+    const float* rope_sin;
+    float* kc;              // this layer's cache [ctx][nkv]
+    float* vc;
+    const Step* step;
+    float* part;            // [n_heads][n_splits][head_dim + 2]: max, sum, weighted V
+    float* ao;              // [nq] attention output
+    unsigned* done;         // [n_heads] finished splits, zero between calls
+    int n_heads, n_kv_heads, hd, n_splits;
+};
+
+// block-wide sum of v in a fixed order (every thread gets the total)
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();  // red is free
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+    return t;
+}
+
+// rmsnorm factor of n floats at p (the QK-norm over the whole projection)
+__device__ __forceinline__ float rms_inv(const float* p, int n, float eps, float* red) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(p[i], p[i], ss);
+    const float tot = block_sum(ss, red);
+    return 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)n), eps));
+}
+
+// v[0..hd) of one head: QK-norm (inv, weights w or none) then RoPE at the table row
+__device__ __forceinline__ void norm_rope(float* v, const float* src, const float* w, float inv, const float* cs,
+                                          const float* sn, int hd) {
+    const int half = hd / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        float a = src[i], b = src[i + half];
+        if (w) {
+            a = __fmul_rn(__fmul_rn(a, inv), w[i]);
+            b = __fmul_rn(__fmul_rn(b, inv), w[i + half]);
+        }
+        // rope(): p[i] = a cs - b sn, p[i + half] = b cs + a sn (rabbit2.c:418-419)
+        v[i] = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
+        v[i + half] = __fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i]));
+    }
+}
+
+// CTA (head h, split s) covers positions [s kSplit, min((s+1) kSplit, pos+1)).
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+    __shared__ __align__(16) float qh[kMaxHeadDim], kn[kMaxHeadDim], vn[kMaxHeadDim];
+    __shared__ float sc[kSplit];
+    __shared__ float red[kAttnThreads / 32];
+    __shared__ unsigned s_last;
+    pdl_wait();
+    const int h = blockIdx.x, s = blockIdx.y, hd = a.hd;
+    const int pos = a.step->pos;
+    const int t0 = s * kSplit;
+    if (t0 > pos) return;  // a split past the current position: no work, not counted
+    const int t1 = min(t0 + kSplit, pos + 1);
+    const int nq = a.n_heads * hd, nkv = a.n_kv_heads * hd;
+    const int kvh = h / (a.n_heads / a.n_kv_heads);
+    const int half = hd / 2;
+    const float* cs = a.rope_cos + (size_t)pos * half;
+    const float* sn = a.rope_sin + (size_t)pos * half;
+    // q of head h (rabbit2.c:477-482)
+    const float inv_q = a.q_norm ? rms_inv(a.qkv, nq, a.eps, red) : 1.0f;
+    norm_rope(qh, a.qkv + (size_t)h * hd, a.q_norm ? a.q_norm + (size_t)h * hd : nullptr, inv_q, cs, sn, hd);
+    const bool has_new = pos < t1;  // this split holds position pos: k, v of this token
+    if (has_new) {
+        const float* k = a.qkv + nq;
+        const float inv_k = a.k_norm ? rms_inv(k, nkv, a.eps, red) : 1.0f;
+        norm_rope(kn, k + (size_t)kvh * hd, a.k_norm ? a.k_norm + (size_t)kvh * hd : nullptr, inv_k, cs, sn, hd);
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) vn[i] = a.qkv[nq + nkv + (size_t)kvh * hd + i];
+    }
+    __syncthreads();
+    if (has_new && h % (a.n_heads / a.n_kv_heads) == 0) {  // one head of the group stores them (:484-486)
+        float* kd = a.kc + (size_t)pos * nkv + (size_t)kvh * hd;
+        float* vd = a.vc + (size_t)pos * nkv + (size_t)kvh * hd;
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+            kd[i] = kn[i];
+            vd[i] = vn[i];
+        }
+    }
+    // scores (rabbit2.c:488-495): warp w takes positions t0 + w, t0 + w + 4, ...
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int t = t0 + warp; t < t1; t += nwarps) {
+        const float* kt = t == pos ? kn : a.kc + (size_t)t * nkv + (size_t)kvh * hd;
+        float d = 0.0f;
+        for (int i = lane; i < hd; i += 32) d = fmaf(qh[i], kt[i], d);
+        d = warp_sum(d);
+        if (lane == 0) sc[t - t0] = d * a.scale;
+    }
+    __syncthreads();
+    // this split's max, exp sum and exp-weighted V (softmax, rabbit2.c:399-405,496-505)
+    const int n = t1 - t0;
+    float mx = -INFINITY;
+    for (int j = 0; j < n; j++) mx = fmaxf(mx, sc[j]);
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) sc[j] = expf(sc[j] - mx);
+    __syncthreads();
+    float l = 0.0f;
+    for (int j = 0; j < n; j++) l += sc[j];
+    float* pp = a.part + ((size_t)h * a.n_splits + s) * (hd + 2);
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float o = 0.0f;
+        for (int j = 0; j < n; j++) {
+            const int t = t0 + j;
+            const float v = t == pos ? vn[i] : a.vc[(size_t)t * nkv + (size_t)kvh * hd + i];
+            o = fmaf(sc[j], v, o);
+        }
+        pp[2 + i] = o;
+    }
+    if (threadIdx.x == 0) {
+        pp[0] = mx;
+        pp[1] = l;
+    }
+    // the last split of head h to finish merges all of them (every writer fences
+    // its partial before the count is taken)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned n_act = (unsigned)(pos / kSplit + 1);
+        const unsigned prev = atomicAdd(a.done + h, 1u);
+        s_last = prev + 1 == n_act;
+        if (s_last) a.done[h] = 0;  // every split of this call has arrived: reset for the next
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int n_act = pos / kSplit + 1;
+    const float* ph = a.part + (size_t)h * a.n_splits * (hd + 2);
+    float M = -INFINITY;
+    for (int j = 0; j < n_act; j++) M = fmaxf(M, __ldcg(ph + (size_t)j * (hd + 2)));
+    float L = 0.0f;
+    for (int j = 0; j < n_act; j++) {
+        const float* pj = ph + (size_t)j * (hd + 2);
+        L += __ldcg(pj + 1) * expf(__ldcg(pj) - M);
+    }
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float o = 0.0f;
+        for (int j = 0; j < n_act; j++) {
+            const float* pj = ph + (size_t)j * (hd + 2);
+            o = fmaf(__ldcg(pj + 2 + i), expf(__ldcg(pj) - M), o);
+        }
+        a.ao[(size_t)h * hd + i] = o / L;
+    }
+}
+
+// ---------------------------------------------------------------- launches
+// Launch with programmatic stream serialization: each kernel calls
+// griddepcontrol.wait before it reads what the previous one wrote.
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+}  // namespace
+
+struct RbtModel {
+    RbtModelConfig cfg{};
+    int ctx = 0, device = 0, sm_count = 0;
+    RbtMoe* moe = nullptr;
+    cudaStream_t stream = nullptr;
+    size_t esz = 0;
+    // weights
+    void* tok_emb = nullptr;
+    void* lm_head = nullptr;
+    float* final_norm = nullptr;
+    struct Layer {
+        float* attn_norm = nullptr;
+        float* q_norm = nullptr;
+        float* k_norm = nullptr;
+        void* wqkv = nullptr;  // [wq; wk; wv] rows, contiguous
+        void* wo = nullptr;
+        bool loaded = false;
+    };
+    std::vector<Layer> layers;
+    bool globals = false;
+    // state
+    float *x = nullptr, *qkv = nullptr, *part = nullptr, *ao = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    int32_t* routing = nullptr;
+    unsigned* done = nullptr;
+    Step* step = nullptr;
+    // pinned host staging
+    Step* h_step = nullptr;
+    float* h_logits = nullptr;
+    int32_t* h_routing = nullptr;
+    // graphs: [0] without lm_head, [1] with
+    cudaGraphExec_t graph[2] = {nullptr, nullptr};
+    int n_splits = 0;
+};
+
+namespace {
+
+int nq_of(const RbtModelConfig& c) { return c.n_heads * c.head_dim; }
+int nkv_of(const RbtModelConfig& c) { return c.n_kv_heads * c.head_dim; }
+
+template <typename T>
+int dalloc(T** p, size_t bytes) {
+    CU(cudaMalloc((void**)p, bytes));
+    return 1;
+}
+
+int upload(void** dst, const void* src, size_t bytes) {
+    if (!*dst) CU(cudaMalloc(dst, bytes));
+    CU(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+    return 1;
+}
+
+template <typename WT>
+int enqueue_token(RbtModel* m, bool with_logits) {
+    const RbtModelConfig& c = m->cfg;
+    const int D = c.dim, nq = nq_of(c), nkv = nkv_of(c), rows_qkv = nq + 2 * nkv;
+    cudaStream_t s = m->stream;
+    CU(cudaMemcpyAsync(m->step, m->h_step, sizeof(Step), cudaMemcpyHostToDevice, s));
+    CU(launch_pdl(embed_kernel<WT>, dim3((D + 255) / 256), dim3(256), 0, s, (const WT*)m->tok_emb, D,
+                  (const Step*)m->step, m->x));
+    const int gemv_grid = m->sm_count * 2;
+    for (int l = 0; l < c.n_layers; l++) {
+        const RbtModel::Layer& L = m->layers[l];
+        CU(launch_pdl(norm_gemv_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)D * 4, s,
+                      (const float*)m->x, (const float*)L.attn_norm, c.rms_eps, D, (const WT*)L.wqkv, rows_qkv,
+                      m->qkv));
+        AttnArgs a;
+        a.qkv = m->qkv;
+        a.q_norm = c.qk_norm ? L.q_norm : nullptr;
+        a.k_norm = c.qk_norm ? L.k_norm : nullptr;
+        a.eps = c.rms_eps;
+        a.scale = 1.0f / sqrtf((float)c.head_dim);
+        a.rope_cos = m->rope_cos;
+        a.rope_sin = m->rope_sin;
+        a.kc = m->kc + (size_t)l * m->ctx * nkv;
+        a.vc = m->vc + (size_t)l * m->ctx * nkv;
+        a.step = m->step;
+        a.part = m->part;
+        a.ao = m->ao;
+        a.done = m->done;
+        a.n_heads = c.n_heads;
+        a.n_kv_heads = c.n_kv_heads;
+        a.hd = c.head_dim;
+        a.n_splits = m->n_splits;
+        CU(launch_pdl(attn_decode_kernel, dim3(c.n_heads, m->n_splits), dim3(kAttnThreads), 0, s, a));
+        CU(launch_pdl(out_proj_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)nq * 4, s, (const float*)m->ao,
+                      nq, (const WT*)L.wo, D, m->x));
+        if (!rbt_moe_block_device(m->moe, l, m->x, 1, m->routing + (size_t)l * c.top_k, c.top_k, (void*)s))
+            return 0;
+    }
+    CU(cudaMemcpyAsync(m->h_routing, m->routing, sizeof(int32_t) * c.n_layers * c.top_k, cudaMemcpyDeviceToHost, s));
+    if (with_logits) {
+        CU(launch_pdl(norm_gemv_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)D * 4, s,
+                      (const float*)m->x, (const float*)m->final_norm, c.rms_eps, D, (const WT*)m->lm_head, c.vocab,
+                      m->logits));
+        CU(cudaMemcpyAsync(m->h_logits, m->logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
+    }
+    return 1;
+}
+
+int build_graph(RbtModel* m, bool with_logits) {
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    const int ok = m->cfg.dtype == RBT_MOE_DT_BF16 ? enqueue_token<uint16_t>(m, with_logits)
+                                                   : enqueue_token<float>(m, with_logits);
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (!ok) {
+        if (g) cudaGraphDestroy(g);
+        return 0;
+    }
+    if (e != cudaSuccess) return fail("stream capture of the token failed: %s", cudaGetErrorString(e));
+    const cudaError_t ei = cudaGraphInstantiate(&m->graph[with_logits], g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) return fail("graph instantiation failed: %s", cudaGetErrorString(ei));
+    return 1;
+}
+
+// device state, pinned staging and the RoPE table of a new model
+int init_state(RbtModel* m) {
+    const RbtModelConfig& c = m->cfg;
+    const int ctx = m->ctx;
+    cudaDeviceProp prop;
+    CU(cudaGetDeviceProperties(&prop, m->device));
+    m->sm_count = prop.multiProcessorCount;
+    CU(cudaSetDevice(m->device));
+    CU(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    const int nq = nq_of(c), nkv = nkv_of(c), half = c.head_dim / 2;
+    const size_t kv = (size_t)c.n_layers * ctx * nkv * sizeof(float);
+    if (!dalloc(&m->x, (size_t)c.dim * 4) || !dalloc(&m->qkv, (size_t)(nq + 2 * nkv) * 4) ||
+        !dalloc(&m->part, (size_t)c.n_heads * m->n_splits * (c.head_dim + 2) * 4) || !dalloc(&m->ao, (size_t)nq * 4) ||
+        !dalloc(&m->logits, (size_t)c.vocab * 4) || !dalloc(&m->kc, kv) || !dalloc(&m->vc, kv) ||
+        !dalloc(&m->rope_cos, (size_t)ctx * half * 4) || !dalloc(&m->rope_sin, (size_t)ctx * half * 4) ||
+        !dalloc(&m->routing, (size_t)c.n_layers * c.top_k * 4) || !dalloc(&m->done, (size_t)c.n_heads * 4) ||
+        !dalloc(&m->step, sizeof(Step)))
+        return 0;
+    CU(cudaMemset(m->kc, 0, kv));
+    CU(cudaMemset(m->vc, 0, kv));
+    CU(cudaMemset(m->done, 0, (size_t)c.n_heads * 4));
+    CU(cudaMallocHost((void**)&m->h_step, sizeof(Step)));
+    CU(cudaMallocHost((void**)&m->h_logits, (size_t)c.vocab * 4));
+    CU(cudaMallocHost((void**)&m->h_routing, (size_t)c.n_layers * c.top_k * 4));
+    // the engine's RoPE angles (rope(), rabbit2.c:410-421): fp64 pow/cos/sin rounded to f32
+    std::vector<float> cs((size_t)ctx * half), sn((size_t)ctx * half);
+    for (int p = 0; p < ctx; p++)
+        for (int i = 0; i < half; i++) {
+            const double freq = pow((double)c.rope_theta, -2.0 * i / c.head_dim);
+            const double ang = p * freq;
+            cs[(size_t)p * half + i] = (float)cos(ang);
+            sn[(size_t)p * half + i] = (float)sin(ang);
+        }
+    CU(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    return rbt_moe_reserve(m->moe, 1);
+}
+
+}  // namespace
+
+extern "C" {
+
+int rbt_model_create(RbtModel** out, const RbtModelConfig* cfg, int ctx, int device) {
+    if (!out || !cfg) return fail("null argument");
+    *out = nullptr;
+    const RbtModelConfig& c = *cfg;
+    if (c.vocab <= 0 || c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0)
+        return fail("invalid config: dims must be positive");
+    if (c.dtype != RBT_MOE_DT_F32 && c.dtype != RBT_MOE_DT_BF16) return fail("dtype must be 0 (f32) or 1 (bf16)");
+    if (c.n_heads % c.n_kv_heads) return fail("n_heads %d is not a multiple of n_kv_heads %d", c.n_heads, c.n_kv_heads);
+    if (c.head_dim % 2 || c.head_dim > kMaxHeadDim) return fail("head_dim %d must be even and <= %d", c.head_dim, kMaxHeadDim);
+    const int vec = c.dtype == RBT_MOE_DT_BF16 ? 8 : 4;  // elements per 16-byte load
+    if (c.dim % vec || nq_of(c) % vec) return fail("dim and n_heads*head_dim must be multiples of %d", vec);
+    if (ctx <= 0 || ctx > c.max_seq) return fail("ctx %d out of range [1, max_seq %d]", ctx, c.max_seq);
+    RbtMoeConfig mc;
+    mc.dim = c.dim;
+    mc.n_experts = c.n_experts;
+    mc.top_k = c.top_k;
+    mc.expert_hidden = c.expert_hidden;
+    mc.n_layers = c.n_layers;
+    mc.dtype = c.dtype;
+    mc.norm_topk = c.norm_topk;
+    mc.rms_eps = c.rms_eps;
+    mc.expert_stride = c.expert_stride;
+    RbtMoe* moe = nullptr;
+    if (!rbt_moe_create(&moe, &mc, device)) return 0;  // validates the MoE part and the device
+    RbtModel* m = new (std::nothrow) RbtModel();
+    if (!m) {
+        rbt_moe_destroy(moe);
+        return fail("out of host memory");
+    }
+    m->cfg = c;
+    m->ctx = ctx;
+    m->device = device;
+    m->moe = moe;
+    m->esz = c.dtype == RBT_MOE_DT_BF16 ? 2 : 4;
+    m->layers.resize(c.n_layers);
+    m->n_splits = (ctx + kSplit - 1) / kSplit;
+    if (!init_state(m)) {
+        rbt_model_destroy(m);
+        return 0;
+    }
+    *out = m;
+    return 1;
+}
+
+void rbt_model_destroy(RbtModel* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    for (cudaGraphExec_t& g : m->graph)
+        if (g) cudaGraphExecDestroy(g);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (RbtModel::Layer& L : m->layers) {
+        cudaFree(L.attn_norm);
+        cudaFree(L.q_norm);
+        cudaFree(L.k_norm);
+        cudaFree(L.wqkv);
+        cudaFree(L.wo);
+    }
+    cudaFree(m->tok_emb);
+    cudaFree(m->lm_head);
+    cudaFree(m->final_norm);
+    void* bufs[] = {m->x, m->qkv, m->part, m->ao, m->logits, m->kc, m->vc, m->rope_cos, m->rope_sin, m->routing,
+                    m->done, m->step};
+    for (void* p : bufs) cudaFree(p);
+    cudaFreeHost(m->h_step);
+    cudaFreeHost(m->h_logits);
+    cudaFreeHost(m->h_routing);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    rbt_moe_destroy(m->moe);
+    delete m;
+}
+
+int rbt_model_load_globals(RbtModel* m, const void* tok_emb, const float* final_norm, const void* lm_head) {
+    if (!m) return fail("null model");
+    if (!tok_emb || !final_norm || !lm_head) return fail("null weight pointer");
+    CU(cudaSetDevice(m->device));
+    const RbtModelConfig& c = m->cfg;
+    const size_t mat = (size_t)c.vocab * c.dim * m->esz;
+    if (!upload(&m->tok_emb, tok_emb, mat) || !upload((void**)&m->final_norm, final_norm, (size_t)c.dim * 4) ||
+        !upload(&m->lm_head, lm_head, mat))
+        return 0;
+    m->globals = true;
+    return 1;
+}
+
+int rbt_model_load_layer(RbtModel* m, int layer, const float* attn_norm, const void* wq, const void* wk,
+                         const void* wv, const void* wo, const float* q_norm, const float* k_norm,
+                         const float* ffn_norm, const void* router, const void* experts) {
+    if (!m) return fail("null model");
+    const RbtModelConfig& c = m->cfg;
+    if (layer < 0 || layer >= c.n_layers) return fail("layer %d out of range [0, %d)", layer, c.n_layers);
+    if (!attn_norm || !wq || !wk || !wv || !wo || !ffn_norm || !router || !experts)
+        return fail("null weight pointer");
+    if (c.qk_norm && (!q_norm || !k_norm)) return fail("qk_norm is set but q_norm/k_norm is null");
+    CU(cudaSetDevice(m->device));
+    RbtModel::Layer& L = m->layers[layer];
+    const int D = c.dim, nq = nq_of(c), nkv = nkv_of(c);
+    const size_t qb = (size_t)nq * D * m->esz, kb = (size_t)nkv * D * m->esz;
+    if (!L.wqkv) CU(cudaMalloc(&L.wqkv, qb + 2 * kb));
+    uint8_t* w = static_cast<uint8_t*>(L.wqkv);
+    CU(cudaMemcpy(w, wq, qb, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(w + qb, wk, kb, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(w + qb + kb, wv, kb, cudaMemcpyHostToDevice));
+    if (!upload(&L.wo, wo, (size_t)D * nq * m->esz) || !upload((void**)&L.attn_norm, attn_norm, (size_t)D * 4))
+        return 0;
+    if (c.qk_norm &&
+        (!upload((void**)&L.q_norm, q_norm, (size_t)nq * 4) || !upload((void**)&L.k_norm, k_norm, (size_t)nkv * 4)))
+        return 0;
+    if (!rbt_moe_load_layer(m->moe, layer, ffn_norm, router, experts)) return 0;
+    L.loaded = true;
+    return 1;
+}
+
+int rbt_model_forward(RbtModel* m, int token, int pos, float* logits, int32_t* routing_out) {
+    if (!m) return fail("null model");
+    const RbtModelConfig& c = m->cfg;
+    if (token < 0 || token >= c.vocab) return fail("token %d out of range", token);
+    if (pos < 0 || pos >= m->ctx) return fail("position %d outside the KV cache of %d", pos, m->ctx);
+    if (!m->globals) return fail("globals not loaded (rbt_model_load_globals)");
+    for (int l = 0; l < c.n_layers; l++)
+        if (!m->layers[l].loaded) return fail("layer %d not loaded (rbt_model_load_layer)", l);
+    CU(cudaSetDevice(m->device));
+    const int with = logits != nullptr;
+    if (!m->graph[with] && !build_graph(m, with)) return 0;
+    m->h_step->token = token;
+    m->h_step->pos = pos;
+    CU(cudaGraphLaunch(m->graph[with], m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    if (!moe_status_ok(m->moe)) return 0;
+    if (logits) memcpy(logits, m->h_logits, sizeof(float) * c.vocab);
+    if (routing_out) memcpy(routing_out, m->h_routing, sizeof(int32_t) * c.n_layers * c.top_k);
+    return 1;
+}
+
+}  // extern "C"

@@ -520,6 +520,12 @@ int forward_host(RbtMoe* m, int layer, const float* x, float* out, int T, int32_
 
 }  // namespace
 
+namespace rbt {
+// 1 if the context's kernels reported no timed-out wait since the last check,
+// else 0 with the message set (for the whole-forward calls of model.cu)
+int moe_status_ok(RbtMoe* m) { return check_status(m); }
+}  // namespace rbt
+
 extern "C" {
 
 const char* rbt_moe_last_error(void) { return g_err; }

@@ -1,0 +1,86 @@
+"""Python binding of the whole-forward calls of librbt_moe.so (rbt_model_*,
+include/rbt_moe.h): the engine's forward() (rabbit2.c:455-550) on one GPU.
+
+Plumbing for the tests and the benchmark, like moe.py: the product is the C ABI.
+``ModelContext.from_file`` maps a ``.rbt2`` file and uploads every tensor from
+the offsets the engine's loader computes (rbt2fmt.layout, rabbit2.c:166-193);
+``forward(token, pos)`` is forward(): the logits [vocab] and the routing rows
+[n_layers, top_k] of the token at position pos.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from rabbit2_b200 import moe
+from rabbit2_b200.rbt2fmt import ModelConfig, layout, unpack_header
+
+
+class RbtModelConfig(C.Structure):
+    _fields_ = [("vocab", C.c_int32), ("dim", C.c_int32), ("n_layers", C.c_int32), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("n_experts", C.c_int32),
+                ("top_k", C.c_int32), ("expert_hidden", C.c_int32), ("max_seq", C.c_int32),
+                ("dtype", C.c_int32), ("qk_norm", C.c_int32), ("norm_topk", C.c_int32),
+                ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("expert_stride", C.c_uint64)]
+
+
+def c_config(cfg: ModelConfig, stride: int) -> RbtModelConfig:
+    return RbtModelConfig(cfg.vocab, cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                          cfg.n_experts, cfg.top_k, cfg.expert_hidden, cfg.max_seq, cfg.dtype, cfg.qk_norm,
+                          cfg.norm_topk, cfg.rope_theta, cfg.rms_eps, stride)
+
+
+class ModelContext:
+    """One RbtModel: every weight and the KV cache on one GPU."""
+
+    def __init__(self, cfg: ModelConfig, ctx: int, device: int = 0):
+        self.lib = moe.load_library()
+        self.cfg = cfg
+        self.lay = layout(cfg)
+        self.handle = C.c_void_p()
+        self._ccfg = c_config(cfg, self.lay["expert_stride"])
+        self._call(self.lib.rbt_model_create, C.byref(self.handle), C.byref(self._ccfg), ctx, device)
+
+    def _call(self, fn, *args):
+        if not fn(*args):
+            raise moe.RbtMoeError(self.lib.rbt_moe_last_error().decode())
+
+    @classmethod
+    def from_file(cls, path: str, ctx: int, device: int = 0) -> "ModelContext":
+        raw = np.memmap(path, dtype=np.uint8, mode="r")
+        cfg = unpack_header(bytes(raw[:68]))
+        self = cls(cfg, ctx, device)
+        base = raw.ctypes.data
+        lay = self.lay
+        at = lambda off: C.c_void_p(base + off)  # noqa: E731
+        self._call(self.lib.rbt_model_load_globals, self.handle, at(lay["tok_emb"]), at(lay["final_norm"]),
+                   at(lay["lm_head"]))
+        for l, ly in enumerate(lay["layers"]):
+            qn = at(ly["q_norm"]) if cfg.qk_norm else None
+            kn = at(ly["k_norm"]) if cfg.qk_norm else None
+            self._call(self.lib.rbt_model_load_layer, self.handle, l, at(ly["attn_norm"]), at(ly["wq"]),
+                       at(ly["wk"]), at(ly["wv"]), at(ly["wo"]), qn, kn, at(ly["ffn_norm"]), at(ly["router"]),
+                       at(ly["experts"]))
+        del raw
+        return self
+
+    def forward(self, token: int, pos: int, logits: bool = True):
+        """(logits [vocab] f32 or None, routing [n_layers, top_k] int32)."""
+        c = self.cfg
+        out = np.empty(c.vocab, np.float32) if logits else None
+        routing = np.empty((c.n_layers, c.top_k), np.int32)
+        self._call(self.lib.rbt_model_forward, self.handle, int(token), int(pos),
+                   out.ctypes.data if logits else None, routing.ctypes.data)
+        return out, routing
+
+    def close(self):
+        if self.handle:
+            self.lib.rbt_model_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -70,6 +70,10 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_ep_plan": [vp, i32, i32, i32, i32, i32, vp, vp, vp],
         "rbt_ep_pack": [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp],
         "rbt_ep_combine": [vp, i32, i32, i32, vp, vp, vp, vp, vp],
+        "rbt_model_create": [C.POINTER(vp), vp, i32, i32],
+        "rbt_model_load_globals": [vp, vp, vp, vp],
+        "rbt_model_load_layer": [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
+        "rbt_model_forward": [vp, i32, i32, vp, vp],
     }
     for name, argtypes in sig.items():
         fn = getattr(lib, name)
@@ -77,6 +81,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         fn.restype = C.c_int
     lib.rbt_moe_destroy.argtypes = [vp]
     lib.rbt_moe_destroy.restype = None
+    lib.rbt_model_destroy.argtypes = [vp]
+    lib.rbt_model_destroy.restype = None
     lib.rbt_moe_last_error.argtypes = []
     lib.rbt_moe_last_error.restype = C.c_char_p
     _lib = lib
@@ -212,4 +218,4 @@ def declared_symbols(header: str = HEADER):
     import re
     with open(header) as f:
         text = f.read()
-    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(rbt_(?:moe|ep)_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(rbt_(?:moe|ep|model)_\w+)\s*\(", text, flags=re.M)))

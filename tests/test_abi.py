@@ -59,3 +59,21 @@ def test_create_without_gpu_fails_loudly():
     cfg = moe.RbtMoeConfig(64, 8, 2, 128, 2, 1, 0, 1e-5, 3 * 128 * 64 * 2)
     assert lib.rbt_moe_create(C.byref(h), C.byref(cfg), 0) == 0
     assert lib.rbt_moe_last_error()
+
+
+def test_bad_model_config_is_rejected_with_a_message():
+    """rbt_model_create checks the attention part of the config before touching a GPU."""
+    from rabbit2_b200 import model, workload
+    lib = moe.load_library()
+    cfg = workload.tiny_olmoe_config()
+    stride = 3 * cfg.expert_hidden * cfg.dim * 4
+    h = C.c_void_p()
+    bad = model.c_config(cfg, stride)
+    bad.n_kv_heads = 3  # 4 heads are not a multiple of 3
+    assert lib.rbt_model_create(C.byref(h), C.byref(bad), 16, 0) == 0
+    assert b"n_kv_heads" in lib.rbt_moe_last_error()
+    good = model.c_config(cfg, stride)
+    assert lib.rbt_model_create(C.byref(h), C.byref(good), cfg.max_seq + 1, 0) == 0
+    assert b"ctx" in lib.rbt_moe_last_error()
+    assert lib.rbt_model_forward(None, 0, 0, None, None) == 0
+    lib.rbt_model_destroy(None)

@@ -1,0 +1,107 @@
+"""The whole forward() on the GPU (rbt_model_*, model.cu) against the reference
+engine itself (oracle/_ref/rabbit2, rabbit2/src/rabbit2.c compiled as is), on the
+same model files, through the engine's CLI outputs:
+
+- every prompt position's logits (`--dump`) within a max relative error of 1e-3
+  (max|d| / max|ref|) and its routing rows identical;
+- 64 greedy tokens after the prompt identical to `--gen 64`.
+
+Models: config 1 (tiny OLMoE, f32), the same shape in bf16, and a grouped-query
+variant (n_kv_heads < n_heads).  A 128-token prompt plus 64 generated tokens
+spans three 64-position attention splits.
+"""
+import dataclasses
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from rabbit2_b200 import moe, workload
+from rabbit2_b200.rbt2fmt import DT_BF16
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "oracle", "_ref", "rabbit2")
+needs_ref = pytest.mark.skipif(not os.path.exists(REF), reason="oracle/_ref/rabbit2 not built")
+LOGIT_RTOL = 1e-3
+
+
+def _cfg(kind):
+    cfg = workload.tiny_olmoe_config()
+    if kind == "bf16":
+        cfg = dataclasses.replace(cfg, dtype=DT_BF16)
+    elif kind == "gqa":
+        cfg = dataclasses.replace(cfg, n_heads=4, n_kv_heads=2, head_dim=64)
+    return cfg
+
+
+@pytest.fixture(scope="module", params=["f32", "bf16", "gqa"])
+def model_file(request, tmp_path_factory):
+    cfg = _cfg(request.param)
+    path = str(tmp_path_factory.mktemp("m") / f"tiny_{request.param}.rbt2")
+    workload.write_model(path, cfg, seed=3)
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=128).tolist()
+    return request.param, path, cfg, prompt
+
+
+def _ref_dump(path, prompt, tmp):
+    lg, rt = os.path.join(tmp, "l.bin"), os.path.join(tmp, "r.bin")
+    p = subprocess.run([REF, path, "--dump", lg, rt, "--ctx", "256", *map(str, prompt)], capture_output=True,
+                       text=True)
+    assert p.returncode == 0, p.stderr
+    return np.fromfile(lg, "<f4"), np.fromfile(rt, "<i4")
+
+
+def _ref_gen(path, prompt, n):
+    p = subprocess.run([REF, path, "--gen", str(n), "--ctx", "256", *map(str, prompt)], capture_output=True,
+                       text=True)
+    assert p.returncode == 0, p.stderr
+    return [int(t) for t in p.stdout.split()]
+
+
+@needs_ref
+@pytest.mark.gpu
+def test_forward_matches_reference_engine(model_file, tmp_path):
+    from rabbit2_b200.model import ModelContext
+    kind, path, cfg, prompt = model_file
+    want_l, want_r = _ref_dump(path, prompt, str(tmp_path))
+    want_l = want_l.reshape(len(prompt), cfg.vocab)
+    want_r = want_r.reshape(len(prompt), cfg.n_layers, cfg.top_k)
+    want_ids = _ref_gen(path, prompt, 64)
+    m = ModelContext.from_file(path, ctx=256)
+    try:
+        got_l = np.empty_like(want_l)
+        for t, tok in enumerate(prompt):
+            got_l[t], r = m.forward(tok, t)
+            np.testing.assert_array_equal(r, want_r[t], err_msg=f"{kind}: routing at position {t}")
+        err = np.abs(got_l.astype(np.float64) - want_l).max() / np.abs(want_l).max()
+        assert err < LOGIT_RTOL, (kind, err)
+        # greedy decode from the prompt's last logits, as the engine's --gen does
+        ids, logits, pos = [], got_l[-1], len(prompt)
+        for g in range(64):
+            nxt = int(np.argmax(logits))
+            ids.append(nxt)
+            if g + 1 == 64:
+                break
+            logits, _ = m.forward(nxt, pos)
+            pos += 1
+        assert ids == want_ids, kind
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+def test_forward_rejects_bad_token_and_position(tmp_path):
+    from rabbit2_b200.model import ModelContext
+    cfg = _cfg("f32")
+    path = str(tmp_path / "m.rbt2")
+    workload.write_model(path, cfg, seed=0)
+    m = ModelContext.from_file(path, ctx=16)
+    try:
+        with pytest.raises(moe.RbtMoeError, match="token"):
+            m.forward(cfg.vocab, 0)
+        with pytest.raises(moe.RbtMoeError, match="position"):
+            m.forward(1, 16)
+        m.forward(1, 0)  # the context still works
+    finally:
+        m.close()
