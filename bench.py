@@ -58,6 +58,11 @@ def parse():
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="moe", choices=["moe", "model-decode"],
+                    help="moe: the MoE stack (the metric's config); model-decode: the whole forward() of an "
+                         "OLMoE-1B-7B-shaped model, batch-1 greedy decode (config 3)")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=256)
     return ap.parse_args()
 
 
@@ -606,8 +611,91 @@ def run_ours(args, rank, world, local_rank):
     return out
 
 
+# ----------------------------------------------------------------------------- config 3
+
+def run_model_decode(args):
+    """Config 3: the whole forward() (rbt_model_forward: attention, MoE, lm_head) of a
+    random-init OLMoE-1B-7B-shaped model on one GPU -- a uniform-random prompt of
+    --prompt tokens, then --gen greedy tokens with the KV cache, as the engine's
+    --gen loop does (logits to the host, argmax there).  value = generated tokens
+    per second of wall clock around the calls (host round trip per token
+    included); prefill_tok_s is the prompt fed token by token."""
+    import torch
+
+    from rabbit2_b200 import model as model_mod
+    from rabbit2_b200.rbt2fmt import DT_BF16, ModelConfig, layout
+    cfg = ModelConfig(vocab=50304, dim=D, n_layers=args.layers, n_heads=16, n_kv_heads=16, head_dim=128,
+                      n_experts=E, top_k=K, expert_hidden=H, max_seq=4096, dtype=DT_BF16, qk_norm=1,
+                      norm_topk=0, rope_theta=10000.0, rms_eps=1e-5)
+    ctx_len = args.prompt + args.gen
+    m = model_mod.ModelContext(cfg, ctx=ctx_len)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+
+    def mat(rows, cols):  # bf16 ~N(0, 0.02), generated on the GPU, uploaded from host memory
+        return (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16).cpu()
+
+    lib, h = m.lib, m.handle
+    ones = np.ones(max(D, 16 * 128), np.float32)
+    emb, head = mat(cfg.vocab, D), mat(cfg.vocab, D)
+    m._call(lib.rbt_model_load_globals, h, emb.data_ptr(), ones.ctypes.data, head.data_ptr())
+    del emb, head
+    stride = layout(cfg)["expert_stride"]
+    assert stride == 3 * H * D * 2
+    for l in range(cfg.n_layers):
+        wq, wk, wv, wo, router = mat(2048, D), mat(2048, D), mat(2048, D), mat(D, 2048), mat(E, D)
+        experts = mat(E, 3 * H * D)
+        m._call(lib.rbt_model_load_layer, h, l, ones.ctypes.data, wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
+                wo.data_ptr(), ones.ctypes.data, ones.ctypes.data, ones.ctypes.data, router.data_ptr(),
+                experts.data_ptr())
+        del wq, wk, wv, wo, router, experts
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
+    # warm-up: graph capture and first launches (positions are rewritten below)
+    for p in range(min(3, args.prompt)):
+        m.forward(int(prompt[p]), p, logits=True)
+    t0 = time.perf_counter()
+    for p in range(args.prompt):
+        logits, _ = m.forward(int(prompt[p]), p, logits=p == args.prompt - 1)
+    t1 = time.perf_counter()
+    ids, pos = [], args.prompt
+    with ClockSampler(0) as clocks:
+        t2 = time.perf_counter()
+        for _ in range(args.gen):
+            nxt = int(np.argmax(logits))
+            ids.append(nxt)
+            logits, _ = m.forward(nxt, pos)
+            pos += 1
+        t3 = time.perf_counter()
+    m.close()
+    hbm, _, src = peaks()
+    dt = (t3 - t2) / args.gen
+    nq = nkv = 16 * 128
+    avg_ctx = args.prompt + (args.gen + 1) / 2
+    per_token = {"attention weights": cfg.n_layers * (nq + 2 * nkv + nq) * D * 2,
+                 "moe weights": cfg.n_layers * (E * D * 2 + K * 3 * H * D * 2),
+                 "lm_head": cfg.vocab * D * 2,
+                 "kv cache (f32, mean context)": cfg.n_layers * avg_ctx * nkv * 4 * 2}
+    total = sum(per_token.values())
+    return {"metric": "olmoe1b7b_full_model_decode_tok_per_s", "value": 1.0 / dt, "unit": "tok/s", "n_gpus": 1,
+            "steps": args.gen, "warmup": 3, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config3_olmoe1b7b_full_model_batch1_decode", "layers": cfg.n_layers,
+                       "prompt": args.prompt, "gen": args.gen, "vocab": cfg.vocab, "dim": D, "heads": 16,
+                       "head_dim": 128, "n_experts": E, "top_k": K, "expert_hidden": H,
+                       "weights": "bf16 ~N(0,0.02) seeded (norms 1)", "timing": "wall clock per forward call"},
+            "prefill_tok_s": args.prompt / (t1 - t0), "clocks": clocks.summary(),
+            "gpu_launches": (2 + 4 * cfg.n_layers) * args.gen,
+            "roofline": {"bound": "hbm", "achieved": total / dt / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": total / dt / 1e9 / hbm, "peak_source": src, "bytes_per_token": total,
+                         "bytes_per_token_parts": per_token, "traffic": None},
+            "generated_ids_head": ids[:8]}
+
+
 def main():
     args = parse()
+    if args.workload == "model-decode":
+        print(json.dumps(run_model_decode(args)), flush=True)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

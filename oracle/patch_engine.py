@@ -4,9 +4,9 @@
 
 Writes a copy of the reference engine source (rabbit2/src/rabbit2.c) into
 oracle/_ref/ with the edits INTEGRATION.md documents -- the include of
-rabbit2_b200/engine/rbt_engine_hook.h, its two CLI flags, its init call, the
-MoE-block call and the batched prompt before the prompt loop -- and nothing else
-changed.  oracle/Makefile compiles it against librbt_moe.so into
+rabbit2_b200/engine/rbt_engine_hook.h, its three CLI flags, its init call, the
+whole-forward and MoE-block calls and the batched prompt before the prompt
+loop -- and nothing else changed.  oracle/Makefile compiles it against librbt_moe.so into
 oracle/_ref/rabbit2_cuda.  Each edit is anchored on one reference line and
 fails loudly if that line is missing or not unique.
 """
@@ -16,6 +16,12 @@ INSERTIONS = [
     # (anchor line, where: before / after / replace, text)
     ("static int forward(Model *m, State *s, int token, int pos, int32_t *routing_out) {", "before",
      '#include "rbt_engine_hook.h"\n\n'),
+    ("static int forward(Model *m, State *s, int token, int pos, int32_t *routing_out) {", "after",
+     "    {\n"
+     "        int f_ = rbt_engine_forward(m, s, token, pos, routing_out);\n"
+     "        if (f_ < 0) return 0;\n"
+     "        if (f_) return 1;\n"
+     "    }\n"),
     ("        /* ---- MoE feed-forward ---- */", "after",
      "        {\n"
      "            int g_ = rbt_engine_moe(m, l, s->x, routing_out + (size_t)l * c->top_k);\n"
@@ -24,7 +30,8 @@ INSERTIONS = [
      "        }\n"),
     ('        else if (!strcmp(argv[i], "--kernel") && i + 1 < argc) kernel = argv[++i];', "before",
      '        else if (!strcmp(argv[i], "--device") && i + 1 < argc) rbt_engine_device = argv[++i];\n'
-     '        else if (!strcmp(argv[i], "--prefill") && i + 1 < argc) rbt_engine_prefill_mode = argv[++i];\n'),
+     '        else if (!strcmp(argv[i], "--prefill") && i + 1 < argc) rbt_engine_prefill_mode = argv[++i];\n'
+     '        else if (!strcmp(argv[i], "--offload") && i + 1 < argc) rbt_engine_offload = argv[++i];\n'),
     ("    if (!load_model(&m, argv[1])) return 1;", "after",
      "    if (!rbt_engine_init(&m)) return 1;\n"),
     ("    double t0 = now_sec();", "after",

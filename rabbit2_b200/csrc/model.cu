@@ -4,7 +4,8 @@
 //
 // One token (decode, batch 1) per call, as forward() does.  Everything the engine
 // keeps in State (rabbit2.c:101-106) lives in HBM: the residual x, q|k|v, the KV
-// cache [n_layers][ctx][kv_dim] (f32, as the engine keeps it), the logits.  The
+// cache (f32, as the engine keeps it, but head-major: [n_layers][n_kv_heads][ctx]
+// [head_dim], so one head's run of positions is contiguous), the logits.  The
 // token and position are read from device memory, so the whole token -- 2 + 4 L
 // kernels -- is one CUDA graph, replayed per token:
 //
@@ -70,95 +71,166 @@ int fail(const char* fmt, ...) {
                                            __FILE__, __LINE__);                                   \
     } while (0)
 
-constexpr int kGemvThreads = 512;
+constexpr int kGemvThreads = 256;
+constexpr int kGemvCtasPerSm = 4;
 constexpr int kGemvUnroll = 8;   // 16-byte weight loads in flight per lane
+constexpr int kMaxVec4 = 2;      // float4s of an input vector per GEMV thread: dim, n_heads*head_dim <= 2048
 constexpr int kAttnThreads = 128;
 constexpr int kSplit = 64;       // positions per attention split
 constexpr int kMaxHeadDim = 256;
+constexpr int kAttnVec4 = 16;    // float4s of q|k per attention thread: nq + nkv <= 8192
+constexpr int kMaxSplits = 128;  // ctx <= kMaxSplits x kSplit
+constexpr uint64_t kWaitNs = 2000000000ull;
 
 struct Step {
     int token, pos;
 };
 
+__device__ __forceinline__ void record_error(unsigned* status, unsigned code) { atomicCAS(status, 0u, code); }
+
 // ---------------------------------------------------------------- embedding
 template <typename WT>
 __global__ void embed_kernel(const WT* emb, int D, const Step* step, float* x) {
     pdl_wait();
+    pdl_launch_dependents();
     const size_t row = (size_t)step->token * D;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x)
         x[i] = WeightTraits<WT>::load1(emb + row + i);
 }
 
 // ---------------------------------------------------------------- GEMV rows
-// out row r = W[r, :] . xs (xs: `cols` floats in shared memory); warp-per-row,
-// rows r = global warp, + total warps, ...; epi(r, dot) stores the row.
-template <typename WT, typename Epi>
-__device__ __forceinline__ void gemv_rows(const float* xs, int cols, const WT* W, int rows, Epi epi) {
+// Warp-per-row GEMV: row r = W[r, :] . xs (xs: `cols` floats in shared memory),
+// rows r = global warp, + total warps, ...  A row is read in chunks of
+// 32 lanes x kGemvUnroll 16-byte loads, all in flight before the products.
+template <typename WT>
+__device__ __forceinline__ void load_chunk(const WT* W, int cols, int r, int v0, uint4 (&q)[kGemvUnroll]) {
+    const int lane = threadIdx.x & 31, nvec = cols / WeightTraits<WT>::kVec;
+    const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)r * cols);
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; u++) {
+        const int v = v0 + lane + 32 * u;
+        q[u] = v < nvec ? ld_stream16(wr + v) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+template <typename WT>
+__device__ __forceinline__ float dot_chunk(const float* xs, int cols, int v0, const uint4 (&q)[kGemvUnroll],
+                                           float acc) {
     constexpr int kV = WeightTraits<WT>::kVec;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int nvec = cols / kV;
-    for (int r = blockIdx.x * nwarps + warp; r < rows; r += gridDim.x * nwarps) {
-        const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)r * cols);
+    const int lane = threadIdx.x & 31, nvec = cols / kV;
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; u++) {
+        const int v = v0 + lane + 32 * u;
+        if (v < nvec) {
+            float f[kV];
+            WeightTraits<WT>::unpack(q[u], f);
+            const float* xv = xs + (size_t)v * kV;
+#pragma unroll
+            for (int e = 0; e < kV; e++) acc = fmaf(f[e], xv[e], acc);
+        }
+    }
+    return acc;
+}
+
+// The rows of this warp; the first chunk of its first row is already in q
+// (loaded before the kernel waited for its inputs).  epi(r, dot) stores a row.
+template <typename WT, typename Epi>
+__device__ __forceinline__ void gemv_rows(const float* xs, int cols, const WT* W, int rows, uint4 (&q)[kGemvUnroll],
+                                          Epi epi) {
+    const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const int nvec = cols / WeightTraits<WT>::kVec;
+    const int r0 = blockIdx.x * nwarps + (threadIdx.x >> 5);
+    for (int r = r0; r < rows; r += gridDim.x * nwarps) {
         float acc = 0.0f;
         for (int v0 = 0; v0 < nvec; v0 += 32 * kGemvUnroll) {
-            uint4 q[kGemvUnroll];
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; u++) {
-                const int v = v0 + lane + 32 * u;
-                q[u] = v < nvec ? ld_stream16(wr + v) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; u++) {
-                const int v = v0 + lane + 32 * u;
-                if (v < nvec) {
-                    float f[kV];
-                    WeightTraits<WT>::unpack(q[u], f);
-                    const float* xv = xs + (size_t)v * kV;
-#pragma unroll
-                    for (int e = 0; e < kV; e++) acc = fmaf(f[e], xv[e], acc);
-                }
-            }
+            if (r != r0 || v0 != 0) load_chunk<WT>(W, cols, r, v0, q);
+            acc = dot_chunk<WT>(xs, cols, v0, q, acc);
         }
         acc = warp_sum(acc);
         if (lane == 0) epi(r, acc);
     }
 }
 
+template <typename WT>
+__device__ __forceinline__ void prefetch_first_chunk(const WT* W, int cols, int rows, uint4 (&q)[kGemvUnroll]) {
+    const int r0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r0 < rows) load_chunk<WT>(W, cols, r0, 0, q);
+}
+
 // out[r] = W[r, :] . rmsnorm(x, nw) for r < rows.  Every CTA normalises x itself
 // with the same fixed-order sum, so all hold the same bits (rmsnorm, rabbit2.c:392-397).
+// The weights are static: the first chunk of every warp's first row is loaded
+// before griddepcontrol.wait, overlapping the previous kernel's tail.
 template <typename WT>
-__global__ void __launch_bounds__(kGemvThreads) norm_gemv_kernel(const float* x, const float* nw, float eps,
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) norm_gemv_kernel(const float* x, const float* nw, float eps,
                                                                  int D, const WT* W, int rows, float* out) {
     extern __shared__ __align__(16) float xs[];
     __shared__ float red[kGemvThreads / 32];
+    uint4 q[kGemvUnroll];
+    prefetch_first_chunk<WT>(W, D, rows, q);
     pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // x and the norm weights: every 16-byte load in flight at once (D <= kMaxVec4 x 4 x threads)
+    float4 xv[kMaxVec4], wv[kMaxVec4];
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        const float v = x[i];
-        xs[i] = v;
-        ss = fmaf(v, v, ss);
+    const int n4 = D / 4;
+#pragma unroll
+    for (int k = 0; k < kMaxVec4; k++) {
+        const int i4 = threadIdx.x + k * kGemvThreads;
+        if (i4 < n4) {
+            xv[k] = __ldcg(reinterpret_cast<const float4*>(x) + i4);
+            wv[k] = __ldg(reinterpret_cast<const float4*>(nw) + i4);
+        }
     }
+#pragma unroll
+    for (int k = 0; k < kMaxVec4; k++)
+        if (threadIdx.x + k * kGemvThreads < n4) {
+            ss = fmaf(xv[k].x, xv[k].x, ss);
+            ss = fmaf(xv[k].y, xv[k].y, ss);
+            ss = fmaf(xv[k].z, xv[k].z, ss);
+            ss = fmaf(xv[k].w, xv[k].w, ss);
+        }
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
     float tot = 0.0f;
     for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += red[w];
     const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), eps));
-    for (int i = threadIdx.x; i < D; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
+#pragma unroll
+    for (int k = 0; k < kMaxVec4; k++) {
+        const int i4 = threadIdx.x + k * kGemvThreads;
+        if (i4 < n4)
+            reinterpret_cast<float4*>(xs)[i4] =
+                make_float4(__fmul_rn(__fmul_rn(xv[k].x, inv), wv[k].x), __fmul_rn(__fmul_rn(xv[k].y, inv), wv[k].y),
+                            __fmul_rn(__fmul_rn(xv[k].z, inv), wv[k].z), __fmul_rn(__fmul_rn(xv[k].w, inv), wv[k].w));
+    }
     __syncthreads();
-    gemv_rows<WT>(xs, D, W, rows, [&](int r, float v) { out[r] = v; });
+    gemv_rows<WT>(xs, D, W, rows, q, [&](int r, float v) { out[r] = v; });
 }
 
-// x[r] += wo[r, :] . attn_out  (rabbit2.c:507-508)
+// x[r] += wo[r, :] . attn_out  (rabbit2.c:507-508).  It does not let the next
+// kernel (the cooperative MoE kernel) start early.
 template <typename WT>
-__global__ void __launch_bounds__(kGemvThreads) out_proj_kernel(const float* ao, int nq, const WT* wo, int D,
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) out_proj_kernel(const float* ao, int nq, const WT* wo, int D,
                                                                 float* x) {
     extern __shared__ __align__(16) float xs[];
+    uint4 q[kGemvUnroll];
+    prefetch_first_chunk<WT>(wo, nq, D, q);
     pdl_wait();
-    for (int i = threadIdx.x; i < nq; i += blockDim.x) xs[i] = __ldcg(ao + i);
+    float4 av[kMaxVec4];
+#pragma unroll
+    for (int k = 0; k < kMaxVec4; k++) {
+        const int i4 = threadIdx.x + k * kGemvThreads;
+        if (i4 < nq / 4) av[k] = __ldcg(reinterpret_cast<const float4*>(ao) + i4);
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxVec4; k++) {
+        const int i4 = threadIdx.x + k * kGemvThreads;
+        if (i4 < nq / 4) reinterpret_cast<float4*>(xs)[i4] = av[k];
+    }
     __syncthreads();
-    gemv_rows<WT>(xs, nq, wo, D, [&](int r, float v) { x[r] = __fadd_rn(x[r], v); });
+    gemv_rows<WT>(xs, nq, wo, D, q, [&](int r, float v) { x[r] = __fadd_rn(x[r], v); });
 }
 
 // ---------------------------------------------------------------- attention
@@ -169,34 +241,15 @@ struct AttnArgs {
     float eps, scale;
     const float* rope_cos;  // [ctx][head_dim / 2]
     const float* rope_sin;
-    float* kc;              // this layer's cache [ctx][nkv]
+    float* kc;              // this layer's cache, head-major [n_kv_heads][ctx][head_dim]
     float* vc;
     const Step* step;
     float* part;            // [n_heads][n_splits][head_dim + 2]: max, sum, weighted V
     float* ao;              // [nq] attention output
     unsigned* done;         // [n_heads] finished splits, zero between calls
-    int n_heads, n_kv_heads, hd, n_splits;
+    unsigned* status;       // error word
+    int n_heads, n_kv_heads, hd, ctx, n_splits;
 };
-
-// block-wide sum of v in a fixed order (every thread gets the total)
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();  // red is free
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.0f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
-    return t;
-}
-
-// rmsnorm factor of n floats at p (the QK-norm over the whole projection)
-__device__ __forceinline__ float rms_inv(const float* p, int n, float eps, float* red) {
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(p[i], p[i], ss);
-    const float tot = block_sum(ss, red);
-    return 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)n), eps));
-}
 
 // v[0..hd) of one head: QK-norm (inv, weights w or none) then RoPE at the table row
 __device__ __forceinline__ void norm_rope(float* v, const float* src, const float* w, float inv, const float* cs,
@@ -215,45 +268,114 @@ __device__ __forceinline__ void norm_rope(float* v, const float* src, const floa
 }
 
 // CTA (head h, split s) covers positions [s kSplit, min((s+1) kSplit, pos+1)).
+// The cached positions of the split (all below pos) are one contiguous run per
+// kv head: two bulk copies bring K and V into shared memory, issued before the
+// kernel waits for this token's q|k|v (the cache was written by earlier tokens).
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+    extern __shared__ __align__(128) float kv_s[];  // K [kSplit][hd] | V [kSplit][hd]
     __shared__ __align__(16) float qh[kMaxHeadDim], kn[kMaxHeadDim], vn[kMaxHeadDim];
     __shared__ float sc[kSplit];
-    __shared__ float red[kAttnThreads / 32];
+    __shared__ float red[kAttnThreads / 32], red2[kAttnThreads / 32];
+    __shared__ float s_m[kMaxSplits], s_w[kMaxSplits];
     __shared__ unsigned s_last;
-    pdl_wait();
+    __shared__ uint64_t bar;
     const int h = blockIdx.x, s = blockIdx.y, hd = a.hd;
-    const int pos = a.step->pos;
+    const int pos = a.step->pos;  // written by the graph's first copy, before every kernel of the token
     const int t0 = s * kSplit;
     if (t0 > pos) return;  // a split past the current position: no work, not counted
     const int t1 = min(t0 + kSplit, pos + 1);
+    const int nc = min(t1, pos) - t0;  // cached positions (position pos is this token's)
+    const int group = a.n_heads / a.n_kv_heads, kvh = h / group;
+    float* Ks = kv_s;
+    float* Vs = kv_s + (size_t)kSplit * hd;
+    const size_t run = ((size_t)kvh * a.ctx + t0) * hd;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        if (nc > 0) {
+            mbar_arrive_expect_tx(&bar, 2u * nc * hd * 4);
+            bulk_load(Ks, a.kc + run, (uint32_t)nc * hd * 4, &bar);
+            bulk_load(Vs, a.vc + run, (uint32_t)nc * hd * 4, &bar);
+        }
+    }
+    pdl_wait();
+    pdl_launch_dependents();
     const int nq = a.n_heads * hd, nkv = a.n_kv_heads * hd;
-    const int kvh = h / (a.n_heads / a.n_kv_heads);
     const int half = hd / 2;
     const float* cs = a.rope_cos + (size_t)pos * half;
     const float* sn = a.rope_sin + (size_t)pos * half;
-    // q of head h (rabbit2.c:477-482)
-    const float inv_q = a.q_norm ? rms_inv(a.qkv, nq, a.eps, red) : 1.0f;
+    // QK-norm factors of the whole q and k projections (rabbit2.c:477-480): one
+    // pass with every 16-byte load of q|k in flight, both sums reduced together
+    float inv_q = 1.0f, inv_k = 1.0f;
+    if (a.q_norm) {
+        const int nq4 = nq / 4, n4 = (nq + nkv) / 4;
+        float4 v[kAttnVec4];
+#pragma unroll
+        for (int k = 0; k < kAttnVec4; k++) {
+            const int i4 = threadIdx.x + k * kAttnThreads;
+            if (i4 < n4) v[k] = __ldcg(reinterpret_cast<const float4*>(a.qkv) + i4);
+        }
+        float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kAttnVec4; k++) {
+            const int i4 = threadIdx.x + k * kAttnThreads;
+            if (i4 < n4) {
+                float t = fmaf(v[k].x, v[k].x, 0.0f);
+                t = fmaf(v[k].y, v[k].y, t);
+                t = fmaf(v[k].z, v[k].z, t);
+                t = fmaf(v[k].w, v[k].w, t);
+                if (i4 < nq4) sq += t;
+                else sk += t;
+            }
+        }
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        if (lane == 0) {
+            red[warp] = sq;
+            red2[warp] = sk;
+        }
+        __syncthreads();  // (also publishes the barrier's initialisation)
+        float tq = 0.0f, tk = 0.0f;
+        for (int w = 0; w < kAttnThreads / 32; w++) {
+            tq += red[w];
+            tk += red2[w];
+        }
+        inv_q = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tq, (float)nq), a.eps));
+        inv_k = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tk, (float)nkv), a.eps));
+    }
+    // q of head h, and for the split that holds position pos this token's k and v
     norm_rope(qh, a.qkv + (size_t)h * hd, a.q_norm ? a.q_norm + (size_t)h * hd : nullptr, inv_q, cs, sn, hd);
-    const bool has_new = pos < t1;  // this split holds position pos: k, v of this token
+    const bool has_new = pos < t1;
     if (has_new) {
         const float* k = a.qkv + nq;
-        const float inv_k = a.k_norm ? rms_inv(k, nkv, a.eps, red) : 1.0f;
         norm_rope(kn, k + (size_t)kvh * hd, a.k_norm ? a.k_norm + (size_t)kvh * hd : nullptr, inv_k, cs, sn, hd);
         for (int i = threadIdx.x; i < hd; i += blockDim.x) vn[i] = a.qkv[nq + nkv + (size_t)kvh * hd + i];
     }
     __syncthreads();
-    if (has_new && h % (a.n_heads / a.n_kv_heads) == 0) {  // one head of the group stores them (:484-486)
-        float* kd = a.kc + (size_t)pos * nkv + (size_t)kvh * hd;
-        float* vd = a.vc + (size_t)pos * nkv + (size_t)kvh * hd;
+    if (has_new && h % group == 0) {  // one head of the group stores them (rabbit2.c:484-486)
+        const size_t at = ((size_t)kvh * a.ctx + pos) * hd;
         for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            kd[i] = kn[i];
-            vd[i] = vn[i];
+            a.kc[at + i] = kn[i];
+            a.vc[at + i] = vn[i];
+        }
+    }
+    if (nc > 0) {
+        const bool got = mbar_wait_bounded(&bar, 0, kWaitNs);
+        if (!__syncthreads_and(got)) {
+            // the copies are of valid memory and end; wait for them (bounded) before leaving
+            if (threadIdx.x == 0) {
+                record_error(a.status, 0x701);
+                (void)mbar_wait_bounded(&bar, 0, kWaitNs);
+            }
+            __syncthreads();
+            return;
         }
     }
     // scores (rabbit2.c:488-495): warp w takes positions t0 + w, t0 + w + 4, ...
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int t = t0 + warp; t < t1; t += nwarps) {
-        const float* kt = t == pos ? kn : a.kc + (size_t)t * nkv + (size_t)kvh * hd;
+        const float* kt = t == pos ? kn : Ks + (size_t)(t - t0) * hd;
         float d = 0.0f;
         for (int i = lane; i < hd; i += 32) d = fmaf(qh[i], kt[i], d);
         d = warp_sum(d);
@@ -272,11 +394,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     float* pp = a.part + ((size_t)h * a.n_splits + s) * (hd + 2);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float o = 0.0f;
-        for (int j = 0; j < n; j++) {
-            const int t = t0 + j;
-            const float v = t == pos ? vn[i] : a.vc[(size_t)t * nkv + (size_t)kvh * hd + i];
-            o = fmaf(sc[j], v, o);
-        }
+        for (int j = 0; j < nc; j++) o = fmaf(sc[j], Vs[(size_t)j * hd + i], o);
+        if (has_new) o = fmaf(sc[n - 1], vn[i], o);
         pp[2 + i] = o;
     }
     if (threadIdx.x == 0) {
@@ -298,22 +417,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     __threadfence();
     const int n_act = pos / kSplit + 1;
     const float* ph = a.part + (size_t)h * a.n_splits * (hd + 2);
-    float M = -INFINITY;
-    for (int j = 0; j < n_act; j++) M = fmaxf(M, __ldcg(ph + (size_t)j * (hd + 2)));
-    float L = 0.0f;
-    for (int j = 0; j < n_act; j++) {
-        const float* pj = ph + (size_t)j * (hd + 2);
-        L += __ldcg(pj + 1) * expf(__ldcg(pj) - M);
+    // every split's max and sum into shared memory (one load each, all in flight)
+    for (int j = threadIdx.x; j < n_act; j += blockDim.x) {
+        s_m[j] = __ldcg(ph + (size_t)j * (hd + 2));
+        s_w[j] = __ldcg(ph + (size_t)j * (hd + 2) + 1);
     }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int j = 0; j < n_act; j++) M = fmaxf(M, s_m[j]);
+    float L = 0.0f;
+    for (int j = 0; j < n_act; j++) L += s_w[j] * expf(s_m[j] - M);
+    __syncthreads();
+    for (int j = threadIdx.x; j < n_act; j += blockDim.x) s_w[j] = expf(s_m[j] - M);  // split weights
+    __syncthreads();
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float o = 0.0f;
-        for (int j = 0; j < n_act; j++) {
-            const float* pj = ph + (size_t)j * (hd + 2);
-            o = fmaf(__ldcg(pj + 2 + i), expf(__ldcg(pj) - M), o);
-        }
+#pragma unroll 8
+        for (int j = 0; j < n_act; j++) o = fmaf(__ldcg(ph + (size_t)j * (hd + 2) + 2 + i), s_w[j], o);
         a.ao[(size_t)h * hd + i] = o / L;
     }
 }
+
+size_t attn_smem_bytes(int hd) { return (size_t)2 * kSplit * hd * sizeof(float); }
 
 // ---------------------------------------------------------------- launches
 // Launch with programmatic stream serialization: each kernel calls
@@ -360,11 +485,13 @@ struct RbtModel {
     float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     int32_t* routing = nullptr;
     unsigned* done = nullptr;
+    unsigned* status = nullptr;  // attention's error word (a bounded wait that ran out)
     Step* step = nullptr;
     // pinned host staging
     Step* h_step = nullptr;
     float* h_logits = nullptr;
     int32_t* h_routing = nullptr;
+    unsigned* h_status = nullptr;
     // graphs: [0] without lm_head, [1] with
     cudaGraphExec_t graph[2] = {nullptr, nullptr};
     int n_splits = 0;
@@ -395,7 +522,7 @@ int enqueue_token(RbtModel* m, bool with_logits) {
     CU(cudaMemcpyAsync(m->step, m->h_step, sizeof(Step), cudaMemcpyHostToDevice, s));
     CU(launch_pdl(embed_kernel<WT>, dim3((D + 255) / 256), dim3(256), 0, s, (const WT*)m->tok_emb, D,
                   (const Step*)m->step, m->x));
-    const int gemv_grid = m->sm_count * 2;
+    const int gemv_grid = m->sm_count * kGemvCtasPerSm;
     for (int l = 0; l < c.n_layers; l++) {
         const RbtModel::Layer& L = m->layers[l];
         CU(launch_pdl(norm_gemv_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)D * 4, s,
@@ -415,17 +542,21 @@ int enqueue_token(RbtModel* m, bool with_logits) {
         a.part = m->part;
         a.ao = m->ao;
         a.done = m->done;
+        a.status = m->status;
+        a.ctx = m->ctx;
         a.n_heads = c.n_heads;
         a.n_kv_heads = c.n_kv_heads;
         a.hd = c.head_dim;
         a.n_splits = m->n_splits;
-        CU(launch_pdl(attn_decode_kernel, dim3(c.n_heads, m->n_splits), dim3(kAttnThreads), 0, s, a));
+        CU(launch_pdl(attn_decode_kernel, dim3(c.n_heads, m->n_splits), dim3(kAttnThreads),
+                      attn_smem_bytes(c.head_dim), s, a));
         CU(launch_pdl(out_proj_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)nq * 4, s, (const float*)m->ao,
                       nq, (const WT*)L.wo, D, m->x));
         if (!rbt_moe_block_device(m->moe, l, m->x, 1, m->routing + (size_t)l * c.top_k, c.top_k, (void*)s))
             return 0;
     }
     CU(cudaMemcpyAsync(m->h_routing, m->routing, sizeof(int32_t) * c.n_layers * c.top_k, cudaMemcpyDeviceToHost, s));
+    CU(cudaMemcpyAsync(m->h_status, m->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
     if (with_logits) {
         CU(launch_pdl(norm_gemv_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)D * 4, s,
                       (const float*)m->x, (const float*)m->final_norm, c.rms_eps, D, (const WT*)m->lm_head, c.vocab,
@@ -468,14 +599,18 @@ int init_state(RbtModel* m) {
         !dalloc(&m->logits, (size_t)c.vocab * 4) || !dalloc(&m->kc, kv) || !dalloc(&m->vc, kv) ||
         !dalloc(&m->rope_cos, (size_t)ctx * half * 4) || !dalloc(&m->rope_sin, (size_t)ctx * half * 4) ||
         !dalloc(&m->routing, (size_t)c.n_layers * c.top_k * 4) || !dalloc(&m->done, (size_t)c.n_heads * 4) ||
-        !dalloc(&m->step, sizeof(Step)))
+        !dalloc(&m->step, sizeof(Step)) || !dalloc(&m->status, sizeof(unsigned)))
         return 0;
+    CU(cudaMemset(m->status, 0, sizeof(unsigned)));
+    CU(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)attn_smem_bytes(c.head_dim)));
     CU(cudaMemset(m->kc, 0, kv));
     CU(cudaMemset(m->vc, 0, kv));
     CU(cudaMemset(m->done, 0, (size_t)c.n_heads * 4));
     CU(cudaMallocHost((void**)&m->h_step, sizeof(Step)));
     CU(cudaMallocHost((void**)&m->h_logits, (size_t)c.vocab * 4));
     CU(cudaMallocHost((void**)&m->h_routing, (size_t)c.n_layers * c.top_k * 4));
+    CU(cudaMallocHost((void**)&m->h_status, sizeof(unsigned)));
     // the engine's RoPE angles (rope(), rabbit2.c:410-421): fp64 pow/cos/sin rounded to f32
     std::vector<float> cs((size_t)ctx * half), sn((size_t)ctx * half);
     for (int p = 0; p < ctx; p++)
@@ -502,10 +637,15 @@ int rbt_model_create(RbtModel** out, const RbtModelConfig* cfg, int ctx, int dev
         return fail("invalid config: dims must be positive");
     if (c.dtype != RBT_MOE_DT_F32 && c.dtype != RBT_MOE_DT_BF16) return fail("dtype must be 0 (f32) or 1 (bf16)");
     if (c.n_heads % c.n_kv_heads) return fail("n_heads %d is not a multiple of n_kv_heads %d", c.n_heads, c.n_kv_heads);
-    if (c.head_dim % 2 || c.head_dim > kMaxHeadDim) return fail("head_dim %d must be even and <= %d", c.head_dim, kMaxHeadDim);
+    if (c.head_dim % 4 || c.head_dim > kMaxHeadDim)  // 16-byte runs of the KV cache for the bulk copies
+        return fail("head_dim %d must be a multiple of 4 and <= %d", c.head_dim, kMaxHeadDim);
     const int vec = c.dtype == RBT_MOE_DT_BF16 ? 8 : 4;  // elements per 16-byte load
     if (c.dim % vec || nq_of(c) % vec) return fail("dim and n_heads*head_dim must be multiples of %d", vec);
     if (ctx <= 0 || ctx > c.max_seq) return fail("ctx %d out of range [1, max_seq %d]", ctx, c.max_seq);
+    if (ctx > kMaxSplits * kSplit) return fail("ctx %d above the supported %d", ctx, kMaxSplits * kSplit);
+    if (c.dim > kMaxVec4 * 4 * kGemvThreads || nq_of(c) > kMaxVec4 * 4 * kGemvThreads ||
+        nq_of(c) + nkv_of(c) > kAttnVec4 * 4 * kAttnThreads)
+        return fail("dim and n_heads*head_dim must be <= %d", kMaxVec4 * 4 * kGemvThreads);
     RbtMoeConfig mc;
     mc.dim = c.dim;
     mc.n_experts = c.n_experts;
@@ -555,11 +695,12 @@ void rbt_model_destroy(RbtModel* m) {
     cudaFree(m->lm_head);
     cudaFree(m->final_norm);
     void* bufs[] = {m->x, m->qkv, m->part, m->ao, m->logits, m->kc, m->vc, m->rope_cos, m->rope_sin, m->routing,
-                    m->done, m->step};
+                    m->done, m->step, m->status};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_step);
     cudaFreeHost(m->h_logits);
     cudaFreeHost(m->h_routing);
+    cudaFreeHost(m->h_status);
     if (m->stream) cudaStreamDestroy(m->stream);
     rbt_moe_destroy(m->moe);
     delete m;
@@ -621,6 +762,11 @@ int rbt_model_forward(RbtModel* m, int token, int pos, float* logits, int32_t* r
     m->h_step->pos = pos;
     CU(cudaGraphLaunch(m->graph[with], m->stream));
     CU(cudaStreamSynchronize(m->stream));
+    if (*m->h_status) {
+        const unsigned st = *m->h_status;
+        CU(cudaMemset(m->status, 0, sizeof(unsigned)));
+        return fail("attention: a bounded wait for the KV tiles ran out (code 0x%x)", st);
+    }
     if (!moe_status_ok(m->moe)) return 0;
     if (logits) memcpy(logits, m->h_logits, sizeof(float) * c.vocab);
     if (routing_out) memcpy(routing_out, m->h_routing, sizeof(int32_t) * c.n_layers * c.top_k);

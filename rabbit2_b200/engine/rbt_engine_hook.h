@@ -7,7 +7,11 @@
  * defined above forward()).  Call sites:
  *   main(), argument loop:  --device cpu|cuda   sets rbt_engine_device
  *                           --prefill batch|token   sets rbt_engine_prefill_mode
+ *                           --offload moe|all       sets rbt_engine_offload
  *   main(), after load_model():  rbt_engine_init(&m)
+ *   forward(), first statement (rabbit2.c:455):
+ *       { int g = rbt_engine_forward(m, s, token, pos, routing_out);
+ *         if (g < 0) return 0; if (g) return 1; }
  *   forward(), first line of the MoE block (rabbit2.c:511):
  *       { int g = rbt_engine_moe(m, l, s->x, routing_out + (size_t)l * c->top_k);
  *         if (g < 0) return 0; if (g) continue; }
@@ -19,6 +23,8 @@
  * With --device cuda every layer's router and expert blobs are copied once from
  * the mapped file into HBM, and each MoE block is one rbt_moe_block() call that
  * returns x updated in place and the layer's routing row, as the CPU block does.
+ * With --device cuda --offload all every weight is copied, and each forward() is
+ * one rbt_model_forward() call (attention and lm_head on the GPU as well).
  */
 #ifndef RBT_ENGINE_HOOK_H
 #define RBT_ENGINE_HOOK_H
@@ -27,12 +33,18 @@
 
 static const char *rbt_engine_device = NULL;
 static const char *rbt_engine_prefill_mode = NULL;  /* --prefill batch|token */
+static const char *rbt_engine_offload = NULL;       /* --offload moe|all */
 static RbtMoe *rbt_engine_ctx = NULL;
+static RbtModel *rbt_engine_model = NULL;           /* --offload all: the whole forward() */
 
 static int rbt_engine_init(Model *m) {
     if (rbt_engine_prefill_mode && strcmp(rbt_engine_prefill_mode, "batch") != 0 &&
         strcmp(rbt_engine_prefill_mode, "token") != 0) {
         fprintf(stderr, "--prefill must be batch or token\n");
+        return 0;
+    }
+    if (rbt_engine_offload && strcmp(rbt_engine_offload, "moe") != 0 && strcmp(rbt_engine_offload, "all") != 0) {
+        fprintf(stderr, "--offload must be moe or all\n");
         return 0;
     }
     if (!rbt_engine_device || !strcmp(rbt_engine_device, "cpu")) return 1;
@@ -41,6 +53,40 @@ static int rbt_engine_init(Model *m) {
         return 0;
     }
     const Config *c = &m->c;
+    if (rbt_engine_offload && !strcmp(rbt_engine_offload, "all")) {
+        /* every weight and a KV cache of max_seq positions in HBM (the engine
+           picks its --ctx later; it never exceeds max_seq) */
+        RbtModelConfig mc;
+        mc.vocab = c->vocab;
+        mc.dim = c->dim;
+        mc.n_layers = c->n_layers;
+        mc.n_heads = c->n_heads;
+        mc.n_kv_heads = c->n_kv_heads;
+        mc.head_dim = c->head_dim;
+        mc.n_experts = c->n_experts;
+        mc.top_k = c->top_k;
+        mc.expert_hidden = c->expert_hidden;
+        mc.max_seq = c->max_seq;
+        mc.dtype = c->dtype;
+        mc.qk_norm = c->qk_norm;
+        mc.norm_topk = c->norm_topk;
+        mc.rope_theta = c->rope_theta;
+        mc.rms_eps = c->rms_eps;
+        mc.expert_stride = (uint64_t)m->expert_stride;
+        if (!rbt_model_create(&rbt_engine_model, &mc, c->max_seq, 0)) return 0;
+        if (!rbt_model_load_globals(rbt_engine_model, MAT(m, m->tok_emb), VEC(m, m->final_norm), MAT(m, m->lm_head)))
+            return 0;
+        for (int l = 0; l < c->n_layers; l++) {
+            const LayerOff *ly = &m->layers[l];
+            if (!rbt_model_load_layer(rbt_engine_model, l, VEC(m, ly->attn_norm), MAT(m, ly->wq), MAT(m, ly->wk),
+                                      MAT(m, ly->wv), MAT(m, ly->wo), c->qk_norm ? VEC(m, ly->q_norm) : NULL,
+                                      c->qk_norm ? VEC(m, ly->k_norm) : NULL, VEC(m, ly->ffn_norm),
+                                      MAT(m, ly->router), m->map.base + ly->experts))
+                return 0;
+        }
+        fprintf(stderr, "forward device: cuda (librbt_moe, whole model resident)\n");
+        return 1;
+    }
     RbtMoeConfig cfg;
     cfg.dim = c->dim;
     cfg.n_experts = c->n_experts;
@@ -60,6 +106,15 @@ static int rbt_engine_init(Model *m) {
     }
     fprintf(stderr, "moe device: cuda (librbt_moe, %d layers resident)\n", c->n_layers);
     return 1;
+}
+
+/* --offload all: forward() for one token on the GPU, s->logits and the routing
+ * rows filled as the engine's own forward() fills them.  1: done; 0: not
+ * enabled (run the engine's forward); -1: error. */
+static int rbt_engine_forward(Model *m, State *s, int token, int pos, int32_t *routing_out) {
+    (void)m;
+    if (!rbt_engine_model) return 0;
+    return rbt_model_forward(rbt_engine_model, token, pos, s->logits, routing_out) ? 1 : -1;
 }
 
 /* 1: the GPU ran the block; 0: not enabled (run the CPU block); -1: error. */

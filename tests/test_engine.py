@@ -88,6 +88,13 @@ def test_bad_prefill_mode_is_rejected(tiny_model):
 
 
 @needs_bins
+def test_bad_offload_is_rejected(tiny_model):
+    model, _, prompt = tiny_model
+    p = subprocess.run([CUDA, model, "--gen", "1", "--offload", "attn", "1"], capture_output=True, text=True)
+    assert p.returncode == 1 and "--offload" in p.stderr
+
+
+@needs_bins
 def test_bad_device_is_rejected(tiny_model):
     model, _, prompt = tiny_model
     p = subprocess.run([CUDA, model, "--gen", "1", "--device", "tpu", "1"], capture_output=True, text=True)
@@ -139,3 +146,22 @@ def test_gpu_batched_prefill_bf16_matches_reference(tiny_model_bf16, tmp_path):
     for got in (gl, tl):
         err = np.abs(got.astype(np.float64) - wl).max() / np.abs(wl).max()
         assert err < 1e-3, err
+
+
+@needs_bins
+@pytest.mark.gpu
+@pytest.mark.parametrize("which", ["f32", "bf16"])
+def test_gpu_whole_forward_engine_matches_reference(tiny_model, tiny_model_bf16, tmp_path, which):
+    """--offload all: every forward() is one rbt_model_forward call (attention,
+    MoE and lm_head on the GPU); same bars as the MoE-only runs."""
+    model, cfg, prompt = tiny_model if which == "f32" else tiny_model_bf16
+    extra = ["--device", "cuda", "--offload", "all"]
+    want_ids, _ = gen(REF, model, prompt, 64)
+    got_ids, log = gen(CUDA, model, prompt, 64, extra)
+    assert "forward device: cuda" in log
+    assert got_ids == want_ids
+    wl, wr, _ = dump(REF, model, prompt, str(tmp_path))
+    gl, gr, _ = dump(CUDA, model, prompt, str(tmp_path), extra)
+    np.testing.assert_array_equal(gr, wr)
+    err = np.abs(gl.astype(np.float64) - wl).max() / np.abs(wl).max()
+    assert err < 1e-3, err
