@@ -251,22 +251,6 @@ struct AttnArgs {
     int n_heads, n_kv_heads, hd, ctx, n_splits;
 };
 
-// v[0..hd) of one head: QK-norm (inv, weights w or none) then RoPE at the table row
-__device__ __forceinline__ void norm_rope(float* v, const float* src, const float* w, float inv, const float* cs,
-                                          const float* sn, int hd) {
-    const int half = hd / 2;
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        float a = src[i], b = src[i + half];
-        if (w) {
-            a = __fmul_rn(__fmul_rn(a, inv), w[i]);
-            b = __fmul_rn(__fmul_rn(b, inv), w[i + half]);
-        }
-        // rope(): p[i] = a cs - b sn, p[i + half] = b cs + a sn (rabbit2.c:418-419)
-        v[i] = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
-        v[i + half] = __fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i]));
-    }
-}
-
 // CTA (head h, split s) covers positions [s kSplit, min((s+1) kSplit, pos+1)).
 // The cached positions of the split (all below pos) are one contiguous run per
 // kv head: two bulk copies bring K and V into shared memory, issued before the
@@ -298,14 +282,41 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
             bulk_load(Vs, a.vc + run, (uint32_t)nc * hd * 4, &bar);
         }
     }
+    const int nq = a.n_heads * hd, nkv = a.n_kv_heads * hd;
+    const int half = hd / 2, i = threadIdx.x;  // thread i < half owns the pair (i, i + half)
+    const bool has_new = pos < t1;  // this split holds position pos: k and v of this token
+    // static inputs before the wait: the RoPE row of pos and the QK-norm weights
+    float cs = 0.0f, sn = 0.0f, wqa = 1.0f, wqb = 1.0f, wka = 1.0f, wkb = 1.0f;
+    if (i < half) {
+        cs = a.rope_cos[(size_t)pos * half + i];
+        sn = a.rope_sin[(size_t)pos * half + i];
+        if (a.q_norm) {
+            wqa = a.q_norm[(size_t)h * hd + i];
+            wqb = a.q_norm[(size_t)h * hd + i + half];
+            wka = a.k_norm[(size_t)kvh * hd + i];
+            wkb = a.k_norm[(size_t)kvh * hd + i + half];
+        }
+    }
     pdl_wait();
     pdl_launch_dependents();
-    const int nq = a.n_heads * hd, nkv = a.n_kv_heads * hd;
-    const int half = hd / 2;
-    const float* cs = a.rope_cos + (size_t)pos * half;
-    const float* sn = a.rope_sin + (size_t)pos * half;
-    // QK-norm factors of the whole q and k projections (rabbit2.c:477-480): one
-    // pass with every 16-byte load of q|k in flight, both sums reduced together
+    // this token's inputs in one round of loads: the head's q pair, the k pair and
+    // v of its kv head, and for the QK-norm all of q|k (16-byte loads)
+    float qa = 0.0f, qb = 0.0f, ka = 0.0f, kb = 0.0f, va = 0.0f, vb = 0.0f;
+    if (i < half) {
+        qa = __ldcg(a.qkv + (size_t)h * hd + i);
+        qb = __ldcg(a.qkv + (size_t)h * hd + i + half);
+        if (has_new) {
+            ka = __ldcg(a.qkv + nq + (size_t)kvh * hd + i);
+            kb = __ldcg(a.qkv + nq + (size_t)kvh * hd + i + half);
+        }
+    }
+    if (has_new) {
+        const float* v = a.qkv + nq + nkv + (size_t)kvh * hd;
+        if (i < hd) va = __ldcg(v + i);
+        if (i + kAttnThreads < hd) vb = __ldcg(v + i + kAttnThreads);
+    }
+    // QK-norm factors of the whole q and k projections (rabbit2.c:477-480), both
+    // sums reduced together
     float inv_q = 1.0f, inv_k = 1.0f;
     if (a.q_norm) {
         const int nq4 = nq / 4, n4 = (nq + nkv) / 4;
@@ -335,7 +346,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
             red[warp] = sq;
             red2[warp] = sk;
         }
-        __syncthreads();  // (also publishes the barrier's initialisation)
+        __syncthreads();
         float tq = 0.0f, tk = 0.0f;
         for (int w = 0; w < kAttnThreads / 32; w++) {
             tq += red[w];
@@ -344,15 +355,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         inv_q = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tq, (float)nq), a.eps));
         inv_k = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tk, (float)nkv), a.eps));
     }
-    // q of head h, and for the split that holds position pos this token's k and v
-    norm_rope(qh, a.qkv + (size_t)h * hd, a.q_norm ? a.q_norm + (size_t)h * hd : nullptr, inv_q, cs, sn, hd);
-    const bool has_new = pos < t1;
-    if (has_new) {
-        const float* k = a.qkv + nq;
-        norm_rope(kn, k + (size_t)kvh * hd, a.k_norm ? a.k_norm + (size_t)kvh * hd : nullptr, inv_k, cs, sn, hd);
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) vn[i] = a.qkv[nq + nkv + (size_t)kvh * hd + i];
+    // QK-norm (x * inv * w, rmsnorm of rabbit2.c:392-397), then RoPE:
+    // p[i] = a cs - b sn, p[i + half] = b cs + a sn (rabbit2.c:418-419)
+    if (i < half) {
+        if (a.q_norm) {
+            qa = __fmul_rn(__fmul_rn(qa, inv_q), wqa);
+            qb = __fmul_rn(__fmul_rn(qb, inv_q), wqb);
+            ka = __fmul_rn(__fmul_rn(ka, inv_k), wka);
+            kb = __fmul_rn(__fmul_rn(kb, inv_k), wkb);
+        }
+        qh[i] = __fsub_rn(__fmul_rn(qa, cs), __fmul_rn(qb, sn));
+        qh[i + half] = __fadd_rn(__fmul_rn(qb, cs), __fmul_rn(qa, sn));
+        if (has_new) {
+            kn[i] = __fsub_rn(__fmul_rn(ka, cs), __fmul_rn(kb, sn));
+            kn[i + half] = __fadd_rn(__fmul_rn(kb, cs), __fmul_rn(ka, sn));
+        }
     }
-    __syncthreads();
+    if (has_new) {
+        if (i < hd) vn[i] = va;
+        if (i + kAttnThreads < hd) vn[i + kAttnThreads] = vb;
+    }
+    __syncthreads();  // (also publishes the mbarrier's initialisation)
     if (has_new && h % group == 0) {  // one head of the group stores them (rabbit2.c:484-486)
         const size_t at = ((size_t)kvh * a.ctx + pos) * hd;
         for (int i = threadIdx.x; i < hd; i += blockDim.x) {
@@ -392,12 +415,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     float l = 0.0f;
     for (int j = 0; j < n; j++) l += sc[j];
     float* pp = a.part + ((size_t)h * a.n_splits + s) * (hd + 2);
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    const bool only = pos < kSplit;  // one split: it is the whole softmax, no merge
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
         float o = 0.0f;
-        for (int j = 0; j < nc; j++) o = fmaf(sc[j], Vs[(size_t)j * hd + i], o);
-        if (has_new) o = fmaf(sc[n - 1], vn[i], o);
-        pp[2 + i] = o;
+        for (int j = 0; j < nc; j++) o = fmaf(sc[j], Vs[(size_t)j * hd + c], o);
+        if (has_new) o = fmaf(sc[n - 1], vn[c], o);
+        if (only)
+            a.ao[(size_t)h * hd + c] = o / l;
+        else
+            pp[2 + c] = o;
     }
+    if (only) return;
     if (threadIdx.x == 0) {
         pp[0] = mx;
         pp[1] = l;
