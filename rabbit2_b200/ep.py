@@ -5,9 +5,10 @@ router.  For its own tokens each GPU
   1. routes them (rmsnorm + exact router + top-k: rbt_moe_route_device),
   2. plans the dispatch: a token goes to every GPU that owns at least one of its
      top-k experts, once per GPU (rbt_ep_plan),
-  3. exchanges the per-GPU row counts, then the token rows, their expert ids
-     (local to the receiving GPU, -1 for slots computed elsewhere) and their
-     combine weights (NCCL all-to-all, rbt_ep_pack builds the send buffers),
+  3. exchanges the per-GPU row counts, then the token rows together with their
+     expert ids (local to the receiving GPU, -1 for slots computed elsewhere) and
+     combine weights, as one [rows, D + 2K] f32 all-to-all (the ids travel as
+     their bit patterns; rbt_ep_pack builds the send buffers),
   4. runs its experts on the rows it received: one partial output row per row,
      the weighted sum over its own slots in selection order
      (rbt_moe_experts_device),
@@ -119,12 +120,13 @@ class ExpertParallelMoe:
         send_wt = torch.empty((n_send, K), dtype=torch.float32, device=dev)
         if T:
             o.pack(xb, idx, wt, pos, counts, send_rows, send_idx, send_wt)
-        recv_rows = torch.empty((n_recv, D), dtype=torch.float32, device=dev)
-        recv_idx = torch.empty((n_recv, K), dtype=torch.int32, device=dev)
-        recv_wt = torch.empty((n_recv, K), dtype=torch.float32, device=dev)
-        self._a2a(recv_rows, send_rows, recv_splits, send_splits)
-        self._a2a(recv_idx, send_idx, recv_splits, send_splits)
-        self._a2a(recv_wt, send_wt, recv_splits, send_splits)
+        # one exchange for a row, its expert ids (their bits carried as f32) and its weights
+        send = torch.cat([send_rows, send_idx.view(torch.float32), send_wt], dim=1)
+        recv = torch.empty((n_recv, D + 2 * K), dtype=torch.float32, device=dev)
+        self._a2a(recv, send, recv_splits, send_splits)
+        recv_rows = recv[:, :D].contiguous()
+        recv_idx = recv[:, D:D + K].contiguous().view(torch.int32)
+        recv_wt = recv[:, D + K:].contiguous()
         partial = torch.empty((n_recv, D), dtype=torch.float32, device=dev)
         if n_recv:
             o.experts(layer, recv_rows, recv_idx, recv_wt, partial)
