@@ -58,9 +58,10 @@ def parse():
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="moe", choices=["moe", "model-decode"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "model-decode", "model-prefill"],
                     help="moe: the MoE stack (the metric's config); model-decode: the whole forward() of an "
-                         "OLMoE-1B-7B-shaped model, batch-1 greedy decode (config 3)")
+                         "OLMoE-1B-7B-shaped model, batch-1 greedy decode (config 3); model-prefill: the same "
+                         "model's prompt of --prompt tokens in one rbt_model_prefill call (config 4, one sequence)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=256)
     return ap.parse_args()
@@ -611,7 +612,80 @@ def run_ours(args, rank, world, local_rank):
     return out
 
 
-# ----------------------------------------------------------------------------- config 3
+# ----------------------------------------------------------------------------- configs 3 and 4
+
+def olmoe_model(args, ctx_len):
+    """A random-init OLMoE-1B-7B-shaped model (args.layers layers, vocab 50304, bf16
+    weights ~N(0, 0.02) from a seeded GPU generator, norms 1) uploaded into an
+    RbtModel with a KV cache of ctx_len positions."""
+    import torch
+
+    from rabbit2_b200 import model as model_mod
+    from rabbit2_b200.rbt2fmt import DT_BF16, ModelConfig, layout
+    cfg = ModelConfig(vocab=50304, dim=D, n_layers=args.layers, n_heads=16, n_kv_heads=16, head_dim=128,
+                      n_experts=E, top_k=K, expert_hidden=H, max_seq=max(4096, ctx_len), dtype=DT_BF16, qk_norm=1,
+                      norm_topk=0, rope_theta=10000.0, rms_eps=1e-5)
+    m = model_mod.ModelContext(cfg, ctx=ctx_len)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+
+    def mat(rows, cols):  # generated on the GPU, uploaded from host memory
+        return (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16).cpu()
+
+    lib, h = m.lib, m.handle
+    ones = np.ones(max(D, 16 * 128), np.float32)
+    emb, head = mat(cfg.vocab, D), mat(cfg.vocab, D)
+    m._call(lib.rbt_model_load_globals, h, emb.data_ptr(), ones.ctypes.data, head.data_ptr())
+    del emb, head
+    assert layout(cfg)["expert_stride"] == 3 * H * D * 2
+    for l in range(cfg.n_layers):
+        wq, wk, wv, wo, router = mat(2048, D), mat(2048, D), mat(2048, D), mat(D, 2048), mat(E, D)
+        experts = mat(E, 3 * H * D)
+        m._call(lib.rbt_model_load_layer, h, l, ones.ctypes.data, wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
+                wo.data_ptr(), ones.ctypes.data, ones.ctypes.data, ones.ctypes.data, router.data_ptr(),
+                experts.data_ptr())
+        del wq, wk, wv, wo, router, experts
+    return cfg, m
+
+
+def run_model_prefill(args):
+    """Config 4's unit of work on one GPU: one sequence of --prompt uniform-random
+    tokens through the whole model in one rbt_model_prefill call (host tokens in,
+    the last token's logits and every routing row out).  value = prompt tokens
+    per second of wall clock around the call, averaged over --steps calls after
+    --warmup (each call rewrites the same cache positions)."""
+    cfg, m = olmoe_model(args, args.prompt)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
+    for _ in range(max(1, args.warmup)):
+        m.prefill(prompt, 0, logit_rows=1)
+    times = []
+    with ClockSampler(0) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            m.prefill(prompt, 0, logit_rows=1)
+            times.append(time.perf_counter() - t0)
+    m.close()
+    dt = statistics.mean(times)
+    T, L = args.prompt, cfg.n_layers
+    nq = nkv = 16 * 128
+    flops = {"attention projections": 2 * T * L * (nq + 2 * nkv + nq) * D,
+             "attention scores and values (causal)": 2 * 2 * L * 16 * 128 * T * (T + 1) / 2,
+             "moe": T * L * (2 * E * D + 6 * K * H * D), "lm_head (last token)": 2 * cfg.vocab * D}
+    total = sum(flops.values())
+    _, tf, src = peaks()
+    return {"metric": "olmoe1b7b_full_model_prefill_tok_per_s", "value": T / dt, "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": max(1, args.warmup), "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config4_olmoe1b7b_full_model_prefill_one_sequence", "layers": L,
+                       "prompt": T, "vocab": cfg.vocab, "dim": D, "heads": 16, "head_dim": 128,
+                       "n_experts": E, "top_k": K, "expert_hidden": H,
+                       "weights": "bf16 ~N(0,0.02) seeded (norms 1)",
+                       "timing": "wall clock per rbt_model_prefill call"},
+            "clocks": clocks.summary(),
+            "roofline": {"bound": "tensor", "achieved": total / dt / 1e12, "peak": tf, "unit": "TFLOP/s",
+                         "frac": total / dt / 1e12 / tf, "peak_source": src, "flops_per_step": total,
+                         "flops_parts": flops, "traffic": None}}
+
 
 def run_model_decode(args):
     """Config 3: the whole forward() (rbt_model_forward: attention, MoE, lm_head) of a
@@ -620,35 +694,7 @@ def run_model_decode(args):
     --gen loop does (logits to the host, argmax there).  value = generated tokens
     per second of wall clock around the calls (host round trip per token
     included); prefill_tok_s is the prompt fed token by token."""
-    import torch
-
-    from rabbit2_b200 import model as model_mod
-    from rabbit2_b200.rbt2fmt import DT_BF16, ModelConfig, layout
-    cfg = ModelConfig(vocab=50304, dim=D, n_layers=args.layers, n_heads=16, n_kv_heads=16, head_dim=128,
-                      n_experts=E, top_k=K, expert_hidden=H, max_seq=4096, dtype=DT_BF16, qk_norm=1,
-                      norm_topk=0, rope_theta=10000.0, rms_eps=1e-5)
-    ctx_len = args.prompt + args.gen
-    m = model_mod.ModelContext(cfg, ctx=ctx_len)
-    g = torch.Generator(device="cuda")
-    g.manual_seed(0)
-
-    def mat(rows, cols):  # bf16 ~N(0, 0.02), generated on the GPU, uploaded from host memory
-        return (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16).cpu()
-
-    lib, h = m.lib, m.handle
-    ones = np.ones(max(D, 16 * 128), np.float32)
-    emb, head = mat(cfg.vocab, D), mat(cfg.vocab, D)
-    m._call(lib.rbt_model_load_globals, h, emb.data_ptr(), ones.ctypes.data, head.data_ptr())
-    del emb, head
-    stride = layout(cfg)["expert_stride"]
-    assert stride == 3 * H * D * 2
-    for l in range(cfg.n_layers):
-        wq, wk, wv, wo, router = mat(2048, D), mat(2048, D), mat(2048, D), mat(D, 2048), mat(E, D)
-        experts = mat(E, 3 * H * D)
-        m._call(lib.rbt_model_load_layer, h, l, ones.ctypes.data, wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
-                wo.data_ptr(), ones.ctypes.data, ones.ctypes.data, ones.ctypes.data, router.data_ptr(),
-                experts.data_ptr())
-        del wq, wk, wv, wo, router, experts
+    cfg, m = olmoe_model(args, args.prompt + args.gen)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
     # warm-up: graph capture and first launches (positions are rewritten below)
     for p in range(min(3, args.prompt)):
@@ -695,6 +741,9 @@ def main():
     args = parse()
     if args.workload == "model-decode":
         print(json.dumps(run_model_decode(args)), flush=True)
+        return
+    if args.workload == "model-prefill":
+        print(json.dumps(run_model_prefill(args)), flush=True)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -251,6 +251,17 @@ int rbt_model_load_layer(RbtModel *m, int layer, const float *attn_norm, const v
  * s->logits and routing rows. */
 int rbt_model_forward(RbtModel *m, int token, int pos, float *logits, int32_t *routing_out);
 
+/* The prompt loop of the engine's main() (rabbit2.c:703-714) in one call:
+ * forward() for tokens[0..n_tokens) at positions pos0 .. pos0 + n_tokens, run
+ * layer by layer over all of them (the projections as GEMMs, the MoE blocks on
+ * the tensor-core path).  logits [logit_rows, vocab] (host) receive the logits of
+ * the LAST logit_rows tokens (0: none; 1: what the sampler reads; n_tokens: every
+ * row, as --dump writes them); routing_out [n_tokens, n_layers, top_k] (host) or
+ * NULL.  The KV cache is the one rbt_model_forward uses: decoding continues at
+ * pos0 + n_tokens.  Needs head_dim 64 or 128. */
+int rbt_model_prefill(RbtModel *m, const int32_t *tokens, int n_tokens, int pos0, float *logits, int logit_rows,
+                      int32_t *routing_out);
+
 /* Last error message of the calling thread ("" if none). */
 const char *rbt_moe_last_error(void);
 

@@ -41,6 +41,7 @@
 #include "../../include/rbt_moe.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "model_internal.h"
 #include "tc_ptx.cuh"
 
 namespace rbt {
@@ -52,6 +53,7 @@ namespace {
 
 using namespace rbt;
 using namespace rbt::tc;
+using rbt::Step;
 
 int fail(const char* fmt, ...) {
     char buf[512];
@@ -81,10 +83,6 @@ constexpr int kMaxHeadDim = 256;
 constexpr int kAttnVec4 = 16;    // float4s of q|k per attention thread: nq + nkv <= 8192
 constexpr int kMaxSplits = 128;  // ctx <= kMaxSplits x kSplit
 constexpr uint64_t kWaitNs = 2000000000ull;
-
-struct Step {
-    int token, pos;
-};
 
 __device__ __forceinline__ void record_error(unsigned* status, unsigned code) { atomicCAS(status, 0u, code); }
 
@@ -488,42 +486,6 @@ cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t 
 
 }  // namespace
 
-struct RbtModel {
-    RbtModelConfig cfg{};
-    int ctx = 0, device = 0, sm_count = 0;
-    RbtMoe* moe = nullptr;
-    cudaStream_t stream = nullptr;
-    size_t esz = 0;
-    // weights
-    void* tok_emb = nullptr;
-    void* lm_head = nullptr;
-    float* final_norm = nullptr;
-    struct Layer {
-        float* attn_norm = nullptr;
-        float* q_norm = nullptr;
-        float* k_norm = nullptr;
-        void* wqkv = nullptr;  // [wq; wk; wv] rows, contiguous
-        void* wo = nullptr;
-        bool loaded = false;
-    };
-    std::vector<Layer> layers;
-    bool globals = false;
-    // state
-    float *x = nullptr, *qkv = nullptr, *part = nullptr, *ao = nullptr, *logits = nullptr;
-    float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
-    int32_t* routing = nullptr;
-    unsigned* done = nullptr;
-    unsigned* status = nullptr;  // attention's error word (a bounded wait that ran out)
-    Step* step = nullptr;
-    // pinned host staging
-    Step* h_step = nullptr;
-    float* h_logits = nullptr;
-    int32_t* h_routing = nullptr;
-    unsigned* h_status = nullptr;
-    // graphs: [0] without lm_head, [1] with
-    cudaGraphExec_t graph[2] = {nullptr, nullptr};
-    int n_splits = 0;
-};
 
 namespace {
 
@@ -729,6 +691,7 @@ void rbt_model_destroy(RbtModel* m) {
     cudaFreeHost(m->h_logits);
     cudaFreeHost(m->h_routing);
     cudaFreeHost(m->h_status);
+    rbt::prefill_free(m);
     if (m->stream) cudaStreamDestroy(m->stream);
     rbt_moe_destroy(m->moe);
     delete m;

@@ -1,0 +1,79 @@
+// model_internal.h -- the RbtModel context shared by model.cu (one-token forward)
+// and model_prefill.cu (the batched prompt); not part of the C ABI.
+#pragma once
+
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/rbt_moe.h"
+
+namespace rbt {
+
+struct Step {
+    int token, pos;
+};
+
+// Row buffers of the batched prompt, for `cap` tokens.
+struct PrefillBufs {
+    int cap = 0;
+    int32_t* tokens = nullptr;  // [cap]
+    float* x = nullptr;         // [cap, dim] residual rows
+    float* qkv = nullptr;       // [cap, nq + 2 nkv]
+    float* ao = nullptr;        // [cap, nq] attention output
+    float* xf = nullptr;        // [cap, max(dim, nq)] f32 GEMM input rows (f32 models)
+    void* hi = nullptr;         // [cap, max(dim, nq)] bf16 GEMM input rows, x = hi + lo (bf16 models)
+    void* lo = nullptr;
+    int32_t* routing = nullptr; // [cap, n_layers, top_k]
+    int logit_rows = 0;
+    float* logits = nullptr;    // [logit_rows, vocab]
+};
+
+}  // namespace rbt
+
+struct RbtModel;
+namespace rbt {
+void prefill_free(RbtModel* m);  // model_prefill.cu: the batched prompt's buffers and cuBLAS handle
+}  // namespace rbt
+
+struct RbtModel {
+    RbtModelConfig cfg{};
+    int ctx = 0, device = 0, sm_count = 0;
+    RbtMoe* moe = nullptr;
+    cudaStream_t stream = nullptr;
+    size_t esz = 0;
+    // weights
+    void* tok_emb = nullptr;
+    void* lm_head = nullptr;
+    float* final_norm = nullptr;
+    struct Layer {
+        float* attn_norm = nullptr;
+        float* q_norm = nullptr;
+        float* k_norm = nullptr;
+        void* wqkv = nullptr;  // [wq; wk; wv] rows, contiguous
+        void* wo = nullptr;
+        bool loaded = false;
+    };
+    std::vector<Layer> layers;
+    bool globals = false;
+    // state
+    float *x = nullptr, *qkv = nullptr, *part = nullptr, *ao = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    int32_t* routing = nullptr;
+    unsigned* done = nullptr;
+    unsigned* status = nullptr;  // attention's error word (a bounded wait that ran out)
+    rbt::Step* step = nullptr;
+    // pinned host staging
+    rbt::Step* h_step = nullptr;
+    float* h_logits = nullptr;
+    int32_t* h_routing = nullptr;
+    unsigned* h_status = nullptr;
+    // batched prompt (model_prefill.cu): cuBLAS handle and row buffers, grown on demand
+    cublasHandle_t blas = nullptr;
+    rbt::PrefillBufs pf;
+    // graphs: [0] without lm_head, [1] with
+    cudaGraphExec_t graph[2] = {nullptr, nullptr};
+    int n_splits = 0;
+};

@@ -1,0 +1,494 @@
+// model_prefill.cu -- the engine's forward() for a whole prompt at once
+// (rbt_model_prefill): positions pos0 .. pos0 + T of one sequence, layer by layer,
+// with every per-token matrix-vector product of forward() (rabbit2.c:455-550)
+// turned into a GEMM over the T rows:
+//
+//   embed_rows             X[t] = tok_emb[tokens[t]]                        (:461-467)
+//   per layer l:
+//     norm_split           rmsnorm(X) rows, as bf16 hi + lo (or f32 rows)   (:473)
+//     GEMM                 QKV = rows . [wq;wk;wv]^T                        (:474-476)
+//     qk_rope_kv           whole-projection QK-norm, RoPE at pos0 + t,      (:477-486)
+//                          k and v into the KV cache
+//     attn_prefill         causal attention over cache positions <= pos0+t  (:487-506)
+//     split + GEMM         X += AO . wo^T                                   (:507-508)
+//     rbt_moe_block_device X += MoE(rmsnorm(X)), all T rows (tensor cores)  (:511-542)
+//   norm_split + GEMM      logits of the last rows = rmsnorm(X) . lm_head^T (:545-546)
+//
+// The projections are plain dense GEMMs, so they go to cuBLAS.  bf16 weights
+// are exact in bf16; the f32 activation rows are split into bf16 hi = rn(x) and
+// lo = rn(x - hi) (16 significant bits), and each projection is two bf16 GEMMs
+// with f32 accumulation into the same output -- the precision scheme of the MoE
+// tensor-core path.  f32 models use f32 SGEMM.  The KV cache is the one the
+// one-token forward uses, so decode continues from pos0 + T.
+#include <cublas_v2.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/rbt_moe.h"
+#include "common.cuh"
+#include "model_internal.h"
+
+namespace rbt {
+void set_last_error(const char* msg);
+int moe_status_ok(RbtMoe* m);
+}  // namespace rbt
+
+namespace {
+
+using namespace rbt;
+
+int fail(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "rbt_model: %s\n", buf);
+    set_last_error(buf);
+    return 0;
+}
+
+#define CU(call)                                                                                  \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess) return fail("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                                   \
+    } while (0)
+#define CB(call)                                                                      \
+    do {                                                                              \
+        cublasStatus_t e_ = (call);                                                   \
+        if (e_ != CUBLAS_STATUS_SUCCESS) return fail("%s failed: cuBLAS status %d (%s:%d)", #call, \
+                                                    (int)e_, __FILE__, __LINE__);     \
+    } while (0)
+
+constexpr int kRowThreads = 256;
+constexpr int kRowVec4 = 2;   // float4s per thread of a row: dim, n_heads*head_dim <= 2048
+constexpr int kQB = 32;       // query rows per attention CTA
+constexpr int kKT = 64;       // key positions per tile
+constexpr int kAttnPThreads = 256;
+
+// ---------------------------------------------------------------- row kernels
+template <typename WT>
+__global__ void embed_rows_kernel(const WT* emb, int D, const int32_t* tokens, float* x) {
+    const int t = blockIdx.x;
+    const size_t row = (size_t)tokens[t] * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)t * D + i] = WeightTraits<WT>::load1(emb + row + i);
+}
+
+// Row t of x (n floats, row stride ld_in): rmsnorm with weights w (or none), then
+// either f32 rows (xf) or bf16 hi/lo rows (hi, lo), row stride ld_out.
+// The sum of squares is in a fixed order; (x * inv) * w as rmsnorm() rounds it.
+__global__ void __launch_bounds__(kRowThreads) norm_split_kernel(const float* x, int ld_in, int n, const float* w,
+                                                                 float eps, int ld_out, float* xf, uint16_t* hi,
+                                                                 uint16_t* lo) {
+    __shared__ float red[kRowThreads / 32];
+    const int t = blockIdx.x, tid = threadIdx.x, n4 = n / 4;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * ld_in);
+    float4 v[kRowVec4];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kRowVec4; k++) {
+        const int i4 = tid + k * kRowThreads;
+        if (i4 < n4) {
+            v[k] = xr[i4];
+            ss = fmaf(v[k].x, v[k].x, ss);
+            ss = fmaf(v[k].y, v[k].y, ss);
+            ss = fmaf(v[k].z, v[k].z, ss);
+            ss = fmaf(v[k].w, v[k].w, ss);
+        }
+    }
+    float inv = 1.0f;
+    if (w) {
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int i = 0; i < kRowThreads / 32; i++) tot += red[i];
+        inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)n), eps));
+    }
+#pragma unroll
+    for (int k = 0; k < kRowVec4; k++) {
+        const int i4 = tid + k * kRowThreads;
+        if (i4 >= n4) continue;
+        float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        if (w) {
+            const float4 wv = reinterpret_cast<const float4*>(w)[i4];
+            const float ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) e[q] = __fmul_rn(__fmul_rn(e[q], inv), ww[q]);
+        }
+        const size_t o = (size_t)t * ld_out + 4 * (size_t)i4;
+        if (xf) {
+            *reinterpret_cast<float4*>(xf + o) = make_float4(e[0], e[1], e[2], e[3]);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const __nv_bfloat16 h = __float2bfloat16_rn(e[q]);
+                hi[o + q] = __bfloat16_as_ushort(h);
+                lo[o + q] = __bfloat16_as_ushort(__float2bfloat16_rn(e[q] - __bfloat162float(h)));
+            }
+        }
+    }
+}
+
+// Row t of q|k|v: QK-norm over the whole q and k projections (rabbit2.c:477-480),
+// RoPE at position pos0 + t (:481-482, the engine's angle table), q written back
+// in place, k and v stored in the head-major KV cache (:484-486).
+__global__ void __launch_bounds__(kRowThreads) qk_rope_kv_kernel(float* qkv, int nq, int nkv, int hd,
+                                                                 const float* q_norm, const float* k_norm, float eps,
+                                                                 const float* rope_cos, const float* rope_sin,
+                                                                 int pos0, float* kc, float* vc, int ctx) {
+    __shared__ float red[kRowThreads / 32], red2[kRowThreads / 32];
+    const int t = blockIdx.x, tid = threadIdx.x, pos = pos0 + t, half = hd / 2;
+    float* row = qkv + (size_t)t * (nq + 2 * nkv);
+    float inv_q = 1.0f, inv_k = 1.0f;
+    if (q_norm) {
+        float sq = 0.0f, sk = 0.0f;
+        for (int i = tid; i < nq; i += kRowThreads) sq = fmaf(row[i], row[i], sq);
+        for (int i = tid; i < nkv; i += kRowThreads) sk = fmaf(row[nq + i], row[nq + i], sk);
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        if ((tid & 31) == 0) {
+            red[tid >> 5] = sq;
+            red2[tid >> 5] = sk;
+        }
+        __syncthreads();
+        float tq = 0.0f, tk = 0.0f;
+        for (int i = 0; i < kRowThreads / 32; i++) {
+            tq += red[i];
+            tk += red2[i];
+        }
+        inv_q = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tq, (float)nq), eps));
+        inv_k = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tk, (float)nkv), eps));
+    }
+    const float* cs = rope_cos + (size_t)pos * half;
+    const float* sn = rope_sin + (size_t)pos * half;
+    const int nqp = nq / 2, nkp = nkv / 2;  // (i, i + half) pairs of every head
+    for (int j = tid; j < nqp + nkp; j += kRowThreads) {
+        const bool is_q = j < nqp;
+        const int jj = is_q ? j : j - nqp, h = jj / half, i = jj % half;
+        float* p = row + (is_q ? 0 : nq) + (size_t)h * hd;
+        float a = p[i], b = p[i + half];
+        const float* w = is_q ? q_norm : k_norm;
+        if (w) {
+            const float inv = is_q ? inv_q : inv_k;
+            a = __fmul_rn(__fmul_rn(a, inv), w[(size_t)h * hd + i]);
+            b = __fmul_rn(__fmul_rn(b, inv), w[(size_t)h * hd + i + half]);
+        }
+        const float ra = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
+        const float rb = __fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i]));
+        if (is_q) {
+            p[i] = ra;
+            p[i + half] = rb;
+        } else {
+            const size_t at = ((size_t)h * ctx + pos) * hd;
+            kc[at + i] = ra;
+            kc[at + i + half] = rb;
+        }
+    }
+    for (int j = tid; j < nkv; j += kRowThreads) {
+        const int h = j / hd, i = j % hd;
+        vc[((size_t)h * ctx + pos) * hd + i] = row[nq + nkv + j];
+    }
+}
+
+// ---------------------------------------------------------------- causal attention
+// CTA (head h, block of kQB query rows): the rows' attention over cache positions
+// 0 .. pos0 + t (rabbit2.c:487-506) with an online softmax over tiles of kKT
+// positions in shared memory: scores = q . k * scale, running max and sum, and
+// the exp-weighted V sum, divided by the sum at the end.  Thread (r = tid / 8,
+// g = tid % 8) owns score columns g + 8 j and output dims 4 (g + 8 k) .. + 4 of
+// query row r.
+template <int HD>
+__global__ void __launch_bounds__(kAttnPThreads) attn_prefill_kernel(const float* qkv, int nq, int nkv, int n_heads,
+                                                                     int n_kv_heads, const float* kc, const float* vc,
+                                                                     int ctx, int pos0, int T, float scale,
+                                                                     float* ao) {
+    constexpr int LD = HD + 4;  // padded rows: the 8 column groups of a warp hit different banks
+    constexpr int DV = HD / 32;  // float4s of output per thread
+    extern __shared__ __align__(16) float sm[];
+    float* Qs = sm;                    // [kQB][LD]
+    float* Ks = Qs + kQB * LD;         // [kKT][LD]
+    float* Vs = Ks + kKT * LD;         // [kKT][LD]
+    float* Ps = Vs + kKT * LD;         // [kQB][kKT]
+    const int h = blockIdx.x, tb = blockIdx.y, tid = threadIdx.x;
+    const int r = tid >> 3, g = tid & 7;
+    const int t0 = tb * kQB, nrow = min(kQB, T - t0);
+    const int kvh = h / (n_heads / n_kv_heads);
+    const int row_stride = nq + 2 * nkv;
+    for (int e = tid; e < kQB * (HD / 4); e += kAttnPThreads) {
+        const int rr = e / (HD / 4), c4 = e % (HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rr < nrow) v = reinterpret_cast<const float4*>(qkv + (size_t)(t0 + rr) * row_stride + (size_t)h * HD)[c4];
+        *reinterpret_cast<float4*>(Qs + rr * LD + 4 * c4) = v;
+    }
+    const int my_t = t0 + r, my_pos = pos0 + my_t;  // this thread's query row and its position
+    const int last = pos0 + t0 + nrow - 1;            // the block's last position
+    float m_run = -INFINITY, l_run = 0.0f;
+    float4 o[DV];
+#pragma unroll
+    for (int k = 0; k < DV; k++) o[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* kb = kc + (size_t)kvh * ctx * HD;
+    const float* vb = vc + (size_t)kvh * ctx * HD;
+    for (int p0 = 0; p0 <= last; p0 += kKT) {
+        __syncthreads();  // the previous tile is consumed (and Qs written, on the first pass)
+        const int np = min(kKT, last + 1 - p0);
+        for (int e = tid; e < kKT * (HD / 4); e += kAttnPThreads) {
+            const int rr = e / (HD / 4), c4 = e % (HD / 4);
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (rr < np) {
+                kv = reinterpret_cast<const float4*>(kb + (size_t)(p0 + rr) * HD)[c4];
+                vv = reinterpret_cast<const float4*>(vb + (size_t)(p0 + rr) * HD)[c4];
+            }
+            *reinterpret_cast<float4*>(Ks + rr * LD + 4 * c4) = kv;
+            *reinterpret_cast<float4*>(Vs + rr * LD + 4 * c4) = vv;
+        }
+        __syncthreads();
+        // q . k for the thread's 8 columns: 16-byte loads, 8 independent accumulators
+        float s[kKT / 8];
+#pragma unroll
+        for (int j = 0; j < kKT / 8; j++) s[j] = 0.0f;
+#pragma unroll 4
+        for (int i4 = 0; i4 < HD / 4; i4++) {
+            const float4 q4 = *reinterpret_cast<const float4*>(Qs + r * LD + 4 * i4);
+#pragma unroll
+            for (int j = 0; j < kKT / 8; j++) {
+                const float4 k4 = *reinterpret_cast<const float4*>(Ks + (g + 8 * j) * LD + 4 * i4);
+                s[j] = fmaf(q4.x, k4.x, s[j]);
+                s[j] = fmaf(q4.y, k4.y, s[j]);
+                s[j] = fmaf(q4.z, k4.z, s[j]);
+                s[j] = fmaf(q4.w, k4.w, s[j]);
+            }
+        }
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kKT / 8; j++) {
+            const int c = g + 8 * j, p = p0 + c;
+            s[j] = (c < np && p <= my_pos && r < nrow) ? s[j] * scale : -INFINITY;
+            tmax = fmaxf(tmax, s[j]);
+        }
+        // the row's 8 threads are adjacent lanes
+        tmax = fmaxf(tmax, __shfl_xor_sync(FULL_MASK, tmax, 1));
+        tmax = fmaxf(tmax, __shfl_xor_sync(FULL_MASK, tmax, 2));
+        tmax = fmaxf(tmax, __shfl_xor_sync(FULL_MASK, tmax, 4));
+        const float m_new = fmaxf(m_run, tmax);
+        const float alpha = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);
+        float psum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kKT / 8; j++) {
+            const float pv = s[j] == -INFINITY ? 0.0f : expf(s[j] - m_new);
+            Ps[r * kKT + g + 8 * j] = pv;
+            psum += pv;
+        }
+        psum += __shfl_xor_sync(FULL_MASK, psum, 1);
+        psum += __shfl_xor_sync(FULL_MASK, psum, 2);
+        psum += __shfl_xor_sync(FULL_MASK, psum, 4);
+        l_run = l_run * alpha + psum;
+        m_run = m_new;
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < DV; k++) {
+            o[k].x *= alpha;
+            o[k].y *= alpha;
+            o[k].z *= alpha;
+            o[k].w *= alpha;
+        }
+        for (int c = 0; c < np; c++) {
+            const float pv = Ps[r * kKT + c];
+#pragma unroll
+            for (int k = 0; k < DV; k++) {
+                const float4 vv = *reinterpret_cast<const float4*>(Vs + c * LD + 4 * (g + 8 * k));
+                o[k].x = fmaf(pv, vv.x, o[k].x);
+                o[k].y = fmaf(pv, vv.y, o[k].y);
+                o[k].z = fmaf(pv, vv.z, o[k].z);
+                o[k].w = fmaf(pv, vv.w, o[k].w);
+            }
+        }
+    }
+    if (r < nrow) {
+        float* out = ao + (size_t)my_t * nq + (size_t)h * HD;
+#pragma unroll
+        for (int k = 0; k < DV; k++)
+            *reinterpret_cast<float4*>(out + 4 * (g + 8 * k)) =
+                make_float4(o[k].x / l_run, o[k].y / l_run, o[k].z / l_run, o[k].w / l_run);
+    }
+}
+
+size_t attn_prefill_smem(int hd) { return (size_t)((kQB + 2 * kKT) * (hd + 4) + kQB * kKT) * sizeof(float); }
+
+cudaError_t launch_attn_prefill(int hd, dim3 grid, cudaStream_t s, const float* qkv, int nq, int nkv, int n_heads,
+                                int n_kv_heads, const float* kc, const float* vc, int ctx, int pos0, int T,
+                                float scale, float* ao) {
+    const size_t smem = attn_prefill_smem(hd);
+    switch (hd) {
+#define RBT_ATTN_CASE(HDV)                                                                                      \
+    case HDV: {                                                                                                 \
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                             (int)smem);                                                        \
+        if (e != cudaSuccess) return e;                                                                         \
+        attn_prefill_kernel<HDV><<<grid, kAttnPThreads, smem, s>>>(qkv, nq, nkv, n_heads, n_kv_heads, kc, vc,   \
+                                                                   ctx, pos0, T, scale, ao);                    \
+        return cudaGetLastError();                                                                              \
+    }
+        RBT_ATTN_CASE(64)
+        RBT_ATTN_CASE(128)
+#undef RBT_ATTN_CASE
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
+
+// ---------------------------------------------------------------- GEMMs
+// out[T, N] (row-major, row stride ldc) (+)= rows[T, K] . W[N, K]^T.  bf16 models:
+// two bf16 GEMMs (hi then lo rows) accumulating in f32; f32 models: one SGEMM.
+int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out, int ldc, bool accumulate) {
+    const float one = 1.0f, zero = 0.0f;
+    cublasHandle_t hb = m->blas;
+    if (m->cfg.dtype == RBT_MOE_DT_BF16) {
+        CB(cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, W, CUDA_R_16BF, K, m->pf.hi, CUDA_R_16BF, ld_in,
+                        accumulate ? &one : &zero, out, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+        CB(cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, W, CUDA_R_16BF, K, m->pf.lo, CUDA_R_16BF, ld_in,
+                        &one, out, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    } else {
+        CB(cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, static_cast<const float*>(W), K, m->pf.xf, ld_in,
+                       accumulate ? &one : &zero, out, ldc));
+    }
+    return 1;
+}
+
+// the GEMM input rows: rmsnorm(src rows) with w, or src rows as they are (w == nullptr)
+int split_rows(RbtModel* m, const float* src, int ld_src, int n, int rows, const float* w, int ld_out) {
+    const bool bf = m->cfg.dtype == RBT_MOE_DT_BF16;
+    norm_split_kernel<<<rows, kRowThreads, 0, m->stream>>>(src, ld_src, n, w, m->cfg.rms_eps, ld_out,
+                                                          bf ? nullptr : m->pf.xf,
+                                                          bf ? static_cast<uint16_t*>(m->pf.hi) : nullptr,
+                                                          bf ? static_cast<uint16_t*>(m->pf.lo) : nullptr);
+    CU(cudaGetLastError());
+    return 1;
+}
+
+int nq_of(const RbtModelConfig& c) { return c.n_heads * c.head_dim; }
+int nkv_of(const RbtModelConfig& c) { return c.n_kv_heads * c.head_dim; }
+
+int reserve(RbtModel* m, int T, int logit_rows) {
+    const RbtModelConfig& c = m->cfg;
+    PrefillBufs& b = m->pf;
+    if (!m->blas) {
+        CB(cublasCreate(&m->blas));
+        CB(cublasSetStream(m->blas, m->stream));
+        CB(cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH));  // f32 SGEMM stays f32 (no TF32)
+    }
+    if (T > b.cap) {
+        void* old[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing};
+        for (void* p : old) cudaFree(p);
+        b = PrefillBufs{b.cap, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, b.logit_rows,
+                        b.logits};
+        const size_t wide = (size_t)(c.dim > nq_of(c) ? c.dim : nq_of(c));
+        const size_t rows = (size_t)T;
+        CU(cudaMalloc((void**)&b.tokens, rows * 4));
+        CU(cudaMalloc((void**)&b.x, rows * c.dim * 4));
+        CU(cudaMalloc((void**)&b.qkv, rows * (nq_of(c) + 2 * nkv_of(c)) * 4));
+        CU(cudaMalloc((void**)&b.ao, rows * nq_of(c) * 4));
+        if (c.dtype == RBT_MOE_DT_BF16) {
+            CU(cudaMalloc(&b.hi, rows * wide * 2));
+            CU(cudaMalloc(&b.lo, rows * wide * 2));
+        } else {
+            CU(cudaMalloc((void**)&b.xf, rows * wide * 4));
+        }
+        CU(cudaMalloc((void**)&b.routing, rows * c.n_layers * c.top_k * 4));
+        b.cap = T;
+    }
+    if (logit_rows > b.logit_rows) {
+        cudaFree(b.logits);
+        b.logits = nullptr;
+        b.logit_rows = 0;
+        CU(cudaMalloc((void**)&b.logits, (size_t)logit_rows * c.vocab * 4));
+        b.logit_rows = logit_rows;
+    }
+    if (!rbt_moe_reserve(m->moe, T)) return 0;
+    return 1;
+}
+
+template <typename WT>
+int run_prefill(RbtModel* m, int T, int pos0, int logit_rows) {
+    const RbtModelConfig& c = m->cfg;
+    const int D = c.dim, nq = nq_of(c), nkv = nkv_of(c), nqkv = nq + 2 * nkv, L = c.n_layers, K = c.top_k;
+    const int wide = D > nq ? D : nq;
+    cudaStream_t s = m->stream;
+    PrefillBufs& b = m->pf;
+    embed_rows_kernel<WT><<<T, 256, 0, s>>>(static_cast<const WT*>(m->tok_emb), D, b.tokens, b.x);
+    CU(cudaGetLastError());
+    const dim3 agrid(c.n_heads, (T + kQB - 1) / kQB);
+    for (int l = 0; l < L; l++) {
+        const RbtModel::Layer& Ly = m->layers[l];
+        if (!split_rows(m, b.x, D, D, T, Ly.attn_norm, wide)) return 0;
+        if (!proj(m, Ly.wqkv, nqkv, D, T, wide, b.qkv, nqkv, false)) return 0;
+        float* kc = m->kc + (size_t)l * m->ctx * nkv;
+        float* vc = m->vc + (size_t)l * m->ctx * nkv;
+        qk_rope_kv_kernel<<<T, kRowThreads, 0, s>>>(b.qkv, nq, nkv, c.head_dim, c.qk_norm ? Ly.q_norm : nullptr,
+                                                   c.qk_norm ? Ly.k_norm : nullptr, c.rms_eps, m->rope_cos,
+                                                   m->rope_sin, pos0, kc, vc, m->ctx);
+        CU(cudaGetLastError());
+        CU(launch_attn_prefill(c.head_dim, agrid, s, b.qkv, nq, nkv, c.n_heads, c.n_kv_heads, kc, vc, m->ctx, pos0, T,
+                               1.0f / sqrtf((float)c.head_dim), b.ao));
+        if (!split_rows(m, b.ao, nq, nq, T, nullptr, wide)) return 0;
+        if (!proj(m, Ly.wo, D, nq, T, wide, b.x, D, true)) return 0;
+        if (!rbt_moe_block_device(m->moe, l, b.x, T, b.routing + (size_t)l * K, L * K, (void*)s)) return 0;
+    }
+    if (logit_rows > 0) {
+        const float* last = b.x + (size_t)(T - logit_rows) * D;
+        if (!split_rows(m, last, D, D, logit_rows, m->final_norm, wide)) return 0;
+        if (!proj(m, m->lm_head, c.vocab, D, logit_rows, wide, b.logits, c.vocab, false)) return 0;
+    }
+    return 1;
+}
+
+}  // namespace
+
+namespace rbt {
+void prefill_free(RbtModel* m) {
+    PrefillBufs& b = m->pf;
+    void* bufs[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing, b.logits};
+    for (void* p : bufs) cudaFree(p);
+    b = PrefillBufs{};
+    if (m->blas) cublasDestroy(m->blas);
+    m->blas = nullptr;
+}
+}  // namespace rbt
+
+extern "C" int rbt_model_prefill(RbtModel* m, const int32_t* tokens, int n_tokens, int pos0, float* logits,
+                                 int logit_rows, int32_t* routing_out) {
+    if (!m) return fail("null model");
+    const RbtModelConfig& c = m->cfg;
+    if (n_tokens <= 0 || !tokens) return fail("no tokens");
+    if (pos0 < 0 || pos0 + n_tokens > m->ctx)
+        return fail("positions %d..%d outside the KV cache of %d", pos0, pos0 + n_tokens - 1, m->ctx);
+    if (logit_rows < 0 || logit_rows > n_tokens || (logit_rows > 0 && !logits))
+        return fail("logit_rows %d must be in [0, n_tokens] with a logits buffer", logit_rows);
+    if (c.head_dim != 64 && c.head_dim != 128) return fail("batched prompt needs head_dim 64 or 128");
+    for (int t = 0; t < n_tokens; t++)
+        if (tokens[t] < 0 || tokens[t] >= c.vocab) return fail("token %d out of range", tokens[t]);
+    if (!m->globals) return fail("globals not loaded (rbt_model_load_globals)");
+    for (int l = 0; l < c.n_layers; l++)
+        if (!m->layers[l].loaded) return fail("layer %d not loaded (rbt_model_load_layer)", l);
+    CU(cudaSetDevice(m->device));
+    if (!reserve(m, n_tokens, logit_rows)) return 0;
+    CU(cudaMemcpyAsync(m->pf.tokens, tokens, (size_t)n_tokens * 4, cudaMemcpyHostToDevice, m->stream));
+    const int ok = c.dtype == RBT_MOE_DT_BF16 ? run_prefill<uint16_t>(m, n_tokens, pos0, logit_rows)
+                                              : run_prefill<float>(m, n_tokens, pos0, logit_rows);
+    if (!ok) {
+        cudaStreamSynchronize(m->stream);
+        return 0;
+    }
+    if (logit_rows > 0)
+        CU(cudaMemcpyAsync(logits, m->pf.logits, (size_t)logit_rows * c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    if (routing_out)
+        CU(cudaMemcpyAsync(routing_out, m->pf.routing, (size_t)n_tokens * c.n_layers * c.top_k * 4,
+                           cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return moe_status_ok(m->moe);
+}

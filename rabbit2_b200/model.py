@@ -74,6 +74,18 @@ class ModelContext:
                    out.ctypes.data if logits else None, routing.ctypes.data)
         return out, routing
 
+    def prefill(self, tokens, pos0: int = 0, logit_rows: int = 1):
+        """The prompt tokens at positions pos0.. in one call (rbt_model_prefill):
+        (logits of the last logit_rows tokens [logit_rows, vocab] f32 or None,
+        routing [len(tokens), n_layers, top_k] int32)."""
+        c = self.cfg
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty((logit_rows, c.vocab), np.float32) if logit_rows else None
+        routing = np.empty((len(toks), c.n_layers, c.top_k), np.int32)
+        self._call(self.lib.rbt_model_prefill, self.handle, toks.ctypes.data, len(toks), int(pos0),
+                   out.ctypes.data if logit_rows else None, int(logit_rows), routing.ctypes.data)
+        return out, routing
+
     def close(self):
         if self.handle:
             self.lib.rbt_model_destroy(self.handle)

@@ -74,6 +74,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_model_load_globals": [vp, vp, vp, vp],
         "rbt_model_load_layer": [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
         "rbt_model_forward": [vp, i32, i32, vp, vp],
+        "rbt_model_prefill": [vp, vp, i32, i32, vp, i32, vp],
     }
     for name, argtypes in sig.items():
         fn = getattr(lib, name)

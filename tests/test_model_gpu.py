@@ -105,3 +105,43 @@ def test_forward_rejects_bad_token_and_position(tmp_path):
         m.forward(1, 0)  # the context still works
     finally:
         m.close()
+
+
+@needs_ref
+@pytest.mark.gpu
+def test_prefill_matches_reference_engine(model_file, tmp_path):
+    """rbt_model_prefill: the whole prompt in one call (and, again, in two chunks
+    that continue the KV cache), every row's logits against the engine's --dump
+    within 1e-3 and its routing identical; then 64 greedy tokens decoded from the
+    prefilled cache equal the engine's --gen."""
+    from rabbit2_b200.model import ModelContext
+    kind, path, cfg, prompt = model_file
+    want_l, want_r = _ref_dump(path, prompt, str(tmp_path))
+    n = len(prompt)
+    want_l = want_l.reshape(n, cfg.vocab)
+    want_r = want_r.reshape(n, cfg.n_layers, cfg.top_k)
+    want_ids = _ref_gen(path, prompt, 64)
+    m = ModelContext.from_file(path, ctx=256)
+    try:
+        for chunks in ([n], [100, n - 100]):
+            got_l, got_r, p0 = [], [], 0
+            for size in chunks:
+                lg, r = m.prefill(prompt[p0:p0 + size], pos0=p0, logit_rows=size)
+                got_l.append(lg)
+                got_r.append(r)
+                p0 += size
+            got_l, got_r = np.concatenate(got_l), np.concatenate(got_r)
+            np.testing.assert_array_equal(got_r, want_r, err_msg=f"{kind} {chunks}: routing")
+            err = np.abs(got_l.astype(np.float64) - want_l).max() / np.abs(want_l).max()
+            assert err < LOGIT_RTOL, (kind, chunks, err)
+        ids, logits, pos = [], got_l[-1], n
+        for g in range(64):
+            nxt = int(np.argmax(logits))
+            ids.append(nxt)
+            if g + 1 == 64:
+                break
+            logits, _ = m.forward(nxt, pos)
+            pos += 1
+        assert ids == want_ids, kind
+    finally:
+        m.close()
