@@ -130,7 +130,9 @@ static int rbt_engine_moe(Model *m, int layer, float *x, int32_t *routing_row) {
  * then ONE rbt_moe_block call for all of them, which the library runs on the
  * tensor cores.  Attention of token t at layer l reads the KV cache of positions
  * <= t of layer l only, which tokens 0..t have written by then, so the order
- * changes no value.  --prefill token keeps the engine's per-token loop. */
+ * changes no value.  With --offload all the whole prompt is one
+ * rbt_model_prefill call instead.  --prefill token keeps the engine's per-token
+ * loop. */
 
 /* Layer l's attention half for the token at position pos; x [dim] is updated in
  * place.  These are the engine's own calls on the same values in the same order
@@ -177,6 +179,37 @@ static void rbt_engine_attention(Model *m, State *s, int l, float *x, int pos) {
     for (int i = 0; i < D; i++) x[i] += s->xb[i];
 }
 
+/* --offload all: the whole prompt in one rbt_model_prefill call (every layer on
+ * the GPU over all prompt rows); the outputs as rbt_engine_prefill below
+ * describes them. */
+static int rbt_engine_prefill_model(Model *m, State *s, const int *tokens, int nt, int32_t *routing, FILE *fl,
+                                    FILE *fr) {
+    const Config *c = &m->c;
+    const size_t row = (size_t)c->n_layers * c->top_k;
+    const int rows = fl ? nt : 1;  /* logits of every token for --dump, else of the last */
+    float *lg = (float *)malloc((size_t)rows * c->vocab * sizeof(float));
+    int32_t *R = (int32_t *)malloc((size_t)nt * row * sizeof(int32_t));
+    int32_t *tok = (int32_t *)malloc((size_t)nt * sizeof(int32_t));
+    int ok = lg && R && tok;
+    if (!ok) fprintf(stderr, "out of memory for the batched prompt (try --prefill token)\n");
+    for (int t = 0; ok && t < nt; t++) tok[t] = tokens[t];
+    if (ok) ok = rbt_model_prefill(rbt_engine_model, tok, nt, 0, lg, rows, R);
+    for (int t = 0; ok && fl && t < nt; t++)
+        if (fwrite(lg + (size_t)t * c->vocab, sizeof(float), (size_t)c->vocab, fl) != (size_t)c->vocab ||
+            fwrite(R + (size_t)t * row, sizeof(int32_t), row, fr) != row) {
+            fprintf(stderr, "cannot write the dump files\n");
+            ok = 0;
+        }
+    if (ok) {
+        memcpy(s->logits, lg + (size_t)(rows - 1) * c->vocab, (size_t)c->vocab * sizeof(float));
+        memcpy(routing, R + (size_t)(nt - 1) * row, row * sizeof(int32_t));
+    }
+    free(lg);
+    free(R);
+    free(tok);
+    return ok ? 1 : -1;
+}
+
 /* The prompt tokens[0..nt) at positions 0..nt: 1 when it ran here (the last
  * token's logits in s->logits and its routing rows in `routing`, as the engine's
  * loop leaves them; with --dump every token's logits and routing rows written to
@@ -184,8 +217,9 @@ static void rbt_engine_attention(Model *m, State *s, int l, float *x, int pos) {
  * -1 on an error (message on stderr). */
 static int rbt_engine_prefill(Model *m, State *s, const int *tokens, int nt, int32_t *routing, FILE *fl,
                               FILE *fr) {
-    if (!rbt_engine_ctx || nt < 2 || (rbt_engine_prefill_mode && !strcmp(rbt_engine_prefill_mode, "token")))
-        return 0;
+    if (nt < 2 || (rbt_engine_prefill_mode && !strcmp(rbt_engine_prefill_mode, "token"))) return 0;
+    if (rbt_engine_model) return rbt_engine_prefill_model(m, s, tokens, nt, routing, fl, fr);
+    if (!rbt_engine_ctx) return 0;
     const Config *c = &m->c;
     const int D = c->dim;
     const size_t row = (size_t)c->n_layers * c->top_k;  /* routing ints per token */

@@ -151,11 +151,14 @@ def test_gpu_batched_prefill_bf16_matches_reference(tiny_model_bf16, tmp_path):
 @needs_bins
 @pytest.mark.gpu
 @pytest.mark.parametrize("which", ["f32", "bf16"])
-def test_gpu_whole_forward_engine_matches_reference(tiny_model, tiny_model_bf16, tmp_path, which):
-    """--offload all: every forward() is one rbt_model_forward call (attention,
-    MoE and lm_head on the GPU); same bars as the MoE-only runs."""
+@pytest.mark.parametrize("prefill", ["batch", "token"])
+def test_gpu_whole_forward_engine_matches_reference(tiny_model, tiny_model_bf16, tmp_path, which, prefill):
+    """--offload all: the prompt is one rbt_model_prefill call (--prefill batch) or
+    one rbt_model_forward call per token, and every generated token one
+    rbt_model_forward call (attention, MoE and lm_head on the GPU); same bars as
+    the MoE-only runs."""
     model, cfg, prompt = tiny_model if which == "f32" else tiny_model_bf16
-    extra = ["--device", "cuda", "--offload", "all"]
+    extra = ["--device", "cuda", "--offload", "all", "--prefill", prefill]
     want_ids, _ = gen(REF, model, prompt, 64)
     got_ids, log = gen(CUDA, model, prompt, 64, extra)
     assert "forward device: cuda" in log
