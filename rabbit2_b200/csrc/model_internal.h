@@ -29,6 +29,8 @@ struct PrefillBufs {
     int32_t* routing = nullptr; // [cap, n_layers, top_k]
     int logit_rows = 0;
     float* logits = nullptr;    // [logit_rows, vocab]
+    size_t att_bytes = 0;       // tensor-core attention scratch (bf16 models): scores, P, q|k|v splits
+    void* att = nullptr;
 };
 
 }  // namespace rbt

@@ -342,6 +342,85 @@ cudaError_t launch_attn_prefill(int hd, dim3 grid, cudaStream_t s, const float* 
     }
 }
 
+// ---------------------------------------------------------------- attention on the tensor cores (bf16 models)
+// scores = q . k as bf16 hi/lo GEMMs, a causal softmax kernel, O = P . V as GEMMs.
+constexpr int kSmaxThreads = 256;
+constexpr int kSmaxPer = 32;  // scores per thread: cache positions <= 8192
+
+// K and V of cache positions [0, nk) of every kv head as bf16 hi/lo rows
+// [n_kv][nk][hd] (one warp per row of hd <= 128 floats)
+__global__ void split_kv_kernel(const float* kc, const float* vc, int ctx, int nk, int hd, int n_kv, uint16_t* kh,
+                                uint16_t* kl, uint16_t* vh, uint16_t* vl) {
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (w >= n_kv * nk) return;
+    const int h = w / nk, p = w % nk;
+    const size_t src = ((size_t)h * ctx + p) * hd, dst = (size_t)w * hd;
+    for (int i4 = lane; i4 < hd / 4; i4 += 32) {
+        const float4 k4 = reinterpret_cast<const float4*>(kc + src)[i4];
+        const float4 v4 = reinterpret_cast<const float4*>(vc + src)[i4];
+        const float ke[4] = {k4.x, k4.y, k4.z, k4.w}, ve[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const __nv_bfloat16 a = __float2bfloat16_rn(ke[q]), b = __float2bfloat16_rn(ve[q]);
+            kh[dst + 4 * i4 + q] = __bfloat16_as_ushort(a);
+            kl[dst + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ke[q] - __bfloat162float(a)));
+            vh[dst + 4 * i4 + q] = __bfloat16_as_ushort(b);
+            vl[dst + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ve[q] - __bfloat162float(b)));
+        }
+    }
+}
+
+// Row (head h, query t) of the scores [H][T][nk]: att = dot * scale for positions
+// p <= pos0 + t, the softmax of rabbit2.c:399-405 (max, exp, sum, divide), and P
+// as bf16 hi/lo (0 past the causal limit).
+__global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const float* S, int T, int nk, int pos0,
+                                                                      float scale, uint16_t* ph, uint16_t* pl) {
+    __shared__ float red[kSmaxThreads / 32];
+    const int row = blockIdx.x, t = row % T, tid = threadIdx.x, lim = pos0 + t;  // valid p <= lim
+    const float* sr = S + (size_t)row * nk;
+    float v[kSmaxPer];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kSmaxPer; k++) {
+        const int p = tid + k * kSmaxThreads;
+        v[k] = p <= lim && p < nk ? sr[p] * scale : -INFINITY;
+        mx = fmaxf(mx, v[k]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 16));
+    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 1));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < kSmaxThreads / 32; i++) mx = fmaxf(mx, red[i]);
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kSmaxPer; k++) {
+        v[k] = v[k] == -INFINITY ? 0.0f : expf(v[k] - mx);
+        sum += v[k];
+    }
+    sum = warp_sum(sum);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < kSmaxThreads / 32; i++) tot += red[i];
+    uint16_t* hr = ph + (size_t)row * nk;
+    uint16_t* lr = pl + (size_t)row * nk;
+#pragma unroll
+    for (int k = 0; k < kSmaxPer; k++) {
+        const int p = tid + k * kSmaxThreads;
+        if (p < nk) {
+            const float pv = v[k] / tot;
+            const __nv_bfloat16 a = __float2bfloat16_rn(pv);
+            hr[p] = __bfloat16_as_ushort(a);
+            lr[p] = __bfloat16_as_ushort(__float2bfloat16_rn(pv - __bfloat162float(a)));
+        }
+    }
+}
+
 // ---------------------------------------------------------------- GEMMs
 // out[T, N] (row-major, row stride ldc) (+)= rows[T, K] . W[N, K]^T.  bf16 models:
 // two bf16 GEMMs (hi then lo rows) accumulating in f32; f32 models: one SGEMM.
@@ -360,6 +439,61 @@ int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out,
     return 1;
 }
 
+// Attention of T query rows (q in place in qkv rows, after RoPE) over cache
+// positions [0, nk), nk = pos0 + T, into ao [T, nq], for bf16 models:
+//   S[h] = (Qhi + Qlo) . (Khi + Klo)^T without the lo.lo term (3 GEMMs),
+//   P = causal softmax(S * scale) as hi/lo, O[h] = (Phi + Plo) . (Vhi + Vlo) (3 GEMMs).
+// Heads of one kv group are batched with the kv head's stride (GQA: one call per
+// position in the group).
+int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) {
+    const RbtModelConfig& c = m->cfg;
+    PrefillBufs& b = m->pf;
+    const int H = c.n_heads, NKV = c.n_kv_heads, hd = c.head_dim, grp = H / NKV;
+    const int nq = H * hd, nqkv = nq + 2 * NKV * hd, nk = pos0 + T;
+    cudaStream_t s = m->stream;
+    float* S = static_cast<float*>(b.att);
+    uint16_t* ph = reinterpret_cast<uint16_t*>(S + (size_t)H * T * nk);
+    uint16_t* pl = ph + (size_t)H * T * nk;
+    uint16_t* qh = pl + (size_t)H * T * nk;
+    uint16_t* ql = qh + (size_t)T * nq;
+    uint16_t* kh = ql + (size_t)T * nq;
+    uint16_t* kl = kh + (size_t)NKV * nk * hd;
+    uint16_t* vh = kl + (size_t)NKV * nk * hd;
+    uint16_t* vl = vh + (size_t)NKV * nk * hd;
+    norm_split_kernel<<<T, kRowThreads, 0, s>>>(b.qkv, nqkv, nq, nullptr, c.rms_eps, nq, nullptr, qh, ql);
+    CU(cudaGetLastError());
+    split_kv_kernel<<<(NKV * nk + 7) / 8, 256, 0, s>>>(kc, vc, m->ctx, nk, hd, NKV, kh, kl, vh, vl);
+    CU(cudaGetLastError());
+    const float one = 1.0f, zero = 0.0f;
+    const long long sK = (long long)nk * hd, sS = (long long)grp * T * nk;
+    for (int g = 0; g < grp; g++) {
+        const uint16_t* A[3] = {kh, kl, kh};
+        const uint16_t* B[3] = {qh, qh, ql};
+        for (int i = 0; i < 3; i++)
+            CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, nk, T, hd, &one, A[i], CUDA_R_16BF, hd,
+                                          sK, B[i] + (size_t)g * hd, CUDA_R_16BF, nq, (long long)grp * hd,
+                                          i ? &one : &zero, S + (size_t)g * T * nk, CUDA_R_32F, nk, sS, NKV,
+                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    }
+    causal_softmax_kernel<<<H * T, kSmaxThreads, 0, s>>>(S, T, nk, pos0, 1.0f / sqrtf((float)hd), ph, pl);
+    CU(cudaGetLastError());
+    for (int g = 0; g < grp; g++) {
+        const uint16_t* A[3] = {vh, vl, vh};
+        const uint16_t* B[3] = {ph, ph, pl};
+        for (int i = 0; i < 3; i++)
+            CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, T, nk, &one, A[i], CUDA_R_16BF, hd,
+                                          sK, B[i] + (size_t)g * T * nk, CUDA_R_16BF, nk, sS, i ? &one : &zero,
+                                          b.ao + (size_t)g * hd, CUDA_R_32F, nq, (long long)grp * hd, NKV,
+                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    }
+    return 1;
+}
+
+size_t attn_tensor_bytes(const RbtModelConfig& c, int T, int nk) {
+    const size_t H = c.n_heads, nq = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * nk * c.head_dim;
+    return H * T * nk * (4 + 2 + 2) + (size_t)T * nq * 2 * 2 + kv * 2 * 4;
+}
+
 // the GEMM input rows: rmsnorm(src rows) with w, or src rows as they are (w == nullptr)
 int split_rows(RbtModel* m, const float* src, int ld_src, int n, int rows, const float* w, int ld_out) {
     const bool bf = m->cfg.dtype == RBT_MOE_DT_BF16;
@@ -374,7 +508,7 @@ int split_rows(RbtModel* m, const float* src, int ld_src, int n, int rows, const
 int nq_of(const RbtModelConfig& c) { return c.n_heads * c.head_dim; }
 int nkv_of(const RbtModelConfig& c) { return c.n_kv_heads * c.head_dim; }
 
-int reserve(RbtModel* m, int T, int logit_rows) {
+int reserve(RbtModel* m, int T, int pos0, int logit_rows) {
     const RbtModelConfig& c = m->cfg;
     PrefillBufs& b = m->pf;
     if (!m->blas) {
@@ -385,8 +519,8 @@ int reserve(RbtModel* m, int T, int logit_rows) {
     if (T > b.cap) {
         void* old[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing};
         for (void* p : old) cudaFree(p);
-        b = PrefillBufs{b.cap, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, b.logit_rows,
-                        b.logits};
+        b = PrefillBufs{b.cap,       nullptr,  nullptr,     nullptr,     nullptr, nullptr, nullptr,
+                        nullptr,     nullptr,  b.logit_rows, b.logits, b.att_bytes, b.att};
         const size_t wide = (size_t)(c.dim > nq_of(c) ? c.dim : nq_of(c));
         const size_t rows = (size_t)T;
         CU(cudaMalloc((void**)&b.tokens, rows * 4));
@@ -401,6 +535,16 @@ int reserve(RbtModel* m, int T, int logit_rows) {
         }
         CU(cudaMalloc((void**)&b.routing, rows * c.n_layers * c.top_k * 4));
         b.cap = T;
+    }
+    if (c.dtype == RBT_MOE_DT_BF16) {
+        const size_t need = attn_tensor_bytes(c, T, pos0 + T);
+        if (need > b.att_bytes) {
+            cudaFree(b.att);
+            b.att = nullptr;
+            b.att_bytes = 0;
+            CU(cudaMalloc(&b.att, need));
+            b.att_bytes = need;
+        }
     }
     if (logit_rows > b.logit_rows) {
         cudaFree(b.logits);
@@ -433,8 +577,12 @@ int run_prefill(RbtModel* m, int T, int pos0, int logit_rows) {
                                                    c.qk_norm ? Ly.k_norm : nullptr, c.rms_eps, m->rope_cos,
                                                    m->rope_sin, pos0, kc, vc, m->ctx);
         CU(cudaGetLastError());
-        CU(launch_attn_prefill(c.head_dim, agrid, s, b.qkv, nq, nkv, c.n_heads, c.n_kv_heads, kc, vc, m->ctx, pos0, T,
-                               1.0f / sqrtf((float)c.head_dim), b.ao));
+        if (c.dtype == RBT_MOE_DT_BF16) {
+            if (!attn_tensor(m, T, pos0, kc, vc)) return 0;
+        } else {
+            CU(launch_attn_prefill(c.head_dim, agrid, s, b.qkv, nq, nkv, c.n_heads, c.n_kv_heads, kc, vc, m->ctx, pos0,
+                                   T, 1.0f / sqrtf((float)c.head_dim), b.ao));
+        }
         if (!split_rows(m, b.ao, nq, nq, T, nullptr, wide)) return 0;
         if (!proj(m, Ly.wo, D, nq, T, wide, b.x, D, true)) return 0;
         if (!rbt_moe_block_device(m->moe, l, b.x, T, b.routing + (size_t)l * K, L * K, (void*)s)) return 0;
@@ -452,7 +600,7 @@ int run_prefill(RbtModel* m, int T, int pos0, int logit_rows) {
 namespace rbt {
 void prefill_free(RbtModel* m) {
     PrefillBufs& b = m->pf;
-    void* bufs[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing, b.logits};
+    void* bufs[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing, b.logits, b.att};
     for (void* p : bufs) cudaFree(p);
     b = PrefillBufs{};
     if (m->blas) cublasDestroy(m->blas);
@@ -476,7 +624,7 @@ extern "C" int rbt_model_prefill(RbtModel* m, const int32_t* tokens, int n_token
     for (int l = 0; l < c.n_layers; l++)
         if (!m->layers[l].loaded) return fail("layer %d not loaded (rbt_model_load_layer)", l);
     CU(cudaSetDevice(m->device));
-    if (!reserve(m, n_tokens, logit_rows)) return 0;
+    if (!reserve(m, n_tokens, pos0, logit_rows)) return 0;
     CU(cudaMemcpyAsync(m->pf.tokens, tokens, (size_t)n_tokens * 4, cudaMemcpyHostToDevice, m->stream));
     const int ok = c.dtype == RBT_MOE_DT_BF16 ? run_prefill<uint16_t>(m, n_tokens, pos0, logit_rows)
                                               : run_prefill<float>(m, n_tokens, pos0, logit_rows);
