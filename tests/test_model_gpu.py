@@ -91,7 +91,7 @@ def test_forward_matches_reference_engine(model_file, tmp_path):
 
 
 @pytest.mark.gpu
-def test_forward_rejects_bad_token_and_position(tmp_path):
+def test_forward_and_prefill_reject_bad_tokens_and_positions(tmp_path):
     from rabbit2_b200.model import ModelContext
     cfg = _cfg("f32")
     path = str(tmp_path / "m.rbt2")
@@ -103,6 +103,14 @@ def test_forward_rejects_bad_token_and_position(tmp_path):
         with pytest.raises(moe.RbtMoeError, match="position"):
             m.forward(1, 16)
         m.forward(1, 0)  # the context still works
+        with pytest.raises(moe.RbtMoeError, match="KV cache"):
+            m.prefill([1] * 10, pos0=8)  # positions 8..17 of a 16-position cache
+        with pytest.raises(moe.RbtMoeError, match="logit_rows"):
+            m.prefill([1, 2, 3], logit_rows=4)
+        with pytest.raises(moe.RbtMoeError, match="token"):
+            m.prefill([1, cfg.vocab])
+        lg, r = m.prefill([1, 2, 3], logit_rows=1)  # and still works
+        assert lg.shape == (1, cfg.vocab) and r.shape == (3, cfg.n_layers, cfg.top_k)
     finally:
         m.close()
 
