@@ -345,16 +345,18 @@ cudaError_t launch_attn_prefill(int hd, dim3 grid, cudaStream_t s, const float* 
 // ---------------------------------------------------------------- attention on the tensor cores (bf16 models)
 // scores = q . k as bf16 hi/lo GEMMs, a causal softmax kernel, O = P . V as GEMMs.
 constexpr int kSmaxThreads = 256;
-constexpr int kSmaxPer = 32;  // scores per thread: cache positions <= 8192
+constexpr int kSmaxPer = 32;  // scores per thread (in pairs): cache positions <= 8192
 
-// K and V of cache positions [0, nk) of every kv head as bf16 hi/lo rows
-// [n_kv][nk][hd] (one warp per row of hd <= 128 floats)
-__global__ void split_kv_kernel(const float* kc, const float* vc, int ctx, int nk, int hd, int n_kv, uint16_t* kh,
-                                uint16_t* kl, uint16_t* vh, uint16_t* vl) {
+// K and V of cache positions [0, nk) of every kv head, as bf16: K rows
+// concatenated [hi | lo | hi] into kcat [n_kv][nk][3 hd] (against q's
+// [hi | hi | lo] one GEMM gives hi.hi + hi.lo + lo.hi), V as hi and lo rows
+// [n_kv][nk][hd].  One warp per row of hd <= 128 floats.
+__global__ void split_kv_kernel(const float* kc, const float* vc, int ctx, int nk, int hd, int n_kv, uint16_t* kcat,
+                                uint16_t* vh, uint16_t* vl) {
     const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (w >= n_kv * nk) return;
     const int h = w / nk, p = w % nk;
-    const size_t src = ((size_t)h * ctx + p) * hd, dst = (size_t)w * hd;
+    const size_t src = ((size_t)h * ctx + p) * hd, dst = (size_t)w * hd, dk = (size_t)w * 3 * hd;
     for (int i4 = lane; i4 < hd / 4; i4 += 32) {
         const float4 k4 = reinterpret_cast<const float4*>(kc + src)[i4];
         const float4 v4 = reinterpret_cast<const float4*>(vc + src)[i4];
@@ -362,29 +364,57 @@ __global__ void split_kv_kernel(const float* kc, const float* vc, int ctx, int n
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             const __nv_bfloat16 a = __float2bfloat16_rn(ke[q]), b = __float2bfloat16_rn(ve[q]);
-            kh[dst + 4 * i4 + q] = __bfloat16_as_ushort(a);
-            kl[dst + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ke[q] - __bfloat162float(a)));
+            const uint16_t ah = __bfloat16_as_ushort(a);
+            kcat[dk + 4 * i4 + q] = ah;
+            kcat[dk + hd + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ke[q] - __bfloat162float(a)));
+            kcat[dk + 2 * hd + 4 * i4 + q] = ah;
             vh[dst + 4 * i4 + q] = __bfloat16_as_ushort(b);
             vl[dst + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ve[q] - __bfloat162float(b)));
         }
     }
 }
 
-// Row (head h, query t) of the scores [H][T][nk]: att = dot * scale for positions
+// q of every head of row t as [hi | hi | lo] per head: qcat [T][H][3 hd]
+__global__ void split_q_kernel(const float* qkv, int nqkv, int H, int hd, uint16_t* qcat) {
+    const int t = blockIdx.x;
+    const float* q = qkv + (size_t)t * nqkv;
+    uint16_t* out = qcat + (size_t)t * H * 3 * hd;
+    for (int j = threadIdx.x; j < H * hd; j += blockDim.x) {
+        const int h = j / hd, i = j % hd;
+        const float x = q[j];
+        const __nv_bfloat16 a = __float2bfloat16_rn(x);
+        const uint16_t ah = __bfloat16_as_ushort(a);
+        uint16_t* o = out + (size_t)h * 3 * hd;
+        o[i] = ah;
+        o[hd + i] = ah;
+        o[2 * hd + i] = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(a)));
+    }
+}
+
+// Row (head h, query t) of the scores [H][T][nk] (nk: the even row stride, at
+// least the number of cache positions): att = dot * scale for positions
 // p <= pos0 + t, the softmax of rabbit2.c:399-405 (max, exp, sum, divide), and P
-// as bf16 hi/lo (0 past the causal limit).
+// as bf16 hi/lo (0 past the causal limit, the padding included).
 __global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const float* S, int T, int nk, int pos0,
                                                                       float scale, uint16_t* ph, uint16_t* pl) {
     __shared__ float red[kSmaxThreads / 32];
     const int row = blockIdx.x, t = row % T, tid = threadIdx.x, lim = pos0 + t;  // valid p <= lim
-    const float* sr = S + (size_t)row * nk;
+    // thread tid takes the pairs (2 q, 2 q + 1), q = tid + k * threads (nk is even)
+    const float2* sr = reinterpret_cast<const float2*>(S + (size_t)row * nk);
     float v[kSmaxPer];
     float mx = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < kSmaxPer; k++) {
-        const int p = tid + k * kSmaxThreads;
-        v[k] = p <= lim && p < nk ? sr[p] * scale : -INFINITY;
-        mx = fmaxf(mx, v[k]);
+    for (int k = 0; k < kSmaxPer / 2; k++) {
+        const int p = 2 * (tid + k * kSmaxThreads);
+        float2 x = make_float2(-INFINITY, -INFINITY);
+        if (p <= lim && p < nk) {
+            x = sr[p / 2];
+            x.x *= scale;
+            x.y = p + 1 <= lim ? x.y * scale : -INFINITY;
+        }
+        v[2 * k] = x.x;
+        v[2 * k + 1] = x.y;
+        mx = fmaxf(mx, fmaxf(x.x, x.y));
     }
     mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 16));
     mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 8));
@@ -407,16 +437,18 @@ __global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const floa
     __syncthreads();
     float tot = 0.0f;
     for (int i = 0; i < kSmaxThreads / 32; i++) tot += red[i];
-    uint16_t* hr = ph + (size_t)row * nk;
-    uint16_t* lr = pl + (size_t)row * nk;
+    uint32_t* hr = reinterpret_cast<uint32_t*>(ph + (size_t)row * nk);
+    uint32_t* lr = reinterpret_cast<uint32_t*>(pl + (size_t)row * nk);
 #pragma unroll
-    for (int k = 0; k < kSmaxPer; k++) {
-        const int p = tid + k * kSmaxThreads;
+    for (int k = 0; k < kSmaxPer / 2; k++) {
+        const int p = 2 * (tid + k * kSmaxThreads);
         if (p < nk) {
-            const float pv = v[k] / tot;
-            const __nv_bfloat16 a = __float2bfloat16_rn(pv);
-            hr[p] = __bfloat16_as_ushort(a);
-            lr[p] = __bfloat16_as_ushort(__float2bfloat16_rn(pv - __bfloat162float(a)));
+            const float p0 = v[2 * k] / tot, p1 = v[2 * k + 1] / tot;
+            const __nv_bfloat16 a0 = __float2bfloat16_rn(p0), a1 = __float2bfloat16_rn(p1);
+            const __nv_bfloat16 b0 = __float2bfloat16_rn(p0 - __bfloat162float(a0));
+            const __nv_bfloat16 b1 = __float2bfloat16_rn(p1 - __bfloat162float(a1));
+            hr[p / 2] = (uint32_t)__bfloat16_as_ushort(a0) | ((uint32_t)__bfloat16_as_ushort(a1) << 16);
+            lr[p / 2] = (uint32_t)__bfloat16_as_ushort(b0) | ((uint32_t)__bfloat16_as_ushort(b1) << 16);
         }
     }
 }
@@ -441,7 +473,8 @@ int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out,
 
 // Attention of T query rows (q in place in qkv rows, after RoPE) over cache
 // positions [0, nk), nk = pos0 + T, into ao [T, nq], for bf16 models:
-//   S[h] = (Qhi + Qlo) . (Khi + Klo)^T without the lo.lo term (3 GEMMs),
+//   S[h] = (Qhi + Qlo) . (Khi + Klo)^T without the lo.lo term, as one GEMM over
+//          the concatenations [Qhi | Qhi | Qlo] . [Khi | Klo | Khi]^T,
 //   P = causal softmax(S * scale) as hi/lo, O[h] = (Phi + Plo) . (Vhi + Vlo) (3 GEMMs).
 // Heads of one kv group are batched with the kv head's stride (GQA: one call per
 // position in the group).
@@ -450,39 +483,35 @@ int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) 
     PrefillBufs& b = m->pf;
     const int H = c.n_heads, NKV = c.n_kv_heads, hd = c.head_dim, grp = H / NKV;
     const int nq = H * hd, nqkv = nq + 2 * NKV * hd, nk = pos0 + T;
+    const int ld = (nk + 1) & ~1;  // row stride of S and P: even, so the softmax moves pairs
     cudaStream_t s = m->stream;
     float* S = static_cast<float*>(b.att);
-    uint16_t* ph = reinterpret_cast<uint16_t*>(S + (size_t)H * T * nk);
-    uint16_t* pl = ph + (size_t)H * T * nk;
-    uint16_t* qh = pl + (size_t)H * T * nk;
-    uint16_t* ql = qh + (size_t)T * nq;
-    uint16_t* kh = ql + (size_t)T * nq;
-    uint16_t* kl = kh + (size_t)NKV * nk * hd;
-    uint16_t* vh = kl + (size_t)NKV * nk * hd;
+    uint16_t* ph = reinterpret_cast<uint16_t*>(S + (size_t)H * T * ld);
+    uint16_t* pl = ph + (size_t)H * T * ld;
+    uint16_t* qcat = pl + (size_t)H * T * ld;        // [T][H][3 hd]
+    uint16_t* kcat = qcat + (size_t)T * H * 3 * hd;  // [NKV][nk][3 hd]
+    uint16_t* vh = kcat + (size_t)NKV * nk * 3 * hd;
     uint16_t* vl = vh + (size_t)NKV * nk * hd;
-    norm_split_kernel<<<T, kRowThreads, 0, s>>>(b.qkv, nqkv, nq, nullptr, c.rms_eps, nq, nullptr, qh, ql);
+    split_q_kernel<<<T, 256, 0, s>>>(b.qkv, nqkv, H, hd, qcat);
     CU(cudaGetLastError());
-    split_kv_kernel<<<(NKV * nk + 7) / 8, 256, 0, s>>>(kc, vc, m->ctx, nk, hd, NKV, kh, kl, vh, vl);
+    split_kv_kernel<<<(NKV * nk + 7) / 8, 256, 0, s>>>(kc, vc, m->ctx, nk, hd, NKV, kcat, vh, vl);
     CU(cudaGetLastError());
     const float one = 1.0f, zero = 0.0f;
-    const long long sK = (long long)nk * hd, sS = (long long)grp * T * nk;
-    for (int g = 0; g < grp; g++) {
-        const uint16_t* A[3] = {kh, kl, kh};
-        const uint16_t* B[3] = {qh, qh, ql};
-        for (int i = 0; i < 3; i++)
-            CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, nk, T, hd, &one, A[i], CUDA_R_16BF, hd,
-                                          sK, B[i] + (size_t)g * hd, CUDA_R_16BF, nq, (long long)grp * hd,
-                                          i ? &one : &zero, S + (size_t)g * T * nk, CUDA_R_32F, nk, sS, NKV,
-                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-    }
-    causal_softmax_kernel<<<H * T, kSmaxThreads, 0, s>>>(S, T, nk, pos0, 1.0f / sqrtf((float)hd), ph, pl);
+    const long long sK = (long long)nk * hd, sS = (long long)grp * T * ld;
+    // S = qcat . kcat^T: one GEMM over the concatenated 3 hd, written once
+    for (int g = 0; g < grp; g++)
+        CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, nk, T, 3 * hd, &one, kcat, CUDA_R_16BF,
+                                      3 * hd, 3 * sK, qcat + (size_t)g * 3 * hd, CUDA_R_16BF, H * 3 * hd,
+                                      (long long)grp * 3 * hd, &zero, S + (size_t)g * T * ld, CUDA_R_32F, ld, sS, NKV,
+                                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    causal_softmax_kernel<<<H * T, kSmaxThreads, 0, s>>>(S, T, ld, pos0, 1.0f / sqrtf((float)hd), ph, pl);
     CU(cudaGetLastError());
     for (int g = 0; g < grp; g++) {
         const uint16_t* A[3] = {vh, vl, vh};
         const uint16_t* B[3] = {ph, ph, pl};
         for (int i = 0; i < 3; i++)
             CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, T, nk, &one, A[i], CUDA_R_16BF, hd,
-                                          sK, B[i] + (size_t)g * T * nk, CUDA_R_16BF, nk, sS, i ? &one : &zero,
+                                          sK, B[i] + (size_t)g * T * ld, CUDA_R_16BF, ld, sS, i ? &one : &zero,
                                           b.ao + (size_t)g * hd, CUDA_R_32F, nq, (long long)grp * hd, NKV,
                                           CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
     }
@@ -491,7 +520,8 @@ int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) 
 
 size_t attn_tensor_bytes(const RbtModelConfig& c, int T, int nk) {
     const size_t H = c.n_heads, nq = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * nk * c.head_dim;
-    return H * T * nk * (4 + 2 + 2) + (size_t)T * nq * 2 * 2 + kv * 2 * 4;
+    const size_t ld = (size_t)((nk + 1) & ~1);
+    return H * T * ld * (4 + 2 + 2) + (size_t)T * nq * 3 * 2 + kv * 2 * 3 + kv * 2 * 2;
 }
 
 // the GEMM input rows: rmsnorm(src rows) with w, or src rows as they are (w == nullptr)

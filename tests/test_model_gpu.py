@@ -131,7 +131,7 @@ def test_prefill_matches_reference_engine(model_file, tmp_path):
     want_ids = _ref_gen(path, prompt, 64)
     m = ModelContext.from_file(path, ctx=256)
     try:
-        for chunks in ([n], [100, n - 100]):
+        for chunks in ([n], [101, n - 101]):  # (101: an odd number of cache positions)
             got_l, got_r, p0 = [], [], 0
             for size in chunks:
                 lg, r = m.prefill(prompt[p0:p0 + size], pos0=p0, logit_rows=size)
