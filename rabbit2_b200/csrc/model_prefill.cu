@@ -478,18 +478,23 @@ int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out,
 //   P = causal softmax(S * scale) as hi/lo, O[h] = (Phi + Plo) . (Vhi + Vlo) (3 GEMMs).
 // Heads of one kv group are batched with the kv head's stride (GQA: one call per
 // position in the group).
+// Query rows go in chunks of kAttnRows: a chunk's rows see cache positions below
+// pos0 + (its end) only, so the causal triangle costs about half of the square.
+constexpr int kAttnRows = 512;
+
 int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) {
     const RbtModelConfig& c = m->cfg;
     PrefillBufs& b = m->pf;
     const int H = c.n_heads, NKV = c.n_kv_heads, hd = c.head_dim, grp = H / NKV;
     const int nq = H * hd, nqkv = nq + 2 * NKV * hd, nk = pos0 + T;
-    const int ld = (nk + 1) & ~1;  // row stride of S and P: even, so the softmax moves pairs
+    const int tc = T < kAttnRows ? T : kAttnRows;
+    const int ld_max = (nk + 1) & ~1;  // row stride of S and P: even, so the softmax moves pairs
     cudaStream_t s = m->stream;
-    float* S = static_cast<float*>(b.att);
-    uint16_t* ph = reinterpret_cast<uint16_t*>(S + (size_t)H * T * ld);
-    uint16_t* pl = ph + (size_t)H * T * ld;
-    uint16_t* qcat = pl + (size_t)H * T * ld;        // [T][H][3 hd]
-    uint16_t* kcat = qcat + (size_t)T * H * 3 * hd;  // [NKV][nk][3 hd]
+    float* S = static_cast<float*>(b.att);                     // [H][tc][ld]
+    uint16_t* ph = reinterpret_cast<uint16_t*>(S + (size_t)H * tc * ld_max);
+    uint16_t* pl = ph + (size_t)H * tc * ld_max;
+    uint16_t* qcat = pl + (size_t)H * tc * ld_max;          // [T][H][3 hd]
+    uint16_t* kcat = qcat + (size_t)T * H * 3 * hd;          // [NKV][nk][3 hd]
     uint16_t* vh = kcat + (size_t)NKV * nk * 3 * hd;
     uint16_t* vl = vh + (size_t)NKV * nk * hd;
     split_q_kernel<<<T, 256, 0, s>>>(b.qkv, nqkv, H, hd, qcat);
@@ -497,31 +502,37 @@ int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) 
     split_kv_kernel<<<(NKV * nk + 7) / 8, 256, 0, s>>>(kc, vc, m->ctx, nk, hd, NKV, kcat, vh, vl);
     CU(cudaGetLastError());
     const float one = 1.0f, zero = 0.0f;
-    const long long sK = (long long)nk * hd, sS = (long long)grp * T * ld;
-    // S = qcat . kcat^T: one GEMM over the concatenated 3 hd, written once
-    for (int g = 0; g < grp; g++)
-        CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, nk, T, 3 * hd, &one, kcat, CUDA_R_16BF,
-                                      3 * hd, 3 * sK, qcat + (size_t)g * 3 * hd, CUDA_R_16BF, H * 3 * hd,
-                                      (long long)grp * 3 * hd, &zero, S + (size_t)g * T * ld, CUDA_R_32F, ld, sS, NKV,
-                                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-    causal_softmax_kernel<<<H * T, kSmaxThreads, 0, s>>>(S, T, ld, pos0, 1.0f / sqrtf((float)hd), ph, pl);
-    CU(cudaGetLastError());
-    for (int g = 0; g < grp; g++) {
-        const uint16_t* A[3] = {vh, vl, vh};
-        const uint16_t* B[3] = {ph, ph, pl};
-        for (int i = 0; i < 3; i++)
-            CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, T, nk, &one, A[i], CUDA_R_16BF, hd,
-                                          sK, B[i] + (size_t)g * T * ld, CUDA_R_16BF, ld, sS, i ? &one : &zero,
-                                          b.ao + (size_t)g * hd, CUDA_R_32F, nq, (long long)grp * hd, NKV,
-                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    const long long sK = (long long)nk * hd;
+    for (int r0 = 0; r0 < T; r0 += tc) {
+        const int tn = T - r0 < tc ? T - r0 : tc;   // rows of this chunk
+        const int nkc = pos0 + r0 + tn;              // the positions they can see
+        const int ld = (nkc + 1) & ~1;
+        const long long sS = (long long)grp * tn * ld;
+        // S = qcat . kcat^T: one GEMM over the concatenated 3 hd, written once
+        for (int g = 0; g < grp; g++)
+            CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, nkc, tn, 3 * hd, &one, kcat, CUDA_R_16BF,
+                                          3 * hd, 3 * sK, qcat + ((size_t)r0 * H + g) * 3 * hd, CUDA_R_16BF,
+                                          H * 3 * hd, (long long)grp * 3 * hd, &zero, S + (size_t)g * tn * ld,
+                                          CUDA_R_32F, ld, sS, NKV, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+        causal_softmax_kernel<<<H * tn, kSmaxThreads, 0, s>>>(S, tn, ld, pos0 + r0, 1.0f / sqrtf((float)hd), ph, pl);
+        CU(cudaGetLastError());
+        for (int g = 0; g < grp; g++) {
+            const uint16_t* A[3] = {vh, vl, vh};
+            const uint16_t* B[3] = {ph, ph, pl};
+            for (int i = 0; i < 3; i++)
+                CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, tn, nkc, &one, A[i], CUDA_R_16BF,
+                                              hd, sK, B[i] + (size_t)g * tn * ld, CUDA_R_16BF, ld, sS,
+                                              i ? &one : &zero, b.ao + (size_t)r0 * nq + (size_t)g * hd, CUDA_R_32F,
+                                              nq, (long long)grp * hd, NKV, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+        }
     }
     return 1;
 }
 
 size_t attn_tensor_bytes(const RbtModelConfig& c, int T, int nk) {
     const size_t H = c.n_heads, nq = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * nk * c.head_dim;
-    const size_t ld = (size_t)((nk + 1) & ~1);
-    return H * T * ld * (4 + 2 + 2) + (size_t)T * nq * 3 * 2 + kv * 2 * 3 + kv * 2 * 2;
+    const size_t ld = (size_t)((nk + 1) & ~1), tc = (size_t)(T < kAttnRows ? T : kAttnRows);
+    return H * tc * ld * (4 + 2 + 2) + (size_t)T * nq * 3 * 2 + kv * 2 * 3 + kv * 2 * 2;
 }
 
 // the GEMM input rows: rmsnorm(src rows) with w, or src rows as they are (w == nullptr)

@@ -153,3 +153,30 @@ def test_prefill_matches_reference_engine(model_file, tmp_path):
         assert ids == want_ids, kind
     finally:
         m.close()
+
+
+@needs_ref
+@pytest.mark.gpu
+def test_prefill_long_prompt_in_causal_chunks(tmp_path):
+    """A 600-token prompt: the tensor-core attention takes its query rows in causal
+    chunks (512 + 88 rows, each against the positions it can see).  Every row's
+    logits against the engine's --dump within 1e-3, routing identical."""
+    from rabbit2_b200.model import ModelContext
+    cfg = dataclasses.replace(workload.tiny_olmoe_config(), dtype=DT_BF16, max_seq=1024)
+    path = str(tmp_path / "long.rbt2")
+    workload.write_model(path, cfg, seed=4)
+    prompt = np.random.default_rng(6).integers(0, cfg.vocab, size=600).tolist()
+    lg, rt = os.path.join(str(tmp_path), "l.bin"), os.path.join(str(tmp_path), "r.bin")
+    p = subprocess.run([REF, path, "--dump", lg, rt, "--ctx", "1024", *map(str, prompt)], capture_output=True,
+                       text=True)
+    assert p.returncode == 0, p.stderr
+    want_l = np.fromfile(lg, "<f4").reshape(len(prompt), cfg.vocab)
+    want_r = np.fromfile(rt, "<i4").reshape(len(prompt), cfg.n_layers, cfg.top_k)
+    m = ModelContext.from_file(path, ctx=1024)
+    try:
+        got_l, got_r = m.prefill(prompt, pos0=0, logit_rows=len(prompt))
+        np.testing.assert_array_equal(got_r, want_r)
+        err = np.abs(got_l.astype(np.float64) - want_l).max() / np.abs(want_l).max()
+        assert err < LOGIT_RTOL, err
+    finally:
+        m.close()
