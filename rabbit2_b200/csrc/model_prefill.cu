@@ -345,7 +345,6 @@ cudaError_t launch_attn_prefill(int hd, dim3 grid, cudaStream_t s, const float* 
 // ---------------------------------------------------------------- attention on the tensor cores (bf16 models)
 // scores = q . k as bf16 hi/lo GEMMs, a causal softmax kernel, O = P . V as GEMMs.
 constexpr int kSmaxThreads = 256;
-constexpr int kSmaxPer = 32;  // scores per thread (in pairs): cache positions <= 8192
 
 // K and V of cache positions [0, nk) of every kv head, as bf16: K rows
 // concatenated [hi | lo | hi] into kcat [n_kv][nk][3 hd] (against q's
@@ -392,64 +391,47 @@ __global__ void split_q_kernel(const float* qkv, int nqkv, int H, int hd, uint16
 }
 
 // Row (head h, query t) of the scores [H][T][nk] (nk: the even row stride, at
-// least the number of cache positions): att = dot * scale for positions
-// p <= pos0 + t, the softmax of rabbit2.c:399-405 (max, exp, sum, divide), and P
-// as bf16 hi/lo (0 past the causal limit, the padding included).
+// least the number of cache positions), one warp per row: att = dot * scale for
+// positions p <= pos0 + t, the softmax of rabbit2.c:399-405 -- p = exp(att - max)
+// / sum -- and P as bf16 hi/lo (0 past the causal limit, the padding included).
+// The max and the sum come from one pass with a running max per lane (rescaling
+// its sum), combined across the warp; a second pass writes P.
 __global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const float* S, int T, int nk, int pos0,
-                                                                      float scale, uint16_t* ph, uint16_t* pl) {
-    __shared__ float red[kSmaxThreads / 32];
-    const int row = blockIdx.x, t = row % T, tid = threadIdx.x, lim = pos0 + t;  // valid p <= lim
-    // thread tid takes the pairs (2 q, 2 q + 1), q = tid + k * threads (nk is even)
+                                                                      float scale, int rows, uint16_t* ph,
+                                                                      uint16_t* pl) {
+    const int row = blockIdx.x * (kSmaxThreads / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int t = row % T, lim = pos0 + t;  // valid p <= lim
     const float2* sr = reinterpret_cast<const float2*>(S + (size_t)row * nk);
-    float v[kSmaxPer];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < kSmaxPer / 2; k++) {
-        const int p = 2 * (tid + k * kSmaxThreads);
-        float2 x = make_float2(-INFINITY, -INFINITY);
-        if (p <= lim && p < nk) {
-            x = sr[p / 2];
-            x.x *= scale;
-            x.y = p + 1 <= lim ? x.y * scale : -INFINITY;
-        }
-        v[2 * k] = x.x;
-        v[2 * k + 1] = x.y;
-        mx = fmaxf(mx, fmaxf(x.x, x.y));
+    const int npairs_valid = lim / 2 + 1, npairs = nk / 2;
+    float m = -INFINITY, l = 0.0f;
+    for (int q = lane; q < npairs_valid; q += 32) {
+        const float2 x = sr[q];
+        const float a = x.x * scale;
+        const float b = 2 * q + 1 <= lim ? x.y * scale : -INFINITY;
+        const float mn = fmaxf(m, fmaxf(a, b));
+        l = l * expf(m - mn) + expf(a - mn) + (b == -INFINITY ? 0.0f : expf(b - mn));
+        m = mn;
     }
-    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 16));
-    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 1));
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int i = 1; i < kSmaxThreads / 32; i++) mx = fmaxf(mx, red[i]);
-    float sum = 0.0f;
+    float M = m;
 #pragma unroll
-    for (int k = 0; k < kSmaxPer; k++) {
-        v[k] = v[k] == -INFINITY ? 0.0f : expf(v[k] - mx);
-        sum += v[k];
-    }
-    sum = warp_sum(sum);
-    __syncthreads();
-    if ((tid & 31) == 0) red[tid >> 5] = sum;
-    __syncthreads();
-    float tot = 0.0f;
-    for (int i = 0; i < kSmaxThreads / 32; i++) tot += red[i];
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL_MASK, M, o));
+    float L = m == -INFINITY ? 0.0f : l * expf(m - M);
+    L = warp_sum(L);
     uint32_t* hr = reinterpret_cast<uint32_t*>(ph + (size_t)row * nk);
     uint32_t* lr = reinterpret_cast<uint32_t*>(pl + (size_t)row * nk);
-#pragma unroll
-    for (int k = 0; k < kSmaxPer / 2; k++) {
-        const int p = 2 * (tid + k * kSmaxThreads);
-        if (p < nk) {
-            const float p0 = v[2 * k] / tot, p1 = v[2 * k + 1] / tot;
-            const __nv_bfloat16 a0 = __float2bfloat16_rn(p0), a1 = __float2bfloat16_rn(p1);
-            const __nv_bfloat16 b0 = __float2bfloat16_rn(p0 - __bfloat162float(a0));
-            const __nv_bfloat16 b1 = __float2bfloat16_rn(p1 - __bfloat162float(a1));
-            hr[p / 2] = (uint32_t)__bfloat16_as_ushort(a0) | ((uint32_t)__bfloat16_as_ushort(a1) << 16);
-            lr[p / 2] = (uint32_t)__bfloat16_as_ushort(b0) | ((uint32_t)__bfloat16_as_ushort(b1) << 16);
+    for (int q = lane; q < npairs; q += 32) {
+        float p0 = 0.0f, p1 = 0.0f;
+        if (q < npairs_valid) {
+            const float2 x = sr[q];
+            p0 = expf(x.x * scale - M) / L;
+            p1 = 2 * q + 1 <= lim ? expf(x.y * scale - M) / L : 0.0f;
         }
+        const __nv_bfloat16 a0 = __float2bfloat16_rn(p0), a1 = __float2bfloat16_rn(p1);
+        const __nv_bfloat16 b0 = __float2bfloat16_rn(p0 - __bfloat162float(a0));
+        const __nv_bfloat16 b1 = __float2bfloat16_rn(p1 - __bfloat162float(a1));
+        hr[q] = (uint32_t)__bfloat16_as_ushort(a0) | ((uint32_t)__bfloat16_as_ushort(a1) << 16);
+        lr[q] = (uint32_t)__bfloat16_as_ushort(b0) | ((uint32_t)__bfloat16_as_ushort(b1) << 16);
     }
 }
 
@@ -514,7 +496,8 @@ int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) 
                                           3 * hd, 3 * sK, qcat + ((size_t)r0 * H + g) * 3 * hd, CUDA_R_16BF,
                                           H * 3 * hd, (long long)grp * 3 * hd, &zero, S + (size_t)g * tn * ld,
                                           CUDA_R_32F, ld, sS, NKV, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-        causal_softmax_kernel<<<H * tn, kSmaxThreads, 0, s>>>(S, tn, ld, pos0 + r0, 1.0f / sqrtf((float)hd), ph, pl);
+        causal_softmax_kernel<<<(H * tn + kSmaxThreads / 32 - 1) / (kSmaxThreads / 32), kSmaxThreads, 0, s>>>(
+            S, tn, ld, pos0 + r0, 1.0f / sqrtf((float)hd), H * tn, ph, pl);
         CU(cudaGetLastError());
         for (int g = 0; g < grp; g++) {
             const uint16_t* A[3] = {vh, vl, vh};
