@@ -47,6 +47,8 @@
 namespace rbt {
 void set_last_error(const char* msg);
 int moe_status_ok(RbtMoe* m);
+unsigned long long moe_workspace_generation(RbtMoe* m);
+unsigned* moe_status_word(RbtMoe* m);
 }  // namespace rbt
 
 namespace {
@@ -547,6 +549,8 @@ int enqueue_token(RbtModel* m, bool with_logits) {
     }
     CU(cudaMemcpyAsync(m->h_routing, m->routing, sizeof(int32_t) * c.n_layers * c.top_k, cudaMemcpyDeviceToHost, s));
     CU(cudaMemcpyAsync(m->h_status, m->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+    if (unsigned* ms = moe_status_word(m->moe))  // the MoE kernels' status comes back with the token
+        CU(cudaMemcpyAsync(m->h_status + 1, ms, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
     if (with_logits) {
         CU(launch_pdl(norm_gemv_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)D * 4, s,
                       (const float*)m->x, (const float*)m->final_norm, c.rms_eps, D, (const WT*)m->lm_head, c.vocab,
@@ -600,7 +604,8 @@ int init_state(RbtModel* m) {
     CU(cudaMallocHost((void**)&m->h_step, sizeof(Step)));
     CU(cudaMallocHost((void**)&m->h_logits, (size_t)c.vocab * 4));
     CU(cudaMallocHost((void**)&m->h_routing, (size_t)c.n_layers * c.top_k * 4));
-    CU(cudaMallocHost((void**)&m->h_status, sizeof(unsigned)));
+    CU(cudaMallocHost((void**)&m->h_status, 2 * sizeof(unsigned)));  // attention's, the MoE kernels'
+    m->h_status[0] = m->h_status[1] = 0;
     // the engine's RoPE angles (rope(), rabbit2.c:410-421): fp64 pow/cos/sin rounded to f32
     std::vector<float> cs((size_t)ctx * half), sn((size_t)ctx * half);
     for (int p = 0; p < ctx; p++)
@@ -747,6 +752,17 @@ int rbt_model_forward(RbtModel* m, int token, int pos, float* logits, int32_t* r
     for (int l = 0; l < c.n_layers; l++)
         if (!m->layers[l].loaded) return fail("layer %d not loaded (rbt_model_load_layer)", l);
     CU(cudaSetDevice(m->device));
+    // the graphs hold the MoE workspace's addresses: a larger call since they were
+    // captured (rbt_model_prefill) reallocated it, so capture them again
+    const unsigned long long gen = moe_workspace_generation(m->moe);
+    if (gen != m->graph_gen) {
+        for (cudaGraphExec_t& g : m->graph)
+            if (g) {
+                CU(cudaGraphExecDestroy(g));
+                g = nullptr;
+            }
+        m->graph_gen = gen;
+    }
     const int with = logits != nullptr;
     if (!m->graph[with] && !build_graph(m, with)) return 0;
     m->h_step->token = token;
@@ -758,7 +774,7 @@ int rbt_model_forward(RbtModel* m, int token, int pos, float* logits, int32_t* r
         CU(cudaMemset(m->status, 0, sizeof(unsigned)));
         return fail("attention: a bounded wait for the KV tiles ran out (code 0x%x)", st);
     }
-    if (!moe_status_ok(m->moe)) return 0;
+    if (m->h_status[1] && !moe_status_ok(m->moe)) return 0;  // (reports and clears it)
     if (logits) memcpy(logits, m->h_logits, sizeof(float) * c.vocab);
     if (routing_out) memcpy(routing_out, m->h_routing, sizeof(int32_t) * c.n_layers * c.top_k);
     return 1;

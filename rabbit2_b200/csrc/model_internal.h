@@ -77,5 +77,6 @@ struct RbtModel {
     rbt::PrefillBufs pf;
     // graphs: [0] without lm_head, [1] with
     cudaGraphExec_t graph[2] = {nullptr, nullptr};
+    unsigned long long graph_gen = 0;  // the MoE workspace generation the graphs were captured with
     int n_splits = 0;
 };

@@ -108,6 +108,8 @@ struct RbtMoe {
     cudaStream_t stream = nullptr;
     std::vector<Layer> layers;
     Workspace ws;
+    unsigned long long ws_gen = 0;  // workspace allocations so far
+    unsigned* h_status = nullptr;   // pinned host copy of the status word (host-pointer calls)
 };
 
 namespace {
@@ -188,6 +190,7 @@ int reserve(RbtMoe* m, int T) {
     if (m->ws.block) CU(cudaFree(m->ws.block));
     w.block = block;
     m->ws = w;
+    m->ws_gen++;  // captured graphs that use the old workspace are stale now
     return 1;
 }
 
@@ -484,16 +487,22 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
 }
 
 // A tensor-core pipeline wait that timed out leaves a code in the status word.
-int check_status(RbtMoe* m) {
-    if (!m->ws.block) return 1;
-    unsigned st = 0;
-    CU(cudaMemcpy(&st, m->ws.status, 4, cudaMemcpyDeviceToHost));
+// The status word's value st (read by the caller): on a timed-out wait, clear the
+// status and the one-token kernel's sync words, and report it.
+int status_error(RbtMoe* m, unsigned st) {
     if (st) {
         CU(cudaMemset(m->ws.status, 0, 4));
         CU(cudaMemset(m->ws.gbar, 0, (size_t)rbt::decode_sync_words(m->cfg.n_experts, m->cfg.top_k) * 4));
         return fail("tensor-core GEMM pipeline wait timed out (code 0x%x)", st);
     }
     return 1;
+}
+
+int check_status(RbtMoe* m) {
+    if (!m->ws.block) return 1;
+    unsigned st = 0;
+    CU(cudaMemcpy(&st, m->ws.status, 4, cudaMemcpyDeviceToHost));
+    return status_error(m, st);
 }
 
 // Host-pointer wrapper: stage through the workspace's device buffers.
@@ -514,8 +523,10 @@ int forward_host(RbtMoe* m, int layer, const float* x, float* out, int T, int32_
     if (routing)
         CU(cudaMemcpy2DAsync(routing, (size_t)routing_stride * 4, w.hrouting, (size_t)c.top_k * 4,
                              (size_t)c.top_k * 4, T, cudaMemcpyDeviceToHost, m->stream));
+    // the status word comes back with the results (one synchronisation per call)
+    CU(cudaMemcpyAsync(m->h_status, w.status, sizeof(unsigned), cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
-    return check_status(m);
+    return status_error(m, *m->h_status);
 }
 
 }  // namespace
@@ -524,6 +535,15 @@ namespace rbt {
 // 1 if the context's kernels reported no timed-out wait since the last check,
 // else 0 with the message set (for the whole-forward calls of model.cu)
 int moe_status_ok(RbtMoe* m) { return check_status(m); }
+
+// Changes whenever the workspace is reallocated (a larger call than any before):
+// a CUDA graph captured with the block/ffn device calls holds workspace
+// addresses and must be captured again after it changes.  (Used by model.cu.)
+unsigned long long moe_workspace_generation(RbtMoe* m) { return m ? m->ws_gen : 0; }
+
+// The device address of the status word (valid until the workspace generation
+// changes), or nullptr before the first reservation.  (Used by model.cu.)
+unsigned* moe_status_word(RbtMoe* m) { return m && m->ws.block ? m->ws.status : nullptr; }
 }  // namespace rbt
 
 extern "C" {
@@ -555,8 +575,10 @@ int rbt_moe_create(RbtMoe** out, const RbtMoeConfig* cfg, int device) {
     if (const char* v = getenv("RBT_MOE_GEMM_MIN_TOKENS")) m->gemm_min_tokens = atoi(v);
     m->layers.resize(c.n_layers);
     bool ok = cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device) == cudaSuccess &&
-              cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
+              cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaMallocHost((void**)&m->h_status, sizeof(unsigned)) == cudaSuccess;
     if (!ok) {
+        if (m->stream) cudaStreamDestroy(m->stream);
         delete m;
         return fail("cannot initialise CUDA device %d", device);
     }
@@ -578,6 +600,7 @@ void rbt_moe_destroy(RbtMoe* m) {
     cudaFree(m->ws.block);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
     cudaStreamDestroy(m->stream);
+    cudaFreeHost(m->h_status);
     delete m;
 }
 

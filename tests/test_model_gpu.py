@@ -180,3 +180,31 @@ def test_prefill_long_prompt_in_causal_chunks(tmp_path):
         assert err < LOGIT_RTOL, err
     finally:
         m.close()
+
+
+@pytest.mark.gpu
+def test_decode_after_a_longer_prefill_recaptures_its_graph(tmp_path):
+    """The per-token graph holds the MoE workspace's addresses; a prompt longer
+    than any call before reallocates that workspace.  Decoding after it must give
+    the same bits as on a context that ran the prompt first."""
+    from rabbit2_b200.model import ModelContext
+    cfg = dataclasses.replace(workload.tiny_olmoe_config(), dtype=DT_BF16)
+    path = str(tmp_path / "m.rbt2")
+    workload.write_model(path, cfg, seed=8)
+    prompt = np.random.default_rng(9).integers(0, cfg.vocab, size=96).tolist()
+    a = ModelContext.from_file(path, ctx=128)
+    b = ModelContext.from_file(path, ctx=128)
+    try:
+        la, ra = a.prefill(prompt, 0, logit_rows=1)
+        nxt = int(np.argmax(la[-1]))
+        want, want_r = a.forward(nxt, len(prompt))
+        b.forward(prompt[0], 0)  # captures the graph with the one-token workspace
+        lb, rb = b.prefill(prompt, 0, logit_rows=1)  # grows the workspace to 96 tokens
+        np.testing.assert_array_equal(lb, la)
+        np.testing.assert_array_equal(rb, ra)
+        got, got_r = b.forward(nxt, len(prompt))
+        np.testing.assert_array_equal(got, want)
+        np.testing.assert_array_equal(got_r, want_r)
+    finally:
+        a.close()
+        b.close()
