@@ -83,7 +83,12 @@ struct Workspace {
     int32_t *tb_e, *tb_p0, *tb_p1, *n_tb;
     bool tc_maps = false;
     CUtensorMap m_xhi[3], m_xlo[3], m_hhi[3], m_hlo[3];  // token-tile widths 32, 64, 128
+    // host-pointer block calls of up to kStageTokens tokens: hx, hrouting and status are
+    // one span of the block, returned by ONE copy into this pinned staging
+    void* pinned = nullptr;
+    size_t span = 0;              // bytes from hx to the end of status
 };
+constexpr int kStageTokens = 128;
 
 }  // namespace
 
@@ -139,22 +144,24 @@ int reserve(RbtMoe* m, int T) {
         {(void**)&w.hhi, SB * H * 2},            {(void**)&w.hlo, SB * H * 2},
         {(void**)&w.tb_e, ntb * 4},              {(void**)&w.tb_p0, ntb * 4},
         {(void**)&w.tb_p1, ntb * 4},             {(void**)&w.n_tb, 4},
-        {(void**)&w.status, 4},
         {(void**)&w.gbar, (size_t)rbt::decode_sync_words((int)E, (int)K) * 4},
         // (the token router keeps one 64-bit expert mask per token in tile_cnt)
         {(void**)&w.tile_cnt, std::max(tiles * E * 4, (size_t)T * 8)}, {(void**)&w.tile_base, tiles * E * 4},
         {(void**)&w.slot_rank, S * 4},
         {(void**)&w.xb, (size_t)T * D * 4},      {(void**)&w.logits, (size_t)T * E * 4},
         {(void**)&w.wt, S * 4},                  {(void**)&w.h, S * H * 4},
-        {(void**)&w.y, S * D * 4},               {(void**)&w.hx, (size_t)T * D * 4},
+        {(void**)&w.y, S * D * 4},
         {(void**)&w.hout, (size_t)T * D * 4},    {(void**)&w.idx, S * 4},
         {(void**)&w.counts, E * 4},              {(void**)&w.offsets, (E + 1) * 4},
         {(void**)&w.perm, S * 4},                {(void**)&w.slot_pos, S * 4},
         {(void**)&w.active, E * 4},              {(void**)&w.n_active, 4},
-        {(void**)&w.hrouting, S * 4},            {(void**)&w.tile_counter, tiles * 4},
+        {(void**)&w.tile_counter, tiles * 4},
         {(void**)&w.done_counter, 4},
         {(void**)&w.partials, rbt::decode_partials_bytes(m->sm_count, (int)D)},
         {(void**)&w.bscale, (SB > 0 ? SB : 1) * 4},
+        // last, in this order: the one span a small host-pointer block call returns
+        {(void**)&w.hx, (size_t)T * D * 4},      {(void**)&w.hrouting, S * 4},
+        {(void**)&w.status, 4},
     };
     size_t total = 0;
     for (auto& p : parts) total = align_up(total, 256) + p.bytes;
@@ -187,7 +194,13 @@ int reserve(RbtMoe* m, int T) {
                         rbt::make_map_2d(&w.m_hlo[i], w.hlo, c.expert_hidden, (long)SB, bn);
         }
     }
+    w.span = (size_t)((char*)w.status - (char*)w.hx) + 4;
+    if (T <= kStageTokens && cudaMallocHost(&w.pinned, w.span) != cudaSuccess) {
+        (void)cudaGetLastError();
+        w.pinned = nullptr;  // the calls then use one copy per output
+    }
     if (m->ws.block) CU(cudaFree(m->ws.block));
+    if (m->ws.pinned) cudaFreeHost(m->ws.pinned);
     w.block = block;
     m->ws = w;
     m->ws_gen++;  // captured graphs that use the old workspace are stale now
@@ -519,6 +532,21 @@ int forward_host(RbtMoe* m, int layer, const float* x, float* out, int T, int32_
     CU(cudaMemcpyAsync(w.hx, x, bytes, cudaMemcpyHostToDevice, m->stream));
     float* dout = block ? w.hx : w.hout;
     if (!forward(m, layer, w.hx, dout, T, routing ? w.hrouting : nullptr, c.top_k, m->stream, block)) return 0;
+    if (block && w.pinned && T <= kStageTokens) {
+        // x (in place), the routing rows and the status word: one span, one copy back
+        CU(cudaMemcpyAsync(w.pinned, w.hx, w.span, cudaMemcpyDeviceToHost, m->stream));
+        CU(cudaStreamSynchronize(m->stream));
+        const char* base = static_cast<const char*>(w.pinned);
+        memcpy(out, base, bytes);
+        if (routing) {
+            const int32_t* r = reinterpret_cast<const int32_t*>(base + ((char*)w.hrouting - (char*)w.hx));
+            for (int t = 0; t < T; t++)
+                memcpy(routing + (size_t)t * routing_stride, r + (size_t)t * c.top_k, sizeof(int32_t) * c.top_k);
+        }
+        unsigned st;
+        memcpy(&st, base + ((char*)w.status - (char*)w.hx), sizeof st);
+        return status_error(m, st);
+    }
     CU(cudaMemcpyAsync(out, dout, bytes, cudaMemcpyDeviceToHost, m->stream));
     if (routing)
         CU(cudaMemcpy2DAsync(routing, (size_t)routing_stride * 4, w.hrouting, (size_t)c.top_k * 4,
@@ -598,6 +626,7 @@ void rbt_moe_destroy(RbtMoe* m) {
         cudaFree(L.router_cm);
     }
     cudaFree(m->ws.block);
+    if (m->ws.pinned) cudaFreeHost(m->ws.pinned);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
     cudaStreamDestroy(m->stream);
     cudaFreeHost(m->h_status);
