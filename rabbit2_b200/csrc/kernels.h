@@ -39,6 +39,11 @@ struct RouterArgs {
     int tile_tokens;          // set by launch_router: tokens per tile of the per-tile permutation (0: one tile)
     const uint16_t* router_cm;  // the router in chain-major order (router_to_chain_major), or nullptr
     unsigned* status;         // error word (a bounded wait that ran out), or nullptr
+    // block form: xb = rmsnorm(x_raw, norm_w) first (written to xb, which then must
+    // not alias x_raw); the token router computes it itself, the others launch it
+    const float* x_raw;       // [T, D] or nullptr (xb given)
+    const float* norm_w;      // [D]
+    float eps;
 };
 // The token router's copy of a bf16 router [E, D]: chain-major, 16-byte groups
 // (E <= 64, D % 256 == 0; E * D * 2 bytes at `out`).

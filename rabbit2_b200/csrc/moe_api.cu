@@ -405,12 +405,13 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     if (m->path == 4 && !given)
         return fail("fused decode path requested but unavailable (needs T == 1, bf16, D <= 2048)");
     const float* xb = x;
-    if (block && !given) {
-        if (!clk.begin(0)) return 0;
-        CU(rbt::launch_rmsnorm(x, L.ffn_norm, w.xb, T, c.dim, c.rms_eps, s));
-        xb = w.xb;
-    }
     rbt::RouterArgs ra{};
+    if (block && !given) {  // xb = rmsnorm(x), inside the router's launch where it can
+        xb = w.xb;
+        ra.x_raw = x;
+        ra.norm_w = L.ffn_norm;
+        ra.eps = c.rms_eps;
+    }
     ra.xb = xb;
     ra.T = T; ra.D = c.dim; ra.E = c.n_experts; ra.K = c.top_k;
     ra.router = L.router; ra.dtype = c.dtype; ra.bias = L.bias; ra.norm_topk = c.norm_topk;

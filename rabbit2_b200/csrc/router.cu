@@ -798,9 +798,37 @@ __global__ void __launch_bounds__(kThreads) router_tok_kernel(RouterArgs a) {
             n_issued++;
         }
     }
+    // the block form's rmsnorm of this token (rabbit2.c:512), with the summation order
+    // of rmsnorm_kernel, so xb has the same bits as there; written to xb for the
+    // kernels that follow
+    float inv = 1.0f;
+    if (a.norm_w) {
+        const float* xr = a.x_raw + (size_t)t * D;
+        float ss = 0.0f;
+        for (int i = tid; i < D; i += kThreads) ss = fmaf(xr[i], xr[i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) s_red[warp] = ss;
+        __syncthreads();
+        if (tid < 32) {
+            float v = tid < kThreads / 32 ? s_red[tid] : 0.0f;
+            v = warp_sum(v);
+            if (tid == 0) s_red[0] = v;
+        }
+        __syncthreads();
+        inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s_red[0], (float)D), a.eps));
+    }
     // this token's xb, chain-major: xcm[c][j] = xb[t][c + 4 j] (rows 4 banks apart)
     for (int i4 = tid; i4 < q4; i4 += kThreads) {
-        const float4 v = reinterpret_cast<const float4*>(a.xb + (size_t)t * D)[i4];
+        float4 v;
+        if (a.norm_w) {
+            const float4 x = reinterpret_cast<const float4*>(a.x_raw + (size_t)t * D)[i4];
+            const float4 w = reinterpret_cast<const float4*>(a.norm_w)[i4];
+            v = make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
+                            __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
+            reinterpret_cast<float4*>(const_cast<float*>(a.xb) + (size_t)t * D)[i4] = v;
+        } else {
+            v = reinterpret_cast<const float4*>(a.xb + (size_t)t * D)[i4];
+        }
         xcm[i4] = v.x;
         xcm[xs + i4] = v.y;
         xcm[2 * xs + i4] = v.z;
@@ -1051,8 +1079,20 @@ cudaError_t launch_typed(const RouterArgs& a, cudaStream_t s, int* launches) {
         return !(v && v[0] == '0');
     }();
     if (tok_on && tok_ok(a) && a.T <= mid_tokens) {
-        // one CTA per token; softmax, top-k and the permutation in the same launch
+        // one CTA per token; rmsnorm (block form), softmax, top-k and the permutation
+        // in the same launch
         return launch_with_smem(router_tok_kernel, dim3(a.T), tok_smem_bytes(a.D, a.E), a, s);
+    }
+    if (a.norm_w) {  // the block form's rmsnorm as its own launch, then the router on xb
+        cudaError_t err = launch_rmsnorm(a.x_raw, a.norm_w, const_cast<float*>(a.xb), a.T, a.D, a.eps, s);
+        if (err != cudaSuccess) return err;
+        RouterArgs b = a;
+        b.norm_w = nullptr;
+        b.x_raw = nullptr;
+        int inner = 0;
+        err = launch_typed<WT>(b, s, &inner);
+        *launches = inner + 1;
+        return err;
     }
     if (a.T <= kSmallTokens || a.T <= mid_tokens) {
         // thread per chain: token tiles of 8 x expert groups of 8 (latency, not
