@@ -543,8 +543,9 @@ int reserve(RbtModel* m, int T, int pos0, int logit_rows) {
     if (T > b.cap) {
         void* old[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing};
         for (void* p : old) cudaFree(p);
-        b = PrefillBufs{b.cap,       nullptr,  nullptr,     nullptr,     nullptr, nullptr, nullptr,
-                        nullptr,     nullptr,  b.logit_rows, b.logits, b.att_bytes, b.att};
+        // capacity 0 until every buffer exists: a failed allocation leaves nothing to reuse
+        b = PrefillBufs{0,       nullptr,  nullptr,     nullptr,     nullptr, nullptr, nullptr,
+                        nullptr, nullptr,  b.logit_rows, b.logits, b.att_bytes, b.att};
         const size_t wide = (size_t)(c.dim > nq_of(c) ? c.dim : nq_of(c));
         const size_t rows = (size_t)T;
         CU(cudaMalloc((void**)&b.tokens, rows * 4));
