@@ -18,6 +18,9 @@ decode; --tokens 4096 is the prefill-sized layer call.
          oracle/_ref) on the host cores, on a bounded sample.
 
 --impl reference times only that CPU path (rank 0) and prints its line.
+--workload model-decode / model-prefill time the whole forward() of an
+OLMoE-1B-7B-shaped model on one GPU instead (rbt_model_forward per generated
+token, config 3; rbt_model_prefill for one prompt, config 4's unit of work).
 Multi-GPU (torchrun, N ranks): expert parallelism.  Rank g holds experts
 [g*64/N, (g+1)*64/N) of every layer and its own T tokens; each layer routes
 locally, sends every token once to each GPU that owns one of its experts (NCCL
