@@ -6,8 +6,9 @@ same model files, through the engine's CLI outputs:
   (max|d| / max|ref|, the north-star bar) and its routing rows identical;
 - 64 greedy tokens after the prompt identical to `--gen 64`.
 
-Models: config 1 (tiny OLMoE, f32), the same shape in bf16, and grouped-query
-variants (n_kv_heads < n_heads) in f32 and bf16.  A 128-token prompt plus 64 generated tokens
+Models: config 1 (tiny OLMoE, f32), the same shape in bf16, grouped-query
+variants (n_kv_heads < n_heads) in f32 and bf16, and head_dim 128 (OLMoE's) in f32
+and bf16.  A 128-token prompt plus 64 generated tokens
 spans three 64-position attention splits.
 """
 import dataclasses
@@ -34,10 +35,13 @@ def _cfg(kind):
         cfg = dataclasses.replace(cfg, n_heads=4, n_kv_heads=2, head_dim=64)
     elif kind == "gqa_bf16":  # the batched prompt's tensor-core attention with two heads per kv head
         cfg = dataclasses.replace(cfg, n_heads=4, n_kv_heads=2, head_dim=64, dtype=DT_BF16)
+    elif kind in ("hd128", "hd128_bf16"):  # OLMoE's head_dim: the 128-wide attention kernels
+        cfg = dataclasses.replace(cfg, n_heads=2, n_kv_heads=2, head_dim=128,
+                                  dtype=DT_BF16 if kind == "hd128_bf16" else cfg.dtype)
     return cfg
 
 
-@pytest.fixture(scope="module", params=["f32", "bf16", "gqa", "gqa_bf16"])
+@pytest.fixture(scope="module", params=["f32", "bf16", "gqa", "gqa_bf16", "hd128", "hd128_bf16"])
 def model_file(request, tmp_path_factory):
     cfg = _cfg(request.param)
     path = str(tmp_path_factory.mktemp("m") / f"tiny_{request.param}.rbt2")
