@@ -76,4 +76,6 @@ def test_bad_model_config_is_rejected_with_a_message():
     assert lib.rbt_model_create(C.byref(h), C.byref(good), cfg.max_seq + 1, 0) == 0
     assert b"ctx" in lib.rbt_moe_last_error()
     assert lib.rbt_model_forward(None, 0, 0, None, None) == 0
+    assert lib.rbt_model_prefill(None, None, 1, 0, None, 0, None) == 0
+    assert b"null model" in lib.rbt_moe_last_error()
     lib.rbt_model_destroy(None)
