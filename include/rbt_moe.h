@@ -179,6 +179,25 @@ typedef struct RbtMoeProfile {
  * out may be NULL. */
 int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
 
+/* Router logits of the most recent block/ffn/route call, [n_tokens, n_experts]
+ * f32 (host pointer; n_tokens <= that call's): the engine's s->router right
+ * after the matvec of rabbit2.c:513 (plus the optional bias), before the
+ * softmax.  Synchronises the device. */
+int rbt_moe_router_logits(RbtMoe *m, float *logits_out, int n_tokens);
+
+/* ---- Self-checks of the routing arithmetic (no counterpart in the reference:
+ * they expose, on their own, the two pieces the router reproduces bit for bit).
+ *   rbt_expf_device: d_out[i] = expf(x_i), x_i the float with bit pattern
+ *     first_bits + i, evaluated as this process's libm expf evaluates it (the
+ *     softmax's exp, rabbit2.c:403; rbt_host_expf_variant() says which of the
+ *     two x86-64 glibc builds of it the host resolved: 1 FMA, 0 without).
+ *   rbt_seq_sumsq_device: d_out[r] = the sequential f32 sum of d_x[r, i]^2 over
+ *     i = 0 .. n-1, rmsnorm's sum (rabbit2.c:394), for rows of n <= 16384 floats.
+ * Device pointers, enqueued on `stream` without synchronising. */
+int rbt_expf_device(uint32_t first_bits, int64_t n, float *d_out, void *stream);
+int rbt_seq_sumsq_device(const float *d_x, int rows, int n, float *d_out, void *stream);
+int rbt_host_expf_variant(void);
+
 /* The one-token MoE block for callers that cannot allocate GPU memory.  No
  * counterpart in the reference (its engine has no GPU and no allocator
  * constraints); it exists for code that runs inside a framework which already
@@ -207,6 +226,17 @@ int rbt_moe_profile(RbtMoe *m, int timing, int reset, RbtMoeProfile *out);
 int rbt_moe_decode_noalloc(const RbtMoeConfig *cfg, const float *d_ffn_norm, const void *d_router,
                            const float *d_router_bias, const void *d_experts, const float *d_x, float *d_out,
                            int32_t *d_routing_out, void *stream);
+
+/* Error status of the most recent rbt_moe_decode_noalloc kernel on the calling
+ * thread's current device.  rbt_moe_decode_noalloc returns 1 as soon as its
+ * kernel is enqueued, so it cannot report what goes wrong inside the kernel;
+ * this call copies the kernel's status word from the fixed array on `stream`,
+ * synchronises that stream and stores it in *status_out: 0 when the kernel
+ * completed normally, otherwise its error code -- 0x603 when no valid routing
+ * could be formed (NaN or Inf in d_x), 0x600-0x6ff when a bounded wait between
+ * CTAs ran out.  After a non-zero status d_out and d_routing_out hold no
+ * result.  Allocates nothing. */
+int rbt_moe_decode_noalloc_status(void *stream, unsigned *status_out);
 
 /* ---- The whole forward() on the GPU (rabbit2.c:455-550) ----
  * The engine's forward(Model*, State*, token, pos, routing_out) computes one

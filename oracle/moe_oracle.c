@@ -267,3 +267,74 @@ int orc_permute(const int32_t *idx, int T, int K, int E, int32_t *counts, int32_
     free(fill);
     return 1;
 }
+
+/* Router logits for T tokens, [T, E]: the matvec of rabbit2.c:513 (plus the
+ * optional bias), before the softmax. */
+int orc_router_logits(const OrcMoeLayer *L, const float *xb, int T, float *logits) {
+    for (int t = 0; t < T; t++) {
+        float *lg = logits + (size_t)t * L->E;
+        orc_matvec(lg, L->router, L->dtype, xb + (size_t)t * L->D, L->E, L->D);
+        if (L->router_bias)
+            for (int e = 0; e < L->E; e++) lg[e] += L->router_bias[e];
+    }
+    return 1;
+}
+
+/* out[r] = the sequential sum of x[r, i]^2, i = 0..n-1 (rmsnorm's ss, rabbit2.c:394). */
+void orc_seq_sumsq(const float *x, int rows, int n, float *out) {
+    for (int r = 0; r < rows; r++) {
+        const float *xr = x + (size_t)r * n;
+        float ss = 0.0f;
+        for (int i = 0; i < n; i++) ss += xr[i] * xr[i];
+        out[r] = ss;
+    }
+}
+
+/* Compare got[i] with libm expf(x_i), x_i the float with bit pattern first_bits + i
+ * (the host's expf, the one rabbit2.c:403 calls).  Returns the number of
+ * bit-level mismatches; *first_bad gets the first mismatching i (or -1). */
+typedef struct {
+    uint32_t first_bits;
+    int64_t i0, i1;
+    const float *got;
+    int64_t bad, first;
+} OrcExpfJob;
+
+static void *orc_expf_worker(void *p) {
+    OrcExpfJob *j = (OrcExpfJob *)p;
+    j->bad = 0;
+    j->first = -1;
+    for (int64_t i = j->i0; i < j->i1; i++) {
+        const uint32_t u = j->first_bits + (uint32_t)i;
+        float x, y;
+        memcpy(&x, &u, 4);
+        y = expf(x);
+        if (memcmp(&y, &j->got[i], 4) != 0) {
+            if (j->first < 0) j->first = i;
+            j->bad++;
+        }
+    }
+    return NULL;
+}
+
+int64_t orc_expf_mismatch(uint32_t first_bits, int64_t n, const float *got, int nthreads, int64_t *first_bad) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    OrcExpfJob jobs[256];
+    pthread_t th[256];
+    for (int k = 0; k < nthreads; k++) {
+        jobs[k].first_bits = first_bits;
+        jobs[k].i0 = n * k / nthreads;
+        jobs[k].i1 = n * (k + 1) / nthreads;
+        jobs[k].got = got;
+        pthread_create(&th[k], NULL, orc_expf_worker, &jobs[k]);
+    }
+    int64_t bad = 0, first = -1;
+    for (int k = 0; k < nthreads; k++) {
+        pthread_join(th[k], NULL);
+        bad += jobs[k].bad;
+        if (first < 0 && jobs[k].first >= 0) first = jobs[k].first;
+    }
+    if (first_bad) *first_bad = first;
+    return bad;
+}

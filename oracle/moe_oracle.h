@@ -30,4 +30,7 @@ int orc_moe_block(const OrcMoeLayer *L, const float *x, int T, float *x_out, int
                   int nthreads);
 int orc_router_topk(const OrcMoeLayer *L, const float *xb, int T, int32_t *idx, float *wt, float *probs_out);
 int orc_permute(const int32_t *idx, int T, int K, int E, int32_t *counts, int32_t *offsets, int32_t *perm);
+int orc_router_logits(const OrcMoeLayer *L, const float *xb, int T, float *logits);
+void orc_seq_sumsq(const float *x, int rows, int n, float *out);
+int64_t orc_expf_mismatch(uint32_t first_bits, int64_t n, const float *got, int nthreads, int64_t *first_bad);
 #endif

@@ -86,8 +86,11 @@ class Oracle(_Lib):
     def __init__(self):
         build()
         self.lib = C.CDLL(ORACLE_SO)
-        for name in ("orc_moe_ffn", "orc_moe_block", "orc_router_topk", "orc_permute"):
+        for name in ("orc_moe_ffn", "orc_moe_block", "orc_router_topk", "orc_permute", "orc_router_logits"):
             getattr(self.lib, name).restype = C.c_int
+        self.lib.orc_expf_mismatch.restype = C.c_int64
+        self.lib.orc_seq_sumsq.restype = None
+        self.lib.orc_rmsnorm.restype = None
 
     def moe_ffn(self, layer, xb, nthreads=1):
         """(moe [T,D], routing [T,K], weights [T,K]) for normalised input xb."""
@@ -107,6 +110,40 @@ class Oracle(_Lib):
         if not self.lib.orc_router_topk(C.byref(st), _ptr(xb), T, _ptr(idx), _ptr(wt), _ptr(probs)):
             raise RuntimeError("orc_router_topk failed")
         return idx, wt, probs
+
+    def router_logits(self, layer, xb):
+        """[T, E] router logits (rabbit2.c:513, plus the optional bias)."""
+        xb = np.ascontiguousarray(xb, dtype=np.float32)
+        T = xb.shape[0]
+        out = np.empty((T, layer.E), np.float32)
+        st = layer.cstruct()
+        self.lib.orc_router_logits(C.byref(st), _ptr(xb), T, _ptr(out))
+        return out
+
+    def rmsnorm(self, x, w, eps):
+        """[T, D] rows of rmsnorm(x[t], w) (rabbit2.c:392-397)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        out = np.empty_like(x)
+        for t in range(x.shape[0]):
+            self.lib.orc_rmsnorm(_ptr(out[t]), _ptr(x[t]), _ptr(w), x.shape[1], C.c_float(eps))
+        return out
+
+    def seq_sumsq(self, x):
+        """[rows] sequential f32 sums of squares (rmsnorm's ss, rabbit2.c:394)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, n = x.shape
+        out = np.empty(rows, np.float32)
+        self.lib.orc_seq_sumsq(_ptr(x), rows, n, _ptr(out))
+        return out
+
+    def expf_mismatch(self, first_bits, got, nthreads=8):
+        """(count, first index) of got[i] != libm expf(float with bits first_bits + i)."""
+        got = np.ascontiguousarray(got, dtype=np.float32)
+        first = C.c_int64(-1)
+        bad = self.lib.orc_expf_mismatch(C.c_uint32(first_bits), C.c_int64(got.size), _ptr(got), int(nthreads),
+                                         C.byref(first))
+        return int(bad), int(first.value)
 
     def permute(self, idx, E):
         idx = np.ascontiguousarray(idx, dtype=np.int32)

@@ -7,12 +7,15 @@
 // gathers its k inputs by slot position, so the result is deterministic (no
 // floating-point atomics).
 #include "common.cuh"
+#include "exact_math.cuh"
 #include "kernels.h"
 
 namespace rbt {
 namespace {
 
 constexpr int kThreads = 256;
+// the squares of one row in shared memory: dim <= 49152
+constexpr size_t kRmsnormMaxSmem = 192 * 1024;
 
 __global__ void __launch_bounds__(kThreads) combine_vec4_kernel(CombineArgs a) {
     const int D4 = a.D / 4;
@@ -52,25 +55,18 @@ __global__ void __launch_bounds__(kThreads) combine_scalar_kernel(CombineArgs a)
     }
 }
 
-// out[t] = (x[t] * inv) * w, inv = 1 / sqrtf(mean(x^2) + eps); one CTA per token.
-// The sum of squares is a parallel fp32 reduction (the reference's is sequential,
-// so xb may differ from it in the last bit).
+// out[t] = (x[t] * inv) * w, inv = 1 / sqrtf(mean(x^2) + eps); one CTA per token
+// (rabbit2.c:392-397).  The sum of squares is the reference's sequential f32 sum,
+// reproduced exactly by block_seq_sum over the squares staged in shared memory.
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* x, const float* w, float* out, int D,
                                                            float eps) {
-    __shared__ float s_part[kThreads / 32];
+    extern __shared__ float s_sq[];
+    __shared__ SeqSumSmem s_seq;
     const float* xr = x + (size_t)blockIdx.x * D;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < D; i += kThreads) ss = fmaf(xr[i], xr[i], ss);
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = ss;
+    for (int i = threadIdx.x; i < D; i += kThreads) s_sq[i] = __fmul_rn(xr[i], xr[i]);
     __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < kThreads / 32 ? s_part[threadIdx.x] : 0.0f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) s_part[0] = v;
-    }
-    __syncthreads();
-    const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s_part[0], (float)D), eps));
+    const float ss = block_seq_sum<kThreads>(s_sq, D, s_seq);
+    const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
     float* o = out + (size_t)blockIdx.x * D;
     for (int i = threadIdx.x; i < D; i += kThreads) o[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
@@ -91,7 +87,14 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s) {
 
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, int D, float eps, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<T, kThreads, 0, s>>>(x, w, out, D, eps);
+    const size_t smem = (size_t)D * sizeof(float);
+    if (smem > kRmsnormMaxSmem) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {  // the attribute belongs to the current device's context
+        cudaError_t err = cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)kRmsnormMaxSmem);
+        if (err != cudaSuccess) return err;
+    }
+    rmsnorm_kernel<<<T, kThreads, smem, s>>>(x, w, out, D, eps);
     return cudaGetLastError();
 }
 

@@ -11,14 +11,15 @@
 //
 //   0  every CTA: bulk-copies its router row(s) and ffn_norm into shared memory
 //      (static weights, so before griddepcontrol.wait: this overlaps the
-//      previous kernel's tail), then x; rmsnorm(x) for the block form, the same
-//      fixed-order reduction in every CTA so all hold the same xb
+//      previous kernel's tail), then x; rmsnorm(x) for the block form with the
+//      reference's sequential sum of squares (block_seq_sum), so every CTA holds
+//      the reference's xb bits
 //   1  CTAs compute router logits -- the four sequential chains of the
 //      reference's scalar matvec (rabbit2.c:378-387), separately rounded
 //      products and sums, (s0+s1)+(s2+s3) -- each expert by two CTAs when the
 //      grid has room; a logit is published with its ready bit in one 64-bit word
-//   2  every CTA, as soon as all E logits are published: softmax (exp, then the
-//      sequential sum in expert order, rabbit2.c:399-405) and top-k (selection
+//   2  every CTA, as soon as all E logits are published: softmax (the host's
+//      expf, then the sequential sum in expert order, rabbit2.c:399-405) and top-k (selection
 //      order = rank: higher probability, or equal and lower index); CTA 0
 //      publishes the routing outputs
 //   3  units of 8 hidden rows of one chosen expert, a contiguous range per CTA.
@@ -37,7 +38,29 @@
 #include <cuda_bf16.h>
 #include <stdlib.h>
 
+#ifdef RBT_DECODE_TIMELINE
+// Optional phase timestamps (%globaltimer) of every CTA, read back with
+// rbt_decode_timeline_read(); built only with -DRBT_DECODE_TIMELINE.
+// Two buffers, alternating by launch, so consecutive launches can be compared.
+namespace rbt {
+__device__ unsigned long long g_timeline[2 * 256 * 32];
+__device__ unsigned g_timeline_seq;
+}  // namespace rbt
+// block_seq_sum's own phases, slots 20..25 of both buffers (no load of the
+// launch parity on the measured path: the stores are fire-and-forget)
+#define RBT_SEQ_STAMP(i)                                                          \
+    do {                                                                          \
+        unsigned long long t_;                                                    \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                   \
+        if (blockIdx.x < 256) {                                                   \
+            ::rbt::g_timeline[blockIdx.x * 32 + 20 + (i)] = t_;                   \
+            ::rbt::g_timeline[(256 + blockIdx.x) * 32 + 20 + (i)] = t_;           \
+        }                                                                         \
+    } while (0)
+#endif
+
 #include "common.cuh"
+#include "exact_math.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
 
@@ -76,11 +99,6 @@ constexpr int kSyncHead = 32;
 constexpr int kLogitStride = 16;  // 64-bit words between two experts' logit words
 
 #ifdef RBT_DECODE_TIMELINE
-// Optional phase timestamps (%globaltimer) of every CTA, read back with
-// rbt_decode_timeline_read(); built only with -DRBT_DECODE_TIMELINE.
-// Two buffers, alternating by launch, so consecutive launches can be compared.
-__device__ unsigned long long g_timeline[2 * 256 * 32];
-__device__ unsigned g_timeline_seq;
 #define TIMELINE(i)                                                                                   \
     do {                                                                                              \
         if (blockIdx.x < 256) g_timeline[(tl_par * 256 + blockIdx.x) * 32 + (i)] = globaltimer_ns(); \
@@ -169,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ __align__(16) float s_h[kSlots][kGURows];
     __shared__ float s_red[kThreads / 32];
     __shared__ int s_fail;
+    __shared__ SeqSumSmem s_seq;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = a.D, H = a.H, E = a.E, K = a.K;
@@ -214,39 +233,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_load(norm_s, a.ffn_norm, (uint32_t)D * 4, &nbar);
         }
     }
+    const uint64_t exp_tab = expf_tab_lane();  // the softmax's table entry of this lane
     // x, the sync words and every output may belong to the previous kernel in
     // the stream until this returns (programmatic dependent launch)
     pdl_wait();
     pdl_launch_dependents();
     // ---------------------------------------------------------------- phase 0
-    // x straight from L2 (the previous kernel wrote it) into registers, squares on the
-    // way: thread t holds the float4s t and t + kThreads (D <= 2048 = 2 x 4 x 288 - 256)
+    // x straight from L2 (the previous kernel wrote it) into registers; for the block
+    // form the squares go to shared memory (the products area, free until phase 1):
+    // thread t holds the float4s t and t + kThreads (D <= 2048 = 2 x 4 x 288 - 256)
     const int n4 = D / 4;
     float4 xv[2];
-    float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < 2; k++) {
         const int i4 = tid + k * kThreads;
         xv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i4 < n4) {
             xv[k] = __ldcg(reinterpret_cast<const float4*>(a.x) + i4);
-            ss = fmaf(xv[k].x, xv[k].x, ss);
-            ss = fmaf(xv[k].y, xv[k].y, ss);
-            ss = fmaf(xv[k].z, xv[k].z, ss);
-            ss = fmaf(xv[k].w, xv[k].w, ss);
+            if (a.ffn_norm)
+                reinterpret_cast<float4*>(prods)[i4] =
+                    make_float4(__fmul_rn(xv[k].x, xv[k].x), __fmul_rn(xv[k].y, xv[k].y),
+                                __fmul_rn(xv[k].z, xv[k].z), __fmul_rn(xv[k].w, xv[k].w));
         }
     }
     if (tid == 0) TIMELINE(13);
-    ss = warp_sum(ss);
-    if (lane == 0) s_red[warp] = ss;
-    __syncthreads();  // the warp sums, and the mbarrier initialisation
-    if (a.ffn_norm) {  // rmsnorm, the same fixed-order reduction in every CTA
+    __syncthreads();  // the squares, and the mbarrier initialisation
+    if (a.ffn_norm) {  // rmsnorm (rabbit2.c:392-397) with the reference's sequential sum of squares
+        const float tot = block_seq_sum_l<kThreads, 8>(prods, D, s_seq);  // D <= 2048 <= 288 * 8
+        if (tid == 0) TIMELINE(19);
         if (!mbar_wait_bounded(&nbar, 0, kWaitNs)) {
             record_error(a.status, 0x605);
             s_fail = 1;
         }
-        float tot = 0.0f;
-        for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
         const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), a.eps));
 #pragma unroll
         for (int k = 0; k < 2; k++) {
@@ -367,8 +385,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tid == 0) TIMELINE(16);
         mx = s_red[0];
         for (int w = 1; w < (E + 31) / 32; w++) mx = fmaxf(mx, s_red[w]);
-        // exp in double, rounded once (correctly rounded expf)
-        const float pe = tid < E ? (float)exp((double)__fsub_rn(lg, mx)) : 0.0f;
+        // the host libm's expf (rabbit2.c:403), by whole warps
+        float pe = 0.0f;
+        if (warp < (E + 31) / 32) {
+            const float v = expf_ref_warp(tid < E ? __fsub_rn(lg, mx) : 0.0f, a.expf_fma, exp_tab);
+            if (tid < E) pe = v;
+        }
         if (tid < E) s_prob[tid] = pe;
         __syncthreads();
         if (tid == 0) TIMELINE(17);
@@ -579,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float gs = warp_sum((f2sum(g[0]) + f2sum(g[1])) + (f2sum(g[2]) + f2sum(g[3])));
             const float us = warp_sum((f2sum(up[0]) + f2sum(up[1])) + (f2sum(up[2]) + f2sum(up[3])));
             // silu(h1) * h3 (rabbit2.c:407, :536), times the expert's combine weight
-            if (lane == 0) s_h[slot][warp] = gs / (1.0f + expf(-gs)) * us * s_wpos[pa];
+            if (lane == 0) s_h[slot][warp] = __fmul_rn(__fmul_rn(silu_ref(gs, a.expf_fma), us), s_wpos[pa]);
             // every consumer warp reaches this barrier once per unit, and the
             // barrier's OR of the timeouts ends the loop in all of them together
             if (named_sync_or(1, kConsumers, !got)) {
@@ -823,13 +845,15 @@ cudaError_t launch_decode_fused(const DecodeArgs& a, const CUtensorMap& w2map, i
     cfg.attrs = attr;
     cfg.numAttrs = (g_pdl_refused || !decode_pdl_enabled()) ? 1 : 2;
     auto kernel = a.w2t ? moe_decode_fused_kernel<true> : moe_decode_fused_kernel<false>;
-    err = cudaLaunchKernelEx(&cfg, kernel, a, w2map);
+    DecodeArgs b = a;
+    b.expf_fma = host_expf_fma();
+    err = cudaLaunchKernelEx(&cfg, kernel, b, w2map);
     if (err != cudaSuccess && cfg.numAttrs == 2) {
         // a driver that refuses the pair launches without the overlap
         (void)cudaGetLastError();
         g_pdl_refused = true;
         cfg.numAttrs = 1;
-        err = cudaLaunchKernelEx(&cfg, kernel, a, w2map);
+        err = cudaLaunchKernelEx(&cfg, kernel, b, w2map);
     }
     return err;
 }

@@ -13,7 +13,10 @@
 // The array below is per GPU and lives until the process exits.  Host code may
 // not use its name as a device address (on the host the name only stands in
 // for the symbol), so set-up asks the runtime for the device address once per
-// device, with that device current, and passes that pointer to the kernel.
+// device and CUDA context, with that device current, and passes that pointer
+// to the kernel.  A device reset destroys the context and may move the array;
+// the next call sees a different current context and looks the address up
+// again.
 // All calls on a GPU share the array and find the previous call's contents in
 // it: the counters that must start at zero are cleared on the caller's stream
 // before every launch, and two calls whose kernels overlap on the GPU (different
@@ -40,6 +43,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 struct DeviceSetup {
     void* scratch = nullptr;  // device address of g_noalloc_scratch on this GPU
+    void* ctx = nullptr;      // the CUDA context that address belongs to
     int sm_count = 0;
 };
 DeviceSetup g_setup[kMaxDevices];
@@ -59,15 +63,37 @@ int fail(const char* fmt, ...) {
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
+// The calling thread's current CUDA context (driver API, through the runtime's
+// entry-point query so that the library needs no link against libcuda).
+void* current_context() {
+    using Fn = CUresult (*)(CUcontext*);
+    static Fn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (Fn) nullptr;
+        return reinterpret_cast<Fn>(p);
+    }();
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
+// Set-up for the current device (see above); false with the error recorded.
+bool device_setup(DeviceSetup* out);
+
 // Byte offsets of the scratch parts for one configuration; returns the total.
+// The status word comes first, at the same place for every model, so that
+// rbt_moe_decode_noalloc_status can read it without the call's configuration.
 struct Layout {
     size_t logits, partials, idx, wt, counts, offsets, perm, slot_pos, active, n_active, sync, status, total;
 };
 Layout layout_for(int E, int K, int D, int grid) {
     Layout l{};
     size_t o = 0;
-    l.sync = o;       o = align256(o + (size_t)rbt::decode_sync_words(E, K) * sizeof(unsigned));
     l.status = o;     o = align256(o + sizeof(unsigned));
+    l.sync = o;       o = align256(o + (size_t)rbt::decode_sync_words(E, K) * sizeof(unsigned));
     l.n_active = o;   o = align256(o + sizeof(int32_t));
     l.logits = o;     o = align256(o + (size_t)E * sizeof(float));
     l.counts = o;     o = align256(o + (size_t)E * sizeof(int32_t));
@@ -101,29 +127,8 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     if ((reinterpret_cast<uintptr_t>(d_ffn_norm) % 16) != 0)
         return fail("rbt_moe_decode_noalloc: d_ffn_norm must be 16-byte aligned");
 
-    // once per device, with that device current: the device address of the array
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(err));
-    if (dev < 0 || dev >= kMaxDevices) return fail("rbt_moe_decode_noalloc: device %d beyond %d", dev, kMaxDevices);
     DeviceSetup setup;
-    {
-        std::lock_guard<std::mutex> lock(g_setup_mutex);
-        if (!g_setup[dev].scratch) {
-            void* p = nullptr;
-            err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-            if (err != cudaSuccess)
-                return fail("rbt_moe_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                            cudaGetErrorString(err));
-            int sms = 0;
-            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-            if (err != cudaSuccess)
-                return fail("rbt_moe_decode_noalloc: cannot query device %d: %s", dev, cudaGetErrorString(err));
-            g_setup[dev].scratch = p;
-            g_setup[dev].sm_count = sms;
-        }
-        setup = g_setup[dev];
-    }
+    if (!device_setup(&setup)) return 0;
     const Layout l = layout_for(c.n_experts, c.top_k, c.dim, setup.sm_count);
     if (l.total > kScratchBytes)
         return fail("rbt_moe_decode_noalloc: this model needs %zu bytes of scratch on this GPU (%d SMs x dim "
@@ -135,7 +140,7 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     uint8_t* base = static_cast<uint8_t*>(setup.scratch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // the cross-CTA counters and the status word must start at zero
-    err = cudaMemsetAsync(base, 0, l.logits, s);
+    cudaError_t err = cudaMemsetAsync(base, 0, l.logits, s);
     if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: cudaMemsetAsync failed: %s", cudaGetErrorString(err));
 
     rbt::DecodeArgs a{};
@@ -167,5 +172,48 @@ extern "C" int rbt_moe_decode_noalloc(const RbtMoeConfig* cfg, const float* d_ff
     a.status = reinterpret_cast<unsigned*>(base + l.status);
     err = rbt::launch_decode_fused(a, w2map, setup.sm_count, s);
     if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: launch failed: %s", cudaGetErrorString(err));
+    return 1;
+}
+
+namespace {
+
+bool device_setup(DeviceSetup* out) {
+    // once per device and context, with that device current: the device address of the array
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return fail("rbt_moe_decode_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(err));
+    if (dev < 0 || dev >= kMaxDevices) return fail("rbt_moe_decode_noalloc: device %d beyond %d", dev, kMaxDevices);
+    // a runtime call first makes the device's primary context current
+    int sms = 0;
+    err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess)
+        return fail("rbt_moe_decode_noalloc: cannot query device %d: %s", dev, cudaGetErrorString(err));
+    void* ctx = current_context();
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (!g_setup[dev].scratch || g_setup[dev].ctx != ctx) {
+        void* p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (err != cudaSuccess)
+            return fail("rbt_moe_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                        cudaGetErrorString(err));
+        g_setup[dev].scratch = p;
+        g_setup[dev].ctx = ctx;
+        g_setup[dev].sm_count = sms;
+    }
+    *out = g_setup[dev];
+    return true;
+}
+
+}  // namespace
+
+extern "C" int rbt_moe_decode_noalloc_status(void* stream, unsigned* status_out) {
+    if (!status_out) return fail("rbt_moe_decode_noalloc_status: null argument");
+    DeviceSetup setup;
+    if (!device_setup(&setup)) return 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaMemcpyAsync(status_out, setup.scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess)
+        return fail("rbt_moe_decode_noalloc_status: reading the status word failed: %s", cudaGetErrorString(err));
     return 1;
 }

@@ -11,6 +11,7 @@
 // w2[D,H] row-major -- the .rbt2 blob, uploaded unchanged.  h[p, H] and y[p, D]
 // are indexed by the slot's position p in expert-grouped order.
 #include "common.cuh"
+#include "exact_math.cuh"
 #include "kernels.h"
 
 namespace rbt {
@@ -20,7 +21,8 @@ constexpr int kThreads = 256;
 // MT: routed slots applied per pass over a weight row (1 when T == 1, where
 // every chosen expert has one token); UNR: 16-byte vectors per lane in flight.
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+// silu(g) * u (rabbit2.c:407, :536) with the host's expf
+__device__ __forceinline__ float silu_mul(float g, float u, int fma) { return __fmul_rn(silu_ref(g, fma), u); }
 
 // acc[i] += dot(w[V], x_i[V]) for the m slots of this pass.
 template <int V, int MT>
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) gateup_gemv_kernel(GemvArgs a) {
             for (int i = 0; i < kMaxTok; i++) {
                 if (i < m) {
                     const float g = warp_sum(acc1[i]), u = warp_sum(acc3[i]);
-                    if (lane == 0) a.h[(size_t)(pb + i) * H + r] = silu_mul(g, u);
+                    if (lane == 0) a.h[(size_t)(pb + i) * H + r] = silu_mul(g, u, a.expf_fma);
                 }
             }
         }
@@ -228,7 +230,11 @@ cudaError_t launch_persistent(KernelT kernel, const GemvArgs& a, cudaStream_t s)
                       : launch_persistent(KERNEL<float, true, 4>, a, s);                                \
     return one ? launch_persistent(KERNEL<float, false, 1>, a, s) : launch_persistent(KERNEL<float, false, 4>, a, s);
 
-cudaError_t launch_gateup_gemv(const GemvArgs& a, cudaStream_t s) { RBT_GEMV_DISPATCH(gateup_gemv_kernel) }
+cudaError_t launch_gateup_gemv(const GemvArgs& args, cudaStream_t s) {
+    GemvArgs a = args;
+    a.expf_fma = host_expf_fma();
+    RBT_GEMV_DISPATCH(gateup_gemv_kernel)
+}
 
 cudaError_t launch_down_gemv(const GemvArgs& a, cudaStream_t s) { RBT_GEMV_DISPATCH(down_gemv_kernel) }
 

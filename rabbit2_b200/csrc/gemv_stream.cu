@@ -23,6 +23,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "exact_math.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
 
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_stream_kernel(StreamArgs a
                 for (int i = 0; i < MT; i++) {
                     if (i < m) {
                         const float gs = warp_sum(g[i]), us = warp_sum(up[i]);
-                        if (lane == 0) a.h[(size_t)(pb + i) * H + r] = gs / (1.0f + expf(-gs)) * us;
+                        if (lane == 0) a.h[(size_t)(pb + i) * H + r] = __fmul_rn(silu_ref(gs, a.expf_fma), us);
                     }
                 }
             }
@@ -365,7 +366,9 @@ bool stream_supported(const StreamArgs& a, int dtype) {
            (reinterpret_cast<uintptr_t>(a.experts) % 16) == 0 && (reinterpret_cast<uintptr_t>(a.xb) % 16) == 0;
 }
 
-cudaError_t launch_gateup_stream(const StreamArgs& a, int grid, cudaStream_t s) {
+cudaError_t launch_gateup_stream(const StreamArgs& args, int grid, cudaStream_t s) {
+    StreamArgs a = args;
+    a.expf_fma = host_expf_fma();
     const size_t smem = (size_t)kStagesGU * 2 * kRows * a.D * 2 + 2 * kStagesGU * 8;
     if (a.T == 1 && a.D <= 2048 && a.D % 256 == 0)
         return launch_pdl(gateup_stream_kernel<1, true>, grid, smem, a, s);

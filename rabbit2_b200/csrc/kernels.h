@@ -11,6 +11,11 @@ namespace rbt {
 constexpr int kMaxExperts = 256;  // router/top-k keeps E logits per token in one warp
 constexpr int kMaxTopK = 64;      // MAX_TOPK, rabbit2.c:59
 
+// 1 when this process's libm expf is the FMA-contracted evaluation of the table
+// method (exact_math.cuh), 0 for the separately rounded one; probed once on the
+// host, so the GPU softmax reproduces the host's expf bit for bit.
+int host_expf_fma();
+
 // K1: router logits + softmax + top-k (+ the routed-slot permutation, done by
 // the last CTA of the grid).
 struct RouterArgs {
@@ -44,6 +49,7 @@ struct RouterArgs {
     const float* x_raw;       // [T, D] or nullptr (xb given)
     const float* norm_w;      // [D]
     float eps;
+    int expf_fma;             // host_expf_fma(): which evaluation of expf the host's libm uses
 };
 // The token router's copy of a bf16 router [E, D]: chain-major, 16-byte groups
 // (E <= 64, D % 256 == 0; E * D * 2 bytes at `out`).
@@ -68,6 +74,7 @@ struct GemvArgs {
     float* h;                 // [T*K, H] SwiGLU activations, permuted order
     float* y;                 // [T*K, D] expert outputs, permuted order
     int grid;                 // CTAs to launch
+    int expf_fma;             // set by the launchers: host_expf_fma()
 };
 cudaError_t launch_gateup_gemv(const GemvArgs& a, cudaStream_t s);
 cudaError_t launch_down_gemv(const GemvArgs& a, cudaStream_t s);
@@ -100,6 +107,7 @@ struct StreamArgs {
     const float* wt;
     float* h;                 // [T*K, H]
     unsigned* status;
+    int expf_fma;             // set by the launchers: host_expf_fma()
 };
 bool stream_supported(const StreamArgs& a, int dtype);
 cudaError_t launch_gateup_stream(const StreamArgs& a, int grid, cudaStream_t s);
@@ -127,6 +135,7 @@ struct DecodeArgs {
     int32_t* routing_out;     // [K] or nullptr
     unsigned* sync;           // [decode_sync_words(E, K)] cross-CTA counters, zero between calls
     unsigned* status;
+    int expf_fma;             // host_expf_fma()
 };
 int decode_sync_words(int E, int K);
 size_t decode_partials_bytes(int grid, int D);

@@ -115,6 +115,7 @@ struct RbtMoe {
     Workspace ws;
     unsigned long long ws_gen = 0;  // workspace allocations so far
     unsigned* h_status = nullptr;   // pinned host copy of the status word (host-pointer calls)
+    int last_routed = 0;            // tokens the most recent routed call computed logits for
 };
 
 namespace {
@@ -380,6 +381,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     Workspace& w = m->ws;
     StageClock clk{m, s};
     m->prof.calls++;
+    if (!given) m->last_routed = T;
     if (!given && (m->path == 0 || m->path == 4) && L.dec &&
         (!block || (reinterpret_cast<uintptr_t>(L.ffn_norm) % 16) == 0) &&
         rbt::decode_fused_supported(T, c.dim, c.expert_hidden, c.n_experts, c.top_k, c.dtype, L.experts,
@@ -744,6 +746,7 @@ int rbt_moe_route_device(RbtMoe* m, int layer, const float* d_x, int n_tokens, i
     cudaStream_t s = (cudaStream_t)stream;
     StageClock clk{m, s};
     m->prof.calls++;
+    m->last_routed = n_tokens;
     if (block) {
         if (!clk.begin(0)) return 0;
         CU(rbt::launch_rmsnorm(d_x, L.ffn_norm, d_xb, n_tokens, c.dim, c.rms_eps, s));
@@ -783,6 +786,18 @@ int rbt_moe_expert_histogram(RbtMoe* m, int32_t* counts_out) {
     }
     CU(cudaDeviceSynchronize());
     CU(cudaMemcpy(counts_out, m->ws.counts, sizeof(int32_t) * (size_t)m->cfg.n_experts, cudaMemcpyDeviceToHost));
+    return 1;
+}
+
+int rbt_moe_router_logits(RbtMoe* m, float* logits_out, int n_tokens) {
+    if (!m || !logits_out) return fail("null argument");
+    if (n_tokens < 1 || n_tokens > m->last_routed)
+        return fail("n_tokens %d outside [1, %d] (the tokens of the most recent routed call)", n_tokens,
+                    m->last_routed);
+    if (!set_device(m)) return 0;
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(logits_out, m->ws.logits, sizeof(float) * (size_t)n_tokens * m->cfg.n_experts,
+                  cudaMemcpyDeviceToHost));
     return 1;
 }
 

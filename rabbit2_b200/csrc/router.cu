@@ -6,10 +6,11 @@
 //    over i = 0,1,2,3 (mod 4), tail folded into chain 0, combined as
 //    (s0+s1)+(s2+s3) (rabbit2.c:378-387).  Every product and sum is an explicit
 //    __fmul_rn / __fadd_rn: the reference has no FMA, so no contraction here.
-//  * softmax: the max, then exp(l - max) rounded to f32, a sequential sum in
-//    expert order, then an IEEE division (rabbit2.c:399-405).  exp is taken in
-//    double and rounded once, i.e. correctly rounded; glibc's expf equals that
-//    except on ~8e-5 of inputs, where the two differ by one ulp.
+//  * softmax: the max, then expf(l - max), a sequential sum in expert order,
+//    then an IEEE division (rabbit2.c:399-405).  expf is the host libm's own
+//    method, bit for bit (expf_ref, exact_math.cuh).
+//  * the block form's rmsnorm (rabbit2.c:392-397): the sum of squares is the
+//    reference's sequential f32 sum, reproduced exactly (block_seq_sum).
 //  * top-k: K rounds of "largest unused probability, lowest index on ties"
 //    (strict '>' scan, rabbit2.c:519-528).
 //
@@ -19,11 +20,36 @@
 // returned to zero by the CTA that consumed them, so no memset between calls.
 #include <stdlib.h>
 
+#include <math.h>
+#include <stdio.h>
+
 #include "common.cuh"
+#include "exact_math.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
 
 namespace rbt {
+
+int host_expf_fma() {
+    static int variant = -1;
+    if (variant < 0) {
+        // expf(-0x1.f8cbb2p+5) is one of the two floats on which the contracted
+        // and the separately rounded evaluations differ
+        volatile float x = -0x1.f8cbb2p+5f;
+        const float y = expf(x);
+        if (y == 0x1.f45326p-92f) {
+            variant = 1;
+        } else if (y == 0x1.f45324p-92f) {
+            variant = 0;
+        } else {
+            fprintf(stderr, "rbt_moe: this libm's expf(%a) = %a is not the table method's; routing can differ "
+                            "from the host engine where two probabilities are within an ulp\n", (double)x, (double)y);
+            variant = 1;
+        }
+    }
+    return variant;
+}
+
 namespace {
 
 using namespace tc;
@@ -152,10 +178,12 @@ __device__ void topk_token(const RouterArgs& a, const float* lrow, int t, float*
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, o));
     float p[NJ];
+    const uint64_t tab = expf_tab_lane();
 #pragma unroll
     for (int j = 0; j < NJ; j++) {
         const int e = lane + 32 * j;
-        p[j] = (e < E) ? (float)exp((double)__fsub_rn(l[j], mx)) : 0.0f;
+        const float v = expf_ref_warp(e < E ? __fsub_rn(l[j], mx) : 0.0f, a.expf_fma, tab);
+        p[j] = (e < E) ? v : 0.0f;
         if (e < E) s_ex[e] = p[j];
     }
     __syncwarp();
@@ -442,9 +470,9 @@ __global__ void __launch_bounds__(kThreads) router_large_kernel(RouterArgs a) {
 // ---------------------------------------------------------------------------
 // Wide router (E <= 64, D % 4 == 0, T > 8): one CTA holds every expert for a
 // tile of 16 tokens, so softmax/top-k need no other CTA.  Thread (e, g) keeps
-// the four chains of expert e for tokens g, g+4, g+8, g+12 as packed f32 pairs
-// (mul.rn.f32x2 / add.rn.f32x2: each half is one IEEE-rounded f32 operation,
-// the same arithmetic as the scalar chains).  Router-weight and activation
+// the four chains of expert e for tokens g, g+4, g+8, g+12 (scalar __fmul_rn /
+// __fadd_rn: packed f32x2 chains measured 1-4 ulp away from the reference's
+// logits on most tokens, so they are not used).  Router-weight and activation
 // chunks of 128 columns are double-buffered in shared memory with cp.async.
 // Each tile then ranks its routed slots per expert (stable) and publishes its
 // per-expert counts; the last tile turns the counts into expert offsets and
@@ -454,21 +482,6 @@ constexpr int kWideChunk = 128;
 constexpr int kWideExperts = 64;
 constexpr int kWideXStride = kWideChunk + 4;  // floats: 528-byte rows (16-byte aligned)
 
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
-}
-__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
 
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
@@ -619,9 +632,11 @@ __global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
         cp_async_commit();
     };
 
-    uint64_t acc01[4], acc23[4];
+    // the four chains of 4 tokens, separately rounded products and sums (__fmul_rn /
+    // __fadd_rn are never contracted into an FMA)
+    float c0[4], c1[4], c2[4], c3[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) acc01[j] = acc23[j] = 0ull;  // +0.0f pairs
+    for (int j = 0; j < 4; j++) c0[j] = c1[j] = c2[j] = c3[j] = 0.0f;
     issue(0, 0);
     for (int ch = 0; ch < nch; ch++) {
         if (ch + 1 < nch) {
@@ -649,12 +664,13 @@ __global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
                     const float4 q = *reinterpret_cast<const float4*>(wr + i);
                     w0 = q.x; w1 = q.y; w2 = q.z; w3 = q.w;
                 }
-                const uint64_t w01 = f2_pack(w0, w1), w23 = f2_pack(w2, w3);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const float4 x = *reinterpret_cast<const float4*>(xs + (g + 4 * j) * kWideXStride + i);
-                    acc01[j] = f2_add(acc01[j], f2_mul(w01, f2_pack(x.x, x.y)));
-                    acc23[j] = f2_add(acc23[j], f2_mul(w23, f2_pack(x.z, x.w)));
+                    c0[j] = __fadd_rn(c0[j], __fmul_rn(w0, x.x));
+                    c1[j] = __fadd_rn(c1[j], __fmul_rn(w1, x.y));
+                    c2[j] = __fadd_rn(c2[j], __fmul_rn(w2, x.z));
+                    c3[j] = __fadd_rn(c3[j], __fmul_rn(w3, x.w));
                 }
             }
         }
@@ -664,10 +680,10 @@ __global__ void __launch_bounds__(kThreads) router_wide_kernel(RouterArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int tl = g + 4 * j;
-            float logit = __fadd_rn(__fadd_rn(f2_lo(acc01[j]), f2_hi(acc01[j])),
-                                    __fadd_rn(f2_lo(acc23[j]), f2_hi(acc23[j])));
+            float logit = __fadd_rn(__fadd_rn(c0[j], c1[j]), __fadd_rn(c2[j], c3[j]));
             if (a.bias) logit = __fadd_rn(logit, a.bias[e]);
             s_logit[tl][e] = logit;
+            if (t0 + tl < a.T) a.logits[(size_t)(t0 + tl) * E + e] = logit;
         }
     }
     __syncthreads();
@@ -798,24 +814,22 @@ __global__ void __launch_bounds__(kThreads) router_tok_kernel(RouterArgs a) {
             n_issued++;
         }
     }
-    // the block form's rmsnorm of this token (rabbit2.c:512), with the summation order
-    // of rmsnorm_kernel, so xb has the same bits as there; written to xb for the
-    // kernels that follow
+    // the block form's rmsnorm of this token (rabbit2.c:512): the sum of squares
+    // is the reference's sequential f32 sum (block_seq_sum; the squares are staged
+    // in the xcm area, which then receives xb); xb is also written for the kernels
+    // that follow
     float inv = 1.0f;
     if (a.norm_w) {
-        const float* xr = a.x_raw + (size_t)t * D;
-        float ss = 0.0f;
-        for (int i = tid; i < D; i += kThreads) ss = fmaf(xr[i], xr[i], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) s_red[warp] = ss;
-        __syncthreads();
-        if (tid < 32) {
-            float v = tid < kThreads / 32 ? s_red[tid] : 0.0f;
-            v = warp_sum(v);
-            if (tid == 0) s_red[0] = v;
+        __shared__ SeqSumSmem s_seq;
+        const float4* xr4 = reinterpret_cast<const float4*>(a.x_raw + (size_t)t * D);
+        for (int i4 = tid; i4 < q4; i4 += kThreads) {
+            const float4 v = xr4[i4];
+            reinterpret_cast<float4*>(xcm)[i4] =
+                make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w));
         }
         __syncthreads();
-        inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(s_red[0], (float)D), a.eps));
+        const float ss = block_seq_sum<kThreads>(xcm, D, s_seq);
+        inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
     }
     // this token's xb, chain-major: xcm[c][j] = xb[t][c + 4 j] (rows 4 banks apart)
     for (int i4 = tid; i4 < q4; i4 += kThreads) {
@@ -896,8 +910,12 @@ __global__ void __launch_bounds__(kThreads) router_tok_kernel(RouterArgs a) {
     __syncthreads();
     mx = s_red[0];
     for (int w = 1; w < (E + 31) / 32; w++) mx = fmaxf(mx, s_red[w]);
-    // exp in double, rounded once (correctly rounded expf)
-    const float pe = tid < E ? (float)exp((double)__fsub_rn(lg, mx)) : 0.0f;
+    // the host libm's expf (rabbit2.c:403), by whole warps
+    float pe = 0.0f;
+    if (warp < (E + 31) / 32) {
+        const float v = expf_ref_warp(tid < E ? __fsub_rn(lg, mx) : 0.0f, a.expf_fma, expf_tab_lane());
+        if (tid < E) pe = v;
+    }
     if (tid < E) s_prob[tid] = pe;
     __syncthreads();
     if (tid == 0) {  // the sequential sum in expert order (rabbit2.c:403)
@@ -1154,7 +1172,9 @@ cudaError_t launch_route_given(const RouterArgs& a, cudaStream_t s, int* launche
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, int* launches) {
     *launches = 0;
     if (a.T <= 0) return cudaSuccess;
-    return a.dtype == 1 ? launch_typed<uint16_t>(a, s, launches) : launch_typed<float>(a, s, launches);
+    RouterArgs b = a;
+    b.expf_fma = host_expf_fma();
+    return b.dtype == 1 ? launch_typed<uint16_t>(b, s, launches) : launch_typed<float>(b, s, launches);
 }
 
 bool router_chain_major_supported(int E, int D, int dtype) {

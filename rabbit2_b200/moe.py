@@ -75,6 +75,9 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_model_load_layer": [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
         "rbt_model_forward": [vp, i32, i32, vp, vp],
         "rbt_model_prefill": [vp, vp, i32, i32, vp, i32, vp],
+        "rbt_moe_router_logits": [vp, vp, i32],
+        "rbt_expf_device": [C.c_uint32, C.c_int64, vp, vp],
+        "rbt_seq_sumsq_device": [vp, i32, i32, vp, vp],
     }
     for name, argtypes in sig.items():
         fn = getattr(lib, name)
@@ -84,6 +87,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.rbt_moe_destroy.restype = None
     lib.rbt_model_destroy.argtypes = [vp]
     lib.rbt_model_destroy.restype = None
+    lib.rbt_host_expf_variant.argtypes = []
+    lib.rbt_host_expf_variant.restype = C.c_int
     lib.rbt_moe_last_error.argtypes = []
     lib.rbt_moe_last_error.restype = C.c_char_p
     _lib = lib
@@ -213,10 +218,41 @@ class MoeContext:
         self._call(self.lib.rbt_moe_expert_histogram, self.handle, _ptr(counts))
         return counts
 
+    def router_logits(self, n_tokens):
+        """[n_tokens, E] router logits of the most recent routed call."""
+        out = np.empty((n_tokens, self.E), np.float32)
+        self._call(self.lib.rbt_moe_router_logits, self.handle, _ptr(out), n_tokens)
+        return out
+
+
+def _check(ok, lib):
+    if not ok:
+        raise RbtMoeError(lib.rbt_moe_last_error().decode() or "call failed")
+
+
+def expf_device(first_bits, out, stream=None):
+    """out[i] = the host libm's expf of the float with bits first_bits + i, on the GPU."""
+    lib = load_library()
+    _check(lib.rbt_expf_device(first_bits, out.numel(), _ptr(out), _ptr(stream) if stream is not None else None),
+           lib)
+
+
+def seq_sumsq_device(x, out, stream=None):
+    """out[r] = sequential f32 sum of x[r, :]**2 (rmsnorm's sum), on the GPU."""
+    lib = load_library()
+    rows, n = x.shape
+    _check(lib.rbt_seq_sumsq_device(_ptr(x), rows, n, _ptr(out), _ptr(stream) if stream is not None else None),
+           lib)
+
+
+def host_expf_variant():
+    """1 when this process's libm expf is the FMA-contracted build, 0 otherwise."""
+    return load_library().rbt_host_expf_variant()
+
 
 def declared_symbols(header: str = HEADER):
     """Function names declared in include/rbt_moe.h."""
     import re
     with open(header) as f:
         text = f.read()
-    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(rbt_(?:moe|ep|model)_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(rbt_\w+)\s*\(", text, flags=re.M)))

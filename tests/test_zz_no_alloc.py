@@ -89,3 +89,53 @@ def test_noalloc_decode_rejects_models_beyond_its_limits():
                      None, None)
         assert ok == 0, (D, H, E, K)
         assert b"unsupported model" in lib.rbt_moe_last_error()
+
+
+def _bind_status(lib):
+    fn = lib.rbt_moe_decode_noalloc_status
+    fn.argtypes = [C.c_void_p, C.POINTER(C.c_uint)]
+    fn.restype = C.c_int
+    return fn
+
+
+def test_noalloc_decode_in_place_and_status():
+    """Block form with d_out == d_x (CTAs read x back while others write out),
+    compared with the context path on a copy; then the status word: 0 after a
+    good call, a routing error after an input with a NaN (the kernel ranks no
+    experts and writes no output), and 0 again after the next good call."""
+    lib = moe.load_library()
+    noalloc, status = _bind(lib), _bind_status(lib)
+    D, H, E, K = 2048, 1024, 64, 8
+    router, experts, stride = workload.device_layer(D, H, E, seed=94)
+    g = torch.Generator(device="cuda").manual_seed(95)
+    ffn_norm = 1.0 + 0.1 * torch.randn(D, generator=g, device="cuda")
+    ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_BF16, 0, stride)
+    try:
+        ctx.bind_layer(0, router, experts, ffn_norm)
+        cfg = ctx.cfg
+        code = C.c_uint(0xffffffff)
+        for call in range(2):
+            x = workload.inputs(1, D, seed=96 + call) * 2.0
+            want = x.clone()
+            want_r = torch.empty(1, K, dtype=torch.int32, device="cuda")
+            ctx.block_device(0, want, want_r)
+            inplace = x.clone()
+            got_r = torch.full((1, K), -1, dtype=torch.int32, device="cuda")
+            assert noalloc(C.byref(cfg), ffn_norm.data_ptr(), router.data_ptr(), None, experts.data_ptr(),
+                           inplace.data_ptr(), inplace.data_ptr(), got_r.data_ptr(), None) == 1
+            assert status(None, C.byref(code)) == 1 and code.value == 0, hex(code.value)
+            np.testing.assert_array_equal(got_r.cpu().numpy(), want_r.cpu().numpy())
+            assert rel_err(inplace.cpu().numpy() - x.cpu().numpy(), want.cpu().numpy() - x.cpu().numpy()) < MOE_RTOL
+        bad = workload.inputs(1, D, seed=98)
+        bad[0, 17] = float("nan")
+        out = torch.zeros_like(bad)
+        assert noalloc(C.byref(cfg), None, router.data_ptr(), None, experts.data_ptr(), bad.data_ptr(),
+                       out.data_ptr(), None, None) == 1
+        assert status(None, C.byref(code)) == 1
+        assert code.value == 0x603, hex(code.value)
+        good = workload.inputs(1, D, seed=99)
+        assert noalloc(C.byref(cfg), None, router.data_ptr(), None, experts.data_ptr(), good.data_ptr(),
+                       out.data_ptr(), None, None) == 1
+        assert status(None, C.byref(code)) == 1 and code.value == 0, hex(code.value)
+    finally:
+        ctx.close()
