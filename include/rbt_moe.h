@@ -5,8 +5,9 @@
  * The reference engine (rabbit2/src/rabbit2.c) has no library boundary: the MoE
  * block is inline code in forward() (rabbit2.c:511-542) on top of the static
  * matvec() (:357-390) and get_expert() (:261-300).  These entry points are the
- * calls a maintainer puts in place of that block; INTEGRATION.md shows the
- * patch.  All pointers are plain C pointers; no CUDA or torch types appear.
+ * calls a maintainer puts in place of that block (rabbit2_b200/engine/
+ * rbt_engine_hook.h holds the engine-side calls, patch_engine.py beside it the
+ * edits).  All pointers are plain C pointers; no CUDA or torch types appear.
  *
  * Conventions, mirroring the reference's own functions:
  *   - every int-returning call returns 1 on success and 0 on error, like

@@ -1,14 +1,13 @@
-"""Build recipe: the reference engine with its MoE block on the GPU.
+"""Build recipe: the RABBIT2 engine with its MoE block (or its whole forward) on the GPU.
 
-    python oracle/patch_engine.py <rabbit2.c> <out.c>
+    python rabbit2_b200/engine/patch_engine.py <rabbit2.c> <out.c>
 
-Writes a copy of the reference engine source (rabbit2/src/rabbit2.c) into
-oracle/_ref/ with the edits INTEGRATION.md documents -- the include of
-rabbit2_b200/engine/rbt_engine_hook.h, its three CLI flags, its init call, the
-whole-forward and MoE-block calls and the batched prompt before the prompt
-loop -- and nothing else changed.  oracle/Makefile compiles it against librbt_moe.so into
-oracle/_ref/rabbit2_cuda.  Each edit is anchored on one reference line and
-fails loudly if that line is missing or not unique.
+Writes a copy of the engine source (rabbit2/src/rabbit2.c) with these edits and
+nothing else changed: the include of rbt_engine_hook.h, its CLI flags, its init
+call, the whole-forward and MoE-block calls in forward(), and the batched prompt
+before the prompt loop.  The Makefile beside this file compiles the copy against
+librbt_moe.so into _build/rabbit2_cuda.  Each edit is anchored on one engine
+line and fails loudly if that line is missing or not unique.
 """
 import sys
 

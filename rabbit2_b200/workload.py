@@ -11,13 +11,13 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from rabbit2_b200.rbt2fmt import DT_BF16, ModelConfig, expert_stride
+from rabbit2_b200.rbt2fmt import DT_BF16, ModelConfig, blob_stride
 
 OLMOE = dict(dim=2048, expert_hidden=1024, n_experts=64, top_k=8)
 
 
 def layer_stride(D: int, H: int, dtype: int = DT_BF16) -> int:
-    return expert_stride(ModelConfig(dim=D, expert_hidden=H, dtype=dtype))
+    return blob_stride(D, H, dtype)
 
 
 def device_layer(D, H, E, seed, device="cuda", std=0.02):
@@ -65,30 +65,25 @@ def write_model(path, cfg, seed=0, std=0.02):
 
     Draw order, from one numpy default_rng(seed): tok_emb; per layer wq, wk, wv, wo,
     router, then each expert's w1, w3, w2; lm_head."""
-    from rabbit2_b200.rbt2fmt import ModelWriter, round_to_dtype
+    from rabbit2_b200.rbt2fmt import ModelImage, encode
     rng = np.random.default_rng(seed)
-    q_dim, kv_dim = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
 
-    def mat(r, c):
-        return round_to_dtype(std * rng.standard_normal((r, c), dtype=np.float32), cfg.dtype)
+    def fill(view):  # matrices: seeded normals in the file's encoding
+        view[...] = encode(std * rng.standard_normal(view.shape, dtype=np.float32), cfg.dtype)
 
-    ones = lambda n: np.ones(n, np.float32)  # noqa: E731
-    with ModelWriter(path, cfg) as w:
-        L = w.offsets
-        w.matrix(L["tok_emb"], mat(cfg.vocab, cfg.dim))
-        for li, lo in enumerate(L["layers"]):
-            w.vector(lo["attn_norm"], ones(cfg.dim))
-            w.matrix(lo["wq"], mat(q_dim, cfg.dim))
-            w.matrix(lo["wk"], mat(kv_dim, cfg.dim))
-            w.matrix(lo["wv"], mat(kv_dim, cfg.dim))
-            w.matrix(lo["wo"], mat(cfg.dim, q_dim))
+    with ModelImage(path, cfg) as img:
+        fill(img.tensor("tok_emb"))
+        for l in range(cfg.n_layers):
+            img.tensor("attn_norm", l)[:] = 1.0
+            for name in ("wq", "wk", "wv", "wo"):
+                fill(img.tensor(name, l))
             if cfg.qk_norm:
-                w.vector(lo["q_norm"], ones(q_dim))
-                w.vector(lo["k_norm"], ones(kv_dim))
-            w.vector(lo["ffn_norm"], ones(cfg.dim))
-            w.matrix(lo["router"], mat(cfg.n_experts, cfg.dim))
+                img.tensor("q_norm", l)[:] = 1.0
+                img.tensor("k_norm", l)[:] = 1.0
+            img.tensor("ffn_norm", l)[:] = 1.0
+            fill(img.tensor("router", l))
             for e in range(cfg.n_experts):
-                w.expert(li, e, mat(cfg.expert_hidden, cfg.dim), mat(cfg.expert_hidden, cfg.dim),
-                         mat(cfg.dim, cfg.expert_hidden))
-        w.vector(L["final_norm"], ones(cfg.dim))
-        w.matrix(L["lm_head"], mat(cfg.vocab, cfg.dim))
+                for m in img.expert(l, e):
+                    fill(m)
+        img.tensor("final_norm")[:] = 1.0
+        fill(img.tensor("lm_head"))

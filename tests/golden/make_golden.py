@@ -1,6 +1,6 @@
 """Generate the MoE-layer golden fixtures from the reference's own NumPy model.
 
-    python tests/golden/make_golden.py [--ref /path/to/rabbit2/ref]
+    python tests/golden/make_golden.py --ref <checkout>/rabbit2/ref   (or $RABBIT2_REF/rabbit2/ref)
 
 Runs ``reference.forward`` (float64, ``rabbit2/ref/reference.py:100-147``) on the
 model shapes of the reference's engine tests (``tests/test_forward.py:80-98`` and
@@ -39,8 +39,11 @@ from rabbit2_b200.rbt2fmt import DT_BF16, DT_F32, ModelConfig  # noqa: E402
 from tests.golden.refweights import make_weights as regen_weights, moe_weight_digest  # noqa: E402
 
 
-def golden_shapes():
-    C = ModelConfig
+def golden_shapes(ref_config):
+    """The shapes, built on the reference's own Config (its defaults are the first
+    shape of tests/test_forward.py), as ModelConfig values."""
+    def C(**kw):
+        return ModelConfig(**dataclasses.asdict(ref_config(**kw)))
     shapes = {
         "f32_gqa_top2_renorm": C(),
         "bf16_gqa_renorm": C(dtype=DT_BF16),
@@ -94,7 +97,9 @@ def capture(reference, cfg, weights, tokens):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/rabbit2/ref")
+    env = os.environ.get("RABBIT2_REF")
+    ap.add_argument("--ref", default=os.path.join(env, "rabbit2", "ref") if env else None,
+                    required=env is None, help="the reference checkout's rabbit2/ref folder")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
@@ -102,7 +107,7 @@ def main():
     import reference  # noqa: E402
 
     index, arrays = [], {}
-    for name, cfg in golden_shapes().items():
+    for name, cfg in golden_shapes(ref_rbt2.Config).items():
         rcfg = ref_rbt2.Config(**dataclasses.asdict(cfg))
         for seed in range(3):
             weights = reference.make_weights(rcfg, seed)

@@ -1,6 +1,6 @@
-"""The drop-in, end to end: the reference engine built with rbt_engine_hook.h
-(oracle/_ref/rabbit2_cuda, made by oracle/Makefile from oracle/patch_engine.py)
-against the unmodified reference engine (oracle/_ref/rabbit2) on the same
+"""The drop-in, end to end: the engine built with rbt_engine_hook.h
+(rabbit2_b200/engine/_build/rabbit2_cuda, made by rabbit2_b200/engine/Makefile
+from patch_engine.py) against the unmodified reference engine (oracle/_ref/rabbit2) on the same
 model file, through the engine's own CLI -- the interface the Python tools use
 (tools/run.py, serve.py: subprocess calls of `rabbit2 --gen` / `--dump`).
 
@@ -20,9 +20,9 @@ from rabbit2_b200.rbt2fmt import DT_BF16
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.path.join(ROOT, "oracle", "_ref", "rabbit2")
-CUDA = os.path.join(ROOT, "oracle", "_ref", "rabbit2_cuda")
+CUDA = os.path.join(ROOT, "rabbit2_b200", "engine", "_build", "rabbit2_cuda")
 needs_bins = pytest.mark.skipif(not (os.path.exists(REF) and os.path.exists(CUDA)),
-                                reason="oracle/_ref engines not built (reference source absent when building)")
+                                reason="engines not built (the engine source was absent when building)")
 
 
 @pytest.fixture(scope="module")

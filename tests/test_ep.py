@@ -17,7 +17,7 @@ torch = pytest.importorskip("torch")
 
 from oracle.oracle import MoeLayerHost, Oracle  # noqa: E402
 from rabbit2_b200 import ep  # noqa: E402
-from rabbit2_b200.rbt2fmt import ModelConfig, expert_stride  # noqa: E402
+from rabbit2_b200.rbt2fmt import blob_stride  # noqa: E402
 
 D, H, E, K = 16, 8, 8, 2
 WORLD = 2
@@ -26,7 +26,7 @@ T_PER_RANK = [5, 3]
 
 def make_layer(seed):
     rng = np.random.default_rng(seed)
-    stride = expert_stride(ModelConfig(dim=D, expert_hidden=H, dtype=0))
+    stride = blob_stride(D, H, 0)
     router = rng.standard_normal((E, D)).astype(np.float32) * 0.5
     experts = np.zeros((E, stride), np.uint8)
     for e in range(E):

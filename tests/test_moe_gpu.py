@@ -327,8 +327,8 @@ def test_token_router_second_shape(orc, T):
 
 def test_tensor_core_path_rejects_f32_weights():
     D, H, E, K = 256, 512, 8, 2
-    from rabbit2_b200.rbt2fmt import ModelConfig, expert_stride
-    stride = expert_stride(ModelConfig(dim=D, expert_hidden=H, dtype=moe.DT_F32))
+    from rabbit2_b200.rbt2fmt import blob_stride
+    stride = blob_stride(D, H, moe.DT_F32)
     ctx = moe.MoeContext(D, E, K, H, 1, moe.DT_F32, 0, stride)
     try:
         ctx.load_layer(0, np.zeros((E, D), np.float32), np.zeros((E, stride), np.uint8))

@@ -67,10 +67,9 @@ def test_oracle_bit_exact_vs_reference_c(orc, key):
 
 def synthetic_layer(D, H, E, K, seed, dtype=1, norm_topk=0, bias=None):
     """Config-2-style random layer: bf16 weights ~N(0, 0.02), small enough for numpy."""
-    from rabbit2_b200.rbt2fmt import expert_stride, f32_to_bf16_bits
+    from rabbit2_b200.rbt2fmt import blob_stride, f32_to_bf16_bits
     rng = np.random.default_rng(seed)
-    stride = expert_stride(__import__("rabbit2_b200.rbt2fmt", fromlist=["ModelConfig"]).ModelConfig(
-        dim=D, expert_hidden=H, dtype=dtype))
+    stride = blob_stride(D, H, dtype)
     router = (0.02 * rng.standard_normal((E, D))).astype(np.float32)
     experts = np.zeros((E, stride), np.uint8)
     for e in range(E):

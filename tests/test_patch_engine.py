@@ -1,15 +1,15 @@
-"""The engine patch recipe (oracle/patch_engine.py) on a synthetic source: every
-edit lands at its anchor line, the replaced prompt-loop header is replaced, and a
-missing or repeated anchor stops the recipe instead of patching the wrong place.
-(The real engine source is patched and built by oracle/Makefile; test_engine.py
-runs the result.)"""
+"""The engine patch recipe (rabbit2_b200/engine/patch_engine.py) on a synthetic
+source: every edit lands at its anchor line, the replaced prompt-loop header is
+replaced, and a missing or repeated anchor stops the recipe instead of patching the
+wrong place.  (The real engine source is patched and built by
+rabbit2_b200/engine/Makefile; test_engine.py runs the result.)"""
 import importlib.util
 import os
 
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-spec = importlib.util.spec_from_file_location("patch_engine", os.path.join(ROOT, "oracle", "patch_engine.py"))
+spec = importlib.util.spec_from_file_location("patch_engine", os.path.join(ROOT, "rabbit2_b200", "engine", "patch_engine.py"))
 patch_engine = importlib.util.module_from_spec(spec)
 spec.loader.exec_module(patch_engine)
 
