@@ -67,6 +67,9 @@ def parse():
                          "model's prompt of --prompt tokens in one rbt_model_prefill call (config 4, one sequence)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=256)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="N=1 only: skip the other configs' keys of the line (moe_T4096, model_prefill, "
+                         "model_decode with its reference-engine baseline)")
     return ap.parse_args()
 
 
@@ -619,45 +622,62 @@ def run_ours(args, rank, world, local_rank):
 
 def olmoe_model(args, ctx_len):
     """A random-init OLMoE-1B-7B-shaped model (args.layers layers, vocab 50304, bf16
-    weights ~N(0, 0.02) from a seeded GPU generator, norms 1) uploaded into an
-    RbtModel with a KV cache of ctx_len positions."""
+    weights ~N(0, 0.02) from a seeded GPU generator, norms 1): assembled as the bytes
+    of its .rbt2 file in host memory (the engine's own view of the model, which the
+    reference engine can run), then uploaded from there into an RbtModel with a KV
+    cache of ctx_len positions.  Returns (cfg, model, image)."""
     import torch
 
     from rabbit2_b200 import model as model_mod
-    from rabbit2_b200.rbt2fmt import DT_BF16, ModelConfig, layout
+    from rabbit2_b200.rbt2fmt import BLOB_ALIGN, DT_BF16, HEADER_BYTES, ModelConfig, layout, pack_header
     cfg = ModelConfig(vocab=50304, dim=D, n_layers=args.layers, n_heads=16, n_kv_heads=16, head_dim=128,
                       n_experts=E, top_k=K, expert_hidden=H, max_seq=max(4096, ctx_len), dtype=DT_BF16, qk_norm=1,
                       norm_topk=0, rope_theta=10000.0, rms_eps=1e-5)
-    m = model_mod.ModelContext(cfg, ctx=ctx_len)
+    lay = layout(cfg)
+    image = torch.empty(-(-lay["total"] // BLOB_ALIGN) * BLOB_ALIGN, dtype=torch.uint8)
+    image[:HEADER_BYTES] = torch.frombuffer(bytearray(pack_header(cfg)), dtype=torch.uint8)
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
 
-    def mat(rows, cols):  # generated on the GPU, uploaded from host memory
-        return (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16).cpu()
+    def put_mat(off, rows, cols):  # drawn on the GPU, copied into the image
+        t = (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        image[off:off + rows * cols * 2].copy_(t.view(torch.uint8).reshape(-1))
 
+    def put_ones(off, n):
+        image[off:off + 4 * n].view(torch.float32).fill_(1.0)
+
+    put_mat(lay["tok_emb"], cfg.vocab, D)
+    for ly in lay["layers"]:
+        put_ones(ly["attn_norm"], D)
+        for name in ("wq", "wk", "wv"):
+            put_mat(ly[name], 16 * 128, D)
+        put_mat(ly["wo"], D, 16 * 128)
+        put_ones(ly["q_norm"], 16 * 128)
+        put_ones(ly["k_norm"], 16 * 128)
+        put_ones(ly["ffn_norm"], D)
+        put_mat(ly["router"], E, D)
+        assert lay["expert_stride"] == 3 * H * D * 2
+        put_mat(ly["experts"], E, 3 * H * D)
+    put_ones(lay["final_norm"], D)
+    put_mat(lay["lm_head"], cfg.vocab, D)
+    torch.cuda.synchronize()
+    m = model_mod.ModelContext(cfg, ctx=ctx_len)
+    base = image.data_ptr()
     lib, h = m.lib, m.handle
-    ones = np.ones(max(D, 16 * 128), np.float32)
-    emb, head = mat(cfg.vocab, D), mat(cfg.vocab, D)
-    m._call(lib.rbt_model_load_globals, h, emb.data_ptr(), ones.ctypes.data, head.data_ptr())
-    del emb, head
-    assert layout(cfg)["expert_stride"] == 3 * H * D * 2
-    for l in range(cfg.n_layers):
-        wq, wk, wv, wo, router = mat(2048, D), mat(2048, D), mat(2048, D), mat(D, 2048), mat(E, D)
-        experts = mat(E, 3 * H * D)
-        m._call(lib.rbt_model_load_layer, h, l, ones.ctypes.data, wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
-                wo.data_ptr(), ones.ctypes.data, ones.ctypes.data, ones.ctypes.data, router.data_ptr(),
-                experts.data_ptr())
-        del wq, wk, wv, wo, router, experts
-    return cfg, m
+    m._call(lib.rbt_model_load_globals, h, base + lay["tok_emb"], base + lay["final_norm"], base + lay["lm_head"])
+    for l, ly in enumerate(lay["layers"]):
+        m._call(lib.rbt_model_load_layer, h, l, *(base + ly[n] for n in (
+            "attn_norm", "wq", "wk", "wv", "wo", "q_norm", "k_norm", "ffn_norm", "router", "experts")))
+    return cfg, m, image
 
 
-def run_model_prefill(args):
+def run_model_prefill(args, built=None):
     """Config 4's unit of work on one GPU: one sequence of --prompt uniform-random
     tokens through the whole model in one rbt_model_prefill call (host tokens in,
     the last token's logits and every routing row out).  value = prompt tokens
     per second of wall clock around the call, averaged over --steps calls after
     --warmup (each call rewrites the same cache positions)."""
-    cfg, m = olmoe_model(args, args.prompt)
+    cfg, m, _ = built if built is not None else olmoe_model(args, args.prompt)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
     for _ in range(max(1, args.warmup)):
         m.prefill(prompt, 0, logit_rows=1)
@@ -667,7 +687,8 @@ def run_model_prefill(args):
             t0 = time.perf_counter()
             m.prefill(prompt, 0, logit_rows=1)
             times.append(time.perf_counter() - t0)
-    m.close()
+    if built is None:
+        m.close()
     dt = statistics.mean(times)
     T, L = args.prompt, cfg.n_layers
     nq = nkv = 16 * 128
@@ -690,14 +711,14 @@ def run_model_prefill(args):
                          "flops_parts": flops, "traffic": None}}
 
 
-def run_model_decode(args):
+def run_model_decode(args, built=None):
     """Config 3: the whole forward() (rbt_model_forward: attention, MoE, lm_head) of a
     random-init OLMoE-1B-7B-shaped model on one GPU -- a uniform-random prompt of
     --prompt tokens, then --gen greedy tokens with the KV cache, as the engine's
     --gen loop does (logits to the host, argmax there).  value = generated tokens
     per second of wall clock around the calls (host round trip per token
     included); prefill_tok_s is the prompt fed token by token."""
-    cfg, m = olmoe_model(args, args.prompt + args.gen)
+    cfg, m, _ = built if built is not None else olmoe_model(args, args.prompt + args.gen)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
     # warm-up: graph capture and first launches (positions are rewritten below)
     for p in range(min(3, args.prompt)):
@@ -715,7 +736,8 @@ def run_model_decode(args):
             logits, _ = m.forward(nxt, pos)
             pos += 1
         t3 = time.perf_counter()
-    m.close()
+    if built is None:
+        m.close()
     hbm, _, src = peaks()
     dt = (t3 - t2) / args.gen
     nq = nkv = 16 * 128
@@ -738,6 +760,81 @@ def run_model_decode(args):
                          "frac": total / dt / 1e9 / hbm, "peak_source": src, "bytes_per_token": total,
                          "bytes_per_token_parts": per_token, "traffic": None},
             "generated_ids_head": ids[:8]}
+
+
+# ----------------------------------------------------------------------------- the other configs, N = 1
+
+def reference_engine_decode(built, prompt_tokens=4, gen=4):
+    """The reference engine's own decode loop (rabbit2.c compiled as is, through
+    oracle/_ref: forward() per token, argmax between) on the same model bytes the GPU
+    model was uploaded from: `prompt_tokens` prompt tokens, then `gen` greedy tokens,
+    --kernel avx2 (its faster kernel), one thread (the engine is single-threaded).
+    The GPU model decodes the same prompt, and the greedy ids are compared."""
+    from oracle.oracle import Reference, available_reference
+    if not available_reference():
+        return {"unavailable": "oracle/_ref not built (the reference source was absent at build time)"}
+    cfg, m, image = built
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab, size=prompt_tokens)
+    ref = Reference()
+    t0 = time.perf_counter()
+    ids, t_prompt, t_gen = ref.decode_image(image.data_ptr(), image.numel(), prompt, gen, avx2=True)
+    wall = time.perf_counter() - t0
+    got = []
+    logits = None
+    for p, tok in enumerate(prompt):
+        logits, _ = m.forward(int(tok), p)
+    for i in range(gen):
+        nxt = int(np.argmax(logits))
+        got.append(nxt)
+        if i + 1 < gen:
+            logits, _ = m.forward(nxt, prompt_tokens + i)
+    return {"value": gen / t_gen, "unit": "tok/s", "kind": "reference", "cores": 1,
+            "prompt_tok_s": prompt_tokens / t_prompt, "host_cpu": cpu_model(),
+            "greedy_ids_equal": got == ids.tolist(), "greedy_ids": ids.tolist(),
+            "sample": f"the engine's decode loop (oracle/_ref, --kernel avx2, 1 thread) on the same "
+                      f"{cfg.n_layers}-layer model: {prompt_tokens} prompt tokens then {gen} greedy tokens, "
+                      f"{wall:.1f} s"}
+
+
+def run_extras(args):
+    """The other BASELINE configs as keys of the N = 1 line, each measured here with
+    its own clocks: the MoE stack at T = 4096 (the prefill-sized layer call whose
+    GEMMs carry the bf16 target), config 4's unit (one 4096-token prompt through the
+    whole model) and config 3 (batch-1 decode of 256 tokens after a 512-token
+    prompt, with the reference engine timed beside it)."""
+    import argparse as ap
+    import copy
+
+    import torch
+    out = {}
+    a = copy.copy(args)
+    a.tokens, a.steps, a.warmup, a.profile_steps = 4096, 5, 3, 2
+    line = run_ours(a, 0, 1, 0)
+    torch.cuda.empty_cache()
+    rf = line["roofline"]
+    _, flops = stage_cost(4096, rf["layer"]["distinct_experts_per_layer"], 4096 * K)
+    _, bf16, src = peaks()
+    gemm = {n: flops[n] / (rf["stage_ms_per_launch"][n] / 1e3) / 1e12 / bf16
+            for n in ("gate_up", "down") if n in rf["stage_ms_per_launch"]}
+    out["moe_T4096"] = {"metric": METRIC, "value": line["value"], "unit": UNIT, "ms_per_step": line["ms_per_step"],
+                        "steps": a.steps, "warmup": a.warmup, "config": line["config"], "clocks": line["clocks"],
+                        "e2e": line["e2e"], "gpu_launches": line["gpu_launches"], "roofline": rf,
+                        "gemm_frac_of_bf16": gemm, "layer_frac_of_bf16": rf["layer"]["tensor_frac"],
+                        "peak_source": src}
+    m_args = ap.Namespace(**vars(args))
+    m_args.layers = LAYERS
+    built = olmoe_model(m_args, 4096)
+    try:
+        p_args = copy.copy(m_args)
+        p_args.prompt, p_args.steps, p_args.warmup = 4096, 3, 1
+        out["model_prefill"] = run_model_prefill(p_args, built)
+        d_args = copy.copy(m_args)
+        d_args.prompt, d_args.gen = 512, 256
+        out["model_decode"] = run_model_decode(d_args, built)
+        out["model_decode"]["cpu_baseline"] = reference_engine_decode(built)
+    finally:
+        built[1].close()
+    return out
 
 
 def main():
@@ -769,6 +866,8 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             v, info, _ = cpu_reference_run(args, seconds=args.cpu_seconds, device="cuda")
             line["cpu_baseline"] = dict(info, value=v, unit=UNIT)
+        if world == 1 and not args.no_extras and args.tokens == 1:
+            line.update(run_extras(args))
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

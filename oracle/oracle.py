@@ -165,11 +165,22 @@ class Reference(_Lib):
         if not os.path.exists(REF_SO):
             raise FileNotFoundError(REF_SO + " (build it with make -C oracle where the reference exists)")
         self.lib = C.CDLL(REF_SO)
-        for name in ("ref_moe_ffn", "ref_moe_block", "ref_set_kernel"):
+        for name in ("ref_moe_ffn", "ref_moe_block", "ref_set_kernel", "ref_decode_image"):
             getattr(self.lib, name).restype = C.c_int
 
     def set_kernel(self, avx2: bool) -> bool:
         return bool(self.lib.ref_set_kernel(int(avx2)))
+
+    def decode_image(self, image_ptr: int, size: int, prompt, n_gen: int, avx2: bool = True):
+        """The engine's greedy decode loop on a .rbt2 image in memory: (ids [n_gen],
+        seconds for the prompt, seconds for the generated tokens)."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        ids = np.empty(n_gen, np.int32)
+        tp, tg = C.c_double(), C.c_double()
+        if not self.lib.ref_decode_image(C.c_void_p(image_ptr), C.c_size_t(size), int(avx2), _ptr(prompt),
+                                         len(prompt), n_gen, _ptr(ids), C.byref(tp), C.byref(tg)):
+            raise RuntimeError("ref_decode_image failed")
+        return ids, tp.value, tg.value
 
     def moe_ffn(self, layer, xb, nthreads=1):
         return self._run(self.lib.ref_moe_ffn, layer, xb, nthreads, False)

@@ -123,3 +123,54 @@ int ref_moe_block(const OrcMoeLayer *L, const float *x, int T, float *x_out, int
                   int nthreads) {
     return ref_run(L, x, T, x_out, routing, routing_stride, 1, nthreads);
 }
+
+/* The engine's greedy decode loop (rabbit2.c:703-738 at temperature 0: forward() for
+ * every prompt token, then argmax and forward() per generated token) on a model whose
+ * .rbt2 bytes are held in memory at `image` (size bytes), in place of the engine's
+ * mmap of the file (map_file, rabbit2.c:129-157).  The header checks of load_model
+ * (rabbit2.c:199-228) are restated; layout(), state_init(), forward() and argmax()
+ * are the reference's own.  Times the two phases with the engine's clock (now_sec)
+ * as its stderr line does (rabbit2.c:742-744).  ids_out [n_gen]. */
+int ref_decode_image(const unsigned char *image, size_t size, int avx2, const int32_t *prompt, int n_prompt,
+                     int n_gen, int32_t *ids_out, double *sec_prompt, double *sec_gen) {
+    Model m;
+    memset(&m, 0, sizeof m);
+    m.map.base = (unsigned char *)image;
+    m.map.size = size;
+    if (size < HEADER_BYTES || memcmp(image, "RBT2", 4) != 0) return 0;
+    uint32_t version;
+    memcpy(&version, image + 4, 4);
+    if (version != 2) return 0;
+    memcpy(&m.c, image + 8, sizeof(Config));
+    const Config *c = &m.c;
+    if (c->vocab <= 0 || c->dim <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
+        c->top_k <= 0 || c->top_k > c->n_experts || c->top_k > MAX_TOPK || n_prompt < 1 || n_gen < 1)
+        return 0;
+    m.esz = (c->dtype == DT_BF16) ? 2 : 4;
+    m.layers = (LayerOff *)calloc((size_t)c->n_layers, sizeof(LayerOff));
+    if (!m.layers) return 0;
+    layout(&m);
+    if (layout_end(&m) > size) { free(m.layers); return 0; }
+    use_avx2 = avx2 && cpu_has_avx2();
+    State s;
+    memset(&s, 0, sizeof s);
+    state_init(&s, c, n_prompt + n_gen);
+    int32_t *routing = (int32_t *)calloc((size_t)c->n_layers * c->top_k, sizeof(int32_t));
+    int ok = state_ok(&s) && routing;
+    double t0 = now_sec();
+    for (int i = 0; ok && i < n_prompt; i++) ok = forward(&m, &s, prompt[i], i, routing);
+    double t1 = now_sec();
+    for (int g = 0, pos = n_prompt; ok && g < n_gen; g++) {
+        const int next = argmax(s.logits, c->vocab);
+        ids_out[g] = next;
+        if (g + 1 < n_gen) ok = forward(&m, &s, next, pos++, routing);
+    }
+    double t2 = now_sec();
+    *sec_prompt = t1 - t0;
+    *sec_gen = t2 - t1;
+    free(routing);
+    free(s.x); free(s.xb); free(s.q); free(s.k); free(s.v); free(s.att); free(s.attn_out); free(s.router);
+    free(s.h1); free(s.h3); free(s.tmp); free(s.moe); free(s.logits); free(s.kcache); free(s.vcache); free(s.used);
+    free(m.layers);
+    return ok;
+}
