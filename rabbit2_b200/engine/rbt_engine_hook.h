@@ -3,11 +3,13 @@
  * blocks on the GPU through librbt_moe.so (include/rbt_moe.h).
  *
  * Included by rabbit2.c right before forward() (it uses the engine's Model,
- * State, LayerOff, VEC, MAT and its rmsnorm / matvec / rope / softmax, all
- * defined above forward()).  Call sites:
+ * State, LayerOff, VEC, MAT and its rmsnorm / matvec, all defined above
+ * forward(), and rbt_engine_attention_block: forward()'s own attention half,
+ * which patch_engine.py copies into a function of its own).  Call sites:
  *   main(), argument loop:  --device cpu|cuda   sets rbt_engine_device
  *                           --prefill batch|token   sets rbt_engine_prefill_mode
  *                           --offload moe|all       sets rbt_engine_offload
+ *                           --routing-trace FILE    sets rbt_engine_trace_path
  *   main(), after load_model():  rbt_engine_init(&m)
  *   forward(), first statement (rabbit2.c:455):
  *       { int g = rbt_engine_forward(m, s, token, pos, routing_out);
@@ -19,6 +21,15 @@
  *       const int pre = rbt_engine_prefill(&m, &s, tokens, nt, routing, fl, fr);
  *       (on -1: close the dump files, return 1), and the loop starts at
  *       i = pre ? nt : 0.
+ *   main(), after each forward() of the prompt loop and of the --gen loop:
+ *       rbt_engine_record(&m, routing)
+ *   main(), after the timing line (rabbit2.c:742-744): rbt_engine_report(&m)
+ * Every run (cpu or cuda) counts the experts each layer routed its tokens to and
+ * reports them at exit as stderr lines in the engine's key=value style
+ * (rabbit2.c:745-751):  expert histogram: layer=<l> tokens=<n> counts=<c0>,<c1>,...
+ * --routing-trace FILE writes every processed token's routing row, int32
+ * [n_layers][top_k] per token in processing order -- the layout of --dump's
+ * routing file (rabbit2.c:711-712), which tools/benchmark_cache.py replays.
  * With --device cpu (the default) nothing changes: the engine's own CPU block runs.
  * With --device cuda every layer's router and expert blobs are copied once from
  * the mapped file into HBM, and each MoE block is one rbt_moe_block() call that
@@ -34,8 +45,46 @@
 static const char *rbt_engine_device = NULL;
 static const char *rbt_engine_prefill_mode = NULL;  /* --prefill batch|token */
 static const char *rbt_engine_offload = NULL;       /* --offload moe|all */
+static const char *rbt_engine_trace_path = NULL;   /* --routing-trace FILE */
 static RbtMoe *rbt_engine_ctx = NULL;
 static RbtModel *rbt_engine_model = NULL;           /* --offload all: the whole forward() */
+static FILE *rbt_engine_trace = NULL;
+static long long *rbt_engine_hist = NULL;           /* [n_layers][n_experts] routed tokens */
+static long long rbt_engine_tokens = 0;
+
+/* One processed token's routing rows [n_layers][top_k]: the histogram, and the trace. */
+static void rbt_engine_record(const Model *m, const int32_t *routing) {
+    const Config *c = &m->c;
+    if (rbt_engine_hist) {
+        for (int l = 0; l < c->n_layers; l++)
+            for (int k = 0; k < c->top_k; k++) {
+                const int e = routing[(size_t)l * c->top_k + k];
+                if (e >= 0 && e < c->n_experts) rbt_engine_hist[(size_t)l * c->n_experts + e]++;
+            }
+        rbt_engine_tokens++;
+    }
+    if (rbt_engine_trace)
+        fwrite(routing, sizeof(int32_t), (size_t)c->n_layers * c->top_k, rbt_engine_trace);
+}
+
+/* At exit: the per-layer expert histogram on stderr; the trace file closed. */
+static void rbt_engine_report(const Model *m) {
+    const Config *c = &m->c;
+    if (rbt_engine_hist && rbt_engine_tokens > 0) {
+        for (int l = 0; l < c->n_layers; l++) {
+            fprintf(stderr, "expert histogram: layer=%d tokens=%lld counts=", l, rbt_engine_tokens);
+            for (int e = 0; e < c->n_experts; e++)
+                fprintf(stderr, "%s%lld", e ? "," : "", rbt_engine_hist[(size_t)l * c->n_experts + e]);
+            fprintf(stderr, "\n");
+        }
+    }
+    if (rbt_engine_trace) {
+        fclose(rbt_engine_trace);
+        rbt_engine_trace = NULL;
+    }
+    free(rbt_engine_hist);
+    rbt_engine_hist = NULL;
+}
 
 static int rbt_engine_init(Model *m) {
     if (rbt_engine_prefill_mode && strcmp(rbt_engine_prefill_mode, "batch") != 0 &&
@@ -45,6 +94,11 @@ static int rbt_engine_init(Model *m) {
     }
     if (rbt_engine_offload && strcmp(rbt_engine_offload, "moe") != 0 && strcmp(rbt_engine_offload, "all") != 0) {
         fprintf(stderr, "--offload must be moe or all\n");
+        return 0;
+    }
+    rbt_engine_hist = (long long *)calloc((size_t)m->c.n_layers * m->c.n_experts, sizeof(long long));
+    if (rbt_engine_trace_path && !(rbt_engine_trace = fopen(rbt_engine_trace_path, "wb"))) {
+        fprintf(stderr, "cannot open the routing trace %s\n", rbt_engine_trace_path);
         return 0;
     }
     if (!rbt_engine_device || !strcmp(rbt_engine_device, "cpu")) return 1;
@@ -135,48 +189,13 @@ static int rbt_engine_moe(Model *m, int layer, float *x, int32_t *routing_row) {
  * loop. */
 
 /* Layer l's attention half for the token at position pos; x [dim] is updated in
- * place.  These are the engine's own calls on the same values in the same order
- * as forward() makes them for one token (rabbit2.c:472-509), so the results are
- * the same bits. */
+ * place.  This is forward()'s own code for it (rbt_engine_attention_block, on
+ * s->x), so the results are the same bits as the engine's per-token loop. */
 static void rbt_engine_attention(Model *m, State *s, int l, float *x, int pos) {
-    const Config *c = &m->c;
-    const LayerOff *ly = &m->layers[l];
-    const int D = c->dim, hd = c->head_dim;
-    const int nq = c->n_heads * hd, nkv = c->n_kv_heads * hd, heads_per_kv = c->n_heads / c->n_kv_heads;
-    rmsnorm(s->xb, x, VEC(m, ly->attn_norm), D, c->rms_eps);
-    matvec(s->q, MAT(m, ly->wq), c->dtype, s->xb, nq, D);
-    matvec(s->k, MAT(m, ly->wk), c->dtype, s->xb, nkv, D);
-    matvec(s->v, MAT(m, ly->wv), c->dtype, s->xb, nkv, D);
-    if (c->qk_norm) {
-        rmsnorm(s->q, s->q, VEC(m, ly->q_norm), nq, c->rms_eps);
-        rmsnorm(s->k, s->k, VEC(m, ly->k_norm), nkv, c->rms_eps);
-    }
-    rope(s->q, c->n_heads, hd, pos, c->rope_theta);
-    rope(s->k, c->n_kv_heads, hd, pos, c->rope_theta);
-    float *keys = s->kcache + (size_t)l * s->ctx * nkv, *vals = s->vcache + (size_t)l * s->ctx * nkv;
-    memcpy(keys + (size_t)pos * nkv, s->k, (size_t)nkv * sizeof(float));
-    memcpy(vals + (size_t)pos * nkv, s->v, (size_t)nkv * sizeof(float));
-    const float scale = 1.0f / sqrtf((float)hd);
-    for (int h = 0; h < c->n_heads; h++) {
-        const float *q = s->q + (size_t)h * hd;
-        const size_t kv_col = (size_t)(h / heads_per_kv) * hd;
-        for (int t = 0; t <= pos; t++) {
-            const float *kt = keys + (size_t)t * nkv + kv_col;
-            float d = 0.0f;
-            for (int i = 0; i < hd; i++) d += q[i] * kt[i];
-            s->att[t] = d * scale;
-        }
-        softmax(s->att, pos + 1);
-        float *o = s->attn_out + (size_t)h * hd;
-        for (int i = 0; i < hd; i++) o[i] = 0.0f;
-        for (int t = 0; t <= pos; t++) {
-            const float *vt = vals + (size_t)t * nkv + kv_col;
-            const float w = s->att[t];
-            for (int i = 0; i < hd; i++) o[i] += w * vt[i];
-        }
-    }
-    matvec(s->xb, MAT(m, ly->wo), c->dtype, s->attn_out, D, nq);
-    for (int i = 0; i < D; i++) x[i] += s->xb[i];
+    const size_t bytes = (size_t)m->c.dim * sizeof(float);
+    memcpy(s->x, x, bytes);
+    rbt_engine_attention_block(m, s, l, pos);
+    memcpy(x, s->x, bytes);
 }
 
 /* --offload all: the whole prompt in one rbt_model_prefill call (every layer on
@@ -203,6 +222,7 @@ static int rbt_engine_prefill_model(Model *m, State *s, const int *tokens, int n
     if (ok) {
         memcpy(s->logits, lg + (size_t)(rows - 1) * c->vocab, (size_t)c->vocab * sizeof(float));
         memcpy(routing, R + (size_t)(nt - 1) * row, row * sizeof(int32_t));
+        for (int t = 0; t < nt; t++) rbt_engine_record(m, R + (size_t)t * row);
     }
     free(lg);
     free(R);
@@ -255,7 +275,10 @@ static int rbt_engine_prefill(Model *m, State *s, const int *tokens, int nt, int
             ok = 0;
         }
     }
-    if (ok) memcpy(routing, R + (size_t)(nt - 1) * row, row * sizeof(int32_t));
+    if (ok) {
+        memcpy(routing, R + (size_t)(nt - 1) * row, row * sizeof(int32_t));
+        for (int t = 0; t < nt; t++) rbt_engine_record(m, R + (size_t)t * row);
+    }
     free(X);
     free(R);
     return ok ? 1 : -1;

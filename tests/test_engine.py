@@ -168,3 +168,59 @@ def test_gpu_whole_forward_engine_matches_reference(tiny_model, tiny_model_bf16,
     np.testing.assert_array_equal(gr, wr)
     err = np.abs(gl.astype(np.float64) - wl).max() / np.abs(wl).max()
     assert err < 1e-3, err
+
+
+def histogram_lines(stderr, n_layers, n_experts):
+    """The engine's 'expert histogram: layer=<l> tokens=<n> counts=...' lines -> [L, E], tokens."""
+    import re
+    rows, tokens = {}, set()
+    for m in re.finditer(r"expert histogram: layer=(\d+) tokens=(\d+) counts=([\d,]+)", stderr):
+        rows[int(m.group(1))] = [int(v) for v in m.group(3).split(",")]
+        tokens.add(int(m.group(2)))
+    assert sorted(rows) == list(range(n_layers)) and len(tokens) == 1
+    hist = np.array([rows[l] for l in range(n_layers)])
+    assert hist.shape == (n_layers, n_experts)
+    return hist, tokens.pop()
+
+
+def check_trace(trace_file, routing_dump, stderr, cfg, n_tokens):
+    trace = np.fromfile(trace_file, "<i4").reshape(-1, cfg.n_layers, cfg.top_k)
+    assert trace.shape[0] == n_tokens
+    if routing_dump is not None:
+        np.testing.assert_array_equal(trace[:routing_dump.shape[0]], routing_dump)
+    hist, tokens = histogram_lines(stderr, cfg.n_layers, cfg.n_experts)
+    assert tokens == n_tokens
+    for l in range(cfg.n_layers):
+        np.testing.assert_array_equal(hist[l], np.bincount(trace[:, l, :].ravel(), minlength=cfg.n_experts))
+    return trace
+
+
+@needs_bins
+def test_routing_trace_and_histogram_cpu(tiny_model, tmp_path):
+    """--routing-trace writes every processed token's routing rows in --dump's layout,
+    and the per-layer expert histogram on stderr counts them; with --gen n the trace
+    holds the prompt and the n - 1 generated tokens that went through forward()."""
+    model, cfg, prompt = tiny_model
+    tr = str(tmp_path / "trace.bin")
+    _, wr, _ = dump(REF, model, prompt[:24], str(tmp_path))
+    _, rr, err = dump(CUDA, model, prompt[:24], str(tmp_path), ["--routing-trace", tr])
+    np.testing.assert_array_equal(rr, wr)
+    check_trace(tr, wr.reshape(-1, cfg.n_layers, cfg.top_k), err, cfg, 24)
+    ids, err = gen(CUDA, model, prompt[:24], 6, ["--routing-trace", tr])
+    want_ids, _ = gen(REF, model, prompt[:24], 6)
+    assert ids == want_ids
+    check_trace(tr, wr.reshape(-1, cfg.n_layers, cfg.top_k), err, cfg, 24 + 5)
+
+
+@needs_bins
+@pytest.mark.gpu
+@pytest.mark.parametrize("extra", [["--device", "cuda"], ["--device", "cuda", "--offload", "all"]])
+def test_routing_trace_and_histogram_gpu(tiny_model_bf16, tmp_path, extra):
+    """The same through the GPU paths (the batched prompt, then one-token calls):
+    the trace equals the unmodified engine's routing for the prompt."""
+    model, cfg, prompt = tiny_model_bf16
+    tr = str(tmp_path / "trace.bin")
+    _, wr, _ = dump(REF, model, prompt, str(tmp_path))
+    ids, err = gen(CUDA, model, prompt, 8, extra + ["--routing-trace", tr])
+    trace = check_trace(tr, wr.reshape(-1, cfg.n_layers, cfg.top_k), err, cfg, len(prompt) + 7)
+    assert trace.shape[0] == len(prompt) + 7

@@ -16,10 +16,15 @@ spec.loader.exec_module(patch_engine)
 
 def synthetic_source():
     anchors = [a for a, _, _ in patch_engine.INSERTIONS]
-    # every anchor once, in the order of the insertions, with filler lines between
+    # every anchor once, in the order of the insertions, with filler lines between;
+    # forward()'s prologue and attention half around their anchors
     lines = []
     for i, a in enumerate(dict.fromkeys(anchors)):
+        if a == patch_engine.HOIST_END:
+            lines += [patch_engine.HOIST_BEGIN, "        attention_body();"]
         lines += [f"/* filler {i} */", a]
+        if a == patch_engine.FORWARD:
+            lines += ["    const int prologue_local = 1;", patch_engine.HOIST_PROLOGUE_END]
     return "\n".join(lines) + "\n", anchors
 
 
@@ -37,6 +42,10 @@ def test_every_edit_lands_at_its_anchor():
     assert '#include "rbt_engine_hook.h"' in out
     assert "rbt_engine_prefill(&m, &s, tokens, nt, routing, fl, fr)" in out
     assert "for (int i = rbt_pre_ ? nt : 0; i < nt; i++) {" in out
+    # the hoisted attention half: forward()'s prologue and attention lines, before the hook's include
+    hoisted = out[out.index("static void rbt_engine_attention_block("):out.index('#include "rbt_engine_hook.h"')]
+    assert "    const int prologue_local = 1;" in hoisted and "        attention_body();" in hoisted
+    assert "/* ---- MoE feed-forward ---- */" not in hoisted
 
 
 def test_missing_or_repeated_anchor_stops_the_recipe():
