@@ -22,11 +22,13 @@ decode; --tokens 4096 is the prefill-sized layer call.
 OLMoE-1B-7B-shaped model on one GPU instead (rbt_model_forward per generated
 token, config 3; rbt_model_prefill for one prompt, config 4's unit of work).
 Multi-GPU (torchrun, N ranks): expert parallelism.  Rank g holds experts
-[g*64/N, (g+1)*64/N) of every layer and its own T tokens; each layer routes
-locally, sends every token once to each GPU that owns one of its experts (NCCL
-all-to-all), runs its experts, and adds the returned partial rows in rank order
-(rabbit2_b200/ep.py).  value = N*T tokens / max-over-ranks step time (weak
-scaling: T tokens per GPU).
+[g*64/N, (g+1)*64/N) of every layer and its own T tokens; each layer is one
+rbt_moe_ep_block_device call per GPU: local routing, each token's row stored once
+into every GPU that owns one of its experts (peer memory over NVLink), the
+experts, the partial rows stored back, and the combine in rank order -- no host
+synchronisation, the 16 layers one CUDA graph.  value = N*T tokens / max-over-ranks
+step time (weak scaling: T tokens per GPU); the line carries a parity check of
+rank 0's tokens against the CPU oracle and the per-stage time of a layer.
 """
 from __future__ import annotations
 
@@ -297,9 +299,14 @@ def stage_cost(T, U, S):
 
 
 def run_ep(args, rank, world, local_rank):
-    """Expert-parallel step over `world` GPUs (one process each)."""
+    """Expert-parallel step over `world` GPUs, one process each (rbt_moe_ep_*): rank g
+    holds experts [g*64/N, (g+1)*64/N) of every layer and its own T tokens; each layer
+    is one library call per GPU (route, peer-memory dispatch over NVLink, experts,
+    return, combine; no host synchronisation), the 16 layers one CUDA graph."""
     import torch
     import torch.distributed as dist
+
+    from oracle.oracle import MoeLayerHost, Oracle
     from rabbit2_b200 import ep, moe, workload
 
     dev = torch.device("cuda", local_rank)
@@ -309,92 +316,125 @@ def run_ep(args, rank, world, local_rank):
     stride = workload.layer_stride(D, H)
     ctx = moe.MoeContext(D, E, K, H, L, moe.DT_BF16, 0, stride, device=local_rank)
     ctx.set_path(args.path)
-    ctx.set_expert_range(e0, epr)
+    ctx.ep_init(rank, world, T)
     ones = torch.ones(D, device=dev)
     keep = []
     bias = workload.zipf_bias(E, 1.2, seed=0) if args.routing == "zipf" else None
+    full0 = None
     for l in range(L):
         router, experts, _ = workload.device_layer(D, H, E, seed=1 + l, device=dev)
         local = experts[e0:e0 + epr].clone()
+        if l == 0 and rank == 0:
+            full0 = workload.host_copy(router, experts)
         del experts
         ctx.bind_layer(l, router, local, ones)
         keep.append((router, local))
         if bias is not None:
             ctx.set_router_bias(l, bias)
-    ctx.reserve(max(T * world, 1))  # a GPU receives at most every token of every rank
-    # decode-sized calls: fixed dispatch segments (no host read of the counts), so the
-    # whole step is captured in one CUDA graph, NCCL all-to-alls included
-    small = T <= 256
-    m = ep.ExpertParallelMoe(ep.GpuOps(ctx, world), capacity=T if small else None)
+    ctx.reserve(world * T)
+    ep.connect(ctx)
     x0 = workload.inputs(T, D, seed=1000 + rank, device=dev)
     x = torch.empty_like(x0)
+    st = torch.cuda.Stream(device=dev)
 
     def step():
         x.copy_(x0)
         for l in range(L):
-            m.block(l, x)
+            ctx.ep_block_device(l, x, stream=st)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    # routed-expert statistics of one step: every rank's local counts, gathered
+    # parity before timing: rank 0's first tokens through layer 0 against the CPU oracle
+    parity = None
+    n_chk = min(8, T)
+    xc = x0[:n_chk].clone()
+    rc = torch.empty(n_chk, K, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(st):
+        ctx.ep_block_device(0, xc if rank == 0 else x0[:0], rc if rank == 0 else None, T=n_chk if rank == 0 else 0,
+                            stream=st)
+    torch.cuda.synchronize()
+    status = ctx.status()
+    if rank == 0:
+        r_h, e_h = full0
+        host = MoeLayerHost(D, H, E, K, moe.DT_BF16, 0, r_h, e_h, stride, ffn_norm=np.ones(D, np.float32),
+                            router_bias=bias)
+        want, want_r = Oracle().moe_block(host, x0[:n_chk].cpu().numpy(), nthreads=8)
+        got = xc.cpu().numpy()
+        xin = x0[:n_chk].cpu().numpy()
+        parity = {"checked": True, "tokens": n_chk, "layer": 0,
+                  "routing_equal": bool(np.array_equal(rc.cpu().numpy(), want_r)),
+                  "max_rel_err": float(np.abs((got - xin) - (want - xin)).max() / np.abs(want - xin).max()),
+                  "status": status, "against": "oracle/ MoE block (CPU), all 64 experts"}
+    del full0
+
+    with torch.cuda.stream(st):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize()
+    # routed slots per expert of one step: each rank's local counts, gathered
     hist = torch.zeros(E, dtype=torch.int64, device=dev)
     U_sum = 0
-    x.copy_(x0)
-    for l in range(L):
-        m.block(l, x)
-        loc = torch.zeros(E, dtype=torch.int64, device=dev)
-        loc[e0:e0 + epr] = torch.from_numpy(ctx.expert_histogram()[:epr].astype(np.int64)).to(dev)
-        dist.all_reduce(loc)
-        hist += loc
-        U_sum += int((loc > 0).sum())
+    with torch.cuda.stream(st):
+        x.copy_(x0)
+        for l in range(L):
+            ctx.ep_block_device(l, x, stream=st)
+            torch.cuda.synchronize()
+            loc = torch.zeros(E, dtype=torch.int64, device=dev)
+            loc[e0:e0 + epr] = torch.from_numpy(ctx.expert_histogram()[:epr].astype(np.int64)).to(dev)
+            dist.all_reduce(loc)
+            hist += loc
+            U_sum += int((loc > 0).sum())
     U = U_sum / L
     ctx.profile(timing=0, reset=True)
-    step()
-    torch.cuda.synchronize()
-    launches_per_step = ctx.profile(reset=True)["launches"] + 3 * L  # + plan, pack, combine per layer
-    g = None
-    if small:
-        s = torch.cuda.Stream(device=dev)
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            step()
-        torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
-        dist.barrier()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            step()
-        torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        step()
+    launches_per_step = ctx.profile(reset=True)["launches"]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
         for _ in range(3):
             g.replay()
-    run_step = g.replay if g is not None else step
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clocks:
-        ev0.record()
-        for _ in range(args.steps):
-            run_step()
-        ev1.record()
         torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local_rank) as clocks:
+            ev0.record(st)
+            for _ in range(args.steps):
+                g.replay()
+            ev1.record(st)
+            torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / args.steps
-    dist.barrier()
-    t = torch.tensor([ms], device=dev)
+    bad = ctx.status()
+    t = torch.tensor([ms, float(bad != 0)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms, any_bad = float(t[0].item()), bool(t[1].item())
     value = world * T / (ms / 1e3)
+
+    # per-stage device time: a second graph with event nodes at every stage boundary
+    ctx.profile(timing=1, reset=True)
+    gp = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gp, stream=st):
+        step()
+    stage_ms = {}
+    with torch.cuda.stream(st):
+        for _ in range(args.profile_steps):
+            gp.replay()
+            torch.cuda.synchronize()
+            for n, v in ctx.profile()["stage_ms"].items():
+                stage_ms[n] = stage_ms.get(n, 0.0) + v
+    ctx.profile(timing=0, reset=True)
+    del gp
+    stage_us_per_layer = {n: v / args.profile_steps / L * 1e3 for n, v in stage_ms.items() if v > 0}
 
     # e2e: this rank's tokens from pinned host memory in, the block output back, every step
     xh = x0.cpu().pin_memory()
     oh = torch.empty_like(xh).pin_memory()
 
     def host_step():
-        xg = xh.to(dev, non_blocking=True)
-        for l in range(L):
-            m.block(l, xg)
-        oh.copy_(xg, non_blocking=True)
-        torch.cuda.synchronize()
+        with torch.cuda.stream(st):
+            x.copy_(xh, non_blocking=True)
+            for l in range(L):
+                ctx.ep_block_device(l, x, stream=st)
+            oh.copy_(x, non_blocking=True)
+        st.synchronize()
 
     for _ in range(max(args.warmup, 3)):
         host_step()
@@ -408,12 +448,11 @@ def run_ep(args, rank, world, local_rank):
     e2e_ms = float(t.item())
     e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
            "d2h_bytes_per_step": T * D * 4,
-           "how": "ExpertParallelMoe.block per layer on this rank's tokens copied in from pinned host memory, "
+           "how": "rbt_moe_ep_block_device per layer on this rank's tokens copied in from pinned host memory, "
                   "output copied back, wall clock, max over ranks (per-rank bytes)"}
 
     hbm, bf16, src = peaks()
     layer_ms = ms / L
-    # whole-job algorithmic bytes and flops of one layer, then per GPU
     layer_bytes = world * E * D * 2 + U * 3 * H * D * 2 + world * T * D * 4 * 2 + world * T * K * 8
     layer_flops = world * T * (2 * E * D + 6 * K * H * D)
     gbs = layer_bytes / world / (layer_ms / 1e3) / 1e9
@@ -423,24 +462,21 @@ def run_ep(args, rank, world, local_rank):
                 "achieved": tfs if tensor_bound else gbs, "peak": bf16 if tensor_bound else hbm,
                 "unit": "TFLOP/s" if tensor_bound else "GB/s",
                 "frac": (tfs / bf16) if tensor_bound else (gbs / hbm), "peak_source": src, "traffic": None,
-                "timing": ("CUDA events around the timed steps (route, plan, pack, NCCL all-to-all, experts, "
-                           "NCCL all-to-all, combine per layer" + ("; the step replayed as one CUDA graph"
-                                                                   if g is not None else "") +
-                           "), max over ranks; per GPU: the job's algorithmic bytes or flops of a layer / N / "
-                           "layer time"),
+                "timing": "CUDA events around the timed graph replays (the 16 layers' library calls), max over "
+                          "ranks; per GPU: the job's algorithmic bytes or flops of a layer / N / layer time",
                 "layer": {"us_per_layer": layer_ms * 1e3, "algorithmic_bytes_job": layer_bytes,
                           "algorithmic_flops_job": layer_flops, "distinct_experts_per_layer": U,
-                          "experts_per_gpu": epr}}
+                          "experts_per_gpu": epr,
+                          "stage_us_per_layer": stage_us_per_layer}}
     out = None
     if rank == 0:
         out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_desc(args),
                "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-               "roofline": roofline, "expert_histogram": hist.cpu().tolist(),
-               "dispatch_rows_last_layer": {"sent": m.last_counts[0], "received": m.last_counts[1]}}
-    if g is not None:
-        del g  # a graph holding NCCL calls goes before the process group
+               "roofline": roofline, "expert_histogram": hist.cpu().tolist(), "parity": parity,
+               "ep_status_error": any_bad}
+    del g
     torch.cuda.synchronize()
     ctx.close()
     return out

@@ -94,55 +94,70 @@ int rbt_moe_ffn_device(RbtMoe *m, int layer, const float *d_xb, int n_tokens, fl
                        int32_t *d_routing_out, int routing_stride, void *stream);
 
 /* ---- Expert parallelism across the GPUs of one node (no counterpart in the
- * reference, which runs one process on CPU; the per-GPU arithmetic is that of
- * rabbit2.c:512-542).  GPU g owns experts [g*E/N, (g+1)*E/N); each GPU routes its
- * own tokens with the whole router, sends every token once to each GPU that owns
- * one of its top-k experts, and adds the partial outputs that come back in
- * ascending GPU order.  The exchanges are NCCL all-to-alls issued by the caller
- * (rabbit2_b200/ep.py); these calls prepare and consume their buffers. */
+ * reference, which runs one CPU process; the per-GPU arithmetic is that of
+ * rabbit2.c:512-542).  GPU g of N owns experts [g*E/N, (g+1)*E/N) and the whole
+ * router.  Each GPU routes its own tokens (bit-exact, as rbt_moe_block), stores
+ * every token's row once into each GPU that owns one of its top-k experts (plain
+ * stores to peer memory over NVLink: a token whose experts are all local never
+ * leaves its GPU), runs its experts on the rows it received, stores each row's
+ * partial output back into the sender's memory, and adds the partials that come
+ * back in ascending GPU order.  Completion is signalled with flags holding a
+ * per-call epoch, so the layer needs no host synchronisation and can be captured
+ * in a CUDA graph.  Every GPU of the group must make the same sequence of calls
+ * (SPMD); each passes its own n_tokens <= max_tokens.
+ * Failure detection: every wait for another GPU is bounded (rbt_moe_ep_set_timeout,
+ * default 2 s); one that runs out leaves the layer's output invalid and a status
+ * code (0x701 rows never arrived, 0x702 partial rows never came back, 0x703 a peer
+ * reported a failure of its own) that rbt_moe_status returns.  After a failure the
+ * group's epochs disagree: destroy every context of the group (the counterpart of
+ * aborting a communicator). */
 
-/* Narrow the context to experts [first_expert, first_expert + n_experts_local):
- * rbt_moe_load_layer / bind_layer then take those n_experts_local blobs, and the
- * block/ffn calls are replaced by rbt_moe_route_device + rbt_moe_experts_device.
- * Call before any layer is loaded or bound. */
-int rbt_moe_set_expert_range(RbtMoe *m, int first_expert, int n_experts_local);
+/* Make this context rank `rank` of an expert-parallel group of n_ranks GPUs
+ * (n_ranks <= 8, dividing n_experts), for calls of up to max_tokens tokens per GPU.
+ * Narrows the context to its expert slice as rbt_moe_set_expert_range does, and
+ * allocates its receive/return block (2 * n_ranks * max_tokens rows of dim floats
+ * plus ids, weights and flags).  Call before any layer is loaded or bound. */
+int rbt_moe_ep_init(RbtMoe *m, int rank, int n_ranks, int max_tokens);
 
-/* Router of the layer for n_tokens rows: block != 0 gives d_xb = rmsnorm(d_x)
- * (rabbit2.c:512), block == 0 copies d_x into d_xb; then d_idx [n_tokens,
- * top_k] receives the global expert ids in selection order and d_wt the combine
- * weights (rabbit2.c:513-531), bit-exact as in rbt_moe_block. */
+/* One GPU per process: the 64-byte IPC handle of this context's block
+ * (cudaIpcMemHandle_t), to be gathered by the caller from every rank in rank order
+ * (n_ranks * 64 bytes) and passed to rbt_moe_ep_connect on every rank. */
+int rbt_moe_ep_handle(RbtMoe *m, void *handle_out);
+int rbt_moe_ep_connect(RbtMoe *m, const void *handles);
+
+/* Every GPU in this process (ms[g] is rank g; one host thread drives them all):
+ * enables peer access between their devices and connects them directly. */
+int rbt_moe_ep_connect_local(RbtMoe *const *ms, int n);
+
+/* Wait limit for the flags of other GPUs, in ns (>= 1000). */
+int rbt_moe_ep_set_timeout(RbtMoe *m, uint64_t timeout_ns);
+
+/* The expert-parallel MoE block of forward(), rabbit2.c:512-542, on this GPU's
+ * n_tokens rows: d_x += MoE(rmsnorm(d_x)) in place; d_routing_out (may be NULL)
+ * receives the global expert ids.  Device pointers, enqueued on `stream` without
+ * synchronising; allocates nothing once rbt_moe_reserve covered n_ranks *
+ * max_tokens rows. */
+int rbt_moe_ep_block_device(RbtMoe *m, int layer, float *d_x, int n_tokens, int32_t *d_routing_out,
+                            int routing_stride, void *stream);
+
+/* The same for a group connected by rbt_moe_ep_connect_local, with host buffers:
+ * GPU 0 (ms[0]) takes the n_tokens rows of x (in place) and returns the routing
+ * rows as rbt_moe_block does; every GPU runs its experts.  Returns after the
+ * results are in host memory; 0 with a message if any GPU failed. */
+int rbt_moe_ep_block(RbtMoe *const *ms, int n, int layer, float *x, int n_tokens, int32_t *routing_out,
+                     int routing_stride);
+
+/* The status word of the context's kernels (0: none failed), cleared after reading;
+ * synchronises the device.  Device-pointer calls report their kernels' failures
+ * (a bounded wait that ran out) only here. */
+int rbt_moe_status(RbtMoe *m, unsigned *status_out);
+
+/* The router of the layer alone, for n_tokens rows: block != 0 gives d_xb =
+ * rmsnorm(d_x) (rabbit2.c:512), block == 0 copies d_x into d_xb; then d_idx
+ * [n_tokens, top_k] receives the expert ids in selection order and d_wt the combine
+ * weights (rabbit2.c:513-531), bit-exact as in rbt_moe_block.  Device pointers. */
 int rbt_moe_route_device(RbtMoe *m, int layer, const float *d_x, int n_tokens, int block, float *d_xb,
                          int32_t *d_idx, float *d_wt, void *stream);
-
-/* The experts of this context on routing computed elsewhere: d_idx [n_rows,
- * top_k] holds expert ids local to the range (0 .. n_experts_local-1) or -1 for
- * slots another GPU computes; d_out[r] = sum over the local slots, in k order,
- * of d_wt[r,k] * FFN_k(d_xb[r]) (rabbit2.c:532-541). */
-int rbt_moe_experts_device(RbtMoe *m, int layer, const float *d_xb, int n_rows, const int32_t *d_idx,
-                           const float *d_wt, float *d_out, void *stream);
-
-/* Dispatch plan: d_pos [n_tokens, n_ranks] = position of token t among the
- * tokens sent to GPU g (ascending t) or -1; d_counts [n_ranks] = tokens sent to
- * each GPU.  GPU g owns experts [g*experts_per_rank, (g+1)*experts_per_rank).
- * capacity > 0 (>= n_tokens): fixed segments instead, position t in a segment of
- * `capacity` rows per GPU, so the exchange sizes are known without reading
- * d_counts on the host (slots of rows not routed there must be -1 in the send
- * idx buffer: fill it with -1 before rbt_ep_pack). */
-int rbt_ep_plan(const int32_t *d_idx, int n_tokens, int top_k, int n_ranks, int experts_per_rank, int capacity,
-                int32_t *d_pos, int32_t *d_counts, void *stream);
-
-/* Send buffers in GPU order (segment g starts at counts[0] + ... + counts[g-1]):
- * rows [., dim] = d_xb[t], idx [., top_k] = expert ids local to GPU g or -1,
- * wt [., top_k] = the token's combine weights. */
-int rbt_ep_pack(const float *d_xb, const int32_t *d_idx, const float *d_wt, int n_tokens, int dim, int top_k,
-                int n_ranks, int experts_per_rank, const int32_t *d_pos, const int32_t *d_counts, float *d_send_rows,
-                int32_t *d_send_idx, float *d_send_wt, void *stream);
-
-/* d_out[t] = d_x[t] (if not NULL) + the returned partial rows of token t added
- * in ascending GPU order; d_back_rows is laid out like the send rows.  d_out
- * may equal d_x. */
-int rbt_ep_combine(const float *d_x, int n_tokens, int dim, int n_ranks, const int32_t *d_pos,
-                   const int32_t *d_counts, const float *d_back_rows, float *d_out, void *stream);
 
 /* Reserve the context's device workspace for up to n_tokens rows per call, so
  * that later calls of that size allocate nothing (e.g. before stream capture). */
@@ -161,7 +176,8 @@ int rbt_moe_set_path(RbtMoe *m, int path);
 
 /* Launch accounting and per-stage device timing.  Stages: 0 rmsnorm, 1 router +
  * top-k + permute, 2 gate/up + SwiGLU, 3 down, 4 combine, 5 operand gather
- * (GEMM path), 6 the fused one-token decode kernel.  With timing on, every call records a CUDA event at each stage
+ * (GEMM path), 6 the fused one-token decode kernel, 7 the expert-parallel plan,
+ * dispatch, receive, return and combine.  With timing on, every call records a CUDA event at each stage
  * boundary on its stream (as graph nodes when the stream is being captured)
  * and nothing waits; stage_ms sums the intervals recorded since the last reset,
  * read from the events' latest timestamps (so after a graph replay it holds

@@ -98,4 +98,13 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, in
     return cudaGetLastError();
 }
 
+// Loads the combine and rmsnorm kernels now (see preload_kernels in kernels.h).
+void preload_combine_kernels() {
+    cudaFuncAttributes f;
+    (void)cudaFuncGetAttributes(&f, combine_vec4_kernel);
+    (void)cudaFuncGetAttributes(&f, combine_scalar_kernel);
+    (void)cudaFuncGetAttributes(&f, rmsnorm_kernel);
+    (void)cudaGetLastError();
+}
+
 }  // namespace rbt

@@ -515,4 +515,22 @@ cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const C
     return launch_gemm<false>(w, hhi, hlo, a, grid, s);
 }
 
+// Loads every tensor-core path kernel now (see preload_kernels in kernels.h).
+void preload_gemm_kernels() {
+    cudaFuncAttributes f;
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<true, 32, false>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<true, 64, false>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<true, 128, false>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<false, 32, false>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<false, 64, false>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<false, 128, false>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<true, 32, true>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<true, 64, true>);
+    (void)cudaFuncGetAttributes(&f, moe_tc_gemm_kernel<true, 128, true>);
+    (void)cudaFuncGetAttributes(&f, gather_split_kernel);
+    (void)cudaFuncGetAttributes(&f, gather_f16_kernel);
+    (void)cudaFuncGetAttributes(&f, tc_schedule_kernel);
+    (void)cudaGetLastError();
+}
+
 }  // namespace rbt

@@ -238,4 +238,22 @@ cudaError_t launch_gateup_gemv(const GemvArgs& args, cudaStream_t s) {
 
 cudaError_t launch_down_gemv(const GemvArgs& a, cudaStream_t s) { RBT_GEMV_DISPATCH(down_gemv_kernel) }
 
+// Loads every CUDA-core GEMV kernel now (see preload_kernels in kernels.h).
+void preload_gemv_kernels() {
+    cudaFuncAttributes f;
+#define RBT_PRELOAD_GEMV(WT, V, M)                                          \
+    (void)cudaFuncGetAttributes(&f, gateup_gemv_kernel<WT, V, M>);          \
+    (void)cudaFuncGetAttributes(&f, down_gemv_kernel<WT, V, M>);
+    RBT_PRELOAD_GEMV(uint16_t, true, 1)
+    RBT_PRELOAD_GEMV(uint16_t, true, 4)
+    RBT_PRELOAD_GEMV(uint16_t, false, 1)
+    RBT_PRELOAD_GEMV(uint16_t, false, 4)
+    RBT_PRELOAD_GEMV(float, true, 1)
+    RBT_PRELOAD_GEMV(float, true, 4)
+    RBT_PRELOAD_GEMV(float, false, 1)
+    RBT_PRELOAD_GEMV(float, false, 4)
+#undef RBT_PRELOAD_GEMV
+    (void)cudaGetLastError();
+}
+
 }  // namespace rbt

@@ -190,3 +190,59 @@ cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const C
                            int grid, cudaStream_t s);
 
 }  // namespace rbt
+
+namespace rbt {
+
+// ---- Expert parallelism over NVLink peer memory (ep.cu) ----
+// GPU g of R owns experts [g*epr, (g+1)*epr).  Each GPU's EP block holds, per
+// source GPU s, a segment of `cap` received rows (f32 [D]), their K expert ids
+// local to this GPU (-1: another GPU's slot, or no row) and K combine weights, the
+// row count, and a dispatch flag; and per destination GPU g a segment of `cap`
+// returned partial rows and a return flag.  Flags hold epochs (one per layer call,
+// counted on the device), so nothing is ever reset.
+constexpr int kEpMaxRanks = 8;
+struct EpPeers {
+    float* recv_rows[kEpMaxRanks];                    // GPU g's [R][cap][D]
+    int32_t* recv_idx[kEpMaxRanks];                   // GPU g's [R][cap][K]
+    float* recv_wt[kEpMaxRanks];                      // GPU g's [R][cap][K]
+    int32_t* recv_count[kEpMaxRanks];                 // GPU g's [R]
+    unsigned long long* flag_dispatch[kEpMaxRanks];   // GPU g's [R], slot = source
+    float* back_rows[kEpMaxRanks];                    // GPU g's [R][cap][D]
+    unsigned long long* flag_return[kEpMaxRanks];     // GPU g's [R], slot = destination
+};
+struct EpArgs {
+    EpPeers peers;            // every GPU's buffers (this GPU's own at [rank])
+    int R, rank, epr, cap, D, K;
+    unsigned long long* epoch;  // this GPU's last finished layer call (read by all, advanced by the combine)
+    unsigned* done;           // [2 + R] zeroed tickets: dispatch, combine, return per source
+    unsigned* status;         // this context's status word
+    unsigned long long timeout_ns;
+};
+// route -> plan (ep_plan, positions of the T tokens among those sent to each GPU)
+// -> dispatch (rows, ids, weights into the owners' segments; count and flag) ->
+// receive (wait for every source's flag; clear the ids of unused rows) -> the
+// experts on the R*cap received rows -> return (each valid row's weighted sum over
+// its slots into its source's segment; flag) -> combine (wait for every GPU's
+// return flag; x += partials in GPU order; advance the epoch).
+cudaError_t launch_ep_plan(const int32_t* idx, int T, int K, int R, int epr, int32_t* pos, int32_t* counts,
+                           cudaStream_t s);
+cudaError_t launch_ep_dispatch(const EpArgs& a, const float* xb, const int32_t* idx, const float* wt,
+                               const int32_t* pos, const int32_t* counts, int T, cudaStream_t s);
+cudaError_t launch_ep_receive(const EpArgs& a, cudaStream_t s);
+cudaError_t launch_ep_return(const EpArgs& a, const float* y, const int32_t* slot_pos, cudaStream_t s);
+cudaError_t launch_ep_combine(const EpArgs& a, float* x, const int32_t* pos, int T, cudaStream_t s);
+
+// With lazy module loading (the CUDA 12 default) a kernel is loaded at its first
+// launch, and that load can wait for kernels already running on the device.  An
+// expert-parallel layer has kernels that wait for other GPUs: a first launch issued
+// behind one of them could stall the host until the wait gives up, before the
+// other GPUs' work is even launched (one host thread driving several GPUs).  These
+// load every kernel of the expert-parallel path up front (cudaFuncGetAttributes),
+// on the current device.
+void preload_router_kernels();
+void preload_gemm_kernels();
+void preload_gemv_kernels();
+void preload_combine_kernels();
+void preload_ep_kernels();
+
+}  // namespace rbt

@@ -96,6 +96,23 @@ struct StageMark {
     int stage, ev_begin, ev_end;  // indices into the event pool
 };
 
+// Expert parallelism (rbt_moe_ep_*): this GPU's exported block of receive and
+// return segments and flags, its local plan buffers, and every GPU's pointers.
+struct EpState {
+    int R = 0, rank = 0, epr = 0, cap = 0;
+    void* block = nullptr;         // exported (IPC) or peer-read block
+    size_t block_bytes = 0;
+    size_t off_rows = 0, off_idx = 0, off_wt = 0, off_count = 0, off_fdisp = 0, off_back = 0, off_fret = 0;
+    void* local = nullptr;         // pos [cap][R], counts [R], epoch, tickets
+    int32_t *pos = nullptr, *counts = nullptr;
+    unsigned long long* epoch = nullptr;
+    unsigned* done = nullptr;
+    rbt::EpPeers peers{};
+    std::vector<void*> opened;     // peer blocks opened from IPC handles
+    bool connected = false;
+    unsigned long long timeout_ns = 2000000000ull;
+};
+
 struct RbtMoe {
     RbtMoeConfig cfg;
     bool timing = false;
@@ -116,6 +133,7 @@ struct RbtMoe {
     unsigned long long ws_gen = 0;  // workspace allocations so far
     unsigned* h_status = nullptr;   // pinned host copy of the status word (host-pointer calls)
     int last_routed = 0;            // tokens the most recent routed call computed logits for
+    EpState ep;
 };
 
 namespace {
@@ -364,12 +382,13 @@ rbt::StreamArgs sa_of(RbtMoe* m, const Layer& L, const float* xb, const float* x
 // x is then the router input itself (no norm, no router) and out = the weighted
 // sum over the local slots.
 int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* routing, int routing_stride,
-            cudaStream_t s, bool block, const int32_t* given_idx = nullptr, const float* given_wt = nullptr) {
+            cudaStream_t s, bool block, const int32_t* given_idx = nullptr, const float* given_wt = nullptr,
+            bool ep_rows = false) {
     if (!check_layer(m, layer, block)) return 0;
     const bool given = given_idx != nullptr;
     if (!given && m->n_local != m->cfg.n_experts)
-        return fail("this context holds experts [%d, %d) only (expert parallelism): use rbt_moe_route_device and "
-                    "rbt_moe_experts_device", m->e0, m->e0 + m->n_local);
+        return fail("this context holds experts [%d, %d) only (expert parallelism): use rbt_moe_ep_block_device",
+                    m->e0, m->e0 + m->n_local);
     const int E_run = given ? m->n_local : m->cfg.n_experts;
     if (T < 0) return fail("n_tokens must be >= 0 (got %d)", T);
     if (T == 0) return 1;
@@ -472,7 +491,8 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
         if (!clk.begin(3)) return 0;
         CU(rbt::launch_tc_down(L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
-    } else if (m->path != 3 && rbt::stream_supported(sa_of(m, L, xb, x, out, T, block && !given), c.dtype)) {
+    } else if (!ep_rows && m->path != 3 &&
+               rbt::stream_supported(sa_of(m, L, xb, x, out, T, block && !given), c.dtype)) {
         rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, block && !given);
         sa.wt = wt;
         if (!clk.begin(2)) return 0;
@@ -491,6 +511,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         if (!clk.begin(3)) return 0;
         CU(rbt::launch_down_gemv(ga, s));
     }
+    if (ep_rows) return clk.end();  // the expert outputs go back to their GPUs (launch_ep_return)
 
     rbt::CombineArgs ca{};
     ca.resid = block && !given ? x : nullptr;
@@ -630,6 +651,9 @@ void rbt_moe_destroy(RbtMoe* m) {
     }
     cudaFree(m->ws.block);
     if (m->ws.pinned) cudaFreeHost(m->ws.pinned);
+    for (void* p : m->ep.opened) cudaIpcCloseMemHandle(p);
+    cudaFree(m->ep.block);
+    cudaFree(m->ep.local);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
     cudaStreamDestroy(m->stream);
     cudaFreeHost(m->h_status);
@@ -721,7 +745,12 @@ int rbt_moe_ffn_device(RbtMoe* m, int layer, const float* d_xb, int n_tokens, fl
     return forward(m, layer, d_xb, d_moe_out, n_tokens, d_routing_out, routing_stride, (cudaStream_t)stream, false);
 }
 
-int rbt_moe_set_expert_range(RbtMoe* m, int first_expert, int n_experts_local) {
+// ---------------------------------------------------------------- expert parallelism
+
+namespace {
+
+// Narrow the context to experts [first_expert, first_expert + n_experts_local) (before any layer is bound).
+int set_expert_range(RbtMoe* m, int first_expert, int n_experts_local) {
     if (!m) return fail("null context");
     const int E = m->cfg.n_experts;
     if (first_expert < 0 || n_experts_local <= 0 || first_expert + n_experts_local > E)
@@ -730,6 +759,266 @@ int rbt_moe_set_expert_range(RbtMoe* m, int first_expert, int n_experts_local) {
         if (L.experts) return fail("set the expert range before loading or binding any layer");
     m->e0 = first_expert;
     m->n_local = n_experts_local;
+    return 1;
+}
+
+// The EP block's layout, the same on every GPU of a group (same config, R, cap).
+void ep_layout(RbtMoe* m) {
+    EpState& p = m->ep;
+    const size_t R = p.R, cap = p.cap, D = m->cfg.dim, K = m->cfg.top_k;
+    size_t o = 256;  // a header first: the block's shape, checked when peers connect
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes, 256);
+        return at;
+    };
+    p.off_rows = take(R * cap * D * 4);
+    p.off_back = take(R * cap * D * 4);
+    p.off_idx = take(R * cap * K * 4);
+    p.off_wt = take(R * cap * K * 4);
+    p.off_count = take(R * 4);
+    p.off_fdisp = take(R * 8);
+    p.off_fret = take(R * 8);
+    p.block_bytes = o;
+}
+
+// Pointers into GPU g's block (whose base in this process is `base`).
+void ep_set_peer(EpState& p, int g, char* base) {
+    p.peers.recv_rows[g] = reinterpret_cast<float*>(base + p.off_rows);
+    p.peers.back_rows[g] = reinterpret_cast<float*>(base + p.off_back);
+    p.peers.recv_idx[g] = reinterpret_cast<int32_t*>(base + p.off_idx);
+    p.peers.recv_wt[g] = reinterpret_cast<float*>(base + p.off_wt);
+    p.peers.recv_count[g] = reinterpret_cast<int32_t*>(base + p.off_count);
+    p.peers.flag_dispatch[g] = reinterpret_cast<unsigned long long*>(base + p.off_fdisp);
+    p.peers.flag_return[g] = reinterpret_cast<unsigned long long*>(base + p.off_fret);
+}
+
+// The header of an EP block: what every GPU of the group must agree on.
+struct EpHeader {
+    uint32_t magic, R, cap, D, K, E;
+};
+constexpr uint32_t kEpMagic = 0x52425445u;  // "ETBR"
+EpHeader ep_header(const RbtMoe* m) {
+    return EpHeader{kEpMagic, (uint32_t)m->ep.R, (uint32_t)m->ep.cap, (uint32_t)m->cfg.dim,
+                    (uint32_t)m->cfg.top_k, (uint32_t)m->cfg.n_experts};
+}
+
+rbt::EpArgs ep_args(RbtMoe* m) {
+    const EpState& p = m->ep;
+    rbt::EpArgs a{};
+    a.peers = p.peers;
+    a.R = p.R; a.rank = p.rank; a.epr = p.epr; a.cap = p.cap; a.D = m->cfg.dim; a.K = m->cfg.top_k;
+    a.epoch = p.epoch; a.done = p.done; a.status = m->ws.status; a.timeout_ns = p.timeout_ns;
+    return a;
+}
+
+// One expert-parallel MoE block on this GPU: d_x [T, D] += MoE(rmsnorm(d_x)).
+int ep_block(RbtMoe* m, int layer, float* d_x, int T, int32_t* d_routing, int routing_stride, cudaStream_t s) {
+    EpState& p = m->ep;
+    if (!p.connected) return fail("expert parallelism: rbt_moe_ep_connect (or _connect_local) first");
+    if (T < 0 || T > p.cap) return fail("n_tokens %d outside [0, %d] (the max_tokens of rbt_moe_ep_init)", T, p.cap);
+    if (T > 0 && !d_x) return fail("null input");
+    if (d_routing && routing_stride < m->cfg.top_k)
+        return fail("routing_stride %d < top_k %d", routing_stride, m->cfg.top_k);
+    if (!check_layer(m, layer, true) || !set_device(m) || !reserve(m, p.R * p.cap)) return 0;
+    const RbtMoeConfig& c = m->cfg;
+    const Layer& L = m->layers[layer];
+    Workspace& w = m->ws;
+    StageClock clk{m, s};
+    m->prof.calls++;
+    if (T > 0) {  // rmsnorm + the whole router (global expert ids), bit-exact as on one GPU
+        m->last_routed = T;
+        rbt::RouterArgs ra{};
+        ra.xb = w.xb; ra.x_raw = d_x; ra.norm_w = L.ffn_norm; ra.eps = c.rms_eps;
+        ra.T = T; ra.D = c.dim; ra.E = c.n_experts; ra.K = c.top_k;
+        ra.router = L.router; ra.dtype = c.dtype; ra.bias = L.bias; ra.norm_topk = c.norm_topk;
+        ra.logits = w.logits; ra.idx = w.idx; ra.wt = w.wt;
+        ra.routing_out = d_routing; ra.routing_stride = routing_stride;
+        ra.tile_counter = w.tile_counter; ra.done_counter = w.done_counter;
+        ra.counts = w.counts; ra.offsets = w.offsets; ra.perm = w.perm; ra.slot_pos = w.slot_pos;
+        ra.active = w.active; ra.n_active = w.n_active;
+        ra.tile_cnt = w.tile_cnt; ra.tile_base = w.tile_base; ra.slot_rank = w.slot_rank;
+        ra.router_cm = static_cast<const uint16_t*>(L.router_cm); ra.status = w.status;
+        if (!clk.begin(1)) return 0;
+        int launches = 0;
+        CU(rbt::launch_router(ra, s, &launches));
+        m->prof.launches += launches - 1;
+    }
+    const rbt::EpArgs a = ep_args(m);
+    if (!clk.begin(7)) return 0;
+    CU(rbt::launch_ep_plan(w.idx, T, c.top_k, p.R, p.epr, p.pos, p.counts, s));
+    m->prof.launches += 2;
+    CU(rbt::launch_ep_dispatch(a, w.xb, w.idx, w.wt, p.pos, p.counts, T, s));
+    CU(rbt::launch_ep_receive(a, s));
+    // the experts of this GPU on every row it received ([R][cap], unused rows have no slots)
+    char* own = static_cast<char*>(p.block);
+    if (!forward(m, layer, reinterpret_cast<const float*>(own + p.off_rows), nullptr, p.R * p.cap, nullptr,
+                 c.top_k, s, false, reinterpret_cast<const int32_t*>(own + p.off_idx),
+                 reinterpret_cast<const float*>(own + p.off_wt), true))
+        return 0;
+    if (!clk.begin(7)) return 0;
+    CU(rbt::launch_ep_return(a, w.y, w.slot_pos, s));
+    m->prof.launches++;
+    CU(rbt::launch_ep_combine(a, d_x, p.pos, T, s));
+    return clk.end();
+}
+
+}  // namespace
+
+int rbt_moe_ep_init(RbtMoe* m, int rank, int n_ranks, int max_tokens) {
+    if (!m) return fail("null context");
+    const int E = m->cfg.n_experts;
+    if (n_ranks < 1 || n_ranks > rbt::kEpMaxRanks || rank < 0 || rank >= n_ranks || E % n_ranks)
+        return fail("expert parallelism: %d experts over %d GPUs (rank %d): need 1 <= n_ranks <= %d dividing the "
+                    "experts", E, n_ranks, rank, rbt::kEpMaxRanks);
+    if (max_tokens < 1) return fail("max_tokens must be >= 1");
+    if (m->cfg.dim % 4) return fail("expert parallelism needs dim %% 4 == 0");
+    if (m->ep.block) return fail("rbt_moe_ep_init was called already");
+    if (!set_expert_range(m, rank * (E / n_ranks), E / n_ranks)) return 0;
+    if (!set_device(m)) return 0;
+    // every kernel of the layer loaded now, not at a first launch behind a waiting kernel
+    rbt::preload_router_kernels();
+    rbt::preload_gemm_kernels();
+    rbt::preload_gemv_kernels();
+    rbt::preload_combine_kernels();
+    rbt::preload_ep_kernels();
+    EpState& p = m->ep;
+    p.R = n_ranks; p.rank = rank; p.epr = E / n_ranks; p.cap = max_tokens;
+    ep_layout(m);
+    CU(cudaMalloc(&p.block, p.block_bytes));
+    CU(cudaMemset(p.block, 0, p.block_bytes));
+    const EpHeader hdr = ep_header(m);
+    CU(cudaMemcpy(p.block, &hdr, sizeof hdr, cudaMemcpyHostToDevice));
+    const size_t pos_b = align_up((size_t)max_tokens * n_ranks * 4, 256), cnt_b = 256, ep_b = 256;
+    CU(cudaMalloc(&p.local, pos_b + cnt_b + ep_b + 256));
+    CU(cudaMemset(p.local, 0, pos_b + cnt_b + ep_b + 256));
+    char* l = static_cast<char*>(p.local);
+    p.pos = reinterpret_cast<int32_t*>(l);
+    p.counts = reinterpret_cast<int32_t*>(l + pos_b);
+    p.epoch = reinterpret_cast<unsigned long long*>(l + pos_b + cnt_b);
+    p.done = reinterpret_cast<unsigned*>(l + pos_b + cnt_b + ep_b);
+    ep_set_peer(p, rank, static_cast<char*>(p.block));
+    return 1;
+}
+
+int rbt_moe_ep_handle(RbtMoe* m, void* handle_out) {
+    if (!m || !handle_out) return fail("null argument");
+    if (!m->ep.block) return fail("rbt_moe_ep_init first");
+    if (!set_device(m)) return 0;
+    cudaIpcMemHandle_t h;
+    CU(cudaIpcGetMemHandle(&h, m->ep.block));
+    memcpy(handle_out, &h, sizeof h);
+    return 1;
+}
+
+int rbt_moe_ep_connect(RbtMoe* m, const void* handles) {
+    if (!m || !handles) return fail("null argument");
+    EpState& p = m->ep;
+    if (!p.block) return fail("rbt_moe_ep_init first");
+    if (p.connected) return fail("already connected");
+    if (!set_device(m)) return 0;
+    for (int g = 0; g < p.R; g++) {
+        if (g == p.rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + (size_t)g * sizeof h, sizeof h);
+        void* base = nullptr;
+        CU(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+        p.opened.push_back(base);
+        EpHeader theirs{}, ours = ep_header(m);
+        CU(cudaMemcpy(&theirs, base, sizeof theirs, cudaMemcpyDeviceToHost));
+        if (memcmp(&theirs, &ours, sizeof ours) != 0)
+            return fail("expert parallelism: rank %d's block has another shape (n_ranks %u, max_tokens %u, dim %u, "
+                        "top_k %u, n_experts %u; here %u, %u, %u, %u, %u)", g, theirs.R, theirs.cap, theirs.D,
+                        theirs.K, theirs.E, ours.R, ours.cap, ours.D, ours.K, ours.E);
+        ep_set_peer(p, g, static_cast<char*>(base));
+    }
+    p.connected = true;
+    return 1;
+}
+
+int rbt_moe_ep_connect_local(RbtMoe* const* ms, int n) {
+    if (!ms || n < 1) return fail("null argument");
+    for (int i = 0; i < n; i++) {
+        if (!ms[i] || !ms[i]->ep.block) return fail("rbt_moe_ep_init every context first");
+        if (ms[i]->ep.R != n || ms[i]->ep.rank != i) return fail("context %d is not rank %d of %d", i, i, n);
+        const EpHeader a = ep_header(ms[i]), b = ep_header(ms[0]);
+        if (memcmp(&a, &b, sizeof a) != 0) return fail("context %d's group shape differs from context 0's", i);
+    }
+    for (int i = 0; i < n; i++) {
+        RbtMoe* m = ms[i];
+        if (!set_device(m)) return 0;
+        for (int j = 0; j < n; j++) {
+            if (j == i) continue;
+            if (ms[j]->device != m->device) {
+                int can = 0;
+                CU(cudaDeviceCanAccessPeer(&can, m->device, ms[j]->device));
+                if (!can) return fail("GPU %d cannot access GPU %d's memory", m->device, ms[j]->device);
+                const cudaError_t e = cudaDeviceEnablePeerAccess(ms[j]->device, 0);
+                if (e == cudaErrorPeerAccessAlreadyEnabled) (void)cudaGetLastError();
+                else if (e != cudaSuccess) return fail("cudaDeviceEnablePeerAccess: %s", cudaGetErrorString(e));
+            }
+            ep_set_peer(m->ep, j, static_cast<char*>(ms[j]->ep.block));
+        }
+        m->ep.connected = true;
+    }
+    return 1;
+}
+
+int rbt_moe_ep_set_timeout(RbtMoe* m, uint64_t timeout_ns) {
+    if (!m) return fail("null context");
+    if (timeout_ns < 1000) return fail("timeout below 1 us");
+    m->ep.timeout_ns = timeout_ns;
+    return 1;
+}
+
+int rbt_moe_ep_block_device(RbtMoe* m, int layer, float* d_x, int n_tokens, int32_t* d_routing_out,
+                            int routing_stride, void* stream) {
+    if (!m) return fail("null context");
+    return ep_block(m, layer, d_x, n_tokens, d_routing_out, routing_stride, (cudaStream_t)stream);
+}
+
+int rbt_moe_ep_block(RbtMoe* const* ms, int n, int layer, float* x, int n_tokens, int32_t* routing_out,
+                     int routing_stride) {
+    if (!ms || n < 1 || !ms[0]) return fail("null argument");
+    RbtMoe* m0 = ms[0];
+    if (n_tokens < 0) return fail("n_tokens must be >= 0 (got %d)", n_tokens);
+    if (n_tokens == 0) return 1;
+    if (!x) return fail("null x");
+    if (n_tokens > m0->ep.cap) return fail("n_tokens %d above max_tokens %d", n_tokens, m0->ep.cap);
+    for (int g = 0; g < n; g++)
+        if (!set_device(ms[g]) || !reserve(ms[g], ms[g]->ep.R * ms[g]->ep.cap)) return 0;
+    Workspace& w0 = m0->ws;
+    const size_t bytes = (size_t)n_tokens * m0->cfg.dim * sizeof(float);
+    if (!set_device(m0)) return 0;
+    CU(cudaMemcpyAsync(w0.hx, x, bytes, cudaMemcpyHostToDevice, m0->stream));
+    // every GPU runs the layer; GPU 0 holds the tokens, the others only their experts
+    for (int g = 0; g < n; g++) {
+        if (!set_device(ms[g])) return 0;
+        if (!ep_block(ms[g], layer, g == 0 ? w0.hx : nullptr, g == 0 ? n_tokens : 0,
+                      g == 0 && routing_out ? w0.hrouting : nullptr, m0->cfg.top_k, ms[g]->stream))
+            return 0;
+    }
+    if (!set_device(m0)) return 0;
+    CU(cudaMemcpyAsync(x, w0.hx, bytes, cudaMemcpyDeviceToHost, m0->stream));
+    if (routing_out)
+        CU(cudaMemcpy2DAsync(routing_out, (size_t)routing_stride * 4, w0.hrouting, (size_t)m0->cfg.top_k * 4,
+                             (size_t)m0->cfg.top_k * 4, n_tokens, cudaMemcpyDeviceToHost, m0->stream));
+    for (int g = 0; g < n; g++) {
+        if (!set_device(ms[g])) return 0;
+        CU(cudaStreamSynchronize(ms[g]->stream));
+        if (!check_status(ms[g])) return fail("expert parallelism: GPU %d (rank %d) failed", ms[g]->device, g);
+    }
+    return 1;
+}
+
+int rbt_moe_status(RbtMoe* m, unsigned* status_out) {
+    if (!m || !status_out) return fail("null argument");
+    *status_out = 0;
+    if (!m->ws.block) return 1;
+    if (!set_device(m)) return 0;
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(status_out, m->ws.status, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (*status_out) CU(cudaMemset(m->ws.status, 0, 4));
     return 1;
 }
 
@@ -768,13 +1057,6 @@ int rbt_moe_route_device(RbtMoe* m, int layer, const float* d_x, int n_tokens, i
     CU(rbt::launch_router(ra, s, &launches));
     m->prof.launches += launches - 1;
     return clk.end();
-}
-
-int rbt_moe_experts_device(RbtMoe* m, int layer, const float* d_xb, int n_rows, const int32_t* d_idx,
-                           const float* d_wt, float* d_out, void* stream) {
-    if (!m) return fail("null context");
-    if (n_rows > 0 && (!d_xb || !d_idx || !d_wt || !d_out)) return fail("null argument");
-    return forward(m, layer, d_xb, d_out, n_rows, nullptr, m->cfg.top_k, (cudaStream_t)stream, false, d_idx, d_wt);
 }
 
 int rbt_moe_expert_histogram(RbtMoe* m, int32_t* counts_out) {

@@ -1189,6 +1189,25 @@ cudaError_t router_to_chain_major(const void* router, int E, int D, void* out, c
     return cudaGetLastError();
 }
 
+// Loads every router kernel now (see preload_kernels in kernels.h).
+void preload_router_kernels() {
+    cudaFuncAttributes f;
+    (void)cudaFuncGetAttributes(&f, router_tok_kernel);
+    (void)cudaFuncGetAttributes(&f, router_small_kernel<uint16_t>);
+    (void)cudaFuncGetAttributes(&f, router_small_kernel<float>);
+    (void)cudaFuncGetAttributes(&f, router_wide_kernel<uint16_t>);
+    (void)cudaFuncGetAttributes(&f, router_wide_kernel<float>);
+    (void)cudaFuncGetAttributes(&f, router_large_kernel<uint16_t, 1>);
+    (void)cudaFuncGetAttributes(&f, router_large_kernel<uint16_t, 2>);
+    (void)cudaFuncGetAttributes(&f, router_large_kernel<uint16_t, 4>);
+    (void)cudaFuncGetAttributes(&f, router_large_kernel<float, 1>);
+    (void)cudaFuncGetAttributes(&f, router_large_kernel<float, 2>);
+    (void)cudaFuncGetAttributes(&f, router_large_kernel<float, 4>);
+    (void)cudaFuncGetAttributes(&f, scatter_kernel);
+    (void)cudaFuncGetAttributes(&f, route_given_kernel);
+    (void)cudaGetLastError();
+}
+
 }  // namespace rbt
 
 #ifdef RBT_ROUTER_TIMELINE

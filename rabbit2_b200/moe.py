@@ -37,7 +37,7 @@ class RbtMoeProfile(C.Structure):
                 ("stage_launches", C.c_int64 * 8)]
 
 
-STAGES = ("rmsnorm", "router", "gate_up", "down", "combine", "gather", "decode_fused", "")
+STAGES = ("rmsnorm", "router", "gate_up", "down", "combine", "gather", "decode_fused", "ep_exchange")
 
 _lib = None
 
@@ -64,12 +64,15 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_moe_expert_histogram": [vp, vp],
         "rbt_moe_set_path": [vp, i32],
         "rbt_moe_profile": [vp, i32, i32, C.POINTER(RbtMoeProfile)],
-        "rbt_moe_set_expert_range": [vp, i32, i32],
         "rbt_moe_route_device": [vp, i32, vp, i32, i32, vp, vp, vp, vp],
-        "rbt_moe_experts_device": [vp, i32, vp, i32, vp, vp, vp, vp],
-        "rbt_ep_plan": [vp, i32, i32, i32, i32, i32, vp, vp, vp],
-        "rbt_ep_pack": [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp],
-        "rbt_ep_combine": [vp, i32, i32, i32, vp, vp, vp, vp, vp],
+        "rbt_moe_ep_init": [vp, i32, i32, i32],
+        "rbt_moe_ep_handle": [vp, vp],
+        "rbt_moe_ep_connect": [vp, vp],
+        "rbt_moe_ep_connect_local": [vp, i32],
+        "rbt_moe_ep_set_timeout": [vp, C.c_uint64],
+        "rbt_moe_ep_block_device": [vp, i32, vp, i32, vp, i32, vp],
+        "rbt_moe_ep_block": [vp, i32, i32, vp, i32, vp, i32],
+        "rbt_moe_status": [vp, C.POINTER(C.c_uint)],
         "rbt_model_create": [C.POINTER(vp), vp, i32, i32],
         "rbt_model_load_globals": [vp, vp, vp, vp],
         "rbt_model_load_layer": [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
@@ -187,23 +190,42 @@ class MoeContext:
         self._call(self.lib.rbt_moe_block_device, self.handle, layer, _ptr(x), T, _ptr(routing),
                    routing_stride or self.K, _ptr(stream) if stream is not None else None)
 
-    # expert parallelism
-    def set_expert_range(self, first_expert, n_local):
-        """Hold only experts [first_expert, first_expert + n_local) (before any layer is bound)."""
-        self._call(self.lib.rbt_moe_set_expert_range, self.handle, first_expert, n_local)
-        self.e0, self.n_local = first_expert, n_local
+    # expert parallelism (rbt_moe_ep_*)
+    def ep_init(self, rank, n_ranks, max_tokens):
+        """Rank `rank` of an n_ranks expert-parallel group (before any layer is bound):
+        this context then holds experts [rank*E/n, (rank+1)*E/n)."""
+        self._call(self.lib.rbt_moe_ep_init, self.handle, rank, n_ranks, max_tokens)
+        self.e0, self.n_local = rank * (self.E // n_ranks), self.E // n_ranks
+
+    def ep_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        self._call(self.lib.rbt_moe_ep_handle, self.handle, buf)
+        return buf.raw
+
+    def ep_connect(self, handles):
+        """handles: every rank's ep_handle() bytes, in rank order."""
+        blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        self._call(self.lib.rbt_moe_ep_connect, self.handle, blob)
+
+    def ep_set_timeout(self, ns):
+        self._call(self.lib.rbt_moe_ep_set_timeout, self.handle, int(ns))
+
+    def ep_block_device(self, layer, x, routing=None, T=None, stream=None, routing_stride=None):
+        T = x.shape[0] if T is None else T
+        self._call(self.lib.rbt_moe_ep_block_device, self.handle, layer, _ptr(x) if T else None, T, _ptr(routing),
+                   routing_stride or self.K, _ptr(stream) if stream is not None else None)
+
+    def status(self):
+        """The status word of this context's kernels (0: none failed), cleared; synchronises."""
+        v = C.c_uint(0)
+        self._call(self.lib.rbt_moe_status, self.handle, C.byref(v))
+        return v.value
 
     def route_device(self, layer, x, xb, idx, wt, block=True, T=None, stream=None):
-        """Router only: xb = rmsnorm(x) (block) or x; idx/wt [T, K] global ids and weights."""
+        """Router only: xb = rmsnorm(x) (block) or x; idx/wt [T, K] expert ids and weights."""
         T = x.shape[0] if T is None else T
         self._call(self.lib.rbt_moe_route_device, self.handle, layer, _ptr(x), T, int(block), _ptr(xb), _ptr(idx),
                    _ptr(wt), _ptr(stream) if stream is not None else None)
-
-    def experts_device(self, layer, xb, idx, wt, out, n=None, stream=None):
-        """out[r] = sum over local slots (idx >= 0, ids local to the range) of wt * FFN(xb[r])."""
-        n = xb.shape[0] if n is None else n
-        self._call(self.lib.rbt_moe_experts_device, self.handle, layer, _ptr(xb), n, _ptr(idx), _ptr(wt),
-                   _ptr(out), _ptr(stream) if stream is not None else None)
 
     def profile(self, timing=-1, reset=False):
         """Launch counts and per-stage device ms since the last reset (dict)."""
@@ -223,6 +245,26 @@ class MoeContext:
         out = np.empty((n_tokens, self.E), np.float32)
         self._call(self.lib.rbt_moe_router_logits, self.handle, _ptr(out), n_tokens)
         return out
+
+
+def ep_connect_local(contexts):
+    """Connect contexts on this process's GPUs (rank g = contexts[g], each ep_init'ed)."""
+    lib = load_library()
+    arr = (C.c_void_p * len(contexts))(*[c.handle for c in contexts])
+    _check(lib.rbt_moe_ep_connect_local(arr, len(contexts)), lib)
+
+
+def ep_block(contexts, layer, x, routing_stride=None):
+    """rbt_moe_ep_block on host arrays: x [T, D] (a copy is updated and returned) with
+    the routing rows [T, K]; rank 0 holds the tokens."""
+    lib = load_library()
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    T, K = x.shape[0], contexts[0].K
+    stride = routing_stride or K
+    routing = np.zeros((T, stride), np.int32)
+    arr = (C.c_void_p * len(contexts))(*[c.handle for c in contexts])
+    _check(lib.rbt_moe_ep_block(arr, len(contexts), layer, _ptr(x), T, _ptr(routing), stride), lib)
+    return x, routing[:, :K]
 
 
 def _check(ok, lib):
