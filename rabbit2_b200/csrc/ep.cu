@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kThreads) ep_receive_kernel(EpArgs a) {
 // straight into source s's return segment for this GPU.  The last CTA of a
 // segment raises that source's flag.
 __global__ void __launch_bounds__(kThreads) ep_return_kernel(EpArgs a, const float* y, const int32_t* slot_pos,
-                                                              int chunks) {
+                                                              const float* rows, int chunks) {
     const unsigned long long e = *a.epoch + 1;
     const int s = blockIdx.x / chunks, c = blockIdx.x - s * chunks, tid = threadIdx.x, D4 = a.D / 4;
     const int n = a.peers.recv_count[a.rank][s];
@@ -160,6 +160,11 @@ __global__ void __launch_bounds__(kThreads) ep_return_kernel(EpArgs a, const flo
     for (int r = c * kReturnRows; r < n && r < (c + 1) * kReturnRows; r++) {
         const size_t row = (size_t)s * a.cap + r;
         float4* dst = reinterpret_cast<float4*>(a.peers.back_rows[s] + ((size_t)a.rank * a.cap + r) * a.D);
+        if (rows) {  // combined already (the streaming GEMV's down kernel)
+            const float4* src = reinterpret_cast<const float4*>(rows + row * a.D);
+            for (int d4 = tid; d4 < D4; d4 += kThreads) dst[d4] = src[d4];
+            continue;
+        }
         for (int d4 = tid; d4 < D4; d4 += kThreads) {
             float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int k = 0; k < a.K; k++) {
@@ -250,9 +255,10 @@ cudaError_t launch_ep_receive(const EpArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_return(const EpArgs& a, const float* y, const int32_t* slot_pos, cudaStream_t s) {
+cudaError_t launch_ep_return(const EpArgs& a, const float* y, const int32_t* slot_pos, const float* rows,
+                             cudaStream_t s) {
     const int chunks = (a.cap + kReturnRows - 1) / kReturnRows;
-    ep_return_kernel<<<a.R * chunks, kThreads, 0, s>>>(a, y, slot_pos, chunks);
+    ep_return_kernel<<<a.R * chunks, kThreads, 0, s>>>(a, y, slot_pos, rows, chunks);
     return cudaGetLastError();
 }
 

@@ -381,4 +381,14 @@ cudaError_t launch_down_combine_stream(const StreamArgs& a, int grid, cudaStream
     return launch_pdl(down_combine_stream_kernel<4>, grid, smem, a, s);
 }
 
+// Loads the weight-streaming kernels now (see preload_kernels in kernels.h).
+void preload_stream_kernels() {
+    cudaFuncAttributes f;
+    (void)cudaFuncGetAttributes(&f, gateup_stream_kernel<1, true>);
+    (void)cudaFuncGetAttributes(&f, gateup_stream_kernel<4, false>);
+    (void)cudaFuncGetAttributes(&f, down_combine_stream_kernel<1>);
+    (void)cudaFuncGetAttributes(&f, down_combine_stream_kernel<4>);
+    (void)cudaGetLastError();
+}
+
 }  // namespace rbt

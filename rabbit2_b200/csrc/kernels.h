@@ -229,7 +229,9 @@ cudaError_t launch_ep_plan(const int32_t* idx, int T, int K, int R, int epr, int
 cudaError_t launch_ep_dispatch(const EpArgs& a, const float* xb, const int32_t* idx, const float* wt,
                                const int32_t* pos, const int32_t* counts, int T, cudaStream_t s);
 cudaError_t launch_ep_receive(const EpArgs& a, cudaStream_t s);
-cudaError_t launch_ep_return(const EpArgs& a, const float* y, const int32_t* slot_pos, cudaStream_t s);
+// rows != nullptr: each received row's combined partial is already there (rows [R*cap][D])
+cudaError_t launch_ep_return(const EpArgs& a, const float* y, const int32_t* slot_pos, const float* rows,
+                             cudaStream_t s);
 cudaError_t launch_ep_combine(const EpArgs& a, float* x, const int32_t* pos, int T, cudaStream_t s);
 
 // With lazy module loading (the CUDA 12 default) a kernel is loaded at its first
@@ -242,6 +244,7 @@ cudaError_t launch_ep_combine(const EpArgs& a, float* x, const int32_t* pos, int
 void preload_router_kernels();
 void preload_gemm_kernels();
 void preload_gemv_kernels();
+void preload_stream_kernels();
 void preload_combine_kernels();
 void preload_ep_kernels();
 

@@ -89,6 +89,8 @@ struct Workspace {
     size_t span = 0;              // bytes from hx to the end of status
 };
 constexpr int kStageTokens = 128;
+// expert parallelism: received slots up to which the streaming GEMV beats the tensor cores
+constexpr int kEpStreamSlots = 128;
 
 }  // namespace
 
@@ -383,7 +385,7 @@ rbt::StreamArgs sa_of(RbtMoe* m, const Layer& L, const float* xb, const float* x
 // sum over the local slots.
 int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* routing, int routing_stride,
             cudaStream_t s, bool block, const int32_t* given_idx = nullptr, const float* given_wt = nullptr,
-            bool ep_rows = false) {
+            bool ep_rows = false, bool* rows_combined = nullptr) {
     if (!check_layer(m, layer, block)) return 0;
     const bool given = given_idx != nullptr;
     if (!given && m->n_local != m->cfg.n_experts)
@@ -457,6 +459,20 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
     m->prof.launches += router_launches - 1;
     const float* wt = given ? given_wt : w.wt;
 
+    // expert parallelism, few received rows: the weight-streaming GEMV, which also
+    // combines each row's slots (into `out`); the caller returns rows instead of slots
+    if (ep_rows && out && (m->path == 0 || m->path == 1) &&
+        (size_t)T * c.top_k <= (size_t)kEpStreamSlots &&
+        rbt::stream_supported(sa_of(m, L, xb, x, out, T, false), c.dtype)) {
+        rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, false);
+        sa.wt = wt;
+        if (!clk.begin(2)) return 0;
+        CU(rbt::launch_gateup_stream(sa, m->sm_count, s));
+        if (!clk.begin(3)) return 0;
+        CU(rbt::launch_down_combine_stream(sa, m->sm_count, s));
+        if (rows_combined) *rows_combined = true;
+        return clk.end();
+    }
     // the split kernel reads xb with 16-byte vectors
     const bool tc_ready = L.tc && w.tc_maps && (reinterpret_cast<uintptr_t>(xb) % 16 == 0);
     if (m->path == 2 && !tc_ready)
@@ -852,12 +868,13 @@ int ep_block(RbtMoe* m, int layer, float* d_x, int T, int32_t* d_routing, int ro
     CU(rbt::launch_ep_receive(a, s));
     // the experts of this GPU on every row it received ([R][cap], unused rows have no slots)
     char* own = static_cast<char*>(p.block);
-    if (!forward(m, layer, reinterpret_cast<const float*>(own + p.off_rows), nullptr, p.R * p.cap, nullptr,
+    bool rows = false;
+    if (!forward(m, layer, reinterpret_cast<const float*>(own + p.off_rows), w.hout, p.R * p.cap, nullptr,
                  c.top_k, s, false, reinterpret_cast<const int32_t*>(own + p.off_idx),
-                 reinterpret_cast<const float*>(own + p.off_wt), true))
+                 reinterpret_cast<const float*>(own + p.off_wt), true, &rows))
         return 0;
     if (!clk.begin(7)) return 0;
-    CU(rbt::launch_ep_return(a, w.y, w.slot_pos, s));
+    CU(rbt::launch_ep_return(a, w.y, w.slot_pos, rows ? w.hout : nullptr, s));
     m->prof.launches++;
     CU(rbt::launch_ep_combine(a, d_x, p.pos, T, s));
     return clk.end();
@@ -880,6 +897,7 @@ int rbt_moe_ep_init(RbtMoe* m, int rank, int n_ranks, int max_tokens) {
     rbt::preload_router_kernels();
     rbt::preload_gemm_kernels();
     rbt::preload_gemv_kernels();
+    rbt::preload_stream_kernels();
     rbt::preload_combine_kernels();
     rbt::preload_ep_kernels();
     EpState& p = m->ep;

@@ -1066,7 +1066,7 @@ __global__ void __launch_bounds__(kThreads) router_tok_kernel(RouterArgs a) {
 }
 
 bool tok_ok(const RouterArgs& a) {
-    return a.router_cm && a.dtype == 1 && a.E <= kTokMaxE && a.D % 256 == 0 && a.T >= 2 && a.T <= kTokMaxTokens &&
+    return a.router_cm && a.dtype == 1 && a.E <= kTokMaxE && a.D % 256 == 0 && a.T >= 1 && a.T <= kTokMaxTokens &&
            a.K <= kMaxTopK && a.tile_cnt && a.done_counter;
 }
 
