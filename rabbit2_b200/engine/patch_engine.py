@@ -34,7 +34,8 @@ INSERTIONS = [
      '        else if (!strcmp(argv[i], "--device") && i + 1 < argc) rbt_engine_device = argv[++i];\n'
      '        else if (!strcmp(argv[i], "--prefill") && i + 1 < argc) rbt_engine_prefill_mode = argv[++i];\n'
      '        else if (!strcmp(argv[i], "--offload") && i + 1 < argc) rbt_engine_offload = argv[++i];\n'
-     '        else if (!strcmp(argv[i], "--routing-trace") && i + 1 < argc) rbt_engine_trace_path = argv[++i];\n'),
+     '        else if (!strcmp(argv[i], "--routing-trace") && i + 1 < argc) rbt_engine_trace_path = argv[++i];\n'
+     '        else if (!strcmp(argv[i], "--ep") && i + 1 < argc) rbt_engine_ep_arg = argv[++i];\n'),
     ("    if (!load_model(&m, argv[1])) return 1;", "after",
      "    if (!rbt_engine_init(&m)) return 1;\n"),
     ("    double t0 = now_sec();", "after",

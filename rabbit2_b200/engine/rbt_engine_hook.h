@@ -10,6 +10,7 @@
  *                           --prefill batch|token   sets rbt_engine_prefill_mode
  *                           --offload moe|all       sets rbt_engine_offload
  *                           --routing-trace FILE    sets rbt_engine_trace_path
+ *                           --ep N                  sets rbt_engine_ep_arg
  *   main(), after load_model():  rbt_engine_init(&m)
  *   forward(), first statement (rabbit2.c:455):
  *       { int g = rbt_engine_forward(m, s, token, pos, routing_out);
@@ -36,6 +37,11 @@
  * returns x updated in place and the layer's routing row, as the CPU block does.
  * With --device cuda --offload all every weight is copied, and each forward() is
  * one rbt_model_forward() call (attention and lm_head on the GPU as well).
+ * With --device cuda --ep N (N > 1; the MoE offload) the experts are split over GPUs
+ * 0..N-1 of this process: GPU g holds experts [g*E/N, (g+1)*E/N) of every layer,
+ * and each MoE block is one rbt_moe_ep_block() call: GPU 0 routes the tokens, every
+ * GPU runs its experts on the rows routed to it (rows and partial results move
+ * over NVLink peer memory), and GPU 0 adds the partials in GPU order.
  */
 #ifndef RBT_ENGINE_HOOK_H
 #define RBT_ENGINE_HOOK_H
@@ -46,6 +52,9 @@ static const char *rbt_engine_device = NULL;
 static const char *rbt_engine_prefill_mode = NULL;  /* --prefill batch|token */
 static const char *rbt_engine_offload = NULL;       /* --offload moe|all */
 static const char *rbt_engine_trace_path = NULL;   /* --routing-trace FILE */
+static const char *rbt_engine_ep_arg = NULL;        /* --ep N */
+static int rbt_engine_ep = 1;                       /* GPUs the experts are split over */
+static RbtMoe *rbt_engine_ep_ctx[8];
 static RbtMoe *rbt_engine_ctx = NULL;
 static RbtModel *rbt_engine_model = NULL;           /* --offload all: the whole forward() */
 static FILE *rbt_engine_trace = NULL;
@@ -107,6 +116,17 @@ static int rbt_engine_init(Model *m) {
         return 0;
     }
     const Config *c = &m->c;
+    if (rbt_engine_ep_arg) {
+        rbt_engine_ep = atoi(rbt_engine_ep_arg);
+        if (rbt_engine_ep < 1 || rbt_engine_ep > 8 || c->n_experts % rbt_engine_ep != 0) {
+            fprintf(stderr, "--ep must be 1..8 and divide n_experts (%d)\n", c->n_experts);
+            return 0;
+        }
+        if (rbt_engine_ep > 1 && rbt_engine_offload && !strcmp(rbt_engine_offload, "all")) {
+            fprintf(stderr, "--ep splits the MoE offload's experts; it does not combine with --offload all\n");
+            return 0;
+        }
+    }
     if (rbt_engine_offload && !strcmp(rbt_engine_offload, "all")) {
         /* every weight and a KV cache of max_seq positions in HBM (the engine
            picks its --ctx later; it never exceeds max_seq) */
@@ -151,6 +171,27 @@ static int rbt_engine_init(Model *m) {
     cfg.norm_topk = c->norm_topk;
     cfg.rms_eps = c->rms_eps;
     cfg.expert_stride = (uint64_t)m->expert_stride;
+    if (rbt_engine_ep > 1) {
+        /* one context per GPU, each holding its slice of every layer's experts; the
+           prompt can reach max_seq tokens in one batched call */
+        const int epr = c->n_experts / rbt_engine_ep;
+        for (int g = 0; g < rbt_engine_ep; g++) {
+            if (!rbt_moe_create(&rbt_engine_ep_ctx[g], &cfg, g) ||
+                !rbt_moe_ep_init(rbt_engine_ep_ctx[g], g, rbt_engine_ep, c->max_seq))
+                return 0;
+            for (int l = 0; l < c->n_layers; l++) {
+                const LayerOff *ly = &m->layers[l];
+                if (!rbt_moe_load_layer(rbt_engine_ep_ctx[g], l, VEC(m, ly->ffn_norm), MAT(m, ly->router),
+                                        m->map.base + ly->experts + (size_t)g * epr * m->expert_stride))
+                    return 0;
+            }
+        }
+        if (!rbt_moe_ep_connect_local(rbt_engine_ep_ctx, rbt_engine_ep)) return 0;
+        rbt_engine_ctx = rbt_engine_ep_ctx[0];
+        fprintf(stderr, "moe device: cuda (librbt_moe, experts split over %d GPUs, %d layers resident)\n",
+                rbt_engine_ep, c->n_layers);
+        return 1;
+    }
     if (!rbt_moe_create(&rbt_engine_ctx, &cfg, 0)) return 0;
     for (int l = 0; l < c->n_layers; l++) {
         const LayerOff *ly = &m->layers[l];
@@ -174,6 +215,8 @@ static int rbt_engine_forward(Model *m, State *s, int token, int pos, int32_t *r
 /* 1: the GPU ran the block; 0: not enabled (run the CPU block); -1: error. */
 static int rbt_engine_moe(Model *m, int layer, float *x, int32_t *routing_row) {
     if (!rbt_engine_ctx) return 0;
+    if (rbt_engine_ep > 1)
+        return rbt_moe_ep_block(rbt_engine_ep_ctx, rbt_engine_ep, layer, x, 1, routing_row, m->c.top_k) ? 1 : -1;
     return rbt_moe_block(rbt_engine_ctx, layer, x, 1, routing_row, m->c.top_k) ? 1 : -1;
 }
 
@@ -263,7 +306,9 @@ static int rbt_engine_prefill(Model *m, State *s, const int *tokens, int nt, int
     int ok = 1;
     for (int l = 0; ok && l < c->n_layers; l++) {
         for (int t = 0; t < nt; t++) rbt_engine_attention(m, s, l, X + (size_t)t * D, t);
-        ok = rbt_moe_block(rbt_engine_ctx, l, X, nt, R + (size_t)l * c->top_k, (int)row);
+        ok = rbt_engine_ep > 1
+                 ? rbt_moe_ep_block(rbt_engine_ep_ctx, rbt_engine_ep, l, X, nt, R + (size_t)l * c->top_k, (int)row)
+                 : rbt_moe_block(rbt_engine_ctx, l, X, nt, R + (size_t)l * c->top_k, (int)row);
     }
     /* final norm and lm_head: every token for --dump, else the last one only */
     for (int t = fl ? 0 : nt - 1; ok && t < nt; t++) {

@@ -224,3 +224,34 @@ def test_routing_trace_and_histogram_gpu(tiny_model_bf16, tmp_path, extra):
     ids, err = gen(CUDA, model, prompt, 8, extra + ["--routing-trace", tr])
     trace = check_trace(tr, wr.reshape(-1, cfg.n_layers, cfg.top_k), err, cfg, len(prompt) + 7)
     assert trace.shape[0] == len(prompt) + 7
+
+
+@needs_bins
+def test_bad_ep_is_rejected(tiny_model):
+    """--ep must divide the experts (8 here); checked before any GPU work."""
+    model, _, prompt = tiny_model
+    p = subprocess.run([CUDA, model, "--gen", "1", "--device", "cuda", "--ep", "3", "1"], capture_output=True,
+                       text=True)
+    assert p.returncode == 1 and "--ep" in p.stderr
+
+
+@needs_bins
+@pytest.mark.gpu
+@pytest.mark.parametrize("which", ["f32", "bf16"])
+def test_gpu_expert_parallel_engine_matches_reference(tiny_model, tiny_model_bf16, tmp_path, which):
+    """--ep 2: the experts split over two GPUs driven by the one engine process
+    (rbt_moe_ep_block per MoE block, the batched prompt included); same bars."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    model, cfg, prompt = tiny_model if which == "f32" else tiny_model_bf16
+    extra = ["--device", "cuda", "--ep", "2"]
+    want_ids, _ = gen(REF, model, prompt, 64)
+    got_ids, log = gen(CUDA, model, prompt, 64, extra)
+    assert "experts split over 2 GPUs" in log
+    assert got_ids == want_ids
+    wl, wr, _ = dump(REF, model, prompt, str(tmp_path))
+    gl, gr, _ = dump(CUDA, model, prompt, str(tmp_path), extra)
+    np.testing.assert_array_equal(gr, wr)
+    err = np.abs(gl.astype(np.float64) - wl).max() / np.abs(wl).max()
+    assert err < 1e-3, err
