@@ -63,15 +63,18 @@ def parse():
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="moe", choices=["moe", "model-decode", "model-prefill"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "model-decode", "model-prefill", "model-batch"],
                     help="moe: the MoE stack (the metric's config); model-decode: the whole forward() of an "
                          "OLMoE-1B-7B-shaped model, batch-1 greedy decode (config 3); model-prefill: the same "
-                         "model's prompt of --prompt tokens in one rbt_model_prefill call (config 4, one sequence)")
+                         "model's prompt of --prompt tokens in one rbt_model_prefill call (config 4, one sequence); "
+                         "model-batch: 64 sequences at context 2048 decoded together with the Zipf router "
+                         "bias (config 5; expert-parallel under torchrun)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=256)
     ap.add_argument("--no-extras", action="store_true",
-                    help="N=1 only: skip the other configs' keys of the line (moe_T4096, model_prefill, "
-                         "model_decode with its reference-engine baseline)")
+                    help="skip the other configs' keys of the line (N=1: moe_T4096, model_prefill, "
+                         "model_decode with its reference-engine baseline, model_batch_decode; N>1: "
+                         "model_batch_decode)")
     return ap.parse_args()
 
 
@@ -656,12 +659,15 @@ def run_ours(args, rank, world, local_rank):
 
 # ----------------------------------------------------------------------------- configs 3 and 4
 
-def olmoe_model(args, ctx_len):
+def olmoe_model(args, ctx_len, ep=None, device=0):
     """A random-init OLMoE-1B-7B-shaped model (args.layers layers, vocab 50304, bf16
     weights ~N(0, 0.02) from a seeded GPU generator, norms 1): assembled as the bytes
     of its .rbt2 file in host memory (the engine's own view of the model, which the
     reference engine can run), then uploaded from there into an RbtModel with a KV
-    cache of ctx_len positions.  Returns (cfg, model, image)."""
+    cache of ctx_len positions.  ep = (rank, n_ranks, max_tokens): the model is that
+    rank of an expert-parallel group, and only its experts are written into the
+    image and uploaded (the same draws as the whole model's).  Returns (cfg, model,
+    image)."""
     import torch
 
     from rabbit2_b200 import model as model_mod
@@ -672,12 +678,19 @@ def olmoe_model(args, ctx_len):
     lay = layout(cfg)
     image = torch.empty(-(-lay["total"] // BLOB_ALIGN) * BLOB_ALIGN, dtype=torch.uint8)
     image[:HEADER_BYTES] = torch.frombuffer(bytearray(pack_header(cfg)), dtype=torch.uint8)
-    g = torch.Generator(device="cuda")
+    dev = torch.device("cuda", device)
+    g = torch.Generator(device=dev)
     g.manual_seed(0)
+    e0, n_local = 0, E
+    if ep is not None:
+        n_local = E // ep[1]
+        e0 = ep[0] * n_local
 
-    def put_mat(off, rows, cols):  # drawn on the GPU, copied into the image
-        t = (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-        image[off:off + rows * cols * 2].copy_(t.view(torch.uint8).reshape(-1))
+    def put_mat(off, rows, cols, first=0, n=None):  # drawn on the GPU, rows [first, first+n) into the image
+        n = rows if n is None else n
+        t = (torch.randn(rows, cols, generator=g, device=dev) * 0.02).to(torch.bfloat16)[first:first + n]
+        off += first * cols * 2
+        image[off:off + n * cols * 2].copy_(t.view(torch.uint8).reshape(-1))
 
     def put_ones(off, n):
         image[off:off + 4 * n].view(torch.float32).fill_(1.0)
@@ -693,17 +706,19 @@ def olmoe_model(args, ctx_len):
         put_ones(ly["ffn_norm"], D)
         put_mat(ly["router"], E, D)
         assert lay["expert_stride"] == 3 * H * D * 2
-        put_mat(ly["experts"], E, 3 * H * D)
+        put_mat(ly["experts"], E, 3 * H * D, e0, n_local)
     put_ones(lay["final_norm"], D)
     put_mat(lay["lm_head"], cfg.vocab, D)
-    torch.cuda.synchronize()
-    m = model_mod.ModelContext(cfg, ctx=ctx_len)
+    torch.cuda.synchronize(dev)
+    m = model_mod.ModelContext(cfg, ctx=ctx_len, device=device)
+    if ep is not None:
+        m.moe().ep_init(*ep)
     base = image.data_ptr()
     lib, h = m.lib, m.handle
     m._call(lib.rbt_model_load_globals, h, base + lay["tok_emb"], base + lay["final_norm"], base + lay["lm_head"])
     for l, ly in enumerate(lay["layers"]):
-        m._call(lib.rbt_model_load_layer, h, l, *(base + ly[n] for n in (
-            "attn_norm", "wq", "wk", "wv", "wo", "q_norm", "k_norm", "ffn_norm", "router", "experts")))
+        ptrs = [base + ly[n] for n in ("attn_norm", "wq", "wk", "wv", "wo", "q_norm", "k_norm", "ffn_norm", "router")]
+        m._call(lib.rbt_model_load_layer, h, l, *ptrs, base + ly["experts"] + e0 * lay["expert_stride"])
     return cfg, m, image
 
 
@@ -798,6 +813,94 @@ def run_model_decode(args, built=None):
             "generated_ids_head": ids[:8]}
 
 
+def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, steps=10, warmup=3):
+    """Config 5: batched decode of `seqs` concurrent sequences per GPU at context
+    ctx_len, the router biased by a Zipf(1.2) expert popularity (the same prior on
+    every layer), one rbt_model_decode_batch call per step (one token of every
+    sequence: host tokens and positions in, greedy ids and routing rows out).  Each
+    sequence's KV cache is first filled by rbt_model_prefill_seq with
+    ctx_len - warmup - steps uniform-random tokens, so the timed steps run at
+    positions up to ctx_len - 1.  With N > 1 ranks the model is expert-parallel
+    (rank g holds experts [g*64/N, (g+1)*64/N) and its own `seqs` sequences; every
+    MoE block goes through the group).  value = N * seqs tokens / max-over-ranks
+    wall time per call; the per-expert histogram counts the routed slots of the
+    timed steps (summed over layers and ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from rabbit2_b200 import ep as ep_mod
+    from rabbit2_b200 import workload
+    m_args = argparse.Namespace(**vars(args))
+    m_args.layers = LAYERS
+    prompt_len = ctx_len - warmup - steps
+    epcfg = (rank, world, max(prompt_len, seqs)) if world > 1 else None
+    cfg, m, image = olmoe_model(m_args, ctx_len, ep=epcfg, device=local_rank)
+    del image
+    try:
+        if world > 1:
+            ep_mod.connect(m.moe())
+        bias = workload.zipf_bias(E, 1.2, seed=0)
+        for l in range(cfg.n_layers):
+            m.set_router_bias(l, bias)
+        m.set_sequences(seqs)
+        rng = np.random.default_rng(100 + rank)
+        t0 = time.perf_counter()
+        for i in range(seqs):
+            m.prefill_seq(i, rng.integers(0, cfg.vocab, size=prompt_len), 0, logit_rows=0)
+        t_fill = time.perf_counter() - t0
+        toks = rng.integers(0, cfg.vocab, size=seqs)
+        pos = np.full(seqs, prompt_len, np.int32)
+        for _ in range(warmup):
+            toks, _, _ = m.decode_batch(toks, pos)
+            pos += 1
+        hist = np.zeros((cfg.n_layers, E), np.int64)
+        if world > 1:
+            dist.barrier()
+        with ClockSampler(local_rank) as clocks:
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                toks, _, rt = m.decode_batch(toks, pos)
+                pos += 1
+                for l in range(cfg.n_layers):
+                    hist[l] += np.bincount(rt[:, l].reshape(-1), minlength=E)
+            dt = (time.perf_counter() - t0) / steps
+        if world > 1:
+            t = torch.tensor([dt], device=f"cuda:{local_rank}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+            h = torch.from_numpy(hist).to(f"cuda:{local_rank}")
+            dist.all_reduce(h)
+            hist = h.cpu().numpy()
+    finally:
+        m.close()
+    per_expert = hist.sum(axis=0)
+    hbm, _, src = peaks()
+    nq = nkv = 16 * 128
+    mean_ctx = prompt_len + warmup + (steps + 1) / 2
+    touched = int((hist.sum(axis=0) > 0).sum())
+    per_step = {"attention weights": cfg.n_layers * (nq + 2 * nkv + nq) * D * 2,
+                "kv cache (f32, every sequence)": seqs * cfg.n_layers * mean_ctx * nkv * 4 * 2,
+                "moe weights (experts touched / N)": cfg.n_layers * (E * D * 2 + touched / world * 3 * H * D * 2),
+                "lm_head": cfg.vocab * D * 2}
+    total = sum(per_step.values())
+    return {"metric": "olmoe1b7b_batched_decode_tok_per_s", "value": world * seqs / dt, "unit": "tok/s",
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak",
+            "config": {"workload": "config5_olmoe1b7b_batched_decode_zipf", "sequences_per_gpu": seqs,
+                       "ctx": ctx_len, "positions_timed": [prompt_len + warmup, prompt_len + warmup + steps - 1],
+                       "layers": cfg.n_layers, "routing": "zipf(1.2) router bias, every layer",
+                       "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                       "timing": "wall clock per rbt_model_decode_batch call (host tokens in, greedy ids and "
+                                 "routing rows out), max over ranks",
+                       "l2": "KV caches of 34 GB per GPU >> 126 MB L2"},
+            "kv_fill_s": t_fill, "clocks": clocks.summary(),
+            "roofline": {"bound": "hbm", "achieved": total / dt / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": total / dt / 1e9 / hbm, "peak_source": src, "bytes_per_step_per_gpu": total,
+                         "bytes_parts": per_step, "traffic": None},
+            "expert_histogram": per_expert.tolist(),
+            "expert_imbalance_max_over_mean": float(per_expert.max() / max(per_expert.mean(), 1e-9))}
+
+
 # ----------------------------------------------------------------------------- the other configs, N = 1
 
 def reference_engine_decode(built, prompt_tokens=4, gen=4):
@@ -870,6 +973,9 @@ def run_extras(args):
         out["model_decode"]["cpu_baseline"] = reference_engine_decode(built)
     finally:
         built[1].close()
+    del built
+    torch.cuda.empty_cache()
+    out["model_batch_decode"] = run_model_batch(args)
     return out
 
 
@@ -880,6 +986,9 @@ def main():
         return
     if args.workload == "model-prefill":
         print(json.dumps(run_model_prefill(args)), flush=True)
+        return
+    if args.workload == "model-batch" and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        print(json.dumps(run_model_batch(args, steps=args.steps, warmup=max(3, args.warmup))), flush=True)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -904,6 +1013,9 @@ def main():
             line["cpu_baseline"] = dict(info, value=v, unit=UNIT)
         if world == 1 and not args.no_extras and args.tokens == 1:
             line.update(run_extras(args))
+        if world > 1 and not args.no_extras:
+            torch.cuda.empty_cache()
+            line["model_batch_decode"] = run_model_batch(args, rank, world, local_rank)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

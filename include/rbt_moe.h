@@ -309,6 +309,44 @@ int rbt_model_forward(RbtModel *m, int token, int pos, float *logits, int32_t *r
 int rbt_model_prefill(RbtModel *m, const int32_t *tokens, int n_tokens, int pos0, float *logits, int logit_rows,
                       int32_t *routing_out);
 
+/* ---- several sequences (serving): the reference decodes one sequence per
+ * process (rabbit2.c:716-738); these calls keep n_seq sequences' KV caches on the
+ * GPU and decode one token of each in one call.
+ *
+ * rbt_model_set_sequences: KV caches for n_seq >= 1 sequences (the model starts
+ * with 1), every cache zeroed.  Sequence 0 is the one rbt_model_forward and
+ * rbt_model_prefill use.
+ *
+ * rbt_model_prefill_seq: rbt_model_prefill into the cache of sequence seq.
+ *
+ * rbt_model_decode_batch: forward() for n rows (1 <= n <= n_seq), row i the token
+ * tokens[i] of sequence i at position pos[i] (its cache holds positions
+ * 0..pos[i]-1, filled by earlier calls).  The projections run as GEMMs over the n
+ * rows and the MoE block over all n rows at once; each row's attention reads
+ * only its own sequence's cache.  Outputs (host, each may be NULL): logits
+ * [n, vocab]; next [n], each row's greedy id as the engine's argmax
+ * (rabbit2.c:552-556: the first maximum); routing_out [n, n_layers, top_k].  Row
+ * i's results equal rbt_model_forward's for that token within the GEMMs'
+ * summation order (f32 models) or operand split (bf16 models).
+ *
+ * rbt_model_set_router_bias: rbt_moe_set_router_bias on the model's MoE layers
+ * (a popularity skew for load-imbalance workloads; not in the reference).
+ *
+ * rbt_model_moe: the model's MoE context, for rbt_moe_ep_init / _handle /
+ * _connect / _connect_local / _set_timeout / rbt_moe_status.  Once it is
+ * connected to an expert-parallel group (rbt_moe_ep_init before the layers are
+ * loaded, each layer's `experts` pointing at this rank's first expert), every
+ * MoE block of rbt_model_forward, _prefill* and _decode_batch runs through the
+ * group, and every rank of the group must make the same sequence of calls (the
+ * row counts may differ, up to max_tokens). */
+int rbt_model_set_sequences(RbtModel *m, int n_seq);
+int rbt_model_prefill_seq(RbtModel *m, int seq, const int32_t *tokens, int n_tokens, int pos0, float *logits,
+                          int logit_rows, int32_t *routing_out);
+int rbt_model_decode_batch(RbtModel *m, const int32_t *tokens, const int32_t *pos, int n, float *logits,
+                           int32_t *next, int32_t *routing_out);
+int rbt_model_set_router_bias(RbtModel *m, int layer, const float *bias);
+RbtMoe *rbt_model_moe(RbtModel *m);
+
 /* Last error message of the calling thread ("" if none). */
 const char *rbt_moe_last_error(void);
 

@@ -49,6 +49,8 @@ void set_last_error(const char* msg);
 int moe_status_ok(RbtMoe* m);
 unsigned long long moe_workspace_generation(RbtMoe* m);
 unsigned* moe_status_word(RbtMoe* m);
+int moe_ep_rows(RbtMoe* m);
+int moe_ep_cap(RbtMoe* m);
 }  // namespace rbt
 
 namespace {
@@ -249,13 +251,17 @@ struct AttnArgs {
     unsigned* done;         // [n_heads] finished splits, zero between calls
     unsigned* status;       // error word
     int n_heads, n_kv_heads, hd, ctx, n_splits;
+    // batched decode (gridDim.z rows, one token of its own sequence each): row z reads
+    // step[z], qkv + z*qkv_stride, its sequence's cache at kc/vc + z*kv_stride, and
+    // writes part/done/ao + z*(part_stride, n_heads, ao_stride).  0 for one token.
+    long qkv_stride, kv_stride, part_stride, ao_stride;
 };
 
 // CTA (head h, split s) covers positions [s kSplit, min((s+1) kSplit, pos+1)).
 // The cached positions of the split (all below pos) are one contiguous run per
 // kv head: two bulk copies bring K and V into shared memory, issued before the
 // kernel waits for this token's q|k|v (the cache was written by earlier tokens).
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs args) {
     extern __shared__ __align__(128) float kv_s[];  // K [kSplit][hd] | V [kSplit][hd]
     __shared__ __align__(16) float qh[kMaxHeadDim], kn[kMaxHeadDim], vn[kMaxHeadDim];
     __shared__ float sc[kSplit];
@@ -263,6 +269,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     __shared__ float s_m[kMaxSplits], s_w[kMaxSplits];
     __shared__ unsigned s_last;
     __shared__ uint64_t bar;
+    AttnArgs a = args;  // this row's views (batched decode), the arguments themselves for one token
+    if (blockIdx.z) {
+        const long z = blockIdx.z;
+        a.step += z;
+        a.qkv += z * a.qkv_stride;
+        a.kc += z * a.kv_stride;
+        a.vc += z * a.kv_stride;
+        a.part += z * a.part_stride;
+        a.ao += z * a.ao_stride;
+        a.done += z * a.n_heads;
+    }
     const int h = blockIdx.x, s = blockIdx.y, hd = a.hd;
     const int pos = a.step->pos;  // written by the graph's first copy, before every kernel of the token
     const int t0 = s * kSplit;
@@ -468,6 +485,46 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
 
 size_t attn_smem_bytes(int hd) { return (size_t)2 * kSplit * hd * sizeof(float); }
 
+}  // namespace
+
+namespace rbt {
+// Batched decode attention (model_prefill.cu): rows 0..n-1, each one token of its own
+// sequence, q|k|v rows of nqkv floats, caches kv_stride floats apart per sequence.
+cudaError_t launch_attn_decode_rows(const RbtModel* m, int layer, const Step* steps, const float* qkv, int n,
+                                    float* ao, float* part, unsigned* done, cudaStream_t s) {
+    const RbtModelConfig& c = m->cfg;
+    const int nq = c.n_heads * c.head_dim, nkv = c.n_kv_heads * c.head_dim;
+    AttnArgs a{};
+    a.qkv = qkv;
+    a.q_norm = c.qk_norm ? m->layers[layer].q_norm : nullptr;
+    a.k_norm = c.qk_norm ? m->layers[layer].k_norm : nullptr;
+    a.eps = c.rms_eps;
+    a.scale = 1.0f / sqrtf((float)c.head_dim);
+    a.rope_cos = m->rope_cos;
+    a.rope_sin = m->rope_sin;
+    a.kc = m->kc + (size_t)layer * m->ctx * nkv;
+    a.vc = m->vc + (size_t)layer * m->ctx * nkv;
+    a.step = steps;
+    a.part = part;
+    a.ao = ao;
+    a.done = done;
+    a.status = m->status;
+    a.ctx = m->ctx;
+    a.n_heads = c.n_heads;
+    a.n_kv_heads = c.n_kv_heads;
+    a.hd = c.head_dim;
+    a.n_splits = m->n_splits;
+    a.qkv_stride = nq + 2 * nkv;
+    a.kv_stride = (long)c.n_layers * m->ctx * nkv;
+    a.part_stride = (long)c.n_heads * m->n_splits * (c.head_dim + 2);
+    a.ao_stride = nq;
+    attn_decode_kernel<<<dim3(c.n_heads, m->n_splits, n), kAttnThreads, attn_smem_bytes(c.head_dim), s>>>(a);
+    return cudaGetLastError();
+}
+}  // namespace rbt
+
+namespace {
+
 // ---------------------------------------------------------------- launches
 // Launch with programmatic stream serialization: each kernel calls
 // griddepcontrol.wait before it reads what the previous one wrote.
@@ -520,7 +577,7 @@ int enqueue_token(RbtModel* m, bool with_logits) {
         CU(launch_pdl(norm_gemv_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)D * 4, s,
                       (const float*)m->x, (const float*)L.attn_norm, c.rms_eps, D, (const WT*)L.wqkv, rows_qkv,
                       m->qkv));
-        AttnArgs a;
+        AttnArgs a{};
         a.qkv = m->qkv;
         a.q_norm = c.qk_norm ? L.q_norm : nullptr;
         a.k_norm = c.qk_norm ? L.k_norm : nullptr;
@@ -544,8 +601,7 @@ int enqueue_token(RbtModel* m, bool with_logits) {
                       attn_smem_bytes(c.head_dim), s, a));
         CU(launch_pdl(out_proj_kernel<WT>, dim3(gemv_grid), dim3(kGemvThreads), (size_t)nq * 4, s, (const float*)m->ao,
                       nq, (const WT*)L.wo, D, m->x));
-        if (!rbt_moe_block_device(m->moe, l, m->x, 1, m->routing + (size_t)l * c.top_k, c.top_k, (void*)s))
-            return 0;
+        if (!rbt::model_moe_block(m, l, m->x, 1, m->routing + (size_t)l * c.top_k, c.top_k, s)) return 0;
     }
     CU(cudaMemcpyAsync(m->h_routing, m->routing, sizeof(int32_t) * c.n_layers * c.top_k, cudaMemcpyDeviceToHost, s));
     CU(cudaMemcpyAsync(m->h_status, m->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
@@ -622,7 +678,68 @@ int init_state(RbtModel* m) {
 
 }  // namespace
 
+namespace rbt {
+int model_moe_block(RbtModel* m, int l, float* x, int T, int32_t* routing, int routing_stride, cudaStream_t s) {
+    if (moe_ep_rows(m->moe)) return rbt_moe_ep_block_device(m->moe, l, x, T, routing, routing_stride, (void*)s);
+    return rbt_moe_block_device(m->moe, l, x, T, routing, routing_stride, (void*)s);
+}
+
+int model_moe_rows(RbtModel* m, int T) {
+    const int ep = moe_ep_rows(m->moe);
+    return ep > T ? ep : T;
+}
+
+int model_moe_fits(RbtModel* m, int T) {
+    const int cap = moe_ep_cap(m->moe);
+    if (cap && T > cap) return fail("%d rows above the expert-parallel group's max_tokens %d", T, cap);
+    return 1;
+}
+
+// The graphs hold device addresses (the KV caches, the MoE workspace, the router
+// bias): changing any of them drops the graphs, which are captured again.
+void model_drop_graphs(RbtModel* m) {
+    for (cudaGraphExec_t& g : m->graph)
+        if (g) {
+            cudaGraphExecDestroy(g);
+            g = nullptr;
+        }
+}
+}  // namespace rbt
+
 extern "C" {
+
+int rbt_model_set_sequences(RbtModel* m, int n_seq) {
+    if (!m) return fail("null model");
+    if (n_seq < 1) return fail("n_seq must be >= 1 (got %d)", n_seq);
+    CU(cudaSetDevice(m->device));
+    CU(cudaStreamSynchronize(m->stream));
+    const RbtModelConfig& c = m->cfg;
+    const size_t kv = (size_t)n_seq * c.n_layers * m->ctx * nkv_of(c) * sizeof(float);
+    model_drop_graphs(m);
+    cudaFree(m->kc);
+    cudaFree(m->vc);
+    m->kc = m->vc = nullptr;
+    m->n_seq = 0;
+    if (!dalloc(&m->kc, kv) || !dalloc(&m->vc, kv)) {
+        cudaFree(m->kc);
+        m->kc = nullptr;
+        return 0;
+    }
+    CU(cudaMemset(m->kc, 0, kv));
+    CU(cudaMemset(m->vc, 0, kv));
+    m->n_seq = n_seq;
+    return 1;
+}
+
+int rbt_model_set_router_bias(RbtModel* m, int layer, const float* bias) {
+    if (!m) return fail("null model");
+    CU(cudaSetDevice(m->device));
+    CU(cudaStreamSynchronize(m->stream));
+    model_drop_graphs(m);
+    return rbt_moe_set_router_bias(m->moe, layer, bias);
+}
+
+RbtMoe* rbt_model_moe(RbtModel* m) { return m ? m->moe : nullptr; }
 
 int rbt_model_create(RbtModel** out, const RbtModelConfig* cfg, int ctx, int device) {
     if (!out || !cfg) return fail("null argument");
@@ -690,12 +807,13 @@ void rbt_model_destroy(RbtModel* m) {
     cudaFree(m->lm_head);
     cudaFree(m->final_norm);
     void* bufs[] = {m->x, m->qkv, m->part, m->ao, m->logits, m->kc, m->vc, m->rope_cos, m->rope_sin, m->routing,
-                    m->done, m->step, m->status};
+                    m->done, m->step, m->status, m->steps, m->dpart, m->ddone, m->dnext};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_step);
     cudaFreeHost(m->h_logits);
     cudaFreeHost(m->h_routing);
     cudaFreeHost(m->h_status);
+    cudaFreeHost(m->h_steps);
     rbt::prefill_free(m);
     if (m->stream) cudaStreamDestroy(m->stream);
     rbt_moe_destroy(m->moe);
@@ -756,11 +874,7 @@ int rbt_model_forward(RbtModel* m, int token, int pos, float* logits, int32_t* r
     // captured (rbt_model_prefill) reallocated it, so capture them again
     const unsigned long long gen = moe_workspace_generation(m->moe);
     if (gen != m->graph_gen) {
-        for (cudaGraphExec_t& g : m->graph)
-            if (g) {
-                CU(cudaGraphExecDestroy(g));
-                g = nullptr;
-            }
+        model_drop_graphs(m);
         m->graph_gen = gen;
     }
     const int with = logits != nullptr;

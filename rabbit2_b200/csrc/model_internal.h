@@ -38,6 +38,17 @@ struct PrefillBufs {
 struct RbtModel;
 namespace rbt {
 void prefill_free(RbtModel* m);  // model_prefill.cu: the batched prompt's buffers and cuBLAS handle
+cudaError_t launch_attn_decode_rows(const RbtModel* m, int layer, const Step* steps, const float* qkv, int n,
+                                    float* ao, float* part, unsigned* done, cudaStream_t s);
+// The MoE block of layer l on T rows of x (device) on stream s: on this GPU, or
+// through the expert-parallel group once the model's MoE context is connected.
+int model_moe_block(RbtModel* m, int l, float* x, int T, int32_t* routing, int routing_stride, cudaStream_t s);
+// The MoE context's rows for a call of T rows (the expert-parallel group's
+// every-rank total when connected), for rbt_moe_reserve.
+int model_moe_rows(RbtModel* m, int T);
+// 0 if T rows fit one call of the model's MoE context, else fails with the message
+int model_moe_fits(RbtModel* m, int T);
+void model_drop_graphs(RbtModel* m);
 }  // namespace rbt
 
 struct RbtModel {
@@ -63,6 +74,7 @@ struct RbtModel {
     // state
     float *x = nullptr, *qkv = nullptr, *part = nullptr, *ao = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    int n_seq = 1;  // KV caches: n_seq sequences, [n_seq][n_layers][n_kv_heads][ctx][head_dim] (sequence 0 first)
     int32_t* routing = nullptr;
     unsigned* done = nullptr;
     unsigned* status = nullptr;  // attention's error word (a bounded wait that ran out)
@@ -75,6 +87,13 @@ struct RbtModel {
     // batched prompt (model_prefill.cu): cuBLAS handle and row buffers, grown on demand
     cublasHandle_t blas = nullptr;
     rbt::PrefillBufs pf;
+    // batched decode (rbt_model_decode_batch), one token per sequence, for dcap rows
+    int dcap = 0;
+    rbt::Step* steps = nullptr;    // [dcap] (token, position) of each row
+    float* dpart = nullptr;        // [dcap][n_heads][n_splits][head_dim + 2] attention split partials
+    unsigned* ddone = nullptr;     // [dcap][n_heads] finished splits, zero between calls
+    int32_t* dnext = nullptr;      // [dcap] greedy ids
+    rbt::Step* h_steps = nullptr;  // [dcap] pinned staging of the steps
     // graphs: [0] without lm_head, [1] with
     cudaGraphExec_t graph[2] = {nullptr, nullptr};
     unsigned long long graph_gen = 0;  // the MoE workspace generation the graphs were captured with

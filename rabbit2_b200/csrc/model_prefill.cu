@@ -79,6 +79,63 @@ __global__ void embed_rows_kernel(const WT* emb, int D, const int32_t* tokens, f
     for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)t * D + i] = WeightTraits<WT>::load1(emb + row + i);
 }
 
+// the batched decode's rows: X[i] = tok_emb[steps[i].token]
+template <typename WT>
+__global__ void embed_steps_kernel(const WT* emb, int D, const Step* steps, float* x) {
+    const int t = blockIdx.x;
+    const size_t row = (size_t)steps[t].token * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)t * D + i] = WeightTraits<WT>::load1(emb + row + i);
+}
+
+// Greedy id of each logits row as the engine's argmax (rabbit2.c:552-556): best
+// starts at 0 and moves to i only when v[i] > v[best], so the first of equal
+// maxima wins, NaNs never win, and a NaN at index 0 keeps 0.  Each thread scans
+// its indices in ascending order; the block then reduces (value, index) pairs,
+// the larger value first, the lower index among equals.
+constexpr int kArgmaxThreads = 512;
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const float* logits, int vocab, int32_t* out) {
+    __shared__ float sv[kArgmaxThreads / 32];
+    __shared__ int si[kArgmaxThreads / 32];
+    const float* v = logits + (size_t)blockIdx.x * vocab;
+    float bv = -INFINITY;
+    int bi = -1;  // no candidate yet (every value seen so far was NaN)
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float x = __ldg(v + i);
+        if (x > bv || (bi < 0 && x == bv)) {
+            bv = x;
+            bi = i;
+        }
+    }
+    auto better = [](float av, int ai, float cv, int ci) {  // is (cv, ci) ahead of (av, ai)?
+        if (ci < 0) return false;
+        if (ai < 0) return true;
+        return cv > av || (cv == av && ci < ai);
+    };
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(FULL_MASK, bv, o);
+        const int oi = __shfl_xor_sync(FULL_MASK, bi, o);
+        if (better(bv, bi, ov, oi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kArgmaxThreads / 32; w++)
+            if (better(bv, bi, sv[w], si[w])) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        out[blockIdx.x] = (bi < 0 || isnan(__ldg(v))) ? 0 : bi;
+    }
+}
+
 // Row t of x (n floats, row stride ld_in): rmsnorm with weights w (or none), then
 // either f32 rows (xf) or bf16 hi/lo rows (hi, lo), row stride ld_out.
 // The sum of squares is in a fixed order; (x * inv) * w as rmsnorm() rounds it.
@@ -578,12 +635,38 @@ int reserve(RbtModel* m, int T, int pos0, int logit_rows) {
         CU(cudaMalloc((void**)&b.logits, (size_t)logit_rows * c.vocab * 4));
         b.logit_rows = logit_rows;
     }
-    if (!rbt_moe_reserve(m->moe, T)) return 0;
+    if (!rbt_moe_reserve(m->moe, model_moe_rows(m, T))) return 0;
+    return 1;
+}
+
+// The batched decode's per-row buffers for n rows: steps, attention partials and
+// split counters (zero between calls), greedy ids, pinned staging of the steps.
+int reserve_decode(RbtModel* m, int n) {
+    if (n <= m->dcap) return 1;
+    const RbtModelConfig& c = m->cfg;
+    cudaFree(m->steps);
+    cudaFree(m->dpart);
+    cudaFree(m->ddone);
+    cudaFree(m->dnext);
+    cudaFreeHost(m->h_steps);
+    m->steps = nullptr;
+    m->dpart = nullptr;
+    m->ddone = nullptr;
+    m->dnext = nullptr;
+    m->h_steps = nullptr;
+    m->dcap = 0;
+    CU(cudaMalloc((void**)&m->steps, (size_t)n * sizeof(Step)));
+    CU(cudaMalloc((void**)&m->dpart, (size_t)n * c.n_heads * m->n_splits * (c.head_dim + 2) * 4));
+    CU(cudaMalloc((void**)&m->ddone, (size_t)n * c.n_heads * 4));
+    CU(cudaMalloc((void**)&m->dnext, (size_t)n * 4));
+    CU(cudaMallocHost((void**)&m->h_steps, (size_t)n * sizeof(Step)));
+    CU(cudaMemset(m->ddone, 0, (size_t)n * c.n_heads * 4));
+    m->dcap = n;
     return 1;
 }
 
 template <typename WT>
-int run_prefill(RbtModel* m, int T, int pos0, int logit_rows) {
+int run_prefill(RbtModel* m, int seq, int T, int pos0, int logit_rows) {
     const RbtModelConfig& c = m->cfg;
     const int D = c.dim, nq = nq_of(c), nkv = nkv_of(c), nqkv = nq + 2 * nkv, L = c.n_layers, K = c.top_k;
     const int wide = D > nq ? D : nq;
@@ -596,8 +679,8 @@ int run_prefill(RbtModel* m, int T, int pos0, int logit_rows) {
         const RbtModel::Layer& Ly = m->layers[l];
         if (!split_rows(m, b.x, D, D, T, Ly.attn_norm, wide)) return 0;
         if (!proj(m, Ly.wqkv, nqkv, D, T, wide, b.qkv, nqkv, false)) return 0;
-        float* kc = m->kc + (size_t)l * m->ctx * nkv;
-        float* vc = m->vc + (size_t)l * m->ctx * nkv;
+        float* kc = m->kc + ((size_t)seq * L + l) * m->ctx * nkv;
+        float* vc = m->vc + ((size_t)seq * L + l) * m->ctx * nkv;
         qk_rope_kv_kernel<<<T, kRowThreads, 0, s>>>(b.qkv, nq, nkv, c.head_dim, c.qk_norm ? Ly.q_norm : nullptr,
                                                    c.qk_norm ? Ly.k_norm : nullptr, c.rms_eps, m->rope_cos,
                                                    m->rope_sin, pos0, kc, vc, m->ctx);
@@ -610,13 +693,54 @@ int run_prefill(RbtModel* m, int T, int pos0, int logit_rows) {
         }
         if (!split_rows(m, b.ao, nq, nq, T, nullptr, wide)) return 0;
         if (!proj(m, Ly.wo, D, nq, T, wide, b.x, D, true)) return 0;
-        if (!rbt_moe_block_device(m->moe, l, b.x, T, b.routing + (size_t)l * K, L * K, (void*)s)) return 0;
+        if (!model_moe_block(m, l, b.x, T, b.routing + (size_t)l * K, L * K, s)) return 0;
     }
     if (logit_rows > 0) {
         const float* last = b.x + (size_t)(T - logit_rows) * D;
         if (!split_rows(m, last, D, D, logit_rows, m->final_norm, wide)) return 0;
         if (!proj(m, m->lm_head, c.vocab, D, logit_rows, wide, b.logits, c.vocab, false)) return 0;
     }
+    return 1;
+}
+
+// One decode step of n sequences (rbt_model_decode_batch): row i is the token of
+// sequence i at its own position.  forward() for every row at once: the
+// projections as GEMMs over the n rows (as in the prompt), the attention of each
+// row over its own sequence's cache (the one-token kernel, one grid slice per row),
+// the MoE block over the n rows, and the logits rows.
+template <typename WT>
+int run_decode(RbtModel* m, int n, bool want_logits) {
+    const RbtModelConfig& c = m->cfg;
+    const int D = c.dim, nq = nq_of(c), nkv = nkv_of(c), nqkv = nq + 2 * nkv, L = c.n_layers, K = c.top_k;
+    const int wide = D > nq ? D : nq;
+    cudaStream_t s = m->stream;
+    PrefillBufs& b = m->pf;
+    embed_steps_kernel<WT><<<n, 256, 0, s>>>(static_cast<const WT*>(m->tok_emb), D, m->steps, b.x);
+    CU(cudaGetLastError());
+    for (int l = 0; l < L; l++) {
+        const RbtModel::Layer& Ly = m->layers[l];
+        if (!split_rows(m, b.x, D, D, n, Ly.attn_norm, wide)) return 0;
+        if (!proj(m, Ly.wqkv, nqkv, D, n, wide, b.qkv, nqkv, false)) return 0;
+        CU(launch_attn_decode_rows(m, l, m->steps, b.qkv, n, b.ao, m->dpart, m->ddone, s));
+        if (!split_rows(m, b.ao, nq, nq, n, nullptr, wide)) return 0;
+        if (!proj(m, Ly.wo, D, nq, n, wide, b.x, D, true)) return 0;
+        if (!model_moe_block(m, l, b.x, n, b.routing + (size_t)l * K, L * K, s)) return 0;
+    }
+    if (want_logits) {
+        if (!split_rows(m, b.x, D, D, n, m->final_norm, wide)) return 0;
+        if (!proj(m, m->lm_head, c.vocab, D, n, wide, b.logits, c.vocab, false)) return 0;
+        argmax_rows_kernel<<<n, kArgmaxThreads, 0, s>>>(b.logits, c.vocab, m->dnext);
+        CU(cudaGetLastError());
+    }
+    return 1;
+}
+
+// the checks every whole-prompt or batched call makes before it runs
+int check_ready(RbtModel* m) {
+    const RbtModelConfig& c = m->cfg;
+    if (!m->globals) return fail("globals not loaded (rbt_model_load_globals)");
+    for (int l = 0; l < c.n_layers; l++)
+        if (!m->layers[l].loaded) return fail("layer %d not loaded (rbt_model_load_layer)", l);
     return 1;
 }
 
@@ -635,7 +759,13 @@ void prefill_free(RbtModel* m) {
 
 extern "C" int rbt_model_prefill(RbtModel* m, const int32_t* tokens, int n_tokens, int pos0, float* logits,
                                  int logit_rows, int32_t* routing_out) {
+    return rbt_model_prefill_seq(m, 0, tokens, n_tokens, pos0, logits, logit_rows, routing_out);
+}
+
+extern "C" int rbt_model_prefill_seq(RbtModel* m, int seq, const int32_t* tokens, int n_tokens, int pos0,
+                                     float* logits, int logit_rows, int32_t* routing_out) {
     if (!m) return fail("null model");
+    if (seq < 0 || seq >= m->n_seq) return fail("sequence %d outside the %d KV caches", seq, m->n_seq);
     const RbtModelConfig& c = m->cfg;
     if (n_tokens <= 0 || !tokens) return fail("no tokens");
     if (pos0 < 0 || pos0 + n_tokens > m->ctx)
@@ -645,14 +775,12 @@ extern "C" int rbt_model_prefill(RbtModel* m, const int32_t* tokens, int n_token
     if (c.head_dim != 64 && c.head_dim != 128) return fail("batched prompt needs head_dim 64 or 128");
     for (int t = 0; t < n_tokens; t++)
         if (tokens[t] < 0 || tokens[t] >= c.vocab) return fail("token %d out of range", tokens[t]);
-    if (!m->globals) return fail("globals not loaded (rbt_model_load_globals)");
-    for (int l = 0; l < c.n_layers; l++)
-        if (!m->layers[l].loaded) return fail("layer %d not loaded (rbt_model_load_layer)", l);
+    if (!check_ready(m) || !model_moe_fits(m, n_tokens)) return 0;
     CU(cudaSetDevice(m->device));
     if (!reserve(m, n_tokens, pos0, logit_rows)) return 0;
     CU(cudaMemcpyAsync(m->pf.tokens, tokens, (size_t)n_tokens * 4, cudaMemcpyHostToDevice, m->stream));
-    const int ok = c.dtype == RBT_MOE_DT_BF16 ? run_prefill<uint16_t>(m, n_tokens, pos0, logit_rows)
-                                              : run_prefill<float>(m, n_tokens, pos0, logit_rows);
+    const int ok = c.dtype == RBT_MOE_DT_BF16 ? run_prefill<uint16_t>(m, seq, n_tokens, pos0, logit_rows)
+                                              : run_prefill<float>(m, seq, n_tokens, pos0, logit_rows);
     if (!ok) {
         cudaStreamSynchronize(m->stream);
         return 0;
@@ -663,5 +791,48 @@ extern "C" int rbt_model_prefill(RbtModel* m, const int32_t* tokens, int n_token
         CU(cudaMemcpyAsync(routing_out, m->pf.routing, (size_t)n_tokens * c.n_layers * c.top_k * 4,
                            cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
+    return moe_status_ok(m->moe);
+}
+
+extern "C" int rbt_model_decode_batch(RbtModel* m, const int32_t* tokens, const int32_t* pos, int n, float* logits,
+                                      int32_t* next, int32_t* routing_out) {
+    if (!m) return fail("null model");
+    const RbtModelConfig& c = m->cfg;
+    if (n < 1 || n > m->n_seq) return fail("n %d outside [1, %d] (the sequences of rbt_model_set_sequences)", n,
+                                           m->n_seq);
+    if (!tokens || !pos) return fail("null tokens or positions");
+    for (int i = 0; i < n; i++) {
+        if (tokens[i] < 0 || tokens[i] >= c.vocab) return fail("row %d: token %d out of range", i, tokens[i]);
+        if (pos[i] < 0 || pos[i] >= m->ctx)
+            return fail("row %d: position %d outside the KV cache of %d", i, pos[i], m->ctx);
+    }
+    if (!check_ready(m) || !model_moe_fits(m, n)) return 0;
+    CU(cudaSetDevice(m->device));
+    const bool want = logits || next;
+    if (!reserve(m, n, 0, want ? n : 0) || !reserve_decode(m, n)) return 0;
+    for (int i = 0; i < n; i++) {
+        m->h_steps[i].token = tokens[i];
+        m->h_steps[i].pos = pos[i];
+    }
+    cudaStream_t s = m->stream;
+    CU(cudaMemcpyAsync(m->steps, m->h_steps, (size_t)n * sizeof(Step), cudaMemcpyHostToDevice, s));
+    const int ok = c.dtype == RBT_MOE_DT_BF16 ? run_decode<uint16_t>(m, n, want) : run_decode<float>(m, n, want);
+    if (!ok) {
+        cudaStreamSynchronize(s);
+        return 0;
+    }
+    if (logits) CU(cudaMemcpyAsync(logits, m->pf.logits, (size_t)n * c.vocab * 4, cudaMemcpyDeviceToHost, s));
+    if (next) CU(cudaMemcpyAsync(next, m->dnext, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+    if (routing_out)
+        CU(cudaMemcpyAsync(routing_out, m->pf.routing, (size_t)n * c.n_layers * c.top_k * 4, cudaMemcpyDeviceToHost,
+                           s));
+    CU(cudaMemcpyAsync(m->h_status, m->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+    CU(cudaStreamSynchronize(s));
+    if (*m->h_status) {
+        const unsigned st = *m->h_status;
+        *m->h_status = 0;
+        CU(cudaMemset(m->status, 0, sizeof(unsigned)));
+        return fail("attention: a bounded wait for the KV tiles ran out (code 0x%x)", st);
+    }
     return moe_status_ok(m->moe);
 }

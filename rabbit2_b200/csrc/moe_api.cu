@@ -612,6 +612,12 @@ unsigned long long moe_workspace_generation(RbtMoe* m) { return m ? m->ws_gen : 
 // The device address of the status word (valid until the workspace generation
 // changes), or nullptr before the first reservation.  (Used by model.cu.)
 unsigned* moe_status_word(RbtMoe* m) { return m && m->ws.block ? m->ws.status : nullptr; }
+
+// Rows an expert-parallel context's workspace must hold (every rank's max_tokens)
+// once it is connected, else 0: the whole-forward calls then run each MoE block
+// through the group (ep_block) instead of on this GPU alone.  (Used by model*.cu.)
+int moe_ep_rows(RbtMoe* m) { return m && m->ep.connected ? m->ep.R * m->ep.cap : 0; }
+int moe_ep_cap(RbtMoe* m) { return m && m->ep.connected ? m->ep.cap : 0; }
 }  // namespace rbt
 
 extern "C" {

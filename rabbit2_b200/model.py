@@ -5,7 +5,11 @@ Plumbing for the tests and the benchmark, like moe.py: the product is the C ABI.
 ``ModelContext.from_file`` maps a ``.rbt2`` file and uploads every tensor from
 the offsets the engine's loader computes (rbt2fmt.layout, rabbit2.c:166-193);
 ``forward(token, pos)`` is forward(): the logits [vocab] and the routing rows
-[n_layers, top_k] of the token at position pos.
+[n_layers, top_k] of the token at position pos.  Several sequences:
+``set_sequences(n)``, ``prefill(tokens, seq=i)`` and ``decode_batch(tokens, pos)``
+(one token of each of the first len(tokens) sequences per call).  Expert
+parallelism: ``from_file(..., ep=(rank, n_ranks, max_tokens))`` loads this rank's
+experts only; ``moe()`` is the model's MoE context for the ep_* calls.
 """
 from __future__ import annotations
 
@@ -47,10 +51,18 @@ class ModelContext:
             raise moe.RbtMoeError(self.lib.rbt_moe_last_error().decode())
 
     @classmethod
-    def from_file(cls, path: str, ctx: int, device: int = 0) -> "ModelContext":
+    def from_file(cls, path: str, ctx: int, device: int = 0, ep=None) -> "ModelContext":
+        """ep: (rank, n_ranks, max_tokens) to hold experts [rank*E/n, (rank+1)*E/n)
+        of every layer as that rank of an expert-parallel group (connect it with
+        ep.connect(model.moe()) or moe.ep_connect_local before the first call)."""
         raw = np.memmap(path, dtype=np.uint8, mode="r")
         cfg = unpack_header(bytes(raw[:68]))
         self = cls(cfg, ctx, device)
+        e0 = 0
+        if ep is not None:
+            rank, n_ranks, max_tokens = ep
+            self.moe().ep_init(rank, n_ranks, max_tokens)
+            e0 = rank * (cfg.n_experts // n_ranks)
         base = raw.ctypes.data
         lay = self.lay
         at = lambda off: C.c_void_p(base + off)  # noqa: E731
@@ -61,7 +73,7 @@ class ModelContext:
             kn = at(ly["k_norm"]) if cfg.qk_norm else None
             self._call(self.lib.rbt_model_load_layer, self.handle, l, at(ly["attn_norm"]), at(ly["wq"]),
                        at(ly["wk"]), at(ly["wv"]), at(ly["wo"]), qn, kn, at(ly["ffn_norm"]), at(ly["router"]),
-                       at(ly["experts"]))
+                       at(ly["experts"] + e0 * lay["expert_stride"]))
         del raw
         return self
 
@@ -85,6 +97,45 @@ class ModelContext:
         self._call(self.lib.rbt_model_prefill, self.handle, toks.ctypes.data, len(toks), int(pos0),
                    out.ctypes.data if logit_rows else None, int(logit_rows), routing.ctypes.data)
         return out, routing
+
+    def moe(self) -> "moe.MoeContext":
+        """The model's MoE context (owned by the model)."""
+        c = self.cfg
+        h = self.lib.rbt_model_moe(self.handle)
+        return moe.MoeContext.borrow(h, c.dim, c.n_experts, c.top_k, c.expert_hidden)
+
+    def set_router_bias(self, layer, bias):
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._call(self.lib.rbt_model_set_router_bias, self.handle, int(layer), None if b is None else b.ctypes.data)
+
+    def set_sequences(self, n_seq: int):
+        """KV caches for n_seq sequences, all empty (sequence 0 is forward()'s)."""
+        self._call(self.lib.rbt_model_set_sequences, self.handle, int(n_seq))
+        self.n_seq = int(n_seq)
+
+    def prefill_seq(self, seq: int, tokens, pos0: int = 0, logit_rows: int = 1):
+        """prefill() into the KV cache of sequence seq."""
+        c = self.cfg
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty((logit_rows, c.vocab), np.float32) if logit_rows else None
+        routing = np.empty((len(toks), c.n_layers, c.top_k), np.int32)
+        self._call(self.lib.rbt_model_prefill_seq, self.handle, int(seq), toks.ctypes.data, len(toks), int(pos0),
+                   out.ctypes.data if logit_rows else None, int(logit_rows), routing.ctypes.data)
+        return out, routing
+
+    def decode_batch(self, tokens, pos, logits: bool = False, routing: bool = True):
+        """One token of each of the first n = len(tokens) sequences at positions pos:
+        (greedy ids [n] int32, logits [n, vocab] f32 or None, routing [n, n_layers, top_k] or None)."""
+        c = self.cfg
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        ps = np.ascontiguousarray(pos, dtype=np.int32)
+        n = len(toks)
+        nxt = np.empty(n, np.int32)
+        lg = np.empty((n, c.vocab), np.float32) if logits else None
+        rt = np.empty((n, c.n_layers, c.top_k), np.int32) if routing else None
+        self._call(self.lib.rbt_model_decode_batch, self.handle, toks.ctypes.data, ps.ctypes.data, n,
+                   lg.ctypes.data if logits else None, nxt.ctypes.data, rt.ctypes.data if routing else None)
+        return nxt, lg, rt
 
     def close(self):
         if self.handle:

@@ -78,6 +78,10 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_model_load_layer": [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
         "rbt_model_forward": [vp, i32, i32, vp, vp],
         "rbt_model_prefill": [vp, vp, i32, i32, vp, i32, vp],
+        "rbt_model_set_sequences": [vp, i32],
+        "rbt_model_prefill_seq": [vp, i32, vp, i32, i32, vp, i32, vp],
+        "rbt_model_decode_batch": [vp, vp, vp, i32, vp, vp, vp],
+        "rbt_model_set_router_bias": [vp, i32, vp],
         "rbt_moe_router_logits": [vp, vp, i32],
         "rbt_expf_device": [C.c_uint32, C.c_int64, vp, vp],
         "rbt_seq_sumsq_device": [vp, i32, i32, vp, vp],
@@ -90,6 +94,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.rbt_moe_destroy.restype = None
     lib.rbt_model_destroy.argtypes = [vp]
     lib.rbt_model_destroy.restype = None
+    lib.rbt_model_moe.argtypes = [vp]
+    lib.rbt_model_moe.restype = vp
     lib.rbt_host_expf_variant.argtypes = []
     lib.rbt_host_expf_variant.restype = C.c_int
     lib.rbt_moe_last_error.argtypes = []
@@ -124,13 +130,26 @@ class MoeContext:
         self.D, self.E, self.K, self.H = dim, n_experts, top_k, expert_hidden
         self._keep = {}
 
+    @classmethod
+    def borrow(cls, handle, dim, n_experts, top_k, expert_hidden):
+        """A view of a context owned by someone else (rbt_model_moe): the same
+        methods, and close() leaves the context alone."""
+        self = cls.__new__(cls)
+        self.lib = load_library()
+        self.handle = handle
+        self.D, self.E, self.K, self.H = dim, n_experts, top_k, expert_hidden
+        self._keep = {}
+        self._borrowed = True
+        return self
+
     def _call(self, fn, *args):
         if not fn(*args):
             raise RbtMoeError(self.lib.rbt_moe_last_error().decode() or f"{fn.__name__} failed")
 
     def close(self):
         if getattr(self, "handle", None):
-            self.lib.rbt_moe_destroy(self.handle)
+            if not getattr(self, "_borrowed", False):
+                self.lib.rbt_moe_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -174,3 +174,87 @@ def test_ep_wait_for_a_missing_peer_times_out():
     finally:
         c0.close()
         c1.close()
+
+
+REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "rabbit2")
+
+
+def _ref_gen(path, prompt, n):
+    import subprocess
+    p = subprocess.run([REF, path, "--gen", str(n), "--ctx", "256", *map(str, prompt)], capture_output=True,
+                       text=True)
+    assert p.returncode == 0, p.stderr
+    return [int(t) for t in p.stdout.split()]
+
+
+def _model_worker(rank, world, port, path, prompts, n_rows, q):
+    import torch.distributed as dist
+
+    from rabbit2_b200 import ep
+    from rabbit2_b200.model import ModelContext
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    out = {"rank": rank, "errors": [], "ids": None}
+    m = None
+    try:
+        cap = 160  # the same on every rank: the longest prompt of either
+        m = ModelContext.from_file(path, ctx=256, device=rank, ep=(rank, world, cap))
+        ep.connect(m.moe())
+        m.moe().ep_set_timeout(30_000_000_000)  # generous: the ranks start their calls at different times
+        m.set_sequences(len(prompts))
+        ids = []
+        for i, p in enumerate(prompts):
+            lg, _ = m.prefill_seq(i, p, logit_rows=1)
+            ids.append([int(np.argmax(lg[-1]))])
+        pos = [len(p) for p in prompts]
+        for _ in range(63):
+            nxt, _, _ = m.decode_batch([s[-1] for s in ids[:n_rows]], pos[:n_rows])
+            for i in range(n_rows):
+                ids[i].append(int(nxt[i]))
+                pos[i] += 1
+        out["ids"] = ids[:n_rows]
+    except Exception as exc:  # reported to the parent
+        out["errors"].append(repr(exc))
+    finally:
+        if m is not None:
+            m.close()
+    q.put(out)
+    dist.destroy_process_group()
+
+
+@needs2
+@pytest.mark.skipif(not os.path.exists(REF), reason="oracle/_ref/rabbit2 not built")
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_ep_model_decode_batch_matches_reference_engine(tmp_path, dtype):
+    """The whole model expert-parallel over two processes (one GPU each, 4 of the
+    tiny model's 8 experts each): each rank prefills its own 3 sequences and
+    decodes them with rbt_model_decode_batch (rank 1 decodes only 2 of them, so
+    the ranks send different row counts), every MoE block through the group.
+    Every sequence's 64 greedy ids equal a separate run of the engine's --gen 64."""
+    import dataclasses
+
+    from rabbit2_b200 import workload
+    from rabbit2_b200.rbt2fmt import DT_BF16
+    cfg = workload.tiny_olmoe_config()
+    if dtype == "bf16":
+        cfg = dataclasses.replace(cfg, dtype=DT_BF16)
+    path = str(tmp_path / "m.rbt2")
+    workload.write_model(path, cfg, seed=21)
+    rng = np.random.default_rng(22)
+    prompts = [[rng.integers(0, cfg.vocab, size=n).tolist() for n in lens] for lens in ([50, 128, 9], [77, 31, 140])]
+    n_rows = [3, 2]
+    want = [[_ref_gen(path, p, 64) for p in prompts[r][:n_rows[r]]] for r in range(2)]
+    mp = torch.multiprocessing.get_context("spawn")
+    q = mp.Queue()
+    port = _free_port()
+    procs = [mp.Process(target=_model_worker, args=(r, 2, port, path, prompts[r], n_rows[r], q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=600) for _ in procs), key=lambda r: r["rank"])
+    for p in procs:
+        p.join(timeout=120)
+    for r in res:
+        assert not r["errors"], r
+        assert r["ids"] == want[r["rank"]], r["rank"]

@@ -214,3 +214,97 @@ def test_decode_after_a_longer_prefill_recaptures_its_graph(tmp_path):
     finally:
         a.close()
         b.close()
+
+
+def _prompts(cfg, first, lengths, seed):
+    rng = np.random.default_rng(seed)
+    return [list(first)] + [rng.integers(0, cfg.vocab, size=n).tolist() for n in lengths]
+
+
+@needs_ref
+@pytest.mark.gpu
+def test_decode_batch_matches_reference_engine(model_file, tmp_path):
+    """Four sequences in one model (rbt_model_set_sequences): each prompt prefilled
+    into its own KV cache (rbt_model_prefill_seq), then 63 calls of
+    rbt_model_decode_batch decode one token of every sequence, each at its own
+    position (the prompts have 128, 100, 77 and 140 tokens, so the rows sit in
+    different attention splits).  Each sequence's 64 greedy ids must equal a
+    separate run of the engine's --gen 64 on that prompt; the greedy ids the call
+    returns must be the argmax of the logits it returns."""
+    from rabbit2_b200.model import ModelContext
+    kind, path, cfg, prompt = model_file
+    prompts = _prompts(cfg, prompt, [100, 77, 140], seed=11)
+    want = [_ref_gen(path, p, 64) for p in prompts]
+    m = ModelContext.from_file(path, ctx=256)
+    try:
+        m.set_sequences(len(prompts))
+        ids = []
+        for i, p in enumerate(prompts):
+            lg, _ = m.prefill_seq(i, p, pos0=0, logit_rows=1)
+            ids.append([int(np.argmax(lg[-1]))])
+        pos = [len(p) for p in prompts]
+        for g in range(63):
+            nxt, lg, rt = m.decode_batch([s[-1] for s in ids], pos, logits=(g == 0))
+            if g == 0:
+                np.testing.assert_array_equal(nxt, np.argmax(lg, axis=1))
+                assert rt.shape == (len(prompts), cfg.n_layers, cfg.top_k)
+            for i in range(len(prompts)):
+                ids[i].append(int(nxt[i]))
+                pos[i] += 1
+        for i in range(len(prompts)):
+            assert ids[i] == want[i], (kind, i)
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+def test_decode_batch_row_equals_one_token_forward(tmp_path):
+    """Sequence 0 of a batch against rbt_model_forward on a second context with the
+    same prompt: the logits agree within 1e-3 (GEMM rows against the GEMV), the
+    routing rows of the batch's other sequences do not disturb it."""
+    from rabbit2_b200.model import ModelContext
+    cfg = workload.tiny_olmoe_config()
+    path = str(tmp_path / "m.rbt2")
+    workload.write_model(path, cfg, seed=12)
+    prompts = _prompts(cfg, np.random.default_rng(13).integers(0, cfg.vocab, size=40), [65, 3], seed=14)
+    a = ModelContext.from_file(path, ctx=128)
+    b = ModelContext.from_file(path, ctx=128)
+    try:
+        a.set_sequences(3)
+        for i, p in enumerate(prompts):
+            a.prefill_seq(i, p, logit_rows=0)
+        b.prefill(prompts[0], logit_rows=0)
+        toks = [5, 6, 7]
+        pos = [len(p) for p in prompts]
+        _, lg, _ = a.decode_batch(toks, pos, logits=True)
+        want, _ = b.forward(toks[0], pos[0])
+        err = np.abs(lg[0].astype(np.float64) - want).max() / np.abs(want).max()
+        assert err < LOGIT_RTOL, err
+    finally:
+        a.close()
+        b.close()
+
+
+@pytest.mark.gpu
+def test_decode_batch_rejects_bad_rows(tmp_path):
+    from rabbit2_b200.model import ModelContext
+    cfg = workload.tiny_olmoe_config()
+    path = str(tmp_path / "m.rbt2")
+    workload.write_model(path, cfg, seed=0)
+    m = ModelContext.from_file(path, ctx=16)
+    try:
+        m.set_sequences(2)
+        with pytest.raises(moe.RbtMoeError, match="outside"):
+            m.decode_batch([1, 2, 3], [0, 0, 0])  # 3 rows, 2 sequences
+        with pytest.raises(moe.RbtMoeError, match="token"):
+            m.decode_batch([1, cfg.vocab], [0, 0])
+        with pytest.raises(moe.RbtMoeError, match="position"):
+            m.decode_batch([1, 2], [0, 16])
+        with pytest.raises(moe.RbtMoeError, match="sequence"):
+            m.prefill_seq(2, [1, 2])
+        with pytest.raises(moe.RbtMoeError, match="n_seq"):
+            m.set_sequences(0)
+        nxt, _, _ = m.decode_batch([1, 2], [0, 0])  # and still works
+        assert nxt.shape == (2,)
+    finally:
+        m.close()
