@@ -877,10 +877,11 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
     hbm, _, src = peaks()
     nq = nkv = 16 * 128
     mean_ctx = prompt_len + warmup + (steps + 1) / 2
-    touched = int((hist.sum(axis=0) > 0).sum())
+    touched = float((hist > 0).sum()) / steps  # distinct experts per step, summed over layers (whole job)
     per_step = {"attention weights": cfg.n_layers * (nq + 2 * nkv + nq) * D * 2,
                 "kv cache (f32, every sequence)": seqs * cfg.n_layers * mean_ctx * nkv * 4 * 2,
-                "moe weights (experts touched / N)": cfg.n_layers * (E * D * 2 + touched / world * 3 * H * D * 2),
+                "router weights": cfg.n_layers * E * D * 2,
+                "expert weights (distinct experts of the step / N)": touched / world * 3 * H * D * 2,
                 "lm_head": cfg.vocab * D * 2}
     total = sum(per_step.values())
     return {"metric": "olmoe1b7b_batched_decode_tok_per_s", "value": world * seqs / dt, "unit": "tok/s",

@@ -269,17 +269,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     __shared__ float s_m[kMaxSplits], s_w[kMaxSplits];
     __shared__ unsigned s_last;
     __shared__ uint64_t bar;
-    AttnArgs a = args;  // this row's views (batched decode), the arguments themselves for one token
-    if (blockIdx.z) {
-        const long z = blockIdx.z;
-        a.step += z;
-        a.qkv += z * a.qkv_stride;
-        a.kc += z * a.kv_stride;
-        a.vc += z * a.kv_stride;
-        a.part += z * a.part_stride;
-        a.ao += z * a.ao_stride;
-        a.done += z * a.n_heads;
-    }
+    // this row's views (batched decode; row 0 is the arguments themselves)
+    const long z = blockIdx.z;
+    AttnArgs a = args;
+    a.step = args.step + z;
+    a.qkv = args.qkv + z * args.qkv_stride;
+    a.kc = args.kc + z * args.kv_stride;
+    a.vc = args.vc + z * args.kv_stride;
+    a.part = args.part + z * args.part_stride;
+    a.ao = args.ao + z * args.ao_stride;
+    a.done = args.done + z * args.n_heads;
     const int h = blockIdx.x, s = blockIdx.y, hd = a.hd;
     const int pos = a.step->pos;  // written by the graph's first copy, before every kernel of the token
     const int t0 = s * kSplit;
