@@ -853,7 +853,7 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
         for _ in range(warmup):
             toks, _, _ = m.decode_batch(toks, pos)
             pos += 1
-        hist = np.zeros((cfg.n_layers, E), np.int64)
+        routed = []
         if world > 1:
             dist.barrier()
         with ClockSampler(local_rank) as clocks:
@@ -861,9 +861,16 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
             for _ in range(steps):
                 toks, _, rt = m.decode_batch(toks, pos)
                 pos += 1
-                for l in range(cfg.n_layers):
-                    hist[l] += np.bincount(rt[:, l].reshape(-1), minlength=E)
+                routed.append(rt)
             dt = (time.perf_counter() - t0) / steps
+        # per step and layer: each expert's routed slots (this rank's rows)
+        counts = np.stack([[np.bincount(rt[:, l].reshape(-1), minlength=E) for l in range(cfg.n_layers)]
+                           for rt in routed])
+        hist = counts.sum(axis=0)
+        if world > 1:
+            c = torch.from_numpy(counts).to(f"cuda:{local_rank}")
+            dist.all_reduce(c)
+            counts = c.cpu().numpy()
         if world > 1:
             t = torch.tensor([dt], device=f"cuda:{local_rank}")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -877,7 +884,7 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
     hbm, _, src = peaks()
     nq = nkv = 16 * 128
     mean_ctx = prompt_len + warmup + (steps + 1) / 2
-    touched = float((hist > 0).sum()) / steps  # distinct experts per step, summed over layers (whole job)
+    touched = float((counts > 0).sum()) / steps  # distinct experts of a step, summed over layers (whole job)
     per_step = {"attention weights": cfg.n_layers * (nq + 2 * nkv + nq) * D * 2,
                 "kv cache (f32, every sequence)": seqs * cfg.n_layers * mean_ctx * nkv * 4 * 2,
                 "router weights": cfg.n_layers * E * D * 2,
