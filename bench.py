@@ -839,6 +839,7 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
     try:
         if world > 1:
             ep_mod.connect(m.moe())
+            m.moe().ep_set_timeout(30_000_000_000)  # the ranks' first calls (cuBLAS set-up) start apart
         bias = workload.zipf_bias(E, 1.2, seed=0)
         for l in range(cfg.n_layers):
             m.set_router_bias(l, bias)
