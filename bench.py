@@ -1023,8 +1023,22 @@ def main():
         if world == 1 and not args.no_extras and args.tokens == 1:
             line.update(run_extras(args))
         if world > 1 and not args.no_extras:
+            # config 4's split (4096 tokens per GPU through the expert-parallel stack)
+            # and config 5 (64 sequences per GPU), every rank taking part
+            import copy
             torch.cuda.empty_cache()
-            line["model_batch_decode"] = run_model_batch(args, rank, world, local_rank)
+            a4 = copy.copy(args)
+            a4.tokens, a4.steps, a4.warmup, a4.profile_steps = 4096, 3, 3, 1
+            r4 = run_ep(a4, rank, world, local_rank)
+            torch.cuda.empty_cache()
+            r5 = run_model_batch(args, rank, world, local_rank)
+            if rank == 0:
+                rf = r4["roofline"]
+                line["moe_T4096_ep"] = {k: r4[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
+                                                          "warmup", "config", "clocks", "parity",
+                                                          "ep_status_error")}
+                line["moe_T4096_ep"]["roofline"] = rf
+                line["model_batch_decode"] = r5
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
