@@ -484,6 +484,287 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
 
 size_t attn_smem_bytes(int hd) { return (size_t)2 * kSplit * hd * sizeof(float); }
 
+// ---------------------------------------------------------------- batched decode attention
+// CTA (head h, split s, row z) of the batched decode (rbt_model_decode_batch): row z's
+// attention over positions [s kRSplit, min((s+1) kRSplit, pos+1)) of its own sequence's
+// cache, with an online softmax over chunks of kRChunk positions.  The chunks' K and
+// V runs stream through a kRStages-slot ring of bulk copies, so the copies of later
+// chunks are in flight while a chunk is computed (a 64-position CTA of the one-token
+// kernel copies, then computes).  Splits merge as in the one-token kernel (the last
+// split of a head rescales the others' partials).  Same inputs and outputs as
+// attn_decode_kernel; head_dim a multiple of 32, at most 256.
+constexpr int kRChunk = 32;
+constexpr int kRStages = 2;
+constexpr int kRSplit = 512;
+constexpr int kRThreads = 128;
+static_assert(kRChunk == 32, "a chunk's positions map onto the lanes of a warp");
+constexpr int kRMaxQ = kMaxHeadDim / 32;           // q values per lane
+constexpr int kRMaxV = kMaxHeadDim / kRThreads;    // output dims per thread
+
+size_t attn_rows_smem_bytes(int hd) { return (size_t)kRStages * 2 * kRChunk * hd * sizeof(float); }
+
+__global__ void __launch_bounds__(kRThreads) attn_rows_kernel(const AttnArgs args) {
+    extern __shared__ __align__(128) float ring[];  // [stage][K | V][kRChunk][hd]
+    __shared__ __align__(16) float qh[kMaxHeadDim], kn[kMaxHeadDim], vn[kMaxHeadDim];
+    __shared__ float sc[kRChunk];
+    __shared__ float red[kRThreads / 32], red2[kRThreads / 32];
+    __shared__ float s_m[kMaxSplits], s_w[kMaxSplits];
+    __shared__ unsigned s_last;
+    __shared__ uint64_t full[kRStages];
+    const long z = blockIdx.z;
+    AttnArgs a = args;
+    a.step = args.step + z;
+    a.qkv = args.qkv + z * args.qkv_stride;
+    a.kc = args.kc + z * args.kv_stride;
+    a.vc = args.vc + z * args.kv_stride;
+    a.part = args.part + z * args.part_stride;
+    a.ao = args.ao + z * args.ao_stride;
+    a.done = args.done + z * args.n_heads;
+    const int h = blockIdx.x, s = blockIdx.y, hd = a.hd, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int pos = a.step->pos;
+    const int t0 = s * kRSplit;
+    if (t0 > pos) return;
+    const int t1 = min(t0 + kRSplit, pos + 1);
+    const int nchunks = (t1 - t0 + kRChunk - 1) / kRChunk;
+    const int group = a.n_heads / a.n_kv_heads, kvh = h / group;
+    const size_t stage_floats = (size_t)2 * kRChunk * hd;
+    const float* kbase = a.kc + ((size_t)kvh * a.ctx) * hd;
+    const float* vbase = a.vc + ((size_t)kvh * a.ctx) * hd;
+    // chunk c covers positions [t0 + c kRChunk, ...); its cached part (< pos) is copied
+    auto issue = [&](int c) {
+        const int c0 = t0 + c * kRChunk, c1 = min(c0 + kRChunk, t1), nc = min(c1, pos) - c0;
+        uint64_t* bar = &full[c % kRStages];
+        float* st = ring + (size_t)(c % kRStages) * stage_floats;
+        if (nc > 0) {
+            mbar_arrive_expect_tx(bar, 2u * nc * hd * 4);
+            bulk_load(st, kbase + (size_t)c0 * hd, (uint32_t)nc * hd * 4, bar);
+            bulk_load(st + (size_t)kRChunk * hd, vbase + (size_t)c0 * hd, (uint32_t)nc * hd * 4, bar);
+        } else {
+            mbar_arrive(bar);  // nothing cached in this chunk (it holds only position pos)
+        }
+    };
+    if (tid == 0) {
+        for (int b = 0; b < kRStages; b++) mbar_init(&full[b], 1);
+        fence_mbar_init();
+        for (int c = 0; c < nchunks && c < kRStages; c++) issue(c);
+    }
+    const int nq = a.n_heads * hd, nkv = a.n_kv_heads * hd, half = hd / 2;
+    const bool has_new = pos < t1;  // this split holds position pos: k and v of this token
+    float cs = 0.0f, sn = 0.0f, wqa = 1.0f, wqb = 1.0f, wka = 1.0f, wkb = 1.0f;
+    if (tid < half) {
+        cs = a.rope_cos[(size_t)pos * half + tid];
+        sn = a.rope_sin[(size_t)pos * half + tid];
+        if (a.q_norm) {
+            wqa = a.q_norm[(size_t)h * hd + tid];
+            wqb = a.q_norm[(size_t)h * hd + tid + half];
+            wka = a.k_norm[(size_t)kvh * hd + tid];
+            wkb = a.k_norm[(size_t)kvh * hd + tid + half];
+        }
+    }
+    float qa = 0.0f, qb = 0.0f, ka = 0.0f, kb = 0.0f, va = 0.0f, vb = 0.0f;
+    if (tid < half) {
+        qa = __ldcg(a.qkv + (size_t)h * hd + tid);
+        qb = __ldcg(a.qkv + (size_t)h * hd + tid + half);
+        if (has_new) {
+            ka = __ldcg(a.qkv + nq + (size_t)kvh * hd + tid);
+            kb = __ldcg(a.qkv + nq + (size_t)kvh * hd + tid + half);
+        }
+    }
+    if (has_new) {
+        const float* v = a.qkv + nq + nkv + (size_t)kvh * hd;
+        if (tid < hd) va = __ldcg(v + tid);
+        if (tid + kRThreads < hd) vb = __ldcg(v + tid + kRThreads);
+    }
+    // QK-norm over the whole q and k projections (rabbit2.c:477-480)
+    float inv_q = 1.0f, inv_k = 1.0f;
+    if (a.q_norm) {
+        const int nq4 = nq / 4, n4 = (nq + nkv) / 4;
+        float sq = 0.0f, sk = 0.0f;
+        for (int i4 = tid; i4 < n4; i4 += kRThreads) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.qkv) + i4);
+            float t = fmaf(v.x, v.x, 0.0f);
+            t = fmaf(v.y, v.y, t);
+            t = fmaf(v.z, v.z, t);
+            t = fmaf(v.w, v.w, t);
+            if (i4 < nq4) sq += t;
+            else sk += t;
+        }
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        if (lane == 0) {
+            red[warp] = sq;
+            red2[warp] = sk;
+        }
+        __syncthreads();
+        float tq = 0.0f, tk = 0.0f;
+        for (int w = 0; w < kRThreads / 32; w++) {
+            tq += red[w];
+            tk += red2[w];
+        }
+        inv_q = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tq, (float)nq), a.eps));
+        inv_k = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tk, (float)nkv), a.eps));
+    }
+    // RoPE (rabbit2.c:418-419): p[i] = a cs - b sn, p[i + half] = b cs + a sn
+    if (tid < half) {
+        if (a.q_norm) {
+            qa = __fmul_rn(__fmul_rn(qa, inv_q), wqa);
+            qb = __fmul_rn(__fmul_rn(qb, inv_q), wqb);
+            ka = __fmul_rn(__fmul_rn(ka, inv_k), wka);
+            kb = __fmul_rn(__fmul_rn(kb, inv_k), wkb);
+        }
+        qh[tid] = __fsub_rn(__fmul_rn(qa, cs), __fmul_rn(qb, sn));
+        qh[tid + half] = __fadd_rn(__fmul_rn(qb, cs), __fmul_rn(qa, sn));
+        if (has_new) {
+            kn[tid] = __fsub_rn(__fmul_rn(ka, cs), __fmul_rn(kb, sn));
+            kn[tid + half] = __fadd_rn(__fmul_rn(kb, cs), __fmul_rn(ka, sn));
+        }
+    }
+    if (has_new) {
+        if (tid < hd) vn[tid] = va;
+        if (tid + kRThreads < hd) vn[tid + kRThreads] = vb;
+    }
+    __syncthreads();  // (also publishes the mbarriers' initialisation)
+    if (has_new && h % group == 0) {  // one head of the group stores them (rabbit2.c:484-486)
+        const size_t at = ((size_t)kvh * a.ctx + pos) * hd;
+        for (int i = tid; i < hd; i += kRThreads) {
+            a.kc[at + i] = kn[i];
+            a.vc[at + i] = vn[i];
+        }
+    }
+    const int nqv = hd / 32;  // q values per lane: q[lane + 32 u]
+    float qr[kRMaxQ];
+#pragma unroll
+    for (int u = 0; u < kRMaxQ; u++) qr[u] = u < nqv ? qh[lane + 32 * u] : 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f, o[kRMaxV];
+#pragma unroll
+    for (int v = 0; v < kRMaxV; v++) o[v] = 0.0f;
+    for (int c = 0; c < nchunks; c++) {
+        const int c0 = t0 + c * kRChunk, nv = min(c0 + kRChunk, t1) - c0;
+        float* Ks = ring + (size_t)(c % kRStages) * stage_floats;
+        float* Vs = Ks + (size_t)kRChunk * hd;
+        const bool got = mbar_wait_bounded(&full[c % kRStages], (uint32_t)(c / kRStages) & 1u, kWaitNs);
+        if (!__syncthreads_and(got)) {
+            // the copies are of valid memory and end: wait (bounded) for those in flight
+            if (tid == 0) {
+                record_error(a.status, 0x701);
+                for (int d = c; d < nchunks && d < c + kRStages; d++)
+                    (void)mbar_wait_bounded(&full[d % kRStages], (uint32_t)(d / kRStages) & 1u, kWaitNs);
+            }
+            __syncthreads();
+            return;
+        }
+        if (has_new && pos < c0 + nv) {  // this token's k and v take the row of position pos
+            const int jp = pos - c0;
+            for (int i = tid; i < hd; i += kRThreads) {
+                Ks[(size_t)jp * hd + i] = kn[i];
+                Vs[(size_t)jp * hd + i] = vn[i];
+            }
+            __syncthreads();
+        }
+        // scores (rabbit2.c:488-495): warp w takes positions 8w .. 8w+7 of the chunk
+        {
+            float d[kRChunk / (kRThreads / 32)];
+#pragma unroll
+            for (int i = 0; i < kRChunk / (kRThreads / 32); i++) {
+                const int j = warp * (kRChunk / (kRThreads / 32)) + i;
+                float acc = 0.0f;
+                if (j < nv) {
+                    const float* kr = Ks + (size_t)j * hd + lane;
+#pragma unroll
+                    for (int u = 0; u < kRMaxQ; u++)
+                        if (u < nqv) acc = fmaf(qr[u], kr[32 * u], acc);
+                }
+                d[i] = acc;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int i = 0; i < kRChunk / (kRThreads / 32); i++) d[i] += __shfl_xor_sync(FULL_MASK, d[i], off);
+            if (lane < kRChunk / (kRThreads / 32)) {
+                float mine = d[0];
+#pragma unroll
+                for (int i = 1; i < kRChunk / (kRThreads / 32); i++)
+                    if (lane == i) mine = d[i];
+                const int j = warp * (kRChunk / (kRThreads / 32)) + lane;
+                if (j < nv) sc[j] = mine * a.scale;
+            }
+        }
+        __syncthreads();
+        // online softmax (rabbit2.c:399-405, 496-505), every warp for itself: lane j holds
+        // position j's score, the max and the exp sum by shuffles, the weights stay in lanes
+        const float sj = lane < nv ? sc[lane] : -INFINITY;
+        float cm = sj;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(FULL_MASK, cm, off));
+        const float m_new = fmaxf(m_run, cm);
+        const float alpha = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+        const float pl = lane < nv ? expf(sj - m_new) : 0.0f;
+        l_run = l_run * alpha + warp_sum(pl);
+#pragma unroll
+        for (int v = 0; v < kRMaxV; v++) {
+            const int col = tid + kRThreads * v;
+            float acc = o[v] * alpha;
+            for (int j = 0; j < nv; j++) {
+                const float pjv = __shfl_sync(FULL_MASK, pl, j);
+                if (col < hd) acc = fmaf(pjv, Vs[(size_t)j * hd + col], acc);
+            }
+            o[v] = acc;
+        }
+        m_run = m_new;
+        __syncthreads();  // stage c % kRStages is free again
+        if (tid == 0 && c + kRStages < nchunks) issue(c + kRStages);
+    }
+    if (pos < kRSplit) {  // one split: it is the whole softmax, no merge
+#pragma unroll
+        for (int v = 0; v < kRMaxV; v++) {
+            const int col = tid + kRThreads * v;
+            if (col < hd) a.ao[(size_t)h * hd + col] = o[v] / l_run;
+        }
+        return;
+    }
+    float* pp = a.part + ((size_t)h * a.n_splits + s) * (hd + 2);
+#pragma unroll
+    for (int v = 0; v < kRMaxV; v++) {
+        const int col = tid + kRThreads * v;
+        if (col < hd) pp[2 + col] = o[v];
+    }
+    if (tid == 0) {
+        pp[0] = m_run;
+        pp[1] = l_run;
+    }
+    // the last split of head h to finish merges all of them
+    __threadfence();
+    __syncthreads();
+    const int n_act = pos / kRSplit + 1;
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(a.done + h, 1u);
+        s_last = prev + 1 == (unsigned)n_act;
+        if (s_last) a.done[h] = 0;  // every split of this call has arrived: reset for the next
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* ph = a.part + (size_t)h * a.n_splits * (hd + 2);
+    for (int j = tid; j < n_act; j += kRThreads) {
+        s_m[j] = __ldcg(ph + (size_t)j * (hd + 2));
+        s_w[j] = __ldcg(ph + (size_t)j * (hd + 2) + 1);
+    }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int j = 0; j < n_act; j++) M = fmaxf(M, s_m[j]);
+    float L = 0.0f;
+    for (int j = 0; j < n_act; j++) L += s_w[j] * expf(s_m[j] - M);
+    __syncthreads();
+    for (int j = tid; j < n_act; j += kRThreads) s_w[j] = expf(s_m[j] - M);  // split weights
+    __syncthreads();
+    for (int i = tid; i < hd; i += kRThreads) {
+        float acc = 0.0f;
+        for (int j = 0; j < n_act; j++) acc = fmaf(__ldcg(ph + (size_t)j * (hd + 2) + 2 + i), s_w[j], acc);
+        a.ao[(size_t)h * hd + i] = acc / L;
+    }
+}
+
 }  // namespace
 
 namespace rbt {
@@ -517,6 +798,11 @@ cudaError_t launch_attn_decode_rows(const RbtModel* m, int layer, const Step* st
     a.kv_stride = (long)c.n_layers * m->ctx * nkv;
     a.part_stride = (long)c.n_heads * m->n_splits * (c.head_dim + 2);
     a.ao_stride = nq;
+    if (c.head_dim % 32 == 0) {  // the pipelined kernel: a few CTAs of kRSplit positions per row and head
+        const int splits = (m->ctx + kRSplit - 1) / kRSplit;
+        attn_rows_kernel<<<dim3(c.n_heads, splits, n), kRThreads, attn_rows_smem_bytes(c.head_dim), s>>>(a);
+        return cudaGetLastError();
+    }
     attn_decode_kernel<<<dim3(c.n_heads, m->n_splits, n), kAttnThreads, attn_smem_bytes(c.head_dim), s>>>(a);
     return cudaGetLastError();
 }
@@ -653,6 +939,9 @@ int init_state(RbtModel* m) {
     CU(cudaMemset(m->status, 0, sizeof(unsigned)));
     CU(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)attn_smem_bytes(c.head_dim)));
+    if (c.head_dim % 32 == 0)
+        CU(cudaFuncSetAttribute(attn_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attn_rows_smem_bytes(c.head_dim)));
     CU(cudaMemset(m->kc, 0, kv));
     CU(cudaMemset(m->vc, 0, kv));
     CU(cudaMemset(m->done, 0, (size_t)c.n_heads * 4));
