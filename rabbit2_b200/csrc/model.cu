@@ -495,7 +495,7 @@ size_t attn_smem_bytes(int hd) { return (size_t)2 * kSplit * hd * sizeof(float);
 // attn_decode_kernel; head_dim a multiple of 32, at most 256.
 constexpr int kRChunk = 32;
 constexpr int kRStages = 2;
-constexpr int kRSplit = 512;
+constexpr int kRSplit = 1024;
 constexpr int kRThreads = 128;
 static_assert(kRChunk == 32, "a chunk's positions map onto the lanes of a warp");
 constexpr int kRMaxQ = kMaxHeadDim / 32;           // q values per lane

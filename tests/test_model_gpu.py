@@ -308,3 +308,40 @@ def test_decode_batch_rejects_bad_rows(tmp_path):
         assert nxt.shape == (2,)
     finally:
         m.close()
+
+
+@needs_ref
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_decode_batch_long_context_merges_splits(tmp_path, kind):
+    """Contexts beyond one split of the batched attention (1024 positions): prompts of
+    1100 and 1500 tokens in two sequences, 16 greedy ids each equal to the engine's
+    --gen 16 (the splits' partial softmaxes merged by the last one to finish)."""
+    from rabbit2_b200.model import ModelContext
+    cfg = dataclasses.replace(_cfg(kind), max_seq=2048)
+    path = str(tmp_path / "long.rbt2")
+    workload.write_model(path, cfg, seed=15)
+    rng = np.random.default_rng(16)
+    prompts = [rng.integers(0, cfg.vocab, size=n).tolist() for n in (1100, 1500)]
+    want = []
+    for p in prompts:
+        r = subprocess.run([REF, path, "--gen", "16", "--ctx", "1600", *map(str, p)], capture_output=True,
+                           text=True)
+        assert r.returncode == 0, r.stderr
+        want.append([int(t) for t in r.stdout.split()])
+    m = ModelContext.from_file(path, ctx=1600)
+    try:
+        m.set_sequences(2)
+        ids = []
+        for i, p in enumerate(prompts):
+            lg, _ = m.prefill_seq(i, p, logit_rows=1)
+            ids.append([int(np.argmax(lg[-1]))])
+        pos = [len(p) for p in prompts]
+        for _ in range(15):
+            nxt, _, _ = m.decode_batch([s[-1] for s in ids], pos)
+            for i in range(2):
+                ids[i].append(int(nxt[i]))
+                pos[i] += 1
+        assert ids == want, kind
+    finally:
+        m.close()
