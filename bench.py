@@ -958,6 +958,12 @@ def run_extras(args):
 
     import torch
     out = {}
+    a16 = copy.copy(args)
+    a16.tokens, a16.steps, a16.warmup, a16.profile_steps = 16, 50, 5, 2
+    l16 = run_ours(a16, 0, 1, 0)
+    out["moe_T16"] = {k: l16[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config",
+                                          "clocks", "e2e", "roofline")}
+    torch.cuda.empty_cache()
     a = copy.copy(args)
     a.tokens, a.steps, a.warmup, a.profile_steps = 4096, 5, 3, 2
     line = run_ours(a, 0, 1, 0)
@@ -1030,6 +1036,10 @@ def main():
             # and config 5 (64 sequences per GPU), every rank taking part
             import copy
             torch.cuda.empty_cache()
+            a16 = copy.copy(args)
+            a16.tokens, a16.steps, a16.warmup, a16.profile_steps = 16, 20, 3, 1
+            r16 = run_ep(a16, rank, world, local_rank)
+            torch.cuda.empty_cache()
             a4 = copy.copy(args)
             a4.tokens, a4.steps, a4.warmup, a4.profile_steps = 4096, 3, 3, 1
             r4 = run_ep(a4, rank, world, local_rank)
@@ -1041,6 +1051,9 @@ def main():
                                                           "warmup", "config", "clocks", "parity",
                                                           "ep_status_error")}
                 line["moe_T4096_ep"]["roofline"] = rf
+                line["moe_T16_ep"] = {k: r16[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
+                                                          "warmup", "config", "clocks", "parity", "roofline",
+                                                          "ep_status_error")}
                 line["model_batch_decode"] = r5
         if rank == 0:
             print(json.dumps(line), flush=True)

@@ -345,7 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 atomicExch(lword + (size_t)e * kLogitStride, (1ull << 32) | (unsigned long long)__float_as_uint(logit));
             }
         }
-        __syncthreads();
+        // the products are rewritten by the next row; after the last row nothing waits
+        // here for the publishing warp (its exchange completes while the logits propagate)
+        if (j + 1 < n_rows) __syncthreads();
     }
     if (n_rows == 0) __syncthreads();  // xs complete
     // consumer lanes keep their slices of xb (elements 8v..8v+8, v = lane + 32 j) in
