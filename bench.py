@@ -72,9 +72,9 @@ def parse():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=256)
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the other configs' keys of the line (N=1: moe_T4096, model_prefill, "
+                    help="skip the other configs' keys of the line (N=1: moe_T16, moe_T4096, model_prefill, "
                          "model_decode with its reference-engine baseline, model_batch_decode; N>1: "
-                         "model_batch_decode)")
+                         "moe_T16_ep, moe_T4096_ep, model_batch_decode)")
     return ap.parse_args()
 
 
