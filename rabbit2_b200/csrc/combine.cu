@@ -71,6 +71,58 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* x, const
     for (int i = threadIdx.x; i < D; i += kThreads) o[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
+// The same rmsnorm for many tokens: one warp per 32 rows, lane r running row r's
+// sum of squares as the reference's plain sequential chain (products and sums
+// separately rounded, in index order: the same bits as block_seq_sum), then the
+// warp writes the 32 normalised rows with coalesced stores.  At thousands of
+// tokens the per-row parallel reproduction costs more issue slots than the chains'
+// latency: one dependent add per element, 32 rows per warp, every SM streaming.
+constexpr int kRowsPerWarp = 32;
+constexpr int kRowsMinTokens = 1024;
+
+__global__ void __launch_bounds__(32) rmsnorm_rows_kernel(const float* x, const float* w, float* out, int T, int D,
+                                                          float eps) {
+    const int lane = threadIdx.x, r0 = blockIdx.x * kRowsPerWarp;
+    const int row = r0 + lane;
+    float ss = 0.0f;
+    if (row < T) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
+        const int n4 = D / 4;
+        int i = 0;
+        for (; i + 4 <= n4; i += 4) {  // four 16-byte loads in flight ahead of the adds
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) v[u] = __ldg(xr + i + u);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+            }
+        }
+        for (; i < n4; i++) {
+            const float4 v = __ldg(xr + i);
+            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+        }
+    }
+    const float inv_mine = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+    const int nrows = min(kRowsPerWarp, T - r0);
+    for (int r = 0; r < nrows; r++) {
+        const float inv = __shfl_sync(0xffffffffu, inv_mine, r);
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(r0 + r) * D);
+        float4* o = reinterpret_cast<float4*>(out + (size_t)(r0 + r) * D);
+        for (int i4 = lane; i4 < D / 4; i4 += 32) {
+            const float4 v = __ldg(xr + i4), ww = __ldg(reinterpret_cast<const float4*>(w) + i4);
+            o[i4] = make_float4(__fmul_rn(__fmul_rn(v.x, inv), ww.x), __fmul_rn(__fmul_rn(v.y, inv), ww.y),
+                                __fmul_rn(__fmul_rn(v.z, inv), ww.z), __fmul_rn(__fmul_rn(v.w, inv), ww.w));
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s) {
@@ -87,6 +139,11 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s) {
 
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, int D, float eps, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
+    if (T >= kRowsMinTokens && D % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+        rmsnorm_rows_kernel<<<(T + kRowsPerWarp - 1) / kRowsPerWarp, 32, 0, s>>>(x, w, out, T, D, eps);
+        return cudaGetLastError();
+    }
     const size_t smem = (size_t)D * sizeof(float);
     if (smem > kRmsnormMaxSmem) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {  // the attribute belongs to the current device's context
@@ -104,6 +161,7 @@ void preload_combine_kernels() {
     (void)cudaFuncGetAttributes(&f, combine_vec4_kernel);
     (void)cudaFuncGetAttributes(&f, combine_scalar_kernel);
     (void)cudaFuncGetAttributes(&f, rmsnorm_kernel);
+    (void)cudaFuncGetAttributes(&f, rmsnorm_rows_kernel);
     (void)cudaGetLastError();
 }
 
