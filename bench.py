@@ -771,9 +771,15 @@ def run_model_decode(args, built=None):
     included); prefill_tok_s is the prompt fed token by token."""
     cfg, m, _ = built if built is not None else olmoe_model(args, args.prompt + args.gen)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
-    # warm-up: graph capture and first launches (positions are rewritten below)
-    for p in range(min(3, args.prompt)):
+    # warm-up: graph capture and first launches (positions are rewritten below); the
+    # last warm-up token is the one an ncu run with --profile-from-start off captures
+    import torch
+    nw = min(3, args.prompt)
+    for p in range(nw):
+        if p == nw - 1:
+            torch.cuda.cudart().cudaProfilerStart()
         m.forward(int(prompt[p]), p, logits=True)
+    torch.cuda.cudart().cudaProfilerStop()
     t0 = time.perf_counter()
     for p in range(args.prompt):
         logits, _ = m.forward(int(prompt[p]), p, logits=p == args.prompt - 1)
