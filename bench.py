@@ -819,7 +819,8 @@ def run_model_decode(args, built=None):
             "generated_ids_head": ids[:8]}
 
 
-def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, steps=10, warmup=3):
+def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, steps=10, warmup=3,
+                    prefill_tokens=4096):
     """Config 5: batched decode of `seqs` concurrent sequences per GPU at context
     ctx_len, the router biased by a Zipf(1.2) expert popularity (the same prior on
     every layer), one rbt_model_decode_batch call per step (one token of every
@@ -830,7 +831,10 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
     (rank g holds experts [g*64/N, (g+1)*64/N) and its own `seqs` sequences; every
     MoE block goes through the group).  value = N * seqs tokens / max-over-ranks
     wall time per call; the per-expert histogram counts the routed slots of the
-    timed steps (summed over layers and ranks)."""
+    timed steps (summed over layers and ranks).  Before the caches are filled, the same
+    model (natural routing) times config 4's split: one prompt of `prefill_tokens`
+    tokens per GPU through rbt_model_prefill, every MoE block through the group
+    (the `prefill` key: N * prefill_tokens tokens / max-over-ranks wall time per call)."""
     import torch
     import torch.distributed as dist
 
@@ -839,13 +843,33 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
     m_args = argparse.Namespace(**vars(args))
     m_args.layers = LAYERS
     prompt_len = ctx_len - warmup - steps
-    epcfg = (rank, world, max(prompt_len, seqs)) if world > 1 else None
-    cfg, m, image = olmoe_model(m_args, ctx_len, ep=epcfg, device=local_rank)
+    epcfg = (rank, world, max(prompt_len, seqs, prefill_tokens)) if world > 1 else None
+    cfg, m, image = olmoe_model(m_args, max(ctx_len, prefill_tokens), ep=epcfg, device=local_rank)
     del image
     try:
         if world > 1:
             ep_mod.connect(m.moe())
             m.moe().ep_set_timeout(30_000_000_000)  # the ranks' first calls (cuBLAS set-up) start apart
+        prompt = np.random.default_rng(200 + rank).integers(0, cfg.vocab, size=prefill_tokens)
+        for _ in range(2):
+            m.prefill(prompt, 0, logit_rows=1)
+        if world > 1:
+            dist.barrier()
+        with ClockSampler(local_rank) as p_clocks:
+            t0 = time.perf_counter()
+            for _ in range(3):
+                m.prefill(prompt, 0, logit_rows=1)
+            p_dt = (time.perf_counter() - t0) / 3
+        if world > 1:
+            t = torch.tensor([p_dt], device=f"cuda:{local_rank}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            p_dt = float(t.item())
+        prefill = {"metric": "olmoe1b7b_full_model_prefill_tok_per_s", "value": world * prefill_tokens / p_dt,
+                   "unit": "tok/s", "ms_per_call": p_dt * 1e3, "calls": 3, "warmup": 2,
+                   "config": {"workload": "config4_split_one_prompt_per_gpu", "prompt_per_gpu": prefill_tokens,
+                              "parallelism": f"ep{world}" if world > 1 else "single GPU", "routing": "natural",
+                              "timing": "wall clock per rbt_model_prefill call, max over ranks"},
+                   "clocks": p_clocks.summary()}
         bias = workload.zipf_bias(E, 1.2, seed=0)
         for l in range(cfg.n_layers):
             m.set_router_bias(l, bias)
@@ -911,7 +935,7 @@ def run_model_batch(args, rank=0, world=1, local_rank=0, seqs=64, ctx_len=2048, 
                        "timing": "wall clock per rbt_model_decode_batch call (host tokens in, greedy ids and "
                                  "routing rows out), max over ranks",
                        "l2": "KV caches of 34 GB per GPU >> 126 MB L2"},
-            "kv_fill_s": t_fill, "clocks": clocks.summary(),
+            "kv_fill_s": t_fill, "clocks": clocks.summary(), "prefill": prefill,
             "roofline": {"bound": "hbm", "achieved": total / dt / 1e9, "peak": hbm, "unit": "GB/s",
                          "frac": total / dt / 1e9 / hbm, "peak_source": src, "bytes_per_step_per_gpu": total,
                          "bytes_parts": per_step, "traffic": None},
