@@ -125,8 +125,9 @@ def layout(cfg: ModelConfig) -> dict:
 def f32_to_bf16_bits(a) -> np.ndarray:
     """float32 -> bf16 bit patterns, round to nearest even; NaN -> 0x7FC0."""
     a = np.ascontiguousarray(a, dtype=np.float32)
-    u = a.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    u = a.view(np.uint32)
+    # (the sum wraps only for NaN patterns, which are replaced below)
+    r = ((u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
     r[np.isnan(a)] = 0x7FC0
     return r
 

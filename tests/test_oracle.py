@@ -65,21 +65,24 @@ def test_oracle_bit_exact_vs_reference_c(orc, key):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-def synthetic_layer(D, H, E, K, seed, dtype=1, norm_topk=0, bias=None):
-    """Config-2-style random layer: bf16 weights ~N(0, 0.02), small enough for numpy."""
+def olmoe_shape_layer(orc, xb, seed, bias):
+    """OLMoE-shaped layer (D 2048, H 1024, 64 experts, top-8, bf16 ~N(0, 0.02)) for
+    the tokens xb: the router is drawn in full, and only the experts those tokens
+    route to get drawn weights (each from its own seeded stream); the others are
+    zeros, which no output reads."""
     from rabbit2_b200.rbt2fmt import blob_stride, f32_to_bf16_bits
-    rng = np.random.default_rng(seed)
-    stride = blob_stride(D, H, dtype)
-    router = (0.02 * rng.standard_normal((E, D))).astype(np.float32)
+    D, H, E, K = 2048, 1024, 64, 8
+    stride = blob_stride(D, H, 1)
+    router = f32_to_bf16_bits(0.02 * np.random.default_rng(seed).standard_normal((E, D), dtype=np.float32))
     experts = np.zeros((E, stride), np.uint8)
-    for e in range(E):
-        m = (0.02 * rng.standard_normal(3 * H * D)).astype(np.float32)
-        raw = f32_to_bf16_bits(m).view(np.uint8) if dtype == 1 else m.view(np.uint8)
-        experts[e, :raw.size] = raw
-    if dtype == 1:
-        router = f32_to_bf16_bits(router)
-    return MoeLayerHost(D, H, E, K, dtype, norm_topk, router, experts, stride,
-                        ffn_norm=np.ones(D, np.float32), router_bias=bias)
+    layer = MoeLayerHost(D, H, E, K, 1, 0, router, experts, stride, ffn_norm=np.ones(D, np.float32),
+                         router_bias=bias)
+    idx, _, _ = orc.router_topk(layer, xb)
+    for e in np.unique(idx):
+        m = 0.02 * np.random.default_rng((seed, int(e))).standard_normal(3 * H * D, dtype=np.float32)
+        experts[e, :m.size * 2] = f32_to_bf16_bits(m).view(np.uint8)
+    return MoeLayerHost(D, H, E, K, 1, 0, router, experts, stride, ffn_norm=np.ones(D, np.float32),
+                        router_bias=bias)
 
 
 @needs_ref
@@ -91,8 +94,8 @@ def test_oracle_bit_exact_vs_reference_c_olmoe_shape(orc, bias):
     if bias:  # Zipf(1.2) popularity as an additive log-prior, the skewed workload
         ranks = np.random.default_rng(7).permutation(E) + 1
         b = np.log(ranks.astype(np.float64) ** -1.2 / np.sum(ranks.astype(np.float64) ** -1.2)).astype(np.float32)
-    layer = synthetic_layer(2048, 1024, E, 8, seed=3, bias=b)
     xb = np.random.default_rng(4).standard_normal((3, 2048)).astype(np.float32)
+    layer = olmoe_shape_layer(orc, xb, seed=3, bias=b)
     ref = Reference()
     ref.set_kernel(False)
     a, ra, _ = orc.moe_ffn(layer, xb, nthreads=3)
