@@ -147,9 +147,17 @@ int rbt_moe_ep_block_device(RbtMoe *m, int layer, float *d_x, int n_tokens, int3
 int rbt_moe_ep_block(RbtMoe *const *ms, int n, int layer, float *x, int n_tokens, int32_t *routing_out,
                      int routing_stride);
 
-/* The status word of the context's kernels (0: none failed), cleared after reading;
- * synchronises the device.  Device-pointer calls report their kernels' failures
- * (a bounded wait that ran out) only here. */
+/* Bound, in ns, of the one-token kernel's waits on its other CTAs (the published
+ * router logits, the grid barrier); 0 restores the default of 2 s.  A wait that
+ * runs out ends the call with a status code (0x601 logits, 0x602 barrier): the
+ * host-pointer calls return 0 with the message, the device calls leave the code
+ * for rbt_moe_status, and both clear the kernel's words for the next call.  Waits
+ * on the CTA's own copies keep their own bound (copies of valid memory end). */
+int rbt_moe_set_timeout(RbtMoe *m, uint64_t timeout_ns);
+
+/* The status word of the context's kernels (0: none failed), cleared after reading
+ * (with the one-token kernel's words); synchronises the device.  Device-pointer
+ * calls report their kernels' failures (a bounded wait that ran out) only here. */
 int rbt_moe_status(RbtMoe *m, unsigned *status_out);
 
 /* The router of the layer alone, for n_tokens rows: block != 0 gives d_xb =

@@ -132,22 +132,22 @@ __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long l
     return v;
 }
 
-// Spin (bounded) until *p >= target.
-__device__ __forceinline__ bool wait_count(const unsigned long long* p, unsigned long long target) {
+// Spin (bounded by limit_ns) until *p >= target.
+__device__ __forceinline__ bool wait_count(const unsigned long long* p, unsigned long long target, uint64_t limit_ns) {
     if (ld_acquire64(p) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire64(p) < target)
-        if (globaltimer_ns() - t0 > kWaitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     return true;
 }
 
-// Spin (bounded) until the logit word is published; returns the logit in *v.
-__device__ __forceinline__ bool wait_logit(const unsigned long long* p, float* v) {
+// Spin (bounded by limit_ns) until the logit word is published; returns the logit in *v.
+__device__ __forceinline__ bool wait_logit(const unsigned long long* p, float* v, uint64_t limit_ns) {
     unsigned long long w = ld_acquire64(p);
     if (!(w >> 32)) {
         const uint64_t t0 = globaltimer_ns();
         while (!((w = ld_acquire64(p)) >> 32))
-            if (globaltimer_ns() - t0 > kWaitNs) return false;
+            if (globaltimer_ns() - t0 > limit_ns) return false;
     }
     *v = __uint_as_float((uint32_t)w);
     return true;
@@ -196,6 +196,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const unsigned tl_par = *(volatile unsigned*)&g_timeline_seq & 1u;
 #endif
     unsigned long long* bar_cnt = reinterpret_cast<unsigned long long*>(a.sync + 2);
+    // waits on other CTAs end at this bound; waits on this CTA's own copies (which
+    // always complete) keep kWaitNs, so a short bound never abandons a copy in flight
+    const uint64_t peer_ns = a.peer_wait_ns ? a.peer_wait_ns : kWaitNs;
     unsigned long long* lword = reinterpret_cast<unsigned long long*>(a.sync + kSyncHead);
     float* xs = reinterpret_cast<float*>(ring + kXsOff);
     float* prods = reinterpret_cast<float*>(ring + kProdOff);
@@ -371,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // thread e < E owns expert e
     float lg = -INFINITY;
     bool ok2 = !s_fail;
-    if (ok2 && tid < E) ok2 = wait_logit(lword + (size_t)tid * kLogitStride, &lg);
+    if (ok2 && tid < E) ok2 = wait_logit(lword + (size_t)tid * kLogitStride, &lg, peer_ns);
     if (!__syncthreads_and(ok2)) {
         if (tid == 0) {
             record_error(a.status, 0x601);
@@ -687,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned long long before;
             asm volatile("atom.release.gpu.global.add.u64 %0, [%1], 1;" : "=l"(before) : "l"(bar_cnt) : "memory");
             const unsigned long long target = (before / (unsigned)G + 1) * (unsigned)G;
-            if (before + 1 < target && !wait_count(bar_cnt, target)) {
+            if (before + 1 < target && !wait_count(bar_cnt, target, peer_ns)) {
                 record_error(a.status, 0x602);
                 s_fail = 1;
             }

@@ -136,6 +136,7 @@ struct DecodeArgs {
     unsigned* sync;           // [decode_sync_words(E, K)] cross-CTA counters, zero between calls
     unsigned* status;
     int expf_fma;             // host_expf_fma()
+    unsigned long long peer_wait_ns;  // bound of the waits on other CTAs (logits, grid barrier); 0: 2 s
 };
 int decode_sync_words(int E, int K);
 size_t decode_partials_bytes(int grid, int D);

@@ -135,6 +135,7 @@ struct RbtMoe {
     unsigned long long ws_gen = 0;  // workspace allocations so far
     unsigned* h_status = nullptr;   // pinned host copy of the status word (host-pointer calls)
     int last_routed = 0;            // tokens the most recent routed call computed logits for
+    unsigned long long peer_wait_ns = 0;  // the one-token kernel's bound on waits for other CTAs (0: 2 s)
     EpState ep;
 };
 
@@ -420,7 +421,7 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         da.next_router = aligned(N.router) ? static_cast<const uint8_t*>(N.router) : nullptr;
         da.next_norm = aligned(N.ffn_norm) ? N.ffn_norm : nullptr; da.idx = w.idx; da.counts = w.counts; da.offsets = w.offsets;
         da.perm = w.perm; da.slot_pos = w.slot_pos; da.active = w.active; da.n_active = w.n_active; da.wt = w.wt;
-        da.routing_out = routing; da.sync = w.gbar; da.status = w.status;
+        da.routing_out = routing; da.sync = w.gbar; da.status = w.status; da.peer_wait_ns = m->peer_wait_ns;
         if (!clk.begin(6)) return 0;
         CU(rbt::launch_decode_fused(da, L.w2_cols, m->sm_count, s));
         return clk.end();
@@ -546,7 +547,7 @@ int status_error(RbtMoe* m, unsigned st) {
     if (st) {
         CU(cudaMemset(m->ws.status, 0, 4));
         CU(cudaMemset(m->ws.gbar, 0, (size_t)rbt::decode_sync_words(m->cfg.n_experts, m->cfg.top_k) * 4));
-        return fail("tensor-core GEMM pipeline wait timed out (code 0x%x)", st);
+        return fail("a bounded wait in the kernels timed out (code 0x%x)", st);
     }
     return 1;
 }
@@ -988,6 +989,12 @@ int rbt_moe_ep_connect_local(RbtMoe* const* ms, int n) {
     return 1;
 }
 
+int rbt_moe_set_timeout(RbtMoe* m, uint64_t timeout_ns) {
+    if (!m) return fail("null context");
+    m->peer_wait_ns = timeout_ns;
+    return 1;
+}
+
 int rbt_moe_ep_set_timeout(RbtMoe* m, uint64_t timeout_ns) {
     if (!m) return fail("null context");
     if (timeout_ns < 1000) return fail("timeout below 1 us");
@@ -1042,7 +1049,10 @@ int rbt_moe_status(RbtMoe* m, unsigned* status_out) {
     if (!set_device(m)) return 0;
     CU(cudaDeviceSynchronize());
     CU(cudaMemcpy(status_out, m->ws.status, sizeof(unsigned), cudaMemcpyDeviceToHost));
-    if (*status_out) CU(cudaMemset(m->ws.status, 0, 4));
+    if (*status_out) {  // a failed call may leave the one-token kernel's words half set: clear them too
+        CU(cudaMemset(m->ws.status, 0, 4));
+        CU(cudaMemset(m->ws.gbar, 0, (size_t)rbt::decode_sync_words(m->cfg.n_experts, m->cfg.top_k) * 4));
+    }
     return 1;
 }
 

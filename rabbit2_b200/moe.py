@@ -70,6 +70,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         "rbt_moe_ep_connect": [vp, vp],
         "rbt_moe_ep_connect_local": [vp, i32],
         "rbt_moe_ep_set_timeout": [vp, C.c_uint64],
+        "rbt_moe_set_timeout": [vp, C.c_uint64],
         "rbt_moe_ep_block_device": [vp, i32, vp, i32, vp, i32, vp],
         "rbt_moe_ep_block": [vp, i32, i32, vp, i32, vp, i32],
         "rbt_moe_status": [vp, C.POINTER(C.c_uint)],
@@ -225,6 +226,10 @@ class MoeContext:
         """handles: every rank's ep_handle() bytes, in rank order."""
         blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
         self._call(self.lib.rbt_moe_ep_connect, self.handle, blob)
+
+    def set_timeout(self, ns):
+        """Bound of the one-token kernel's waits on its other CTAs (0: the default 2 s)."""
+        self._call(self.lib.rbt_moe_set_timeout, self.handle, int(ns))
 
     def ep_set_timeout(self, ns):
         self._call(self.lib.rbt_moe_ep_set_timeout, self.handle, int(ns))

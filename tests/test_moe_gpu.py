@@ -507,3 +507,23 @@ def test_decode_layers_in_a_cuda_graph(orc):
         del g
     finally:
         ctx.close()
+
+
+def test_one_token_kernel_wait_bound_reports_and_recovers():
+    """rbt_moe_set_timeout(1 ns): the one-token kernel's waits for the other CTAs'
+    logits and for the grid barrier cannot be met in time, so the host call returns
+    an error with the status code instead of a result (no fault, no hang); with the
+    default bound restored the next call gives the same bits as before."""
+    ctx, host = olmoe_ctx(seed=21)
+    try:
+        x = workload.inputs(1, workload.OLMOE["dim"], seed=22).cpu().numpy()
+        want, want_r = ctx.ffn(0, x)
+        ctx.set_timeout(1)
+        with pytest.raises(moe.RbtMoeError, match="timed out"):
+            ctx.ffn(0, x)
+        ctx.set_timeout(0)
+        got, got_r = ctx.ffn(0, x)
+        np.testing.assert_array_equal(got_r, want_r)
+        np.testing.assert_array_equal(got, want)
+    finally:
+        ctx.close()
