@@ -730,8 +730,13 @@ def run_model_prefill(args, built=None):
     --warmup (each call rewrites the same cache positions)."""
     cfg, m, _ = built if built is not None else olmoe_model(args, args.prompt)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, size=args.prompt)
-    for _ in range(max(1, args.warmup)):
+    import torch
+    nw = max(1, args.warmup)
+    for w in range(nw):
+        if w == nw - 1:  # the last warm-up call is the one an ncu run with --profile-from-start off captures
+            torch.cuda.cudart().cudaProfilerStart()
         m.prefill(prompt, 0, logit_rows=1)
+    torch.cuda.cudart().cudaProfilerStop()
     times = []
     with ClockSampler(0) as clocks:
         for _ in range(args.steps):
