@@ -89,12 +89,12 @@ __global__ void __launch_bounds__(32) rmsnorm_rows_kernel(const float* x, const 
         const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
         const int n4 = D / 4;
         int i = 0;
-        for (; i + 4 <= n4; i += 4) {  // four 16-byte loads in flight ahead of the adds
-            float4 v[4];
+        for (; i + 8 <= n4; i += 8) {  // eight 16-byte loads in flight ahead of the adds
+            float4 v[8];
 #pragma unroll
-            for (int u = 0; u < 4; u++) v[u] = __ldg(xr + i + u);
+            for (int u = 0; u < 8; u++) v[u] = __ldg(xr + i + u);
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < 8; u++) {
                 ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
                 ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
                 ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));

@@ -401,7 +401,6 @@ cudaError_t launch_attn_prefill(int hd, dim3 grid, cudaStream_t s, const float* 
 
 // ---------------------------------------------------------------- attention on the tensor cores (bf16 models)
 // scores = q . k as bf16 hi/lo GEMMs, a causal softmax kernel, O = P . V as GEMMs.
-constexpr int kSmaxThreads = 256;
 
 // K and V of cache positions [0, nk) of every kv head, as bf16: K rows
 // concatenated [hi | lo | hi] into kcat [n_kv][nk][3 hd] (against q's
@@ -451,38 +450,63 @@ __global__ void split_q_kernel(const float* qkv, int nqkv, int H, int hd, uint16
 // least the number of cache positions), one warp per row: att = dot * scale for
 // positions p <= pos0 + t, the softmax of rabbit2.c:399-405 -- p = exp(att - max)
 // / sum -- and P as bf16 hi/lo (0 past the causal limit, the padding included).
-// The max and the sum come from one pass with a running max per lane (rescaling
-// its sum), combined across the warp; a second pass writes P.
+// The row's valid scores are read once into this warp's shared-memory row (the
+// lanes keep their maximum on the way); the exp sum and the P pass then read
+// shared memory.  exp is the hardware's exp2 of a pre-scaled argument and the
+// division a multiply by 1/sum: P is rounded to 16 significant bits (hi + lo) anyway.
+constexpr int kSmaxWarps = 4;
+constexpr int kSmaxThreads = kSmaxWarps * 32;
+size_t causal_softmax_smem(int nk) { return (size_t)kSmaxWarps * nk * sizeof(float); }
+
 __global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const float* S, int T, int nk, int pos0,
                                                                       float scale, int rows, uint16_t* ph,
                                                                       uint16_t* pl) {
-    const int row = blockIdx.x * (kSmaxThreads / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    extern __shared__ __align__(16) float srow_all[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kSmaxWarps + warp;
     if (row >= rows) return;
+    float* srow = srow_all + (size_t)warp * nk;
     const int t = row % T, lim = pos0 + t;  // valid p <= lim
     const float2* sr = reinterpret_cast<const float2*>(S + (size_t)row * nk);
     const int npairs_valid = lim / 2 + 1, npairs = nk / 2;
-    float m = -INFINITY, l = 0.0f;
-    for (int q = lane; q < npairs_valid; q += 32) {
-        const float2 x = sr[q];
-        const float a = x.x * scale;
-        const float b = 2 * q + 1 <= lim ? x.y * scale : -INFINITY;
-        const float mn = fmaxf(m, fmaxf(a, b));
-        l = l * expf(m - mn) + expf(a - mn) + (b == -INFINITY ? 0.0f : expf(b - mn));
-        m = mn;
-    }
-    float M = m;
+    const float k2 = scale * 1.4426950408889634f;  // log2(e) * scale
+    float m = -INFINITY;
+    for (int q0 = lane; q0 < npairs_valid; q0 += 32 * 8) {  // 8 loads of every lane in flight
+        float2 v[8];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL_MASK, M, o));
-    float L = m == -INFINITY ? 0.0f : l * expf(m - M);
-    L = warp_sum(L);
+        for (int u = 0; u < 8; u++) {
+            const int q = q0 + 32 * u;
+            v[u] = q < npairs_valid ? __ldcs(sr + q) : make_float2(-INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int q = q0 + 32 * u;
+            if (q < npairs_valid) {
+                if (2 * q + 1 > lim) v[u].y = -INFINITY;
+                reinterpret_cast<float2*>(srow)[q] = v[u];
+                m = fmaxf(m, fmaxf(v[u].x, v[u].y));
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL_MASK, m, o));
+    const float mk = m * k2;
+    __syncwarp();
+    float l = 0.0f;
+    for (int q = lane; q < npairs_valid; q += 32) {
+        const float2 x = reinterpret_cast<const float2*>(srow)[q];
+        l += exp2f(fmaf(x.x, k2, -mk)) + exp2f(fmaf(x.y, k2, -mk));
+    }
+    l = warp_sum(l);
+    const float inv = 1.0f / l;
     uint32_t* hr = reinterpret_cast<uint32_t*>(ph + (size_t)row * nk);
     uint32_t* lr = reinterpret_cast<uint32_t*>(pl + (size_t)row * nk);
     for (int q = lane; q < npairs; q += 32) {
         float p0 = 0.0f, p1 = 0.0f;
         if (q < npairs_valid) {
-            const float2 x = sr[q];
-            p0 = expf(x.x * scale - M) / L;
-            p1 = 2 * q + 1 <= lim ? expf(x.y * scale - M) / L : 0.0f;
+            const float2 x = reinterpret_cast<const float2*>(srow)[q];
+            p0 = exp2f(fmaf(x.x, k2, -mk)) * inv;
+            p1 = exp2f(fmaf(x.y, k2, -mk)) * inv;  // (0 past the limit: exp2(-inf))
         }
         const __nv_bfloat16 a0 = __float2bfloat16_rn(p0), a1 = __float2bfloat16_rn(p1);
         const __nv_bfloat16 b0 = __float2bfloat16_rn(p0 - __bfloat162float(a0));
@@ -553,7 +577,10 @@ int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) 
                                           3 * hd, 3 * sK, qcat + ((size_t)r0 * H + g) * 3 * hd, CUDA_R_16BF,
                                           H * 3 * hd, (long long)grp * 3 * hd, &zero, S + (size_t)g * tn * ld,
                                           CUDA_R_32F, ld, sS, NKV, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-        causal_softmax_kernel<<<(H * tn + kSmaxThreads / 32 - 1) / (kSmaxThreads / 32), kSmaxThreads, 0, s>>>(
+        if (causal_softmax_smem(ld) > 48 * 1024)
+            CU(cudaFuncSetAttribute(causal_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)causal_softmax_smem(ld)));
+        causal_softmax_kernel<<<(H * tn + kSmaxWarps - 1) / kSmaxWarps, kSmaxThreads, causal_softmax_smem(ld), s>>>(
             S, tn, ld, pos0 + r0, 1.0f / sqrtf((float)hd), H * tn, ph, pl);
         CU(cudaGetLastError());
         for (int g = 0; g < grp; g++) {
