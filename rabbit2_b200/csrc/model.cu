@@ -494,7 +494,7 @@ size_t attn_smem_bytes(int hd) { return (size_t)2 * kSplit * hd * sizeof(float);
 // split of a head rescales the others' partials).  Same inputs and outputs as
 // attn_decode_kernel; head_dim a multiple of 32, at most 256.
 constexpr int kRChunk = 32;
-constexpr int kRStages = 3;
+constexpr int kRStages = 2;
 constexpr int kRSplit = 1024;
 constexpr int kRThreads = 128;
 static_assert(kRChunk == 32, "a chunk's positions map onto the lanes of a warp");
