@@ -108,7 +108,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int n_tiles = *a.n_tb * a.MB;
+    // tile = (K slice, token block, weight block); one K slice except split-K dense calls
+    const int n_blk = a.dense_T ? (a.dense_T + BN - 1) / BN : *a.n_tb;
+    const int n_ks = a.ksplit > 1 ? a.ksplit : 1;
+    const int kb_per = n_ks > 1 ? a.kb_per : a.KB;
+    const int n_tiles = n_blk * a.MB * n_ks;
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ TMA producer
         int stage = 0;
@@ -118,9 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < C::kStages; s++) used[s] = false;
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-            const int tbi = tile / a.MB, mb = tile - tbi * a.MB;
-            const int e = a.tb_e[tbi], p0 = a.tb_p0[tbi];
-            for (int kb = 0; kb < a.KB; kb++) {
+            const int ks = tile / (n_blk * a.MB), rem = tile - ks * n_blk * a.MB;
+            const int tbi = rem / a.MB, mb = rem - tbi * a.MB;
+            const int e = a.dense_T ? 0 : a.tb_e[tbi], p0 = a.dense_T ? tbi * BN : a.tb_p0[tbi];
+            const int kb0 = ks * kb_per, kb1 = min(a.KB, kb0 + kb_per);
+            for (int kb = kb0; kb < kb1; kb++) {
                 if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kWaitNs)) {
                     record_error(a.status, 0x101);
                     ok = false;
@@ -158,7 +164,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t d1 = tmem_base + buf * C::kAccCols;
-            for (int kb = 0; kb < a.KB; kb++) {
+            const int ks = tile / (n_blk * a.MB);
+            const int kb0 = ks * kb_per, kb1 = min(a.KB, kb0 + kb_per);
+            for (int kb = kb0; kb < kb1; kb++) {
                 if (!mbar_wait_bounded(&full[stage], phase, kWaitNs)) {
                     record_error(a.status, 0x202);
                     ok = false;
@@ -172,11 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t koff = kk * 32;  // 16 bf16 = 32 bytes along K
                     const uint64_t bh = sw128_kmajor_desc(sbh + koff), bl = sw128_kmajor_desc(sbl + koff);
                     const uint64_t a1 = sw128_kmajor_desc(sa + koff);
-                    mma_bf16(d1, a1, bh, idesc, (kb | kk) != 0);
+                    const uint32_t acc = (kb != kb0 || kk != 0) ? 1u : 0u;
+                    mma_bf16(d1, a1, bh, idesc, acc);
                     if (!kF16) mma_bf16(d1, a1, bl, idesc, 1u);
                     if (kGateUp) {
                         const uint64_t a3 = sw128_kmajor_desc(sa + kTileBytes + koff);
-                        mma_bf16(d1 + BN, a3, bh, idesc, (kb | kk) != 0);
+                        mma_bf16(d1 + BN, a3, bh, idesc, acc);
                         if (!kF16) mma_bf16(d1 + BN, a3, bl, idesc, 1u);
                     }
                 }
@@ -203,8 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int buf = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-            const int tbi = tile / a.MB, mb = tile - tbi * a.MB;
-            const int p0 = a.tb_p0[tbi], p1 = a.tb_p1[tbi];
+            const int ks = tile / (n_blk * a.MB), rem = tile - ks * n_blk * a.MB;
+            const int tbi = rem / a.MB, mb = rem - tbi * a.MB;
+            const int p0 = a.dense_T ? tbi * BN : a.tb_p0[tbi], p1 = a.dense_T ? a.dense_T : a.tb_p1[tbi];
             const int ntok = min(BN, p1 - p0);
             bool ok = mbar_wait_bounded(&tfull[buf], acc_phase, kWaitNs);
             ok = __all_sync(FULL_MASK, ok);
@@ -242,10 +252,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     tmem_ld_wait();
                     const int col = mb * kBM + row;
+                    const size_t ldy = a.ldy ? (size_t)a.ldy : (size_t)a.D;
+                    if (n_ks > 1) {  // this K slice's partial sums, reduced by dense_reduce_kernel
+                        float* part = a.part + (size_t)ks * a.dense_T * a.D + col;
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj++) {
-                        const int p = p0 + j0 + jj;
-                        if (j0 + jj < ntok) a.y[(size_t)p * a.D + col] = __uint_as_float(g[jj]);
+                        for (int jj = 0; jj < 32; jj++)
+                            if (j0 + jj < ntok) part[(size_t)(p0 + j0 + jj) * a.D] = __uint_as_float(g[jj]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj++) {
+                            const int p = p0 + j0 + jj;
+                            if (j0 + jj < ntok) {
+                                float* dst = a.y + (size_t)p * ldy + col;
+                                *dst = a.accumulate ? *dst + __uint_as_float(g[jj]) : __uint_as_float(g[jj]);
+                            }
+                        }
                     }
                 }
             }
@@ -261,6 +282,226 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- dense, rows as M
+// A dense projection of many rows (T >= 128): the activation rows are the MMA's
+// M side (128 per tile, hi and lo) and the weight rows its N side (256 per tile),
+// D = 128 x 256 f32 in TMEM, two buffers (all 512 columns).  Per K step of 64 the
+// CTA stages 32 KB of rows and 32 KB of weights for two 128x256x64 MMA groups:
+// two thirds of the shared-memory traffic per MMA of the 128-row weight tiles
+// above, whose N = 128 MMAs read as many operand bytes per cycle as the shared
+// memory delivers.
+constexpr int kRM = 128, kRN = 256;
+constexpr int kRATile = kRM * kBK * 2;                  // 16 KB of rows (hi or lo)
+constexpr int kRStageBytes = 2 * kRATile + kRN * kBK * 2;  // 64 KB
+constexpr int kRStages = 3;
+constexpr int kRSmemBytes = kRStages * kRStageBytes + 1024 + 256;
+
+struct RowsGemmArgs {
+    int T, N, KB;
+    float* y;
+    int ldy;
+    int accumulate;
+    unsigned* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    dense_rows_gemm_kernel(const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+                           const __grid_constant__ CUtensorMap tm_w, RowsGemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kRStages * kRStageBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kRStages;
+    uint64_t* tfull = bars + 2 * kRStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    constexpr int kCols = 2 * kRN;  // 512
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4 * 32);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tm_xhi);
+        prefetch_tmap(&tm_xlo);
+        prefetch_tmap(&tm_w);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int NT = a.N / kRN;
+    const int n_tiles = ((a.T + kRM - 1) / kRM) * NT;
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_parity[kRStages];
+        bool used[kRStages];
+        for (int s = 0; s < kRStages; s++) used[s] = false;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+            const int mt = tile / NT, nt = tile - mt * NT;
+            for (int kb = 0; kb < a.KB; kb++) {
+                if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kWaitNs)) {
+                    record_error(a.status, 0x111);
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + stage * kRStageBytes;
+                mbar_arrive_expect_tx(&full[stage], kRStageBytes);
+                tma_load_2d(st, &tm_xhi, &full[stage], kb * kBK, mt * kRM);
+                tma_load_2d(st + kRATile, &tm_xlo, &full[stage], kb * kBK, mt * kRM);
+                tma_load_2d(st + 2 * kRATile, &tm_w, &full[stage], kb * kBK, nt * kRN);
+                used[stage] = true;
+                last_parity[stage] = phase;
+                if (++stage == kRStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        for (int s = 0; s < kRStages; s++)
+            if (used[s] && !mbar_wait_bounded(&full[s], last_parity[s], kWaitNs)) record_error(a.status, 0x112);
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = idesc_bf16_f32(kRM, kRN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int buf = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+            if (!mbar_wait_bounded(&tempty[buf], acc_phase ^ 1u, kWaitNs)) {
+                record_error(a.status, 0x211);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem_base + buf * kRN;
+            for (int kb = 0; kb < a.KB; kb++) {
+                if (!mbar_wait_bounded(&full[stage], phase, kWaitNs)) {
+                    record_error(a.status, 0x212);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sh = smem_u32(smem + stage * kRStageBytes);
+                const uint32_t sl = sh + kRATile, sw = sh + 2 * kRATile;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; kk++) {
+                    const uint32_t koff = kk * 32;
+                    const uint64_t bw = sw128_kmajor_desc(sw + koff);
+                    mma_bf16(d, sw128_kmajor_desc(sh + koff), bw, idesc, (kb | kk) != 0);
+                    mma_bf16(d, sw128_kmajor_desc(sl + koff), bw, idesc, 1u);
+                }
+                mma_commit(&empty[stage]);
+                if (++stage == kRStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            mma_commit(&tfull[buf]);
+            if (++buf == 2) {
+                buf = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        mma_commit(done);
+        if (!mbar_wait_bounded(done, 0, kWaitNs)) record_error(a.status, 0x213);
+    } else if (warp >= 2) {
+        // ------------------------------------------------ epilogue: thread = one activation row
+        const int q = warp & 3;
+        int buf = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int mt = tile / NT, nt = tile - mt * NT;
+            const int t = mt * kRM + q * 32 + lane;
+            bool ok = mbar_wait_bounded(&tfull[buf], acc_phase, kWaitNs);
+            ok = __all_sync(FULL_MASK, ok);
+            if (!ok) {
+                record_error(a.status, 0x311);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * kRN;
+            float* yrow = a.y + (size_t)t * a.ldy + nt * kRN;
+            for (int c0 = 0; c0 < kRN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tbase + c0, v);
+                tmem_ld_wait();
+                if (t < a.T) {
+                    float4* dst = reinterpret_cast<float4*>(yrow + c0);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float4 o = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                        if (a.accumulate) {
+                            const float4 old = dst[i];
+                            o.x += old.x;
+                            o.y += old.y;
+                            o.z += old.z;
+                            o.w += old.w;
+                        }
+                        dst[i] = o;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[buf]);
+            if (++buf == 2) {
+                buf = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kCols);
+    }
+}
+
+// y[t, n] (+)= sum over the K slices s of part[s][t][n], in slice order.
+__global__ void __launch_bounds__(256) dense_reduce_kernel(const float* __restrict__ part, int S, int T, int N,
+                                                           float* y, int ldy, int accumulate) {
+    const int n4 = N / 4;
+    const long total = (long)T * n4;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / n4), c = (int)(i - (long)t * n4) * 4;
+        float4 acc = reinterpret_cast<const float4*>(part + (size_t)t * N + c)[0];
+        for (int s = 1; s < S; s++) {
+            const float4 v = reinterpret_cast<const float4*>(part + ((size_t)s * T + t) * N + c)[0];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        float4* dst = reinterpret_cast<float4*>(y + (size_t)t * ldy + c);
+        if (accumulate) {
+            const float4 old = *dst;
+            acc.x += old.x;
+            acc.y += old.y;
+            acc.z += old.z;
+            acc.w += old.w;
+        }
+        *dst = acc;
     }
 }
 
@@ -451,6 +692,19 @@ bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int bo
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Row-major bf16 matrix [rows, cols] with a row pitch of ld elements, kBK x box_rows box.
+bool make_map_2d_ld(CUtensorMap* map, const void* base, int cols, int ld, long rows, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Per-expert row-major bf16 matrices [rows, cols] `stride` bytes apart as a 3-D
 // map (x = column, y = row, z = expert) with a kBK x kBM x 1 box.
 bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride) {
@@ -525,6 +779,90 @@ cudaError_t launch_tc_down(const CUtensorMap& w, const CUtensorMap& hhi, const C
     return launch_gemm<false>(w, hhi, hlo, a, grid, s);
 }
 
+// Dense projections: many rows (T >= 128, N % 256 == 0) take the rows-as-M
+// kernel; fewer take the down GEMM's one-matrix case (the weight rows as M, the
+// rows as N in blocks of BN consecutive rows, rows past T read as zeros), with K
+// split over up to 8 CTAs per tile when the tiles alone would leave SMs idle.
+struct DensePlan {
+    bool rows;  // rows-as-M kernel
+    int bn, ksplit, kb_per;
+};
+
+static DensePlan dense_plan(int N, int K, int T, int grid) {
+    DensePlan p{false, 32, 1, K / kBK};
+    if (T >= kRM && N % kRN == 0) {
+        p.rows = true;
+        return p;
+    }
+    p.bn = T > 64 ? 128 : T > 32 ? 64 : 32;
+    const int KB = K / kBK, tiles = (N / kBM) * ((T + p.bn - 1) / p.bn);
+    if (2 * tiles <= grid) {
+        int S = grid / tiles < 8 ? grid / tiles : 8;
+        S = S < KB ? S : KB;
+        p.kb_per = (KB + S - 1) / S;
+        p.ksplit = (KB + p.kb_per - 1) / p.kb_per;
+    }
+    return p;
+}
+
+
+size_t tc_dense_part_bytes(int N, int K, int T, int grid) {
+    if (T <= 0 || N % kBM || K % kBK) return 0;
+    const DensePlan p = dense_plan(N, K, T, grid);
+    return p.rows || p.ksplit <= 1 ? 0 : (size_t)p.ksplit * T * N * 4;
+}
+
+cudaError_t launch_tc_dense(const void* W, int N, int K, const void* xhi, const void* xlo, int ld_in, int T,
+                            float* y, int ldy, bool accumulate, unsigned* status, float* part, size_t part_bytes,
+                            int grid, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (N % kBM || K % kBK || ld_in % 8 || ld_in < K || ldy % 4 || ldy < N ||
+        ((uintptr_t)W | (uintptr_t)xhi | (uintptr_t)xlo | (uintptr_t)y) & 15 || !encode_fn())
+        return cudaErrorNotSupported;
+    DensePlan p = dense_plan(N, K, T, grid);
+    if (p.rows) {
+        CUtensorMap mh, ml, mw;
+        if (!make_map_2d_ld(&mh, xhi, K, ld_in, T, kRM) || !make_map_2d_ld(&ml, xlo, K, ld_in, T, kRM) ||
+            !make_map_2d_ld(&mw, W, K, K, N, kRN))
+            return cudaErrorNotSupported;
+        RowsGemmArgs a{T, N, K / kBK, y, ldy, accumulate ? 1 : 0, status};
+        cudaError_t err = cudaFuncSetAttribute(dense_rows_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kRSmemBytes);
+        if (err != cudaSuccess) return err;
+        const int tiles = ((T + kRM - 1) / kRM) * (N / kRN);
+        dense_rows_gemm_kernel<<<tiles < grid ? tiles : grid, kThreads, kRSmemBytes, s>>>(mh, ml, mw, a);
+        return cudaGetLastError();
+    }
+    if (p.ksplit > 1 && (!part || part_bytes < (size_t)p.ksplit * T * N * 4)) p.ksplit = 1;
+    CUtensorMap mw, mh, ml;
+    if (!make_map_experts(&mw, W, K, N, 1, (size_t)N * K * 2) || !make_map_2d_ld(&mh, xhi, K, ld_in, T, p.bn) ||
+        !make_map_2d_ld(&ml, xlo, K, ld_in, T, p.bn))
+        return cudaErrorNotSupported;
+    TcGemmArgs a{};
+    a.BN = p.bn;
+    a.MB = N / kBM;
+    a.KB = K / kBK;
+    a.D = N;
+    a.y = y;
+    a.status = status;
+    a.dense_T = T;
+    a.ldy = ldy;
+    a.accumulate = accumulate ? 1 : 0;
+    if (p.ksplit > 1) {
+        a.ksplit = p.ksplit;
+        a.kb_per = p.kb_per;
+        a.part = part;
+    }
+    const int tiles = a.MB * ((T + p.bn - 1) / p.bn) * (p.ksplit > 1 ? p.ksplit : 1);
+    cudaError_t err = launch_gemm<false>(mw, mh, ml, a, tiles < grid ? tiles : grid, s);
+    if (err != cudaSuccess || p.ksplit <= 1) return err;
+    const long n4 = (long)T * (N / 4);
+    const long blocks = (n4 + 255) / 256;
+    dense_reduce_kernel<<<(int)(blocks < 148L * 4 ? blocks : 148L * 4), 256, 0, s>>>(part, p.ksplit, T, N, y, ldy,
+                                                                                      a.accumulate);
+    return cudaGetLastError();
+}
+
 // Loads every tensor-core path kernel now (see preload_kernels in kernels.h).
 void preload_gemm_kernels() {
     cudaFuncAttributes f;
@@ -540,6 +878,8 @@ void preload_gemm_kernels() {
     (void)cudaFuncGetAttributes(&f, gather_split_kernel);
     (void)cudaFuncGetAttributes(&f, gather_f16_kernel);
     (void)cudaFuncGetAttributes(&f, tc_schedule_kernel);
+    (void)cudaFuncGetAttributes(&f, dense_rows_gemm_kernel);
+    (void)cudaFuncGetAttributes(&f, dense_reduce_kernel);
     (void)cudaGetLastError();
 }
 

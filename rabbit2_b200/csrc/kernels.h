@@ -163,11 +163,31 @@ struct TcGemmArgs {
     float* y;                 // [S_cap, D] f32 (down output)
     unsigned* status;         // 0, or the code of a timed-out pipeline wait
     const float* bscale;      // [S_cap] power-of-two scale of each fp16 activation row (fp16 gate/up only)
+    // dense projections (launch_tc_dense): dense_T > 0 rows, one weight matrix
+    // (expert 0), token blocks of BN consecutive rows, y row pitch ldy, y += when
+    // accumulate; 0 for the MoE GEMMs (schedule from tb_*, y pitch D)
+    int dense_T;
+    int ldy;
+    int accumulate;
+    // split K (dense only): ksplit slices of kb_per K blocks each, slice s's partial
+    // rows into part[s][dense_T][D]; ksplit <= 1 writes y directly
+    int ksplit;
+    int kb_per;
+    float* part;
 };
 int tc_block_n();
 int tc_pick_bn(int T, int K, int E);
 bool tc_supported(int D, int H, int dtype);
 bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int box_rows);
+// out[T, N] (row pitch ldy) (+)= (xhi + xlo)[T, K] (row pitch ld_in) . W[N, K]^T on the
+// tensor cores, W bf16; cudaErrorNotSupported when the shape does not tile
+// (N % 128, K % 64, ld_in % 8) so the caller takes its CUDA-core form
+// part/part_bytes: f32 scratch for split-K partial sums at small T (may be null).
+cudaError_t launch_tc_dense(const void* W, int N, int K, const void* xhi, const void* xlo, int ld_in, int T,
+                            float* y, int ldy, bool accumulate, unsigned* status, float* part, size_t part_bytes,
+                            int grid, cudaStream_t s);
+// the scratch launch_tc_dense uses for T rows of N outputs (0: none)
+size_t tc_dense_part_bytes(int N, int K, int T, int grid);
 bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride);
 // bf16 [E][rows][cols] with row pitch cols*2 and matrix pitch `stride`, unswizzled boxes
 bool make_map_3d_plain(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride, int box_cols,

@@ -87,6 +87,8 @@ struct RbtModel {
     // batched prompt (model_prefill.cu): cuBLAS handle and row buffers, grown on demand
     cublasHandle_t blas = nullptr;
     rbt::PrefillBufs pf;
+    float* proj_part = nullptr;  // split-K partial sums of the small-batch projections
+    size_t proj_part_bytes = 0;
     // batched decode (rbt_model_decode_batch), one token per sequence, for dcap rows
     int dcap = 0;
     rbt::Step* steps = nullptr;    // [dcap] (token, position) of each row

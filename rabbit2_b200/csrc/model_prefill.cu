@@ -30,6 +30,7 @@
 
 #include "../../include/rbt_moe.h"
 #include "common.cuh"
+#include "kernels.h"
 #include "model_internal.h"
 
 namespace rbt {
@@ -517,20 +518,93 @@ __global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const floa
 }
 
 // ---------------------------------------------------------------- GEMMs
-// out[T, N] (row-major, row stride ldc) (+)= rows[T, K] . W[N, K]^T.  bf16 models:
-// two bf16 GEMMs (hi then lo rows) accumulating in f32; f32 models: one SGEMM.
-int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out, int ldc, bool accumulate) {
-    const float one = 1.0f, zero = 0.0f;
-    cublasHandle_t hb = m->blas;
-    if (m->cfg.dtype == RBT_MOE_DT_BF16) {
-        CB(cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, W, CUDA_R_16BF, K, m->pf.hi, CUDA_R_16BF, ld_in,
-                        accumulate ? &one : &zero, out, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-        CB(cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, W, CUDA_R_16BF, K, m->pf.lo, CUDA_R_16BF, ld_in,
-                        &one, out, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-    } else {
-        CB(cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, static_cast<const float*>(W), K, m->pf.xf, ld_in,
-                       accumulate ? &one : &zero, out, ldc));
+// out[T, N] (row pitch ldc) (+)= rows[T, K] . W[N, K]^T on the CUDA cores: f32
+// weights, and bf16 shapes the tensor-core tiles do not cover (N % 128, K % 64).
+// The rows are the f32 rows (f32 models) or hi + lo (bf16 models, the values the
+// tensor-core form multiplies).  Each output is one f32 FMA chain in ascending k.
+constexpr int kPjTile = 64;   // outputs per CTA along N and along T
+constexpr int kPjK = 16;      // K elements per shared-memory stage
+template <typename WT>
+__global__ void __launch_bounds__(256) proj_rows_kernel(const WT* __restrict__ W, int N, int K,
+                                                        const float* __restrict__ xf, const uint16_t* __restrict__ xhi,
+                                                        const uint16_t* __restrict__ xlo, int ld_in, int T,
+                                                        float* out, int ldc, int accumulate) {
+    __shared__ float ws[kPjK][kPjTile + 1];
+    __shared__ float xs[kPjK][kPjTile + 1];
+    const int n0 = blockIdx.x * kPjTile, t0 = blockIdx.y * kPjTile;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // outputs n0 + tx + 16 i, t0 + ty + 16 j
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += kPjK) {
+        for (int i = threadIdx.x; i < kPjK * kPjTile; i += 256) {
+            const int r = i / kPjK, kk = i - r * kPjK, k = k0 + kk;
+            const int n = n0 + r, t = t0 + r;
+            ws[kk][r] = (n < N && k < K) ? WeightTraits<WT>::load1(W + (size_t)n * K + k) : 0.0f;
+            float v = 0.0f;
+            if (t < T && k < K) {
+                const size_t o = (size_t)t * ld_in + k;
+                v = xf ? xf[o] : __uint_as_float((uint32_t)xhi[o] << 16) + __uint_as_float((uint32_t)xlo[o] << 16);
+            }
+            xs[kk][r] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kPjK; kk++) {
+            float wv[4], xv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) wv[i] = ws[kk][tx + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) xv[j] = xs[kk][ty + 16 * j];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[j][i] = fmaf(xv[j], wv[i], acc[j][i]);
+        }
+        __syncthreads();
     }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int t = t0 + ty + 16 * j;
+        if (t >= T) continue;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int n = n0 + tx + 16 * i;
+            if (n >= N) continue;
+            float* o = out + (size_t)t * ldc + n;
+            *o = accumulate ? *o + acc[j][i] : acc[j][i];
+        }
+    }
+}
+
+// out[T, N] (row pitch ldc) (+)= rows[T, K] . W[N, K]^T.  bf16 models: the
+// tensor-core GEMM over the hi and lo rows (two MMAs per K step into one f32
+// accumulator); f32 models and untiled shapes: the CUDA-core kernel above.
+int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out, int ldc, bool accumulate) {
+    if (T <= 0) return 1;
+    cudaStream_t s = m->stream;
+    if (m->cfg.dtype == RBT_MOE_DT_BF16) {
+        const size_t need = tc_dense_part_bytes(N, K, T, m->sm_count);
+        if (need > m->proj_part_bytes) {  // split-K scratch, grown on demand
+            cudaFree(m->proj_part);
+            m->proj_part = nullptr;
+            m->proj_part_bytes = 0;
+            CU(cudaMalloc((void**)&m->proj_part, need));
+            m->proj_part_bytes = need;
+        }
+        const cudaError_t e = launch_tc_dense(W, N, K, m->pf.hi, m->pf.lo, ld_in, T, out, ldc, accumulate, m->status,
+                                              m->proj_part, m->proj_part_bytes, m->sm_count, s);
+        if (e == cudaSuccess) return 1;
+        if (e != cudaErrorNotSupported) return fail("tensor-core projection: %s", cudaGetErrorString(e));
+    }
+    const dim3 grid((N + kPjTile - 1) / kPjTile, (T + kPjTile - 1) / kPjTile);
+    if (m->cfg.dtype == RBT_MOE_DT_BF16)
+        proj_rows_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(W), N, K, nullptr,
+                                                         static_cast<const uint16_t*>(m->pf.hi),
+                                                         static_cast<const uint16_t*>(m->pf.lo), ld_in, T, out, ldc,
+                                                         accumulate);
+    else
+        proj_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(W), N, K, m->pf.xf, nullptr, nullptr,
+                                                      ld_in, T, out, ldc, accumulate);
+    CU(cudaGetLastError());
     return 1;
 }
 
@@ -779,6 +853,9 @@ void prefill_free(RbtModel* m) {
     void* bufs[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing, b.logits, b.att};
     for (void* p : bufs) cudaFree(p);
     b = PrefillBufs{};
+    cudaFree(m->proj_part);
+    m->proj_part = nullptr;
+    m->proj_part_bytes = 0;
     if (m->blas) cublasDestroy(m->blas);
     m->blas = nullptr;
 }
@@ -817,7 +894,14 @@ extern "C" int rbt_model_prefill_seq(RbtModel* m, int seq, const int32_t* tokens
     if (routing_out)
         CU(cudaMemcpyAsync(routing_out, m->pf.routing, (size_t)n_tokens * c.n_layers * c.top_k * 4,
                            cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaMemcpyAsync(m->h_status, m->status, sizeof(unsigned), cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
+    if (*m->h_status) {
+        const unsigned st = *m->h_status;
+        *m->h_status = 0;
+        CU(cudaMemset(m->status, 0, sizeof(unsigned)));
+        return fail("a bounded wait in the projection or attention kernels ran out (code 0x%x)", st);
+    }
     return moe_status_ok(m->moe);
 }
 
@@ -859,7 +943,7 @@ extern "C" int rbt_model_decode_batch(RbtModel* m, const int32_t* tokens, const 
         const unsigned st = *m->h_status;
         *m->h_status = 0;
         CU(cudaMemset(m->status, 0, sizeof(unsigned)));
-        return fail("attention: a bounded wait for the KV tiles ran out (code 0x%x)", st);
+        return fail("a bounded wait in the projection or attention kernels ran out (code 0x%x)", st);
     }
     return moe_status_ok(m->moe);
 }
