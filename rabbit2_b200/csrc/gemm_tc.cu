@@ -705,6 +705,22 @@ bool make_map_2d_ld(CUtensorMap* map, const void* base, int cols, int ld, long r
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                    const uint32_t* box) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || rank < 2 || rank > 3 || box[0] != 64) return false;
+    cuuint64_t d[3], st[2];
+    cuuint32_t b[3], es[3] = {1, 1, 1};
+    for (int i = 0; i < rank; i++) {
+        d[i] = dims[i];
+        b[i] = box[i];
+    }
+    for (int i = 0; i + 1 < rank; i++) st[i] = strides[i];
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st, b, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Per-expert row-major bf16 matrices [rows, cols] `stride` bytes apart as a 3-D
 // map (x = column, y = row, z = expert) with a kBK x kBM x 1 box.
 bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride) {

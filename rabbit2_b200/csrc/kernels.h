@@ -188,6 +188,18 @@ cudaError_t launch_tc_dense(const void* W, int N, int K, const void* xhi, const 
                             int grid, cudaStream_t s);
 // the scratch launch_tc_dense uses for T rows of N outputs (0: none)
 size_t tc_dense_part_bytes(int N, int K, int T, int grid);
+// bf16 tensor map of rank 2 or 3 (dims / byte strides of dims 1.. / box, innermost
+// first) with 128-byte swizzling; the box's inner extent must be 64 elements
+bool make_map_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                    const uint32_t* box);
+// Causal attention of T query rows (positions pos0 .. pos0+T-1; q in the rows of
+// qkv after RoPE) over the f32 KV cache positions [0, pos0 + T) of one layer
+// ([n_kv][ctx][hd]) on the tensor cores (attn_tc.cu), hd 64 or 128, into ao
+// [T][n_heads * hd]; scratch of attn_tc_scratch_bytes, 256-byte aligned.
+size_t attn_tc_scratch_bytes(int T, int nq, int n_kv, int hd, int nk);
+cudaError_t launch_attn_tc(const float* qkv, int nqkv, int n_heads, int n_kv, int hd, const float* kc,
+                           const float* vc, int ctx, int pos0, int T, void* scratch, size_t scratch_bytes, float* ao,
+                           unsigned* status, cudaStream_t s);
 bool make_map_experts(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride);
 // bf16 [E][rows][cols] with row pitch cols*2 and matrix pitch `stride`, unswizzled boxes
 bool make_map_3d_plain(CUtensorMap* map, const void* base, int cols, int rows, int E, size_t stride, int box_cols,
@@ -267,6 +279,7 @@ void preload_gemm_kernels();
 void preload_gemv_kernels();
 void preload_stream_kernels();
 void preload_combine_kernels();
+void preload_attn_tc_kernels();
 void preload_ep_kernels();
 
 }  // namespace rbt

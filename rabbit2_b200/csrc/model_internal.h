@@ -2,7 +2,6 @@
 // and model_prefill.cu (the batched prompt); not part of the C ABI.
 #pragma once
 
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -37,7 +36,7 @@ struct PrefillBufs {
 
 struct RbtModel;
 namespace rbt {
-void prefill_free(RbtModel* m);  // model_prefill.cu: the batched prompt's buffers and cuBLAS handle
+void prefill_free(RbtModel* m);  // model_prefill.cu: the batched prompt's buffers
 cudaError_t launch_attn_decode_rows(const RbtModel* m, int layer, const Step* steps, const float* qkv, int n,
                                     float* ao, float* part, unsigned* done, cudaStream_t s);
 // The MoE block of layer l on T rows of x (device) on stream s: on this GPU, or
@@ -84,8 +83,7 @@ struct RbtModel {
     float* h_logits = nullptr;
     int32_t* h_routing = nullptr;
     unsigned* h_status = nullptr;
-    // batched prompt (model_prefill.cu): cuBLAS handle and row buffers, grown on demand
-    cublasHandle_t blas = nullptr;
+    // batched prompt (model_prefill.cu): row buffers, grown on demand
     rbt::PrefillBufs pf;
     float* proj_part = nullptr;  // split-K partial sums of the small-batch projections
     size_t proj_part_bytes = 0;

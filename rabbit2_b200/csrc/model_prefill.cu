@@ -14,13 +14,13 @@
 //     rbt_moe_block_device X += MoE(rmsnorm(X)), all T rows (tensor cores)  (:511-542)
 //   norm_split + GEMM      logits of the last rows = rmsnorm(X) . lm_head^T (:545-546)
 //
-// The projections are plain dense GEMMs, so they go to cuBLAS.  bf16 weights
-// are exact in bf16; the f32 activation rows are split into bf16 hi = rn(x) and
-// lo = rn(x - hi) (16 significant bits), and each projection is two bf16 GEMMs
-// with f32 accumulation into the same output -- the precision scheme of the MoE
-// tensor-core path.  f32 models use f32 SGEMM.  The KV cache is the one the
-// one-token forward uses, so decode continues from pos0 + T.
-#include <cublas_v2.h>
+// The projections are dense GEMMs on the tensor cores (gemm_tc.cu: launch_tc_dense)
+// and the attention a fused tcgen05 kernel (attn_tc.cu).  bf16 weights are exact
+// in bf16; the f32 activation rows are split into bf16 hi = rn(x) and lo =
+// rn(x - hi) (16 significant bits), and each product is two MMAs (hi and lo) with
+// f32 accumulation into the same output -- the precision scheme of the MoE
+// tensor-core path.  f32 models take CUDA-core forms of both.  The KV cache is
+// the one the one-token forward uses, so decode continues from pos0 + T.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -58,12 +58,6 @@ int fail(const char* fmt, ...) {
         cudaError_t e_ = (call);                                                                  \
         if (e_ != cudaSuccess) return fail("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
                                            __FILE__, __LINE__);                                   \
-    } while (0)
-#define CB(call)                                                                      \
-    do {                                                                              \
-        cublasStatus_t e_ = (call);                                                   \
-        if (e_ != CUBLAS_STATUS_SUCCESS) return fail("%s failed: cuBLAS status %d (%s:%d)", #call, \
-                                                    (int)e_, __FILE__, __LINE__);     \
     } while (0)
 
 constexpr int kRowThreads = 256;
@@ -400,123 +394,6 @@ cudaError_t launch_attn_prefill(int hd, dim3 grid, cudaStream_t s, const float* 
     }
 }
 
-// ---------------------------------------------------------------- attention on the tensor cores (bf16 models)
-// scores = q . k as bf16 hi/lo GEMMs, a causal softmax kernel, O = P . V as GEMMs.
-
-// K and V of cache positions [0, nk) of every kv head, as bf16: K rows
-// concatenated [hi | lo | hi] into kcat [n_kv][nk][3 hd] (against q's
-// [hi | hi | lo] one GEMM gives hi.hi + hi.lo + lo.hi), V as hi and lo rows
-// [n_kv][nk][hd].  One warp per row of hd <= 128 floats.
-__global__ void split_kv_kernel(const float* kc, const float* vc, int ctx, int nk, int hd, int n_kv, uint16_t* kcat,
-                                uint16_t* vh, uint16_t* vl) {
-    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (w >= n_kv * nk) return;
-    const int h = w / nk, p = w % nk;
-    const size_t src = ((size_t)h * ctx + p) * hd, dst = (size_t)w * hd, dk = (size_t)w * 3 * hd;
-    for (int i4 = lane; i4 < hd / 4; i4 += 32) {
-        const float4 k4 = reinterpret_cast<const float4*>(kc + src)[i4];
-        const float4 v4 = reinterpret_cast<const float4*>(vc + src)[i4];
-        const float ke[4] = {k4.x, k4.y, k4.z, k4.w}, ve[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const __nv_bfloat16 a = __float2bfloat16_rn(ke[q]), b = __float2bfloat16_rn(ve[q]);
-            const uint16_t ah = __bfloat16_as_ushort(a);
-            kcat[dk + 4 * i4 + q] = ah;
-            kcat[dk + hd + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ke[q] - __bfloat162float(a)));
-            kcat[dk + 2 * hd + 4 * i4 + q] = ah;
-            vh[dst + 4 * i4 + q] = __bfloat16_as_ushort(b);
-            vl[dst + 4 * i4 + q] = __bfloat16_as_ushort(__float2bfloat16_rn(ve[q] - __bfloat162float(b)));
-        }
-    }
-}
-
-// q of every head of row t as [hi | hi | lo] per head: qcat [T][H][3 hd]
-__global__ void split_q_kernel(const float* qkv, int nqkv, int H, int hd, uint16_t* qcat) {
-    const int t = blockIdx.x;
-    const float* q = qkv + (size_t)t * nqkv;
-    uint16_t* out = qcat + (size_t)t * H * 3 * hd;
-    for (int j = threadIdx.x; j < H * hd; j += blockDim.x) {
-        const int h = j / hd, i = j % hd;
-        const float x = q[j];
-        const __nv_bfloat16 a = __float2bfloat16_rn(x);
-        const uint16_t ah = __bfloat16_as_ushort(a);
-        uint16_t* o = out + (size_t)h * 3 * hd;
-        o[i] = ah;
-        o[hd + i] = ah;
-        o[2 * hd + i] = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(a)));
-    }
-}
-
-// Row (head h, query t) of the scores [H][T][nk] (nk: the even row stride, at
-// least the number of cache positions), one warp per row: att = dot * scale for
-// positions p <= pos0 + t, the softmax of rabbit2.c:399-405 -- p = exp(att - max)
-// / sum -- and P as bf16 hi/lo (0 past the causal limit, the padding included).
-// The row's valid scores are read once into this warp's shared-memory row (the
-// lanes keep their maximum on the way); the exp sum and the P pass then read
-// shared memory.  exp is the hardware's exp2 of a pre-scaled argument and the
-// division a multiply by 1/sum: P is rounded to 16 significant bits (hi + lo) anyway.
-constexpr int kSmaxWarps = 4;
-constexpr int kSmaxThreads = kSmaxWarps * 32;
-size_t causal_softmax_smem(int nk) { return (size_t)kSmaxWarps * nk * sizeof(float); }
-
-__global__ void __launch_bounds__(kSmaxThreads) causal_softmax_kernel(const float* S, int T, int nk, int pos0,
-                                                                      float scale, int rows, uint16_t* ph,
-                                                                      uint16_t* pl) {
-    extern __shared__ __align__(16) float srow_all[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kSmaxWarps + warp;
-    if (row >= rows) return;
-    float* srow = srow_all + (size_t)warp * nk;
-    const int t = row % T, lim = pos0 + t;  // valid p <= lim
-    const float2* sr = reinterpret_cast<const float2*>(S + (size_t)row * nk);
-    const int npairs_valid = lim / 2 + 1, npairs = nk / 2;
-    const float k2 = scale * 1.4426950408889634f;  // log2(e) * scale
-    float m = -INFINITY;
-    for (int q0 = lane; q0 < npairs_valid; q0 += 32 * 8) {  // 8 loads of every lane in flight
-        float2 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int q = q0 + 32 * u;
-            v[u] = q < npairs_valid ? __ldcs(sr + q) : make_float2(-INFINITY, -INFINITY);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int q = q0 + 32 * u;
-            if (q < npairs_valid) {
-                if (2 * q + 1 > lim) v[u].y = -INFINITY;
-                reinterpret_cast<float2*>(srow)[q] = v[u];
-                m = fmaxf(m, fmaxf(v[u].x, v[u].y));
-            }
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL_MASK, m, o));
-    const float mk = m * k2;
-    __syncwarp();
-    float l = 0.0f;
-    for (int q = lane; q < npairs_valid; q += 32) {
-        const float2 x = reinterpret_cast<const float2*>(srow)[q];
-        l += exp2f(fmaf(x.x, k2, -mk)) + exp2f(fmaf(x.y, k2, -mk));
-    }
-    l = warp_sum(l);
-    const float inv = 1.0f / l;
-    uint32_t* hr = reinterpret_cast<uint32_t*>(ph + (size_t)row * nk);
-    uint32_t* lr = reinterpret_cast<uint32_t*>(pl + (size_t)row * nk);
-    for (int q = lane; q < npairs; q += 32) {
-        float p0 = 0.0f, p1 = 0.0f;
-        if (q < npairs_valid) {
-            const float2 x = reinterpret_cast<const float2*>(srow)[q];
-            p0 = exp2f(fmaf(x.x, k2, -mk)) * inv;
-            p1 = exp2f(fmaf(x.y, k2, -mk)) * inv;  // (0 past the limit: exp2(-inf))
-        }
-        const __nv_bfloat16 a0 = __float2bfloat16_rn(p0), a1 = __float2bfloat16_rn(p1);
-        const __nv_bfloat16 b0 = __float2bfloat16_rn(p0 - __bfloat162float(a0));
-        const __nv_bfloat16 b1 = __float2bfloat16_rn(p1 - __bfloat162float(a1));
-        hr[q] = (uint32_t)__bfloat16_as_ushort(a0) | ((uint32_t)__bfloat16_as_ushort(a1) << 16);
-        lr[q] = (uint32_t)__bfloat16_as_ushort(b0) | ((uint32_t)__bfloat16_as_ushort(b1) << 16);
-    }
-}
-
 // ---------------------------------------------------------------- GEMMs
 // out[T, N] (row pitch ldc) (+)= rows[T, K] . W[N, K]^T on the CUDA cores: f32
 // weights, and bf16 shapes the tensor-core tiles do not cover (N % 128, K % 64).
@@ -608,72 +485,19 @@ int proj(RbtModel* m, const void* W, int N, int K, int T, int ld_in, float* out,
     return 1;
 }
 
-// Attention of T query rows (q in place in qkv rows, after RoPE) over cache
-// positions [0, nk), nk = pos0 + T, into ao [T, nq], for bf16 models:
-//   S[h] = (Qhi + Qlo) . (Khi + Klo)^T without the lo.lo term, as one GEMM over
-//          the concatenations [Qhi | Qhi | Qlo] . [Khi | Klo | Khi]^T,
-//   P = causal softmax(S * scale) as hi/lo, O[h] = (Phi + Plo) . (Vhi + Vlo) (3 GEMMs).
-// Heads of one kv group are batched with the kv head's stride (GQA: one call per
-// position in the group).
-// Query rows go in chunks of kAttnRows: a chunk's rows see cache positions below
-// pos0 + (its end) only, so the causal triangle costs about half of the square.
-constexpr int kAttnRows = 512;
-
+// Attention of T query rows (q in the qkv rows, after RoPE) over cache positions
+// [0, pos0 + T) into ao [T, nq], bf16 models: the tensor-core kernel of attn_tc.cu
+// (S = Q K^T and O = P V as bf16 hi/lo MMAs, an exact two-pass softmax).
 int attn_tensor(RbtModel* m, int T, int pos0, const float* kc, const float* vc) {
     const RbtModelConfig& c = m->cfg;
-    PrefillBufs& b = m->pf;
-    const int H = c.n_heads, NKV = c.n_kv_heads, hd = c.head_dim, grp = H / NKV;
-    const int nq = H * hd, nqkv = nq + 2 * NKV * hd, nk = pos0 + T;
-    const int tc = T < kAttnRows ? T : kAttnRows;
-    const int ld_max = (nk + 1) & ~1;  // row stride of S and P: even, so the softmax moves pairs
-    cudaStream_t s = m->stream;
-    float* S = static_cast<float*>(b.att);                     // [H][tc][ld]
-    uint16_t* ph = reinterpret_cast<uint16_t*>(S + (size_t)H * tc * ld_max);
-    uint16_t* pl = ph + (size_t)H * tc * ld_max;
-    uint16_t* qcat = pl + (size_t)H * tc * ld_max;          // [T][H][3 hd]
-    uint16_t* kcat = qcat + (size_t)T * H * 3 * hd;          // [NKV][nk][3 hd]
-    uint16_t* vh = kcat + (size_t)NKV * nk * 3 * hd;
-    uint16_t* vl = vh + (size_t)NKV * nk * hd;
-    split_q_kernel<<<T, 256, 0, s>>>(b.qkv, nqkv, H, hd, qcat);
-    CU(cudaGetLastError());
-    split_kv_kernel<<<(NKV * nk + 7) / 8, 256, 0, s>>>(kc, vc, m->ctx, nk, hd, NKV, kcat, vh, vl);
-    CU(cudaGetLastError());
-    const float one = 1.0f, zero = 0.0f;
-    const long long sK = (long long)nk * hd;
-    for (int r0 = 0; r0 < T; r0 += tc) {
-        const int tn = T - r0 < tc ? T - r0 : tc;   // rows of this chunk
-        const int nkc = pos0 + r0 + tn;              // the positions they can see
-        const int ld = (nkc + 1) & ~1;
-        const long long sS = (long long)grp * tn * ld;
-        // S = qcat . kcat^T: one GEMM over the concatenated 3 hd, written once
-        for (int g = 0; g < grp; g++)
-            CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, nkc, tn, 3 * hd, &one, kcat, CUDA_R_16BF,
-                                          3 * hd, 3 * sK, qcat + ((size_t)r0 * H + g) * 3 * hd, CUDA_R_16BF,
-                                          H * 3 * hd, (long long)grp * 3 * hd, &zero, S + (size_t)g * tn * ld,
-                                          CUDA_R_32F, ld, sS, NKV, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-        if (causal_softmax_smem(ld) > 48 * 1024)
-            CU(cudaFuncSetAttribute(causal_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)causal_softmax_smem(ld)));
-        causal_softmax_kernel<<<(H * tn + kSmaxWarps - 1) / kSmaxWarps, kSmaxThreads, causal_softmax_smem(ld), s>>>(
-            S, tn, ld, pos0 + r0, 1.0f / sqrtf((float)hd), H * tn, ph, pl);
-        CU(cudaGetLastError());
-        for (int g = 0; g < grp; g++) {
-            const uint16_t* A[3] = {vh, vl, vh};
-            const uint16_t* B[3] = {ph, ph, pl};
-            for (int i = 0; i < 3; i++)
-                CB(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, tn, nkc, &one, A[i], CUDA_R_16BF,
-                                              hd, sK, B[i] + (size_t)g * tn * ld, CUDA_R_16BF, ld, sS,
-                                              i ? &one : &zero, b.ao + (size_t)r0 * nq + (size_t)g * hd, CUDA_R_32F,
-                                              nq, (long long)grp * hd, NKV, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-        }
-    }
+    const int nq = c.n_heads * c.head_dim, nqkv = nq + 2 * c.n_kv_heads * c.head_dim;
+    CU(launch_attn_tc(m->pf.qkv, nqkv, c.n_heads, c.n_kv_heads, c.head_dim, kc, vc, m->ctx, pos0, T, m->pf.att,
+                      m->pf.att_bytes, m->pf.ao, m->status, m->stream));
     return 1;
 }
 
 size_t attn_tensor_bytes(const RbtModelConfig& c, int T, int nk) {
-    const size_t H = c.n_heads, nq = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * nk * c.head_dim;
-    const size_t ld = (size_t)((nk + 1) & ~1), tc = (size_t)(T < kAttnRows ? T : kAttnRows);
-    return H * tc * ld * (4 + 2 + 2) + (size_t)T * nq * 3 * 2 + kv * 2 * 3 + kv * 2 * 2;
+    return attn_tc_scratch_bytes(T, c.n_heads * c.head_dim, c.n_kv_heads, c.head_dim, nk);
 }
 
 // the GEMM input rows: rmsnorm(src rows) with w, or src rows as they are (w == nullptr)
@@ -693,11 +517,6 @@ int nkv_of(const RbtModelConfig& c) { return c.n_kv_heads * c.head_dim; }
 int reserve(RbtModel* m, int T, int pos0, int logit_rows) {
     const RbtModelConfig& c = m->cfg;
     PrefillBufs& b = m->pf;
-    if (!m->blas) {
-        CB(cublasCreate(&m->blas));
-        CB(cublasSetStream(m->blas, m->stream));
-        CB(cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH));  // f32 SGEMM stays f32 (no TF32)
-    }
     if (T > b.cap) {
         void* old[] = {b.tokens, b.x, b.qkv, b.ao, b.xf, b.hi, b.lo, b.routing};
         for (void* p : old) cudaFree(p);
@@ -856,8 +675,6 @@ void prefill_free(RbtModel* m) {
     cudaFree(m->proj_part);
     m->proj_part = nullptr;
     m->proj_part_bytes = 0;
-    if (m->blas) cublasDestroy(m->blas);
-    m->blas = nullptr;
 }
 }  // namespace rbt
 

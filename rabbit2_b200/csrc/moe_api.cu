@@ -906,6 +906,7 @@ int rbt_moe_ep_init(RbtMoe* m, int rank, int n_ranks, int max_tokens) {
     rbt::preload_gemv_kernels();
     rbt::preload_stream_kernels();
     rbt::preload_combine_kernels();
+    rbt::preload_attn_tc_kernels();
     rbt::preload_ep_kernels();
     EpState& p = m->ep;
     p.R = n_ranks; p.rank = rank; p.epr = E / n_ranks; p.cap = max_tokens;
