@@ -7,11 +7,12 @@
 // One CTA per (head, 128 query rows); key positions in blocks of 64.  Precision:
 // q, k, v, P are f32 values split into bf16 hi = rn(x) and lo = rn(x - hi); each
 // product is hi.hi + hi.lo + lo.hi (three MMAs into one f32 accumulator; lo.lo is
-// below f32 rounding of the sum).  The softmax is exact in two passes over the
-// key blocks: pass 1 computes S = Q K^T block by block into TMEM and keeps each
-// row's running max and exp-sum; pass 2 computes S again, writes the normalised
-// P = exp(att - max) / sum as bf16 hi/lo rows into shared memory, and accumulates
-// O += P V in TMEM, so O needs no rescaling.
+// below f32 rounding of the sum).  The softmax takes two passes over the key
+// blocks: pass 1 computes S = Q K^T block by block into TMEM and keeps each row's
+// max; pass 2 computes S again, writes p = exp(att - max) (in (0, 1]) as bf16
+// hi/lo rows into shared memory, sums the f32 p of the row, and accumulates
+// O += P V in TMEM; the epilogue divides O by the sum.  With the row's final max
+// known in pass 2, O needs no rescaling, and pass 1 needs no exponentials.
 //
 // Roles (192 threads): warp 0 issues the TMA loads (Q once; K blocks in a 2-slot
 // ring; in pass 2 V^T blocks in a 2-slot ring); warp 1 owns TMEM and issues the
@@ -71,6 +72,14 @@ __device__ __forceinline__ void record(unsigned* status, unsigned code) { atomic
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2^x of the MUFU unit (results below 2^-126 flush to 0: they are below the f32
+// resolution of a softmax row whose largest term is 1)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // 16-byte chunk `c` (of 8) of row `r` in a 128-byte-swizzled K-major tile
@@ -291,31 +300,43 @@ __global__ void __launch_bounds__(kAThreads, 1)
             sn++;
             return true;
         };
-        for (int j = 0; ok && j < nblk; j++) {  // pass 1: row max and exp-sum
+        for (int j = 0; ok && j < nblk; j++) {  // pass 1: the row's max over its visible scores
             uint32_t v[64];
             if (!(ok = load_s(v))) break;
             const int lim = qpos - j * kAK;  // columns c <= lim are visible
-            float bm = -INFINITY;
+            if (lim >= kAK - 1) {
 #pragma unroll
-            for (int c = 0; c < 64; c++)
-                if (c <= lim) bm = fmaxf(bm, __uint_as_float(v[c]));
-            if (bm > m) {
-                l *= exp2f((m - bm) * k2);
-                m = bm;
+                for (int c = 0; c < 64; c++) m = fmaxf(m, __uint_as_float(v[c]));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++)
+                    if (c <= lim) m = fmaxf(m, __uint_as_float(v[c]));
             }
-            const float mk = m * k2;
-#pragma unroll
-            for (int c = 0; c < 64; c++)
-                if (c <= lim) l += exp2f(fmaf(__uint_as_float(v[c]), k2, -mk));
         }
-        const float inv = 1.0f / l, mk = m * k2;
+        // pass 2: p = 2^(att k2 - max k2) (unnormalised, in (0, 1]) as bf16 hi/lo rows of
+        // P for the P.V MMAs, and the row's sum l of the f32 p in ascending position
+        const float mk = m * k2;
         uint8_t* prow_h = smem + C::oP;
         uint8_t* prow_l = prow_h + C::kPBytes;
-        for (int j = 0; ok && j < nblk; j++) {  // pass 2: P rows for the P.V MMAs
+        for (int j = 0; ok && j < nblk; j++) {
             uint32_t v[64];
             if (!(ok = load_s(v))) break;
             const int lim = qpos - j * kAK;
-            if (j > 0) {
+            uint32_t hw[32], lw[32];  // the row's P, packed bf16 pairs, before waiting for the P buffer
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const int c = 2 * i;
+                const float p0 = c <= lim ? ex2_approx(fmaf(__uint_as_float(v[c]), k2, -mk)) : 0.0f;
+                const float p1 = c + 1 <= lim ? ex2_approx(fmaf(__uint_as_float(v[c + 1]), k2, -mk)) : 0.0f;
+                l += p0;
+                l += p1;
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(p0, p1);
+                const float2 hf = __bfloat1622float2(hi);
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
+                hw[i] = *reinterpret_cast<const uint32_t*>(&hi);
+                lw[i] = *reinterpret_cast<const uint32_t*>(&lo);
+            }
+            if (j > 0) {  // the P.V MMAs of block j - 1 have read the P buffer
                 bool w = mbar_wait_bounded(pfree, (j - 1) & 1, kAWaitNs);
                 w = __all_sync(FULL_MASK, w);
                 if (!w) {
@@ -326,25 +347,16 @@ __global__ void __launch_bounds__(kAThreads, 1)
             }
 #pragma unroll
             for (int c8 = 0; c8 < 8; c8++) {
-                uint32_t hw[4], lw[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int c = c8 * 8 + 2 * i;
-                    const float p0 = c <= lim ? exp2f(fmaf(__uint_as_float(v[c]), k2, -mk)) * inv : 0.0f;
-                    const float p1 = c + 1 <= lim ? exp2f(fmaf(__uint_as_float(v[c + 1]), k2, -mk)) * inv : 0.0f;
-                    const __nv_bfloat16 h0 = __float2bfloat16_rn(p0), h1 = __float2bfloat16_rn(p1);
-                    const __nv_bfloat16 l0 = __float2bfloat16_rn(p0 - __bfloat162float(h0));
-                    const __nv_bfloat16 l1 = __float2bfloat16_rn(p1 - __bfloat162float(h1));
-                    hw[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-                    lw[i] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
-                }
                 const uint32_t off = sw128_offset(r, c8);
-                *reinterpret_cast<uint4*>(prow_h + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                *reinterpret_cast<uint4*>(prow_l + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                *reinterpret_cast<uint4*>(prow_h + off) =
+                    make_uint4(hw[4 * c8], hw[4 * c8 + 1], hw[4 * c8 + 2], hw[4 * c8 + 3]);
+                *reinterpret_cast<uint4*>(prow_l + off) =
+                    make_uint4(lw[4 * c8], lw[4 * c8 + 1], lw[4 * c8 + 2], lw[4 * c8 + 3]);
             }
             fence_proxy_async_smem();  // the generic-proxy writes, visible to the tensor cores
             mbar_arrive(pfull);
         }
+        const float inv = 1.0f / l;
         if (ok) {
             bool w = mbar_wait_bounded(ofull, 0, kAWaitNs);
             w = __all_sync(FULL_MASK, w);
@@ -363,8 +375,9 @@ __global__ void __launch_bounds__(kAThreads, 1)
                         float4* dst = reinterpret_cast<float4*>(orow + c0);
 #pragma unroll
                         for (int i = 0; i < 8; i++)
-                            dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
-                                                 __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+                            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                                 __uint_as_float(o[4 * i + 2]) * inv,
+                                                 __uint_as_float(o[4 * i + 3]) * inv);
                     }
                 }
             }
