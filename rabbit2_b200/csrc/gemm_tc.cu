@@ -299,17 +299,33 @@ constexpr int kRStageBytes = 2 * kRATile + kRN * kBK * 2;  // 64 KB
 constexpr int kRStages = 3;
 constexpr int kRSmemBytes = kRStages * kRStageBytes + 1024 + 256;
 
+// kRowsDense: y[t, n] (+)= rows . W^T, one weight matrix (2-D map, 256-row box).
+// kRowsGateUp / kRowsDown: the MoE GEMMs over routed slots in expert order, token
+// blocks of up to 128 slots of one expert (tb_* from tc_schedule_kernel with 128),
+// weights through the experts' 3-D maps (128-row boxes): gate/up tile nt = w1
+// rows [128 nt, +128) and w3 rows [H + 128 nt, +128), epilogue h = silu(g) * u as
+// bf16 hi + lo; down tile nt = w2 rows [256 nt, +256), epilogue y rows (f32).
+constexpr int kRowsDense = 0, kRowsGateUp = 1, kRowsDown = 2;
+
 struct RowsGemmArgs {
-    int T, N, KB;
-    float* y;
-    int ldy;
-    int accumulate;
+    int T, N, KB;             // dense: rows, outputs; every mode: 64-element K blocks
+    float* y;                 // dense / down output rows
+    int ldy;                  // dense: y row pitch
+    int accumulate;           // dense: y +=
     unsigned* status;
+    const int32_t* tb_e;      // MoE: token blocks (expert, first slot, end of the expert's slots)
+    const int32_t* tb_p0;
+    const int32_t* tb_p1;
+    const int32_t* n_tb;
+    int H, D;                 // MoE: expert hidden, model dim
+    void* h_hi;               // gate/up output [S_cap, H] bf16
+    void* h_lo;
 };
 
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
-    dense_rows_gemm_kernel(const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
-                           const __grid_constant__ CUtensorMap tm_w, RowsGemmArgs a) {
+    rows_gemm_kernel(const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+                     const __grid_constant__ CUtensorMap tm_w, RowsGemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kRStages * kRStageBytes);
@@ -346,8 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int NT = a.N / kRN;
-    const int n_tiles = ((a.T + kRM - 1) / kRM) * NT;
+    // tile = (row block, 256-column block of the output)
+    const int NT = kMode == kRowsDense ? a.N / kRN : kMode == kRowsGateUp ? a.H / 128 : a.D / kRN;
+    const int n_tiles = (kMode == kRowsDense ? (a.T + kRM - 1) / kRM : *a.n_tb) * NT;
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ TMA producer
         int stage = 0;
@@ -358,6 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
             const int mt = tile / NT, nt = tile - mt * NT;
+            const int row0 = kMode == kRowsDense ? mt * kRM : a.tb_p0[mt];
+            const int e = kMode == kRowsDense ? 0 : a.tb_e[mt];
             for (int kb = 0; kb < a.KB; kb++) {
                 if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kWaitNs)) {
                     record_error(a.status, 0x111);
@@ -366,9 +385,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 uint8_t* st = smem + stage * kRStageBytes;
                 mbar_arrive_expect_tx(&full[stage], kRStageBytes);
-                tma_load_2d(st, &tm_xhi, &full[stage], kb * kBK, mt * kRM);
-                tma_load_2d(st + kRATile, &tm_xlo, &full[stage], kb * kBK, mt * kRM);
-                tma_load_2d(st + 2 * kRATile, &tm_w, &full[stage], kb * kBK, nt * kRN);
+                tma_load_2d(st, &tm_xhi, &full[stage], kb * kBK, row0);
+                tma_load_2d(st + kRATile, &tm_xlo, &full[stage], kb * kBK, row0);
+                if (kMode == kRowsDense) {
+                    tma_load_2d(st + 2 * kRATile, &tm_w, &full[stage], kb * kBK, nt * kRN);
+                } else {
+                    const int w0 = kMode == kRowsGateUp ? nt * 128 : nt * kRN;
+                    const int w1 = kMode == kRowsGateUp ? a.H + nt * 128 : nt * kRN + 128;
+                    tma_load_3d(st + 2 * kRATile, &tm_w, &full[stage], kb * kBK, w0, e);
+                    tma_load_3d(st + 2 * kRATile + kTileBytes, &tm_w, &full[stage], kb * kBK, w1, e);
+                }
                 used[stage] = true;
                 last_parity[stage] = phase;
                 if (++stage == kRStages) {
@@ -432,7 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int mt = tile / NT, nt = tile - mt * NT;
-            const int t = mt * kRM + q * 32 + lane;
+            const int t = (kMode == kRowsDense ? mt * kRM : a.tb_p0[mt]) + q * 32 + lane;
+            const int t_end = kMode == kRowsDense ? a.T : a.tb_p1[mt];
             bool ok = mbar_wait_bounded(&tfull[buf], acc_phase, kWaitNs);
             ok = __all_sync(FULL_MASK, ok);
             if (!ok) {
@@ -441,18 +468,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * kRN;
-            float* yrow = a.y + (size_t)t * a.ldy + nt * kRN;
+            if (kMode == kRowsGateUp) {
+                // columns [0, 128): gate, [128, 256): up, of hidden units 128 nt + c
+                for (int c0 = 0; c0 < 128; c0 += 32) {
+                    uint32_t g[32], u[32];
+                    tmem_ld_32x32b_x32(tbase + c0, g);
+                    tmem_ld_32x32b_x32(tbase + 128 + c0, u);
+                    tmem_ld_wait();
+                    if (t < t_end) {
+                        uint32_t hw[16], lw[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            float hv[2];
+#pragma unroll
+                            for (int k = 0; k < 2; k++) {
+                                const float gv = __uint_as_float(g[2 * i + k]), uv = __uint_as_float(u[2 * i + k]);
+                                hv[k] = gv / (1.0f + expf(-gv)) * uv;
+                            }
+                            const __nv_bfloat16 h0 = __float2bfloat16_rn(hv[0]), h1 = __float2bfloat16_rn(hv[1]);
+                            const __nv_bfloat16 l0 = __float2bfloat16_rn(hv[0] - __bfloat162float(h0));
+                            const __nv_bfloat16 l1 = __float2bfloat16_rn(hv[1] - __bfloat162float(h1));
+                            hw[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+                            lw[i] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+                        }
+                        const size_t o = (size_t)t * a.H + nt * 128 + c0;
+                        uint4* dh = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.h_hi) + o);
+                        uint4* dl = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.h_lo) + o);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            dh[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+                            dl[i] = make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
+                        }
+                    }
+                }
+            } else {
+            float* yrow = a.y + (size_t)t * (kMode == kRowsDense ? a.ldy : a.D) + nt * kRN;
             for (int c0 = 0; c0 < kRN; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + c0, v);
                 tmem_ld_wait();
-                if (t < a.T) {
+                if (t < t_end) {
                     float4* dst = reinterpret_cast<float4*>(yrow + c0);
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         float4 o = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-                        if (a.accumulate) {
+                        if (kMode == kRowsDense && a.accumulate) {
                             const float4 old = dst[i];
                             o.x += old.x;
                             o.y += old.y;
@@ -462,6 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         dst[i] = o;
                     }
                 }
+            }
             }
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
@@ -841,12 +903,19 @@ cudaError_t launch_tc_dense(const void* W, int N, int K, const void* xhi, const 
         if (!make_map_2d_ld(&mh, xhi, K, ld_in, T, kRM) || !make_map_2d_ld(&ml, xlo, K, ld_in, T, kRM) ||
             !make_map_2d_ld(&mw, W, K, K, N, kRN))
             return cudaErrorNotSupported;
-        RowsGemmArgs a{T, N, K / kBK, y, ldy, accumulate ? 1 : 0, status};
-        cudaError_t err = cudaFuncSetAttribute(dense_rows_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               kRSmemBytes);
+        RowsGemmArgs a{};
+        a.T = T;
+        a.N = N;
+        a.KB = K / kBK;
+        a.y = y;
+        a.ldy = ldy;
+        a.accumulate = accumulate ? 1 : 0;
+        a.status = status;
+        cudaError_t err = cudaFuncSetAttribute(rows_gemm_kernel<kRowsDense>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmemBytes);
         if (err != cudaSuccess) return err;
         const int tiles = ((T + kRM - 1) / kRM) * (N / kRN);
-        dense_rows_gemm_kernel<<<tiles < grid ? tiles : grid, kThreads, kRSmemBytes, s>>>(mh, ml, mw, a);
+        rows_gemm_kernel<kRowsDense><<<tiles < grid ? tiles : grid, kThreads, kRSmemBytes, s>>>(mh, ml, mw, a);
         return cudaGetLastError();
     }
     if (p.ksplit > 1 && (!part || part_bytes < (size_t)p.ksplit * T * N * 4)) p.ksplit = 1;
@@ -879,6 +948,34 @@ cudaError_t launch_tc_dense(const void* W, int N, int K, const void* xhi, const 
     return cudaGetLastError();
 }
 
+// The MoE GEMMs of 128-slot token blocks (tc_pick_bn 128) with the activation
+// slots as the MMA's M side: t, its BN = 128 schedule; xhi/xlo the 128-row maps
+// of the gate/up input rows (h rows for down), w the experts' 3-D map.
+cudaError_t launch_tc_rows_moe(bool gate_up, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
+                               const TcGemmArgs& t, int grid, cudaStream_t s) {
+    if (t.BN != kRM || (gate_up ? t.H % 128 : t.D % kRN)) return cudaErrorInvalidValue;
+    RowsGemmArgs a{};
+    a.KB = t.KB;
+    a.y = t.y;
+    a.status = t.status;
+    a.tb_e = t.tb_e;
+    a.tb_p0 = t.tb_p0;
+    a.tb_p1 = t.tb_p1;
+    a.n_tb = t.n_tb;
+    a.H = t.H;
+    a.D = t.D;
+    a.h_hi = t.h_hi;
+    a.h_lo = t.h_lo;
+    cudaError_t err = cudaFuncSetAttribute(gate_up ? rows_gemm_kernel<kRowsGateUp> : rows_gemm_kernel<kRowsDown>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmemBytes);
+    if (err != cudaSuccess) return err;
+    if (gate_up)
+        rows_gemm_kernel<kRowsGateUp><<<grid, kThreads, kRSmemBytes, s>>>(xhi, xlo, w, a);
+    else
+        rows_gemm_kernel<kRowsDown><<<grid, kThreads, kRSmemBytes, s>>>(xhi, xlo, w, a);
+    return cudaGetLastError();
+}
+
 // Loads every tensor-core path kernel now (see preload_kernels in kernels.h).
 void preload_gemm_kernels() {
     cudaFuncAttributes f;
@@ -894,7 +991,9 @@ void preload_gemm_kernels() {
     (void)cudaFuncGetAttributes(&f, gather_split_kernel);
     (void)cudaFuncGetAttributes(&f, gather_f16_kernel);
     (void)cudaFuncGetAttributes(&f, tc_schedule_kernel);
-    (void)cudaFuncGetAttributes(&f, dense_rows_gemm_kernel);
+    (void)cudaFuncGetAttributes(&f, rows_gemm_kernel<kRowsDense>);
+    (void)cudaFuncGetAttributes(&f, rows_gemm_kernel<kRowsGateUp>);
+    (void)cudaFuncGetAttributes(&f, rows_gemm_kernel<kRowsDown>);
     (void)cudaFuncGetAttributes(&f, dense_reduce_kernel);
     (void)cudaGetLastError();
 }

@@ -186,6 +186,11 @@ bool make_map_2d(CUtensorMap* map, const void* base, int cols, long rows, int bo
 cudaError_t launch_tc_dense(const void* W, int N, int K, const void* xhi, const void* xlo, int ld_in, int T,
                             float* y, int ldy, bool accumulate, unsigned* status, float* part, size_t part_bytes,
                             int grid, cudaStream_t s);
+// The MoE gate/up (gate_up) or down GEMM of a BN = 128 schedule with the slots as
+// the MMA's M side (128 slots x 256 weight rows per tile); xhi/xlo: the input
+// rows' 128-row maps (x for gate/up, h for down); w: the experts' 3-D map.
+cudaError_t launch_tc_rows_moe(bool gate_up, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo,
+                               const TcGemmArgs& t, int grid, cudaStream_t s);
 // the scratch launch_tc_dense uses for T rows of N outputs (0: none)
 size_t tc_dense_part_bytes(int N, int K, int T, int grid);
 // bf16 tensor map of rank 2 or 3 (dims / byte strides of dims 1.. / box, innermost

@@ -500,14 +500,21 @@ int forward(RbtMoe* m, int layer, const float* x, float* out, int T, int32_t* ro
         ta.H = c.expert_hidden; ta.D = c.dim; ta.h_hi = w.hhi; ta.h_lo = w.hlo; ta.y = w.y; ta.status = w.status;
         ta.MB = c.expert_hidden / 128; ta.KB = c.dim / 64;
         ta.bscale = w.bscale;
+        // 128-slot blocks: the slots as the MMA's M side against 256 weight rows per tile
+        const bool rows = bn == 128 && c.dim % 256 == 0;
         if (!clk.begin(2)) return 0;
         if (f16)
             CU(rbt::launch_tc_gateup_f16(L.w_gateup16, w.m_xhi[bi], ta, m->sm_count, s));
+        else if (rows)
+            CU(rbt::launch_tc_rows_moe(true, L.w_gateup, w.m_xhi[bi], w.m_xlo[bi], ta, m->sm_count, s));
         else
             CU(rbt::launch_tc_gateup(L.w_gateup, w.m_xhi[bi], w.m_xlo[bi], ta, m->sm_count, s));
         ta.MB = c.dim / 128; ta.KB = c.expert_hidden / 64;
         if (!clk.begin(3)) return 0;
-        CU(rbt::launch_tc_down(L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
+        if (rows)
+            CU(rbt::launch_tc_rows_moe(false, L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
+        else
+            CU(rbt::launch_tc_down(L.w_down, w.m_hhi[bi], w.m_hlo[bi], ta, m->sm_count, s));
     } else if (!ep_rows && m->path != 3 &&
                rbt::stream_supported(sa_of(m, L, xb, x, out, T, block && !given), c.dtype)) {
         rbt::StreamArgs sa = sa_of(m, L, xb, x, out, T, block && !given);
