@@ -7,15 +7,15 @@
 // One CTA per (head, 128 query rows); key positions in blocks of 64.  Precision:
 // q, k, v, P are f32 values split into bf16 hi = rn(x) and lo = rn(x - hi); each
 // product is hi.hi + hi.lo + lo.hi (three MMAs into one f32 accumulator; lo.lo is
-// below f32 rounding of the sum).  The softmax takes two passes over the key
-// blocks: pass 1 computes S = Q K^T block by block into TMEM and keeps each row's
-// max; pass 2 computes S again, writes p = exp(att - max) (in (0, 1]) as bf16
-// hi/lo rows into shared memory, sums the f32 p of the row, and accumulates
-// O += P V in TMEM; the epilogue divides O by the sum.  With the row's final max
-// known in pass 2, O needs no rescaling, and pass 1 needs no exponentials.
+// below f32 rounding of the sum).  One pass over the key blocks: S = Q K^T of a
+// block into TMEM, p = exp(att - m) against the row's running max m, written as
+// bf16 hi/lo rows of P into shared memory and summed in f32, and O += P V in TMEM;
+// the epilogue divides O by the sum.  m moves only when a block's max exceeds it
+// by enough to make p larger than 2^8, and then the row threads rescale O in TMEM
+// between two blocks' P.V MMAs (rarely: a row's max settles within a few blocks).
 //
-// Roles (192 threads): warp 0 issues the TMA loads (Q once; K blocks in a 2-slot
-// ring; in pass 2 V^T blocks in a 2-slot ring); warp 1 owns TMEM and issues the
+// Roles (192 threads): warp 0 issues the TMA loads (Q once; K and V^T blocks in
+// 2-slot rings); warp 1 owns TMEM and issues the
 // MMAs; warps 2-5 (one thread per query row, TMEM lane quadrant warp % 4) run the
 // softmax and the epilogue.  TMEM: two 64-column S buffers and the O accumulator.
 // Every mbarrier wait is bounded by %globaltimer; a wait that runs out records a
@@ -39,6 +39,7 @@ constexpr int kAQ = 128;  // query rows per CTA (MMA M)
 constexpr int kAK = 64;   // key positions per block (S MMA N; P.V MMA K)
 constexpr int kAThreads = 192;
 constexpr uint64_t kAWaitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
+constexpr float kRescale = 8.0f;              // log2 of the largest p before the running max moves
 
 template <int HD>
 struct AttnCfg {
@@ -158,39 +159,34 @@ __global__ void __launch_bounds__(kAThreads, 1)
             tma_load_2d(smem + C::oQ + c * C::kQChunk, &tm_qh, qfull, h * HD + c * 64, q0);
             tma_load_2d(smem + C::oQ + C::kQBytes + c * C::kQChunk, &tm_ql, qfull, h * HD + c * 64, q0);
         }
-        int kn = 0;
-        for (int pass = 0; ok && pass < 2; pass++) {
-            for (int j = 0; j < nblk; j++, kn++) {
-                const int ks = kn & 1;
-                if (!mbar_wait_bounded(&kempty[ks], ((kn >> 1) & 1) ^ 1u, kAWaitNs)) {
-                    record(a.status, 0x121);
-                    ok = false;
-                    break;
-                }
-                uint8_t* st = smem + C::oK + ks * 2 * C::kKBytes;
-                mbar_arrive_expect_tx(&kfull[ks], 2 * C::kKBytes);
-#pragma unroll
-                for (int c = 0; c < HD / 64; c++) {
-                    tma_load_3d(st + c * C::kKChunk, &tm_kh, &kfull[ks], c * 64, j * kAK, g);
-                    tma_load_3d(st + C::kKBytes + c * C::kKChunk, &tm_kl, &kfull[ks], c * 64, j * kAK, g);
-                }
-                kused[ks] = true;
-                kpar[ks] = (kn >> 1) & 1;
-                if (pass == 1) {
-                    const int vs = j & 1;
-                    if (!mbar_wait_bounded(&vempty[vs], ((j >> 1) & 1) ^ 1u, kAWaitNs)) {
-                        record(a.status, 0x122);
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* sv = smem + C::oV + vs * 2 * C::kVBytes;
-                    mbar_arrive_expect_tx(&vfull[vs], 2 * C::kVBytes);
-                    tma_load_3d(sv, &tm_vh, &vfull[vs], j * kAK, 0, g);
-                    tma_load_3d(sv + C::kVBytes, &tm_vl, &vfull[vs], j * kAK, 0, g);
-                    vused[vs] = true;
-                    vpar[vs] = (j >> 1) & 1;
-                }
+        for (int j = 0; j < nblk; j++) {
+            const int ks = j & 1;
+            if (!mbar_wait_bounded(&kempty[ks], ((j >> 1) & 1) ^ 1u, kAWaitNs)) {
+                record(a.status, 0x121);
+                ok = false;
+                break;
             }
+            uint8_t* st = smem + C::oK + ks * 2 * C::kKBytes;
+            mbar_arrive_expect_tx(&kfull[ks], 2 * C::kKBytes);
+#pragma unroll
+            for (int c = 0; c < HD / 64; c++) {
+                tma_load_3d(st + c * C::kKChunk, &tm_kh, &kfull[ks], c * 64, j * kAK, g);
+                tma_load_3d(st + C::kKBytes + c * C::kKChunk, &tm_kl, &kfull[ks], c * 64, j * kAK, g);
+            }
+            kused[ks] = true;
+            kpar[ks] = (j >> 1) & 1;
+            const int vs = j & 1;
+            if (!mbar_wait_bounded(&vempty[vs], ((j >> 1) & 1) ^ 1u, kAWaitNs)) {
+                record(a.status, 0x122);
+                ok = false;
+                break;
+            }
+            uint8_t* sv = smem + C::oV + vs * 2 * C::kVBytes;
+            mbar_arrive_expect_tx(&vfull[vs], 2 * C::kVBytes);
+            tma_load_3d(sv, &tm_vh, &vfull[vs], j * kAK, 0, g);
+            tma_load_3d(sv + C::kVBytes, &tm_vl, &vfull[vs], j * kAK, 0, g);
+            vused[vs] = true;
+            vpar[vs] = (j >> 1) & 1;
         }
         // every copy this thread issued has landed before the CTA may exit
         if (!mbar_wait_bounded(qfull, 0, kAWaitNs)) record(a.status, 0x123);
@@ -238,8 +234,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
             sn++;
             return true;
         };
-        for (int j = 0; ok && j < nblk; j++) ok = issue_s();  // pass 1
-        if (ok) ok = issue_s();                               // pass 2, block 0
+        if (ok) ok = issue_s();  // block 0
         for (int j = 0; ok && j < nblk; j++) {
             if (j + 1 < nblk && !(ok = issue_s())) break;  // S of block j+1 overlaps the softmax of j
             const int vs = j & 1;
@@ -300,28 +295,34 @@ __global__ void __launch_bounds__(kAThreads, 1)
             sn++;
             return true;
         };
-        for (int j = 0; ok && j < nblk; j++) {  // pass 1: the row's max over its visible scores
-            uint32_t v[64];
-            if (!(ok = load_s(v))) break;
-            const int lim = qpos - j * kAK;  // columns c <= lim are visible
-            if (lim >= kAK - 1) {
-#pragma unroll
-                for (int c = 0; c < 64; c++) m = fmaxf(m, __uint_as_float(v[c]));
-            } else {
-#pragma unroll
-                for (int c = 0; c < 64; c++)
-                    if (c <= lim) m = fmaxf(m, __uint_as_float(v[c]));
-            }
-        }
-        // pass 2: p = 2^(att k2 - max k2) (unnormalised, in (0, 1]) as bf16 hi/lo rows of
-        // P for the P.V MMAs, and the row's sum l of the f32 p in ascending position
-        const float mk = m * k2;
+        // p = 2^(att k2 - m k2) as bf16 hi/lo rows of P for the P.V MMAs, and the row's
+        // sum l of the f32 p in ascending position.  m is the row's running max, moved
+        // only when a block's max exceeds it by more than 2^kRescale in p (p stays
+        // below 2^kRescale): then O (in TMEM) and l are scaled by 2^((m_old - m) k2),
+        // between the P.V MMAs of the previous block and those of this one.
         uint8_t* prow_h = smem + C::oP;
         uint8_t* prow_l = prow_h + C::kPBytes;
         for (int j = 0; ok && j < nblk; j++) {
             uint32_t v[64];
             if (!(ok = load_s(v))) break;
-            const int lim = qpos - j * kAK;
+            const int lim = qpos - j * kAK;  // columns c <= lim are visible
+            float bm = -INFINITY;
+            if (lim >= kAK - 1) {
+#pragma unroll
+                for (int c = 0; c < 64; c++) bm = fmaxf(bm, __uint_as_float(v[c]));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++)
+                    if (c <= lim) bm = fmaxf(bm, __uint_as_float(v[c]));
+            }
+            float alpha = 1.0f;
+            const bool move = j == 0 ? true : (bm - m) * k2 > kRescale;
+            if (move && bm > m) {
+                if (j > 0) alpha = ex2_approx((m - bm) * k2);
+                m = bm;
+                l *= alpha;
+            }
+            const float mk = m * k2;
             uint32_t hw[32], lw[32];  // the row's P, packed bf16 pairs, before waiting for the P buffer
 #pragma unroll
             for (int i = 0; i < 32; i++) {
@@ -336,13 +337,27 @@ __global__ void __launch_bounds__(kAThreads, 1)
                 hw[i] = *reinterpret_cast<const uint32_t*>(&hi);
                 lw[i] = *reinterpret_cast<const uint32_t*>(&lo);
             }
-            if (j > 0) {  // the P.V MMAs of block j - 1 have read the P buffer
+            if (j > 0) {  // the P.V MMAs of block j - 1 are done: P is free, O is stable
                 bool w = mbar_wait_bounded(pfree, (j - 1) & 1, kAWaitNs);
                 w = __all_sync(FULL_MASK, w);
                 if (!w) {
                     record(a.status, 0x322);
                     ok = false;
                     break;
+                }
+                if (__any_sync(FULL_MASK, alpha != 1.0f)) {  // O *= alpha (1 on the rows that keep m)
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c0 = 0; c0 < HD; c0 += 32) {
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(trow + C::kOCol + c0, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st_32x32b_x32(trow + C::kOCol + c0, o);
+                    }
+                    tmem_st_wait();
+                    tc_fence_before();
                 }
             }
 #pragma unroll
@@ -411,31 +426,52 @@ __global__ void __launch_bounds__(256) split_kv_t_kernel(const float* __restrict
                                                          int ctx, int nk, int hd, int ldv, uint16_t* kh,
                                                          uint16_t* kl, uint16_t* vh, uint16_t* vl) {
     __shared__ float tile[kAK][128 + 1];
-    const int g = blockIdx.y, p0 = blockIdx.x * kAK;
+    const int g = blockIdx.y, p0 = blockIdx.x * kAK, hd4 = hd / 4;
     const float* ksrc = kc + (size_t)g * ctx * hd;
     const float* vsrc = vc + (size_t)g * ctx * hd;
-    for (int i = threadIdx.x; i < kAK * hd; i += blockDim.x) {
-        const int p = i / hd, d = i - p * hd, pos = p0 + p;
-        float v = 0.0f;
+    for (int i = threadIdx.x; i < kAK * hd4; i += blockDim.x) {  // float4 of position p, dims 4 d4 ..
+        const int p = i / hd4, d = (i - p * hd4) * 4, pos = p0 + p;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (pos < nk) {
-            const float x = ksrc[(size_t)pos * hd + d];
-            const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+            const float4 k = *reinterpret_cast<const float4*>(ksrc + (size_t)pos * hd + d);
+            const float ke[4] = {k.x, k.y, k.z, k.w};
+            uint32_t hw[2], lw[2];
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const __nv_bfloat16 h0 = __float2bfloat16_rn(ke[2 * q]), h1 = __float2bfloat16_rn(ke[2 * q + 1]);
+                const __nv_bfloat16 l0 = __float2bfloat16_rn(ke[2 * q] - __bfloat162float(h0));
+                const __nv_bfloat16 l1 = __float2bfloat16_rn(ke[2 * q + 1] - __bfloat162float(h1));
+                hw[q] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+                lw[q] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+            }
             const size_t o = ((size_t)g * nk + pos) * hd + d;
-            kh[o] = __bfloat16_as_ushort(hi);
-            kl[o] = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(hi)));
-            v = vsrc[(size_t)pos * hd + d];
+            *reinterpret_cast<uint2*>(kh + o) = make_uint2(hw[0], hw[1]);
+            *reinterpret_cast<uint2*>(kl + o) = make_uint2(lw[0], lw[1]);
+            v = *reinterpret_cast<const float4*>(vsrc + (size_t)pos * hd + d);
         }
-        tile[p][d] = v;
+        tile[p][d] = v.x;
+        tile[p][d + 1] = v.y;
+        tile[p][d + 2] = v.z;
+        tile[p][d + 3] = v.w;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kAK * hd; i += blockDim.x) {
-        const int d = i / kAK, p = i - d * kAK, pos = p0 + p;
+    constexpr int kP4 = kAK / 4;
+    for (int i = threadIdx.x; i < hd * kP4; i += blockDim.x) {  // dim d, positions 4 p4 .. + 4
+        const int d = i / kP4, p = (i - d * kP4) * 4, pos = p0 + p;
         if (pos >= ldv) continue;
-        const float x = tile[p][d];
-        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+        uint32_t hw[2], lw[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const float x0 = tile[p + 2 * q][d], x1 = tile[p + 2 * q + 1][d];
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+            const __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
+            const __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
+            hw[q] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+            lw[q] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+        }
         const size_t o = ((size_t)g * hd + d) * ldv + pos;
-        vh[o] = __bfloat16_as_ushort(hi);
-        vl[o] = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(hi)));
+        *reinterpret_cast<uint2*>(vh + o) = make_uint2(hw[0], hw[1]);
+        *reinterpret_cast<uint2*>(vl + o) = make_uint2(lw[0], lw[1]);
     }
 }
 

@@ -71,51 +71,86 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* x, const
     for (int i = threadIdx.x; i < D; i += kThreads) o[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
-// The same rmsnorm for many tokens: one warp per 32 rows, lane r running row r's
+// The same rmsnorm for many tokens: one CTA per 32 rows, lane r of warp 0 running row r's
 // sum of squares as the reference's plain sequential chain (products and sums
 // separately rounded, in index order: the same bits as block_seq_sum), then the
-// warp writes the 32 normalised rows with coalesced stores.  At thousands of
+// CTA's eight warps write the 32 normalised rows with coalesced stores.  At thousands of
 // tokens the per-row parallel reproduction costs more issue slots than the chains'
 // latency: one dependent add per element, 32 rows per warp, every SM streaming.
+// The rows come through a shared-memory ring of kRowsStages chunks (32 rows x
+// kRowsChunk floats), copied with coalesced cp.async (the warp moves one row's
+// chunk per instruction), so that several chunks are in flight while the chains
+// run; each row's chunk sits kRowsPitch bytes apart (16 bytes of padding keep the
+// lanes' float4 reads on distinct banks).
 constexpr int kRowsPerWarp = 32;
 constexpr int kRowsMinTokens = 1024;
+constexpr int kRowsChunk = 128;                      // floats per row per stage
+constexpr int kRowsPitch = kRowsChunk * 4 + 16;      // bytes per row in a stage
+constexpr int kRowsStages = 8;
+constexpr int kRowsSmem = kRowsStages * kRowsPerWarp * kRowsPitch;
+constexpr int kRowsWarps = 8;  // warp 0 runs the chains; all eight write the rows
+constexpr int kRowsThreads = kRowsWarps * 32;
 
-__global__ void __launch_bounds__(32) rmsnorm_rows_kernel(const float* x, const float* w, float* out, int T, int D,
-                                                          float eps) {
-    const int lane = threadIdx.x, r0 = blockIdx.x * kRowsPerWarp;
-    const int row = r0 + lane;
-    float ss = 0.0f;
-    if (row < T) {
-        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
-        const int n4 = D / 4;
-        int i = 0;
-        for (; i + 8 <= n4; i += 8) {  // eight 16-byte loads in flight ahead of the adds
-            float4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = __ldg(xr + i + u);
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
-                ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
-                ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
-                ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
-            }
-        }
-        for (; i < n4; i++) {
-            const float4 v = __ldg(xr + i);
-            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
-            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
-            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
-            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
-        }
-    }
-    const float inv_mine = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kRowsThreads) rmsnorm_rows_kernel(const float* x, const float* w, float* out, int T,
+                                                                    int D, float eps) {
+    extern __shared__ __align__(16) uint8_t ring[];
+    __shared__ float s_inv[kRowsPerWarp];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, r0 = blockIdx.x * kRowsPerWarp;
     const int nrows = min(kRowsPerWarp, T - r0);
-    for (int r = 0; r < nrows; r++) {
-        const float inv = __shfl_sync(0xffffffffu, inv_mine, r);
+    const int n_chunks = D / kRowsChunk;
+    // stage c % kRowsStages <- chunk c of every row (lane l copies bytes [16 l, 16 l + 16))
+    auto load = [&](int c) {
+        uint8_t* st = ring + (c % kRowsStages) * (kRowsPerWarp * kRowsPitch);
+        if (c < n_chunks)
+            for (int r = 0; r < nrows; r++)
+                cp_async16(st + r * kRowsPitch + lane * 16, x + (size_t)(r0 + r) * D + c * kRowsChunk + lane * 4);
+        cp_async_commit();  // (an empty group past the last chunk keeps the wait count uniform)
+    };
+    if (warp == 0) {  // the 32 chains
+#pragma unroll 1
+        for (int c = 0; c < kRowsStages - 1; c++) load(c);
+        float ss = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < n_chunks; c++) {
+            cp_async_wait<kRowsStages - 2>();  // chunk c has landed (this lane's copies)
+            __syncwarp();                       // ... and every lane's
+            if (lane < nrows) {
+                const float4* v = reinterpret_cast<const float4*>(
+                    ring + (c % kRowsStages) * (kRowsPerWarp * kRowsPitch) + lane * kRowsPitch);
+#pragma unroll 8
+                for (int i = 0; i < kRowsChunk / 4; i++) {
+                    const float4 q = v[i];
+                    ss = __fadd_rn(ss, __fmul_rn(q.x, q.x));
+                    ss = __fadd_rn(ss, __fmul_rn(q.y, q.y));
+                    ss = __fadd_rn(ss, __fmul_rn(q.z, q.z));
+                    ss = __fadd_rn(ss, __fmul_rn(q.w, q.w));
+                }
+            }
+            __syncwarp();  // every lane is done with the stage that chunk c + kRowsStages - 1 reuses
+            load(c + kRowsStages - 1);
+        }
+        cp_async_wait<0>();
+        s_inv[lane] = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+    }
+    __syncthreads();
+    // the normalised rows, every warp of the CTA: row r by warp r % kRowsWarps
+    const int n4 = D / 4;
+    for (int r = warp; r < nrows; r += kRowsWarps) {
+        const float inv = s_inv[r];
         const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(r0 + r) * D);
         float4* o = reinterpret_cast<float4*>(out + (size_t)(r0 + r) * D);
-        for (int i4 = lane; i4 < D / 4; i4 += 32) {
+#pragma unroll 4
+        for (int i4 = lane; i4 < n4; i4 += 32) {
             const float4 v = __ldg(xr + i4), ww = __ldg(reinterpret_cast<const float4*>(w) + i4);
             o[i4] = make_float4(__fmul_rn(__fmul_rn(v.x, inv), ww.x), __fmul_rn(__fmul_rn(v.y, inv), ww.y),
                                 __fmul_rn(__fmul_rn(v.z, inv), ww.z), __fmul_rn(__fmul_rn(v.w, inv), ww.w));
@@ -139,9 +174,13 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t s) {
 
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int T, int D, float eps, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    if (T >= kRowsMinTokens && D % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+    if (T >= kRowsMinTokens && D % kRowsChunk == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
         reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
-        rmsnorm_rows_kernel<<<(T + kRowsPerWarp - 1) / kRowsPerWarp, 32, 0, s>>>(x, w, out, T, D, eps);
+        cudaError_t err = cudaFuncSetAttribute(rmsnorm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kRowsSmem);
+        if (err != cudaSuccess) return err;
+        rmsnorm_rows_kernel<<<(T + kRowsPerWarp - 1) / kRowsPerWarp, kRowsThreads, kRowsSmem, s>>>(x, w, out, T, D,
+                                                                                                 eps);
         return cudaGetLastError();
     }
     const size_t smem = (size_t)D * sizeof(float);

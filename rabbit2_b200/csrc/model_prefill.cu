@@ -176,13 +176,18 @@ __global__ void __launch_bounds__(kRowThreads) norm_split_kernel(const float* x,
         const size_t o = (size_t)t * ld_out + 4 * (size_t)i4;
         if (xf) {
             *reinterpret_cast<float4*>(xf + o) = make_float4(e[0], e[1], e[2], e[3]);
-        } else {
+        } else {  // four bf16 hi and four lo as one 8-byte store each
+            uint32_t hw[2], lw[2];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const __nv_bfloat16 h = __float2bfloat16_rn(e[q]);
-                hi[o + q] = __bfloat16_as_ushort(h);
-                lo[o + q] = __bfloat16_as_ushort(__float2bfloat16_rn(e[q] - __bfloat162float(h)));
+            for (int q = 0; q < 2; q++) {
+                const __nv_bfloat16 h0 = __float2bfloat16_rn(e[2 * q]), h1 = __float2bfloat16_rn(e[2 * q + 1]);
+                const __nv_bfloat16 l0 = __float2bfloat16_rn(e[2 * q] - __bfloat162float(h0));
+                const __nv_bfloat16 l1 = __float2bfloat16_rn(e[2 * q + 1] - __bfloat162float(h1));
+                hw[q] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+                lw[q] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
             }
+            *reinterpret_cast<uint2*>(hi + o) = make_uint2(hw[0], hw[1]);
+            *reinterpret_cast<uint2*>(lo + o) = make_uint2(lw[0], lw[1]);
         }
     }
 }
