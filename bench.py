@@ -281,7 +281,7 @@ class ClockSampler:
 # workload (natural routing); the profile summary named beside each figure holds the capture.
 MEASURED_TRAFFIC = {
     ("decode_fused", 1): (101.294080e6 + 3.348480e6, "profiles/decode_fused_olmoe_T1.md"),
-    ("gate_up", 4096): (870.818304e6 + 121.764352e6, "profiles/prefill_tc_olmoe_T4096.md"),
+    ("gate_up", 4096): (843.422976e6 + 124.197632e6, "profiles/prefill_tc_olmoe_T4096.md"),
 }
 
 
