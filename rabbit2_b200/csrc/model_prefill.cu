@@ -224,32 +224,37 @@ __global__ void __launch_bounds__(kRowThreads) qk_rope_kv_kernel(float* qkv, int
     }
     const float* cs = rope_cos + (size_t)pos * half;
     const float* sn = rope_sin + (size_t)pos * half;
-    const int nqp = nq / 2, nkp = nkv / 2;  // (i, i + half) pairs of every head
+    // (i, i + half) pairs of every head, two adjacent i per thread (8-byte accesses;
+    // head_dim is a multiple of 4)
+    const int hh = half / 2, nqp = nq / 4, nkp = nkv / 4;
     for (int j = tid; j < nqp + nkp; j += kRowThreads) {
         const bool is_q = j < nqp;
-        const int jj = is_q ? j : j - nqp, h = jj / half, i = jj % half;
+        const int jj = is_q ? j : j - nqp, h = jj / hh, i = (jj % hh) * 2;
         float* p = row + (is_q ? 0 : nq) + (size_t)h * hd;
-        float a = p[i], b = p[i + half];
+        const float2 a2 = *reinterpret_cast<const float2*>(p + i), b2 = *reinterpret_cast<const float2*>(p + i + half);
+        const float2 c2 = *reinterpret_cast<const float2*>(cs + i), s2 = *reinterpret_cast<const float2*>(sn + i);
+        float a[2] = {a2.x, a2.y}, b[2] = {b2.x, b2.y};
+        const float cc[2] = {c2.x, c2.y}, ss[2] = {s2.x, s2.y};
         const float* w = is_q ? q_norm : k_norm;
-        if (w) {
-            const float inv = is_q ? inv_q : inv_k;
-            a = __fmul_rn(__fmul_rn(a, inv), w[(size_t)h * hd + i]);
-            b = __fmul_rn(__fmul_rn(b, inv), w[(size_t)h * hd + i + half]);
+        float ra[2], rb[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            if (w) {
+                const float inv = is_q ? inv_q : inv_k;
+                a[u] = __fmul_rn(__fmul_rn(a[u], inv), w[(size_t)h * hd + i + u]);
+                b[u] = __fmul_rn(__fmul_rn(b[u], inv), w[(size_t)h * hd + i + u + half]);
+            }
+            ra[u] = __fsub_rn(__fmul_rn(a[u], cc[u]), __fmul_rn(b[u], ss[u]));
+            rb[u] = __fadd_rn(__fmul_rn(b[u], cc[u]), __fmul_rn(a[u], ss[u]));
         }
-        const float ra = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
-        const float rb = __fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i]));
-        if (is_q) {
-            p[i] = ra;
-            p[i + half] = rb;
-        } else {
-            const size_t at = ((size_t)h * ctx + pos) * hd;
-            kc[at + i] = ra;
-            kc[at + i + half] = rb;
-        }
+        float* dst = is_q ? p : kc + ((size_t)h * ctx + pos) * hd;
+        *reinterpret_cast<float2*>(dst + i) = make_float2(ra[0], ra[1]);
+        *reinterpret_cast<float2*>(dst + i + half) = make_float2(rb[0], rb[1]);
     }
-    for (int j = tid; j < nkv; j += kRowThreads) {
-        const int h = j / hd, i = j % hd;
-        vc[((size_t)h * ctx + pos) * hd + i] = row[nq + nkv + j];
+    for (int j = tid; j < nkv / 4; j += kRowThreads) {  // v rows into the cache, 16 bytes at a time
+        const int h = (4 * j) / hd, i = (4 * j) % hd;
+        *reinterpret_cast<float4*>(vc + ((size_t)h * ctx + pos) * hd + i) =
+            *reinterpret_cast<const float4*>(row + nq + nkv + 4 * j);
     }
 }
 
