@@ -189,6 +189,40 @@ def test_prefill_long_prompt_in_causal_chunks(tmp_path):
 
 
 @pytest.mark.gpu
+def test_prefill_at_olmoe_width_matches_token_by_token_forward(tmp_path):
+    """OLMoE-1B-7B's attention width (dim 2048, 16 heads x 128) and a 1000-token
+    prompt: the batched prompt (tensor-core projections over 128-row tiles, the
+    tensor-core attention over 8 query tiles and up to 16 key blocks per tile)
+    against the one-token forward (GEMV projections, split attention) fed the same
+    tokens one at a time, on the same model file.  Sampled rows' logits within 1e-3;
+    routing rows equal except near-tie rows (at most 0.5 % of them)."""
+    from rabbit2_b200.model import ModelContext
+    cfg = dataclasses.replace(workload.tiny_olmoe_config(), vocab=4096, dim=2048, n_layers=2, n_heads=16,
+                              n_kv_heads=16, head_dim=128, n_experts=8, top_k=2, expert_hidden=1024,
+                              max_seq=2048, dtype=DT_BF16)
+    path = str(tmp_path / "wide.rbt2")
+    workload.write_model(path, cfg, seed=11)
+    n = 1000
+    prompt = np.random.default_rng(12).integers(0, cfg.vocab, size=n).tolist()
+    rows = [0, 1, 127, 128, 129, 511, 640, 999]
+    a = ModelContext.from_file(path, ctx=1024)
+    b = ModelContext.from_file(path, ctx=1024)
+    try:
+        got_l, got_r = a.prefill(prompt, 0, logit_rows=n)
+        want_r = np.empty_like(got_r)
+        for pos, tok in enumerate(prompt):
+            lg, want_r[pos] = b.forward(tok, pos, logits=pos in rows)
+            if pos in rows:
+                err = np.abs(got_l[pos].astype(np.float64) - lg).max() / np.abs(lg).max()
+                assert err < LOGIT_RTOL, (pos, err)
+        same = np.mean(np.all(got_r == want_r, axis=-1))
+        assert same >= 0.995, same
+    finally:
+        a.close()
+        b.close()
+
+
+@pytest.mark.gpu
 def test_decode_after_a_longer_prefill_recaptures_its_graph(tmp_path):
     """The per-token graph holds the MoE workspace's addresses; a prompt longer
     than any call before reallocates that workspace.  Decoding after it must give
